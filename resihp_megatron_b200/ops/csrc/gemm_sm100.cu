@@ -1,0 +1,405 @@
+// Persistent warp-specialised bf16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM).
+//
+//   D[m, n] = alpha * sum_k A(m, k) * B(n, k)          (+ epilogue: residual / accumulate)
+//
+// A and B are each either K-major (row of the operand contiguous along k) or MN-major
+// (contiguous along m / n), so a linear layer's forward (x W^T), dgrad (dy W) and wgrad
+// (dy^T x) all run without a transpose.
+//
+// Roles per CTA (one CTA per SM, grid = min(#tiles, #SMs), static round-robin over tiles):
+//   warp 0      : TMA producer, STAGES-deep ring of (A, B) tiles, 128B swizzle
+//   warp 1      : TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 2..5  : epilogue, tcgen05.ld of the accumulator rows owned by the warp's lane
+//                 quadrant, fused scale / residual / fp32 accumulate, vector stores
+// The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of tile i
+// overlaps the MMAs of tile i+1.
+//
+// This file is new work: the reference framework has no GEMM of its own (its compute
+// validation probe `resihp/detect/validation.py:17-31` calls torch.matmul).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "sm100.cuh"
+
+namespace rb {
+
+enum : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiBF16Res = 3 };
+
+struct GemmArgs {
+  int M, N, K;
+  void* D;
+  long long ldd;
+  const __nv_bfloat16* R;
+  long long ldr;
+  float alpha;
+  int* err;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;  // 64 bf16 = 128 B = one swizzle row
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 192;
+  static constexpr int GROUP_M = 16;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb,
+                                            int& nb) {
+  const int per_group = group_m * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * group_m;
+  const int gsize = min(num_m - first_m, group_m);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+// lane 0 waits, the whole warp learns the outcome
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    GemmArgs p) {
+  using C = GemmCfg<BN>;
+  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 4]);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;      // stages with a load in flight at some point
+      uint32_t issued_parity = 0;    // parity of the last load issued into each stage
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+          const uint32_t a_dst = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_dst = smem_u32(sB + stage * C::B_BYTES);
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, fb, kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, fb, mb * BM + 64 * j, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d(b_dst, &tmB, fb, kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, fb, nb * BN + 64 * j, kb * BK);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain: every load this thread issued must have landed before the CTA exits.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, true, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? make_smem_desc(a_base + k * 2048, 8192, 1024, kSwizzle128B)
+                                     : make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = B_MN ? make_smem_desc(b_base + k * 2048, 8192, 1024, kSwizzle128B)
+                                     : make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1;
+      }
+      // Every MMA issued by this thread completes before TMEM is released.
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
+      if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+        const bool full = (col0 + 32 <= p.N);
+        if (EPI == kEpiBF16 || EPI == kEpiBF16Res) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+          if (EPI == kEpiBF16Res) {
+            const __nv_bfloat16* res = p.R + row * p.ldr + col0;
+            if (full) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 u = *reinterpret_cast<const uint4*>(res + 8 * j);
+                float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y), f2 = unpack_bf16x2(u.z),
+                       f3 = unpack_bf16x2(u.w);
+                v[8 * j + 0] += f0.x; v[8 * j + 1] += f0.y; v[8 * j + 2] += f1.x; v[8 * j + 3] += f1.y;
+                v[8 * j + 4] += f2.x; v[8 * j + 5] += f2.y; v[8 * j + 6] += f3.x; v[8 * j + 7] += f3.y;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) v[j] += __bfloat162float(res[j]);
+            }
+          }
+          if (full) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u;
+              u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+              u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+              u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+              u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+              *reinterpret_cast<uint4*>(dst + 8 * j) = u;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+          }
+        } else {
+          float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col0;
+          if (full) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (EPI == kEpiF32Acc) {
+                const float4 old = *reinterpret_cast<const float4*>(dst + 4 * j);
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              *reinterpret_cast<float4*>(dst + 4 * j) = o;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) dst[j] = (EPI == kEpiF32Acc) ? dst[j] + v[j] : v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+    if (h) fn = reinterpret_cast<EncodeTiledFn>(dlsym(h, "cuTensorMapEncodeTiled"));
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128B swizzle: `inner` contiguous elements per row, `outer` rows.
+int make_tmap_bf16_2d(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
+                       cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
+  static bool attr_set = false;  // per instantiation; attribute is per function and device-agnostic
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  const int tiles = ((a.M + C::BM - 1) / C::BM) * ((a.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kern<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int EPI>
+static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const GemmArgs& a, int num_sms, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(ta, tb, a, num_sms, s);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(ta, tb, a, num_sms, s);
+  if (a_mn && !b_mn) return launch_gemm<BN, true, false, EPI>(ta, tb, a, num_sms, s);
+  return launch_gemm<BN, true, true, EPI>(ta, tb, a, num_sms, s);
+}
+
+template <int BN>
+static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                        const GemmArgs& a, int num_sms, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBF16: return dispatch_major<BN, kEpiBF16>(a_mn, b_mn, ta, tb, a, num_sms, s);
+    case kEpiF32: return dispatch_major<BN, kEpiF32>(a_mn, b_mn, ta, tb, a, num_sms, s);
+    case kEpiF32Acc: return dispatch_major<BN, kEpiF32Acc>(a_mn, b_mn, ta, tb, a, num_sms, s);
+    case kEpiBF16Res: return dispatch_major<BN, kEpiBF16Res>(a_mn, b_mn, ta, tb, a, num_sms, s);
+  }
+  return -2;
+}
+
+// A(m,k) = a_mn ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_mn ? B[k*ldb + n] : B[n*ldb + k].
+// Returns 0 on success, a negative value for a bad argument, else a CUDA error code.
+int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn,
+              void* D, long long ldd, const void* R, long long ldr, int M, int N, int K, int epi,
+              float alpha, int* err, int num_sms, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return -3;
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
+  if ((lda * 2) % 16 || (ldb * 2) % 16) return -5;
+  const int esz = (epi == kEpiF32 || epi == kEpiF32Acc) ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(D) & 15) || (ldd * esz) % 16) return -6;
+  if (epi == kEpiBF16Res && ((reinterpret_cast<uintptr_t>(R) & 15) || (ldr * 2) % 16)) return -7;
+  const int BN = (N <= 128) ? 128 : 256;
+  CUtensorMap ta, tb;
+  int rc;
+  if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
+  else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
+  if (rc) return -100 - rc;
+  if (!b_mn) rc = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, BN);
+  else rc = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, 64);
+  if (rc) return -100 - rc;
+  GemmArgs a{M, N, K, D, ldd, reinterpret_cast<const __nv_bfloat16*>(R), ldr, alpha, err};
+  if (BN == 128) return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, num_sms, stream);
+  return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, num_sms, stream);
+}
+
+}  // namespace rb

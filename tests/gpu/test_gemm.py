@@ -1,0 +1,74 @@
+"""Numerics of the tcgen05 GEMM against a plain PyTorch fp32 reference of the same op."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, a_t, b_t):
+    A = (a.t() if a_t else a).float()
+    B = (b.t() if b_t else b).float()
+    return A @ B.t()
+
+
+def _mk(M, N, K, a_t, b_t, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn((K, M) if a_t else (M, K), device="cuda", generator=g).bfloat16()
+    b = torch.randn((K, N) if b_t else (N, K), device="cuda", generator=g).bfloat16()
+    return a, b
+
+
+SHAPES = [(128, 128, 64), (256, 512, 256), (384, 256, 1024), (1000, 296, 200), (136, 520, 72)]
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_bf16_out(M, N, K, a_t, b_t):
+    from resihp_megatron_b200.ops.gemm import gemm, error_state
+
+    a, b = _mk(M, N, K, a_t, b_t)
+    out = gemm(a, b, a_t=a_t, b_t=b_t)
+    ref = _ref(a, b, a_t, b_t)
+    torch.cuda.synchronize()
+    assert int(error_state()[0]) == 0
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-2 * scale + 1e-2, (err, scale)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1000, 296, 200)])
+def test_gemm_fp32_accumulate(M, N, K):
+    from resihp_megatron_b200.ops.gemm import gemm
+
+    a, b = _mk(M, N, K, True, True, seed=1)
+    base = torch.randn(M, N, device="cuda")
+    out = base.clone()
+    gemm(a, b, a_t=True, b_t=True, out=out, accumulate=True)
+    ref = base + _ref(a, b, True, True)
+    torch.cuda.synchronize()
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3), (out - ref).abs().max().item()
+    out2 = gemm(a, b, a_t=True, b_t=True, out_dtype=torch.float32, alpha=0.5)
+    assert torch.allclose(out2, 0.5 * _ref(a, b, True, True), rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_residual():
+    from resihp_megatron_b200.ops.gemm import gemm
+
+    a, b = _mk(512, 768, 384, False, False, seed=2)
+    r = torch.randn(512, 768, device="cuda").bfloat16()
+    out = gemm(a, b, residual=r)
+    ref = _ref(a, b, False, False) + r.float()
+    torch.cuda.synchronize()
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 2e-2
+
+
+def test_gemm_large_square():
+    from resihp_megatron_b200.ops.gemm import gemm
+
+    a, b = _mk(4096, 4096, 4096, False, False, seed=3)
+    out = gemm(a, b)
+    ref = _ref(a, b, False, False)
+    torch.cuda.synchronize()
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item(), err
