@@ -1,0 +1,254 @@
+#!/usr/bin/env python3
+"""Headline benchmark: Llama-3-8B-shaped pre-training step on N GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+Config (BASELINE config 2 shape): 32 layers, hidden 4096, GQA 32q/8kv heads, SwiGLU FFN
+14336, vocab 128256, seq 4096, bf16 compute with fp32 master weights and Adam, random
+N(0, 0.02) init, uniform random token ids (synthetic).  Weak scaling: 8 sequences per GPU
+per step (global batch 64 at 8 GPUs), micro-batch 1, gradient accumulation over the
+rest; for N > 1 data parallel with a sharded optimizer.
+
+Device timing: W untimed warm-up steps, then exactly K steps between a barrier +
+``torch.cuda.synchronize()`` on each side, timed with CUDA events on the launching stream;
+the slowest rank's time is used.  Every step touches > 100 GB (weights, gradients, optimizer
+state), far larger than the 126 MB L2, so no separate L2 flush is needed.  SM clocks and
+throttle reasons are sampled with ``nvidia-smi`` during the timed region.
+
+End-to-end number (``e2e``): the same K steps again through the public API
+``GPUTrainer.train_step``, which copies each step's ids/labels from pinned host memory to the
+device and reads the loss back to the host; timed on the host, max over ranks.
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "tokens/sec/box (device, max over ranks) pre/post reconfig; fault→commit s"
+SEQS_PER_GPU = 8
+BASELINE_PUBLISHED = None  # BASELINE.md publishes no GPU tokens/s for the reference
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--seqs-per-gpu", type=int, default=SEQS_PER_GPU)
+    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=None, help="override (testing only; result is marked invalid)")
+    return ap.parse_args()
+
+
+def reference_unavailable(args) -> None:
+    """The reference's GPU training path is Megatron-Core + Transformer Engine
+    (resihp/train/megatron_binding.py); neither is installed nor fetchable offline
+    (scripts/setup_megatron.sh clones Megatron-LM from GitHub)."""
+    why = None
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        import resihp  # noqa: F401
+        try:
+            import megatron.core  # noqa: F401
+        except Exception:
+            why = ("reference installed in baseline/_ref, but its only GPU training path (MegatronBinding) needs "
+                   "Megatron-Core + Transformer Engine, which are not installed and cannot be fetched offline; its "
+                   "runnable model is a float64 CPU MLP stack, not this config")
+    except Exception as e:  # noqa: BLE001
+        why = f"reference not importable from baseline/_ref: {e}"
+    if why is None:
+        why = "reference Megatron path present but not wired into this bench"
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons of the GPUs in use while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = set(indices)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                if int(f[0]) not in self.indices:
+                    continue
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def main() -> None:
+    args = _args()
+    if args.impl == "reference":
+        reference_unavailable(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from resihp_megatron_b200 import ops
+    from resihp_megatron_b200.models.config import get_config
+    from resihp_megatron_b200.train.gpu_trainer import GPUTrainer, init_distributed
+
+    rank, world, local = init_distributed()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    cfg = get_config(args.model, seq_len=args.seq)
+    if args.layers:
+        cfg = cfg.with_(layers=args.layers)
+    global_batch = args.seqs_per_gpu * world
+    group = dist.group.WORLD if world > 1 else None
+    trainer = GPUTrainer(cfg, global_batch=global_batch, micro_batch=args.micro_batch, seq_len=args.seq, seed=0,
+                         dp_group=group)
+    dev = trainer.device
+
+    # synthetic data: uniform random token ids, next-token labels, one batch per step
+    n_batches = args.warmup + args.steps
+    g = torch.Generator().manual_seed(1)
+    host_batches = []
+    for _ in range(min(n_batches, 4)):
+        seq = torch.randint(0, cfg.vocab_size, (global_batch, args.seq + 1), generator=g)
+        lo, hi = rank * trainer.local_batch, (rank + 1) * trainer.local_batch
+        ids = seq[lo:hi, :-1].contiguous().pin_memory()
+        lab = seq[lo:hi, 1:].contiguous().pin_memory()
+        host_batches.append((ids, lab))
+    dev_batches = [(i.to(dev), l.to(dev)) for i, l in host_batches]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up
+    for s in range(args.warmup):
+        trainer.step_device(*dev_batches[s % len(dev_batches)])
+    torch.cuda.synchronize()
+
+    # ---- device-timed region
+    sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    l0 = ops.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    loss = None
+    for s in range(args.steps):
+        loss = trainer.step_device(*dev_batches[s % len(dev_batches)])
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = ops.launches() - l0
+    clocks = sampler.stop() if sampler else None
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = trainer.tokens_per_step * args.steps
+    value = tokens / (ms_max / 1000.0)
+    last_loss = float(loss.item())
+
+    # ---- end-to-end region through the public API (H2D of inputs + D2H of the loss every step)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        ids, lab = host_batches[s % len(host_batches)]
+        trainer.train_step(ids, lab)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = tokens / float(te.item())
+    ids0, lab0 = host_batches[0]
+    h2d = ids0.numel() * ids0.element_size() + lab0.numel() * lab0.element_size()
+
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": (value / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None,
+            "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
+            "config": {
+                "model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
+                "global_batch": global_batch,
+                "seq_len": args.seq,
+                "micro_batch": args.micro_batch,
+                "parallelism": "tp1pp1dp1" if world == 1 else f"dp{world}-zero1",
+                "l2": "inputs larger than L2 (each step touches >100 GB of weights/grads/optimizer state)",
+                "params": cfg.num_params(),
+                "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * value / world / 1e12,
+            },
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": 4 * world},
+            "gpu_launches": launches,
+            "loss": last_loss,
+            "impl": "ours",
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,255 @@
+"""Llama-style decoder on this package's sm_100a kernels: explicit forward and backward.
+
+The model is functional: weights live in a ``FlatParams`` (bf16 compute copy + fp32 master,
+gradient and Adam moments), activations in buffers allocated once for one micro-batch, and
+``forward_backward`` runs one micro-batch and accumulates fp32 gradients.  No autograd, no
+``nn.Module`` and no allocation inside a step, so a step is a fixed sequence of kernel
+launches (capturable in a CUDA graph).
+
+Per layer (``T`` tokens of one micro-batch):
+
+    h   = rmsnorm(x)                 qkv = h Wqkv^T          rope(q, k)
+    o   = attention(q, k, v)         x2  = x + o Wo^T        (residual fused in the GEMM epilogue)
+    h2  = rmsnorm(x2)                gu  = h2 W13^T          a = silu(gate) * up
+    x'  = x2 + a W2^T
+
+Saved for backward: x, x2, qkv (after RoPE), o, lse, gu and the two rstd vectors; h, h2 and
+``a`` are recomputed (cheap, bandwidth bound), which keeps activations at ~23 bytes x hidden
+per token per layer.  Gradients of every GEMM use the MN-major operand modes of the GEMM
+kernel, so no transpose is materialised.
+
+The reference framework delegates the GPU model to Megatron-Core
+(``resihp/runtime/megatron_runtime.py:162``); its CPU semantics oracle is
+``resihp/runtime/reference_model.py``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from .config import GPTConfig
+from .params import FlatParams, ParamSpec
+
+
+def layer_param_specs(cfg: GPTConfig, layer: int, tp_rank: int = 0, tp_size: int = 1) -> list[ParamSpec]:
+    """Parameters of one decoder layer (column-parallel qkv / w13, row-parallel wo / w2)."""
+    from ..utils.intervals import even_split
+
+    H, D, F = cfg.hidden, cfg.head_dim, cfg.ffn
+    qh = even_split(cfg.heads, tp_size)[tp_rank]
+    kh = even_split(cfg.kv_heads, tp_size)[tp_rank]
+    fr = even_split(F, tp_size)[tp_rank]
+    nq, nk, nf = qh[1] - qh[0], kh[1] - kh[0], fr[1] - fr[0]
+    p = f"layers.{layer}."
+    if tp_size == 1:
+        return [
+            ParamSpec(p + "attn_norm", (H,), init="ones"),
+            ParamSpec(p + "wqkv", ((cfg.heads + 2 * cfg.kv_heads) * D, H)),
+            ParamSpec(p + "wo", (H, cfg.heads * D)),
+            ParamSpec(p + "mlp_norm", (H,), init="ones"),
+            ParamSpec(p + "w13", (2 * F, H)),
+            ParamSpec(p + "w2", (H, F)),
+        ]
+    # Sharded: q/k/v and gate/up are stored as separate logical tensors so each rank's slice
+    # is a contiguous row range of every logical tensor.
+    return [
+        ParamSpec(p + "attn_norm", (H,), init="ones"),
+        ParamSpec(p + "wq", (nq * D, H), (cfg.heads * D, H), 0, (qh[0] * D, qh[1] * D)),
+        ParamSpec(p + "wk", (nk * D, H), (cfg.kv_heads * D, H), 0, (kh[0] * D, kh[1] * D)),
+        ParamSpec(p + "wv", (nk * D, H), (cfg.kv_heads * D, H), 0, (kh[0] * D, kh[1] * D)),
+        ParamSpec(p + "wo", (H, nq * D), (H, cfg.heads * D), 1, (qh[0] * D, qh[1] * D)),
+        ParamSpec(p + "mlp_norm", (H,), init="ones"),
+        ParamSpec(p + "w1", (nf, H), (F, H), 0, fr),
+        ParamSpec(p + "w3", (nf, H), (F, H), 0, fr),
+        ParamSpec(p + "w2", (H, nf), (H, F), 1, fr),
+    ]
+
+
+def model_param_specs(cfg: GPTConfig, layers: range | None = None, first: bool = True, last: bool = True):
+    specs: list[ParamSpec] = []
+    if first:
+        specs.append(ParamSpec("embed", (cfg.vocab_size, cfg.hidden)))
+    for l in (layers if layers is not None else range(cfg.layers)):
+        specs.extend(layer_param_specs(cfg, l))
+    if last:
+        specs.append(ParamSpec("final_norm", (cfg.hidden,), init="ones"))
+        specs.append(ParamSpec("lm_head", (cfg.vocab_size, cfg.hidden)))
+    return specs
+
+
+class LlamaModel:
+    """Single-device Llama decoder (optionally a contiguous layer range of it, for pipelines)."""
+
+    def __init__(self, cfg: GPTConfig, device="cuda", *, micro_batch: int = 1, seq_len: int | None = None,
+                 seed: int = 0, layers: range | None = None, first: bool = True, last: bool = True,
+                 shard_rank: int = 0, shard_count: int = 1):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.mb = micro_batch
+        self.S = seq_len or cfg.seq_len
+        self.T = self.mb * self.S
+        self.layer_ids = list(layers if layers is not None else range(cfg.layers))
+        self.first, self.last = first, last
+        self.params = FlatParams(model_param_specs(cfg, self.layer_ids, first, last), self.device,
+                                 shard_rank=shard_rank, shard_count=shard_count)
+        self.params.initialize(seed, cfg.init_std)
+        self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
+        self._alloc()
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc(self) -> None:
+        cfg, T, dev = self.cfg, self.T, self.device
+        H, F, V = cfg.hidden, cfg.ffn, cfg.vocab_size
+        L = len(self.layer_ids)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.xs = [torch.empty(T, H, **bf) for _ in range(L + 1)]
+        self.x2 = [torch.empty(T, H, **bf) for _ in range(L)]
+        self.qkv = [torch.empty(T, cfg.qkv_rows, **bf) for _ in range(L)]
+        self.o = [torch.empty(T, cfg.heads * cfg.head_dim, **bf) for _ in range(L)]
+        self.lse = [torch.empty(self.mb, cfg.heads, self.S, **f32) for _ in range(L)]
+        self.gu = [torch.empty(T, 2 * F, **bf) for _ in range(L)]
+        self.rstd1 = [torch.empty(T, **f32) for _ in range(L)]
+        self.rstd2 = [torch.empty(T, **f32) for _ in range(L)]
+        self.ws_h = torch.empty(T, H, **bf)
+        self.ws_a = torch.empty(T, F, **bf)
+        self.ws_da = torch.empty(T, F, **bf)
+        self.ws_dh = torch.empty(T, H, **bf)
+        self.ws_dx = torch.empty(T, H, **bf)
+        self.ws_dx2 = torch.empty(T, H, **bf)
+        self.ws_do = torch.empty(T, cfg.heads * cfg.head_dim, **bf)
+        self.ws_dqkv = torch.empty(T, cfg.qkv_rows, **bf)
+        if self.last:
+            self.hf = torch.empty(T, H, **bf)
+            self.rstd_f = torch.empty(T, **f32)
+            self.logits = torch.empty(T, V, **bf)
+        self.loss_acc = torch.zeros((), **f32)
+
+    def activation_bytes(self) -> int:
+        tot = 0
+        for name, v in vars(self).items():
+            if isinstance(v, torch.Tensor) and name not in ("cos", "sin"):
+                tot += v.numel() * v.element_size()
+            elif isinstance(v, list) and v and isinstance(v[0], torch.Tensor):
+                tot += sum(t.numel() * t.element_size() for t in v)
+        return tot
+
+    # ------------------------------------------------------------------ helpers
+    def _views(self, i: int):
+        cfg = self.cfg
+        D = cfg.head_dim
+        q = self.qkv[i][:, : cfg.heads * D]
+        k = self.qkv[i][:, cfg.heads * D: (cfg.heads + cfg.kv_heads) * D]
+        v = self.qkv[i][:, (cfg.heads + cfg.kv_heads) * D:]
+        return q, k, v
+
+    def _attn_kw(self):
+        c = self.cfg
+        return dict(batch=self.mb, seq=self.S, heads=c.heads, kv_heads=c.kv_heads, head_dim=c.head_dim)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, ids: torch.Tensor | None = None, x_in: torch.Tensor | None = None) -> torch.Tensor:
+        """Run the layers; returns the last residual stream ([T, H] bf16)."""
+        cfg, P = self.cfg, self.params
+        if self.first:
+            ops.embedding_fwd(ids, P.w("embed"), out=self.xs[0])
+        else:
+            self.xs[0].copy_(x_in)
+        for i, l in enumerate(self.layer_ids):
+            p = f"layers.{l}."
+            x = self.xs[i]
+            h, r1 = self._rmsnorm(x, P.w(p + "attn_norm"), self.ws_h, self.rstd1[i])
+            ops.gemm(h, P.w(p + "wqkv"), out=self.qkv[i])
+            q, k, v = self._views(i)
+            ops.rope_(q, cfg.heads, cfg.head_dim, self.cos, self.sin, self.S)
+            ops.rope_(k, cfg.kv_heads, cfg.head_dim, self.cos, self.sin, self.S)
+            self._attention_fwd(i, q, k, v)
+            ops.gemm(self.o[i], P.w(p + "wo"), residual=x, out=self.x2[i])
+            h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])
+            ops.gemm(h2, P.w(p + "w13"), out=self.gu[i])
+            ops.swiglu_fwd(self.gu[i], out=self.ws_a)
+            ops.gemm(self.ws_a, P.w(p + "w2"), residual=self.x2[i], out=self.xs[i + 1])
+        return self.xs[-1]
+
+    def _rmsnorm(self, x, w, out, rstd):
+        ops.ext().rmsnorm_fwd(x, w, out, rstd, float(self.cfg.norm_eps))
+        ops.count(1)
+        return out, rstd
+
+    def _attention_fwd(self, i, q, k, v):
+        ops.ext().attention_fwd(q, k, v, self.o[i], self.lse[i], self.mb, self.S, self.cfg.heads, self.cfg.kv_heads,
+                                self.cfg.head_dim, self.cfg.head_dim ** -0.5, True)
+        ops.count(1)
+
+    def head_loss(self, labels: torch.Tensor, grad_scale: float) -> torch.Tensor:
+        """Final norm + LM head + cross-entropy; leaves dlogits in ``self.logits``."""
+        P = self.params
+        self._rmsnorm(self.xs[-1], P.w("final_norm"), self.hf, self.rstd_f)
+        ops.gemm(self.hf, P.w("lm_head"), out=self.logits)
+        loss = ops.cross_entropy_(self.logits, labels, grad_scale=grad_scale)
+        return loss
+
+    # ------------------------------------------------------------------ backward
+    def backward(self, ids: torch.Tensor | None = None, dx_top: torch.Tensor | None = None) -> torch.Tensor:
+        """Backward of the layers given dlogits (last stage) or ``dx_top`` (earlier stages);
+        returns the gradient of the stage input."""
+        cfg, P = self.cfg, self.params
+        dx = self.ws_dx
+        if self.last:
+            ops.gemm(self.logits, P.w("lm_head"), b_t=True, out=self.ws_dh)
+            ops.gemm(self.logits, self.hf, a_t=True, b_t=True, out=P.g("lm_head"), accumulate=True)
+            ops.rmsnorm_bwd(self.xs[-1], P.w("final_norm"), self.rstd_f, self.ws_dh, P.g("final_norm"), out=dx)
+        else:
+            dx.copy_(dx_top)
+        for i in reversed(range(len(self.layer_ids))):
+            l = self.layer_ids[i]
+            p = f"layers.{l}."
+            # MLP
+            ops.swiglu_fwd(self.gu[i], out=self.ws_a)
+            ops.gemm(dx, P.w(p + "w2"), b_t=True, out=self.ws_da)
+            ops.gemm(dx, self.ws_a, a_t=True, b_t=True, out=P.g(p + "w2"), accumulate=True)
+            ops.swiglu_bwd(self.gu[i], self.ws_da, out=self.gu[i])
+            dgu = self.gu[i]
+            h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])
+            ops.gemm(dgu, P.w(p + "w13"), b_t=True, out=self.ws_dh)
+            ops.gemm(dgu, h2, a_t=True, b_t=True, out=P.g(p + "w13"), accumulate=True)
+            ops.rmsnorm_bwd(self.x2[i], P.w(p + "mlp_norm"), self.rstd2[i], self.ws_dh, P.g(p + "mlp_norm"), dres=dx,
+                            out=self.ws_dx2)
+            dx2 = self.ws_dx2
+            # attention
+            ops.gemm(dx2, P.w(p + "wo"), b_t=True, out=self.ws_do)
+            ops.gemm(dx2, self.o[i], a_t=True, b_t=True, out=P.g(p + "wo"), accumulate=True)
+            q, k, v = self._views(i)
+            D = cfg.head_dim
+            dq = self.ws_dqkv[:, : cfg.heads * D]
+            dk = self.ws_dqkv[:, cfg.heads * D: (cfg.heads + cfg.kv_heads) * D]
+            dv = self.ws_dqkv[:, (cfg.heads + cfg.kv_heads) * D:]
+            ops.attention_bwd(q, k, v, self.o[i], self.ws_do, self.lse[i], dq, dk, dv, **self._attn_kw())
+            ops.rope_(dq, cfg.heads, D, self.cos, self.sin, self.S, inverse=True)
+            ops.rope_(dk, cfg.kv_heads, D, self.cos, self.sin, self.S, inverse=True)
+            h, _ = self._rmsnorm(self.xs[i], P.w(p + "attn_norm"), self.ws_h, self.rstd1[i])
+            ops.gemm(self.ws_dqkv, P.w(p + "wqkv"), b_t=True, out=self.ws_dh)
+            ops.gemm(self.ws_dqkv, h, a_t=True, b_t=True, out=P.g(p + "wqkv"), accumulate=True)
+            ops.rmsnorm_bwd(self.xs[i], P.w(p + "attn_norm"), self.rstd1[i], self.ws_dh, P.g(p + "attn_norm"),
+                            dres=dx2, out=dx)
+        if self.first:
+            ops.embedding_bwd(ids, dx, P.g("embed"))
+        return dx
+
+    # ------------------------------------------------------------------ training step pieces
+    def forward_backward(self, ids: torch.Tensor, labels: torch.Tensor, grad_scale: float) -> torch.Tensor:
+        """One micro-batch on a single device holding every layer; accumulates gradients and
+        adds the summed token loss into ``self.loss_acc``."""
+        self.forward(ids)
+        loss = self.head_loss(labels, grad_scale)
+        self.loss_acc += loss.sum()
+        self.backward(ids)
+        return self.loss_acc
+
+    def optimizer_step(self, lr: float, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
+                       grad_scale: float = 1.0) -> None:
+        P = self.params
+        P.step += 1
+        ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, lr=lr, beta1=betas[0], beta2=betas[1],
+                      eps=eps, weight_decay=weight_decay, step=P.step, grad_scale=grad_scale, zero_grad=True)

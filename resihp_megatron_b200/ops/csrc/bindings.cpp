@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
 #include <mutex>
 #include <unordered_map>
 
@@ -93,6 +94,180 @@ void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, to
   TORCH_CHECK(rc == 0, "gemm_bf16 failed with code ", rc);
 }
 
+
+#define CHECK_BF16(t) TORCH_CHECK((t).is_cuda() && (t).scalar_type() == torch::kBFloat16 && (t).is_contiguous(), #t " must be a contiguous CUDA bf16 tensor")
+#define CHECK_F32(t) TORCH_CHECK((t).is_cuda() && (t).scalar_type() == torch::kFloat32 && (t).is_contiguous(), #t " must be a contiguous CUDA fp32 tensor")
+#define RB_CALL(expr, name)                                        \
+  do {                                                             \
+    const int rc__ = (expr);                                       \
+    TORCH_CHECK(rc__ == 0, name " failed with code ", rc__);       \
+  } while (0)
+
+static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+// y = rmsnorm(x) * w ; returns rstd [T]
+void rmsnorm_fwd(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y, torch::Tensor& rstd, double eps) {
+  CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(y); CHECK_F32(rstd);
+  const int H = x.size(-1);
+  const int T = x.numel() / H;
+  const c10::cuda::CUDAGuard g(x.device());
+  RB_CALL(rb::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), T, H,
+                          static_cast<float>(eps), cur_stream()), "rmsnorm_fwd");
+}
+
+void rmsnorm_bwd(const torch::Tensor& x, const torch::Tensor& w, const torch::Tensor& rstd, const torch::Tensor& dy,
+                 const c10::optional<torch::Tensor>& dres, torch::Tensor& dx, torch::Tensor& dw, bool accumulate) {
+  CHECK_BF16(x); CHECK_BF16(w); CHECK_F32(rstd); CHECK_BF16(dy); CHECK_BF16(dx); CHECK_F32(dw);
+  const int H = x.size(-1);
+  const int T = x.numel() / H;
+  const void* dr = nullptr;
+  if (dres.has_value()) { CHECK_BF16(*dres); dr = dres->data_ptr(); }
+  const c10::cuda::CUDAGuard g(x.device());
+  auto part = torch::empty({rb::rmsnorm_bwd_blocks(T), H}, x.options().dtype(torch::kFloat32));
+  RB_CALL(rb::rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), dr, dx.data_ptr(),
+                          dw.data_ptr<float>(), accumulate ? 1 : 0, part.data_ptr<float>(), T, H, cur_stream()),
+          "rmsnorm_bwd");
+}
+
+// In-place rotary embedding on a [T, heads * D] view with row stride (elements).
+void rope(torch::Tensor& t, int64_t row_stride, int64_t heads, int64_t D, const torch::Tensor& cos_t,
+          const torch::Tensor& sin_t, int64_t S, int64_t T, bool inverse) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16, "rope: bf16 CUDA tensor expected");
+  CHECK_F32(cos_t); CHECK_F32(sin_t);
+  const c10::cuda::CUDAGuard g(t.device());
+  RB_CALL(rb::rope_apply(t.data_ptr(), row_stride, heads, D, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), S, T,
+                         inverse ? 1 : 0, cur_stream()), "rope");
+}
+
+void swiglu_fwd(const torch::Tensor& gu, torch::Tensor& a) {
+  CHECK_BF16(gu); CHECK_BF16(a);
+  const int F = a.size(-1);
+  const int T = a.numel() / F;
+  TORCH_CHECK(gu.numel() == 2LL * T * F, "swiglu_fwd: gu must be [T, 2F]");
+  const c10::cuda::CUDAGuard g(gu.device());
+  RB_CALL(rb::swiglu_fwd(gu.data_ptr(), a.data_ptr(), T, F, cur_stream()), "swiglu_fwd");
+}
+
+void swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& da, torch::Tensor& dgu) {
+  CHECK_BF16(gu); CHECK_BF16(da); CHECK_BF16(dgu);
+  const int F = da.size(-1);
+  const int T = da.numel() / F;
+  const c10::cuda::CUDAGuard g(gu.device());
+  RB_CALL(rb::swiglu_bwd(gu.data_ptr(), da.data_ptr(), dgu.data_ptr(), T, F, cur_stream()), "swiglu_bwd");
+}
+
+void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& E, torch::Tensor& x) {
+  TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.is_contiguous(), "ids must be contiguous int64");
+  CHECK_BF16(E); CHECK_BF16(x);
+  const c10::cuda::CUDAGuard g(E.device());
+  RB_CALL(rb::embedding_fwd(ids.data_ptr<int64_t>(), E.data_ptr(), x.data_ptr(), ids.numel(), E.size(1), E.size(0),
+                            err_ptr(E), cur_stream()), "embedding_fwd");
+}
+
+// Deterministic dE += scatter(dx) using a stable sort of the ids.
+void embedding_bwd(const torch::Tensor& ids, const torch::Tensor& dx, torch::Tensor& dE) {
+  CHECK_BF16(dx); CHECK_F32(dE);
+  const c10::cuda::CUDAGuard g(dx.device());
+  auto flat = ids.reshape({-1});
+  auto sorted = torch::sort(flat, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+  auto vals = std::get<0>(sorted);
+  auto order = std::get<1>(sorted).contiguous();
+  auto uc = torch::unique_consecutive(vals, /*return_inverse=*/false, /*return_counts=*/true);
+  auto uniq = std::get<0>(uc).contiguous();
+  auto counts = std::get<2>(uc);
+  auto starts = torch::zeros({uniq.numel() + 1}, counts.options());
+  starts.narrow(0, 1, uniq.numel()).copy_(torch::cumsum(counts, 0));
+  RB_CALL(rb::embedding_bwd(order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), uniq.data_ptr<int64_t>(),
+                            uniq.numel(), dx.data_ptr(), dE.data_ptr<float>(), dE.size(1), cur_stream()),
+          "embedding_bwd");
+}
+
+void adam_step(torch::Tensor& p, torch::Tensor& grad, torch::Tensor& m, torch::Tensor& v,
+               const c10::optional<torch::Tensor>& p_bf16, double lr, double b1, double b2, double eps, double wd,
+               bool decoupled, int64_t step, double grad_scale, bool zero_grad) {
+  CHECK_F32(p); CHECK_F32(grad); CHECK_F32(m); CHECK_F32(v);
+  void* pb = nullptr;
+  if (p_bf16.has_value()) { CHECK_BF16(*p_bf16); TORCH_CHECK(p_bf16->numel() == p.numel()); pb = p_bf16->data_ptr(); }
+  const double bc1 = 1.0 - std::pow(b1, static_cast<double>(step));
+  const double bc2 = 1.0 - std::pow(b2, static_cast<double>(step));
+  const c10::cuda::CUDAGuard g(p.device());
+  RB_CALL(rb::adam_step(p.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), pb,
+                        p.numel(), lr, b1, b2, eps, wd, decoupled ? 1 : 0, static_cast<float>(bc1),
+                        static_cast<float>(std::sqrt(bc2)), static_cast<float>(grad_scale), zero_grad ? 1 : 0,
+                        cur_stream()), "adam_step");
+}
+
+// Deterministic sum of squares of a flat fp32 buffer (fixed 296-way split, fixed order).
+torch::Tensor sumsq(const torch::Tensor& x) {
+  CHECK_F32(x);
+  const c10::cuda::CUDAGuard g(x.device());
+  constexpr int kParts = 296;
+  auto part = torch::empty({kParts}, x.options());
+  RB_CALL(rb::sumsq_partial(x.data_ptr<float>(), x.numel(), part.data_ptr<float>(), kParts, cur_stream()), "sumsq");
+  return part.sum();
+}
+
+// Fused cross-entropy: returns per-row loss (fp32); overwrites logits with dlogits when write_grad.
+void cross_entropy(torch::Tensor& logits, const torch::Tensor& labels, torch::Tensor& loss,
+                   const c10::optional<torch::Tensor>& lse, int64_t v0, double grad_scale, int64_t ignore_index,
+                   bool write_grad) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kBFloat16 && logits.dim() == 2 &&
+              logits.stride(1) == 1, "logits must be a 2-D bf16 CUDA tensor with contiguous rows");
+  TORCH_CHECK(labels.scalar_type() == torch::kInt64 && labels.is_contiguous(), "labels must be int64");
+  CHECK_F32(loss);
+  float* lp = nullptr;
+  if (lse.has_value()) { CHECK_F32(*lse); lp = lse->data_ptr<float>(); }
+  const c10::cuda::CUDAGuard g(logits.device());
+  RB_CALL(rb::cross_entropy_fwd_bwd(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(),
+                                    loss.data_ptr<float>(), lp, logits.size(0), logits.size(1), v0, grad_scale,
+                                    ignore_index, write_grad ? 1 : 0, cur_stream()), "cross_entropy");
+}
+
+static rb::AttnArgs attn_args(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                              torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                              double scale, bool causal) {
+  rb::AttnArgs a;
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr();
+  a.q_stride = q.stride(0); a.k_stride = k.stride(0); a.v_stride = v.stride(0);
+  a.o = o.data_ptr(); a.o_stride = o.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.B = B; a.S = S; a.Hq = Hq; a.Hkv = Hkv; a.scale = scale; a.causal = causal ? 1 : 0;
+  return a;
+}
+
+// q/k/v/o: 2-D [B*S, heads*D] views with contiguous rows (row stride may exceed heads*D).
+void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
+                   torch::Tensor& lse, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, double scale,
+                   bool causal) {
+  for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
+                "attention operands must be 2-D bf16 CUDA views with contiguous rows");
+  CHECK_F32(lse);
+  const c10::cuda::CUDAGuard g(q.device());
+  auto a = attn_args(q, k, v, o, lse, B, S, Hq, Hkv, scale, causal);
+  RB_CALL(rb::attention_fwd_mma(a, D, cur_stream()), "attention_fwd");
+}
+
+void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
+                   const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& delta, torch::Tensor& dq,
+                   torch::Tensor& dk, torch::Tensor& dv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
+                   double scale, bool causal) {
+  for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o, &dout, &dq, &dk, &dv})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
+                "attention operands must be 2-D bf16 CUDA views with contiguous rows");
+  CHECK_F32(lse); CHECK_F32(delta);
+  const c10::cuda::CUDAGuard g(q.device());
+  rb::AttnBwdArgs a;
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr(); a.dout = dout.data_ptr();
+  a.q_stride = q.stride(0); a.k_stride = k.stride(0); a.v_stride = v.stride(0); a.o_stride = o.stride(0);
+  a.do_stride = dout.stride(0);
+  a.lse = lse.data_ptr<float>(); a.delta = delta.data_ptr<float>();
+  a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
+  a.dq_stride = dq.stride(0); a.dk_stride = dk.stride(0); a.dv_stride = dv.stride(0);
+  a.B = B; a.S = S; a.Hq = Hq; a.Hkv = Hkv; a.scale = scale; a.causal = causal ? 1 : 0;
+  RB_CALL(rb::attention_bwd_mma(a, D, cur_stream()), "attention_bwd");
+}
+
 torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(device)); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -100,4 +275,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_t"), py::arg("b"), py::arg("b_t"),
         py::arg("out"), py::arg("epi"), py::arg("alpha"), py::arg("residual") = py::none());
   m.def("error_state", &error_state, "per-device kernel error words");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("adam_step", &adam_step);
+  m.def("sumsq", &sumsq);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
 }

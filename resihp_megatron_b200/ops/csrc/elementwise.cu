@@ -1,0 +1,444 @@
+// Bandwidth-bound kernels of the decoder: RMSNorm (fwd / bwd), rotary embedding, SwiGLU,
+// token embedding gather / deterministic scatter, and the fused Adam update.
+//
+// All kernels move 16-byte vectors (8 bf16 or 4 fp32) and keep reductions deterministic:
+// cross-row sums (RMSNorm weight gradient, embedding gradient) are computed by fixed
+// assignments of rows to CTAs and summed in a fixed order, never with float atomics, so a
+// result does not depend on scheduling.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace rb {
+
+namespace {
+
+__device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = (l < THREADS / 32) ? sh[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (l == 0) sh[0] = t;
+  }
+  __syncthreads();
+  t = sh[0];
+  __syncthreads();
+  return t;
+}
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 4;  // up to 256 * 4 * 8 = 8192 features per row
+
+// y = x * rsqrt(mean(x^2) + eps) * w ; rstd saved for the backward pass.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   __nv_bfloat16* __restrict__ y,
+                                                                   float* __restrict__ rstd, int H, float eps) {
+  __shared__ float sh[32];
+  const long long row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * H;
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+  const int nvec = H / 8;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (threadIdx.x + i * kNormThreads);
+    if (c < nvec) {
+      load_bf16x8(xr + c * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum<kNormThreads>(ss, sh);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (threadIdx.x + i * kNormThreads);
+    if (c < nvec) {
+      float wv[8];
+      load_bf16x8(w + c * 8, wv);
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * r * wv[j];
+      store_bf16x8(y + row * H + c * 8, o);
+    }
+  }
+}
+
+// dx = rstd * (w*dy - xhat * mean(xhat * w*dy)) (+ dres) ; per-CTA partial dw over a fixed
+// block of ROWS rows written to dw_part[blockIdx.x, :] (fp32), reduced later in order.
+constexpr int kNormBwdRows = 32;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy,
+    const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T,
+    int H) {
+  __shared__ float sh[32];
+  const int nvec = H / 8;
+  float wv[kNormMaxVec][8];
+  float dwacc[kNormMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
+    if (c < nvec) load_bf16x8(w + c * 8, wv[i]);
+  }
+  const int r0 = blockIdx.x * kNormBwdRows;
+  const int r1 = min(T, r0 + kNormBwdRows);
+  for (int row = r0; row < r1; ++row) {
+    const long long off = static_cast<long long>(row) * H;
+    const float r = rstd[row];
+    float xh[kNormMaxVec][8], g[kNormMaxVec][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int c = threadIdx.x + i * kNormThreads;
+      if (c < nvec) {
+        load_bf16x8(x + off + c * 8, xh[i]);
+        load_bf16x8(dy + off + c * 8, g[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[i][j] *= r;
+          dwacc[i][j] += g[i][j] * xh[i][j];
+          g[i][j] *= wv[i][j];
+          dot += g[i][j] * xh[i][j];
+        }
+      }
+    }
+    dot = block_sum<kNormThreads>(dot, sh) / H;
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int c = threadIdx.x + i * kNormThreads;
+      if (c < nvec) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = r * (g[i][j] - xh[i][j] * dot);
+        if (dres != nullptr) {
+          float d[8];
+          load_bf16x8(dres + off + c * 8, d);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += d[j];
+        }
+        store_bf16x8(dx + off + c * 8, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    if (c < nvec) {
+      float4* dst = reinterpret_cast<float4*>(dw_part + static_cast<long long>(blockIdx.x) * H + c * 8);
+      dst[0] = make_float4(dwacc[i][0], dwacc[i][1], dwacc[i][2], dwacc[i][3]);
+      dst[1] = make_float4(dwacc[i][4], dwacc[i][5], dwacc[i][6], dwacc[i][7]);
+    }
+  }
+}
+
+// out[c] (+)= sum_{b < nb} part[b, c], summed in increasing b.
+__global__ void colsum_kernel(const float* __restrict__ part, float* __restrict__ out, int nb, int H,
+                              int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  float s = 0.f;
+  for (int b = 0; b < nb; ++b) s += part[static_cast<long long>(b) * H + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+// Rotary embedding, rotate-half convention, in place on a [T, heads, D] strided view.
+// cos/sin tables are [S, D/2] fp32; token t uses position pos0 + (t % S).
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ q, long long row_stride, int heads, int D,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t, int S, int T,
+                            int inverse) {
+  const int half = D / 2;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(T) * heads * (half / 2);
+  if (idx >= total) return;
+  const int pairs = half / 2;  // two rotation pairs per thread
+  const int p = idx % pairs;
+  const long long th = idx / pairs;
+  const int h = th % heads;
+  const int t = th / heads;
+  const int pos = t % S;
+  __nv_bfloat16* base = q + static_cast<long long>(t) * row_stride + static_cast<long long>(h) * D;
+  const int i = 2 * p;
+  const float2 lo = unpack_bf16x2(*reinterpret_cast<uint32_t*>(base + i));
+  const float2 hi = unpack_bf16x2(*reinterpret_cast<uint32_t*>(base + half + i));
+  const float c0 = cos_t[pos * half + i], c1 = cos_t[pos * half + i + 1];
+  float s0 = sin_t[pos * half + i], s1 = sin_t[pos * half + i + 1];
+  if (inverse) {
+    s0 = -s0;
+    s1 = -s1;
+  }
+  // (x1, x2) -> (x1 c - x2 s, x2 c + x1 s)
+  *reinterpret_cast<uint32_t*>(base + i) = pack_bf16x2(lo.x * c0 - hi.x * s0, lo.y * c1 - hi.y * s1);
+  *reinterpret_cast<uint32_t*>(base + half + i) = pack_bf16x2(hi.x * c0 + lo.x * s0, hi.y * c1 + lo.y * s1);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
+
+// gu = [T, 2F] with gate in [:, :F] and up in [:, F:]; a = silu(gate) * up.
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int T,
+                                  int F) {
+  const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  const int nv = F / 8;
+  if (idx >= static_cast<long long>(T) * nv) return;
+  const int t = idx / nv, c = idx % nv;
+  float g[8], u[8], o[8];
+  load_bf16x8(gu + static_cast<long long>(t) * 2 * F + c * 8, g);
+  load_bf16x8(gu + static_cast<long long>(t) * 2 * F + F + c * 8, u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = silu(g[j]) * u[j];
+  store_bf16x8(a + static_cast<long long>(t) * F + c * 8, o);
+}
+
+// dgu[:, :F] = da * up * silu'(gate) ; dgu[:, F:] = da * silu(gate).  May run in place (dgu == gu).
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* __restrict__ da,
+                                  __nv_bfloat16* dgu, int T, int F) {
+  const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  const int nv = F / 8;
+  if (idx >= static_cast<long long>(T) * nv) return;
+  const int t = idx / nv, c = idx % nv;
+  const long long gofs = static_cast<long long>(t) * 2 * F + c * 8;
+  float g[8], u[8], d[8], dg[8], du[8];
+  load_bf16x8(gu + gofs, g);
+  load_bf16x8(gu + gofs + F, u);
+  load_bf16x8(da + static_cast<long long>(t) * F + c * 8, d);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float sg = 1.f / (1.f + __expf(-g[j]));
+    const float s = g[j] * sg;
+    du[j] = d[j] * s;
+    dg[j] = d[j] * u[j] * (sg * (1.f + g[j] * (1.f - sg)));
+  }
+  store_bf16x8(dgu + gofs, dg);
+  store_bf16x8(dgu + gofs + F, du);
+}
+
+// x[t, :] = E[ids[t], :]
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
+                                     __nv_bfloat16* __restrict__ x, int T, int H, int V, int* err) {
+  const int t = blockIdx.x;
+  long long id = ids[t];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) record_error(err, kErrBadArg);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(E + id * H);
+  uint4* dst = reinterpret_cast<uint4*>(x + static_cast<long long>(t) * H);
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+// Deterministic embedding gradient.  `order` lists token positions sorted by (id, position)
+// and `starts[k]..starts[k+1]` is the run of positions of the k-th distinct id `uniq[k]`.
+// dE[uniq[k], :] += sum over the run, in position order.
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ order, const int64_t* __restrict__ starts,
+                                     const int64_t* __restrict__ uniq, const __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ dE, int H) {
+  const int k = blockIdx.x;
+  const long long s0 = starts[k], s1 = starts[k + 1];
+  const long long id = uniq[k];
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (long long s = s0; s < s1; ++s) {
+      float v[8];
+      load_bf16x8(dx + order[s] * H + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+    float4* dst = reinterpret_cast<float4*>(dE + id * H + c);
+    float4 a = dst[0], b = dst[1];
+    a.x += acc[0]; a.y += acc[1]; a.z += acc[2]; a.w += acc[3];
+    b.x += acc[4]; b.y += acc[5]; b.z += acc[6]; b.w += acc[7];
+    dst[0] = a;
+    dst[1] = b;
+  }
+}
+
+// Adam(W) on flat fp32 master weights, with the gradient scale (e.g. 1 / global tokens) and
+// the bf16 model copy fused in.  Formula order follows torch.optim.Adam (single tensor):
+//   g = grad * scale (+ wd * p for classic L2) ; m = lerp(m, g, 1-b1) ; v = b2 v + (1-b2) g^2
+//   p -= lr / bc1 * m / (sqrt(v) / sqrt(bc2) + eps)
+__global__ void adam_kernel(float* __restrict__ p, const float* __restrict__ grad, float* __restrict__ m,
+                            float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, long long n, float lr,
+                            float b1, float b2, float eps, float wd, int decoupled, float bc1, float bc2_sqrt,
+                            float grad_scale, int zero_grad) {
+  const long long i4 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i4 >= n) return;
+  const float step_size = lr / bc1;
+  const int cnt = (n - i4) >= 4 ? 4 : static_cast<int>(n - i4);
+  float pp[4], gg[4], mm[4], vv[4];
+  if (cnt == 4) {
+    *reinterpret_cast<float4*>(pp) = *reinterpret_cast<const float4*>(p + i4);
+    *reinterpret_cast<float4*>(gg) = *reinterpret_cast<const float4*>(grad + i4);
+    *reinterpret_cast<float4*>(mm) = *reinterpret_cast<const float4*>(m + i4);
+    *reinterpret_cast<float4*>(vv) = *reinterpret_cast<const float4*>(v + i4);
+  } else {
+    for (int j = 0; j < cnt; ++j) {
+      pp[j] = p[i4 + j]; gg[j] = grad[i4 + j]; mm[j] = m[i4 + j]; vv[j] = v[i4 + j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float g = gg[j] * grad_scale;
+    if (wd != 0.f) {
+      if (decoupled) pp[j] *= (1.f - lr * wd);
+      else g = g + wd * pp[j];
+    }
+    mm[j] = mm[j] + (1.f - b1) * (g - mm[j]);
+    vv[j] = vv[j] * b2 + (1.f - b2) * g * g;
+    const float denom = sqrtf(vv[j]) / bc2_sqrt + eps;
+    pp[j] = pp[j] - step_size * (mm[j] / denom);
+  }
+  if (cnt == 4) {
+    *reinterpret_cast<float4*>(p + i4) = *reinterpret_cast<float4*>(pp);
+    *reinterpret_cast<float4*>(m + i4) = *reinterpret_cast<float4*>(mm);
+    *reinterpret_cast<float4*>(v + i4) = *reinterpret_cast<float4*>(vv);
+    if (zero_grad) *reinterpret_cast<float4*>(const_cast<float*>(grad) + i4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p_bf16 != nullptr) {
+      uint2 u;
+      u.x = pack_bf16x2(pp[0], pp[1]);
+      u.y = pack_bf16x2(pp[2], pp[3]);
+      *reinterpret_cast<uint2*>(p_bf16 + i4) = u;
+    }
+  } else {
+    for (int j = 0; j < cnt; ++j) {
+      p[i4 + j] = pp[j]; m[i4 + j] = mm[j]; v[i4 + j] = vv[j];
+      if (zero_grad) const_cast<float*>(grad)[i4 + j] = 0.f;
+      if (p_bf16 != nullptr) p_bf16[i4 + j] = __float2bfloat16_rn(pp[j]);
+    }
+  }
+}
+
+// Sum of squares of a flat fp32 buffer into per-CTA partials (fixed grid -> deterministic).
+__global__ void sumsq_partial_kernel(const float* __restrict__ x, long long n, float* __restrict__ part) {
+  __shared__ float sh[32];
+  float s = 0.f;
+  for (long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x * 4) {
+    if (i + 4 <= n) {
+      const float4 v = *reinterpret_cast<const float4*>(x + i);
+      s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    } else {
+      for (long long j = i; j < n; ++j) s += x[j] * x[j];
+    }
+  }
+  s = block_sum<256>(s, sh);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+}  // namespace
+
+static inline int cdiv_ll(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s) {
+  if (H % 8 || H > kNormThreads * kNormMaxVec * 8) return -1;
+  rmsnorm_fwd_kernel<<<T, kNormThreads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x),
+                                                reinterpret_cast<const __nv_bfloat16*>(w),
+                                                reinterpret_cast<__nv_bfloat16*>(y), rstd, H, eps);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int rmsnorm_bwd_blocks(int T) { return (T + kNormBwdRows - 1) / kNormBwdRows; }
+
+int rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres, void* dx,
+                float* dw, int accumulate, float* part, int T, int H, cudaStream_t s) {
+  if (H % 8 || H > kNormThreads * kNormMaxVec * 8) return -1;
+  const int nb = rmsnorm_bwd_blocks(T);
+  rmsnorm_bwd_kernel<<<nb, kNormThreads, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w), rstd,
+      reinterpret_cast<const __nv_bfloat16*>(dy), reinterpret_cast<const __nv_bfloat16*>(dres),
+      reinterpret_cast<__nv_bfloat16*>(dx), part, T, H);
+  colsum_kernel<<<cdiv_ll(H, 256), 256, 0, s>>>(part, dw, nb, H, accumulate);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos_t, const float* sin_t, int S,
+               int T, int inverse, cudaStream_t s) {
+  if (D % 4) return -1;
+  const long long total = static_cast<long long>(T) * heads * (D / 4);
+  rope_kernel<<<cdiv_ll(total, 256), 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(q), row_stride, heads, D,
+                                                   cos_t, sin_t, S, T, inverse);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int swiglu_fwd(const void* gu, void* a, int T, int F, cudaStream_t s) {
+  if (F % 8) return -1;
+  const long long total = static_cast<long long>(T) * (F / 8);
+  swiglu_fwd_kernel<<<cdiv_ll(total, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+                                                        reinterpret_cast<__nv_bfloat16*>(a), T, F);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStream_t s) {
+  if (F % 8) return -1;
+  const long long total = static_cast<long long>(T) * (F / 8);
+  swiglu_bwd_kernel<<<cdiv_ll(total, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+                                                        reinterpret_cast<const __nv_bfloat16*>(da),
+                                                        reinterpret_cast<__nv_bfloat16*>(dgu), T, F);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int V, int* err, cudaStream_t s) {
+  if (H % 8) return -1;
+  embedding_fwd_kernel<<<T, 128, 0, s>>>(ids, reinterpret_cast<const __nv_bfloat16*>(E),
+                                         reinterpret_cast<__nv_bfloat16*>(x), T, H, V, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int embedding_bwd(const int64_t* order, const int64_t* starts, const int64_t* uniq, int n_uniq, const void* dx,
+                  float* dE, int H, cudaStream_t s) {
+  if (H % 8 || n_uniq <= 0) return n_uniq == 0 ? 0 : -1;
+  embedding_bwd_kernel<<<n_uniq, 128, 0, s>>>(order, starts, uniq, reinterpret_cast<const __nv_bfloat16*>(dx),
+                                              dE, H);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int adam_step(float* p, float* grad, float* m, float* v, void* p_bf16, long long n, float lr, float b1, float b2,
+              float eps, float wd, int decoupled, float bc1, float bc2_sqrt, float grad_scale, int zero_grad,
+              cudaStream_t s) {
+  if (n <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(m) |
+       reinterpret_cast<uintptr_t>(v)) & 15)
+    return -1;
+  if (p_bf16 != nullptr && (reinterpret_cast<uintptr_t>(p_bf16) & 7)) return -1;
+  const long long nthreads = (n + 3) / 4;
+  adam_kernel<<<cdiv_ll(nthreads, 256), 256, 0, s>>>(p, grad, m, v, reinterpret_cast<__nv_bfloat16*>(p_bf16), n,
+                                                     lr, b1, b2, eps, wd, decoupled, bc1, bc2_sqrt, grad_scale,
+                                                     zero_grad);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int sumsq_partial(const float* x, long long n, float* part, int nblocks, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(x) & 15) return -1;
+  sumsq_partial_kernel<<<nblocks, 256, 0, s>>>(x, n, part);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rb

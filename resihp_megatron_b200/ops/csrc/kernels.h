@@ -5,10 +5,68 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
 namespace rb {
 
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* D,
               long long ldd, const void* R, long long ldr, int M, int N, int K, int epi, float alpha,
               int* err, int num_sms, cudaStream_t stream);
 
+int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s);
+int rmsnorm_bwd_blocks(int T);
+int rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres, void* dx,
+                float* dw, int accumulate, float* part, int T, int H, cudaStream_t s);
+int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos_t, const float* sin_t, int S,
+               int T, int inverse, cudaStream_t s);
+int swiglu_fwd(const void* gu, void* a, int T, int F, cudaStream_t s);
+int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStream_t s);
+int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int V, int* err, cudaStream_t s);
+int embedding_bwd(const int64_t* order, const int64_t* starts, const int64_t* uniq, int n_uniq, const void* dx,
+                  float* dE, int H, cudaStream_t s);
+int adam_step(float* p, float* grad, float* m, float* v, void* p_bf16, long long n, float lr, float b1, float b2,
+              float eps, float wd, int decoupled, float bc1, float bc2_sqrt, float grad_scale, int zero_grad,
+              cudaStream_t s);
+int sumsq_partial(const float* x, long long n, float* part, int nblocks, cudaStream_t s);
+int cross_entropy_fwd_bwd(void* logits, long long ld, const int64_t* labels, float* loss, float* lse, int T, int V,
+                          long long v0, float grad_scale, long long ignore_index, int write_grad, cudaStream_t s);
+
+struct AttnArgs;
+struct AttnBwdArgs;
+
+}  // namespace rb
+
+// Attention argument blocks (shared by the mma.sync and tcgen05 implementations).
+namespace rb {
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  long long q_stride, k_stride, v_stride;
+  void* o;
+  long long o_stride;
+  float* lse;
+  int B, S, Hq, Hkv;
+  float scale;
+  int causal;
+};
+struct AttnBwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  long long q_stride, k_stride, v_stride, o_stride, do_stride;
+  const float* lse;
+  float* delta;
+  void* dq;
+  void* dk;
+  void* dv;
+  long long dq_stride, dk_stride, dv_stride;
+  int B, S, Hq, Hkv;
+  float scale;
+  int causal;
+};
+int attention_fwd_mma(const AttnArgs& a, int D, cudaStream_t s);
+int attention_bwd_mma(const AttnBwdArgs& a, int D, cudaStream_t s);
 }  // namespace rb

@@ -20,6 +20,7 @@ from __future__ import annotations
 import torch
 
 from ._build import ext
+from .counter import count
 
 EPI_BF16 = 0
 EPI_F32 = 1
@@ -53,6 +54,7 @@ def gemm(
         out = torch.empty((M, N), dtype=torch.float32 if epi in (EPI_F32, EPI_F32_ACC) else torch.bfloat16,
                           device=a.device)
     ext().gemm(a, a_t, b, b_t, out, epi, float(alpha), residual)
+    count(1)
     return out
 
 

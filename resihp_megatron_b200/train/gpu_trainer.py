@@ -1,0 +1,108 @@
+"""GPU training engine: one process per GPU, data parallel with a sharded optimizer (ZeRO-1).
+
+``GPUTrainer.train_step(ids, labels)`` is the public entry point: it takes one step's token
+ids and labels for this rank (pinned host tensors), copies them to the device, runs every
+micro-batch forward and backward on the package's kernels, reduces the gradients across the
+data-parallel group, applies Adam to this rank's shard of the fp32 master weights, gathers
+the updated bf16 weights, and returns the step's mean token loss.
+
+Gradients are scaled by ``1 / tokens in the global batch`` inside the cross-entropy kernel,
+so the reduced gradient is the gradient of the global mean loss whatever the DP degree.
+The global batch and the order of micro-batches are those of the failure-free run: rank r of
+a DP group of size d takes sequences ``[r * B / d, (r + 1) * B / d)`` of every global batch
+(the reference keeps the same invariant with its index-addressable sampler,
+``resihp/state/rng_data.py:41``).
+"""
+
+from __future__ import annotations
+
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+from ..models.config import GPTConfig
+from ..models.gpt import LlamaModel
+
+
+class GPUTrainer:
+    def __init__(self, cfg: GPTConfig, *, global_batch: int, micro_batch: int = 1, seq_len: int | None = None,
+                 lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, seed: int = 0,
+                 device=None, dp_group: dist.ProcessGroup | None = None):
+        self.cfg = cfg
+        self.S = seq_len or cfg.seq_len
+        self.group = dp_group
+        self.dp = dist.get_world_size(dp_group) if (dist.is_initialized() and dp_group is not None) else 1
+        self.rank = dist.get_rank(dp_group) if self.dp > 1 else 0
+        if global_batch % self.dp:
+            raise ValueError(f"global batch {global_batch} is not divisible by DP={self.dp}")
+        self.global_batch = global_batch
+        self.local_batch = global_batch // self.dp
+        if self.local_batch % micro_batch:
+            raise ValueError("local batch must be a multiple of the micro-batch")
+        self.micro_batch = micro_batch
+        self.n_micro = self.local_batch // micro_batch
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
+        self.model = LlamaModel(cfg, self.device, micro_batch=micro_batch, seq_len=self.S, seed=seed,
+                                shard_rank=self.rank, shard_count=self.dp)
+        self.tokens_per_step = global_batch * self.S
+        self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
+        self.labels_dev = torch.empty_like(self.ids_dev)
+        P = self.model.params
+        if self.dp > 1:
+            self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
+        self.step_count = 0
+
+    # ------------------------------------------------------------------ device-resident step
+    def step_device(self, ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on device-resident ``[local_batch, S]`` ids/labels; returns the
+        global mean loss as a 0-d device tensor (no host synchronisation)."""
+        m = self.model
+        m.loss_acc.zero_()
+        scale = 1.0 / self.tokens_per_step
+        mb = self.micro_batch
+        for i in range(self.n_micro):
+            m.forward_backward(ids[i * mb:(i + 1) * mb].reshape(-1), labels[i * mb:(i + 1) * mb].reshape(-1), scale)
+        self._reduce_and_update()
+        self.step_count += 1
+        return m.loss_acc / self.tokens_per_step
+
+    def _reduce_and_update(self) -> None:
+        from .. import ops
+
+        P = self.model.params
+        P.step += 1
+        kw = dict(lr=self.lr, beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, weight_decay=self.wd,
+                  step=P.step)
+        if self.dp == 1:
+            ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, zero_grad=True, **kw)
+            return
+        dist.reduce_scatter_tensor(self.grad_shard, P.grad, op=dist.ReduceOp.SUM, group=self.group)
+        dist.all_reduce(self.model.loss_acc, group=self.group)
+        P.grad.zero_()
+        ops.adam_step(P.master, self.grad_shard, P.exp_avg, P.exp_avg_sq, P.shard_slice(P.bf16), zero_grad=False,
+                      **kw)
+        dist.all_gather_into_tensor(P.bf16, P.shard_slice(P.bf16), group=self.group)
+
+    # ------------------------------------------------------------------ public end-to-end step
+    def train_step(self, ids_host: torch.Tensor, labels_host: torch.Tensor) -> float:
+        """Copy this rank's inputs (pinned host ``[local_batch, S]`` int64) to the device, run the
+        step, and return the global mean token loss read back to the host."""
+        self.ids_dev.copy_(ids_host, non_blocking=True)
+        self.labels_dev.copy_(labels_host, non_blocking=True)
+        loss = self.step_device(self.ids_dev, self.labels_dev)
+        return float(loss.item())
+
+
+def init_distributed(timeout_s: float = 300.0) -> tuple[int, int, int]:
+    """Initialise NCCL from torchrun's environment; returns (rank, world, local_rank)."""
+    import os
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=torch.device("cuda", local))
+    return rank, world, local
