@@ -178,9 +178,8 @@ class LlamaModel:
         return out, rstd
 
     def _attention_fwd(self, i, q, k, v):
-        ops.ext().attention_fwd(q, k, v, self.o[i], self.lse[i], self.mb, self.S, self.cfg.heads, self.cfg.kv_heads,
-                                self.cfg.head_dim, self.cfg.head_dim ** -0.5, True)
-        ops.count(1)
+        ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.cfg.heads, kv_heads=self.cfg.kv_heads,
+                          head_dim=self.cfg.head_dim, out=self.o[i], lse=self.lse[i])
 
     def head_loss(self, labels: torch.Tensor, grad_scale: float) -> torch.Tensor:
         """Final norm + LM head + cross-entropy; leaves dlogits in ``self.logits``."""

@@ -115,13 +115,20 @@ def cross_entropy_(logits: torch.Tensor, labels: torch.Tensor, *, grad_scale: fl
     return loss
 
 
+ATTN_AUTO, ATTN_MMA, ATTN_TCGEN05 = 0, 1, 2
+
+
 def attention_fwd(q, k, v, *, batch: int, seq: int, heads: int, kv_heads: int, head_dim: int, causal: bool = True,
-                  scale: float | None = None, out: torch.Tensor | None = None):
-    """Causal GQA attention on token-major 2-D views; returns ``(o, lse)``."""
+                  scale: float | None = None, out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+                  impl: int = ATTN_AUTO):
+    """Causal GQA attention on token-major 2-D views; returns ``(o, lse)``.  ``impl``: the
+    tcgen05 kernel (head dim 128, causal, seq % 256 == 0) with the mma.sync kernel for other
+    shapes (``ATTN_AUTO``), or one of them explicitly."""
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
     o = torch.empty((q.shape[0], heads * head_dim), dtype=q.dtype, device=q.device) if out is None else out
-    lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
-    ext().attention_fwd(q, k, v, o, lse, batch, seq, heads, kv_heads, head_dim, float(scale), bool(causal))
+    if lse is None:
+        lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
+    ext().attention_fwd(q, k, v, o, lse, batch, seq, heads, kv_heads, head_dim, float(scale), bool(causal), int(impl))
     count(1)
     return o, lse
 

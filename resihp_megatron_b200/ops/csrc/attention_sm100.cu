@@ -1,0 +1,335 @@
+// Causal GQA flash-attention forward on tcgen05 tensor cores (head dim 128).
+//
+// CTA = 256 query rows of one (batch, head): two 128-row tiles A and B that share every K/V
+// block.  Roles (320 threads):
+//   warps 0-3  softmax + epilogue of tile A (thread = query row = TMEM lane)
+//   warps 4-7  softmax + epilogue of tile B
+//   warp 8     TMA producer: Q_A, Q_B once, then K_j and V_j (128 x 128 bf16 each)
+//   warp 9     TMEM allocator and single-thread MMA issuer
+// TMEM (512 columns): S_A | S_B | O_A | O_B, 128 fp32 columns each.
+// Per key block j:  S_X = Q_X K_j^T (tcgen05, both operands K-major from shared memory);
+// softmax reads its S row from TMEM, applies the causal mask on the diagonal block, updates the
+// running max, and writes P (bf16) to shared memory in the 128B-swizzled K-major layout the MMA
+// reads; then O_X += P_X V_j (V as an MN-major operand, no transpose).  O stays in TMEM; it is
+// rescaled (TMEM load / multiply / store) only when a row's max grows by more than 2^8, so the
+// common case costs nothing -- l and O always share the same reference max, so the result is
+// exact.  Output rows are normalised by l in the epilogue and LSE is written for the backward.
+//
+// Every mbarrier wait is bounded (see sm100.cuh); a timeout unwinds all roles and the kernel
+// returns with an error word set.  No TMA multicast is used.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace rb {
+
+int make_tmap_bf16_2d(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                      uint32_t box_inner, uint32_t box_outer);
+
+namespace {
+
+constexpr int kTile = 128;                    // rows of a Q tile / K block, and the head dim
+constexpr int kTileBytes = kTile * kTile * 2;  // 32 KB: two 16 KB halves of 64 columns
+constexpr int kHalf = kTileBytes / 2;
+constexpr int kThreads = 320;
+constexpr int kSmem = 1024 + 6 * kTileBytes + 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdParams {
+  __nv_bfloat16* o;
+  long long o_stride;
+  float* lse;
+  int B, S, Hq, Hkv;
+  float scale_log2;  // softmax scale * log2(e)
+  int* err;
+};
+
+__device__ __forceinline__ bool warp_wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// K-major operand descriptor for k-step s (16 columns) of a [128 x 128] tile stored as two
+// 128B-swizzled halves of 64 columns.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int s) {
+  return make_smem_desc(base + (s >> 2) * kHalf + (s & 3) * 32, 16, 1024, kSwizzle128B);
+}
+
+// MN-major operand descriptor (V: N = head dim in two 64-wide halves, K = key rows) for k-step s.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int s) {
+  return make_smem_desc(base + s * 2048, kHalf, 1024, kSwizzle128B);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                    // Q_A, Q_B
+  uint8_t* sK = smem + 2 * kTileBytes;
+  uint8_t* sV = smem + 3 * kTileBytes;
+  uint8_t* sP = smem + 4 * kTileBytes;   // P_A, P_B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  const uint32_t bar_final = smem_u32(&bars[11]);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t bar_q = smem_u32(&bars[0]);
+  const uint32_t bar_kf = smem_u32(&bars[1]), bar_ke = smem_u32(&bars[2]);
+  const uint32_t bar_vf = smem_u32(&bars[3]), bar_ve = smem_u32(&bars[4]);
+  auto bar_s = [&](int x) { return smem_u32(&bars[5 + x]); };
+  auto bar_p = [&](int x) { return smem_u32(&bars[7 + x]); };
+  auto bar_o = [&](int x) { return smem_u32(&bars[9 + x]); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = gridDim.x;
+  const int qb = nqb - 1 - blockIdx.x;  // heaviest (latest) query blocks first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int q0 = qb * 2 * kTile;
+  const int jA = 2 * qb, jB = 2 * qb + 1;  // last key block of tile A / tile B
+  const int nkv = jB + 1;
+  const int row_base = b * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    mbar_init(bar_kf, 1);
+    mbar_init(bar_ke, 1);
+    mbar_init(bar_vf, 1);
+    mbar_init(bar_ve, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar_s(x), 1);
+      mbar_init(bar_p(x), 4);
+      mbar_init(bar_o(x), 1);
+    }
+    mbar_init(bar_final, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(bar_q, 2 * kTileBytes);
+      for (int x = 0; x < 2; ++x)
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(smem_u32(sQ + x * kTileBytes + hf * kHalf), &tmQ, bar_q, h * kTile + hf * 64,
+                      row_base + q0 + x * kTile);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait(bar_ke, (j & 1) ^ 1, abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(bar_kf, kTileBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(smem_u32(sK + hf * kHalf), &tmK, bar_kf, hk * kTile + hf * 64, row_base + j * kTile);
+        issued_k = j + 1;
+        if (!mbar_wait(bar_ve, (j & 1) ^ 1, abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(bar_vf, kTileBytes);
+        for (int hf = 0; hf < 2; ++hf)
+          tma_load_2d(smem_u32(sV + hf * kHalf), &tmV, bar_vf, hk * kTile + hf * 64, row_base + j * kTile);
+        issued_v = j + 1;
+      }
+      // drain: the last loads issued must land before the CTA may exit
+      mbar_wait(bar_q, 0, nullptr, p.err, 200000000ull);
+      if (issued_k) mbar_wait(bar_kf, (issued_k - 1) & 1, nullptr, p.err, 200000000ull);
+      if (issued_v) mbar_wait(bar_vf, (issued_v - 1) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(128, 128, true, false, false);
+      constexpr uint32_t idesc_o = make_idesc_f16(128, 128, true, false, true);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.err);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const bool doA = j <= jA;
+        if (!(ok = mbar_wait(bar_kf, j & 1, abort_flag, p.err))) break;
+        tc_fence_after();
+        for (int x = doA ? 0 : 1; x < 2; ++x) {
+#pragma unroll
+          for (int s = 0; s < 8; ++s)
+            umma_f16(tmem + x * 128, kmajor_desc(q_base + x * kTileBytes, s), kmajor_desc(k_base, s), idesc_s,
+                     s > 0 ? 1u : 0u);
+          umma_commit(bar_s(x));
+        }
+        umma_commit(bar_ke);
+        if (!(ok = mbar_wait(bar_vf, j & 1, abort_flag, p.err))) break;
+        for (int x = doA ? 0 : 1; x < 2; ++x) {
+          if (!(ok = mbar_wait(bar_p(x), j & 1, abort_flag, p.err))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int s = 0; s < 8; ++s)
+            umma_f16(tmem + 256 + x * 128, kmajor_desc(p_base + x * kTileBytes, s), mnmajor_desc(v_base, s),
+                     idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+          umma_commit(bar_o(x));
+        }
+        umma_commit(bar_ve);
+      }
+      // every MMA this thread issued completes before TMEM is released
+      umma_commit(bar_final);
+      mbar_wait(bar_final, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int X = warp >> 2;                 // tile
+    const int r = (warp & 3) * 32 + lane;    // row in tile == TMEM lane
+    const int jmax = X == 0 ? jA : jB;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + X * 128;
+    const uint32_t o_addr = tmem + lane_off + 256 + X * 128;
+    uint8_t* prow = sP + X * kTileBytes + r * 128;
+    const int sw = r & 7;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j <= jmax; ++j) {
+      if (!(ok = warp_wait_bar(bar_s(X), j & 1, abort_flag, p.err))) break;
+      tc_fence_after();
+      float v[128];
+      {
+        uint32_t t[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld_32x32b_x32(s_addr + c * 32, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[i]) * p.scale_log2;
+        }
+      }
+      float mx = -INFINITY;
+      if (j == jmax) {  // diagonal block: key index > query index is masked
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          if (c > r) v[c] = -INFINITY;
+          mx = fmaxf(mx, v[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, v[c]);
+      }
+      // PV of the previous block must be done: O is stable and P's buffer is free
+      if (j > 0) {
+        if (!(ok = warp_wait_bar(bar_o(X), (j - 1) & 1, abort_flag, p.err))) break;
+        tc_fence_after();
+      }
+      const bool need = mx > m_ref + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - mx);
+        l *= alpha;
+        m_ref = mx;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        uint32_t t[32];
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld_32x32b_x32(o_addr + c * 32, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+          tmem_st_32x32b_x32(o_addr + c * 32, t);
+        }
+        tmem_st_wait();
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = ex2(v[c8 * 8 + i] - m_ref);
+          sum += e[i];
+        }
+        uint4 u;
+        u.x = pack_bf16x2(e[0], e[1]);
+        u.y = pack_bf16x2(e[2], e[3]);
+        u.z = pack_bf16x2(e[4], e[5]);
+        u.w = pack_bf16x2(e[6], e[7]);
+        const int half = c8 >> 3, chunk = c8 & 7;
+        *reinterpret_cast<uint4*>(prow + half * kHalf + ((chunk ^ sw) << 4)) = u;
+      }
+      l += sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p(X));
+    }
+    if (ok && warp_wait_bar(bar_o(X), jmax & 1, abort_flag, p.err)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int q = q0 + X * kTile + r;
+      __nv_bfloat16* orow = p.o + static_cast<long long>(row_base + q) * p.o_stride + h * kTile;
+      uint32_t t[32];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld_32x32b_x32(o_addr + c * 32, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 u;
+          u.x = pack_bf16x2(__uint_as_float(t[8 * i + 0]) * inv, __uint_as_float(t[8 * i + 1]) * inv);
+          u.y = pack_bf16x2(__uint_as_float(t[8 * i + 2]) * inv, __uint_as_float(t[8 * i + 3]) * inv);
+          u.z = pack_bf16x2(__uint_as_float(t[8 * i + 4]) * inv, __uint_as_float(t[8 * i + 5]) * inv);
+          u.w = pack_bf16x2(__uint_as_float(t[8 * i + 6]) * inv, __uint_as_float(t[8 * i + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * i) = u;
+        }
+      }
+      p.lse[(static_cast<long long>(b) * p.Hq + h) * p.S + q] = (m_ref + __log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+// Returns 1 when the shape is not handled by this kernel (the caller uses the mma.sync path).
+int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t stream) {
+  if (D != 128 || !a.causal || a.S % 256 != 0 || a.Hq % a.Hkv != 0) return 1;
+  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
+       reinterpret_cast<uintptr_t>(a.o)) & 15)
+    return 1;
+  if ((a.q_stride | a.k_stride | a.v_stride | a.o_stride) & 7) return 1;
+  const long long T = static_cast<long long>(a.B) * a.S;
+  CUtensorMap tq, tk, tv;
+  if (make_tmap_bf16_2d(&tq, a.q, static_cast<uint64_t>(a.Hq) * 128, T, a.q_stride, 64, 128)) return -20;
+  if (make_tmap_bf16_2d(&tk, a.k, static_cast<uint64_t>(a.Hkv) * 128, T, a.k_stride, 64, 128)) return -21;
+  if (make_tmap_bf16_2d(&tv, a.v, static_cast<uint64_t>(a.Hkv) * 128, T, a.v_stride, 64, 128)) return -22;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr = true;
+  }
+  FwdParams p{reinterpret_cast<__nv_bfloat16*>(a.o), a.o_stride, a.lse, a.B, a.S, a.Hq, a.Hkv,
+              a.scale * 1.4426950408889634f, err};
+  dim3 grid(a.S / 256, a.Hq, a.B);
+  attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream>>>(tq, tk, tv, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rb

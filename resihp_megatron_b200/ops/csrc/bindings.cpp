@@ -236,15 +236,21 @@ static rb::AttnArgs attn_args(const torch::Tensor& q, const torch::Tensor& k, co
 }
 
 // q/k/v/o: 2-D [B*S, heads*D] views with contiguous rows (row stride may exceed heads*D).
+// impl: 0 = tcgen05 kernel when the shape allows, else mma.sync; 1 = mma.sync; 2 = tcgen05 only.
 void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
                    torch::Tensor& lse, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, double scale,
-                   bool causal) {
+                   bool causal, int64_t impl) {
   for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "attention operands must be 2-D bf16 CUDA views with contiguous rows");
   CHECK_F32(lse);
   const c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k, v, o, lse, B, S, Hq, Hkv, scale, causal);
+  if (impl != 1) {
+    const int rc = rb::attention_fwd_sm100(a, D, err_ptr(q), cur_stream());
+    if (rc == 0) return;
+    TORCH_CHECK(rc == 1 && impl == 0, "attention_fwd (tcgen05) failed with code ", rc);
+  }
   RB_CALL(rb::attention_fwd_mma(a, D, cur_stream()), "attention_fwd");
 }
 
@@ -285,6 +291,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam_step", &adam_step);
   m.def("sumsq", &sumsq);
   m.def("cross_entropy", &cross_entropy);
-  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"),
+        py::arg("impl") = 0);
   m.def("attention_bwd", &attention_bwd);
 }

@@ -68,5 +68,6 @@ struct AttnBwdArgs {
   int causal;
 };
 int attention_fwd_mma(const AttnArgs& a, int D, cudaStream_t s);
+int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t s);
 int attention_bwd_mma(const AttnBwdArgs& a, int D, cudaStream_t s);
 }  // namespace rb
