@@ -5,9 +5,9 @@ Hang causes designed out:
   (with abort of whatever the dead ranks left in flight) when the new world is an
   order-preserving subset of the old one and NCCL >= 2.27.3, else a fresh world on a
   generation-scoped ``PrefixStore`` of the coordinator-hosted ``TCPStore``;
-* creation order depending on local state -> plan-derived canonical order, one ``split_group``
-  per layer of disjoint groups, entered by every rank (or ``new_group`` in canonical order with
-  local synchronisation and the c10d group-counter kept in step on non-members);
+* creation order depending on local state -> plan-derived canonical order: one ``split_group``
+  per layer of disjoint groups on NCCL, or ``new_group`` for every group on every rank in that
+  order on gloo;
 * a rendezvous store on a training rank -> the store lives on the coordinator;
 * blocking forever in a collective -> ``guarded_wait`` (abortable, deadline) and a validation
   all-reduce of ones on every group under a deadline before the generation may report READY
@@ -196,7 +196,10 @@ class ResilientCommManager:
 
     def _make_subgroups(self, rank: int, specs: list[GroupSpec]) -> dict[str, Any]:
         by_ranks: dict[tuple[int, ...], Any] = {}
-        if self.subgroup_mode == "split":
+        # split_group needs a device bound to the default group (NCCL with device_id); gloo
+        # worlds use canonical-order new_group instead
+        use_split = self.subgroup_mode == "split" and self.backend == "nccl" and self.device is not None
+        if use_split:
             for layer in split_layers(specs):
                 self._check_abort()
                 pg = dist.split_group(split_ranks=[list(s.ranks) for s in layer], timeout=self.timeout,
@@ -205,20 +208,15 @@ class ResilientCommManager:
                     if rank in s.ranks:
                         by_ranks[s.ranks] = pg
         else:
-            # c10d salts group names with a per-process creation counter that a non-member's
-            # new_group(use_local_synchronization=True) does not advance; keep it in step so
-            # overlapping groups get the same name on every rank.
+            # every rank creates every group in the same canonical order (non-members too), so
+            # c10d derives identical group names everywhere and creation cannot deadlock
             made: set[tuple[int, ...]] = set()
             for s in canonical_order(specs):
                 if not s.materialized or s.ranks in made:
                     continue
                 made.add(s.ranks)
                 self._check_abort()
-                before = c10d._world.group_count
-                pg = dist.new_group(list(s.ranks), timeout=self.timeout, use_local_synchronization=True,
-                                    group_desc=f"resihp:{s.name}")
-                if c10d._world.group_count == before:
-                    c10d._world.group_count = before + 1
+                pg = dist.new_group(list(s.ranks), timeout=self.timeout, group_desc=f"resihp:{s.name}")
                 if rank in s.ranks:
                     by_ranks[s.ranks] = pg
         groups = {s.name: (by_ranks.get(s.ranks) if rank in s.ranks and s.materialized else None) for s in specs}
