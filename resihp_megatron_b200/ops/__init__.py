@@ -134,10 +134,12 @@ def attention_fwd(q, k, v, *, batch: int, seq: int, heads: int, kv_heads: int, h
 
 
 def attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, *, batch: int, seq: int, heads: int, kv_heads: int,
-                  head_dim: int, causal: bool = True, scale: float | None = None):
-    """Writes dq/dk/dv (token-major 2-D views, may be column slices of one buffer)."""
+                  head_dim: int, causal: bool = True, scale: float | None = None, impl: int = ATTN_AUTO):
+    """Writes dq/dk/dv (token-major 2-D views, may be column slices of one buffer).  ``impl`` as
+    in ``attention_fwd``: the tcgen05 kernels (head dim 128, causal, seq % 128 == 0) or the
+    mma.sync kernels."""
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
     delta = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
     ext().attention_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, batch, seq, heads, kv_heads, head_dim, float(scale),
-                        bool(causal))
+                        bool(causal), int(impl))
     count(3)

@@ -257,7 +257,7 @@ void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
 void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
                    const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& delta, torch::Tensor& dq,
                    torch::Tensor& dk, torch::Tensor& dv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
-                   double scale, bool causal) {
+                   double scale, bool causal, int64_t impl) {
   for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o, &dout, &dq, &dk, &dv})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "attention operands must be 2-D bf16 CUDA views with contiguous rows");
@@ -271,6 +271,13 @@ void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
   a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
   a.dq_stride = dq.stride(0); a.dk_stride = dk.stride(0); a.dv_stride = dv.stride(0);
   a.B = B; a.S = S; a.Hq = Hq; a.Hkv = Hkv; a.scale = scale; a.causal = causal ? 1 : 0;
+  TORCH_CHECK(delta.numel() >= B * Hq * S, "delta needs B * Hq * S floats");
+  if (impl != 1) {
+    auto nl2 = torch::empty_like(delta);
+    const int rc = rb::attention_bwd_sm100(a, D, nl2.data_ptr<float>(), err_ptr(q), cur_stream());
+    if (rc == 0) return;
+    TORCH_CHECK(rc == 1 && impl == 0, "attention_bwd (tcgen05) failed with code ", rc);
+  }
   RB_CALL(rb::attention_bwd_mma(a, D, cur_stream()), "attention_bwd");
 }
 
@@ -294,5 +301,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"),
         py::arg("impl") = 0);
-  m.def("attention_bwd", &attention_bwd);
+  m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
+        py::arg("lse"), py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("S"),
+        py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0);
 }

@@ -70,4 +70,6 @@ struct AttnBwdArgs {
 int attention_fwd_mma(const AttnArgs& a, int D, cudaStream_t s);
 int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t s);
 int attention_bwd_mma(const AttnBwdArgs& a, int D, cudaStream_t s);
+// tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
+int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
 }  // namespace rb

@@ -36,3 +36,41 @@ def test_tcgen05_attention_forward(B, S, Hq, Hkv, amp):
     assert err < 2e-2 * ref.abs().max().item() + 1e-2, err
     assert (lse.view(B, Hq, S) - ref_lse).abs().max().item() < 1e-2
     assert (o.float() - o2.float()).abs().max().item() < 3e-2 * ref.abs().max().item() + 1e-2
+
+
+def _ref_grads(q, k, v, dout, B, S, Hq, Hkv, D):
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    o, _ = _ref(qf, kf, vf, B, S, Hq, Hkv, D)
+    o.backward(dout.float())
+    return qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("B,S,Hq,Hkv", [(1, 256, 2, 2), (2, 384, 4, 1), (1, 1024, 8, 2)])
+def test_tcgen05_attention_backward(B, S, Hq, Hkv):
+    """dQ/dK/dV of the tcgen05 kernels against fp32 autograd and the mma.sync kernels; two
+    runs are bitwise equal (no atomics)."""
+    from resihp_megatron_b200 import ops
+
+    D = 128
+    torch.manual_seed(1)
+    q = torch.randn(B * S, Hq * D, device="cuda").bfloat16()
+    k = torch.randn(B * S, Hkv * D, device="cuda").bfloat16()
+    v = torch.randn(B * S, Hkv * D, device="cuda").bfloat16()
+    dout = torch.randn(B * S, Hq * D, device="cuda").bfloat16()
+    kw = dict(batch=B, seq=S, heads=Hq, kv_heads=Hkv, head_dim=D)
+    o, lse = ops.attention_fwd(q, k, v, impl=ops.ATTN_MMA, **kw)
+    outs = {}
+    for name, impl in (("tc", ops.ATTN_TCGEN05), ("tc2", ops.ATTN_TCGEN05), ("mma", ops.ATTN_MMA)):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        ops.attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, impl=impl, **kw)
+        outs[name] = (dq, dk, dv)
+    torch.cuda.synchronize()
+    assert int(ops.error_state()[0]) == 0
+    ref = _ref_grads(q, k, v, dout, B, S, Hq, Hkv, D)
+    for got, want, mma, name in zip(outs["tc"], ref, outs["mma"], ("dq", "dk", "dv")):
+        scale = want.abs().max().item()
+        err = (got.float() - want).abs().max().item()
+        assert err < 2e-2 * scale + 1e-2, (name, err, scale)
+        assert (got.float() - mma.float()).abs().max().item() < 3e-2 * scale + 1e-2, name
+    for a, b in zip(outs["tc"], outs["tc2"]):
+        assert torch.equal(a, b)
