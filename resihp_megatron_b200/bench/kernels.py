@@ -1,0 +1,190 @@
+"""Kernel microbenchmarks with roofline fractions (``resihp-bench kernels``).
+
+    python -m resihp_megatron_b200.bench.kernels gemm --m 8192 --n 8192 --k 8192
+    python -m resihp_megatron_b200.bench.kernels attention --batch 2 --seq 4096 --heads 32 --kv-heads 8
+    python -m resihp_megatron_b200.bench.kernels adam --numel 1000000000
+    python -m resihp_megatron_b200.bench.kernels all
+
+Timing: ``--warmup`` untimed launches, then ``--iters`` launches each bracketed by CUDA events
+on the launching stream with a synchronize on both sides; the median is reported.  Inputs of
+the memory-bound kernels are larger than the 126 MB L2; for GEMMs an L2-sized buffer is
+rewritten between timed launches (``--flush``).  Fractions are of the measured copy bandwidth
+and cuBLAS bf16 throughput in ``MEASURED_PEAKS.json`` at the repository root when present,
+otherwise of the fallback figures 6.65 TB/s and 1.59 PFLOP/s.  One JSON line per case.
+
+The reference has no kernels of its own; its only compute probe is a cuBLAS matmul
+(``resihp/detect/validation.py:17-31``), reported here as ``cublas`` beside our GEMM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Timer:
+    def __init__(self, warmup: int, iters: int, flush: bool):
+        self.warmup, self.iters = warmup, iters
+        self.scratch = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if flush else None
+
+    def __call__(self, fn) -> float:
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(self.iters):
+            if self.scratch is not None:
+                self.scratch.fill_(1)  # evict L2 between launches
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        return statistics.median(times)
+
+
+def emit(kind: str, ms: float, *, flops: float = 0.0, bytes_: float = 0.0, **extra) -> dict:
+    pk = peaks()
+    row = {"kernel": kind, "ms": round(ms, 4)}
+    if flops:
+        tf = flops / ms / 1e9
+        row.update(tflops=round(tf, 1), frac_of_bf16_peak=round(tf / pk["bf16_tflops"], 3))
+    if bytes_:
+        gbs = bytes_ / ms / 1e6
+        row.update(gbs=round(gbs, 1), frac_of_hbm=round(gbs / pk["hbm_gbs"], 3))
+    row["peaks"] = pk["source"]
+    row.update(extra)
+    print(json.dumps(row), flush=True)
+    return row
+
+
+def bench_gemm(a, t: Timer) -> None:
+    from .. import ops
+
+    M, N, K = a.m, a.n, a.k
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(N, K, device="cuda").bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    fl = 2.0 * M * N * K
+    emit("gemm_tcgen05_nt", t(lambda: ops.gemm(x, w, out=out)), flops=fl, shape=[M, N, K])
+    xt = x.t().contiguous()
+    emit("gemm_tcgen05_tn", t(lambda: ops.gemm(xt, w, a_t=True, out=out)), flops=fl, shape=[M, N, K])
+    emit("cublas", t(lambda: torch.matmul(x, w.t(), out=out)), flops=fl, shape=[M, N, K])
+    assert int(ops.error_state()[0]) == 0
+
+
+def bench_attention(a, t: Timer) -> None:
+    from .. import ops
+
+    B, S, Hq, Hkv, D = a.batch, a.seq, a.heads, a.kv_heads, 128
+    qkv = torch.randn(B * S, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D:(Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    kw = dict(batch=B, seq=S, heads=Hq, kv_heads=Hkv, head_dim=D)
+    fwd_flops = 4.0 * B * Hq * S * S * D / 2  # causal
+    impls = [("tcgen05", ops.ATTN_TCGEN05), ("mma", ops.ATTN_MMA)] if a.with_mma else [("tcgen05", ops.ATTN_TCGEN05)]
+    o, lse = ops.attention_fwd(q, k, v, **kw)
+    dout = torch.randn_like(o)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    for name, impl in impls:
+        emit(f"attention_fwd_{name}", t(lambda: ops.attention_fwd(q, k, v, out=o, lse=lse, impl=impl, **kw)),
+             flops=fwd_flops, shape=[B, S, Hq, Hkv, D])
+        emit(f"attention_bwd_{name}",
+             t(lambda: ops.attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, impl=impl, **kw)),
+             flops=2.5 * fwd_flops, shape=[B, S, Hq, Hkv, D])
+    assert int(ops.error_state()[0]) == 0
+
+
+def bench_adam(a, t: Timer) -> None:
+    from .. import ops
+
+    n = a.numel
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    step = [0]
+
+    def run():
+        step[0] += 1
+        ops.adam_step(p, g, m, v, pb, lr=1e-4, step=step[0], zero_grad=False)
+
+    # reads p, g, m, v (16 B) and writes p, m, v, bf16 copy (14 B) per element
+    emit("adam_fused", t(run), bytes_=30.0 * n, numel=n)
+
+
+def bench_norm(a, t: Timer) -> None:
+    from .. import ops
+
+    T, H = a.tokens, a.hidden
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = torch.ones(H, device="cuda").bfloat16()
+    y, rstd = ops.rmsnorm_fwd(x, w)
+    emit("rmsnorm_fwd", t(lambda: ops.rmsnorm_fwd(x, w, out=y)), bytes_=4.0 * T * H, shape=[T, H])
+    dy = torch.randn_like(x)
+    dw = torch.zeros(H, device="cuda")
+    emit("rmsnorm_bwd", t(lambda: ops.rmsnorm_bwd(x, w, rstd, dy, dw)), bytes_=6.0 * T * H, shape=[T, H])
+    gu = torch.randn(T, 2 * a.ffn, device="cuda").bfloat16()
+    act = torch.empty(T, a.ffn, device="cuda", dtype=torch.bfloat16)
+    emit("swiglu_fwd", t(lambda: ops.swiglu_fwd(gu, out=act)), bytes_=6.0 * T * a.ffn, shape=[T, a.ffn])
+
+
+def bench_ce(a, t: Timer) -> None:
+    from .. import ops
+
+    T, V = a.tokens, a.vocab
+    logits = torch.randn(T, V, device="cuda").bfloat16()
+    labels = torch.randint(0, V, (T,), device="cuda")
+    emit("cross_entropy_fwd_bwd", t(lambda: ops.cross_entropy_(logits, labels, grad_scale=1.0 / T)),
+         bytes_=4.0 * T * V, shape=[T, V])
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(prog="resihp-bench kernels")
+    ap.add_argument("which", choices=["gemm", "attention", "adam", "norm", "ce", "all"])
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=8192)
+    ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--batch", type=int, default=2)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--with-mma", action="store_true", help="also time the mma.sync attention kernels")
+    ap.add_argument("--numel", type=int, default=1 << 28)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--hidden", type=int, default=4096)
+    ap.add_argument("--ffn", type=int, default=14336)
+    ap.add_argument("--vocab", type=int, default=128256)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--no-flush", action="store_true")
+    a = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel benchmarks need a GPU")
+    t = Timer(a.warmup, a.iters, not a.no_flush)
+    table = {"gemm": bench_gemm, "attention": bench_attention, "adam": bench_adam, "norm": bench_norm,
+             "ce": bench_ce}
+    for name in (table if a.which == "all" else [a.which]):
+        table[name](a, t)
+
+
+if __name__ == "__main__":
+    main()

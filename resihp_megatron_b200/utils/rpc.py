@@ -129,6 +129,9 @@ class Server:
                 s, _ = self._listener.accept()
             except OSError:
                 return
+            if self._stop.is_set():  # accepted while stopping: refuse
+                s.close()
+                return
             c = Connection(s, self._on_message, self._forget)
             with self._lock:
                 self.connections.add(c)
@@ -143,10 +146,13 @@ class Server:
 
     def stop(self) -> None:
         self._stop.set()
-        try:
-            self._listener.close()
-        except OSError:
-            pass
+        # shutdown() first: a bare close() leaves a listener that another thread is blocked in
+        # accept() on still accepting connections on Linux
+        for op in (lambda: self._listener.shutdown(socket.SHUT_RDWR), self._listener.close):
+            try:
+                op()
+            except OSError:
+                pass
         with self._lock:
             live = list(self.connections)
         for c in live:
