@@ -1,5 +1,21 @@
-"""Named planner instances for ``resihp-run --planner module:attr``."""
+"""Named planner instances for ``resihp-run --planner module:attr``.
 
+``dp_8mb``: replica-DP with 8 micro-batches (the float64 GPT demo, ``examples/gpt_dp_demo.py``).
+``hetero_tp2_pp2_dp2``: the progressive TP -> PP -> DP planner for the reference model of
+``examples/hetero_demo.py`` (4 layers, TP2 x PP2 x DP2, sequence parallel, 8 micro-batches).
+"""
+
+from ..plan.coordinator_adapter import make_hetero_planner
 from ..plan.dp_planner import make_dp_planner
+from ..plan.model_spec import ModelProfile, ModelSpec
+from ..plan.planner import PlannerConfig
 
 dp_8mb = make_dp_planner(num_microbatches=8)
+
+HETERO_REF = PlannerConfig(
+    model=ModelSpec(num_layers=4, hidden=8, ffn=24, num_heads=12, num_kv_heads=12, vocab=16, seq_len=24,
+                    micro_batch_size=2),
+    profile=ModelProfile(alpha=1e-6, beta=1e-9, last_stage_extra_layers=0.0),
+    num_stages=2, num_replicas=2, tp=2, num_microbatches=8, sequence_parallel=True, migration_rounds=16)
+
+hetero_tp2_pp2_dp2 = make_hetero_planner(HETERO_REF)
