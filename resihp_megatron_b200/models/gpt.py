@@ -83,7 +83,7 @@ class LlamaModel:
 
     def __init__(self, cfg: GPTConfig, device="cuda", *, micro_batch: int = 1, seq_len: int | None = None,
                  seed: int = 0, layers: range | None = None, first: bool = True, last: bool = True,
-                 shard_rank: int = 0, shard_count: int = 1):
+                 shard_rank: int = 0, shard_count: int = 1, buffer_factory=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.mb = micro_batch
@@ -92,7 +92,7 @@ class LlamaModel:
         self.layer_ids = list(layers if layers is not None else range(cfg.layers))
         self.first, self.last = first, last
         self.params = FlatParams(model_param_specs(cfg, self.layer_ids, first, last), self.device,
-                                 shard_rank=shard_rank, shard_count=shard_count)
+                                 shard_rank=shard_rank, shard_count=shard_count, buffer_factory=buffer_factory)
         self.params.initialize(seed, cfg.init_std)
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
         self._alloc()

@@ -49,10 +49,11 @@ class FlatParams:
     """bf16 compute weights + fp32 master / grad / exp_avg / exp_avg_sq over one flat index space."""
 
     def __init__(self, specs: list[ParamSpec], device, with_optimizer: bool = True, shard_rank: int = 0,
-                 shard_count: int = 1):
+                 shard_count: int = 1, buffer_factory=None):
         """``shard_rank / shard_count`` > 1 keeps the optimizer state (master, moments) for one
         contiguous slice of the flat index space only (ZeRO-1); bf16 weights and gradients stay
-        full size."""
+        full size.  ``buffer_factory(numel) -> (bf16, grad)`` supplies zero-filled flat buffers
+        from elsewhere (the symmetric peer heap of the fused data-parallel step)."""
         self.specs = {s.name: s for s in specs}
         self.order = [s.name for s in specs]
         self.offsets: dict[str, int] = {}
@@ -66,8 +67,12 @@ class FlatParams:
         self.shard_numel = self.numel // shard_count
         self.shard_lo = shard_rank * self.shard_numel
         self.device = torch.device(device)
-        self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        if buffer_factory is not None:
+            self.bf16, self.grad = buffer_factory(self.numel)
+            assert self.bf16.numel() == self.numel and self.grad.numel() == self.numel
+        else:
+            self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device)
+            self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
         if with_optimizer:
             n = self.shard_numel
             self.master = torch.zeros(n, dtype=torch.float32, device=self.device)

@@ -5,6 +5,7 @@
 #include <torch/extension.h>
 
 #include <cmath>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -281,6 +282,108 @@ void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
   RB_CALL(rb::attention_bwd_mma(a, D, cur_stream()), "attention_bwd");
 }
 
+
+// ------------------------------------------------------------------------- symmetric peer memory
+// Raw allocations of the per-generation heap; the Python side owns their lifetime.
+py::tuple symm_alloc(int64_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, static_cast<size_t>(bytes)) == cudaSuccess, "symm_alloc: cudaMalloc of ", bytes, " bytes failed");
+  TORCH_CHECK(cudaMemset(p, 0, static_cast<size_t>(bytes)) == cudaSuccess, "symm_alloc: memset failed");
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, p) == cudaSuccess, "symm_alloc: cudaIpcGetMemHandle failed");
+  return py::make_tuple(reinterpret_cast<int64_t>(p), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t symm_open(const std::string& handle, int64_t device) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "symm_open: bad handle size");
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "symm_open: cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+}
+
+void symm_free(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  cudaFree(reinterpret_cast<void*>(ptr));
+}
+
+// Non-owning tensor view of heap memory.
+torch::Tensor symm_tensor(int64_t ptr, int64_t numel, const std::string& dtype, int64_t device) {
+  torch::ScalarType st;
+  if (dtype == "float32") st = torch::kFloat32;
+  else if (dtype == "bfloat16") st = torch::kBFloat16;
+  else if (dtype == "int32") st = torch::kInt32;
+  else if (dtype == "int64") st = torch::kInt64;
+  else if (dtype == "uint8") st = torch::kUInt8;
+  else TORCH_CHECK(false, "symm_tensor: unsupported dtype ", dtype);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, [](void*) {},
+                          torch::TensorOptions().dtype(st).device(torch::kCUDA, device));
+}
+
+// Pinned, device-mapped host words (the abort word): the host writes, kernels poll.
+py::tuple host_words_alloc(int64_t n) {
+  void* h = nullptr;
+  TORCH_CHECK(cudaHostAlloc(&h, n * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess,
+              "host_words_alloc failed");
+  std::memset(h, 0, n * sizeof(int));
+  void* d = nullptr;
+  TORCH_CHECK(cudaHostGetDevicePointer(&d, h, 0) == cudaSuccess, "cudaHostGetDevicePointer failed");
+  return py::make_tuple(reinterpret_cast<int64_t>(h), reinterpret_cast<int64_t>(d));
+}
+
+void host_words_free(int64_t host_ptr) { cudaFreeHost(reinterpret_cast<void*>(host_ptr)); }
+
+void host_word_set(int64_t host_ptr, int64_t i, int64_t value) {
+  reinterpret_cast<volatile int*>(host_ptr)[i] = static_cast<int>(value);
+}
+
+int64_t host_word_get(int64_t host_ptr, int64_t i) { return reinterpret_cast<volatile int*>(host_ptr)[i]; }
+
+int64_t symm_signal_bytes(int64_t world) { return rb::symm_signal_bytes(static_cast<int>(world)); }
+
+// pads: int64 CUDA tensor [world] of signal-pad addresses (own pad at index rank).
+void symm_barrier(const torch::Tensor& pads, int64_t rank, int64_t world, int64_t epoch, int64_t abort_dev,
+                  torch::Tensor& status, double budget_s) {
+  TORCH_CHECK(pads.is_cuda() && pads.scalar_type() == torch::kInt64 && pads.numel() == world, "bad pads");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 2, "bad status");
+  const c10::cuda::CUDAGuard g(pads.device());
+  RB_CALL(rb::symm_barrier(reinterpret_cast<unsigned long long* const*>(pads.data_ptr<int64_t>()),
+                           static_cast<int>(rank), static_cast<int>(world), static_cast<unsigned long long>(epoch),
+                           reinterpret_cast<const int*>(abort_dev), status.data_ptr<int>(), err_ptr(pads), budget_s,
+                           cur_stream()), "symm_barrier");
+}
+
+void dp_step_fused(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& weight_ptrs,
+                   torch::Tensor& master, torch::Tensor& m, torch::Tensor& v, int64_t shard_lo, double lr, double b1,
+                   double b2, double eps, double wd, bool decoupled, int64_t step, double grad_scale,
+                   int64_t abort_dev) {
+  CHECK_F32(master); CHECK_F32(m); CHECK_F32(v);
+  TORCH_CHECK(grad_ptrs.size() == weight_ptrs.size() && !grad_ptrs.empty(), "one grad and weight pointer per rank");
+  std::vector<const float*> g(grad_ptrs.size());
+  std::vector<__nv_bfloat16*> w(weight_ptrs.size());
+  for (size_t i = 0; i < g.size(); ++i) {
+    g[i] = reinterpret_cast<const float*>(grad_ptrs[i]);
+    w[i] = reinterpret_cast<__nv_bfloat16*>(weight_ptrs[i]);
+  }
+  const double bc1 = 1.0 - std::pow(b1, static_cast<double>(step));
+  const double bc2 = 1.0 - std::pow(b2, static_cast<double>(step));
+  const c10::cuda::CUDAGuard guard(master.device());
+  RB_CALL(rb::dp_step_fused(g.data(), w.data(), static_cast<int>(g.size()), master.data_ptr<float>(),
+                            m.data_ptr<float>(), v.data_ptr<float>(), shard_lo, master.numel(), lr, b1, b2, eps, wd,
+                            decoupled ? 1 : 0, static_cast<float>(bc1), static_cast<float>(std::sqrt(bc2)),
+                            static_cast<float>(grad_scale), reinterpret_cast<const int*>(abort_dev),
+                            num_sms(master.get_device()), cur_stream()), "dp_step_fused");
+}
+
 torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(device)); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -301,6 +404,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"),
         py::arg("impl") = 0);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_free", &symm_free);
+  m.def("symm_tensor", &symm_tensor);
+  m.def("host_words_alloc", &host_words_alloc);
+  m.def("host_words_free", &host_words_free);
+  m.def("host_word_set", &host_word_set);
+  m.def("host_word_get", &host_word_get);
+  m.def("symm_signal_bytes", &symm_signal_bytes);
+  m.def("symm_barrier", &symm_barrier);
+  m.def("dp_step_fused", &dp_step_fused);
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("S"),
         py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0);

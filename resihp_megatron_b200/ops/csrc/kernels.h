@@ -3,6 +3,7 @@
 // positive values are CUDA error codes.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -70,6 +71,14 @@ struct AttnBwdArgs {
 int attention_fwd_mma(const AttnArgs& a, int D, cudaStream_t s);
 int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t s);
 int attention_bwd_mma(const AttnBwdArgs& a, int D, cudaStream_t s);
+// Symmetric peer memory (symm.cu).
+int symm_signal_bytes(int world);
+int symm_barrier(unsigned long long* const* pads_dev, int rank, int world, unsigned long long epoch,
+                 const int* abort_word, int* status, int* err, double budget_s, cudaStream_t s);
+int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int world, float* master, float* m,
+                  float* v, long long shard_lo, long long n, float lr, float b1, float b2, float eps, float wd,
+                  int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
+                  cudaStream_t s);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
 int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
 }  // namespace rb

@@ -1,0 +1,197 @@
+// Symmetric peer memory for one generation of ranks on one NVLink/NVSwitch node, and the
+// kernels that use it.
+//
+// * Heap: each rank cudaMallocs one region, exports a CUDA IPC handle, and maps every peer's
+//   region (cudaIpcOpenMemHandle); a generation change unmaps and rebuilds.  The first
+//   kSignalBytes of every region are a signal pad: slot p (one 64-bit word per rank, on its own
+//   128-byte line) is written only by rank p.
+// * Abort word: pinned, host-mapped memory.  The control plane sets it from the host while a
+//   kernel runs; every spin-wait below polls it and returns with an error status.
+// * Barrier kernel: rank r stores `epoch` into slot r of every peer's pad (release, system
+//   scope, after a system fence so all earlier writes of this rank are visible), then waits --
+//   bounded by %globaltimer -- until every slot of its own pad reaches `epoch`.  Runs as one
+//   block; ranks are different GPUs, so the waiting kernels always run concurrently.
+// * Fused data-parallel step: rank r owns a contiguous shard of the flat parameter space.  One
+//   kernel sums the shard's fp32 gradients over all ranks with peer loads in rank order (fixed
+//   order: deterministic and identical on every rank), applies Adam to the fp32 master shard,
+//   and stores the new bf16 weights of the shard into every rank's weight buffer with peer
+//   stores: reduce-scatter + optimizer + all-gather in one pass over NVLink, with no
+//   intermediate buffers.
+//
+// Only this file's own kernels touch peer memory; no TMA and no library kernel reads it.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace rb {
+
+namespace {
+
+constexpr int kPadStride = 16;  // 64-bit words per signal slot (128 bytes)
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// status[0] = 0 ok, 1 timeout, 2 aborted; status[1] = the rank that was waited for.
+__global__ void symm_barrier_kernel(unsigned long long* const* pads, int rank, int world, unsigned long long epoch,
+                                    const int* abort_word, int* status, int* err, unsigned long long budget_ns) {
+  __threadfence_system();
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < world) st_release_sys(pads[t] + rank * kPadStride, epoch);
+  __syncthreads();
+  if (t < world) {
+    const unsigned long long* mine = pads[rank] + t * kPadStride;
+    const uint64_t t0 = globaltimer();
+    int outcome = 0;
+    while (ld_acquire_sys(mine) < epoch) {
+      if (abort_word != nullptr && ld_volatile_int(abort_word) != 0) {
+        outcome = 2;
+        break;
+      }
+      if (globaltimer() - t0 > budget_ns) {
+        outcome = 1;
+        break;
+      }
+      __nanosleep(200);
+    }
+    if (outcome != 0) {
+      if (atomicCAS(status, 0, outcome) == 0) status[1] = t;
+      record_error(err, outcome == 1 ? kErrPeerTimeout : kErrAborted);
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
+constexpr int kMaxWorld = 16;
+
+struct DpStepArgs {
+  const float* grads[kMaxWorld];     // every rank's full gradient buffer (peer pointers)
+  __nv_bfloat16* weights[kMaxWorld];  // every rank's full bf16 weight buffer (peer pointers)
+  float* master;                      // this rank's shard
+  float* m;
+  float* v;
+  long long shard_lo, n;
+  int world;
+  float lr, b1, b2, eps, wd, bc1, bc2_sqrt, grad_scale;
+  int decoupled;
+  const int* abort_word;
+};
+
+// 4 elements per thread, grid-stride.  Loads of the W gradients are issued together before
+// the sum so their NVLink latencies overlap.
+__global__ void __launch_bounds__(256) dp_step_kernel(const __grid_constant__ DpStepArgs a) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x * 4;
+  const float step_size = a.lr / a.bc1;
+  for (long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < a.n; i += stride) {
+    if (a.abort_word != nullptr && ld_volatile_int(a.abort_word) != 0) return;
+    const long long gi = a.shard_lo + i;
+    float4 parts[kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+      if (r < a.world) parts[r] = __ldcv(reinterpret_cast<const float4*>(a.grads[r] + gi));
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+      if (r < a.world) {
+        g[0] += parts[r].x;
+        g[1] += parts[r].y;
+        g[2] += parts[r].z;
+        g[3] += parts[r].w;
+      }
+    float4 pp = *reinterpret_cast<const float4*>(a.master + i);
+    float4 mm = *reinterpret_cast<const float4*>(a.m + i);
+    float4 vv = *reinterpret_cast<const float4*>(a.v + i);
+    float* P = &pp.x;
+    float* M = &mm.x;
+    float* V = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float gj = g[j] * a.grad_scale;
+      if (a.wd != 0.f) {
+        if (a.decoupled) P[j] *= (1.f - a.lr * a.wd);
+        else gj = gj + a.wd * P[j];
+      }
+      M[j] = M[j] + (1.f - a.b1) * (gj - M[j]);
+      V[j] = V[j] * a.b2 + (1.f - a.b2) * gj * gj;
+      const float denom = sqrtf(V[j]) / a.bc2_sqrt + a.eps;
+      P[j] = P[j] - step_size * (M[j] / denom);
+    }
+    *reinterpret_cast<float4*>(a.master + i) = pp;
+    *reinterpret_cast<float4*>(a.m + i) = mm;
+    *reinterpret_cast<float4*>(a.v + i) = vv;
+    uint2 u;
+    u.x = pack_bf16x2(pp.x, pp.y);
+    u.y = pack_bf16x2(pp.z, pp.w);
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+      if (r < a.world) __stcg(reinterpret_cast<uint2*>(a.weights[r] + gi), u);
+  }
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------------- host side
+int symm_signal_bytes(int world) { return world * kPadStride * 8; }
+
+int symm_barrier(unsigned long long* const* pads_dev, int rank, int world, unsigned long long epoch,
+                 const int* abort_word, int* status, int* err, double budget_s, cudaStream_t s) {
+  if (world < 1 || world > 1024 || rank < 0 || rank >= world) return -1;
+  const int threads = ((world + 31) / 32) * 32;
+  symm_barrier_kernel<<<1, threads, 0, s>>>(pads_dev, rank, world, epoch, abort_word, status, err,
+                                            static_cast<unsigned long long>(budget_s * 1e9));
+  return static_cast<int>(cudaGetLastError());
+}
+
+int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int world, float* master, float* m,
+                  float* v, long long shard_lo, long long n, float lr, float b1, float b2, float eps, float wd,
+                  int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
+                  cudaStream_t s) {
+  if (world < 1 || world > kMaxWorld || (n & 3) || (shard_lo & 3)) return -1;
+  DpStepArgs a{};
+  for (int r = 0; r < world; ++r) {
+    a.grads[r] = grads[r];
+    a.weights[r] = weights[r];
+    if ((reinterpret_cast<uintptr_t>(grads[r]) & 15) || (reinterpret_cast<uintptr_t>(weights[r]) & 7)) return -2;
+  }
+  if ((reinterpret_cast<uintptr_t>(master) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15)
+    return -2;
+  a.master = master;
+  a.m = m;
+  a.v = v;
+  a.shard_lo = shard_lo;
+  a.n = n;
+  a.world = world;
+  a.lr = lr;
+  a.b1 = b1;
+  a.b2 = b2;
+  a.eps = eps;
+  a.wd = wd;
+  a.decoupled = decoupled;
+  a.bc1 = bc1;
+  a.bc2_sqrt = bc2_sqrt;
+  a.grad_scale = grad_scale;
+  a.abort_word = abort_word;
+  const long long threads_needed = n / 4;
+  long long blocks = (threads_needed + 255) / 256;
+  const long long cap = static_cast<long long>(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  dp_step_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rb

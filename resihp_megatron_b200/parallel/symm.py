@@ -1,0 +1,182 @@
+"""Per-generation symmetric peer memory on one NVLink/NVSwitch node.
+
+Each rank allocates one device region holding a signal pad and named segments at identical
+offsets, exports a CUDA IPC handle, and maps every peer's region; kernels then read and write
+peers' segments directly over NVLink.  A reconfiguration tears the heap down (``close``) and
+builds the next generation's heap over the new world -- the counterpart of rebuilding NCCL
+communicators (reference: ``resihp/comm/comm_manager.py:138-251``).
+
+``AbortWord`` is pinned host memory mapped into the device: the control plane raises it from
+the host (``ResilientCommManager.add_abort_hook``) while a kernel runs, and every bounded wait
+in the peer kernels polls it, so survivors leave an in-flight fused kernel without waiting for a
+timeout.  ``barrier`` is a bounded cross-GPU barrier on the signal pad; its outcome is read with
+``check`` (which synchronises) and raised as ``PeerTimeout`` / ``PeerAborted``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+
+from ..ops._build import ext
+
+ALIGN = 256
+_DTYPES = {torch.float32: "float32", torch.bfloat16: "bfloat16", torch.int32: "int32", torch.int64: "int64",
+           torch.uint8: "uint8"}
+
+
+class PeerTimeout(RuntimeError):
+    pass
+
+
+class PeerAborted(RuntimeError):
+    pass
+
+
+class AbortWord:
+    """One host-mapped int per device context; ``set()`` is safe from any host thread."""
+
+    def __init__(self):
+        self.host, self.dev = ext().host_words_alloc(4)
+
+    def set(self, value: int = 1) -> None:
+        ext().host_word_set(self.host, 0, value)
+
+    def clear(self) -> None:
+        ext().host_word_set(self.host, 0, 0)
+
+    @property
+    def raised(self) -> bool:
+        return ext().host_word_get(self.host, 0) != 0
+
+    def close(self) -> None:
+        if self.host:
+            ext().host_words_free(self.host)
+            self.host = self.dev = 0
+
+
+@dataclass
+class Segment:
+    offset: int
+    numel: int
+    dtype: torch.dtype
+
+    @property
+    def nbytes(self) -> int:
+        return self.numel * torch.empty(0, dtype=self.dtype).element_size()
+
+
+def layout(segments: dict[str, tuple[int, torch.dtype]], world: int) -> tuple[dict[str, Segment], int, int]:
+    """Offsets of the signal pad and of every segment; returns (segments, pad bytes, total)."""
+    pad = (ext().symm_signal_bytes(world) + ALIGN - 1) // ALIGN * ALIGN
+    off = pad
+    out = {}
+    for name, (numel, dtype) in segments.items():
+        seg = Segment(off, numel, dtype)
+        out[name] = seg
+        off += (seg.nbytes + ALIGN - 1) // ALIGN * ALIGN
+    return out, pad, off
+
+
+class SymmetricHeap:
+    """``exchange(handle: bytes) -> list[bytes]`` all-gathers the IPC handles in rank order
+    (``exchange_via_group`` / ``exchange_via_store``)."""
+
+    def __init__(self, segments: dict[str, tuple[int, torch.dtype]], rank: int, world: int,
+                 exchange: Callable[[bytes], list[bytes]] | None, device, abort: AbortWord | None = None,
+                 _bases: list[int] | None = None):
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.segments, self.pad_bytes, self.nbytes = layout(segments, world)
+        self.abort = abort
+        self.epoch = 0
+        self._opened: list[int] = []
+        if _bases is not None:  # emulated ranks in one process (tests on one GPU)
+            self.bases = list(_bases)
+            self.local_base = self.bases[rank]
+            self._owns_local = False
+        else:
+            self.local_base, handle = ext().symm_alloc(self.nbytes, self.dev_index)
+            self._owns_local = True
+            handles = exchange(handle) if world > 1 else [handle]
+            assert len(handles) == world
+            self.bases = []
+            for r, h in enumerate(handles):
+                if r == rank:
+                    self.bases.append(self.local_base)
+                else:
+                    p = ext().symm_open(h, self.dev_index)
+                    self._opened.append(p)
+                    self.bases.append(p)
+        self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    @classmethod
+    def emulated(cls, segments: dict[str, tuple[int, torch.dtype]], world: int, device) -> list["SymmetricHeap"]:
+        """``world`` heaps in one process on one device, wired as peers of each other.  Only for
+        kernels that do not wait on one another (one launch per emulated rank in turn)."""
+        _, _, total = layout(segments, world)
+        dev = torch.device(device)
+        idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        bases = [ext().symm_alloc(total, idx)[0] for _ in range(world)]
+        heaps = [cls(segments, r, world, None, dev, _bases=bases) for r in range(world)]
+        heaps[0]._emulated_bases = bases
+        return heaps
+
+    # -- views
+    def tensor(self, name: str, rank: int | None = None) -> torch.Tensor:
+        seg = self.segments[name]
+        base = self.bases[self.rank if rank is None else rank]
+        return ext().symm_tensor(base + seg.offset, seg.numel, _DTYPES[seg.dtype], self.dev_index)
+
+    def peer_ptrs(self, name: str) -> list[int]:
+        off = self.segments[name].offset
+        return [b + off for b in self.bases]
+
+    # -- synchronisation
+    def barrier(self, budget_s: float = 30.0) -> None:
+        """Enqueue a bounded barrier over all ranks on the current stream."""
+        self.epoch += 1
+        ext().symm_barrier(self.pads, self.rank, self.world, self.epoch, self.abort.dev if self.abort else 0,
+                           self.status, float(budget_s))
+
+    def check(self) -> None:
+        st = self.status.tolist()
+        if st[0] == 1:
+            raise PeerTimeout(f"rank {self.rank}: peer {st[1]} did not reach the barrier in time")
+        if st[0] == 2 or (self.abort is not None and self.abort.raised):
+            raise PeerAborted(f"rank {self.rank}: aborted by the control plane")
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            ext().symm_close(p, self.dev_index)
+        self._opened = []
+        if self._owns_local and self.local_base:
+            ext().symm_free(self.local_base, self.dev_index)
+        for b in getattr(self, "_emulated_bases", []):
+            ext().symm_free(b, self.dev_index)
+        self._emulated_bases = []
+        self.local_base = 0
+
+
+def exchange_via_group(group=None) -> Callable[[bytes], list[bytes]]:
+    import torch.distributed as dist
+
+    def exchange(handle: bytes) -> list[bytes]:
+        out: list = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, handle, group=group)
+        return out
+
+    return exchange
+
+
+def exchange_via_store(store, prefix: str, rank: int, world: int) -> Callable[[bytes], list[bytes]]:
+    def exchange(handle: bytes) -> list[bytes]:
+        store.set(f"{prefix}/{rank}", handle)
+        return [bytes(store.get(f"{prefix}/{r}")) for r in range(world)]
+
+    return exchange

@@ -4,7 +4,9 @@
 ids and labels for this rank (pinned host tensors), copies them to the device, runs every
 micro-batch forward and backward on the package's kernels, reduces the gradients across the
 data-parallel group, applies Adam to this rank's shard of the fp32 master weights, gathers
-the updated bf16 weights, and returns the step's mean token loss.
+the updated bf16 weights, and returns the step's mean token loss.  With ``dp_impl="fused"``
+(default) reduction, Adam and gather are one kernel over NVLink peer memory
+(``parallel.dp_fused``); ``"nccl"`` uses reduce-scatter / Adam / all-gather.
 
 Gradients are scaled by ``1 / tokens in the global batch`` inside the cross-entropy kernel,
 so the reduced gradient is the gradient of the global mean loss whatever the DP degree.
@@ -28,7 +30,7 @@ from ..models.gpt import LlamaModel
 class GPUTrainer:
     def __init__(self, cfg: GPTConfig, *, global_batch: int, micro_batch: int = 1, seq_len: int | None = None,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, seed: int = 0,
-                 device=None, dp_group: dist.ProcessGroup | None = None):
+                 device=None, dp_group: dist.ProcessGroup | None = None, dp_impl: str = "fused"):
         self.cfg = cfg
         self.S = seq_len or cfg.seq_len
         self.group = dp_group
@@ -44,13 +46,26 @@ class GPUTrainer:
         self.n_micro = self.local_batch // micro_batch
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
+        if dp_impl not in ("fused", "nccl"):
+            raise ValueError(dp_impl)
+        self.dp_impl = dp_impl if self.dp > 1 else "single"
+        self.fused = None
+        factory = None
+        if self.dp_impl == "fused":
+            from ..parallel.dp_fused import FusedDataParallel
+            from ..parallel.symm import AbortWord, exchange_via_group
+
+            self.abort_word = AbortWord()
+            self.fused = FusedDataParallel(self.rank, self.dp, exchange_via_group(dp_group), self.device,
+                                           abort=self.abort_word)
+            factory = self.fused.buffer_factory
         self.model = LlamaModel(cfg, self.device, micro_batch=micro_batch, seq_len=self.S, seed=seed,
-                                shard_rank=self.rank, shard_count=self.dp)
+                                shard_rank=self.rank, shard_count=self.dp, buffer_factory=factory)
         self.tokens_per_step = global_batch * self.S
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
         self.labels_dev = torch.empty_like(self.ids_dev)
         P = self.model.params
-        if self.dp > 1:
+        if self.dp_impl == "nccl":
             self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
         self.step_count = 0
 
@@ -78,6 +93,11 @@ class GPUTrainer:
         if self.dp == 1:
             ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, zero_grad=True, **kw)
             return
+        if self.dp_impl == "fused":
+            dist.all_reduce(self.model.loss_acc, group=self.group)
+            self.fused.step(P, lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)
+            ops.count(3)  # barrier, fused step, barrier
+            return
         dist.reduce_scatter_tensor(self.grad_shard, P.grad, op=dist.ReduceOp.SUM, group=self.group)
         dist.all_reduce(self.model.loss_acc, group=self.group)
         P.grad.zero_()
@@ -92,7 +112,16 @@ class GPUTrainer:
         self.ids_dev.copy_(ids_host, non_blocking=True)
         self.labels_dev.copy_(labels_host, non_blocking=True)
         loss = self.step_device(self.ids_dev, self.labels_dev)
-        return float(loss.item())
+        value = float(loss.item())
+        if self.fused is not None:
+            self.fused.check()
+        return value
+
+    def close(self) -> None:
+        """Release the symmetric heap (before the process group is destroyed)."""
+        if self.fused is not None:
+            self.fused.close()
+            self.fused = None
 
 
 def init_distributed(timeout_s: float = 300.0) -> tuple[int, int, int]:

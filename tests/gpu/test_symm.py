@@ -1,0 +1,81 @@
+"""Symmetric peer memory on one GPU: the fused data-parallel step with emulated ranks against
+an fp32 reference, and the bounded barrier's timeout and abort paths (a flag nothing sets; the
+kernel returns a status, the context stays usable)."""
+
+import time
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_fused_dp_step_emulated_ranks_matches_reference():
+    from resihp_megatron_b200.ops._build import ext
+    from resihp_megatron_b200.parallel.symm import SymmetricHeap
+
+    W, n = 4, 1 << 16
+    heaps = SymmetricHeap.emulated({"grad": (n, torch.float32), "weight": (n, torch.bfloat16)}, W, "cuda")
+    torch.manual_seed(0)
+    grads = [torch.randn(n, device="cuda") for _ in range(W)]
+    for r, h in enumerate(heaps):
+        h.tensor("grad").copy_(grads[r])
+    master = torch.randn(n, device="cuda")
+    shard = n // W
+    lr, b1, b2, eps, wd, scale, step = 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.5, 3
+    m0 = torch.randn(n, device="cuda").abs() * 0.01
+    v0 = torch.randn(n, device="cuda").abs() * 0.01
+    states = []
+    for r, h in enumerate(heaps):
+        sl = slice(r * shard, (r + 1) * shard)
+        st = [master[sl].clone(), m0[sl].clone(), v0[sl].clone()]
+        ext().dp_step_fused(h.peer_ptrs("grad"), h.peer_ptrs("weight"), st[0], st[1], st[2], r * shard, lr, b1, b2,
+                            eps, wd, False, step, scale, 0)
+        states.append(st)
+    torch.cuda.synchronize()
+    # fp32 reference in the same formula order as torch.optim.Adam (L2 weight decay)
+    g = sum(grads) * scale + wd * master
+    m = m0 + (1 - b1) * (g - m0)
+    v = v0 * b2 + (1 - b2) * g * g
+    bc1, bc2 = 1 - b1 ** step, 1 - b2 ** step
+    p = master - lr / bc1 * (m / (v.sqrt() / bc2 ** 0.5 + eps))
+    got = torch.cat([s[0] for s in states])
+    torch.testing.assert_close(got, p, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(torch.cat([s[1] for s in states]), m, rtol=1e-5, atol=1e-7)
+    for h in heaps:  # every rank received every shard
+        assert torch.equal(h.tensor("weight"), got.bfloat16())
+    heaps[0].close()
+
+
+def test_barrier_single_rank_then_timeout_and_abort_paths():
+    from resihp_megatron_b200.parallel.symm import AbortWord, PeerAborted, PeerTimeout, SymmetricHeap
+
+    one = SymmetricHeap({"x": (16, torch.float32)}, 0, 1, None, "cuda")
+    one.barrier(1.0)
+    one.barrier(1.0)
+    one.check()
+    one.close()
+    # two emulated ranks, but only rank 0 ever arrives: its wait runs out and reports rank 1
+    pair = SymmetricHeap.emulated({"x": (16, torch.float32)}, 2, "cuda")
+    t0 = time.monotonic()
+    pair[0].barrier(0.3)
+    with pytest.raises(PeerTimeout, match="peer 1"):
+        pair[0].check()
+    assert time.monotonic() - t0 < 10
+    # the raised abort word ends the wait early
+    abort = AbortWord()
+    pair[0].abort = abort
+    pair[0].status.zero_()
+    abort.set()
+    pair[0].barrier(30.0)
+    t0 = time.monotonic()
+    with pytest.raises(PeerAborted):
+        pair[0].check()
+    assert time.monotonic() - t0 < 5
+    abort.close()
+    from resihp_megatron_b200.ops.gemm import error_state
+
+    error_state().zero_()  # the intended timeout recorded an error word
+    x = torch.ones(4, device="cuda") * 2  # context still usable
+    assert x.sum().item() == 8
+    pair[0].close()
