@@ -55,7 +55,7 @@ long long ld_of(const torch::Tensor& t, const char* name) {
 
 // out[M,N] (+)= alpha * op(a) @ op(b)^T ; a is [M,K] (or [K,M] if a_t), b is [N,K] (or [K,N] if b_t)
 void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, torch::Tensor& out,
-          int64_t epi, double alpha, const c10::optional<torch::Tensor>& residual) {
+          int64_t epi, double alpha, const c10::optional<torch::Tensor>& residual, int64_t variant) {
   check_cuda(a, "a");
   check_cuda(b, "b");
   check_cuda(out, "out");
@@ -91,7 +91,8 @@ void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, to
   }
   const int rc = rb::gemm_bf16(a.data_ptr(), lda, a_t, b.data_ptr(), ldb, b_t, out.data_ptr(), ldd, rptr, ldr,
                                M, N, K, static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a),
-                               num_sms(a.get_device()), at::cuda::getCurrentCUDAStream());
+                               num_sms(a.get_device()), at::cuda::getCurrentCUDAStream(),
+                               static_cast<int>(variant));
   TORCH_CHECK(rc == 0, "gemm_bf16 failed with code ", rc);
 }
 
@@ -389,7 +390,8 @@ torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(d
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of resihp_megatron_b200";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_t"), py::arg("b"), py::arg("b_t"),
-        py::arg("out"), py::arg("epi"), py::arg("alpha"), py::arg("residual") = py::none());
+        py::arg("out"), py::arg("epi"), py::arg("alpha"), py::arg("residual") = py::none(),
+        py::arg("variant") = 0);
   m.def("error_state", &error_state, "per-device kernel error words");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

@@ -65,6 +65,65 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   nb = r / gsize;
 }
 
+// Epilogue of one 32-column chunk of one accumulator row: scale, optional residual / fp32
+// accumulate, vector stores (column tail handled scalar).
+template <int EPI>
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], int row, int col0, const GemmArgs& p) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+  const bool full = (col0 + 32 <= p.N);
+  if (EPI == kEpiBF16 || EPI == kEpiBF16Res) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+    if (EPI == kEpiBF16Res) {
+      const __nv_bfloat16* res = p.R + row * p.ldr + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 u = *reinterpret_cast<const uint4*>(res + 8 * j);
+          float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y), f2 = unpack_bf16x2(u.z),
+                 f3 = unpack_bf16x2(u.w);
+          v[8 * j + 0] += f0.x; v[8 * j + 1] += f0.y; v[8 * j + 2] += f1.x; v[8 * j + 3] += f1.y;
+          v[8 * j + 4] += f2.x; v[8 * j + 5] += f2.y; v[8 * j + 6] += f3.x; v[8 * j + 7] += f3.y;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N) v[j] += __bfloat162float(res[j]);
+      }
+    }
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 u;
+        u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        *reinterpret_cast<uint4*>(dst + 8 * j) = u;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (EPI == kEpiF32Acc) {
+          const float4 old = *reinterpret_cast<const float4*>(dst + 4 * j);
+          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+        }
+        *reinterpret_cast<float4*>(dst + 4 * j) = o;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) dst[j] = (EPI == kEpiF32Acc) ? dst[j] + v[j] : v[j];
+    }
+  }
+}
+
 // lane 0 waits, the whole warp learns the outcome
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
@@ -238,59 +297,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_wait();
         const int col0 = nb * BN + c * 32;
         if (!row_ok || col0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-        const bool full = (col0 + 32 <= p.N);
-        if (EPI == kEpiBF16 || EPI == kEpiBF16Res) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
-          if (EPI == kEpiBF16Res) {
-            const __nv_bfloat16* res = p.R + row * p.ldr + col0;
-            if (full) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint4 u = *reinterpret_cast<const uint4*>(res + 8 * j);
-                float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y), f2 = unpack_bf16x2(u.z),
-                       f3 = unpack_bf16x2(u.w);
-                v[8 * j + 0] += f0.x; v[8 * j + 1] += f0.y; v[8 * j + 2] += f1.x; v[8 * j + 3] += f1.y;
-                v[8 * j + 4] += f2.x; v[8 * j + 5] += f2.y; v[8 * j + 6] += f3.x; v[8 * j + 7] += f3.y;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) v[j] += __bfloat162float(res[j]);
-            }
-          }
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 u;
-              u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-              u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-              u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-              u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-              *reinterpret_cast<uint4*>(dst + 8 * j) = u;
-            }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
-          }
-        } else {
-          float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col0;
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-              if (EPI == kEpiF32Acc) {
-                const float4 old = *reinterpret_cast<const float4*>(dst + 4 * j);
-                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-              }
-              *reinterpret_cast<float4*>(dst + 4 * j) = o;
-            }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) dst[j] = (EPI == kEpiF32Acc) ? dst[j] + v[j] : v[j];
-          }
-        }
+        store_chunk<EPI>(r, row, col0, p);
       }
       tc_fence_before();
       __syncwarp();
@@ -305,6 +312,226 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------- CTA-pair kernel
+// Same roles, but a cluster of two CTAs computes one 256 x 256 tile with cta_group::2 MMAs:
+// CTA r holds rows [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B
+// tile, and its TMEM receives rows [128 r, 128 r + 128) of D (all 256 columns).  Per k-block each
+// CTA loads 32 KB instead of 48 KB, so 6 stages fit and L2->SM traffic per FLOP drops by a third.
+//   * both CTAs' TMA loads count on the leader's full barrier (the leader expects both halves);
+//   * the leader issues the MMAs and commits separately to each CTA's empty / accumulator-full
+//     barriers (no multicast);
+//   * epilogue warps of both CTAs release the accumulator on the leader's barrier (8 arrivals).
+struct PairCfg {
+  static constexpr int BM = 128;  // rows per CTA (the pair covers 256)
+  static constexpr int BN = 256;  // columns of the pair's tile
+  static constexpr int BNH = 128; // B rows held per CTA
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BNH * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 192;
+  static constexpr int GROUP_M = 8;  // in 256-row pair tiles
+};
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         GemmArgs p) {
+  using C = PairCfg;
+  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 4]);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
+  const int num_n = (p.N + C::BN - 1) / C::BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += num_pairs) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
+        const int m0 = mb * 2 * BM + static_cast<int>(cta) * BM;
+        const int n0 = nb * C::BN + static_cast<int>(cta) * C::BNH;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = full_bar(stage);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * C::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(fb_local, 0);
+          const uint32_t a_dst = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_dst = smem_u32(sB + stage * C::B_BYTES);
+          if (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 8192, &tmA, fb, m0 + 64 * j, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < C::BNH / 64; ++j) tma_load_2d_pair(b_dst + j * 8192, &tmB, fb, n0 + 64 * j, kb * BK);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain (leader: its full barriers count both CTAs' loads; the peer's loads of a stage
+      // complete before the leader's barrier phase does).
+      if (leader)
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_f16(2 * BM, C::BN, true, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+        if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? make_smem_desc(a_base + k * 2048, 8192, 1024, kSwizzle128B)
+                                     : make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = B_MN ? make_smem_desc(b_base + k * 2048, 8192, 1024, kSwizzle128B)
+                                     : make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty_bar(stage));
+          umma_commit_pair(mapa_shared(empty_bar(stage), 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc));
+        umma_commit_pair(mapa_shared(tfull_bar(acc), 1));
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1;
+      }
+      umma_commit_pair(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    const uint32_t release = leader ? 0u : mapa_shared(tempty_bar(0), 0);  // peer: leader's barrier
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
+      if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = mb * 2 * BM + static_cast<int>(cta) * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < C::BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::BN + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nb * C::BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        store_chunk<EPI>(r, row, col0, p);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(tempty_bar(acc));
+        else mbar_arrive_cluster(release + acc * 8);
+      }
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs may still read its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -356,6 +583,33 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   return static_cast<int>(cudaGetLastError());
 }
 
+template <bool A_MN, bool B_MN, int EPI>
+static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
+                            cudaStream_t stream) {
+  using C = PairCfg;
+  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  const int tiles = ((a.M + 2 * C::BM - 1) / (2 * C::BM)) * ((a.N + C::BN - 1) / C::BN);
+  int pairs = num_sms / 2;
+  if (tiles < pairs) pairs = tiles;
+  kern<<<2 * pairs, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int EPI>
+static int dispatch_major_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                               const GemmArgs& a, int num_sms, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, a, num_sms, s);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, a, num_sms, s);
+  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, a, num_sms, s);
+  return launch_gemm_pair<true, true, EPI>(ta, tb, a, num_sms, s);
+}
+
 template <int BN, int EPI>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           const GemmArgs& a, int num_sms, cudaStream_t s) {
@@ -381,7 +635,7 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, co
 // Returns 0 on success, a negative value for a bad argument, else a CUDA error code.
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn,
               void* D, long long ldd, const void* R, long long ldr, int M, int N, int K, int epi,
-              float alpha, int* err, int num_sms, cudaStream_t stream) {
+              float alpha, int* err, int num_sms, cudaStream_t stream, int variant) {
   if (M <= 0 || N <= 0 || K <= 0) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
   if ((lda * 2) % 16 || (ldb * 2) % 16) return -5;
@@ -391,6 +645,24 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
   const int BN = (N <= 128) ? 128 : 256;
   CUtensorMap ta, tb;
   int rc;
+  // variant: 0 auto (CTA pair for large tiles), 1 single CTA, 2 CTA pair
+  const bool use_pair = variant == 2 || (variant == 0 && M >= 512 && N >= 256);
+  if (use_pair) {
+    if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
+    else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
+    if (rc) return -100 - rc;
+    if (!b_mn) rc = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, 128);
+    else rc = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, 64);
+    if (rc) return -100 - rc;
+    GemmArgs ga{M, N, K, D, ldd, reinterpret_cast<const __nv_bfloat16*>(R), ldr, alpha, err};
+    switch (epi) {
+      case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
+      case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
+      case kEpiF32Acc: return dispatch_major_pair<kEpiF32Acc>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
+      case kEpiBF16Res: return dispatch_major_pair<kEpiBF16Res>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
+    }
+    return -2;
+  }
   if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
   else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
   if (rc) return -100 - rc;

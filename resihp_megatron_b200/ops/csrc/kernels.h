@@ -12,7 +12,7 @@ namespace rb {
 
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* D,
               long long ldd, const void* R, long long ldr, int M, int N, int K, int epi, float alpha,
-              int* err, int num_sms, cudaStream_t stream);
+              int* err, int num_sms, cudaStream_t stream, int variant = 0);
 
 int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s);
 int rmsnorm_bwd_blocks(int T);

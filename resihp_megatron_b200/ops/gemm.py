@@ -39,6 +39,7 @@ def gemm(
     accumulate: bool = False,
     residual: torch.Tensor | None = None,
     alpha: float = 1.0,
+    variant: int = 0,
 ) -> torch.Tensor:
     M = a.shape[1] if a_t else a.shape[0]
     N = b.shape[1] if b_t else b.shape[0]
@@ -53,7 +54,7 @@ def gemm(
     if out is None:
         out = torch.empty((M, N), dtype=torch.float32 if epi in (EPI_F32, EPI_F32_ACC) else torch.bfloat16,
                           device=a.device)
-    ext().gemm(a, a_t, b, b_t, out, epi, float(alpha), residual)
+    ext().gemm(a, a_t, b, b_t, out, epi, float(alpha), residual, int(variant))
     count(1)
     return out
 

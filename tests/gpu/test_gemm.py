@@ -72,3 +72,33 @@ def test_gemm_large_square():
     torch.cuda.synchronize()
     err = (out.float() - ref).abs().max().item()
     assert err <= 1e-2 * ref.abs().max().item(), err
+
+
+PAIR_SHAPES = [(256, 256, 64), (640, 384, 320), (1000, 520, 200), (512, 1024, 1024)]
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_gemm_cta_pair_variant(M, N, K, a_t, b_t):
+    """The 2-CTA (cta_group::2) kernel against fp32 and against the single-CTA kernel, with every
+    epilogue (bf16, fp32, fp32 accumulate, bf16 + residual)."""
+    from resihp_megatron_b200.ops.gemm import error_state, gemm
+
+    a, b = _mk(M, N, K, a_t, b_t, seed=7)
+    ref = _ref(a, b, a_t, b_t)
+    scale = ref.abs().max().item()
+    pair = gemm(a, b, a_t=a_t, b_t=b_t, variant=2)
+    single = gemm(a, b, a_t=a_t, b_t=b_t, variant=1)
+    f32 = gemm(a, b, a_t=a_t, b_t=b_t, out_dtype=torch.float32, variant=2)
+    base = torch.randn(M, N, device="cuda")
+    acc = base.clone()
+    gemm(a, b, a_t=a_t, b_t=b_t, out=acc, accumulate=True, variant=2)
+    r = torch.randn(M, N, device="cuda").bfloat16()
+    res = gemm(a, b, a_t=a_t, b_t=b_t, residual=r, variant=2)
+    torch.cuda.synchronize()
+    assert int(error_state()[0]) == 0
+    assert (pair.float() - ref).abs().max().item() <= 1e-2 * scale + 1e-2
+    assert torch.equal(pair, single), "same math and summation order as the single-CTA kernel"
+    assert torch.allclose(f32, ref, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(acc, base + ref, rtol=1e-4, atol=1e-3)
+    assert (res.float() - (ref + r.float())).abs().max().item() <= 1e-2 * scale + 2e-2
