@@ -52,6 +52,8 @@ def _args():
     ap.add_argument("--seqs-per-gpu", type=int, default=SEQS_PER_GPU)
     ap.add_argument("--micro-batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=None, help="override (testing only; result is marked invalid)")
+    ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: fused NVLink reduction + Adam + gather kernel, or NCCL reduce-scatter/all-gather")
     return ap.parse_args()
 
 
@@ -146,7 +148,7 @@ def main() -> None:
     global_batch = args.seqs_per_gpu * world
     group = dist.group.WORLD if world > 1 else None
     trainer = GPUTrainer(cfg, global_batch=global_batch, micro_batch=args.micro_batch, seq_len=args.seq, seed=0,
-                         dp_group=group)
+                         dp_group=group, dp_impl=args.dp_impl)
     dev = trainer.device
 
     # synthetic data: uniform random token ids, next-token labels, one batch per step
@@ -232,7 +234,7 @@ def main() -> None:
                 "global_batch": global_batch,
                 "seq_len": args.seq,
                 "micro_batch": args.micro_batch,
-                "parallelism": "tp1pp1dp1" if world == 1 else f"dp{world}-zero1",
+                "parallelism": "tp1pp1dp1" if world == 1 else f"dp{world}-zero1-{args.dp_impl}",
                 "l2": "inputs larger than L2 (each step touches >100 GB of weights/grads/optimizer state)",
                 "params": cfg.num_params(),
                 "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * value / world / 1e12,
@@ -246,6 +248,8 @@ def main() -> None:
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        dist.barrier()
+        trainer.close()  # unmap peer memory before the process group goes away
         dist.barrier()
         dist.destroy_process_group()
 

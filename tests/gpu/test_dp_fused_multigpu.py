@@ -36,7 +36,11 @@ def _worker(rank, world, port, q):
         tr.close()
     dist.barrier()
     dist.destroy_process_group()
-    q.put((rank, out["fused"][0], out["nccl"][0], out["fused"][1], out["nccl"][1]))
+    import io
+
+    buf = io.BytesIO()  # bytes, not shared-memory tensors: the child exits before the parent reads
+    torch.save((rank, out["fused"][0], out["nccl"][0], out["fused"][1], out["nccl"][1]), buf)
+    q.put(buf.getvalue())
 
 
 def test_fused_dp_matches_nccl_path_on_two_gpus():
@@ -54,7 +58,9 @@ def test_fused_dp_matches_nccl_path_on_two_gpus():
         p.start()
     res = {}
     for _ in range(2):
-        r, lf, ln, wf, wn = q.get(timeout=600)
+        import io
+
+        r, lf, ln, wf, wn = torch.load(io.BytesIO(q.get(timeout=600)))
         res[r] = (lf, ln, wf, wn)
     for p in procs:
         p.join(timeout=60)
