@@ -50,7 +50,9 @@ def _args():
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--seqs-per-gpu", type=int, default=SEQS_PER_GPU)
-    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--micro-batch", type=int, default=None,
+                    help="sequences per micro-batch; default 1 on one GPU (the unsharded optimizer state leaves "
+                         "room for one), 2 on more (bigger GEMMs, fewer partial waves)")
     ap.add_argument("--layers", type=int, default=None, help="override (testing only; result is marked invalid)")
     ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
                     help="N > 1: fused NVLink reduction + Adam + gather kernel, or NCCL reduce-scatter/all-gather")
@@ -146,6 +148,8 @@ def main() -> None:
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
     global_batch = args.seqs_per_gpu * world
+    if args.micro_batch is None:
+        args.micro_batch = 1 if world == 1 else 2
     group = dist.group.WORLD if world > 1 else None
     trainer = GPUTrainer(cfg, global_batch=global_batch, micro_batch=args.micro_batch, seq_len=args.seq, seed=0,
                          dp_group=group, dp_impl=args.dp_impl)
