@@ -54,6 +54,10 @@ def _args():
                     help="sequences per micro-batch; default 1 on one GPU (the unsharded optimizer state leaves "
                          "room for one), 2 on more (bigger GEMMs, fewer partial waves)")
     ap.add_argument("--layers", type=int, default=None, help="override (testing only; result is marked invalid)")
+    ap.add_argument("--reconfig", action="store_true",
+                    help="N > 1: after the timed steps evict the last rank (planned, e.g. fail-slow), migrate its "
+                         "optimizer state peer to peer, and time the same steps on N-1 GPUs (pre/post tokens/s "
+                         "and the eviction-to-commit time)")
     ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
                     help="N > 1: fused NVLink reduction + Adam + gather kernel, or NCCL reduce-scatter/all-gather")
     return ap.parse_args()
@@ -219,6 +223,41 @@ def main() -> None:
     ids0, lab0 = host_batches[0]
     h2d = ids0.numel() * ids0.element_size() + lab0.numel() * lab0.element_size()
 
+    # ---- optional live reconfiguration: the last rank leaves, state migrates, N-1 GPUs continue
+    recfg, alive, post_group = None, True, None
+    if args.reconfig and world > 1 and args.dp_impl == "fused":
+        survivors = list(range(world - 1))
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        post_group = dist.new_group(survivors)
+        alive = trainer.shrink(survivors, post_group)
+        torch.cuda.synchronize()
+        commit_s = time.perf_counter() - t0
+        if alive:
+            g2 = torch.Generator().manual_seed(2)
+            post_batches = []
+            for _ in range(min(n_batches, 4)):
+                seq = torch.randint(0, cfg.vocab_size, (global_batch, args.seq + 1), generator=g2)
+                lo, hi = trainer.batch_offset, trainer.batch_offset + trainer.local_batch
+                post_batches.append((seq[lo:hi, :-1].contiguous().to(dev), seq[lo:hi, 1:].contiguous().to(dev)))
+            for s in range(max(2, min(args.warmup, 3))):
+                trainer.step_device(*post_batches[s % len(post_batches)])
+            torch.cuda.synchronize()
+            dist.barrier(group=post_group)
+            start.record()
+            for s in range(args.steps):
+                loss2 = trainer.step_device(*post_batches[s % len(post_batches)])
+            end.record()
+            torch.cuda.synchronize()
+            vals = torch.tensor([start.elapsed_time(end), commit_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX, group=post_group)
+            post_ms, commit_max = vals.tolist()
+            recfg = {"kind": "planned eviction of the last rank; optimizer shards migrated peer to peer over NVLink",
+                     "n_gpus_post": world - 1, "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
+                     "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
+                     "post_micro_batch": trainer.micro_batch, "post_loss": float(loss2.item())}
+
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -250,11 +289,19 @@ def main() -> None:
             "loss": last_loss,
             "impl": "ours",
         }
+        if recfg is not None:
+            out["reconfig"] = recfg
         print(json.dumps(out), flush=True)
     if world > 1:
-        dist.barrier()
-        trainer.close()  # unmap peer memory before the process group goes away
-        dist.barrier()
+        if post_group is not None:
+            if alive:
+                dist.barrier(group=post_group)
+                trainer.close()  # unmap peer memory before the process group goes away
+                dist.barrier(group=post_group)
+        else:
+            dist.barrier()
+            trainer.close()
+            dist.barrier()
         dist.destroy_process_group()
 
 

@@ -83,7 +83,7 @@ class LlamaModel:
 
     def __init__(self, cfg: GPTConfig, device="cuda", *, micro_batch: int = 1, seq_len: int | None = None,
                  seed: int = 0, layers: range | None = None, first: bool = True, last: bool = True,
-                 shard_rank: int = 0, shard_count: int = 1, buffer_factory=None):
+                 shard_rank: int = 0, shard_count: int = 1, buffer_factory=None, opt_factory=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.mb = micro_batch
@@ -91,13 +91,26 @@ class LlamaModel:
         self.T = self.mb * self.S
         self.layer_ids = list(layers if layers is not None else range(cfg.layers))
         self.first, self.last = first, last
-        self.params = FlatParams(model_param_specs(cfg, self.layer_ids, first, last), self.device,
-                                 shard_rank=shard_rank, shard_count=shard_count, buffer_factory=buffer_factory)
+        self.param_specs = model_param_specs(cfg, self.layer_ids, first, last)
+        self.params = FlatParams(self.param_specs, self.device, shard_rank=shard_rank, shard_count=shard_count,
+                                 buffer_factory=buffer_factory, opt_factory=opt_factory)
         self.params.initialize(seed, cfg.init_std)
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
         self._alloc()
 
     # ------------------------------------------------------------------ buffers
+    def set_micro_batch(self, micro_batch: int) -> None:
+        """Re-size the activation buffers for another micro-batch size (after a reconfiguration)."""
+        if micro_batch == self.mb:
+            return
+        self.mb = micro_batch
+        self.T = self.mb * self.S
+        for name in [k for k, v in vars(self).items() if isinstance(v, (torch.Tensor, list)) and k not in (
+                "layer_ids", "param_specs", "cos", "sin")]:
+            delattr(self, name)
+        torch.cuda.empty_cache()
+        self._alloc()
+
     def _alloc(self) -> None:
         cfg, T, dev = self.cfg, self.T, self.device
         H, F, V = cfg.hidden, cfg.ffn, cfg.vocab_size

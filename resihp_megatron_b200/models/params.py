@@ -49,11 +49,12 @@ class FlatParams:
     """bf16 compute weights + fp32 master / grad / exp_avg / exp_avg_sq over one flat index space."""
 
     def __init__(self, specs: list[ParamSpec], device, with_optimizer: bool = True, shard_rank: int = 0,
-                 shard_count: int = 1, buffer_factory=None):
+                 shard_count: int = 1, buffer_factory=None, opt_factory=None):
         """``shard_rank / shard_count`` > 1 keeps the optimizer state (master, moments) for one
         contiguous slice of the flat index space only (ZeRO-1); bf16 weights and gradients stay
-        full size.  ``buffer_factory(numel) -> (bf16, grad)`` supplies zero-filled flat buffers
-        from elsewhere (the symmetric peer heap of the fused data-parallel step)."""
+        full size.  ``buffer_factory(numel) -> (bf16, grad)`` and ``opt_factory(shard_numel) ->
+        (master, exp_avg, exp_avg_sq)`` supply zero-filled flat buffers from elsewhere (the
+        symmetric peer heap of the fused data-parallel step, where peers can read them)."""
         self.specs = {s.name: s for s in specs}
         self.order = [s.name for s in specs]
         self.offsets: dict[str, int] = {}
@@ -73,7 +74,9 @@ class FlatParams:
         else:
             self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device)
             self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        if with_optimizer:
+        if with_optimizer and opt_factory is not None:
+            self.master, self.exp_avg, self.exp_avg_sq = opt_factory(self.shard_numel)
+        elif with_optimizer:
             n = self.shard_numel
             self.master = torch.zeros(n, dtype=torch.float32, device=self.device)
             self.exp_avg = torch.zeros(n, dtype=torch.float32, device=self.device)

@@ -385,6 +385,20 @@ void dp_step_fused(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
                             num_sms(master.get_device()), cur_stream()), "dp_step_fused");
 }
 
+// Slice copies (src, dst, bytes) into this rank's memory; src may be peer memory.
+void symm_copy(const std::vector<int64_t>& triples, int64_t device) {
+  TORCH_CHECK(triples.size() % 3 == 0, "symm_copy: triples");
+  const int n = static_cast<int>(triples.size() / 3);
+  long long pieces = 0;
+  for (int i = 0; i < n; ++i) pieces += (triples[3 * i + 2] + (1 << 20) - 1) >> 20;
+  if (pieces == 0) return;
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  auto scratch = torch::empty({pieces * rb::symm_copy_piece_bytes()},
+                              torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+  RB_CALL(rb::symm_copy(reinterpret_cast<const long long*>(triples.data()), n, scratch.data_ptr(),
+                        static_cast<int>(pieces), num_sms(static_cast<int>(device)), cur_stream()), "symm_copy");
+}
+
 torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(device)); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -418,6 +432,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_signal_bytes", &symm_signal_bytes);
   m.def("symm_barrier", &symm_barrier);
   m.def("dp_step_fused", &dp_step_fused);
+  m.def("symm_copy", &symm_copy);
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("S"),
         py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0);

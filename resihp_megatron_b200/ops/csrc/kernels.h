@@ -79,6 +79,8 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
                   float* v, long long shard_lo, long long n, float lr, float b1, float b2, float eps, float wd,
                   int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
                   cudaStream_t s);
+int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
+int symm_copy_piece_bytes();
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
 int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
 }  // namespace rb

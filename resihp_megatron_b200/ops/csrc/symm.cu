@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "kernels.h"
 #include "sm100.cuh"
@@ -141,6 +142,30 @@ __global__ void __launch_bounds__(256) dp_step_kernel(const __grid_constant__ Dp
   }
 }
 
+// Slice migration: every (src, dst, bytes) piece is copied with 16-byte loads and stores; the
+// source may be a peer's memory (old generation's heap), the destination is this rank's.  Pieces
+// are pre-split on the host to at most kPieceBytes so CTAs share the work evenly.
+struct CopyPiece {
+  const uint4* src;
+  uint4* dst;
+  long long n16;  // number of 16-byte units
+};
+
+__global__ void __launch_bounds__(256) symm_copy_kernel(const CopyPiece* __restrict__ pieces, int n_pieces) {
+  for (int pi = blockIdx.x; pi < n_pieces; pi += gridDim.x) {
+    const CopyPiece c = pieces[pi];
+    for (long long i = threadIdx.x; i < c.n16; i += blockDim.x * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * blockDim.x < c.n16) v[u] = __ldcv(c.src + i + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * blockDim.x < c.n16) c.dst[i + u * blockDim.x] = v[u];
+    }
+  }
+}
+
 }  // namespace
 
 // ----------------------------------------------------------------------------------- host side
@@ -192,5 +217,38 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
   dp_step_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(a);
   return static_cast<int>(cudaGetLastError());
 }
+
+}  // namespace rb
+
+namespace rb {
+
+// pieces: host array of (src, dst, bytes) triples, each 16-byte aligned; `dev_scratch` holds at
+// least `max_pieces` CopyPiece records on the device.
+int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s) {
+  constexpr long long kPieceBytes = 1 << 20;
+  std::vector<CopyPiece> pieces;
+  for (int i = 0; i < n; ++i) {
+    const long long src = triples[3 * i], dst = triples[3 * i + 1], bytes = triples[3 * i + 2];
+    if ((src | dst | bytes) & 15) return -1;
+    for (long long off = 0; off < bytes; off += kPieceBytes) {
+      const long long b = bytes - off < kPieceBytes ? bytes - off : kPieceBytes;
+      pieces.push_back({reinterpret_cast<const uint4*>(src + off), reinterpret_cast<uint4*>(dst + off), b / 16});
+    }
+  }
+  if (pieces.empty()) return 0;
+  if (static_cast<int>(pieces.size()) > max_pieces) return -2;
+  cudaError_t e = cudaMemcpyAsync(dev_scratch, pieces.data(), pieces.size() * sizeof(CopyPiece),
+                                  cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  // the host vector must outlive the async copy: wait for it on the stream before returning
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int grid = static_cast<int>(pieces.size()) < num_sms * 4 ? static_cast<int>(pieces.size()) : num_sms * 4;
+  symm_copy_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const CopyPiece*>(dev_scratch),
+                                        static_cast<int>(pieces.size()));
+  return static_cast<int>(cudaGetLastError());
+}
+
+int symm_copy_piece_bytes() { return static_cast<int>(sizeof(CopyPiece)); }
 
 }  // namespace rb

@@ -31,10 +31,19 @@ class FusedDataParallel:
         self.heap: SymmetricHeap | None = None
 
     def buffer_factory(self, numel: int):
-        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad buffers."""
-        self.heap = SymmetricHeap({"grad": (numel, torch.float32), "weight": (numel, torch.bfloat16)}, self.rank,
-                                  self.world, self.exchange, self.device, self.abort)
+        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad buffers,
+        plus room for this rank's optimizer shard (``opt_factory``), so a later reconfiguration can
+        pull master weights and moments from this rank's memory peer to peer."""
+        shard = numel // self.world
+        self.heap = SymmetricHeap({"grad": (numel, torch.float32), "weight": (numel, torch.bfloat16),
+                                   "master": (shard, torch.float32), "exp_avg": (shard, torch.float32),
+                                   "exp_avg_sq": (shard, torch.float32)}, self.rank, self.world, self.exchange,
+                                  self.device, self.abort)
         return self.heap.tensor("weight"), self.heap.tensor("grad")
+
+    def opt_factory(self, shard_numel: int):
+        assert self.heap is not None and self.heap.segments["master"].numel == shard_numel
+        return self.heap.tensor("master"), self.heap.tensor("exp_avg"), self.heap.tensor("exp_avg_sq")
 
     def step(self, P, *, lr, betas, eps, weight_decay, grad_scale: float = 1.0, decoupled: bool = False) -> None:
         """One optimizer step of flat parameters ``P`` (whose buffers came from ``buffer_factory``)."""
@@ -55,3 +64,19 @@ class FusedDataParallel:
         if self.heap is not None:
             self.heap.close()
             self.heap = None
+
+
+def reshard_pull_plan(old_world: int, old_shard: int, old_ptrs: dict[str, list[int]], new_lo: int, new_hi: int,
+                      new_ptrs: dict[str, int], old_numel: int) -> list[int]:
+    """Flat (src, dst, bytes) triples that fill this rank's new optimizer shard ``[new_lo, new_hi)``
+    from the old owners' shards (old owner ``o`` held ``[o * old_shard, (o + 1) * old_shard)``).
+    Elements past the old flat size are padding and stay zero."""
+    triples: list[int] = []
+    for o in range(old_world):
+        a = max(new_lo, o * old_shard)
+        b = min(new_hi, (o + 1) * old_shard, old_numel)
+        if a >= b:
+            continue
+        for seg in ("master", "exp_avg", "exp_avg_sq"):
+            triples += [old_ptrs[seg][o] + (a - o * old_shard) * 4, new_ptrs[seg] + (a - new_lo) * 4, (b - a) * 4]
+    return triples

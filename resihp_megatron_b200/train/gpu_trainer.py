@@ -50,7 +50,7 @@ class GPUTrainer:
             raise ValueError(dp_impl)
         self.dp_impl = dp_impl if self.dp > 1 else "single"
         self.fused = None
-        factory = None
+        factory = opt_factory = None
         if self.dp_impl == "fused":
             from ..parallel.dp_fused import FusedDataParallel
             from ..parallel.symm import AbortWord, exchange_via_group
@@ -58,10 +58,12 @@ class GPUTrainer:
             self.abort_word = AbortWord()
             self.fused = FusedDataParallel(self.rank, self.dp, exchange_via_group(dp_group), self.device,
                                            abort=self.abort_word)
-            factory = self.fused.buffer_factory
+            factory, opt_factory = self.fused.buffer_factory, self.fused.opt_factory
         self.model = LlamaModel(cfg, self.device, micro_batch=micro_batch, seq_len=self.S, seed=seed,
-                                shard_rank=self.rank, shard_count=self.dp, buffer_factory=factory)
+                                shard_rank=self.rank, shard_count=self.dp, buffer_factory=factory,
+                                opt_factory=opt_factory)
         self.tokens_per_step = global_batch * self.S
+        self.batch_offset = self.rank * self.local_batch  # first sequence of this rank in the global batch
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
         self.labels_dev = torch.empty_like(self.ids_dev)
         P = self.model.params
@@ -116,6 +118,62 @@ class GPUTrainer:
         if self.fused is not None:
             self.fused.check()
         return value
+
+    # ------------------------------------------------------------------ live reconfiguration
+    def shrink(self, survivors: list[int], new_group) -> bool:
+        """Planned removal of data-parallel ranks with live state migration (e.g. evicting a
+        fail-slow GPU).  Every current rank calls it between steps; ``survivors`` are the kept
+        ranks (old numbering, ascending) and ``new_group`` their process group.  Survivors build
+        the next generation's symmetric heap, pull their new optimizer shard -- fp32 master
+        weights and both Adam moments -- straight from the old owners' memory over NVLink with
+        one copy kernel (the departing ranks included, so no state is lost), copy the bf16
+        weights locally and re-split the global batch by largest remainder.  Returns False on a
+        rank that leaves.  (Reference: the transfer engine's slice migration,
+        ``resihp/state/transfer_engine.py:24-59``, and the DP planner's batch-preserving
+        assignment, ``resihp/plan/dp_planner.py:11-22``.)"""
+        from ..models.params import FlatParams
+        from ..ops._build import ext
+        from ..parallel.dp_fused import FusedDataParallel, reshard_pull_plan
+        from ..parallel.symm import exchange_via_group
+        from ..plan.dp_migration import largest_remainder
+
+        if self.fused is None:
+            raise RuntimeError("live reshard needs the fused data-parallel path")
+        old_fdp, old_P = self.fused, self.model.params
+        old_fdp.heap.barrier(old_fdp.budget)  # every rank finished its last step
+        leaving = self.rank not in survivors
+        new_P = new_fdp = None
+        if not leaving:
+            new_rank, new_world = survivors.index(self.rank), len(survivors)
+            new_fdp = FusedDataParallel(new_rank, new_world, exchange_via_group(new_group), self.device,
+                                        abort=self.abort_word, barrier_budget_s=old_fdp.budget)
+            new_P = FlatParams(self.model.param_specs, self.device, shard_rank=new_rank, shard_count=new_world,
+                               buffer_factory=new_fdp.buffer_factory, opt_factory=new_fdp.opt_factory)
+            new_P.step = old_P.step
+            triples = reshard_pull_plan(
+                self.dp, old_P.shard_numel, {k: old_fdp.heap.peer_ptrs(k) for k in ("master", "exp_avg", "exp_avg_sq")},
+                new_P.shard_lo, new_P.shard_lo + new_P.shard_numel,
+                {k: new_fdp.heap.peer_ptrs(k)[new_rank] for k in ("master", "exp_avg", "exp_avg_sq")}, old_P.numel)
+            ext().symm_copy(triples, self.device.index if self.device.index is not None else 0)
+            n = min(old_P.numel, new_P.numel)
+            new_P.bf16[:n].copy_(old_P.bf16[:n])
+        old_fdp.heap.barrier(old_fdp.budget)  # every pull from this rank's memory has landed
+        old_fdp.check()
+        old_fdp.close()
+        if leaving:
+            self.fused = None
+            return False
+        self.model.params, self.fused = new_P, new_fdp
+        self.group, self.rank, self.dp = new_group, survivors.index(self.rank), len(survivors)
+        shares = largest_remainder(self.global_batch, [1.0] * self.dp)
+        self.local_batch = shares[self.rank]
+        self.batch_offset = sum(shares[:self.rank])
+        mb = self.micro_batch if self.local_batch % self.micro_batch == 0 else 1
+        self.micro_batch, self.n_micro = mb, self.local_batch // mb
+        self.model.set_micro_batch(mb)
+        self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
+        self.labels_dev = torch.empty_like(self.ids_dev)
+        return True
 
     def close(self) -> None:
         """Release the symmetric heap (before the process group is destroyed)."""
