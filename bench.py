@@ -26,6 +26,7 @@ Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import os
 import statistics
@@ -133,6 +134,7 @@ class ClockSampler:
 
 
 def main() -> None:
+    faulthandler.enable()
     args = _args()
     if args.impl == "reference":
         reference_unavailable(args)
@@ -225,7 +227,10 @@ def main() -> None:
 
     # ---- optional live reconfiguration: the last rank leaves, state migrates, N-1 GPUs continue
     recfg, alive, post_group = None, True, None
-    if args.reconfig and world > 1 and args.dp_impl == "fused":
+    if args.reconfig and world == 2:
+        recfg = {"skipped": "one survivor cannot hold the unsharded fp32 master + Adam state next to its old shard "
+                            "(needs N >= 3 for this model on 180 GB)"}
+    elif args.reconfig and world > 2 and args.dp_impl == "fused":
         survivors = list(range(world - 1))
         barrier()
         torch.cuda.synchronize()

@@ -99,16 +99,17 @@ class LlamaModel:
         self._alloc()
 
     # ------------------------------------------------------------------ buffers
-    def set_micro_batch(self, micro_batch: int) -> None:
-        """Re-size the activation buffers for another micro-batch size (after a reconfiguration)."""
-        if micro_batch == self.mb:
-            return
-        self.mb = micro_batch
-        self.T = self.mb * self.S
+    def release_buffers(self) -> None:
+        """Free the activation buffers (a reconfiguration needs the memory)."""
         for name in [k for k, v in vars(self).items() if isinstance(v, (torch.Tensor, list)) and k not in (
                 "layer_ids", "param_specs", "cos", "sin")]:
             delattr(self, name)
         torch.cuda.empty_cache()
+
+    def restore_buffers(self, micro_batch: int) -> None:
+        """Re-allocate the activation buffers, possibly for another micro-batch size."""
+        self.mb = micro_batch
+        self.T = self.mb * self.S
         self._alloc()
 
     def _alloc(self) -> None:

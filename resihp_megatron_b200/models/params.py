@@ -85,6 +85,15 @@ class FlatParams:
             self.master = self.exp_avg = self.exp_avg_sq = None
         self.step = 0
 
+    @staticmethod
+    def flat_numel(specs: list[ParamSpec], shard_count: int) -> int:
+        """Padded flat size for ``shard_count`` optimizer shards (what ``__init__`` computes)."""
+        off = 0
+        for s in specs:
+            off += (s.numel + ALIGN - 1) // ALIGN * ALIGN
+        quantum = ALIGN * shard_count
+        return (off + quantum - 1) // quantum * quantum
+
     @property
     def sharded(self) -> bool:
         return self.shard_count > 1

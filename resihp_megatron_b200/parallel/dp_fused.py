@@ -21,6 +21,13 @@ from .symm import AbortWord, SymmetricHeap
 
 
 class FusedDataParallel:
+    """Two symmetric heaps per generation: ``state`` (bf16 weights + this rank's fp32 master and
+    Adam moments; its signal pad carries the barriers) and ``grads`` (the full fp32 gradient).
+    Keeping them apart lets a reconfiguration drop the gradients first and hold only the old and
+    new optimizer state at the same time."""
+
+    STATE = ("master", "exp_avg", "exp_avg_sq")
+
     def __init__(self, rank: int, world: int, exchange, device, abort: AbortWord | None = None,
                  barrier_budget_s: float = 60.0):
         self.rank, self.world = rank, world
@@ -28,42 +35,62 @@ class FusedDataParallel:
         self.device = torch.device(device)
         self.abort = abort
         self.budget = barrier_budget_s
-        self.heap: SymmetricHeap | None = None
+        self.state: SymmetricHeap | None = None
+        self.grads: SymmetricHeap | None = None
+
+    @property
+    def heap(self) -> SymmetricHeap | None:
+        """The heap whose signal pad orders the ranks (the state heap)."""
+        return self.state
+
+    def alloc_state(self, numel: int) -> None:
+        shard = numel // self.world
+        self.state = SymmetricHeap({"weight": (numel, torch.bfloat16), "master": (shard, torch.float32),
+                                    "exp_avg": (shard, torch.float32), "exp_avg_sq": (shard, torch.float32)},
+                                   self.rank, self.world, self.exchange, self.device, self.abort)
+
+    def alloc_grads(self, numel: int) -> None:
+        self.grads = SymmetricHeap({"grad": (numel, torch.float32)}, self.rank, self.world, self.exchange,
+                                   self.device, self.abort)
 
     def buffer_factory(self, numel: int):
-        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad buffers,
-        plus room for this rank's optimizer shard (``opt_factory``), so a later reconfiguration can
-        pull master weights and moments from this rank's memory peer to peer."""
-        shard = numel // self.world
-        self.heap = SymmetricHeap({"grad": (numel, torch.float32), "weight": (numel, torch.bfloat16),
-                                   "master": (shard, torch.float32), "exp_avg": (shard, torch.float32),
-                                   "exp_avg_sq": (shard, torch.float32)}, self.rank, self.world, self.exchange,
-                                  self.device, self.abort)
-        return self.heap.tensor("weight"), self.heap.tensor("grad")
+        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad buffers
+        (allocated here unless already allocated)."""
+        if self.state is None:
+            self.alloc_state(numel)
+        if self.grads is None:
+            self.alloc_grads(numel)
+        return self.state.tensor("weight"), self.grads.tensor("grad")
 
     def opt_factory(self, shard_numel: int):
-        assert self.heap is not None and self.heap.segments["master"].numel == shard_numel
-        return self.heap.tensor("master"), self.heap.tensor("exp_avg"), self.heap.tensor("exp_avg_sq")
+        assert self.state is not None and self.state.segments["master"].numel == shard_numel
+        return tuple(self.state.tensor(k) for k in self.STATE)
 
     def step(self, P, *, lr, betas, eps, weight_decay, grad_scale: float = 1.0, decoupled: bool = False) -> None:
         """One optimizer step of flat parameters ``P`` (whose buffers came from ``buffer_factory``)."""
-        heap = self.heap
-        assert heap is not None, "buffers were not allocated by this FusedDataParallel"
-        heap.barrier(self.budget)
-        ext().dp_step_fused(heap.peer_ptrs("grad"), heap.peer_ptrs("weight"), P.master, P.exp_avg, P.exp_avg_sq,
-                            P.shard_lo, float(lr), float(betas[0]), float(betas[1]), float(eps), float(weight_decay),
-                            bool(decoupled), int(P.step), float(grad_scale), self.abort.dev if self.abort else 0)
-        heap.barrier(self.budget)
+        assert self.state is not None and self.grads is not None, "buffers were not allocated here"
+        self.state.barrier(self.budget)
+        ext().dp_step_fused(self.grads.peer_ptrs("grad"), self.state.peer_ptrs("weight"), P.master, P.exp_avg,
+                            P.exp_avg_sq, P.shard_lo, float(lr), float(betas[0]), float(betas[1]), float(eps),
+                            float(weight_decay), bool(decoupled), int(P.step), float(grad_scale),
+                            self.abort.dev if self.abort else 0)
+        self.state.barrier(self.budget)
         P.grad.zero_()
 
     def check(self) -> None:
-        if self.heap is not None:
-            self.heap.check()
+        if self.state is not None:
+            self.state.check()
+
+    def close_grads(self) -> None:
+        if self.grads is not None:
+            self.grads.close()
+            self.grads = None
 
     def close(self) -> None:
-        if self.heap is not None:
-            self.heap.close()
-            self.heap = None
+        self.close_grads()
+        if self.state is not None:
+            self.state.close()
+            self.state = None
 
 
 def reshard_pull_plan(old_world: int, old_shard: int, old_ptrs: dict[str, list[int]], new_lo: int, new_hi: int,

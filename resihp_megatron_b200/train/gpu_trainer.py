@@ -141,36 +141,49 @@ class GPUTrainer:
             raise RuntimeError("live reshard needs the fused data-parallel path")
         old_fdp, old_P = self.fused, self.model.params
         old_fdp.heap.barrier(old_fdp.budget)  # every rank finished its last step
+        torch.cuda.synchronize(self.device)
+        old_fdp.check()
+        # peak memory: drop the (zero) gradients and the activations before the new state exists
+        old_fdp.close_grads()
+        mb_old = self.micro_batch
+        self.model.release_buffers()
         leaving = self.rank not in survivors
         new_P = new_fdp = None
         if not leaving:
             new_rank, new_world = survivors.index(self.rank), len(survivors)
             new_fdp = FusedDataParallel(new_rank, new_world, exchange_via_group(new_group), self.device,
                                         abort=self.abort_word, barrier_budget_s=old_fdp.budget)
-            new_P = FlatParams(self.model.param_specs, self.device, shard_rank=new_rank, shard_count=new_world,
-                               buffer_factory=new_fdp.buffer_factory, opt_factory=new_fdp.opt_factory)
-            new_P.step = old_P.step
+            numel = FlatParams.flat_numel(self.model.param_specs, new_world)
+            new_fdp.alloc_state(numel)
+            new_shard = numel // new_world
             triples = reshard_pull_plan(
-                self.dp, old_P.shard_numel, {k: old_fdp.heap.peer_ptrs(k) for k in ("master", "exp_avg", "exp_avg_sq")},
-                new_P.shard_lo, new_P.shard_lo + new_P.shard_numel,
-                {k: new_fdp.heap.peer_ptrs(k)[new_rank] for k in ("master", "exp_avg", "exp_avg_sq")}, old_P.numel)
+                self.dp, old_P.shard_numel, {k: old_fdp.heap.peer_ptrs(k) for k in new_fdp.STATE},
+                new_rank * new_shard, (new_rank + 1) * new_shard,
+                {k: new_fdp.heap.peer_ptrs(k)[new_rank] for k in new_fdp.STATE}, old_P.numel)
             ext().symm_copy(triples, self.device.index if self.device.index is not None else 0)
-            n = min(old_P.numel, new_P.numel)
-            new_P.bf16[:n].copy_(old_P.bf16[:n])
+            n = min(old_P.numel, numel)
+            new_fdp.heap.tensor("weight")[:n].copy_(old_P.bf16[:n])
         old_fdp.heap.barrier(old_fdp.budget)  # every pull from this rank's memory has landed
+        torch.cuda.synchronize(self.device)
         old_fdp.check()
         old_fdp.close()
+        del old_P
+        self.model.params = None
         if leaving:
             self.fused = None
             return False
+        new_fdp.alloc_grads(numel)
+        new_P = FlatParams(self.model.param_specs, self.device, shard_rank=new_rank, shard_count=new_world,
+                           buffer_factory=new_fdp.buffer_factory, opt_factory=new_fdp.opt_factory)
+        new_P.step = self.step_count
         self.model.params, self.fused = new_P, new_fdp
-        self.group, self.rank, self.dp = new_group, survivors.index(self.rank), len(survivors)
+        self.group, self.rank, self.dp = new_group, new_rank, new_world
         shares = largest_remainder(self.global_batch, [1.0] * self.dp)
         self.local_batch = shares[self.rank]
         self.batch_offset = sum(shares[:self.rank])
-        mb = self.micro_batch if self.local_batch % self.micro_batch == 0 else 1
+        mb = mb_old if self.local_batch % mb_old == 0 else 1
         self.micro_batch, self.n_micro = mb, self.local_batch // mb
-        self.model.set_micro_batch(mb)
+        self.model.restore_buffers(mb)
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
         self.labels_dev = torch.empty_like(self.ids_dev)
         return True
