@@ -261,7 +261,8 @@ def main() -> None:
             recfg = {"kind": "planned eviction of the last rank; optimizer shards migrated peer to peer over NVLink",
                      "n_gpus_post": world - 1, "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
                      "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
-                     "post_micro_batch": trainer.micro_batch, "post_loss": float(loss2.item())}
+                     "post_micro_batch": trainer.micro_batch, "post_loss": float(loss2.item()),
+                     "phases_s_rank0": getattr(trainer, "last_reconfig", None)}
 
     if rank == 0:
         out = {

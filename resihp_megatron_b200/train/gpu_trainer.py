@@ -139,6 +139,14 @@ class GPUTrainer:
 
         if self.fused is None:
             raise RuntimeError("live reshard needs the fused data-parallel path")
+        import time
+
+        marks = [("start", time.perf_counter())]
+
+        def mark(name: str) -> None:
+            torch.cuda.synchronize(self.device)
+            marks.append((name, time.perf_counter()))
+
         old_fdp, old_P = self.fused, self.model.params
         old_fdp.heap.barrier(old_fdp.budget)  # every rank finished its last step
         torch.cuda.synchronize(self.device)
@@ -147,6 +155,7 @@ class GPUTrainer:
         old_fdp.close_grads()
         mb_old = self.micro_batch
         self.model.release_buffers()
+        mark("drain_and_free")
         leaving = self.rank not in survivors
         new_P = new_fdp = None
         if not leaving:
@@ -155,6 +164,7 @@ class GPUTrainer:
                                         abort=self.abort_word, barrier_budget_s=old_fdp.budget)
             numel = FlatParams.flat_numel(self.model.param_specs, new_world)
             new_fdp.alloc_state(numel)
+            mark("new_state_heap")
             new_shard = numel // new_world
             triples = reshard_pull_plan(
                 self.dp, old_P.shard_numel, {k: old_fdp.heap.peer_ptrs(k) for k in new_fdp.STATE},
@@ -163,6 +173,7 @@ class GPUTrainer:
             ext().symm_copy(triples, self.device.index if self.device.index is not None else 0)
             n = min(old_P.numel, numel)
             new_fdp.heap.tensor("weight")[:n].copy_(old_P.bf16[:n])
+            mark("migrate")
         old_fdp.heap.barrier(old_fdp.budget)  # every pull from this rank's memory has landed
         torch.cuda.synchronize(self.device)
         old_fdp.check()
@@ -172,7 +183,9 @@ class GPUTrainer:
         if leaving:
             self.fused = None
             return False
+        mark("release_old")
         new_fdp.alloc_grads(numel)
+        mark("new_grad_heap")
         new_P = FlatParams(self.model.param_specs, self.device, shard_rank=new_rank, shard_count=new_world,
                            buffer_factory=new_fdp.buffer_factory, opt_factory=new_fdp.opt_factory)
         new_P.step = self.step_count
@@ -186,6 +199,9 @@ class GPUTrainer:
         self.model.restore_buffers(mb)
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
         self.labels_dev = torch.empty_like(self.ids_dev)
+        mark("activations")
+        self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
+        self.last_reconfig["migrated_bytes"] = sum(triples[2::3])
         return True
 
     def close(self) -> None:
