@@ -27,7 +27,9 @@
 
 namespace rb {
 
-enum : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiBF16Res = 3 };
+enum : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiBF16Res = 3, kEpiScatterBF16 = 4 };
+
+constexpr int kMaxTP = 8;
 
 struct GemmArgs {
   int M, N, K;
@@ -37,6 +39,19 @@ struct GemmArgs {
   long long ldr;
   float alpha;
   int* err;
+  // kEpiScatterBF16 (GEMM -> reduce-scatter): output rows [q * rs_rows, (q + 1) * rs_rows) are
+  // stored as bf16 into rank q's receive buffer, slot `rs_slot` ([world][rs_rows][N] elements).
+  int rs_slot, rs_rows;
+  void* rs_dst[kMaxTP];
+  // all-gather -> GEMM: A's rows come in `ag_world` chunks of `ag_chunk_rows`; this rank owns
+  // chunk `ag_self` (already in place in `ag_dst`); the kernel's copy warps pull the other chunks
+  // from `ag_src[c]` into `ag_dst` and count finished slices in `ag_ready[c]`.
+  int ag_world, ag_self, ag_chunk_rows;
+  long long ag_chunk_bytes;
+  const void* ag_src[kMaxTP];
+  void* ag_dst;
+  int* ag_ready;
+  const int* abort_word;
 };
 
 template <int BN>
@@ -73,6 +88,26 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], int row, in
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
   const bool full = (col0 + 32 <= p.N);
+  if (EPI == kEpiScatterBF16) {
+    const int q = row / p.rs_rows;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.rs_dst[q]) +
+                         (static_cast<long long>(p.rs_slot) * p.rs_rows + (row - q * p.rs_rows)) * p.N + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 u;
+        u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        *reinterpret_cast<uint4*>(dst + 8 * j) = u;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+    }
+    return;
+  }
   if (EPI == kEpiBF16 || EPI == kEpiBF16Res) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
     if (EPI == kEpiBF16Res) {
@@ -304,6 +339,236 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive(tempty_bar(acc));
       acc ^= 1;
       if (acc == 0) aphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------- all-gather -> GEMM
+// Column-parallel layer with sequence-parallel input: Y = AllGather_rows(X) @ W^T in one
+// cooperative persistent launch.  Warps 0-5 are the GEMM above (K-major A and B, 128 x 256
+// tiles); warps 6-9 pull the other ranks' row chunks of X over NVLink into this rank's gather
+// buffer (16-byte peer loads, every CTA a slice of every chunk, in the rotated order
+// self+1, self+2, ...) and count finished slices per chunk.  Tiles are visited in the same
+// rotated chunk order starting with this rank's own chunk, so the MMAs of chunk c overlap the
+// transfer of chunk c+1; the TMA producer waits (bounded, acquire + proxy fence) until every CTA
+// finished its slice of a chunk before loading its rows.  All CTAs are co-resident (cooperative
+// launch, one per SM), so these waits between CTAs of the launch always make progress; the
+// launch never waits on another kernel.  The caller orders the launch after the peers wrote their
+// chunks (a bounded cross-GPU barrier) and before they overwrite them.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(320, 1)
+    gemm_ag_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  using C = GemmCfg<256>;
+  constexpr int BM = C::BM, BN = 256, BK = C::BK, STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 4]);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int mb_per_chunk = p.ag_chunk_rows / BM;
+  const int rot = p.ag_self * mb_per_chunk;  // visit this rank's own chunk first
+  auto coords = [&](int tile, int& mb, int& nb) {
+    tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
+    mb = (mb + rot) % num_m;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, issued_parity = 0;
+      unsigned ready_mask = 1u << p.ag_self;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mb, nb;
+        coords(tile, mb, nb);
+        const int chunk = mb / mb_per_chunk;
+        if (!(ready_mask & (1u << chunk))) {
+          const uint64_t t0 = globaltimer();
+          bool ok = true;
+          while (ld_acquire_gpu(p.ag_ready + chunk) < static_cast<int>(gridDim.x)) {
+            if (*abort_flag || (p.abort_word != nullptr && *reinterpret_cast<const volatile int*>(p.abort_word))) {
+              ok = false;
+              break;
+            }
+            if (globaltimer() - t0 > kWaitBudgetNs) {
+              *abort_flag = 1;
+              record_error(p.err, kErrPeerTimeout);
+              ok = false;
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // generic-proxy writes of the copy warps -> TMA reads
+          ready_mask |= 1u << chunk;
+        }
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fb, kb * BK, mb * BM);
+          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * BK, nb * BN);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, true, false, false);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, aphase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d_tmem, make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B),
+                     make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B), idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1;
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      coords(tile, mb, nb);
+      if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        store_chunk<EPI>(r, row, col0, p);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1;
+    }
+  } else {
+    // ------------------------------------------------------------ copy warps 6..9
+    const int t = threadIdx.x - 192;  // 0..127
+    const long long units = p.ag_chunk_bytes / 16;
+    const long long per = (units + gridDim.x - 1) / gridDim.x;
+    const long long lo = per * blockIdx.x;
+    const long long hi = lo + per < units ? lo + per : units;
+    for (int k = 1; k < p.ag_world; ++k) {
+      const int c = (p.ag_self + k) % p.ag_world;
+      const uint4* src = reinterpret_cast<const uint4*>(p.ag_src[c]);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.ag_dst) + c * p.ag_chunk_bytes);
+      for (long long i = lo + t; i < hi; i += 128 * 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * 128 < hi) v[u] = __ldcv(src + i + u * 128);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * 128 < hi) dst[i + u * 128] = v[u];
+      }
+      __threadfence();
+      named_bar_sync(1, 128);
+      if (t == 0) atomicAdd(p.ag_ready + c, 1);
     }
   }
 
@@ -629,6 +894,66 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, co
     case kEpiBF16Res: return dispatch_major<BN, kEpiBF16Res>(a_mn, b_mn, ta, tb, a, num_sms, s);
   }
   return -2;
+}
+
+// Y[M, N] = AllGather(X)[M, K] @ W[N, K]^T with the gather fused (see gemm_ag_sm100).
+// `x_full` is this rank's [M, K] gather buffer (its own chunk already in place), `x_src[c]` the
+// address of chunk c in rank c's buffer (peer memory), `ready` `world` zeroed ints.
+int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
+                 void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
+                 cudaStream_t stream) {
+  if (world < 1 || world > kMaxTP || chunk_rows % 128 || M != chunk_rows * world || K % 8 || N % 8) return -3;
+  if ((reinterpret_cast<uintptr_t>(x_full) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(Y)) & 15)
+    return -4;
+  CUtensorMap ta, tb;
+  if (int rc = make_tmap_bf16_2d(&ta, x_full, K, M, K, 64, 128)) return -100 - rc;
+  if (int rc = make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256)) return -100 - rc;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.D = Y; a.ldd = N; a.alpha = 1.f; a.err = err;
+  a.ag_world = world; a.ag_self = self; a.ag_chunk_rows = chunk_rows;
+  a.ag_chunk_bytes = static_cast<long long>(chunk_rows) * K * 2;
+  for (int c = 0; c < world; ++c) a.ag_src[c] = x_src[c];
+  a.ag_dst = const_cast<void*>(x_full);
+  a.ag_ready = ready;
+  a.abort_word = abort_word;
+  using C = GemmCfg<256>;
+  auto kern = gemm_ag_sm100<kEpiBF16>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms);
+  cfg.blockDim = dim3(320);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeCooperative;
+  attrs[0].val.cooperative = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+}
+
+// Partial products of a row-parallel layer, scattered for a reduce-scatter: rows
+// [q * (M / world), (q + 1) * (M / world)) of X[M, K] @ W[N, K]^T are stored (bf16) into
+// `recv[q]` (rank q's receive buffer, [world][M / world][N]) at slot `slot`.
+int gemm_rs_scatter_bf16(const void* X, const void* W, void* const* recv, int world, int slot, int M, int N, int K,
+                         int* err, int num_sms, cudaStream_t stream) {
+  if (world < 1 || world > kMaxTP || M % world || N % 8 || K % 8) return -3;
+  if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(W)) & 15) return -4;
+  for (int q = 0; q < world; ++q)
+    if (reinterpret_cast<uintptr_t>(recv[q]) & 15) return -4;
+  CUtensorMap ta, tb;
+  if (int rc = make_tmap_bf16_2d(&ta, X, K, M, K, 64, 128)) return -100 - rc;
+  if (int rc = make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256)) return -100 - rc;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.alpha = 1.f; a.err = err;
+  a.rs_slot = slot; a.rs_rows = M / world;
+  for (int q = 0; q < world; ++q) a.rs_dst[q] = recv[q];
+  return launch_gemm<256, false, false, kEpiScatterBF16>(ta, tb, a, num_sms, stream);
 }
 
 // A(m,k) = a_mn ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_mn ? B[k*ldb + n] : B[n*ldb + k].

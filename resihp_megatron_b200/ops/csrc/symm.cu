@@ -251,4 +251,38 @@ int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces
 
 int symm_copy_piece_bytes() { return static_cast<int>(sizeof(CopyPiece)); }
 
+namespace {
+// Reduce-scatter finish: out[i] = sum over slots s (rank order) of recv[s][i], fp32 accumulate.
+__global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, int world, long long n,
+                                 __nv_bfloat16* __restrict__ out) {
+  const long long i8 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i8 >= n) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < world; ++s) {
+    const uint4 u = __ldcv(reinterpret_cast<const uint4*>(recv + s * n + i8));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
+    }
+  }
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  *reinterpret_cast<uint4*>(out + i8) = o;
+}
+}  // namespace
+
+int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t s) {
+  if ((n & 7) || ((reinterpret_cast<uintptr_t>(recv) | reinterpret_cast<uintptr_t>(out)) & 15)) return -1;
+  const long long threads = n / 8;
+  rs_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(recv), world, n, reinterpret_cast<__nv_bfloat16*>(out));
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace rb
