@@ -9,11 +9,13 @@
 // TMEM (512 columns): S_A | S_B | O_A | O_B, 128 fp32 columns each.
 // Per key block j:  S_X = Q_X K_j^T (tcgen05, both operands K-major from shared memory);
 // softmax reads its S row from TMEM, applies the causal mask on the diagonal block, updates the
-// running max, and writes P (bf16) to shared memory in the 128B-swizzled K-major layout the MMA
-// reads; then O_X += P_X V_j (V as an MN-major operand, no transpose).  O stays in TMEM; it is
-// rescaled (TMEM load / multiply / store) only when a row's max grows by more than 2^8, so the
-// common case costs nothing -- l and O always share the same reference max, so the result is
-// exact.  Output rows are normalised by l in the epilogue and LSE is written for the backward.
+// running max, and writes P (bf16 pairs) back over the first half of S_X's TMEM columns; then
+// O_X += P_X V_j with P read from TMEM (TS MMA) and V as an MN-major operand.  K and V are
+// double-buffered.  The MMA issue order PV_A(j), S_A(j+1), PV_B(j), S_B(j+1) lets one tile's
+// softmax overlap the other tile's MMAs.  O stays in TMEM; it is rescaled (TMEM load / multiply
+// / store) only when a row's max grows by more than 2^8, so the common case costs nothing -- l
+// and O always share the same reference max, so the result is exact.  Output rows are
+// normalised by l in the epilogue and LSE is written for the backward.
 //
 // Every mbarrier wait is bounded (see sm100.cuh); a timeout unwinds all roles and the kernel
 // returns with an error word set.  No TMA multicast is used.
@@ -76,25 +78,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tmV, FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                    // Q_A, Q_B
-  uint8_t* sK = smem + 2 * kTileBytes;
-  uint8_t* sV = smem + 3 * kTileBytes;
-  uint8_t* sP = smem + 4 * kTileBytes;   // P_A, P_B
+  uint8_t* sQ = smem;                   // Q_A, Q_B
+  uint8_t* sK = smem + 2 * kTileBytes;  // 2 stages
+  uint8_t* sV = smem + 4 * kTileBytes;  // 2 stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  const uint32_t bar_final = smem_u32(&bars[11]);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t bar_q = smem_u32(&bars[0]);
-  const uint32_t bar_kf = smem_u32(&bars[1]), bar_ke = smem_u32(&bars[2]);
-  const uint32_t bar_vf = smem_u32(&bars[3]), bar_ve = smem_u32(&bars[4]);
-  auto bar_s = [&](int x) { return smem_u32(&bars[5 + x]); };
-  auto bar_p = [&](int x) { return smem_u32(&bars[7 + x]); };
-  auto bar_o = [&](int x) { return smem_u32(&bars[9 + x]); };
+  auto bar_kf = [&](int st) { return smem_u32(&bars[1 + st]); };
+  auto bar_ke = [&](int st) { return smem_u32(&bars[3 + st]); };
+  auto bar_vf = [&](int st) { return smem_u32(&bars[5 + st]); };
+  auto bar_ve = [&](int st) { return smem_u32(&bars[7 + st]); };
+  auto bar_s = [&](int x) { return smem_u32(&bars[9 + x]); };
+  auto bar_p = [&](int x) { return smem_u32(&bars[11 + x]); };
+  auto bar_o = [&](int x) { return smem_u32(&bars[13 + x]); };
+  const uint32_t bar_final = smem_u32(&bars[15]);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqb = gridDim.x;
-  const int qb = nqb - 1 - blockIdx.x;  // heaviest (latest) query blocks first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // heaviest (latest) query blocks first across the whole grid
+  const int per_qb = p.Hq * p.B;
+  const int nqb = p.S / (2 * kTile);
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x / per_qb);
+  const int h = (blockIdx.x % per_qb) % p.Hq;
+  const int b = (blockIdx.x % per_qb) / p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
   const int q0 = qb * 2 * kTile;
   const int jA = 2 * qb, jB = 2 * qb + 1;  // last key block of tile A / tile B
@@ -103,10 +109,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    mbar_init(bar_kf, 1);
-    mbar_init(bar_ke, 1);
-    mbar_init(bar_vf, 1);
-    mbar_init(bar_ve, 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(bar_kf(st), 1);
+      mbar_init(bar_ke(st), 1);
+      mbar_init(bar_vf(st), 1);
+      mbar_init(bar_ve(st), 1);
+    }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar_s(x), 1);
       mbar_init(bar_p(x), 4);
@@ -123,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;  // columns: S_A | S_B | O_A | O_B
 
   if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer
@@ -138,52 +146,86 @@ __global__ void __launch_bounds__(kThreads, 1)
                       row_base + q0 + x * kTile);
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nkv; ++j) {
-        if (!mbar_wait(bar_ke, (j & 1) ^ 1, abort_flag, p.err)) break;
-        mbar_arrive_expect_tx(bar_kf, kTileBytes);
+        const int st = j & 1;
+        if (!mbar_wait(bar_ke(st), ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(bar_kf(st), kTileBytes);
         for (int hf = 0; hf < 2; ++hf)
-          tma_load_2d(smem_u32(sK + hf * kHalf), &tmK, bar_kf, hk * kTile + hf * 64, row_base + j * kTile);
+          tma_load_2d(smem_u32(sK + st * kTileBytes + hf * kHalf), &tmK, bar_kf(st), hk * kTile + hf * 64,
+                      row_base + j * kTile);
         issued_k = j + 1;
-        if (!mbar_wait(bar_ve, (j & 1) ^ 1, abort_flag, p.err)) break;
-        mbar_arrive_expect_tx(bar_vf, kTileBytes);
+        if (!mbar_wait(bar_ve(st), ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(bar_vf(st), kTileBytes);
         for (int hf = 0; hf < 2; ++hf)
-          tma_load_2d(smem_u32(sV + hf * kHalf), &tmV, bar_vf, hk * kTile + hf * 64, row_base + j * kTile);
+          tma_load_2d(smem_u32(sV + st * kTileBytes + hf * kHalf), &tmV, bar_vf(st), hk * kTile + hf * 64,
+                      row_base + j * kTile);
         issued_v = j + 1;
       }
       // drain: the last loads issued must land before the CTA may exit
       mbar_wait(bar_q, 0, nullptr, p.err, 200000000ull);
-      if (issued_k) mbar_wait(bar_kf, (issued_k - 1) & 1, nullptr, p.err, 200000000ull);
-      if (issued_v) mbar_wait(bar_vf, (issued_v - 1) & 1, nullptr, p.err, 200000000ull);
+      for (int j = issued_k > 2 ? issued_k - 2 : 0; j < issued_k; ++j)
+        mbar_wait(bar_kf(j & 1), (j >> 1) & 1, nullptr, p.err, 200000000ull);
+      for (int j = issued_v > 2 ? issued_v - 2 : 0; j < issued_v; ++j)
+        mbar_wait(bar_vf(j & 1), (j >> 1) & 1, nullptr, p.err, 200000000ull);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
+    // Order per key block j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).  While the softmax warps of one
+    // tile work on their S, the tensor cores run the other tile's two MMAs.  tcgen05 MMAs of one
+    // thread execute in issue order, so S_X(j+1) overwrites P_X(j) (kept in S_X's columns) only
+    // after PV_X(j) consumed it.
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(128, 128, true, false, false);
       constexpr uint32_t idesc_o = make_idesc_f16(128, 128, true, false, true);
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.err);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const bool doA = j <= jA;
-        if (!(ok = mbar_wait(bar_kf, j & 1, abort_flag, p.err))) break;
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      auto issue_s = [&](int x, int j) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          umma_f16(tmem + x * 128, kmajor_desc(q_base + x * kTileBytes, s),
+                   kmajor_desc(k_base + (j & 1) * kTileBytes, s), idesc_s, s > 0 ? 1u : 0u);
+        umma_commit(bar_s(x));
+      };
+      auto issue_pv = [&](int x, int j) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          umma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + s * 8, mnmajor_desc(v_base + (j & 1) * kTileBytes, s),
+                      idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+        umma_commit(bar_o(x));
+      };
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.err) && mbar_wait(bar_kf(0), 0, abort_flag, p.err);
+      if (ok) {
         tc_fence_after();
-        for (int x = doA ? 0 : 1; x < 2; ++x) {
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            umma_f16(tmem + x * 128, kmajor_desc(q_base + x * kTileBytes, s), kmajor_desc(k_base, s), idesc_s,
-                     s > 0 ? 1u : 0u);
-          umma_commit(bar_s(x));
-        }
-        umma_commit(bar_ke);
-        if (!(ok = mbar_wait(bar_vf, j & 1, abort_flag, p.err))) break;
-        for (int x = doA ? 0 : 1; x < 2; ++x) {
-          if (!(ok = mbar_wait(bar_p(x), j & 1, abort_flag, p.err))) break;
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(bar_ke(0));
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        const int nx = j + 1;
+        if (!(ok = mbar_wait(bar_vf(st), (j >> 1) & 1, abort_flag, p.err))) break;
+        bool k_waited = false;
+        if (j <= jA) {
+          if (!(ok = mbar_wait(bar_p(0), j & 1, abort_flag, p.err))) break;
           tc_fence_after();
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            umma_f16(tmem + 256 + x * 128, kmajor_desc(p_base + x * kTileBytes, s), mnmajor_desc(v_base, s),
-                     idesc_o, (j > 0 || s > 0) ? 1u : 0u);
-          umma_commit(bar_o(x));
+          issue_pv(0, j);
+          if (nx <= jA) {
+            if (!(ok = mbar_wait(bar_kf(nx & 1), (nx >> 1) & 1, abort_flag, p.err))) break;
+            k_waited = true;
+            tc_fence_after();
+            issue_s(0, nx);
+          }
         }
-        umma_commit(bar_ve);
+        if (!(ok = mbar_wait(bar_p(1), j & 1, abort_flag, p.err))) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(bar_ve(st));
+        if (nx <= jB) {
+          if (!k_waited) {
+            if (!(ok = mbar_wait(bar_kf(nx & 1), (nx >> 1) & 1, abort_flag, p.err))) break;
+            tc_fence_after();
+          }
+          issue_s(1, nx);
+          umma_commit(bar_ke(nx & 1));
+        }
       }
       // every MMA this thread issued completes before TMEM is released
       umma_commit(bar_final);
@@ -197,8 +239,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + X * 128;
     const uint32_t o_addr = tmem + lane_off + 256 + X * 128;
-    uint8_t* prow = sP + X * kTileBytes + r * 128;
-    const int sw = r & 7;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j <= jmax; ++j) {
@@ -226,11 +266,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) mx = fmaxf(mx, v[c]);
       }
-      // PV of the previous block must be done: O is stable and P's buffer is free
-      if (j > 0) {
-        if (!(ok = warp_wait_bar(bar_o(X), (j - 1) & 1, abort_flag, p.err))) break;
-        tc_fence_after();
-      }
       const bool need = mx > m_ref + kRescaleThreshold;
       float alpha = 1.f;
       if (need) {
@@ -239,6 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = mx;
       }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O is rescaled in place once the previous PV finished writing it
+        if (!(ok = warp_wait_bar(bar_o(X), (j - 1) & 1, abort_flag, p.err))) break;
+        tc_fence_after();
         uint32_t t[32];
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -252,23 +290,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float sum = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        float e[8];
+      for (int c32 = 0; c32 < 2; ++c32) {
+        uint32_t packed[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = ex2(v[c8 * 8 + i] - m_ref);
-          sum += e[i];
+        for (int i = 0; i < 32; ++i) {
+          const float e0 = ex2(v[c32 * 64 + 2 * i] - m_ref);
+          const float e1 = ex2(v[c32 * 64 + 2 * i + 1] - m_ref);
+          sum += e0 + e1;
+          packed[i] = pack_bf16x2(e0, e1);
         }
-        uint4 u;
-        u.x = pack_bf16x2(e[0], e[1]);
-        u.y = pack_bf16x2(e[2], e[3]);
-        u.z = pack_bf16x2(e[4], e[5]);
-        u.w = pack_bf16x2(e[6], e[7]);
-        const int half = c8 >> 3, chunk = c8 & 7;
-        *reinterpret_cast<uint4*>(prow + half * kHalf + ((chunk ^ sw) << 4)) = u;
+        tmem_st_32x32b_x32(s_addr + c32 * 32, packed);
       }
+      tmem_st_wait();
       l += sum;
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p(X));
@@ -327,8 +361,7 @@ int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t stream)
   }
   FwdParams p{reinterpret_cast<__nv_bfloat16*>(a.o), a.o_stride, a.lse, a.B, a.S, a.Hq, a.Hkv,
               a.scale * 1.4426950408889634f, err};
-  dim3 grid(a.S / 256, a.Hq, a.B);
-  attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream>>>(tq, tk, tv, p);
+  attn_fwd_sm100_kernel<<<(a.S / 256) * a.Hq * a.B, kThreads, kSmem, stream>>>(tq, tk, tv, p);
   return static_cast<int>(cudaGetLastError());
 }
 
