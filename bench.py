@@ -227,10 +227,10 @@ def main() -> None:
 
     # ---- optional live reconfiguration: the last rank leaves, state migrates, N-1 GPUs continue
     recfg, alive, post_group = None, True, None
-    if args.reconfig and world == 2:
-        recfg = {"skipped": "one survivor cannot hold the unsharded fp32 master + Adam state next to its old shard "
-                            "(needs N >= 3 for this model on 180 GB)"}
-    elif args.reconfig and world > 2 and args.dp_impl == "fused":
+    if args.reconfig and 1 < world < 4:
+        recfg = {"skipped": "the spare optimizer bank of a live shrink (sized for N - 1 ranks) does not fit next "
+                            "to the 8B model's state on 180 GB below 4 GPUs"}
+    elif args.reconfig and world >= 4 and args.dp_impl == "fused":
         survivors = list(range(world - 1))
         barrier()
         torch.cuda.synchronize()

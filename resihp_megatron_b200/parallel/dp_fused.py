@@ -21,76 +21,79 @@ from .symm import AbortWord, SymmetricHeap
 
 
 class FusedDataParallel:
-    """Two symmetric heaps per generation: ``state`` (bf16 weights + this rank's fp32 master and
-    Adam moments; its signal pad carries the barriers) and ``grads`` (the full fp32 gradient).
-    Keeping them apart lets a reconfiguration drop the gradients first and hold only the old and
-    new optimizer state at the same time."""
+    """Symmetric heap per job: the full fp32 gradient, the full bf16 weights and the fp32 optimizer
+    shard (master weights + both Adam moments) of this rank.
+
+    With ``spare_bank`` (default when there are at least 4 ranks) the optimizer state has two
+    banks, each sized for a world one rank smaller, and the gradient / weight segments are sized
+    for any shard count up to the world size.  A live shrink then moves only the optimizer shards
+    -- peer to peer, from the old owners' current bank into each survivor's other bank -- and keeps
+    every buffer and every mapping: the weights and gradients do not depend on the shard layout.
+    Without a spare bank a shrink builds the next generation's heap instead."""
 
     STATE = ("master", "exp_avg", "exp_avg_sq")
 
     def __init__(self, rank: int, world: int, exchange, device, abort: AbortWord | None = None,
-                 barrier_budget_s: float = 60.0):
+                 barrier_budget_s: float = 60.0, numel_cap: int | None = None, spare_bank: bool | None = None):
         self.rank, self.world = rank, world
         self.exchange = exchange
         self.device = torch.device(device)
         self.abort = abort
         self.budget = barrier_budget_s
-        self.state: SymmetricHeap | None = None
-        self.grads: SymmetricHeap | None = None
+        self.numel_cap = numel_cap
+        self.banks = 2 if (spare_bank if spare_bank is not None else world >= 4) else 1
+        self.bank = 0
+        self.heap: SymmetricHeap | None = None
+        self.numel = 0
 
-    @property
-    def heap(self) -> SymmetricHeap | None:
-        """The heap whose signal pad orders the ranks (the state heap)."""
-        return self.state
+    def _shard_cap(self) -> int:
+        from ..models.params import ALIGN
 
-    def alloc_state(self, numel: int) -> None:
-        shard = numel // self.world
-        self.state = SymmetricHeap({"weight": (numel, torch.bfloat16), "master": (shard, torch.float32),
-                                    "exp_avg": (shard, torch.float32), "exp_avg_sq": (shard, torch.float32)},
-                                   self.rank, self.world, self.exchange, self.device, self.abort)
-
-    def alloc_grads(self, numel: int) -> None:
-        self.grads = SymmetricHeap({"grad": (numel, torch.float32)}, self.rank, self.world, self.exchange,
-                                   self.device, self.abort)
+        ranks = self.world - 1 if self.banks == 2 else self.world
+        cap = self.numel_cap or self.numel
+        return -(-cap // (ranks * ALIGN)) * ALIGN
 
     def buffer_factory(self, numel: int):
-        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad buffers
-        (allocated here unless already allocated)."""
-        if self.state is None:
-            self.alloc_state(numel)
-        if self.grads is None:
-            self.alloc_grads(numel)
-        return self.state.tensor("weight"), self.grads.tensor("grad")
+        """For ``FlatParams(buffer_factory=...)``: zero-filled heap-resident bf16 and grad views."""
+        if self.heap is None:
+            self.numel = numel
+            cap = max(self.numel_cap or numel, numel)
+            self.numel_cap = cap
+            segs: dict = {"grad": (cap, torch.float32), "weight": (cap, torch.bfloat16)}
+            for b in range(self.banks):
+                for k in self.STATE:
+                    segs[f"{k}{b}"] = (self._shard_cap(), torch.float32)
+            self.heap = SymmetricHeap(segs, self.rank, self.world, self.exchange, self.device, self.abort)
+        assert numel <= self.numel_cap
+        self.numel = numel
+        return self.heap.tensor("weight")[:numel], self.heap.tensor("grad")[:numel]
 
     def opt_factory(self, shard_numel: int):
-        assert self.state is not None and self.state.segments["master"].numel == shard_numel
-        return tuple(self.state.tensor(k) for k in self.STATE)
+        assert self.heap is not None and shard_numel <= self.heap.segments[f"master{self.bank}"].numel
+        return tuple(self.heap.tensor(f"{k}{self.bank}")[:shard_numel] for k in self.STATE)
+
+    def state_ptrs(self, bank: int) -> dict[str, list[int]]:
+        return {k: self.heap.peer_ptrs(f"{k}{bank}") for k in self.STATE}
 
     def step(self, P, *, lr, betas, eps, weight_decay, grad_scale: float = 1.0, decoupled: bool = False) -> None:
         """One optimizer step of flat parameters ``P`` (whose buffers came from ``buffer_factory``)."""
-        assert self.state is not None and self.grads is not None, "buffers were not allocated here"
-        self.state.barrier(self.budget)
-        ext().dp_step_fused(self.grads.peer_ptrs("grad"), self.state.peer_ptrs("weight"), P.master, P.exp_avg,
-                            P.exp_avg_sq, P.shard_lo, float(lr), float(betas[0]), float(betas[1]), float(eps),
-                            float(weight_decay), bool(decoupled), int(P.step), float(grad_scale),
-                            self.abort.dev if self.abort else 0)
-        self.state.barrier(self.budget)
+        heap = self.heap
+        assert heap is not None, "buffers were not allocated here"
+        heap.barrier(self.budget)
+        ext().dp_step_fused(heap.peer_ptrs("grad"), heap.peer_ptrs("weight"), P.master, P.exp_avg, P.exp_avg_sq,
+                            P.shard_lo, float(lr), float(betas[0]), float(betas[1]), float(eps), float(weight_decay),
+                            bool(decoupled), int(P.step), float(grad_scale), self.abort.dev if self.abort else 0)
+        heap.barrier(self.budget)
         P.grad.zero_()
 
     def check(self) -> None:
-        if self.state is not None:
-            self.state.check()
-
-    def close_grads(self) -> None:
-        if self.grads is not None:
-            self.grads.close()
-            self.grads = None
+        if self.heap is not None:
+            self.heap.check()
 
     def close(self) -> None:
-        self.close_grads()
-        if self.state is not None:
-            self.state.close()
-            self.state = None
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
 
 
 def reshard_pull_plan(old_world: int, old_shard: int, old_ptrs: dict[str, list[int]], new_lo: int, new_hi: int,

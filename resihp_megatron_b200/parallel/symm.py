@@ -143,6 +143,24 @@ class SymmetricHeap:
         ext().symm_barrier(self.pads, self.rank, self.world, self.epoch, self.abort.dev if self.abort else 0,
                            self.status, float(budget_s))
 
+    def restrict(self, keep: list[int]) -> None:
+        """Continue with the ranks ``keep`` (old numbering, ascending) as the next generation,
+        reusing every mapping: the dropped ranks' regions are unmapped, ranks are renumbered, the
+        barrier epoch restarts and this rank's signal pad is cleared.  The caller makes sure every
+        kept rank cleared its pad before the next barrier (a host barrier over the new group)."""
+        assert self.rank in keep, "a departing rank closes its heap instead"
+        bases = [self.bases[r] for r in keep]
+        for r, b in enumerate(self.bases):
+            if r not in keep and b in self._opened:
+                torch.cuda.synchronize(self.device)
+                ext().symm_close(b, self.dev_index)
+                self._opened.remove(b)
+        self.rank, self.world, self.bases = keep.index(self.rank), len(keep), bases
+        self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
+        ext().symm_tensor(self.local_base, self.pad_bytes, "uint8", self.dev_index).zero_()
+        self.status.zero_()
+        self.epoch = 0
+
     def check(self) -> None:
         st = self.status.tolist()
         if st[0] == 1:

@@ -30,7 +30,8 @@ from ..models.gpt import LlamaModel
 class GPUTrainer:
     def __init__(self, cfg: GPTConfig, *, global_batch: int, micro_batch: int = 1, seq_len: int | None = None,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, seed: int = 0,
-                 device=None, dp_group: dist.ProcessGroup | None = None, dp_impl: str = "fused"):
+                 device=None, dp_group: dist.ProcessGroup | None = None, dp_impl: str = "fused",
+                 spare_bank: bool | None = None):
         self.cfg = cfg
         self.S = seq_len or cfg.seq_len
         self.group = dp_group
@@ -55,9 +56,13 @@ class GPUTrainer:
             from ..parallel.dp_fused import FusedDataParallel
             from ..parallel.symm import AbortWord, exchange_via_group
 
+            from ..models.gpt import model_param_specs
+            from ..models.params import ALIGN, FlatParams
+
             self.abort_word = AbortWord()
+            cap = FlatParams.flat_numel(model_param_specs(cfg, list(range(cfg.layers)), True, True), 1) + ALIGN * self.dp
             self.fused = FusedDataParallel(self.rank, self.dp, exchange_via_group(dp_group), self.device,
-                                           abort=self.abort_word)
+                                           abort=self.abort_word, numel_cap=cap, spare_bank=spare_bank)
             factory, opt_factory = self.fused.buffer_factory, self.fused.opt_factory
         self.model = LlamaModel(cfg, self.device, micro_batch=micro_batch, seq_len=self.S, seed=seed,
                                 shard_rank=self.rank, shard_count=self.dp, buffer_factory=factory,
@@ -123,85 +128,80 @@ class GPUTrainer:
     def shrink(self, survivors: list[int], new_group) -> bool:
         """Planned removal of data-parallel ranks with live state migration (e.g. evicting a
         fail-slow GPU).  Every current rank calls it between steps; ``survivors`` are the kept
-        ranks (old numbering, ascending) and ``new_group`` their process group.  Survivors build
-        the next generation's symmetric heap, pull their new optimizer shard -- fp32 master
-        weights and both Adam moments -- straight from the old owners' memory over NVLink with
-        one copy kernel (the departing ranks included, so no state is lost), copy the bf16
-        weights locally and re-split the global batch by largest remainder.  Returns False on a
-        rank that leaves.  (Reference: the transfer engine's slice migration,
-        ``resihp/state/transfer_engine.py:24-59``, and the DP planner's batch-preserving
-        assignment, ``resihp/plan/dp_planner.py:11-22``.)"""
-        from ..models.params import FlatParams
-        from ..ops._build import ext
-        from ..parallel.dp_fused import FusedDataParallel, reshard_pull_plan
-        from ..parallel.symm import exchange_via_group
-        from ..plan.dp_migration import largest_remainder
-
-        if self.fused is None:
-            raise RuntimeError("live reshard needs the fused data-parallel path")
+        ranks (old numbering, ascending) and ``new_group`` their process group.  Each survivor pulls
+        its new optimizer shard -- fp32 master weights and both Adam moments -- from the old owners'
+        current bank into its spare bank over NVLink with one copy kernel (the departing ranks are
+        sources too, so no state is lost); weights and gradients stay where they are (their layout
+        does not depend on the sharding) and every peer mapping is reused; the global batch is
+        re-split by largest remainder.  Returns False on a rank that leaves.  (Reference: the
+        transfer engine's slice migration, ``resihp/state/transfer_engine.py:24-59``, and the DP
+        planner's batch-preserving assignment, ``resihp/plan/dp_planner.py:11-22``.)"""
         import time
 
+        from ..models.params import FlatParams
+        from ..ops._build import ext
+        from ..parallel.dp_fused import reshard_pull_plan
+        from ..plan.dp_migration import largest_remainder
+
+        fdp = self.fused
+        if fdp is None or fdp.banks != 2:
+            raise RuntimeError("live shrink needs the fused data-parallel path with a spare optimizer bank")
         marks = [("start", time.perf_counter())]
 
         def mark(name: str) -> None:
             torch.cuda.synchronize(self.device)
             marks.append((name, time.perf_counter()))
 
-        old_fdp, old_P = self.fused, self.model.params
-        old_fdp.heap.barrier(old_fdp.budget)  # every rank finished its last step
+        old_P, heap = self.model.params, fdp.heap
+        specs = self.model.param_specs
+        heap.barrier(fdp.budget)  # every rank finished its last step
         torch.cuda.synchronize(self.device)
-        old_fdp.check()
-        # peak memory: drop the (zero) gradients and the activations before the new state exists
-        old_fdp.close_grads()
-        mb_old = self.micro_batch
-        self.model.release_buffers()
-        mark("drain_and_free")
+        fdp.check()
+        mark("drain")
         leaving = self.rank not in survivors
-        new_P = new_fdp = None
+        nb = 1 - fdp.bank
+        moved = 0
         if not leaving:
             new_rank, new_world = survivors.index(self.rank), len(survivors)
-            new_fdp = FusedDataParallel(new_rank, new_world, exchange_via_group(new_group), self.device,
-                                        abort=self.abort_word, barrier_budget_s=old_fdp.budget)
-            numel = FlatParams.flat_numel(self.model.param_specs, new_world)
-            new_fdp.alloc_state(numel)
-            mark("new_state_heap")
+            numel = FlatParams.flat_numel(specs, new_world)
             new_shard = numel // new_world
-            triples = reshard_pull_plan(
-                self.dp, old_P.shard_numel, {k: old_fdp.heap.peer_ptrs(k) for k in new_fdp.STATE},
-                new_rank * new_shard, (new_rank + 1) * new_shard,
-                {k: new_fdp.heap.peer_ptrs(k)[new_rank] for k in new_fdp.STATE}, old_P.numel)
+            dst = {k: heap.peer_ptrs(f"{k}{nb}")[self.rank] for k in fdp.STATE}
+            for k in fdp.STATE:
+                heap.tensor(f"{k}{nb}")[:new_shard].zero_()  # padding past the old flat size
+            triples = reshard_pull_plan(self.dp, old_P.shard_numel, fdp.state_ptrs(fdp.bank), new_rank * new_shard,
+                                        (new_rank + 1) * new_shard, dst, old_P.numel)
             ext().symm_copy(triples, self.device.index if self.device.index is not None else 0)
-            n = min(old_P.numel, numel)
-            new_fdp.heap.tensor("weight")[:n].copy_(old_P.bf16[:n])
-            mark("migrate")
-        old_fdp.heap.barrier(old_fdp.budget)  # every pull from this rank's memory has landed
+            moved = sum(triples[2::3])
+        mark("migrate")
+        heap.barrier(fdp.budget)  # every pull from this rank's memory has landed
         torch.cuda.synchronize(self.device)
-        old_fdp.check()
-        old_fdp.close()
-        del old_P
-        self.model.params = None
+        fdp.check()
         if leaving:
+            fdp.close()
             self.fused = None
             return False
-        mark("release_old")
-        new_fdp.alloc_grads(numel)
-        mark("new_grad_heap")
-        new_P = FlatParams(self.model.param_specs, self.device, shard_rank=new_rank, shard_count=new_world,
-                           buffer_factory=new_fdp.buffer_factory, opt_factory=new_fdp.opt_factory)
+        heap.restrict(survivors)
+        dist.barrier(group=new_group)  # every survivor cleared its signal pad
+        mark("regroup")
+        fdp.rank, fdp.world, fdp.bank = new_rank, new_world, nb
+        new_P = FlatParams(specs, self.device, shard_rank=new_rank, shard_count=new_world,
+                           buffer_factory=fdp.buffer_factory, opt_factory=fdp.opt_factory)
         new_P.step = self.step_count
-        self.model.params, self.fused = new_P, new_fdp
+        self.model.params = new_P
         self.group, self.rank, self.dp = new_group, new_rank, new_world
         shares = largest_remainder(self.global_batch, [1.0] * self.dp)
         self.local_batch = shares[self.rank]
         self.batch_offset = sum(shares[:self.rank])
-        mb = mb_old if self.local_batch % mb_old == 0 else 1
+        mb = self.micro_batch if self.local_batch % self.micro_batch == 0 else 1
+        if mb != self.micro_batch:
+            self.model.release_buffers()
+            self.model.restore_buffers(mb)
         self.micro_batch, self.n_micro = mb, self.local_batch // mb
-        self.model.restore_buffers(mb)
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
         self.labels_dev = torch.empty_like(self.ids_dev)
-        mark("activations")
+        mark("commit")
         self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
-        self.last_reconfig["migrated_bytes"] = sum(triples[2::3])
+        self.last_reconfig["migrated_bytes"] = moved
         return True
 
     def close(self) -> None:

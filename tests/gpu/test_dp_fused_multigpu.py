@@ -92,7 +92,8 @@ def _shrink_worker(rank, world, port, q):
 
     results = {}
     for mode in ("steady", "shrink"):
-        tr = GPUTrainer(TINY, global_batch=4, micro_batch=2, seq_len=256, lr=1e-3, dp_group=dist.group.WORLD)
+        tr = GPUTrainer(TINY, global_batch=4, micro_batch=2, seq_len=256, lr=1e-3, dp_group=dist.group.WORLD,
+                        spare_bank=True)
         losses = [tr.train_step(*local(tr, b)) for b in batches[:2]]
         group = dist.new_group([0])
         alive = True
