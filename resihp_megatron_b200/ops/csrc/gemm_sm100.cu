@@ -64,7 +64,8 @@ struct GemmCfg {
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int STAGING_BYTES = 4 * 4096;  // scatter epilogue: 32 rows x 64 bf16 per warp
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 192;
   static constexpr int GROUP_M = 16;
 };
@@ -179,7 +180,8 @@ __global__ void __launch_bounds__(192, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint8_t* staging = sB + STAGES * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -325,14 +327,56 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
+      if constexpr (EPI == kEpiScatterBF16) {
+        // Stores to another GPU's memory: stage 32 rows x 64 columns per warp in shared memory so
+        // that each warp instruction writes four whole 128-byte row segments (8 KB per flush),
+        // instead of 32 scattered 16-byte pieces.
+        uint8_t* st = staging + (warp - 2) * 4096;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nb * BN + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        store_chunk<EPI>(r, row, col0, p);
+        for (int c = 0; c < BN / 32; c += 2) {
+          uint32_t r0[32], r1[32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32;
+          tmem_ld_32x32b_x32(taddr, r0);
+          tmem_ld_32x32b_x32(taddr + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // 16-byte chunk j of this lane's 128-byte row, XOR-swizzled
+            const uint32_t* src = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(src[0]) * p.alpha, __uint_as_float(src[1]) * p.alpha);
+            u.y = pack_bf16x2(__uint_as_float(src[2]) * p.alpha, __uint_as_float(src[3]) * p.alpha);
+            u.z = pack_bf16x2(__uint_as_float(src[4]) * p.alpha, __uint_as_float(src[5]) * p.alpha);
+            u.w = pack_bf16x2(__uint_as_float(src[6]) * p.alpha, __uint_as_float(src[7]) * p.alpha);
+            *reinterpret_cast<uint4*>(st + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = i * 4 + (lane >> 3);  // row within the warp's 32
+            const int seg = lane & 7;
+            const int grow = mb * BM + q * 32 + rr;
+            const int gcol = nb * BN + c * 32 + seg * 8;
+            if (grow < p.M && gcol < p.N) {
+              const uint4 u = *reinterpret_cast<const uint4*>(st + rr * 128 + ((seg ^ (rr & 7)) << 4));
+              const int owner = grow / p.rs_rows;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.rs_dst[owner]) +
+                                   (static_cast<long long>(p.rs_slot) * p.rs_rows + (grow - owner * p.rs_rows)) * p.N +
+                                   gcol;
+              *reinterpret_cast<uint4*>(dst) = u;
+            }
+          }
+          __syncwarp();
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (!row_ok || col0 >= p.N) continue;
+          store_chunk<EPI>(r, row, col0, p);
+        }
       }
       tc_fence_before();
       __syncwarp();
