@@ -435,6 +435,75 @@ void tp_rs_reduce(const torch::Tensor& recv, int64_t world, torch::Tensor& out) 
           "tp_rs_reduce");
 }
 
+// ------------------------------------------------------------------------- expert parallelism
+static std::vector<void*> as_ptrs(const std::vector<int64_t>& v) {
+  std::vector<void*> out(v.size());
+  for (size_t i = 0; i < v.size(); ++i) out[i] = reinterpret_cast<void*>(v[i]);
+  return out;
+}
+
+void moe_route(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& bias, int64_t k,
+               torch::Tensor& logits, torch::Tensor& topi, torch::Tensor& gates) {
+  CHECK_BF16(x); CHECK_BF16(w);
+  const c10::cuda::CUDAGuard g(x.device());
+  RB_CALL(rb::moe_route(x.data_ptr(), w.data_ptr(), bias.has_value() ? bias->data_ptr<float>() : nullptr,
+                        x.size(0), x.size(1), w.size(0), k, logits.data_ptr<float>(), topi.data_ptr<int>(),
+                        gates.data_ptr<float>(), cur_stream()), "moe_route");
+}
+
+void moe_positions(const torch::Tensor& topi, int64_t E, torch::Tensor& pos, torch::Tensor& counts) {
+  const c10::cuda::CUDAGuard g(topi.device());
+  RB_CALL(rb::moe_positions(topi.data_ptr<int>(), topi.numel(), E, pos.data_ptr<int>(), counts.data_ptr<int>(),
+                            cur_stream()), "moe_positions");
+}
+
+void moe_dispatch(const torch::Tensor& x, const torch::Tensor& topi, const torch::Tensor& pos, int64_t k,
+                  int64_t me, const torch::Tensor& holder, const torch::Tensor& rowbase,
+                  const std::vector<int64_t>& recv, torch::Tensor& route_row) {
+  CHECK_BF16(x);
+  const c10::cuda::CUDAGuard g(x.device());
+  auto r = as_ptrs(recv);
+  RB_CALL(rb::moe_dispatch(x.data_ptr(), topi.data_ptr<int>(), pos.data_ptr<int>(), x.size(0), k, x.size(1),
+                           static_cast<int>(r.size()), me, holder.numel(), holder.data_ptr<int>(),
+                           rowbase.data_ptr<int64_t>() ? reinterpret_cast<const long long*>(rowbase.data_ptr<int64_t>()) : nullptr,
+                           r.data(), reinterpret_cast<long long*>(route_row.data_ptr<int64_t>()), cur_stream()),
+          "moe_dispatch");
+}
+
+void moe_combine(const torch::Tensor& residual, const torch::Tensor& gates, const torch::Tensor& route_row,
+                 int64_t k, const std::vector<int64_t>& ybuf, torch::Tensor& out, torch::Tensor& ycache) {
+  CHECK_BF16(residual);
+  const c10::cuda::CUDAGuard g(residual.device());
+  auto y = as_ptrs(ybuf);
+  RB_CALL(rb::moe_combine(residual.data_ptr(), gates.data_ptr<float>(),
+                          reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), residual.size(0), k,
+                          residual.size(1), static_cast<int>(y.size()), y.data(), out.data_ptr(), ycache.data_ptr(),
+                          cur_stream()), "moe_combine");
+}
+
+void moe_grad_push(const torch::Tensor& dout, const torch::Tensor& gates, const torch::Tensor& ycache,
+                   const torch::Tensor& route_row, int64_t k, const std::vector<int64_t>& dyrecv, torch::Tensor& dgate) {
+  CHECK_BF16(dout);
+  const c10::cuda::CUDAGuard g(dout.device());
+  auto d = as_ptrs(dyrecv);
+  RB_CALL(rb::moe_grad_push(dout.data_ptr(), gates.data_ptr<float>(), ycache.data_ptr(),
+                            reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), dout.size(0), k,
+                            dout.size(1), static_cast<int>(d.size()), d.data(), dgate.data_ptr<float>(), cur_stream()),
+          "moe_grad_push");
+}
+
+void moe_grad_pull(const torch::Tensor& dout, const torch::Tensor& gates, const torch::Tensor& dgate,
+                   const torch::Tensor& topi, const torch::Tensor& route_row, int64_t k, int64_t E,
+                   const std::vector<int64_t>& dxbuf, torch::Tensor& dx, torch::Tensor& dlogits) {
+  CHECK_BF16(dout);
+  const c10::cuda::CUDAGuard g(dout.device());
+  auto b = as_ptrs(dxbuf);
+  RB_CALL(rb::moe_grad_pull(dout.data_ptr(), gates.data_ptr<float>(), dgate.data_ptr<float>(), topi.data_ptr<int>(),
+                            reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), dout.size(0), k,
+                            dout.size(1), E, static_cast<int>(b.size()), b.data(), dx.data_ptr(),
+                            dlogits.data_ptr<float>(), cur_stream()), "moe_grad_pull");
+}
+
 torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(device)); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -470,6 +539,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_step_fused", &dp_step_fused);
   m.def("symm_copy", &symm_copy);
   m.def("tp_ag_gemm", &tp_ag_gemm);
+  m.def("moe_route", &moe_route);
+  m.def("moe_positions", &moe_positions);
+  m.def("moe_dispatch", &moe_dispatch);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_grad_push", &moe_grad_push);
+  m.def("moe_grad_pull", &moe_grad_pull);
   m.def("tp_rs_gemm", &tp_rs_gemm);
   m.def("tp_rs_reduce", &tp_rs_reduce);
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),

@@ -82,6 +82,19 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
 int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
 int symm_copy_piece_bytes();
 int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t s);
+// Expert parallelism (moe.cu).
+int moe_route(const void* x, const void* w, const float* bias, int T, int H, int E, int k, float* logits, int* topi,
+              float* gates, cudaStream_t s);
+int moe_positions(const int* topi, int n, int E, int* pos, int* counts, cudaStream_t s);
+int moe_dispatch(const void* x, const int* topi, const int* pos, int T, int k, int H, int world, int me, int E,
+                 const int* holder, const long long* rowbase, void* const* recv, long long* route_row, cudaStream_t s);
+int moe_combine(const void* residual, const float* gates, const long long* route_row, int T, int k, int H, int world,
+                void* const* ybuf, void* out, void* ycache, cudaStream_t s);
+int moe_grad_push(const void* dout, const float* gates, const void* ycache, const long long* route_row, int T, int k,
+                  int H, int world, void* const* dyrecv, float* dgate, cudaStream_t s);
+int moe_grad_pull(const void* dout, const float* gates, const float* dgate, const int* topi,
+                  const long long* route_row, int T, int k, int H, int E, int world, void* const* dxbuf, void* dx,
+                  float* dlogits, cudaStream_t s);
 // Tensor-parallel fused GEMMs (gemm_sm100.cu).
 int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
                  void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,

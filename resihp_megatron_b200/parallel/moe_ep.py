@@ -1,0 +1,204 @@
+"""Expert-parallel MoE layer on GPUs: routing, dispatch and combine over NVLink peer memory.
+
+One layer ``y = x + sum_k g_k(x) E_{e_k}(x)`` (top-k routing, softmax over the selected logits, a
+non-trainable bias that only selects, SwiGLU experts ``w2 (silu(x w1^T) * (x w3^T))`` with
+``w13 = [w1; w3]``).  Expert ``e`` lives on rank ``holder[e]``.  Per step:
+
+1. ``moe_route`` (router kernel) and ``moe_positions`` (fixed-order ranks of each (token, slot)
+   within its expert) on every rank; the per-expert counts go to the symmetric heap.
+2. Bounded barrier, every rank pulls all count vectors (one slice-copy launch), and the host derives
+   each expert's receive rows: expert-major, then source rank, then position -- a layout that does
+   not depend on timing, so expert weight gradients are fixed-order sums.
+3. ``moe_dispatch``: every (token, slot) row is stored straight into its holder's receive buffer.
+4. Barrier; each holder runs its local experts' GEMMs on contiguous row ranges (tcgen05 kernels).
+5. Barrier; ``moe_combine`` pulls the expert outputs back and adds them with the gates.
+Backward mirrors it (``moe_grad_push`` / expert backward / ``moe_grad_pull``).
+
+Replaces the reference's EP runtime transport (``resihp/runtime/moe.py:149-265``: counts
+all-to-all, autograd ``all_to_all_single``, ``index_add``).  Placement changes (expert
+re-placement after a fail-slow) only change ``holder``; expert state moves with ``symm_copy``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..ops._build import ext
+from .symm import AbortWord, SymmetricHeap
+
+
+class ExpertParallelMoE:
+    def __init__(self, rank: int, world: int, exchange, device, *, hidden: int, num_experts: int, top_k: int,
+                 max_tokens: int, holder: list[int], abort: AbortWord | None = None, budget_s: float = 30.0,
+                 _heap: SymmetricHeap | None = None):
+        self.rank, self.world = rank, world
+        self.H, self.E, self.k = hidden, num_experts, top_k
+        self.holder = list(holder)
+        self.local = [e for e in range(num_experts) if holder[e] == rank]
+        self.max_rows = max_tokens * world * max(1, len(self.local))
+        self.device = torch.device(device)
+        self.abort, self.budget = abort, budget_s
+        segs = {"counts": (world * 16, torch.int32),
+                "recv": (self.max_rows * hidden, torch.bfloat16), "y": (self.max_rows * hidden, torch.bfloat16),
+                "dyrecv": (self.max_rows * hidden, torch.bfloat16), "dxrecv": (self.max_rows * hidden, torch.bfloat16)}
+        self.heap = _heap or SymmetricHeap(segs, rank, world, exchange, device, abort)
+        self.emulated = _heap is not None
+        self.holder_t = torch.tensor(self.holder, dtype=torch.int32, device=self.device)
+        self.saved: dict = {}
+
+    @classmethod
+    def emulated_group(cls, world: int, device, **kw) -> list["ExpertParallelMoE"]:
+        """``world`` ranks in one process on one GPU (tests); call each phase on every rank in turn."""
+        E = kw["num_experts"]
+        holder = kw["holder"]
+        local = max(sum(1 for e in range(E) if holder[e] == r) for r in range(world))
+        rows = kw["max_tokens"] * world * max(1, local)
+        H = kw["hidden"]
+        segs = {"counts": (world * 16, torch.int32), "recv": (rows * H, torch.bfloat16), "y": (rows * H, torch.bfloat16),
+                "dyrecv": (rows * H, torch.bfloat16), "dxrecv": (rows * H, torch.bfloat16)}
+        heaps = SymmetricHeap.emulated(segs, world, device)
+        return [cls(r, world, None, device, _heap=heaps[r], **kw) for r in range(world)]
+
+    def _barrier(self) -> None:
+        if not self.emulated:
+            self.heap.barrier(self.budget)
+
+    def rows(self, name: str, n: int) -> torch.Tensor:
+        return self.heap.tensor(name)[: n * self.H].view(n, self.H)
+
+    # ------------------------------------------------------------------ phase 1: route
+    def route(self, x: torch.Tensor, router_w: torch.Tensor, bias: torch.Tensor | None = None) -> None:
+        T = x.shape[0]
+        logits = torch.empty(T, self.E, dtype=torch.float32, device=x.device)
+        topi = torch.empty(T, self.k, dtype=torch.int32, device=x.device)
+        gates = torch.empty(T, self.k, dtype=torch.float32, device=x.device)
+        ext().moe_route(x, router_w, bias, self.k, logits, topi, gates)
+        pos = torch.empty_like(topi)
+        counts = self.heap.tensor("counts")[self.rank * 16:(self.rank + 1) * 16]
+        counts.zero_()
+        ext().moe_positions(topi, self.E, pos, counts)
+        ops.count(2)
+        self.saved = {"x": x, "logits": logits, "topi": topi, "gates": gates, "pos": pos, "T": T}
+
+    # ------------------------------------------------------------------ phase 2: counts
+    def exchange_counts(self) -> None:
+        """Pull every rank's count vector into this rank's table; derive receive rows."""
+        self._barrier()
+        base = self.heap.peer_ptrs("counts")
+        me = self.rank
+        triples = []
+        for r in range(self.world):
+            if r != me:
+                triples += [base[r] + r * 64, base[me] + r * 64, 64]
+        if triples:
+            ext().symm_copy(triples, self.device.index if self.device.index is not None else 0)
+        table = self.heap.tensor("counts").view(self.world, 16)[:, : self.E].to("cpu", torch.int64)
+        self._layout(table)
+
+    def set_counts_table(self, table: torch.Tensor) -> None:
+        """Emulated groups: the full [world, E] count table (every rank's counts)."""
+        self._layout(table.to("cpu", torch.int64))
+
+    def _layout(self, table: torch.Tensor) -> None:
+        E, me = self.E, self.rank
+        totals = table.sum(0).tolist()
+        # receive rows at each holder: its local experts in order, each [source 0, source 1, ...]
+        start = [0] * E
+        for h in range(self.world):
+            off = 0
+            for e in range(E):
+                if self.holder[e] == h:
+                    start[e] = off
+                    off += totals[e]
+        rowbase = [start[e] + int(table[:me, e].sum()) for e in range(E)]
+        self.saved["rowbase"] = torch.tensor(rowbase, dtype=torch.int64, device=self.device)
+        self.saved["local_ranges"] = [(start[e], totals[e]) for e in self.local]
+        self.saved["recv_rows"] = sum(totals[e] for e in self.local)
+
+    # ------------------------------------------------------------------ phase 3: dispatch
+    def dispatch(self) -> None:
+        s = self.saved
+        route_row = torch.empty(s["T"] * self.k, dtype=torch.int64, device=self.device)
+        ext().moe_dispatch(s["x"], s["topi"], s["pos"], self.k, self.rank, self.holder_t, s["rowbase"],
+                           self.heap.peer_ptrs("recv"), route_row)
+        ops.count(1)
+        s["route_row"] = route_row
+        self._barrier()
+
+    # ------------------------------------------------------------------ phase 4: experts
+    def experts_forward(self, weights: dict[int, tuple[torch.Tensor, torch.Tensor]]) -> None:
+        """``weights[e] = (w13 [2F, H], w2 [H, F])`` for this rank's experts."""
+        s = self.saved
+        s["expert_cache"] = {}
+        for e, (lo, n) in zip(self.local, s["local_ranges"]):
+            if n == 0:
+                continue
+            xin = self.rows("recv", lo + n)[lo:]
+            w13, w2 = weights[e]
+            gu = ops.gemm(xin, w13)
+            a = ops.swiglu_fwd(gu)
+            ops.gemm(a, w2, out=self.rows("y", lo + n)[lo:])
+            s["expert_cache"][e] = (gu, a)
+        self._barrier()
+
+    # ------------------------------------------------------------------ phase 5: combine
+    def combine(self, residual: torch.Tensor) -> torch.Tensor:
+        s = self.saved
+        out = torch.empty_like(residual)
+        ycache = torch.empty(s["T"] * self.k, self.H, dtype=torch.bfloat16, device=self.device)
+        ext().moe_combine(residual, s["gates"], s["route_row"], self.k, self.heap.peer_ptrs("y"), out, ycache)
+        ops.count(1)
+        s["ycache"] = ycache
+        return out
+
+    def finish_forward(self) -> None:
+        self._barrier()  # holders may reuse their buffers
+
+    # ------------------------------------------------------------------ backward
+    def grad_push(self, dout: torch.Tensor) -> None:
+        s = self.saved
+        dgate = torch.empty(s["T"] * self.k, dtype=torch.float32, device=self.device)
+        ext().moe_grad_push(dout, s["gates"], s["ycache"], s["route_row"], self.k, self.heap.peer_ptrs("dyrecv"),
+                            dgate)
+        ops.count(1)
+        s["dgate"], s["dout"] = dgate, dout
+        self._barrier()
+
+    def experts_backward(self, weights, grads) -> None:
+        """``grads[e] = (dw13 fp32, dw2 fp32)`` accumulated (fixed row order)."""
+        s = self.saved
+        for e, (lo, n) in zip(self.local, s["local_ranges"]):
+            if n == 0:
+                continue
+            w13, w2 = weights[e]
+            gu, a = s["expert_cache"][e]
+            dy = self.rows("dyrecv", lo + n)[lo:]
+            xin = self.rows("recv", lo + n)[lo:]
+            da = ops.gemm(dy, w2, b_t=True)
+            ops.gemm(dy, a, a_t=True, b_t=True, out=grads[e][1], accumulate=True)
+            dgu = ops.swiglu_bwd(gu, da)
+            ops.gemm(dgu, xin, a_t=True, b_t=True, out=grads[e][0], accumulate=True)
+            ops.gemm(dgu, w13, b_t=True, out=self.rows("dxrecv", lo + n)[lo:])
+        self._barrier()
+
+    def grad_pull(self, router_w: torch.Tensor, router_grad: torch.Tensor) -> torch.Tensor:
+        """Input gradient of the layer (residual + expert paths + router path); accumulates the
+        router weight gradient (fp32) into ``router_grad``."""
+        s = self.saved
+        T = s["T"]
+        dx = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
+        dlogits = torch.empty(T, self.E, dtype=torch.float32, device=self.device)
+        ext().moe_grad_pull(s["dout"], s["gates"], s["dgate"], s["topi"], s["route_row"], self.k, self.E,
+                            self.heap.peer_ptrs("dxrecv"), dx, dlogits)
+        ops.count(1)
+        dl = dlogits.bfloat16()
+        ops.gemm(dl, s["x"], a_t=True, b_t=True, out=router_grad, accumulate=True)  # dW_r += dl^T x
+        dx_router = ops.gemm(dl, router_w, b_t=True)  # [T, E] @ [E, H]
+        dx.add_(dx_router)
+        self._barrier()
+        return dx
+
+    def close(self) -> None:
+        if not self.emulated or self.rank == 0:
+            self.heap.close()
