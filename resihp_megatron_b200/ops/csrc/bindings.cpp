@@ -330,6 +330,22 @@ torch::Tensor symm_tensor(int64_t ptr, int64_t numel, const std::string& dtype, 
                           torch::TensorOptions().dtype(st).device(torch::kCUDA, device));
 }
 
+// Register an existing host mapping (e.g. an mmap'd ring file) for device access; returns the
+// device address.
+int64_t host_register_mapped(int64_t host_ptr, int64_t bytes) {
+  void* d = nullptr;
+  TORCH_CHECK(cudaHostRegister(reinterpret_cast<void*>(host_ptr), bytes, cudaHostRegisterMapped) == cudaSuccess,
+              "cudaHostRegister failed");
+  TORCH_CHECK(cudaHostGetDevicePointer(&d, reinterpret_cast<void*>(host_ptr), 0) == cudaSuccess,
+              "cudaHostGetDevicePointer failed");
+  return reinterpret_cast<int64_t>(d);
+}
+
+void host_unregister(int64_t host_ptr) { cudaHostUnregister(reinterpret_cast<void*>(host_ptr)); }
+
+int64_t ring_record_bytes() { return rb::ring_record_bytes(); }
+int64_t kernel_stamp_bytes() { return rb::kernel_stamp_bytes(); }
+
 // Pinned, device-mapped host words (the abort word): the host writes, kernels poll.
 py::tuple host_words_alloc(int64_t n) {
   void* h = nullptr;
@@ -366,7 +382,7 @@ void symm_barrier(const torch::Tensor& pads, int64_t rank, int64_t world, int64_
 void dp_step_fused(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& weight_ptrs,
                    torch::Tensor& master, torch::Tensor& m, torch::Tensor& v, int64_t shard_lo, double lr, double b1,
                    double b2, double eps, double wd, bool decoupled, int64_t step, double grad_scale,
-                   int64_t abort_dev) {
+                   int64_t abort_dev, int64_t ring_dev, int64_t ring_capacity, int64_t stamp_dev) {
   CHECK_F32(master); CHECK_F32(m); CHECK_F32(v);
   TORCH_CHECK(grad_ptrs.size() == weight_ptrs.size() && !grad_ptrs.empty(), "one grad and weight pointer per rank");
   std::vector<const float*> g(grad_ptrs.size());
@@ -382,7 +398,8 @@ void dp_step_fused(const std::vector<int64_t>& grad_ptrs, const std::vector<int6
                             m.data_ptr<float>(), v.data_ptr<float>(), shard_lo, master.numel(), lr, b1, b2, eps, wd,
                             decoupled ? 1 : 0, static_cast<float>(bc1), static_cast<float>(std::sqrt(bc2)),
                             static_cast<float>(grad_scale), reinterpret_cast<const int*>(abort_dev),
-                            num_sms(master.get_device()), cur_stream()), "dp_step_fused");
+                            num_sms(master.get_device()), cur_stream(), reinterpret_cast<void*>(ring_dev),
+                            static_cast<int>(ring_capacity), reinterpret_cast<void*>(stamp_dev)), "dp_step_fused");
 }
 
 // Slice copies (src, dst, bytes) into this rank's memory; src may be peer memory.
@@ -538,6 +555,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &symm_barrier);
   m.def("dp_step_fused", &dp_step_fused);
   m.def("symm_copy", &symm_copy);
+  m.def("host_register_mapped", &host_register_mapped);
+  m.def("host_unregister", &host_unregister);
+  m.def("ring_record_bytes", &ring_record_bytes);
+  m.def("kernel_stamp_bytes", &kernel_stamp_bytes);
   m.def("tp_ag_gemm", &tp_ag_gemm);
   m.def("moe_route", &moe_route);
   m.def("moe_positions", &moe_positions);

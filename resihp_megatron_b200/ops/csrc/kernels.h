@@ -78,7 +78,9 @@ int symm_barrier(unsigned long long* const* pads_dev, int rank, int world, unsig
 int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int world, float* master, float* m,
                   float* v, long long shard_lo, long long n, float lr, float b1, float b2, float eps, float wd,
                   int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
-                  cudaStream_t s);
+                  cudaStream_t s, void* ring_base = nullptr, int ring_capacity = 0, void* stamp = nullptr);
+int ring_record_bytes();
+int kernel_stamp_bytes();
 int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
 int symm_copy_piece_bytes();
 int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t s);

@@ -77,6 +77,68 @@ __global__ void symm_barrier_kernel(unsigned long long* const* pads, int rank, i
   __threadfence_system();
 }
 
+// ---------------------------------------------------------------- device timing ring
+// Host-mapped ring in the NCCL profiler plugin's record format (so detect/nccl_profile_reader
+// reads both): header {u32 magic, u32 version, u32 capacity, u32 record size, u64 head}, then
+// records {u64 start_ns, u64 end_ns, u64 comm_id, u64 count, i32 rank, i32 nranks, i32 type,
+// i32 peer, char func[24], u64 seq}; seq = index + 1 is written last (seqlock).  A kernel that
+// reports itself keeps {min start, max end, blocks done} in a device stamp; the last block to
+// finish appends one record.
+struct RingRecord {
+  unsigned long long start_ns, end_ns, comm_id, count;
+  int rank, nranks, type, peer;
+  char func[24];
+  unsigned long long seq;
+};
+
+struct DevRing {
+  unsigned long long* head;  // host-mapped
+  RingRecord* records;       // host-mapped
+  int capacity, rank, nranks;
+};
+
+struct KernelStamp {
+  unsigned long long start, end;
+  unsigned int done;
+};
+
+constexpr int kTypeKernel = 1 << 3;
+
+__device__ __forceinline__ void stamp_begin(KernelStamp* st) {
+  if (st != nullptr && threadIdx.x == 0) atomicMin(&st->start, static_cast<unsigned long long>(globaltimer()));
+}
+
+__device__ void stamp_end(KernelStamp* st, const DevRing& ring, const char (&name)[24], unsigned long long count,
+                          unsigned long long comm_id) {
+  if (st == nullptr || ring.records == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  atomicMax(&st->end, static_cast<unsigned long long>(globaltimer()));
+  __threadfence();
+  if (atomicAdd(&st->done, 1u) + 1 != gridDim.x) return;
+  // last block: append the record, then reset the stamp for the next launch
+  const unsigned long long start = atomicAdd(&st->start, 0ull), end = atomicAdd(&st->end, 0ull);
+  const unsigned long long idx = atomicAdd_system(ring.head, 1ull);
+  RingRecord* r = ring.records + (idx % static_cast<unsigned long long>(ring.capacity));
+  volatile RingRecord* v = r;
+  v->seq = 0;
+  v->start_ns = start;
+  v->end_ns = end;
+  v->comm_id = comm_id;
+  v->count = count;
+  v->rank = ring.rank;
+  v->nranks = ring.nranks;
+  v->type = kTypeKernel;
+  v->peer = -1;
+  for (int i = 0; i < 24; ++i) v->func[i] = name[i];
+  __threadfence_system();
+  v->seq = idx + 1;
+  st->start = ~0ull;
+  st->end = 0;
+  st->done = 0;
+  __threadfence();
+}
+
 constexpr int kMaxWorld = 16;
 
 struct DpStepArgs {
@@ -89,12 +151,15 @@ struct DpStepArgs {
   int world;
   float lr, b1, b2, eps, wd, bc1, bc2_sqrt, grad_scale;
   int decoupled;
+  DevRing ring;
+  KernelStamp* stamp;
 };
 
 // 4 elements per thread, grid-stride.  Loads of the W gradients are issued together before
 // the sum so their NVLink latencies overlap.  The kernel never waits on another rank, so it does
 // not poll the abort word (a host-memory read per iteration would cost a PCIe round trip).
 __global__ void __launch_bounds__(256) dp_step_kernel(const __grid_constant__ DpStepArgs a) {
+  stamp_begin(a.stamp);
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x * 4;
   const float step_size = a.lr / a.bc1;
   for (long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < a.n; i += stride) {
@@ -140,6 +205,8 @@ __global__ void __launch_bounds__(256) dp_step_kernel(const __grid_constant__ Dp
     for (int r = 0; r < kMaxWorld; ++r)
       if (r < a.world) __stcg(reinterpret_cast<uint2*>(a.weights[r] + gi), u);
   }
+  static constexpr char kName[24] = "dp_reduce_adam_gather";
+  stamp_end(a.stamp, a.ring, kName, static_cast<unsigned long long>(a.n), 0ull);
 }
 
 // Slice migration: every (src, dst, bytes) piece is copied with 16-byte loads and stores; the
@@ -183,7 +250,7 @@ int symm_barrier(unsigned long long* const* pads_dev, int rank, int world, unsig
 int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int world, float* master, float* m,
                   float* v, long long shard_lo, long long n, float lr, float b1, float b2, float eps, float wd,
                   int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
-                  cudaStream_t s) {
+                  cudaStream_t s, void* ring_base, int ring_capacity, void* stamp) {
   if (world < 1 || world > kMaxWorld || (n & 3) || (shard_lo & 3)) return -1;
   DpStepArgs a{};
   for (int r = 0; r < world; ++r) {
@@ -209,6 +276,14 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
   a.bc2_sqrt = bc2_sqrt;
   a.grad_scale = grad_scale;
   (void)abort_word;  // no waits inside: see dp_step_kernel
+  // ring header: u32 magic, version, capacity, record size, u64 head (offset 16); records at 24
+  a.ring.head = ring_base != nullptr ? reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(ring_base) + 16)
+                                     : nullptr;
+  a.ring.records = ring_base != nullptr ? reinterpret_cast<RingRecord*>(static_cast<uint8_t*>(ring_base) + 24) : nullptr;
+  a.ring.capacity = ring_capacity;
+  a.ring.rank = 0;
+  a.ring.nranks = world;
+  a.stamp = reinterpret_cast<KernelStamp*>(stamp);
   const long long threads_needed = n / 4;
   long long blocks = (threads_needed + 255) / 256;
   const long long cap = static_cast<long long>(num_sms) * 8;
@@ -285,4 +360,9 @@ int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t 
   return static_cast<int>(cudaGetLastError());
 }
 
+}  // namespace rb
+
+namespace rb {
+int ring_record_bytes() { return static_cast<int>(sizeof(RingRecord)); }
+int kernel_stamp_bytes() { return static_cast<int>(sizeof(KernelStamp)); }
 }  // namespace rb

@@ -45,6 +45,7 @@ class FusedDataParallel:
         self.bank = 0
         self.heap: SymmetricHeap | None = None
         self.numel = 0
+        self.ring = None  # DeviceRing: one timing record per fused step
 
     def _shard_cap(self) -> int:
         from ..models.params import ALIGN
@@ -82,7 +83,9 @@ class FusedDataParallel:
         heap.barrier(self.budget)
         ext().dp_step_fused(heap.peer_ptrs("grad"), heap.peer_ptrs("weight"), P.master, P.exp_avg, P.exp_avg_sq,
                             P.shard_lo, float(lr), float(betas[0]), float(betas[1]), float(eps), float(weight_decay),
-                            bool(decoupled), int(P.step), float(grad_scale), self.abort.dev if self.abort else 0)
+                            bool(decoupled), int(P.step), float(grad_scale), self.abort.dev if self.abort else 0,
+                            self.ring.dev if self.ring else 0, self.ring.capacity if self.ring else 0,
+                            self.ring.stamp.data_ptr() if self.ring else 0)
         heap.barrier(self.budget)
         P.grad.zero_()
 

@@ -10,12 +10,16 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def test_fused_dp_step_emulated_ranks_matches_reference():
+def test_fused_dp_step_emulated_ranks_matches_reference(tmp_path):
     from resihp_megatron_b200.ops._build import ext
     from resihp_megatron_b200.parallel.symm import SymmetricHeap
 
+    from resihp_megatron_b200.detect.nccl_profile_reader import RingReader
+    from resihp_megatron_b200.parallel.device_ring import DeviceRing
+
     W, n = 4, 1 << 16
     heaps = SymmetricHeap.emulated({"grad": (n, torch.float32), "weight": (n, torch.bfloat16)}, W, "cuda")
+    ring = DeviceRing(directory=str(tmp_path), capacity=16)
     torch.manual_seed(0)
     grads = [torch.randn(n, device="cuda") for _ in range(W)]
     for r, h in enumerate(heaps):
@@ -30,7 +34,7 @@ def test_fused_dp_step_emulated_ranks_matches_reference():
         sl = slice(r * shard, (r + 1) * shard)
         st = [master[sl].clone(), m0[sl].clone(), v0[sl].clone()]
         ext().dp_step_fused(h.peer_ptrs("grad"), h.peer_ptrs("weight"), st[0], st[1], st[2], r * shard, lr, b1, b2,
-                            eps, wd, False, step, scale, 0)
+                            eps, wd, False, step, scale, 0, ring.dev, ring.capacity, ring.stamp.data_ptr())
         states.append(st)
     torch.cuda.synchronize()
     # fp32 reference in the same formula order as torch.optim.Adam (L2 weight decay)
@@ -44,6 +48,11 @@ def test_fused_dp_step_emulated_ranks_matches_reference():
     torch.testing.assert_close(torch.cat([s[1] for s in states]), m, rtol=1e-5, atol=1e-7)
     for h in heaps:  # every rank received every shard
         assert torch.equal(h.tensor("weight"), got.bfloat16())
+    # one device timing record per launch, readable by the NCCL-ring reader
+    recs = RingReader(ring.path).poll()
+    assert [r.func for r in recs] == ["dp_reduce_adam_gather"] * W
+    assert all(r.end_ns > r.start_ns for r in recs) and all(r.count == shard for r in recs)
+    ring.close()
     heaps[0].close()
 
 
