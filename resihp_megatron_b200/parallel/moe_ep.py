@@ -28,6 +28,25 @@ from ..ops._build import ext
 from .symm import AbortWord, SymmetricHeap
 
 
+def receive_layout(table, holder: list[int], me: int, world: int) -> tuple[list[int], list[tuple[int, int]]]:
+    """Receive rows of a step from the count table ``table[source][expert]``: at every holder its
+    local experts in expert order, each expert's rows ordered by source rank.  Returns, for
+    source ``me``, the first row of each expert ``e`` at ``holder[e]`` (``rowbase[e]``), and for
+    ``me`` as a holder the (first row, rows) range of each of its experts."""
+    E = len(holder)
+    totals = [int(sum(int(table[s][e]) for s in range(world))) for e in range(E)]
+    start = [0] * E
+    for h in range(world):
+        off = 0
+        for e in range(E):
+            if holder[e] == h:
+                start[e] = off
+                off += totals[e]
+    rowbase = [start[e] + sum(int(table[s][e]) for s in range(me)) for e in range(E)]
+    ranges = [(start[e], totals[e]) for e in range(E) if holder[e] == me]
+    return rowbase, ranges
+
+
 class ExpertParallelMoE:
     def __init__(self, rank: int, world: int, exchange, device, *, hidden: int, num_experts: int, top_k: int,
                  max_tokens: int, holder: list[int], abort: AbortWord | None = None, budget_s: float = 30.0,
@@ -101,20 +120,10 @@ class ExpertParallelMoE:
         self._layout(table.to("cpu", torch.int64))
 
     def _layout(self, table: torch.Tensor) -> None:
-        E, me = self.E, self.rank
-        totals = table.sum(0).tolist()
-        # receive rows at each holder: its local experts in order, each [source 0, source 1, ...]
-        start = [0] * E
-        for h in range(self.world):
-            off = 0
-            for e in range(E):
-                if self.holder[e] == h:
-                    start[e] = off
-                    off += totals[e]
-        rowbase = [start[e] + int(table[:me, e].sum()) for e in range(E)]
+        rowbase, ranges = receive_layout(table, self.holder, self.rank, self.world)
         self.saved["rowbase"] = torch.tensor(rowbase, dtype=torch.int64, device=self.device)
-        self.saved["local_ranges"] = [(start[e], totals[e]) for e in self.local]
-        self.saved["recv_rows"] = sum(totals[e] for e in self.local)
+        self.saved["local_ranges"] = ranges
+        self.saved["recv_rows"] = sum(n for _, n in ranges)
 
     # ------------------------------------------------------------------ phase 3: dispatch
     def dispatch(self) -> None:
