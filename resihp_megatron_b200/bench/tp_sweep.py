@@ -78,9 +78,8 @@ def run(M: int = 8192, K: int = 8192, N: int = 8192, tps=(2, 4, 8), iters: int =
         w_col = torch.randn(N // tp, K, device=dev, generator=g).bfloat16()
         x_all = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
         y = torch.empty(M, N // tp, dtype=torch.bfloat16, device=dev)
-        comm.local_chunk(M, K).copy_(x_loc)
-
         def ag_fused():
+            comm.local_chunk(M, K).copy_(x_loc)  # the producer of x writes its rows into the gather buffer
             comm.all_gather_gemm(M, w_col, out=y)
 
         def ag_nccl():

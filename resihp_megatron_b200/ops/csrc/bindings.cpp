@@ -418,38 +418,42 @@ void symm_copy(const std::vector<int64_t>& triples, int64_t device) {
 
 // Tensor parallel: all-gather -> GEMM (column-parallel) and GEMM -> reduce-scatter (row-parallel).
 void tp_ag_gemm(const torch::Tensor& x_full, const std::vector<int64_t>& src_ptrs, int64_t self, const torch::Tensor& w,
-                torch::Tensor& y, torch::Tensor& ready, int64_t abort_dev) {
+                bool w_t, torch::Tensor& y, torch::Tensor& ready, int64_t abort_dev) {
   CHECK_BF16(x_full); CHECK_BF16(w); CHECK_BF16(y);
   TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == torch::kInt32 && ready.numel() >= (int64_t)src_ptrs.size());
   const int world = static_cast<int>(src_ptrs.size());
-  const int M = x_full.size(0), K = x_full.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K && y.size(0) == M && y.size(1) == N, "tp_ag_gemm: shapes");
+  const int M = x_full.size(0), K = x_full.size(1), N = w_t ? w.size(1) : w.size(0);
+  TORCH_CHECK((w_t ? w.size(0) : w.size(1)) == K && y.size(0) == M && y.size(1) == N, "tp_ag_gemm: shapes");
   std::vector<const void*> src(world);
   for (int c = 0; c < world; ++c) src[c] = reinterpret_cast<const void*>(src_ptrs[c]);
   const c10::cuda::CUDAGuard g(x_full.device());
   cudaMemsetAsync(ready.data_ptr(), 0, world * sizeof(int), cur_stream());
   RB_CALL(rb::gemm_ag_bf16(x_full.data_ptr(), src.data(), world, static_cast<int>(self), M / world, w.data_ptr(),
-                           y.data_ptr(), M, N, K, ready.data_ptr<int>(), reinterpret_cast<const int*>(abort_dev),
+                           w_t, y.data_ptr(), M, N, K, ready.data_ptr<int>(), reinterpret_cast<const int*>(abort_dev),
                            err_ptr(x_full), num_sms(x_full.get_device()), cur_stream()), "tp_ag_gemm");
 }
 
-void tp_rs_gemm(const torch::Tensor& x, const torch::Tensor& w, const std::vector<int64_t>& recv_ptrs, int64_t slot) {
+void tp_rs_gemm(const torch::Tensor& x, const torch::Tensor& w, bool w_t, const std::vector<int64_t>& recv_ptrs,
+                int64_t slot) {
   CHECK_BF16(x); CHECK_BF16(w);
   const int world = static_cast<int>(recv_ptrs.size());
   std::vector<void*> recv(world);
   for (int q = 0; q < world; ++q) recv[q] = reinterpret_cast<void*>(recv_ptrs[q]);
+  const int N = w_t ? w.size(1) : w.size(0);
+  TORCH_CHECK((w_t ? w.size(0) : w.size(1)) == x.size(1), "tp_rs_gemm: contraction sizes differ");
   const c10::cuda::CUDAGuard g(x.device());
-  RB_CALL(rb::gemm_rs_scatter_bf16(x.data_ptr(), w.data_ptr(), recv.data(), world, static_cast<int>(slot),
-                                   x.size(0), w.size(0), x.size(1), err_ptr(x), num_sms(x.get_device()),
-                                   cur_stream()), "tp_rs_gemm");
+  RB_CALL(rb::gemm_rs_scatter_bf16(x.data_ptr(), w.data_ptr(), w_t, recv.data(), world, static_cast<int>(slot),
+                                   x.size(0), N, x.size(1), err_ptr(x), num_sms(x.get_device()), cur_stream()),
+          "tp_rs_gemm");
 }
 
-void tp_rs_reduce(const torch::Tensor& recv, int64_t world, torch::Tensor& out) {
+void tp_rs_reduce(const torch::Tensor& recv, int64_t world, torch::Tensor& out,
+                  const c10::optional<torch::Tensor>& residual) {
   CHECK_BF16(recv); CHECK_BF16(out);
   TORCH_CHECK(recv.numel() >= world * out.numel(), "tp_rs_reduce: receive buffer too small");
   const c10::cuda::CUDAGuard g(out.device());
-  RB_CALL(rb::rs_reduce(recv.data_ptr(), static_cast<int>(world), out.numel(), out.data_ptr(), cur_stream()),
-          "tp_rs_reduce");
+  RB_CALL(rb::rs_reduce(recv.data_ptr(), static_cast<int>(world), out.numel(), out.data_ptr(),
+                        residual.has_value() ? residual->data_ptr() : nullptr, cur_stream()), "tp_rs_reduce");
 }
 
 // ------------------------------------------------------------------------- expert parallelism
@@ -567,7 +571,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_grad_push", &moe_grad_push);
   m.def("moe_grad_pull", &moe_grad_pull);
   m.def("tp_rs_gemm", &tp_rs_gemm);
-  m.def("tp_rs_reduce", &tp_rs_reduce);
+  m.def("tp_rs_reduce", &tp_rs_reduce, py::arg("recv"), py::arg("world"), py::arg("out"),
+        py::arg("residual") = py::none());
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("S"),
         py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0);

@@ -420,7 +420,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int EPI>
+template <int EPI, bool B_MN>
 __global__ void __launch_bounds__(320, 1)
     gemm_ag_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using C = GemmCfg<256>;
@@ -515,7 +515,13 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
           tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fb, kb * BK, mb * BM);
-          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * BK, nb * BN);
+          if (!B_MN) {
+            tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(smem_u32(sB + stage * C::B_BYTES) + j * 8192, &tmB, fb, nb * BN + 64 * j, kb * BK);
+          }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -530,7 +536,7 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(BM, BN, true, false, false);
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, true, false, B_MN);
       int stage = 0, acc = 0;
       uint32_t phase = 0, aphase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -549,7 +555,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_f16(d_tmem, make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B),
-                     make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B), idesc, (kb | k) != 0 ? 1u : 0u);
+                     B_MN ? make_smem_desc(b_base + k * 2048, 8192, 1024, kSwizzle128B)
+                          : make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B),
+                     idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) {
             stage = 0;
@@ -944,14 +952,16 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, co
 // `x_full` is this rank's [M, K] gather buffer (its own chunk already in place), `x_src[c]` the
 // address of chunk c in rank c's buffer (peer memory), `ready` `world` zeroed ints.
 int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
-                 void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
+                 bool w_mn, void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
                  cudaStream_t stream) {
   if (world < 1 || world > kMaxTP || chunk_rows % 128 || M != chunk_rows * world || K % 8 || N % 8) return -3;
   if ((reinterpret_cast<uintptr_t>(x_full) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(Y)) & 15)
     return -4;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_bf16_2d(&ta, x_full, K, M, K, 64, 128)) return -100 - rc;
-  if (int rc = make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256)) return -100 - rc;
+  // W is [N, K] (K-major) or, with w_mn, [K, N] (B(n, k) = W[k * N + n])
+  if (int rc = w_mn ? make_tmap_bf16_2d(&tb, W, N, K, N, 64, 64) : make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256))
+    return -100 - rc;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.D = Y; a.ldd = N; a.alpha = 1.f; a.err = err;
   a.ag_world = world; a.ag_self = self; a.ag_chunk_rows = chunk_rows;
@@ -961,12 +971,12 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
   a.ag_ready = ready;
   a.abort_word = abort_word;
   using C = GemmCfg<256>;
-  auto kern = gemm_ag_sm100<kEpiBF16>;
-  static bool attr = false;
-  if (!attr) {
+  auto kern = w_mn ? gemm_ag_sm100<kEpiBF16, true> : gemm_ag_sm100<kEpiBF16, false>;
+  static bool attr[2] = {false, false};
+  if (!attr[w_mn]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return static_cast<int>(e);
-    attr = true;
+    attr[w_mn] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms);
@@ -984,20 +994,22 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
 // Partial products of a row-parallel layer, scattered for a reduce-scatter: rows
 // [q * (M / world), (q + 1) * (M / world)) of X[M, K] @ W[N, K]^T are stored (bf16) into
 // `recv[q]` (rank q's receive buffer, [world][M / world][N]) at slot `slot`.
-int gemm_rs_scatter_bf16(const void* X, const void* W, void* const* recv, int world, int slot, int M, int N, int K,
-                         int* err, int num_sms, cudaStream_t stream) {
+int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* recv, int world, int slot, int M, int N,
+                         int K, int* err, int num_sms, cudaStream_t stream) {
   if (world < 1 || world > kMaxTP || M % world || N % 8 || K % 8) return -3;
   if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(W)) & 15) return -4;
   for (int q = 0; q < world; ++q)
     if (reinterpret_cast<uintptr_t>(recv[q]) & 15) return -4;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_bf16_2d(&ta, X, K, M, K, 64, 128)) return -100 - rc;
-  if (int rc = make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256)) return -100 - rc;
+  if (int rc = w_mn ? make_tmap_bf16_2d(&tb, W, N, K, N, 64, 64) : make_tmap_bf16_2d(&tb, W, K, N, K, 64, 256))
+    return -100 - rc;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.alpha = 1.f; a.err = err;
   a.rs_slot = slot; a.rs_rows = M / world;
   for (int q = 0; q < world; ++q) a.rs_dst[q] = recv[q];
-  return launch_gemm<256, false, false, kEpiScatterBF16>(ta, tb, a, num_sms, stream);
+  return w_mn ? launch_gemm<256, false, true, kEpiScatterBF16>(ta, tb, a, num_sms, stream)
+              : launch_gemm<256, false, false, kEpiScatterBF16>(ta, tb, a, num_sms, stream);
 }
 
 // A(m,k) = a_mn ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_mn ? B[k*ldb + n] : B[n*ldb + k].

@@ -83,7 +83,7 @@ int ring_record_bytes();
 int kernel_stamp_bytes();
 int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
 int symm_copy_piece_bytes();
-int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t s);
+int rs_reduce(const void* recv, int world, long long n, void* out, const void* residual, cudaStream_t s);
 // Expert parallelism (moe.cu).
 int moe_route(const void* x, const void* w, const float* bias, int T, int H, int E, int k, float* logits, int* topi,
               float* gates, cudaStream_t s);
@@ -99,10 +99,10 @@ int moe_grad_pull(const void* dout, const float* gates, const float* dgate, cons
                   float* dlogits, cudaStream_t s);
 // Tensor-parallel fused GEMMs (gemm_sm100.cu).
 int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
-                 void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
+                 bool w_mn, void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
                  cudaStream_t stream);
-int gemm_rs_scatter_bf16(const void* X, const void* W, void* const* recv, int world, int slot, int M, int N, int K,
-                         int* err, int num_sms, cudaStream_t stream);
+int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* recv, int world, int slot, int M, int N,
+                         int K, int* err, int num_sms, cudaStream_t stream);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
 int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
 }  // namespace rb

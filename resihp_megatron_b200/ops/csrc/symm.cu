@@ -329,10 +329,20 @@ int symm_copy_piece_bytes() { return static_cast<int>(sizeof(CopyPiece)); }
 namespace {
 // Reduce-scatter finish: out[i] = sum over slots s (rank order) of recv[s][i], fp32 accumulate.
 __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, int world, long long n,
-                                 __nv_bfloat16* __restrict__ out) {
+                                 __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ residual) {
   const long long i8 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   if (i8 >= n) return;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (residual != nullptr) {  // residual added first, then the slots in rank order
+    const uint4 u = *reinterpret_cast<const uint4*>(residual + i8);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      acc[2 * j] = f.x;
+      acc[2 * j + 1] = f.y;
+    }
+  }
   for (int s = 0; s < world; ++s) {
     const uint4 u = __ldcv(reinterpret_cast<const uint4*>(recv + s * n + i8));
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -352,11 +362,14 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ recv, int wor
 }
 }  // namespace
 
-int rs_reduce(const void* recv, int world, long long n, void* out, cudaStream_t s) {
-  if ((n & 7) || ((reinterpret_cast<uintptr_t>(recv) | reinterpret_cast<uintptr_t>(out)) & 15)) return -1;
+int rs_reduce(const void* recv, int world, long long n, void* out, const void* residual, cudaStream_t s) {
+  if ((n & 7) || ((reinterpret_cast<uintptr_t>(recv) | reinterpret_cast<uintptr_t>(out) |
+                   reinterpret_cast<uintptr_t>(residual)) & 15))
+    return -1;
   const long long threads = n / 8;
   rs_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
-      reinterpret_cast<const __nv_bfloat16*>(recv), world, n, reinterpret_cast<__nv_bfloat16*>(out));
+      reinterpret_cast<const __nv_bfloat16*>(recv), world, n, reinterpret_cast<__nv_bfloat16*>(out),
+      reinterpret_cast<const __nv_bfloat16*>(residual));
   return static_cast<int>(cudaGetLastError());
 }
 

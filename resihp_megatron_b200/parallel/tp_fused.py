@@ -27,70 +27,113 @@ from .symm import AbortWord, SymmetricHeap
 
 
 class TensorParallelComm:
+    """Per tensor-parallel group: two gather buffers and two reduce-scatter receive buffers in the
+    symmetric heap, used alternately.  Every collective starts with a bounded barrier; since a
+    buffer is reused only two collectives later, that leading barrier (which each rank reaches
+    after finishing its previous kernels) already guarantees nobody still reads it, so no trailing
+    barrier is needed."""
+
     def __init__(self, rank: int, world: int, exchange, device, *, max_rows: int, max_k: int, max_n: int,
                  abort: AbortWord | None = None, budget_s: float = 30.0, _heap: SymmetricHeap | None = None):
         self.rank, self.world = rank, world
         self.max_rows, self.max_k, self.max_n = max_rows, max_k, max_n
         self.abort = abort
         self.budget = budget_s
-        segs = {"x_full": (max_rows * max_k, torch.bfloat16),
-                "rs_recv": (world * (max_rows // world) * max_n, torch.bfloat16)}
-        self.heap = _heap or SymmetricHeap(segs, rank, world, exchange, device, abort)
+        self.heap = _heap or SymmetricHeap(self.segments(world, max_rows, max_k, max_n), rank, world, exchange,
+                                           device, abort)
         self.ready = torch.zeros(world, dtype=torch.int32, device=device)
         self.emulated = _heap is not None
+        self._ag = 0
+        self._rs = 0
+
+    @staticmethod
+    def segments(world: int, max_rows: int, max_k: int, max_n: int) -> dict:
+        return {"x_full0": (max_rows * max_k, torch.bfloat16), "x_full1": (max_rows * max_k, torch.bfloat16),
+                "rs_recv0": (world * (max_rows // world) * max_n, torch.bfloat16),
+                "rs_recv1": (world * (max_rows // world) * max_n, torch.bfloat16)}
 
     @classmethod
     def emulated_group(cls, world: int, device, **kw) -> list["TensorParallelComm"]:
         """``world`` ranks in one process on one GPU (tests): call the per-rank steps in turn."""
-        segs = {"x_full": (kw["max_rows"] * kw["max_k"], torch.bfloat16),
-                "rs_recv": (world * (kw["max_rows"] // world) * kw["max_n"], torch.bfloat16)}
-        heaps = SymmetricHeap.emulated(segs, world, device)
+        heaps = SymmetricHeap.emulated(cls.segments(world, kw["max_rows"], kw["max_k"], kw["max_n"]), world, device)
         return [cls(r, world, None, device, _heap=heaps[r], **kw) for r in range(world)]
 
     def _barrier(self) -> None:
         if not self.emulated:
             self.heap.barrier(self.budget)
 
-    # ------------------------------------------------------------------ all-gather -> GEMM
-    def gather_buffer(self, M: int, K: int) -> torch.Tensor:
-        return self.heap.tensor("x_full")[: M * K].view(M, K)
+    # ------------------------------------------------------------------ all-gather (-> GEMM)
+    def gather_buffer(self, M: int, K: int, buf: int | None = None) -> torch.Tensor:
+        b = self._ag if buf is None else buf
+        return self.heap.tensor(f"x_full{b}")[: M * K].view(M, K)
 
     def local_chunk(self, M: int, K: int) -> torch.Tensor:
-        """Where this rank writes its ``[M / tp, K]`` shard before ``all_gather_gemm``."""
+        """Where this rank writes its ``[M / tp, K]`` shard before the next gather."""
         rows = M // self.world
         return self.gather_buffer(M, K)[self.rank * rows:(self.rank + 1) * rows]
 
-    def all_gather_gemm(self, M: int, w: torch.Tensor, out: torch.Tensor | None = None,
-                        finish: bool = True) -> torch.Tensor:
-        K = w.shape[1]
+    def _sources(self, M: int, K: int, b: int) -> list[int]:
         rows = M // self.world
-        xf = self.gather_buffer(M, K)
-        y = torch.empty(M, w.shape[0], dtype=torch.bfloat16, device=w.device) if out is None else out
-        base = self.heap.peer_ptrs("x_full")
-        src = [base[c] + c * rows * K * 2 for c in range(self.world)]
-        self._barrier()  # every rank's chunk is in place
-        ext().tp_ag_gemm(xf, src, self.rank, w, y, self.ready, self.abort.dev if self.abort else 0)
-        if finish:
-            self._barrier()  # nobody still reads this rank's chunk
-        count(3 if not self.emulated else 1)
+        base = self.heap.peer_ptrs(f"x_full{b}")
+        return [base[c] + c * rows * K * 2 for c in range(self.world)]
+
+    def all_gather_gemm(self, M: int, w: torch.Tensor, out: torch.Tensor | None = None, w_t: bool = False,
+                        advance: bool = True) -> torch.Tensor:
+        """``AllGather(chunks)[M, K] @ op(w)^T`` with ``op(w) = w`` ([N, K]) or ``w.T`` (``w_t``,
+        ``w`` is [K, N]).  The gathered input stays in the gather buffer until the buffer's next
+        use (two gathers later) -- weight gradients read it from there."""
+        K = w.shape[0] if w_t else w.shape[1]
+        N = w.shape[1] if w_t else w.shape[0]
+        b = self._ag
+        xf = self.gather_buffer(M, K, b)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=w.device) if out is None else out
+        self._barrier()  # every rank's chunk is in place; the buffer's previous readers are done
+        ext().tp_ag_gemm(xf, self._sources(M, K, b), self.rank, w, bool(w_t), y, self.ready,
+                         self.abort.dev if self.abort else 0)
+        count(2 if not self.emulated else 1)
+        if advance:
+            self._ag ^= 1
         return y
 
-    # ------------------------------------------------------------------ GEMM -> reduce-scatter
-    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Emulated groups: call ``scatter_partials`` on every rank, then ``reduce_received``."""
-        self._barrier()  # receive slots are free again
-        self.scatter_partials(x, w)
-        self._barrier()  # every partial has landed
-        return self.reduce_received(x.shape[0], w.shape[0], out)
+    def all_gather(self, M: int, K: int, advance: bool = True) -> torch.Tensor:
+        """Plain all-gather of the chunks (peer pulls); returns the gathered ``[M, K]`` view."""
+        b = self._ag
+        xf = self.gather_buffer(M, K, b)
+        rows = M // self.world
+        self._barrier()
+        src = self._sources(M, K, b)
+        dst = self.heap.peer_ptrs(f"x_full{b}")[self.rank]
+        triples = []
+        for c in range(self.world):
+            if c != self.rank:
+                triples += [src[c], dst + c * rows * K * 2, rows * K * 2]
+        ext().symm_copy(triples, xf.device.index if xf.device.index is not None else 0)
+        count(2 if not self.emulated else 1)
+        if advance:
+            self._ag ^= 1
+        return xf
 
-    def scatter_partials(self, x: torch.Tensor, w: torch.Tensor) -> None:
-        ext().tp_rs_gemm(x, w, self.heap.peer_ptrs("rs_recv"), self.rank)
+    # ------------------------------------------------------------------ GEMM -> reduce-scatter
+    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                            w_t: bool = False, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``ReduceScatter_rows(x @ op(w)^T)`` (+ ``residual``, this rank's rows).  Emulated groups:
+        call ``scatter_partials`` on every rank, then ``reduce_received``."""
+        self._barrier()  # receive slots of this buffer are free again
+        self.scatter_partials(x, w, w_t)
+        self._barrier()  # every partial has landed
+        y = self.reduce_received(x.shape[0], w.shape[1] if w_t else w.shape[0], out, residual)
+        self._rs ^= 1
+        return y
+
+    def scatter_partials(self, x: torch.Tensor, w: torch.Tensor, w_t: bool = False) -> None:
+        ext().tp_rs_gemm(x, w, bool(w_t), self.heap.peer_ptrs(f"rs_recv{self._rs}"), self.rank)
         count(1)
 
-    def reduce_received(self, M: int, N: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    def reduce_received(self, M: int, N: int, out: torch.Tensor | None = None,
+                        residual: torch.Tensor | None = None) -> torch.Tensor:
         rows = M // self.world
         y = torch.empty(rows, N, dtype=torch.bfloat16, device=self.ready.device) if out is None else out
-        ext().tp_rs_reduce(self.heap.tensor("rs_recv")[: self.world * rows * N], self.world, y)
+        ext().tp_rs_reduce(self.heap.tensor(f"rs_recv{self._rs}")[: self.world * rows * N], self.world, y, residual)
         count(1)
         return y
 

@@ -28,7 +28,7 @@ def test_all_gather_gemm(world, M, K, N):
         assert int(error_state()[0]) == 0
         ref = x_all @ ws[r].float().t()
         assert (y.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-2, r
-        assert torch.equal(t.gather_buffer(M, K), x_all.bfloat16()), "the gather buffer holds every chunk"
+        assert torch.equal(t.gather_buffer(M, K, buf=0), x_all.bfloat16()), "the gather buffer holds every chunk"
     ranks[0].close()
 
 
@@ -45,9 +45,45 @@ def test_gemm_reduce_scatter(world, M, K, N):
     parts = [(xs[r].float() @ ws[r].float().t()).bfloat16().float() for r in range(world)]
     full = sum(parts)
     rows = M // world
-    outs = [t.reduce_received(M, N) for t in ranks]
+    res = [torch.randn(rows, N, device="cuda").bfloat16() for _ in range(world)]
+    outs = [t.reduce_received(M, N, residual=res[q]) for q, t in enumerate(ranks)]
+    full = full + torch.cat(res).float()
     torch.cuda.synchronize()
     for q, y in enumerate(outs):
         ref = full[q * rows:(q + 1) * rows]
         assert (y.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 2e-2, q
+    ranks[0].close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_transposed_weight_variants(world):
+    """The backward forms: all-gather -> GEMM and GEMM -> reduce-scatter with the weight read
+    MN-major (``w_t``), as the input-gradient GEMMs of row- and column-parallel layers use it."""
+    from resihp_megatron_b200.parallel.tp_fused import TensorParallelComm
+
+    M, K, N = 512, 384, 256
+    ranks = TensorParallelComm.emulated_group(world, "cuda", max_rows=M, max_k=max(K, N), max_n=max(K, N))
+    torch.manual_seed(2)
+    rows = M // world
+    xs = [torch.randn(rows, K, device="cuda").bfloat16() for _ in range(world)]
+    wts = [torch.randn(K, N, device="cuda").bfloat16() for _ in range(world)]  # stored [K, N]
+    for r, t in enumerate(ranks):
+        t.local_chunk(M, K).copy_(xs[r])
+    x_all = torch.cat(xs).float()
+    for r, t in enumerate(ranks):
+        y = t.all_gather_gemm(M, wts[r], w_t=True, advance=False)
+        ref = x_all @ wts[r].float()
+        assert (y.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-2
+    xf = [torch.randn(M, K, device="cuda").bfloat16() for _ in range(world)]
+    for r, t in enumerate(ranks):
+        t.scatter_partials(xf[r], wts[r], w_t=True)
+    full = sum((xf[r].float() @ wts[r].float()).bfloat16().float() for r in range(world))
+    for q, t in enumerate(ranks):
+        y = t.reduce_received(M, N)
+        ref = full[q * rows:(q + 1) * rows]
+        assert (y.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 2e-2
+    # plain gather
+    for r, t in enumerate(ranks):
+        g = t.all_gather(M, K, advance=False)
+        assert torch.equal(g, x_all.bfloat16())
     ranks[0].close()
