@@ -100,6 +100,8 @@ struct DevRing {
 struct KernelStamp {
   unsigned long long start, end;
   unsigned int done;
+  unsigned int pad;
+  unsigned long long head;  // records appended so far (device memory: no atomics on host memory)
 };
 
 constexpr int kTypeKernel = 1 << 3;
@@ -118,7 +120,7 @@ __device__ void stamp_end(KernelStamp* st, const DevRing& ring, const char (&nam
   if (atomicAdd(&st->done, 1u) + 1 != gridDim.x) return;
   // last block: append the record, then reset the stamp for the next launch
   const unsigned long long start = atomicAdd(&st->start, 0ull), end = atomicAdd(&st->end, 0ull);
-  const unsigned long long idx = atomicAdd_system(ring.head, 1ull);
+  const unsigned long long idx = st->head++;  // launches of one stamp are serialised on their stream
   RingRecord* r = ring.records + (idx % static_cast<unsigned long long>(ring.capacity));
   volatile RingRecord* v = r;
   v->seq = 0;
@@ -133,6 +135,8 @@ __device__ void stamp_end(KernelStamp* st, const DevRing& ring, const char (&nam
   for (int i = 0; i < 24; ++i) v->func[i] = name[i];
   __threadfence_system();
   v->seq = idx + 1;
+  __threadfence_system();
+  *reinterpret_cast<volatile unsigned long long*>(ring.head) = idx + 1;  // publish after the record
   st->start = ~0ull;
   st->end = 0;
   st->done = 0;

@@ -201,10 +201,9 @@ class ExpertParallelMoE:
         ext().moe_grad_pull(s["dout"], s["gates"], s["dgate"], s["topi"], s["route_row"], self.k, self.E,
                             self.heap.peer_ptrs("dxrecv"), dx, dlogits)
         ops.count(1)
-        dl = dlogits.bfloat16()
-        ops.gemm(dl, s["x"], a_t=True, b_t=True, out=router_grad, accumulate=True)  # dW_r += dl^T x
-        dx_router = ops.gemm(dl, router_w, b_t=True)  # [T, E] @ [E, H]
-        dx.add_(dx_router)
+        # router path: [T, E] x [E, H] products with E <= 16 (too narrow for the tensor-core tiles)
+        router_grad.add_(dlogits.t() @ s["x"].float())
+        dx.add_((dlogits @ router_w.float()).bfloat16())
         self._barrier()
         return dx
 

@@ -19,7 +19,14 @@ def test_fused_dp_step_emulated_ranks_matches_reference(tmp_path):
 
     W, n = 4, 1 << 16
     heaps = SymmetricHeap.emulated({"grad": (n, torch.float32), "weight": (n, torch.bfloat16)}, W, "cuda")
-    ring = DeviceRing(directory=str(tmp_path), capacity=16)
+    import os
+
+    ring_dir = tmp_path
+    if os.path.isdir("/dev/shm"):  # tmpfs: registering its pages for device writes is supported
+        import tempfile
+
+        ring_dir = tempfile.mkdtemp(dir="/dev/shm")
+    ring = DeviceRing(directory=str(ring_dir), capacity=16)
     torch.manual_seed(0)
     grads = [torch.randn(n, device="cuda") for _ in range(W)]
     for r, h in enumerate(heaps):
