@@ -181,6 +181,7 @@ def main() -> None:
     for s in range(args.warmup):
         trainer.step_device(*dev_batches[s % len(dev_batches)])
     torch.cuda.synchronize()
+    trainer.check()  # a peer that never reached a barrier ends the run here, not after every step
 
     # ---- device-timed region
     sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
@@ -200,6 +201,7 @@ def main() -> None:
     barrier()
     launches = ops.launches() - l0
     clocks = sampler.stop() if sampler else None
+    trainer.check()
     ms = start.elapsed_time(end)
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:

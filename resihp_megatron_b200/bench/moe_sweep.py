@@ -102,6 +102,7 @@ def run(H=4096, Fd=14336, E=8, k=2, T=4096, iters=5) -> list[dict]:
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
+        moe.heap.check()  # a peer that missed a barrier ends the sweep here
         times = []
         for _ in range(iters):
             dist.barrier()

@@ -112,6 +112,7 @@ def run(M: int = 8192, K: int = 8192, N: int = 8192, tps=(2, 4, 8), iters: int =
         ref_rs = y_rs.float().clone()
         rs_nccl()
         rs_err = (ref_rs - y_rs.float()).abs().max().item() / (y_rs.float().abs().max().item() + 1e-6)
+        comm.heap.check()  # a peer that missed a barrier ends the sweep here
         for op, fns, nbytes, flops in (("allgather_gemm", (("fused", ag_fused), ("nccl", ag_nccl)), ag_bytes, ag_flops),
                                        ("gemm_reducescatter", (("fused", rs_fused), ("nccl", rs_nccl)), rs_bytes,
                                         rs_flops)):

@@ -45,9 +45,14 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 
 __device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
-// status[0] = 0 ok, 1 timeout, 2 aborted; status[1] = the rank that was waited for.
+// status[0] = 0 ok, 1 timeout, 2 aborted (sticky until the host clears it); status[1] = the rank
+// that was waited for.
 __global__ void symm_barrier_kernel(unsigned long long* const* pads, int rank, int world, unsigned long long epoch,
                                     const int* abort_word, int* status, int* err, unsigned long long budget_ns) {
+  // A failed barrier is sticky: once one barrier of this heap timed out or was aborted, later
+  // ones return at once, so a broken generation costs one budget, not one per barrier, before
+  // the host reads the status and raises.
+  if (ld_volatile_int(status) != 0) return;
   __threadfence_system();
   __syncthreads();
   const int t = threadIdx.x;

@@ -120,9 +120,14 @@ class GPUTrainer:
         self.labels_dev.copy_(labels_host, non_blocking=True)
         loss = self.step_device(self.ids_dev, self.labels_dev)
         value = float(loss.item())
+        self.check()
+        return value
+
+    def check(self) -> None:
+        """Raise ``PeerTimeout`` / ``PeerAborted`` if a peer barrier of the fused data-parallel
+        step failed since the heap was built (synchronises with the device)."""
         if self.fused is not None:
             self.fused.check()
-        return value
 
     # ------------------------------------------------------------------ live reconfiguration
     def shrink(self, survivors: list[int], new_group) -> bool:
@@ -211,7 +216,7 @@ class GPUTrainer:
             self.fused = None
 
 
-def init_distributed(timeout_s: float = 300.0) -> tuple[int, int, int]:
+def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
     """Initialise NCCL from torchrun's environment; returns (rank, world, local_rank)."""
     import os
 

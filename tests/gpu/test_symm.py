@@ -78,6 +78,12 @@ def test_barrier_single_rank_then_timeout_and_abort_paths():
     with pytest.raises(PeerTimeout, match="peer 1"):
         pair[0].check()
     assert time.monotonic() - t0 < 10
+    # a failed barrier is sticky: the next one returns at once instead of waiting its budget
+    t0 = time.monotonic()
+    pair[0].barrier(30.0)
+    with pytest.raises(PeerTimeout):
+        pair[0].check()
+    assert time.monotonic() - t0 < 5
     # the raised abort word ends the wait early
     abort = AbortWord()
     pair[0].abort = abort
