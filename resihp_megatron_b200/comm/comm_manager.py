@@ -182,6 +182,24 @@ class ResilientCommManager:
                  len(groups))
         return comms
 
+    def adopt(self, generation: int, world: list[str], my_id: str, specs: list[GroupSpec]) -> GenerationComms:
+        """Use the already initialised default process group (a launcher's environment, e.g.
+        ``torchrun``) as this generation's world and create the plan's subgroups on it."""
+        t0 = time.monotonic()
+        self._abort.clear()
+        rank = world.index(my_id)
+        if not dist.is_initialized() or dist.get_world_size() != len(world) or dist.get_rank() != rank:
+            raise RuntimeError("adopt() needs an initialised default group matching the world")
+        with self._lock:
+            self._live = [c10d._get_default_group()]
+        groups = self._make_subgroups(rank, specs)
+        if self.validate:
+            self._validate(len(world), groups, specs)
+        comms = GenerationComms(generation, rank, tuple(world), {s.name: s for s in specs}, groups, "adopted",
+                                time.monotonic() - t0)
+        self.current = comms
+        return comms
+
     def _init_world(self, rank: int, world_size: int, store) -> None:
         kw: dict = {"backend": self.backend, "store": store, "rank": rank, "world_size": world_size,
                     "timeout": self.timeout}

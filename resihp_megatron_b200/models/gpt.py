@@ -187,9 +187,7 @@ class LlamaModel:
         return self.xs[-1]
 
     def _rmsnorm(self, x, w, out, rstd):
-        ops.ext().rmsnorm_fwd(x, w, out, rstd, float(self.cfg.norm_eps))
-        ops.count(1)
-        return out, rstd
+        return ops.rmsnorm_fwd(x, w, float(self.cfg.norm_eps), out=out, rstd=rstd)
 
     def _attention_fwd(self, i, q, k, v):
         ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.cfg.heads, kv_heads=self.cfg.kv_heads,

@@ -1,0 +1,282 @@
+"""One pipeline stage of the Llama decoder on one tensor-parallel rank, with sequence parallelism.
+
+Layout (Megatron's, on this package's kernels): q/k/v and gate/up projections are column
+parallel (this rank holds ``heads / tp`` query heads, ``kv_heads / tp`` key/value heads and
+``ffn / tp`` FFN columns), ``wo`` and ``w2`` are row parallel; the residual stream between the
+projections is sharded by token rows (sequence parallel).  Per layer, ``T`` tokens of a
+micro-batch, ``T / tp`` of them on this rank:
+
+    h   = rmsnorm(x)                         (this rank's rows, written into the gather chunk)
+    qkv = AllGather(h) Wqkv_r^T              (all-gather -> GEMM)        rope(q, k)
+    o   = attention(q, k, v)                 (this rank's heads, full sequences)
+    x2  = x + ReduceScatter(o Wo_r^T)        (GEMM -> reduce-scatter, residual fused)
+    h2  = rmsnorm(x2);  gu = AllGather(h2) W13_r^T;  a = silu(gate) * up
+    x'  = x2 + ReduceScatter(a W2_r^T)
+
+The backward mirrors it: the gradient of a reduce-scatter is an all-gather feeding the dgrad GEMM
+of ``wo`` / ``w2`` (whose gathered input also feeds the weight gradient), the gradient of an
+all-gather is a reduce-scatter after the dgrad GEMM of ``wqkv`` / ``w13``, and the normalised
+inputs of the column-parallel weight gradients are recomputed and re-gathered.
+
+Parameters live in two flat sets: ``shd`` (tensor-parallel shards: wq, wk, wv, wo, w1, w3, w2)
+and ``rep`` (replicated on every TP rank: the norms, the embedding on the first stage, the final
+norm and LM head on the last).  With sequence parallelism every TP rank computes the replicated
+parameters' gradients from its own token rows, so ``rep`` is reduced over TP x DP and ``shd``
+over DP only.  Initialisation is layout invariant (each logical tensor is drawn from its own
+``(seed, name)`` stream and sliced), so every TP/PP/DP layout starts from the same model.
+
+Activations of every in-flight micro-batch live in a slot (allocated on first use, reused after
+the micro-batch's backward), so pipeline schedules with several micro-batches in flight do not
+allocate in steady state.  (Reference: the TP/SP stage of the CPU model,
+``resihp/runtime/reference_model.py:134-260``; the GPU model of the reference is Megatron-Core,
+``resihp/runtime/megatron_runtime.py:162``.)
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+from ..utils.intervals import even_split
+from .config import GPTConfig
+from .params import FlatParams, ParamSpec
+
+SHARDED = ("wq", "wk", "wv", "wo", "w1", "w3", "w2")
+
+
+def stage_param_specs(cfg: GPTConfig, layers, first: bool, last: bool, tp_rank: int,
+                      tp_size: int) -> tuple[list[ParamSpec], list[ParamSpec]]:
+    """``(replicated, sharded)`` parameter specs of a stage on TP rank ``tp_rank``."""
+    H, D, F = cfg.hidden, cfg.head_dim, cfg.ffn
+    if cfg.heads % tp_size or cfg.kv_heads % tp_size or F % tp_size:
+        raise ValueError(f"tp={tp_size} must divide heads ({cfg.heads}), kv heads ({cfg.kv_heads}) and ffn ({F})")
+    qh = even_split(cfg.heads, tp_size)[tp_rank]
+    kh = even_split(cfg.kv_heads, tp_size)[tp_rank]
+    fr = even_split(F, tp_size)[tp_rank]
+    nq, nk, nf = qh[1] - qh[0], kh[1] - kh[0], fr[1] - fr[0]
+    rep: list[ParamSpec] = []
+    shd: list[ParamSpec] = []
+    if first:
+        rep.append(ParamSpec("embed", (cfg.vocab_size, H)))
+    for l in layers:
+        p = f"layers.{l}."
+        rep.append(ParamSpec(p + "attn_norm", (H,), init="ones"))
+        rep.append(ParamSpec(p + "mlp_norm", (H,), init="ones"))
+        shd += [
+            ParamSpec(p + "wq", (nq * D, H), (cfg.heads * D, H), 0, (qh[0] * D, qh[1] * D)),
+            ParamSpec(p + "wk", (nk * D, H), (cfg.kv_heads * D, H), 0, (kh[0] * D, kh[1] * D)),
+            ParamSpec(p + "wv", (nk * D, H), (cfg.kv_heads * D, H), 0, (kh[0] * D, kh[1] * D)),
+            ParamSpec(p + "wo", (H, nq * D), (H, cfg.heads * D), 1, (qh[0] * D, qh[1] * D)),
+            ParamSpec(p + "w1", (nf, H), (F, H), 0, fr),
+            ParamSpec(p + "w3", (nf, H), (F, H), 0, fr),
+            ParamSpec(p + "w2", (H, nf), (H, F), 1, fr),
+        ]
+    if last:
+        rep.append(ParamSpec("final_norm", (H,), init="ones"))
+        rep.append(ParamSpec("lm_head", (cfg.vocab_size, H)))
+    return rep, shd
+
+
+class _Slot:
+    """Saved activations of one in-flight micro-batch."""
+
+    def __init__(self, stage: "TPStage"):
+        c, dev = stage.cfg, stage.device
+        T, Tl, H, L = stage.T, stage.Tl, c.hidden, len(stage.layer_ids)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.x = [torch.empty(Tl, H, **bf) for _ in range(L + 1)]
+        self.x2 = [torch.empty(Tl, H, **bf) for _ in range(L)]
+        self.rstd1 = [torch.empty(Tl, **f32) for _ in range(L)]
+        self.rstd2 = [torch.empty(Tl, **f32) for _ in range(L)]
+        self.qkv = [torch.empty(T, stage.qkv_cols, **bf) for _ in range(L)]
+        self.o = [torch.empty(T, stage.nq * c.head_dim, **bf) for _ in range(L)]
+        self.lse = [torch.empty(stage.mb, stage.nq, stage.S, **f32) for _ in range(L)]
+        self.gu = [torch.empty(T, 2 * stage.nf, **bf) for _ in range(L)]
+        self.ids: torch.Tensor | None = None
+        if stage.last:
+            self.hf = torch.empty(Tl, H, **bf)
+            self.rstd_f = torch.empty(Tl, **f32)
+            self.logits = torch.empty(Tl, c.vocab_size, **bf)
+
+
+class TPStage:
+    def __init__(self, cfg: GPTConfig, device, *, layers, first: bool, last: bool, tp, micro_batch: int = 1,
+                 seq_len: int | None = None, seed: int = 0, rep_shard: tuple[int, int] = (0, 1),
+                 shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None)):
+        """``tp``: the tensor-parallel backend (``parallel.tp_backend``); ``*_shard`` the
+        (rank, count) of the ZeRO-1 optimizer shard of each parameter set over its
+        data-parallel group; ``*_factories`` the (buffer, optimizer) factories of ``FlatParams``
+        (the fused data-parallel step's peer heap)."""
+        self.cfg, self.device = cfg, torch.device(device)
+        self.tp = tp
+        self.tp_rank, self.tp_size = tp.rank, tp.world
+        self.layer_ids = list(layers)
+        self.first, self.last = first, last
+        self.mb = micro_batch
+        self.S = seq_len or cfg.seq_len
+        self.T = self.mb * self.S
+        if self.T % self.tp_size:
+            raise ValueError(f"{self.T} tokens per micro-batch do not split over tp={self.tp_size}")
+        self.Tl = self.T // self.tp_size
+        self.nq, self.nk = cfg.heads // self.tp_size, cfg.kv_heads // self.tp_size
+        self.nf = cfg.ffn // self.tp_size
+        self.qkv_cols = (self.nq + 2 * self.nk) * cfg.head_dim
+        rep_specs, shd_specs = stage_param_specs(cfg, self.layer_ids, first, last, self.tp_rank, self.tp_size)
+        self.rep = FlatParams(rep_specs, self.device, shard_rank=rep_shard[0], shard_count=rep_shard[1],
+                              buffer_factory=rep_factories[0], opt_factory=rep_factories[1])
+        self.shd = FlatParams(shd_specs, self.device, shard_rank=shd_shard[0], shard_count=shd_shard[1],
+                              buffer_factory=shd_factories[0], opt_factory=shd_factories[1])
+        self.rep.initialize(seed, cfg.init_std)
+        self.shd.initialize(seed, cfg.init_std)
+        self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
+        for l in self.layer_ids:  # fused projection weights are views over consecutive tensors
+            self._check_adjacent(f"layers.{l}.", ("wq", "wk", "wv"))
+            self._check_adjacent(f"layers.{l}.", ("w1", "w3"))
+        bf = dict(dtype=torch.bfloat16, device=self.device)
+        T, Tl, H = self.T, self.Tl, cfg.hidden
+        self.ws_a = torch.empty(T, self.nf, **bf)
+        self.ws_da = torch.empty(T, self.nf, **bf)
+        self.ws_do = torch.empty(T, self.nq * cfg.head_dim, **bf)
+        self.ws_dqkv = torch.empty(T, self.qkv_cols, **bf)
+        self.ws_dh = torch.empty(Tl, H, **bf)
+        self.ws_dx = torch.empty(Tl, H, **bf)
+        self.ws_dx2 = torch.empty(Tl, H, **bf)
+        self.ws_rstd = torch.empty(Tl, dtype=torch.float32, device=self.device)
+        self.loss_acc = torch.zeros((), dtype=torch.float32, device=self.device)
+        self.slots: dict[object, _Slot] = {}
+        self.free: list[_Slot] = []
+
+    # ------------------------------------------------------------------ parameter views
+    def _check_adjacent(self, p: str, names) -> None:
+        P = self.shd
+        off = P.offsets[p + names[0]]
+        for n in names:
+            if P.offsets[p + n] != off:
+                raise ValueError(f"{p + n} does not follow {p + names[0]} in the flat buffer")
+            off += P.specs[p + n].numel
+
+    def _fused(self, buf: torch.Tensor, p: str, names, rows: int) -> torch.Tensor:
+        o = self.shd.offsets[p + names[0]]
+        return buf[o:o + rows * self.cfg.hidden].view(rows, self.cfg.hidden)
+
+    def wqkv(self, p: str, grad: bool = False) -> torch.Tensor:
+        return self._fused(self.shd.grad if grad else self.shd.bf16, p, ("wq", "wk", "wv"), self.qkv_cols)
+
+    def w13(self, p: str, grad: bool = False) -> torch.Tensor:
+        return self._fused(self.shd.grad if grad else self.shd.bf16, p, ("w1", "w3"), 2 * self.nf)
+
+    def param_sets(self) -> tuple[FlatParams, FlatParams]:
+        return self.rep, self.shd
+
+    # ------------------------------------------------------------------ slots
+    def _take(self, key) -> _Slot:
+        s = self.free.pop() if self.free else _Slot(self)
+        self.slots[key] = s
+        return s
+
+    def _release(self, key) -> None:
+        self.free.append(self.slots.pop(key))
+
+    def inflight(self) -> int:
+        return len(self.slots)
+
+    # ------------------------------------------------------------------ forward
+    def _rms(self, x, w, out, rstd):
+        return ops.rmsnorm_fwd(x, w, float(self.cfg.norm_eps), out=out, rstd=rstd)[0]
+
+    def _qkv_views(self, qkv: torch.Tensor):
+        D = self.cfg.head_dim
+        return (qkv[:, : self.nq * D], qkv[:, self.nq * D:(self.nq + self.nk) * D],
+                qkv[:, (self.nq + self.nk) * D:])
+
+    def forward(self, key, ids_local: torch.Tensor | None = None, x_in: torch.Tensor | None = None,
+                labels_local: torch.Tensor | None = None, grad_scale: float = 1.0) -> torch.Tensor | None:
+        """Forward of micro-batch ``key``: token ids of this rank's rows (first stage) or the
+        received ``[T / tp, H]`` activation; returns the stage output rows (kept until the
+        micro-batch's backward) or, on the last stage, None after adding the summed token loss
+        into ``loss_acc`` and leaving the logits' gradient in place."""
+        cfg, R, P = self.cfg, self.rep, self.shd
+        T, H, D = self.T, cfg.hidden, cfg.head_dim
+        slot = self._take(key)
+        if self.first:
+            slot.ids = ids_local
+            ops.embedding_fwd(ids_local, R.w("embed"), out=slot.x[0])
+        else:
+            slot.x[0] = x_in
+        for i, l in enumerate(self.layer_ids):
+            p = f"layers.{l}."
+            x = slot.x[i]
+            self._rms(x, R.w(p + "attn_norm"), self.tp.chunk(T, H), slot.rstd1[i])
+            self.tp.ag_gemm(T, self.wqkv(p), out=slot.qkv[i])
+            q, k, v = self._qkv_views(slot.qkv[i])
+            ops.rope_(q, self.nq, D, self.cos, self.sin, self.S)
+            ops.rope_(k, self.nk, D, self.cos, self.sin, self.S)
+            ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.nq, kv_heads=self.nk, head_dim=D,
+                              out=slot.o[i], lse=slot.lse[i])
+            self.tp.gemm_rs(slot.o[i], P.w(p + "wo"), out=slot.x2[i], residual=x)
+            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), slot.rstd2[i])
+            self.tp.ag_gemm(T, self.w13(p), out=slot.gu[i])
+            ops.swiglu_fwd(slot.gu[i], out=self.ws_a)
+            self.tp.gemm_rs(self.ws_a, P.w(p + "w2"), out=slot.x[i + 1], residual=slot.x2[i])
+        if not self.last:
+            return slot.x[-1]
+        self._rms(slot.x[-1], R.w("final_norm"), slot.hf, slot.rstd_f)
+        ops.gemm(slot.hf, R.w("lm_head"), out=slot.logits)
+        loss = ops.cross_entropy_(slot.logits, labels_local, grad_scale=grad_scale)
+        self.loss_acc += loss.sum()
+        return None
+
+    # ------------------------------------------------------------------ backward
+    def backward(self, key, dx_top: torch.Tensor | None = None) -> torch.Tensor | None:
+        """Backward of micro-batch ``key`` (after its forward); accumulates both parameter
+        sets' gradients and returns the gradient of the stage input rows (None on the first
+        stage)."""
+        cfg, R, P = self.cfg, self.rep, self.shd
+        T, H, D = self.T, cfg.hidden, cfg.head_dim
+        slot = self.slots[key]
+        dx = self.ws_dx
+        if self.last:
+            ops.gemm(slot.logits, R.w("lm_head"), b_t=True, out=self.ws_dh)
+            ops.gemm(slot.logits, slot.hf, a_t=True, b_t=True, out=R.g("lm_head"), accumulate=True)
+            ops.rmsnorm_bwd(slot.x[-1], R.w("final_norm"), slot.rstd_f, self.ws_dh, R.g("final_norm"), out=dx)
+        else:
+            dx.copy_(dx_top)
+        for i in reversed(range(len(self.layer_ids))):
+            l = self.layer_ids[i]
+            p = f"layers.{l}."
+            # MLP: the reduce-scatter's gradient is an all-gather feeding w2's dgrad and wgrad
+            self.tp.chunk(T, H).copy_(dx)
+            _, dy = self.tp.ag_gemm(T, P.w(p + "w2"), out=self.ws_da, w_t=True)
+            ops.swiglu_fwd(slot.gu[i], out=self.ws_a)
+            ops.gemm(dy, self.ws_a, a_t=True, b_t=True, out=P.g(p + "w2"), accumulate=True)
+            dgu = ops.swiglu_bwd(slot.gu[i], self.ws_da, out=slot.gu[i])
+            self.tp.gemm_rs(dgu, self.w13(p), out=self.ws_dh, w_t=True)
+            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), self.ws_rstd)
+            h2 = self.tp.all_gather(T, H)
+            ops.gemm(dgu, h2, a_t=True, b_t=True, out=self.w13(p, grad=True), accumulate=True)
+            ops.rmsnorm_bwd(slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.ws_dh, R.g(p + "mlp_norm"), dres=dx,
+                            out=self.ws_dx2)
+            dx2 = self.ws_dx2
+            # attention
+            self.tp.chunk(T, H).copy_(dx2)
+            _, dy = self.tp.ag_gemm(T, P.w(p + "wo"), out=self.ws_do, w_t=True)
+            ops.gemm(dy, slot.o[i], a_t=True, b_t=True, out=P.g(p + "wo"), accumulate=True)
+            q, k, v = self._qkv_views(slot.qkv[i])
+            dq, dk, dv = self._qkv_views(self.ws_dqkv)
+            ops.attention_bwd(q, k, v, slot.o[i], self.ws_do, slot.lse[i], dq, dk, dv, batch=self.mb, seq=self.S,
+                              heads=self.nq, kv_heads=self.nk, head_dim=D)
+            ops.rope_(dq, self.nq, D, self.cos, self.sin, self.S, inverse=True)
+            ops.rope_(dk, self.nk, D, self.cos, self.sin, self.S, inverse=True)
+            self.tp.gemm_rs(self.ws_dqkv, self.wqkv(p), out=self.ws_dh, w_t=True)
+            self._rms(slot.x[i], R.w(p + "attn_norm"), self.tp.chunk(T, H), self.ws_rstd)
+            h = self.tp.all_gather(T, H)
+            ops.gemm(self.ws_dqkv, h, a_t=True, b_t=True, out=self.wqkv(p, grad=True), accumulate=True)
+            ops.rmsnorm_bwd(slot.x[i], R.w(p + "attn_norm"), slot.rstd1[i], self.ws_dh, R.g(p + "attn_norm"),
+                            dres=dx2, out=dx)
+        if self.first:
+            ops.embedding_bwd(slot.ids, dx, R.g("embed"))
+            self._release(key)
+            return None
+        self._release(key)
+        return dx

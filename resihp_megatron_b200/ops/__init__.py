@@ -23,11 +23,13 @@ __all__ = [
 ]
 
 
-def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5, out: torch.Tensor | None = None):
-    """``y = x / rms(x) * w`` over the last dim; returns ``(y, rstd)``."""
+def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5, out: torch.Tensor | None = None,
+                rstd: torch.Tensor | None = None):
+    """``y = x / rms(x) * w`` over the last dim; returns ``(y, rstd)`` (``rstd``: fp32 per row)."""
     H = x.shape[-1]
     y = torch.empty_like(x) if out is None else out
-    rstd = torch.empty(x.numel() // H, dtype=torch.float32, device=x.device)
+    if rstd is None:
+        rstd = torch.empty(x.numel() // H, dtype=torch.float32, device=x.device)
     ext().rmsnorm_fwd(x, w, y, rstd, float(eps))
     count(1)
     return y, rstd

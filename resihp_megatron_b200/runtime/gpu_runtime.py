@@ -1,0 +1,252 @@
+"""One generation's hybrid-parallel data plane on GPUs: TP (+ sequence parallel) x PP x DP.
+
+Every rank runs one (replica, stage) slot of a ``HeteroParallelPlan``: a ``TPStage`` (its layer
+range, its TP shard) driven by the pipeline IR ``Interpreter`` with the planner's validated
+schedule; pipeline-boundary activations and gradients go over NCCL point to point (one 2-rank
+channel per direction, ``comm.p2p``); tensor-parallel collectives are fused into the GEMMs over
+NVLink peer memory (``tp_impl="fused"``) or run as NCCL collectives (``"collective"``, the
+baseline).  After the last backward each parameter set is reduced over its data-parallel group
+and updated by a sharded Adam: the tensor-parallel shards over the same TP rank of every
+replica, the replicated set (norms, embedding, LM head, whose gradients are per-TP-rank partial
+sums under sequence parallelism) over every rank of the stage -- the fused peer-memory step
+(``dp_impl="fused"``) or reduce-scatter / Adam / all-gather (``"collective"``).
+
+GPU stages need the same TP degree and layer range in every replica of a stage (the shard
+layouts of a data-parallel group must coincide); heterogeneous plans run on the CPU runtime.
+(Reference: ``resihp/runtime/hetero_runtime.py:33-148`` and ``resihp/runtime/dp_runtime.py``.)
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..comm.group_spec import GroupSpec
+from ..comm.p2p import P2PEngine
+from ..models.config import GPTConfig
+from ..plan.hetero_plan import HeteroParallelPlan, StageGroup, tp_group_name
+from ..plan.ir import Op, Schedule
+from .gpu_executor import GPUStageExecutor, TokenSource
+from .hetero_runtime import channel_map, channel_specs
+from .interpreter import Interpreter
+
+
+def shard_group_name(stage: int, tp_rank: int) -> str:
+    return f"dp/s{stage}/t{tp_rank}"
+
+
+def replicated_group_name(stage: int) -> str:
+    return f"dprep/s{stage}"
+
+
+def check_homogeneous(plan: HeteroParallelPlan) -> None:
+    for s in range(plan.num_stages):
+        gs = plan.groups_at(s)
+        if len({(g.tp, g.cp, g.layers) for g in gs}) != 1:
+            raise NotImplementedError(f"stage {s}: replicas differ in TP degree or layers; the GPU runtime needs "
+                                      f"identical shard layouts within a data-parallel group")
+        for g in gs:
+            if g.cp != 1:
+                raise NotImplementedError("context parallelism is not wired into the GPU runtime")
+            r = plan.ranks(g)
+            if list(r) != sorted(r):
+                raise NotImplementedError(f"group r{g.replica}/s{g.stage}: devices must be in rank order")
+    if plan.vpp != 1:
+        raise NotImplementedError("interleaved stages are not wired into the GPU runtime")
+
+
+def gpu_group_specs(plan: HeteroParallelPlan, schedule: Schedule, tokens_per_microbatch: int) -> list[GroupSpec]:
+    """TP groups, the two data-parallel groups of every stage and one channel per direction of
+    every pipeline-boundary rank pair."""
+    check_homogeneous(plan)
+    specs: dict[str, GroupSpec] = {}
+    for g in plan.stage_groups:
+        if g.tp > 1:
+            n = tp_group_name(g.replica, g.stage)
+            specs[n] = GroupSpec(n, plan.ranks(g), "tp")
+    for s in range(plan.num_stages):
+        gs = plan.groups_at(s)
+        for j in range(gs[0].tp):
+            n = shard_group_name(s, j)
+            specs[n] = GroupSpec(n, tuple(sorted(plan.ranks(g)[j] for g in gs)), "dp")
+        n = replicated_group_name(s)
+        specs[n] = GroupSpec(n, tuple(sorted(r for g in gs for r in plan.ranks(g))), "dp")
+    out = list(specs.values())
+    out += channel_specs(plan, schedule, tokens_per_microbatch, row_counts=[tokens_per_microbatch])
+    return out
+
+
+class ParamSetSync:
+    """Reduction over the data-parallel group + sharded Adam + weight gather of one flat
+    parameter set (``FlatParams``)."""
+
+    def __init__(self, ranks: tuple[int, ...], me: int, group, impl: str, device, *, abort=None,
+                 budget_s: float = 60.0, waiter=None):
+        self.size, self.index = len(ranks), ranks.index(me)
+        self.group = group
+        self.device = torch.device(device)
+        self.impl = "single" if self.size == 1 else impl
+        if self.impl not in ("single", "fused", "collective"):
+            raise ValueError(impl)
+        self.wait = waiter or (lambda work: work.wait())
+        self.fdp = None
+        if self.impl == "fused":
+            from ..parallel.dp_fused import FusedDataParallel
+            from ..parallel.symm import exchange_via_group
+
+            self.fdp = FusedDataParallel(self.index, self.size, exchange_via_group(group), self.device, abort=abort,
+                                         barrier_budget_s=budget_s, spare_bank=False)
+        self.P = None
+        self.grad_shard = None
+
+    @property
+    def shard(self) -> tuple[int, int]:
+        return (self.index, self.size)
+
+    @property
+    def factories(self):
+        return (self.fdp.buffer_factory, self.fdp.opt_factory) if self.fdp is not None else (None, None)
+
+    def attach(self, P) -> None:
+        self.P = P
+        if self.impl == "collective":
+            self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
+
+    def step(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+        P = self.P
+        P.step += 1
+        if self.impl == "fused":
+            self.fdp.step(P, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+            return
+        kw = dict(lr=lr, beta1=betas[0], beta2=betas[1], eps=eps, weight_decay=weight_decay, step=P.step)
+        if self.impl == "single":
+            ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, zero_grad=True, **kw)
+            return
+        self.wait(dist.reduce_scatter_tensor(self.grad_shard, P.grad, group=self.group, async_op=True))
+        P.grad.zero_()
+        mine = P.shard_slice(P.bf16)
+        ops.adam_step(P.master, self.grad_shard, P.exp_avg, P.exp_avg_sq, mine, zero_grad=False, **kw)
+        src = mine if dist.get_backend(self.group) == "nccl" else mine.clone()
+        self.wait(dist.all_gather_into_tensor(P.bf16, src, group=self.group, async_op=True))
+
+    def check(self) -> None:
+        if self.fdp is not None:
+            self.fdp.check()
+
+    def close(self) -> None:
+        if self.fdp is not None:
+            self.fdp.close()
+            self.fdp = None
+
+
+class GPUHybridRuntime:
+    def __init__(self, cfg: GPTConfig, plan: HeteroParallelPlan, schedule: Schedule, comms, mgr, *, device,
+                 micro_batch: int = 1, seq_len: int | None = None, tokens: TokenSource | None = None,
+                 tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0, lr: float = 3e-4,
+                 betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, budget_s: float = 60.0,
+                 progress=None, hook=None):
+        from ..models.tp_stage import TPStage
+
+        check_homogeneous(plan)
+        self.cfg, self.plan, self.comms, self.mgr = cfg, plan, comms, mgr
+        self.device = torch.device(device)
+        self.S = seq_len or cfg.seq_len
+        self.micro_batch = micro_batch
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        me = comms.world[comms.rank]
+        g: StageGroup = plan.group_of_device(me)
+        if g is None:
+            raise RuntimeError(f"{me} has no slot in generation {plan.generation} (standby)")
+        self.group, self.replica, self.stage_index = g, g.replica, g.stage
+        ranks = plan.ranks(g)
+        tp_rank = ranks.index(comms.rank)
+        T = micro_batch * self.S
+        self.tokens_per_step = plan.num_microbatches * T
+        waiter = (lambda w: mgr.guarded_wait(w, what="data-parallel collective")) if mgr is not None else None
+        self.abort = None
+        if "fused" in (tp_impl, dp_impl):
+            from ..parallel.symm import AbortWord
+
+            self.abort = AbortWord()
+            if mgr is not None:
+                mgr.add_abort_hook(self.abort.set)
+        # tensor parallelism
+        tp_pg = comms.group(tp_group_name(g.replica, g.stage)) if g.tp > 1 else None
+        from ..parallel import tp_backend
+
+        if g.tp == 1:
+            self.tp = tp_backend.SoloTP(self.device)
+        elif tp_impl == "fused":
+            from ..parallel.symm import exchange_via_group
+            from ..parallel.tp_fused import TensorParallelComm
+
+            comm = TensorParallelComm(tp_rank, g.tp, exchange_via_group(tp_pg), self.device, max_rows=T,
+                                      max_k=cfg.hidden, max_n=cfg.hidden, abort=self.abort, budget_s=budget_s)
+            self.tp = tp_backend.FusedTP(comm)
+        elif tp_impl == "collective":
+            self.tp = tp_backend.CollectiveTP(tp_rank, g.tp, tp_pg, self.device,
+                                              waiter=(lambda w: mgr.guarded_wait(w, what="tp collective"))
+                                              if mgr is not None else None)
+        else:
+            raise ValueError(tp_impl)
+        # data parallelism: the sharded set over the same TP rank of every replica, the
+        # replicated set over the whole stage
+        stage_groups = plan.groups_at(g.stage)
+        shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
+        rep_ranks = tuple(sorted(r for h in stage_groups for r in plan.ranks(h)))
+        self.shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(g.stage, tp_rank)),
+                                     dp_impl, self.device, abort=self.abort, budget_s=budget_s, waiter=waiter)
+        self.rep_sync = ParamSetSync(rep_ranks, comms.rank, comms.group(replicated_group_name(g.stage)), dp_impl,
+                                     self.device, abort=self.abort, budget_s=budget_s, waiter=waiter)
+        self.stage = TPStage(cfg, self.device, layers=range(*g.layers), first=g.stage == 0,
+                             last=g.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch,
+                             seq_len=self.S, seed=seed, rep_shard=self.rep_sync.shard, shd_shard=self.shd_sync.shard,
+                             rep_factories=self.rep_sync.factories, shd_factories=self.shd_sync.factories)
+        self.rep_sync.attach(self.stage.rep)
+        self.shd_sync.attach(self.stage.shd)
+        self.tokens = tokens or TokenSource(cfg.vocab_size, micro_batch, self.S)
+        self.executor = GPUStageExecutor(self.stage, plan, g.replica, g.stage, comms.rank, self.tokens,
+                                         grad_scale=1.0 / self.tokens_per_step)
+        stream = schedule[(g.replica, g.stage)]
+        if any(ins.op == Op.W for ins in stream):
+            raise NotImplementedError("zero-bubble (B/W split) schedules are not wired into the GPU stage")
+        p2p = P2PEngine(comms.rank, mgr, channels=channel_map(comms), device=str(self.device))
+        self.interp = Interpreter(plan, stream, self.executor, p2p, g.replica, g.stage, (cfg.hidden,), torch.bfloat16,
+                                  tp_group=tp_pg, progress=progress, hook=hook)
+        self.iteration = 0
+
+    def run_iteration(self, iteration: int | None = None) -> torch.Tensor:
+        """One training step of this slot; returns the global mean token loss as a 0-d device
+        tensor (no host synchronisation)."""
+        it = self.iteration if iteration is None else iteration
+        self.interp.run(it)
+        kw = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)
+        self.shd_sync.step(**kw)
+        self.rep_sync.step(**kw)
+        loss = self.stage.loss_acc.clone()
+        work = dist.all_reduce(loss, async_op=True)
+        if self.mgr is not None:
+            self.mgr.guarded_wait(work, what="loss all-reduce")
+        else:
+            work.wait()
+        self.iteration = it + 1
+        return loss / self.tokens_per_step
+
+    def check(self) -> None:
+        """Raise if a peer barrier of a fused collective timed out or was aborted."""
+        for s in (self.shd_sync, self.rep_sync):
+            s.check()
+        if hasattr(self.tp, "check"):
+            self.tp.check()
+
+    def close(self) -> None:
+        """Release the symmetric heaps (before the process groups are destroyed)."""
+        if torch.cuda.is_available() and self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        for s in (self.shd_sync, self.rep_sync):
+            s.close()
+        self.tp.close()
+        if self.abort is not None:
+            self.abort.close()
+            self.abort = None

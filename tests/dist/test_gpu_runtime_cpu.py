@@ -1,0 +1,102 @@
+"""Orchestration of the GPU hybrid-parallel runtime (TP2 x PP2 x DP2 with sequence parallelism)
+on 8 gloo ranks, with PyTorch stand-ins for the kernels (``tests/helpers/fake_kernels``):
+data-parallel-reduced gradients of every logical tensor and the per-step losses must match the
+same model trained on one rank (tp=1, one stage)."""
+
+import pytest
+import torch
+
+from tests.dist_utils import spawn
+
+pytestmark = pytest.mark.dist
+
+MB, S, MICRO = 2, 8, 4
+
+
+def _cfg():
+    from resihp_megatron_b200.models.config import GPTConfig
+
+    return GPTConfig(name="t", vocab_size=64, hidden=64, layers=4, heads=4, kv_heads=2, ffn=128, seq_len=S)
+
+
+def _plan(layout, ids):
+    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup
+
+    if layout == "tp2pp2dp2":
+        groups = (StageGroup(0, 0, ids[0:2], (0, 2)), StageGroup(0, 1, ids[2:4], (2, 4)),
+                  StageGroup(1, 0, ids[4:6], (0, 2)), StageGroup(1, 1, ids[6:8], (2, 4)))
+        plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)), sequence_parallel=True)
+    else:
+        groups = (StageGroup(0, 0, ids[0:1], (0, 4)),)
+        plan = HeteroParallelPlan(1, ids, 4, 1, 1, groups, MICRO, ((0, 0, 0, 0),), sequence_parallel=True)
+    plan.validate()
+    return plan
+
+
+def _worker(rank, world, port, store_addr, layout, iters):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.comm.comm_manager import ResilientCommManager
+    from resihp_megatron_b200.plan.ir import compute_order_to_ir, validate
+    from resihp_megatron_b200.plan.simulator import schedule_with_fallback
+    from resihp_megatron_b200.runtime.gpu_runtime import GPUHybridRuntime, gpu_group_specs
+
+    cfg = _cfg()
+    ids = tuple(f"w{i}" for i in range(world))
+    plan = _plan(layout, ids)
+    res = schedule_with_fallback(plan, lambda k, op, mb: 1.0 if op == "F" else 2.0, lambda a, b, kind: 0.1)
+    schedule = compute_order_to_ir(plan, res.order)
+    validate(plan, schedule)
+    specs = gpu_group_specs(plan, schedule, MB * S)
+    mgr = ResilientCommManager("gloo", timeout_s=60)
+    comms = mgr.build(1, list(ids), ids[rank], specs, store_addr=store_addr, store_prefix=f"{layout}/gen1/")
+    rt = GPUHybridRuntime(cfg, plan, schedule, comms, mgr, device="cpu", micro_batch=MB, seq_len=S,
+                          tp_impl="collective", dp_impl="collective", lr=1e-2)
+    # iteration 0's gradients before any update, reduced over each set's data-parallel group
+    rt.interp.run(0)
+    grads = {}
+    for P, sync in ((rt.stage.rep, rt.rep_sync), (rt.stage.shd, rt.shd_sync)):
+        total = P.grad.clone()
+        if sync.size > 1:
+            dist.all_reduce(total, group=sync.group)
+        for name in P.order:
+            s, o = P.specs[name], P.offsets[name]
+            grads[name] = (total[o:o + s.numel].view(s.shape).clone(), s.full_shape or s.shape, s.shard_dim,
+                           s.shard_range)
+        P.grad.zero_()
+    losses = [float(rt.run_iteration(it)) for it in range(iters)]
+    out = {"grads": grads, "losses": losses, "inflight": rt.stage.inflight(), "slots": len(rt.stage.free)}
+    rt.close()
+    mgr.destroy()
+    return out
+
+
+def _assemble(results):
+    full = {}
+    for res in results.values():
+        for name, (g, shape, dim, rng) in res["grads"].items():
+            if dim is None:
+                full.setdefault(name, g)
+                continue
+            t = full.setdefault(name, torch.zeros(shape))
+            t.narrow(dim, rng[0], rng[1] - rng[0]).copy_(g)
+    return full
+
+
+def test_tp2_pp2_dp2_sequence_parallel_matches_single_rank(store):
+    one = spawn(_worker, 1, store, "single", 2, timeout=240)
+    many = spawn(_worker, 8, store, "tp2pp2dp2", 2, timeout=300)
+    ref, got = _assemble(one), _assemble(many)
+    assert set(ref) == set(got)
+    for name in ref:
+        err = (got[name] - ref[name]).abs().max().item()
+        scale = ref[name].abs().max().item() + 1e-12
+        assert err <= 3e-2 * scale, (name, err, scale)
+    ref_losses = one[0]["losses"]
+    for r, res in many.items():
+        assert res["inflight"] == 0  # every micro-batch's slot was released after its backward
+        for a, b in zip(res["losses"], ref_losses):
+            assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], ref_losses)
