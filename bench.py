@@ -61,7 +61,19 @@ def _args():
                          "and the eviction-to-commit time)")
     ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
                     help="N > 1: fused NVLink reduction + Adam + gather kernel, or NCCL reduce-scatter/all-gather")
+    ap.add_argument("--parallelism", default="dp",
+                    help="'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' with T*P*D = N: tensor (+ sequence) x "
+                         "pipeline x data parallelism through the plan-driven runtime (BASELINE config 2: tp2pp2dp2)")
+    ap.add_argument("--tp-impl", choices=["fused", "collective"], default="fused",
+                    help="with --parallelism tp..: TP collectives fused into the GEMMs over NVLink, or NCCL")
     return ap.parse_args()
+
+
+def parse_layout(text: str) -> tuple[int, int, int] | None:
+    import re
+
+    m = re.fullmatch(r"tp(\d+)pp(\d+)dp(\d+)", text)
+    return None if m is None else tuple(int(x) for x in m.groups())
 
 
 def reference_unavailable(args) -> None:
@@ -150,6 +162,9 @@ def main() -> None:
     rank, world, local = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.parallelism != "dp":
+        run_hybrid(args, rank, world, local)
+        return
     cfg = get_config(args.model, seq_len=args.seq)
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
@@ -311,6 +326,96 @@ def main() -> None:
             trainer.close()
             dist.barrier()
         dist.destroy_process_group()
+
+
+def run_hybrid(args, rank: int, world: int, local: int) -> None:
+    """TP x PP x DP step through ``GPUHybridTrainer`` (same metric, timing and JSON line)."""
+    import torch
+    import torch.distributed as dist
+
+    from resihp_megatron_b200 import ops
+    from resihp_megatron_b200.models.config import get_config
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer, ensure_process_group
+
+    layout = parse_layout(args.parallelism)
+    if layout is None or layout[0] * layout[1] * layout[2] != world:
+        raise SystemExit(f"--parallelism {args.parallelism!r} is not tp{{T}}pp{{P}}dp{{D}} with T*P*D = {world}")
+    tp, pp, dp = layout
+    ensure_process_group(torch.device("cuda", local))
+    cfg = get_config(args.model, seq_len=args.seq)
+    if args.layers:
+        cfg = cfg.with_(layers=args.layers)
+    global_batch = args.seqs_per_gpu * world
+    mb = args.micro_batch or 1
+    trainer = GPUHybridTrainer(cfg, tp=tp, pp=pp, dp=dp, global_batch=global_batch, micro_batch=mb,
+                               seq_len=args.seq, tp_impl=args.tp_impl,
+                               dp_impl="fused" if args.dp_impl == "fused" else "collective")
+    for _ in range(args.warmup):
+        trainer.step_device()
+    torch.cuda.synchronize()
+    trainer.check()
+    sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    l0 = ops.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    loss = None
+    for _ in range(args.steps):
+        loss = trainer.step_device()
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches = ops.launches() - l0
+    clocks = sampler.stop() if sampler else None
+    trainer.check()
+    t = torch.tensor([start.elapsed_time(end)], device=trainer.device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = trainer.tokens_per_step * args.steps
+    value = tokens / (ms_max / 1000.0)
+    last_loss = float(loss.item())
+    # end to end through the public API: host tokens copied in by the consuming ranks, loss read back
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    h2d = 0
+    for _ in range(args.steps):
+        trainer.train_step()
+        h2d += trainer.h2d_bytes_last_step
+    torch.cuda.synchronize()
+    te = torch.tensor([time.perf_counter() - t0, h2d / args.steps], device=trainer.device, dtype=torch.float64)
+    dist.all_reduce(te[:1], op=dist.ReduceOp.MAX)
+    hb = te[1:].clone()
+    dist.all_reduce(hb)
+    e2e_value = tokens / float(te[0].item())
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None, "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
+            "config": {
+                "model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
+                "global_batch": global_batch, "seq_len": args.seq, "micro_batch": mb,
+                "parallelism": trainer.layout,
+                "layers_per_stage": [b - a for a, b in trainer.plan.layer_partition()],
+                "l2": "inputs larger than L2 (each step touches > 10 GB of weights/grads/optimizer state per GPU)",
+                "params": cfg.num_params(),
+                "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * value / world / 1e12,
+            },
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(hb.item()),
+                    "d2h_bytes_per_step": 4 * world},
+            "gpu_launches": launches, "loss": last_loss, "impl": "ours",
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    trainer.close()
+    dist.barrier()
 
 
 if __name__ == "__main__":

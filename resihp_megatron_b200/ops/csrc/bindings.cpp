@@ -420,14 +420,16 @@ void symm_copy(const std::vector<int64_t>& triples, int64_t device) {
 void tp_ag_gemm(const torch::Tensor& x_full, const std::vector<int64_t>& src_ptrs, int64_t self, const torch::Tensor& w,
                 bool w_t, torch::Tensor& y, torch::Tensor& ready, int64_t abort_dev) {
   CHECK_BF16(x_full); CHECK_BF16(w); CHECK_BF16(y);
-  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == torch::kInt32 && ready.numel() >= (int64_t)src_ptrs.size());
   const int world = static_cast<int>(src_ptrs.size());
   const int M = x_full.size(0), K = x_full.size(1), N = w_t ? w.size(1) : w.size(0);
   TORCH_CHECK((w_t ? w.size(0) : w.size(1)) == K && y.size(0) == M && y.size(1) == N, "tp_ag_gemm: shapes");
+  const int words = rb::gemm_ag_ready_words(M, K);
+  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == torch::kInt32 && ready.numel() >= words,
+              "tp_ag_gemm: `ready` needs ", words, " int32 words");
   std::vector<const void*> src(world);
   for (int c = 0; c < world; ++c) src[c] = reinterpret_cast<const void*>(src_ptrs[c]);
   const c10::cuda::CUDAGuard g(x_full.device());
-  cudaMemsetAsync(ready.data_ptr(), 0, world * sizeof(int), cur_stream());
+  cudaMemsetAsync(ready.data_ptr(), 0, words * sizeof(int), cur_stream());
   RB_CALL(rb::gemm_ag_bf16(x_full.data_ptr(), src.data(), world, static_cast<int>(self), M / world, w.data_ptr(),
                            w_t, y.data_ptr(), M, N, K, ready.data_ptr<int>(), reinterpret_cast<const int*>(abort_dev),
                            err_ptr(x_full), num_sms(x_full.get_device()), cur_stream()), "tp_ag_gemm");
@@ -546,6 +548,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"),
         py::arg("impl") = 0);
+  m.def("tp_ag_ready_words", [](int64_t M, int64_t K) { return rb::gemm_ag_ready_words(M, K); });
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

@@ -30,6 +30,7 @@ namespace rb {
 enum : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiBF16Res = 3, kEpiScatterBF16 = 4 };
 
 constexpr int kMaxTP = 8;
+constexpr int kAgSegCols = 512;  // columns per all-gather copy unit (a multiple of the 64-column k-block)
 
 struct GemmArgs {
   int M, N, K;
@@ -45,9 +46,9 @@ struct GemmArgs {
   void* rs_dst[kMaxTP];
   // all-gather -> GEMM: A's rows come in `ag_world` chunks of `ag_chunk_rows`; this rank owns
   // chunk `ag_self` (already in place in `ag_dst`); the kernel's copy warps pull the other chunks
-  // from `ag_src[c]` into `ag_dst` and count finished slices in `ag_ready[c]`.
-  int ag_world, ag_self, ag_chunk_rows;
-  long long ag_chunk_bytes;
+  // from `ag_src[c]` into `ag_dst` in units of 128 rows x `ag_kseg` columns, taken from the work
+  // counter `ag_ready[0]`, and publish each finished unit in its flag `ag_ready[1 + unit]`.
+  int ag_world, ag_self, ag_chunk_rows, ag_kseg;
   const void* ag_src[kMaxTP];
   void* ag_dst;
   int* ag_ready;
@@ -396,20 +397,26 @@ __global__ void __launch_bounds__(192, 1)
 
 // ---------------------------------------------------------------------------- all-gather -> GEMM
 // Column-parallel layer with sequence-parallel input: Y = AllGather_rows(X) @ W^T in one
-// cooperative persistent launch.  Warps 0-5 are the GEMM above (K-major A and B, 128 x 256
-// tiles); warps 6-9 pull the other ranks' row chunks of X over NVLink into this rank's gather
-// buffer (16-byte peer loads, every CTA a slice of every chunk, in the rotated order
-// self+1, self+2, ...) and count finished slices per chunk.  Tiles are visited in the same
-// rotated chunk order starting with this rank's own chunk, so the MMAs of chunk c overlap the
-// transfer of chunk c+1; the TMA producer waits (bounded, acquire + proxy fence) until every CTA
-// finished its slice of a chunk before loading its rows.  All CTAs are co-resident (cooperative
-// launch, one per SM), so these waits between CTAs of the launch always make progress; the
-// launch never waits on another kernel.  The caller orders the launch after the peers wrote their
-// chunks (a bounded cross-GPU barrier) and before they overwrite them.
+// persistent launch.  Warps 0-5 are the GEMM above (128 x 256 tiles); warps 6-9 pull the other
+// ranks' row chunks of X over NVLink into this rank's gather buffer (16-byte peer loads).  The
+// remote rows are cut into units of 128 rows x `ag_kseg` columns, enumerated chunk by chunk in
+// the rotated order self+1, self+2, ...; each CTA's copy warps take the next unit from a global
+// work counter, copy it and publish it with a release flag.  Tiles are visited in the same
+// rotated order starting with this rank's own chunk, so the MMAs of early chunks overlap the
+// transfer of later ones; before loading A's k-block the TMA producer waits (bounded, acquire +
+// proxy fence) for the flag of the unit holding it.  A unit is only ever awaited after some
+// running CTA claimed it or while unclaimed units remain for the copy warps of running CTAs, so
+// the waits make progress however many CTAs are resident: the launch is an ordinary one and may
+// share the GPU with other kernels (NCCL's included).  The caller orders the launch after the
+// peers wrote their chunks (a bounded cross-GPU barrier) and before they overwrite them.
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -433,6 +440,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* unit_slot = reinterpret_cast<int*>(tmem_slot + 2);  // copy warps: the unit being copied
   auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
   auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
   auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
@@ -472,6 +480,7 @@ __global__ void __launch_bounds__(320, 1)
   const int kblocks = (p.K + BK - 1) / BK;
   const int mb_per_chunk = p.ag_chunk_rows / BM;
   const int rot = p.ag_self * mb_per_chunk;  // visit this rank's own chunk first
+  const int nseg = (p.K + p.ag_kseg - 1) / p.ag_kseg;
   auto coords = [&](int tile, int& mb, int& nb) {
     tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
     mb = (mb + rot) % num_m;
@@ -481,33 +490,34 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0, issued_parity = 0;
-      unsigned ready_mask = 1u << p.ag_self;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok && !*abort_flag; tile += gridDim.x) {
         int mb, nb;
         coords(tile, mb, nb);
-        const int chunk = mb / mb_per_chunk;
-        if (!(ready_mask & (1u << chunk))) {
-          const uint64_t t0 = globaltimer();
-          bool ok = true;
-          while (ld_acquire_gpu(p.ag_ready + chunk) < static_cast<int>(gridDim.x)) {
-            if (*abort_flag || (p.abort_word != nullptr && *reinterpret_cast<const volatile int*>(p.abort_word))) {
-              ok = false;
-              break;
-            }
-            if (globaltimer() - t0 > kWaitBudgetNs) {
-              *abort_flag = 1;
-              record_error(p.err, kErrPeerTimeout);
-              ok = false;
-              break;
-            }
-            __nanosleep(64);
-          }
-          if (!ok) break;
-          fence_proxy_async_global();  // generic-proxy writes of the copy warps -> TMA reads
-          ready_mask |= 1u << chunk;
-        }
-        bool ok = true;
+        const bool remote = mb / mb_per_chunk != p.ag_self;
+        int seg_ready = remote ? -1 : nseg;  // k-segments of this row block known to be in place
         for (int kb = 0; kb < kblocks; ++kb) {
+          const int seg = kb * BK / p.ag_kseg;
+          if (seg > seg_ready) {
+            const int* flag = p.ag_ready + 1 + mb * nseg + seg;
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_gpu(flag) == 0) {
+              if (*abort_flag || (p.abort_word != nullptr && *reinterpret_cast<const volatile int*>(p.abort_word))) {
+                ok = false;
+                break;
+              }
+              if (globaltimer() - t0 > kWaitBudgetNs) {
+                *abort_flag = 1;
+                record_error(p.err, kErrPeerTimeout);
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (!ok) break;
+            fence_proxy_async_global();  // generic-proxy writes of the copy warps -> TMA reads
+            seg_ready = seg;
+          }
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
             ok = false;
             break;
@@ -529,8 +539,8 @@ __global__ void __launch_bounds__(320, 1)
             phase ^= 1;
           }
         }
-        if (!ok) break;
       }
+      if (!ok) *abort_flag = 1;
       for (int s = 0; s < STAGES; ++s)
         if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
     }
@@ -601,26 +611,47 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // ------------------------------------------------------------ copy warps 6..9
     const int t = threadIdx.x - 192;  // 0..127
-    const long long units = p.ag_chunk_bytes / 16;
-    const long long per = (units + gridDim.x - 1) / gridDim.x;
-    const long long lo = per * blockIdx.x;
-    const long long hi = lo + per < units ? lo + per : units;
-    for (int k = 1; k < p.ag_world; ++k) {
-      const int c = (p.ag_self + k) % p.ag_world;
+    const int remote_blocks = (p.ag_world - 1) * mb_per_chunk;
+    const int units = remote_blocks * nseg;
+    for (;;) {
+      if (t == 0) *unit_slot = atomicAdd(p.ag_ready, 1);
+      named_bar_sync(1, 128);
+      const int u = *unit_slot;
+      named_bar_sync(1, 128);  // every copy thread read the unit before it is replaced
+      if (u >= units) break;
+      const int rb = u / nseg, seg = u - rb * nseg;
+      const int c = (p.ag_self + 1 + rb / mb_per_chunk) % p.ag_world;
+      const int mb = c * mb_per_chunk + rb % mb_per_chunk;
+      const int row0 = mb * BM - c * p.ag_chunk_rows;  // first row of the unit within chunk c
+      const int col0 = seg * p.ag_kseg;
+      const int gpr = (min(p.K - col0, p.ag_kseg)) / 8;  // 16-byte granules per row of the unit
+      const int total = BM * gpr;
       const uint4* src = reinterpret_cast<const uint4*>(p.ag_src[c]);
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.ag_dst) + c * p.ag_chunk_bytes);
-      for (long long i = lo + t; i < hi; i += 128 * 4) {
-        uint4 v[4];
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.ag_dst) +
+                                            static_cast<long long>(c) * p.ag_chunk_rows * p.K * 2);
+      const long long ld16 = p.K / 8;  // granules per row of the matrix
+      for (int i = t; i < total; i += 128 * 8) {
+        uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (i + u * 128 < hi) v[u] = __ldcv(src + i + u * 128);
+        for (int w = 0; w < 8; ++w) {
+          const int g = i + w * 128;
+          if (g < total) {
+            const int r = g / gpr, q = g - r * gpr;
+            v[w] = __ldcv(src + (row0 + r) * ld16 + col0 / 8 + q);
+          }
+        }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (i + u * 128 < hi) dst[i + u * 128] = v[u];
+        for (int w = 0; w < 8; ++w) {
+          const int g = i + w * 128;
+          if (g < total) {
+            const int r = g / gpr, q = g - r * gpr;
+            dst[(row0 + r) * ld16 + col0 / 8 + q] = v[w];
+          }
+        }
       }
       __threadfence();
       named_bar_sync(1, 128);
-      if (t == 0) atomicAdd(p.ag_ready + c, 1);
+      if (t == 0) st_release_gpu(p.ag_ready + 1 + mb * nseg + seg, 1);
     }
   }
 
@@ -957,6 +988,8 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
   if (world < 1 || world > kMaxTP || chunk_rows % 128 || M != chunk_rows * world || K % 8 || N % 8) return -3;
   if ((reinterpret_cast<uintptr_t>(x_full) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(Y)) & 15)
     return -4;
+  for (int c = 0; c < world; ++c)
+    if (reinterpret_cast<uintptr_t>(x_src[c]) & 15) return -4;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_bf16_2d(&ta, x_full, K, M, K, 64, 128)) return -100 - rc;
   // W is [N, K] (K-major) or, with w_mn, [K, N] (B(n, k) = W[k * N + n])
@@ -964,8 +997,7 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
     return -100 - rc;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.D = Y; a.ldd = N; a.alpha = 1.f; a.err = err;
-  a.ag_world = world; a.ag_self = self; a.ag_chunk_rows = chunk_rows;
-  a.ag_chunk_bytes = static_cast<long long>(chunk_rows) * K * 2;
+  a.ag_world = world; a.ag_self = self; a.ag_chunk_rows = chunk_rows; a.ag_kseg = kAgSegCols;
   for (int c = 0; c < world; ++c) a.ag_src[c] = x_src[c];
   a.ag_dst = const_cast<void*>(x_full);
   a.ag_ready = ready;
@@ -978,18 +1010,11 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
     if (e != cudaSuccess) return static_cast<int>(e);
     attr[w_mn] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms);
-  cfg.blockDim = dim3(320);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeCooperative;
-  attrs[0].val.cooperative = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+  kern<<<num_sms, 320, C::SMEM_BYTES, stream>>>(ta, tb, a);
+  return static_cast<int>(cudaGetLastError());
 }
+
+int gemm_ag_ready_words(int M, int K) { return 1 + (M / 128) * ((K + kAgSegCols - 1) / kAgSegCols); }
 
 // Partial products of a row-parallel layer, scattered for a reduce-scatter: rows
 // [q * (M / world), (q + 1) * (M / world)) of X[M, K] @ W[N, K]^T are stored (bf16) into

@@ -101,6 +101,8 @@ int moe_grad_pull(const void* dout, const float* gates, const float* dgate, cons
 int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
                  bool w_mn, void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,
                  cudaStream_t stream);
+// Words of the `ready` buffer of gemm_ag_bf16 (a work counter and one flag per copy unit).
+int gemm_ag_ready_words(int M, int K);
 int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* recv, int world, int slot, int M, int N,
                          int K, int* err, int num_sms, cudaStream_t stream);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.

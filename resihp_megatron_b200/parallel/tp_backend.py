@@ -6,7 +6,7 @@ all-gathered, after every row-parallel GEMM the partial products are reduce-scat
 the row shards.  Three implementations:
 
 * ``FusedTP`` -- the collectives fused into the GEMMs on symmetric NVLink peer memory
-  (``TensorParallelComm``: one cooperative all-gather -> GEMM kernel; a GEMM whose epilogue stores
+  (``TensorParallelComm``: one persistent all-gather -> GEMM kernel; a GEMM whose epilogue stores
   the partial tiles into their owners' receive slots, then a rank-ordered reduce);
 * ``CollectiveTP`` -- ``torch.distributed`` all-gather / reduce-scatter around the same GEMM
   kernel (NCCL on GPUs, gloo on CPU): the baseline the fused path is measured against;

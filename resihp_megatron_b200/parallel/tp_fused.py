@@ -3,8 +3,9 @@
 * ``all_gather_gemm`` -- column-parallel layer with sequence-parallel input:
   ``Y[M, N_local] = AllGather_rows(X)[M, K] @ W_local[N_local, K]^T``.  Each rank writes its
   ``[M / tp, K]`` token shard into its own chunk of a heap-resident gather buffer; after a bounded
-  barrier one cooperative kernel pulls the peers' chunks over NVLink with dedicated copy warps
-  while its MMA warps already multiply the chunks that have landed (own chunk first).
+  barrier one persistent kernel pulls the peers' chunks over NVLink with dedicated copy warps
+  (128-row x 512-column units claimed from a work counter, each published by a flag) while its
+  MMA warps already multiply the units that have landed (own chunk first).
   Replaces reference call site C2 (``resihp/runtime/reference_model.py:173-181``: all-gather then
   ``F.linear``).
 * ``gemm_reduce_scatter`` -- row-parallel layer with sequence-parallel output:
@@ -41,7 +42,8 @@ class TensorParallelComm:
         self.budget = budget_s
         self.heap = _heap or SymmetricHeap(self.segments(world, max_rows, max_k, max_n), rank, world, exchange,
                                            device, abort)
-        self.ready = torch.zeros(world, dtype=torch.int32, device=device)
+        # work counter + one flag per copy unit of the all-gather -> GEMM kernel
+        self.ready = torch.zeros(1 + (max_rows // 128) * (-(-max_k // 512)), dtype=torch.int32, device=device)
         self.emulated = _heap is not None
         self._ag = 0
         self._rs = 0

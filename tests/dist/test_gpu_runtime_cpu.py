@@ -100,3 +100,34 @@ def test_tp2_pp2_dp2_sequence_parallel_matches_single_rank(store):
         assert res["inflight"] == 0  # every micro-batch's slot was released after its backward
         for a, b in zip(res["losses"], ref_losses):
             assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], ref_losses)
+
+
+def _trainer(rank, world, port, layout):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tp, pp, dp = layout
+    tr = GPUHybridTrainer(_cfg(), tp=tp, pp=pp, dp=dp, global_batch=4, micro_batch=1, seq_len=S,
+                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2)
+    losses = [tr.train_step() for _ in range(2)]
+    out = {"losses": losses, "parts": tr.plan.layer_partition(), "h2d": tr.h2d_bytes_last_step}
+    tr.close()
+    dist.destroy_process_group()
+    return out
+
+
+def test_hybrid_trainer_plans_its_layout_and_matches_one_rank():
+    one = spawn(_trainer, 1, (1, 1, 1), timeout=240)
+    many = spawn(_trainer, 4, (2, 2, 1), timeout=300)
+    ref = one[0]["losses"]
+    assert many[0]["parts"][0][0] == 0 and many[0]["parts"][-1][1] == 4
+    for r, res in many.items():
+        for a, b in zip(res["losses"], ref):
+            assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], ref)
+    # token rows are copied by the first (ids) and last (labels) stage ranks only
+    assert sum(res["h2d"] for res in many.values()) == one[0]["h2d"]
