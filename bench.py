@@ -392,6 +392,33 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
     hb = te[1:].clone()
     dist.all_reduce(hb)
     e2e_value = tokens / float(te[0].item())
+    # optional live reconfiguration: the last rank leaves; the planner re-plans the survivors
+    # (TP shrink or eviction of its group, min-max layer repartition) and state migrates slice by slice
+    recfg, alive = None, True
+    if args.reconfig:
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        alive = trainer.reconfigure([world - 1])
+        commit_s = time.perf_counter() - t0
+        if alive:
+            for _ in range(max(2, min(args.warmup, 3))):
+                trainer.step_device()
+            torch.cuda.synchronize()
+            trainer.check()
+            dist.barrier()
+            start.record()
+            for _ in range(args.steps):
+                loss2 = trainer.step_device()
+            end.record()
+            torch.cuda.synchronize()
+            vals = torch.tensor([start.elapsed_time(end), commit_s], device=trainer.device, dtype=torch.float64)
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+            post_ms, commit_max = vals.tolist()
+            recfg = {"kind": "planned eviction of the last rank; re-planned layout, slice-level state migration",
+                     "n_gpus_post": dist.get_world_size(), "post_value": tokens / (post_ms / 1000),
+                     "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
+                     "post_loss": float(loss2.item()), "phases_s_rank0": trainer.last_reconfig}
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -412,7 +439,11 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
                     "d2h_bytes_per_step": 4 * world},
             "gpu_launches": launches, "loss": last_loss, "impl": "ours",
         }
+        if recfg is not None:
+            out["reconfig"] = recfg
         print(json.dumps(out), flush=True)
+    if not alive:
+        return
     dist.barrier()
     trainer.close()
     dist.barrier()

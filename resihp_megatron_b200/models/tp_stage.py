@@ -103,11 +103,12 @@ class _Slot:
 class TPStage:
     def __init__(self, cfg: GPTConfig, device, *, layers, first: bool, last: bool, tp, micro_batch: int = 1,
                  seq_len: int | None = None, seed: int = 0, rep_shard: tuple[int, int] = (0, 1),
-                 shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None)):
+                 shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None),
+                 init: bool = True):
         """``tp``: the tensor-parallel backend (``parallel.tp_backend``); ``*_shard`` the
         (rank, count) of the ZeRO-1 optimizer shard of each parameter set over its
         data-parallel group; ``*_factories`` the (buffer, optimizer) factories of ``FlatParams``
-        (the fused data-parallel step's peer heap)."""
+        (the fused data-parallel step's peer heap); ``init`` draws the initial weights."""
         self.cfg, self.device = cfg, torch.device(device)
         self.tp = tp
         self.tp_rank, self.tp_size = tp.rank, tp.world
@@ -127,8 +128,9 @@ class TPStage:
                               buffer_factory=rep_factories[0], opt_factory=rep_factories[1])
         self.shd = FlatParams(shd_specs, self.device, shard_rank=shd_shard[0], shard_count=shd_shard[1],
                               buffer_factory=shd_factories[0], opt_factory=shd_factories[1])
-        self.rep.initialize(seed, cfg.init_std)
-        self.shd.initialize(seed, cfg.init_std)
+        if init:  # else a migrated state is loaded next
+            self.rep.initialize(seed, cfg.init_std)
+            self.shd.initialize(seed, cfg.init_std)
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
         for l in self.layer_ids:  # fused projection weights are views over consecutive tensors
             self._check_adjacent(f"layers.{l}.", ("wq", "wk", "wv"))

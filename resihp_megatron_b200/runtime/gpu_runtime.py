@@ -11,8 +11,9 @@ replica, the replicated set (norms, embedding, LM head, whose gradients are per-
 sums under sequence parallelism) over every rank of the stage -- the fused peer-memory step
 (``dp_impl="fused"``) or reduce-scatter / Adam / all-gather (``"collective"``).
 
-GPU stages need the same TP degree and layer range in every replica of a stage (the shard
-layouts of a data-parallel group must coincide); heterogeneous plans run on the CPU runtime.
+Replicas of a stage share its layer range; their TP degrees may differ (after a failure the
+planner shrinks a group's TP degree): the shards are then reduced slice by slice over the holders
+of each interval of the common shard refinement (``HeteroParamSync``).
 (Reference: ``resihp/runtime/hetero_runtime.py:33-148`` and ``resihp/runtime/dp_runtime.py``.)
 """
 
@@ -25,8 +26,9 @@ from .. import ops
 from ..comm.group_spec import GroupSpec
 from ..comm.p2p import P2PEngine
 from ..models.config import GPTConfig
-from ..plan.hetero_plan import HeteroParallelPlan, StageGroup, tp_group_name
+from ..plan.hetero_plan import HeteroParallelPlan, StageGroup, dpshard_group_name, tp_group_name
 from ..plan.ir import Op, Schedule
+from ..utils.intervals import even_split, locate, refine
 from .gpu_executor import GPUStageExecutor, TokenSource
 from .hetero_runtime import channel_map, channel_specs
 from .interpreter import Interpreter
@@ -40,12 +42,16 @@ def replicated_group_name(stage: int) -> str:
     return f"dprep/s{stage}"
 
 
-def check_homogeneous(plan: HeteroParallelPlan) -> None:
+def stage_is_homogeneous(plan: HeteroParallelPlan, stage: int) -> bool:
+    """Every replica of the stage has the same TP degree (so shard layouts coincide)."""
+    return len({g.tp for g in plan.groups_at(stage)}) == 1
+
+
+def check_supported(plan: HeteroParallelPlan) -> None:
     for s in range(plan.num_stages):
         gs = plan.groups_at(s)
-        if len({(g.tp, g.cp, g.layers) for g in gs}) != 1:
-            raise NotImplementedError(f"stage {s}: replicas differ in TP degree or layers; the GPU runtime needs "
-                                      f"identical shard layouts within a data-parallel group")
+        if len({g.layers for g in gs}) != 1:
+            raise NotImplementedError(f"stage {s}: replicas hold different layer ranges")
         for g in gs:
             if g.cp != 1:
                 raise NotImplementedError("context parallelism is not wired into the GPU runtime")
@@ -56,10 +62,14 @@ def check_homogeneous(plan: HeteroParallelPlan) -> None:
         raise NotImplementedError("interleaved stages are not wired into the GPU runtime")
 
 
-def gpu_group_specs(plan: HeteroParallelPlan, schedule: Schedule, tokens_per_microbatch: int) -> list[GroupSpec]:
-    """TP groups, the two data-parallel groups of every stage and one channel per direction of
-    every pipeline-boundary rank pair."""
-    check_homogeneous(plan)
+def gpu_group_specs(plan: HeteroParallelPlan, schedule: Schedule, tokens_per_microbatch: int,
+                    partitions: tuple[int, ...] = ()) -> list[GroupSpec]:
+    """TP groups; per stage the data-parallel group of the replicated set and, for the
+    tensor-parallel shards, one group per TP rank (replicas with equal TP degrees) or one group
+    per holder set of the common shard refinement (``partitions``: the lengths of the
+    tensor-parallel dimensions; replicas with different TP degrees); one channel per direction
+    of every pipeline-boundary rank pair."""
+    check_supported(plan)
     specs: dict[str, GroupSpec] = {}
     for g in plan.stage_groups:
         if g.tp > 1:
@@ -67,9 +77,16 @@ def gpu_group_specs(plan: HeteroParallelPlan, schedule: Schedule, tokens_per_mic
             specs[n] = GroupSpec(n, plan.ranks(g), "tp")
     for s in range(plan.num_stages):
         gs = plan.groups_at(s)
-        for j in range(gs[0].tp):
-            n = shard_group_name(s, j)
-            specs[n] = GroupSpec(n, tuple(sorted(plan.ranks(g)[j] for g in gs)), "dp")
+        if stage_is_homogeneous(plan, s):
+            for j in range(gs[0].tp):
+                n = shard_group_name(s, j)
+                specs[n] = GroupSpec(n, tuple(sorted(plan.ranks(g)[j] for g in gs)), "dp")
+        else:
+            if not partitions:
+                raise ValueError("a stage with unequal TP degrees needs the partitioned dimension lengths")
+            for holders in plan.dpshard_holder_sets(s, partitions):
+                n = dpshard_group_name(s, holders)
+                specs[n] = GroupSpec(n, holders, "dpshard")
         n = replicated_group_name(s)
         specs[n] = GroupSpec(n, tuple(sorted(r for g in gs for r in plan.ranks(g))), "dp")
     out = list(specs.values())
@@ -82,13 +99,19 @@ class ParamSetSync:
     parameter set (``FlatParams``)."""
 
     def __init__(self, ranks: tuple[int, ...], me: int, group, impl: str, device, *, abort=None,
-                 budget_s: float = 60.0, waiter=None):
+                 budget_s: float = 60.0, waiter=None, zero: bool = True):
+        """``zero=False`` keeps the whole optimizer state on every rank of the group (gradients
+        all-reduced, every rank updates everything): redundant state that survives the loss of
+        any one replica, at 12 more bytes per parameter (collective path only)."""
         self.size, self.index = len(ranks), ranks.index(me)
         self.group = group
         self.device = torch.device(device)
         self.impl = "single" if self.size == 1 else impl
         if self.impl not in ("single", "fused", "collective"):
             raise ValueError(impl)
+        self.zero = zero and self.size > 1
+        if not self.zero and self.impl == "fused":
+            raise ValueError("the fused data-parallel step shards the optimizer state (zero=True)")
         self.wait = waiter or (lambda work: work.wait())
         self.fdp = None
         if self.impl == "fused":
@@ -102,7 +125,7 @@ class ParamSetSync:
 
     @property
     def shard(self) -> tuple[int, int]:
-        return (self.index, self.size)
+        return (self.index, self.size) if self.zero else (0, 1)
 
     @property
     def factories(self):
@@ -110,7 +133,7 @@ class ParamSetSync:
 
     def attach(self, P) -> None:
         self.P = P
-        if self.impl == "collective":
+        if self.impl == "collective" and self.zero:
             self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
 
     def step(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
@@ -120,7 +143,9 @@ class ParamSetSync:
             self.fdp.step(P, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
             return
         kw = dict(lr=lr, beta1=betas[0], beta2=betas[1], eps=eps, weight_decay=weight_decay, step=P.step)
-        if self.impl == "single":
+        if self.impl == "single" or not self.zero:
+            if self.impl != "single":
+                self.wait(dist.all_reduce(P.grad, group=self.group, async_op=True))
             ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, zero_grad=True, **kw)
             return
         self.wait(dist.reduce_scatter_tensor(self.grad_shard, P.grad, group=self.group, async_op=True))
@@ -140,15 +165,76 @@ class ParamSetSync:
             self.fdp = None
 
 
+class HeteroParamSync:
+    """Data-parallel reduction of the tensor-parallel shards when the replicas of a stage use
+    different TP degrees.  On the common refinement of every replica's shard boundaries each
+    interval has exactly one holder per replica; those holders all-reduce exactly that slice
+    (all slices of one holder set packed into one flat buffer, one all-reduce per set), then
+    every rank applies Adam to its whole local shard (optimizer state not sharded: local
+    layouts differ across the group).  (Reference: ``resihp/runtime/hetero_grad_sync.py:60-120``.)"""
+
+    impl = "hetero"
+    shard = (0, 1)
+    factories = (None, None)
+    size, group = 1, None
+
+    def __init__(self, plan: HeteroParallelPlan, stage: int, me: int, comms, device, waiter=None):
+        self.plan, self.stage, self.me, self.comms = plan, stage, me, comms
+        self.device = torch.device(device)
+        self.wait = waiter or (lambda work: work.wait())
+        self.P = None
+        self.slices: dict[tuple[int, ...], list[tuple[str, int, int, int]]] = {}
+
+    def attach(self, P) -> None:
+        self.P = P
+        tp_slices = self.plan.tp_slices(self.stage)
+        for name in P.order:
+            s = P.specs[name]
+            if s.shard_dim is None:
+                continue
+            n = s.full_shape[s.shard_dim]
+            parts = [even_split(n, len(sl)) for sl in tp_slices]
+            for iv in refine(parts):
+                holders = tuple(sorted(self.plan.rank(sl[locate(part, iv)]) for sl, part in zip(tp_slices, parts)))
+                if self.me not in holders or len(holders) == 1:
+                    continue
+                self.slices.setdefault(holders, []).append((name, s.shard_dim, iv[0] - s.shard_range[0],
+                                                            iv[1] - iv[0]))
+
+    def step(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+        P = self.P
+        for holders, pieces in self.slices.items():
+            views = [P.g(name).narrow(dim, lo, ln) for name, dim, lo, ln in pieces]
+            flat = torch.cat([v.reshape(-1) for v in views])
+            self.wait(dist.all_reduce(flat, group=self.comms.group(dpshard_group_name(self.stage, holders)),
+                                      async_op=True))
+            off = 0
+            for v in views:
+                v.copy_(flat[off:off + v.numel()].view(v.shape))
+                off += v.numel()
+        P.step += 1
+        ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, lr=lr, beta1=betas[0], beta2=betas[1],
+                      eps=eps, weight_decay=weight_decay, step=P.step, zero_grad=True)
+
+    def check(self) -> None:
+        pass
+
+    def close(self) -> None:
+        pass
+
+
 class GPUHybridRuntime:
     def __init__(self, cfg: GPTConfig, plan: HeteroParallelPlan, schedule: Schedule, comms, mgr, *, device,
                  micro_batch: int = 1, seq_len: int | None = None, tokens: TokenSource | None = None,
                  tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0, lr: float = 3e-4,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, budget_s: float = 60.0,
-                 progress=None, hook=None):
+                 progress=None, hook=None, zero: bool = True, init: bool = True):
+        """``zero``: shard the optimizer state over each data-parallel group (ZeRO-1) or keep it
+        whole on every replica (redundant: survives a fail-stop); ``init``: draw the initial
+        weights (False when a migrated state is loaded next)."""
         from ..models.tp_stage import TPStage
 
-        check_homogeneous(plan)
+        check_supported(plan)
         self.cfg, self.plan, self.comms, self.mgr = cfg, plan, comms, mgr
         self.device = torch.device(device)
         self.S = seq_len or cfg.seq_len
@@ -193,16 +279,21 @@ class GPUHybridRuntime:
         # data parallelism: the sharded set over the same TP rank of every replica, the
         # replicated set over the whole stage
         stage_groups = plan.groups_at(g.stage)
-        shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
         rep_ranks = tuple(sorted(r for h in stage_groups for r in plan.ranks(h)))
-        self.shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(g.stage, tp_rank)),
-                                     dp_impl, self.device, abort=self.abort, budget_s=budget_s, waiter=waiter)
+        if stage_is_homogeneous(plan, g.stage):
+            shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
+            self.shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(g.stage, tp_rank)),
+                                         dp_impl, self.device, abort=self.abort, budget_s=budget_s, waiter=waiter,
+                                         zero=zero)
+        else:
+            self.shd_sync = HeteroParamSync(plan, g.stage, comms.rank, comms, self.device, waiter=waiter)
         self.rep_sync = ParamSetSync(rep_ranks, comms.rank, comms.group(replicated_group_name(g.stage)), dp_impl,
-                                     self.device, abort=self.abort, budget_s=budget_s, waiter=waiter)
+                                     self.device, abort=self.abort, budget_s=budget_s, waiter=waiter, zero=zero)
         self.stage = TPStage(cfg, self.device, layers=range(*g.layers), first=g.stage == 0,
                              last=g.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch,
                              seq_len=self.S, seed=seed, rep_shard=self.rep_sync.shard, shd_shard=self.shd_sync.shard,
-                             rep_factories=self.rep_sync.factories, shd_factories=self.shd_sync.factories)
+                             rep_factories=self.rep_sync.factories, shd_factories=self.shd_sync.factories,
+                             init=init)
         self.rep_sync.attach(self.stage.rep)
         self.shd_sync.attach(self.stage.shd)
         self.tokens = tokens or TokenSource(cfg.vocab_size, micro_batch, self.S)

@@ -33,8 +33,10 @@ def ensure_process_group(device: torch.device) -> None:
     dist.init_process_group(backend, store=dist.HashStore(), rank=0, world_size=1, **kw)
 
 
-def plan_layout(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatches: int, micro_batch: int, seq_len: int):
-    """``(plan, schedule)`` of a ``tp x pp x dp`` layout on one node (device ids ``n0g{i}``)."""
+def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatches: int, micro_batch: int,
+                   seq_len: int):
+    """The joint planner for a ``tp x pp x dp`` layout of ``cfg`` on one node, and the node's
+    topology (device ids ``n0g{i}``)."""
     from ..plan.model_spec import ModelProfile, ModelSpec
     from ..plan.planner import HeteroPlanner, PlannerConfig
     from ..plan.topology import ClusterTopology
@@ -43,11 +45,7 @@ def plan_layout(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatches: 
                      num_kv_heads=cfg.kv_heads, vocab=cfg.vocab_size, seq_len=seq_len, micro_batch_size=micro_batch)
     pc = PlannerConfig(model=spec, profile=ModelProfile.b200(spec), num_stages=pp, num_replicas=dp, tp=tp,
                        num_microbatches=num_microbatches, sequence_parallel=True, mem_capacity=math.inf)
-    planner = HeteroPlanner(pc)
-    topo = ClusterTopology.uniform(1, tp * pp * dp)
-    plan = planner.initial_plan(topo)
-    schedule, _ = planner.schedule(plan, topo)
-    return plan, schedule
+    return HeteroPlanner(pc), ClusterTopology.uniform(1, tp * pp * dp)
 
 
 class GPUHybridTrainer:
@@ -57,7 +55,7 @@ class GPUHybridTrainer:
                  data_seed: int = 1):
         from ..comm.comm_manager import ResilientCommManager
         from ..runtime.gpu_executor import TokenSource
-        from ..runtime.gpu_runtime import GPUHybridRuntime, gpu_group_specs
+        from ..runtime.gpu_runtime import GPUHybridRuntime
 
         world = dist.get_world_size() if dist.is_initialized() else 1
         rank = dist.get_rank() if dist.is_initialized() else 0
@@ -70,21 +68,29 @@ class GPUHybridTrainer:
         self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
         self.micro_batch = micro_batch
         n_micro = global_batch // micro_batch
-        self.plan, self.schedule = plan_layout(cfg, tp=tp, pp=pp, dp=dp, num_microbatches=n_micro,
-                                               micro_batch=micro_batch, seq_len=self.S)
+        self.planner, self.topology = layout_planner(cfg, tp=tp, pp=pp, dp=dp, num_microbatches=n_micro,
+                                                     micro_batch=micro_batch, seq_len=self.S)
+        self.plan = self.planner.initial_plan(self.topology)
+        self.schedule, _ = self.planner.schedule(self.plan, self.topology)
         ids = list(self.plan.world)
         self.mgr = ResilientCommManager("nccl" if self.device.type == "cuda" else "gloo", device=str(self.device),
                                         subgroup_mode="local", timeout_s=120)
-        specs = gpu_group_specs(self.plan, self.schedule, micro_batch * self.S)
-        self.comms = self.mgr.adopt(1, ids, ids[rank], specs)
+        self.comms = self.mgr.adopt(1, ids, ids[rank], self._group_specs(self.plan, self.schedule))
         self.tokens = TokenSource(cfg.vocab_size, micro_batch, self.S, seed=data_seed)
+        self.opts = dict(micro_batch=micro_batch, seq_len=self.S, tokens=self.tokens, tp_impl=tp_impl, dp_impl=dp_impl,
+                         seed=seed, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         self.runtime = GPUHybridRuntime(cfg, self.plan, self.schedule, self.comms, self.mgr, device=self.device,
-                                        micro_batch=micro_batch, seq_len=self.S, tokens=self.tokens, tp_impl=tp_impl,
-                                        dp_impl=dp_impl, seed=seed, lr=lr, betas=betas, eps=eps,
-                                        weight_decay=weight_decay)
+                                        **self.opts)
         self.tokens_per_step = self.runtime.tokens_per_step
         self.global_batch = global_batch
         self.layout = f"tp{tp}pp{pp}dp{dp}-sp-{tp_impl}tp-{dp_impl}dp"
+        self.last_reconfig: dict | None = None
+
+    def _group_specs(self, plan, schedule):
+        from ..runtime.gpu_runtime import gpu_group_specs
+        from ..runtime.gpu_state import partition_sizes
+
+        return gpu_group_specs(plan, schedule, self.micro_batch * self.S, partition_sizes(self.cfg))
 
     def step_device(self) -> torch.Tensor:
         """One step; the global mean loss as a 0-d device tensor (no host synchronisation)."""
@@ -104,5 +110,94 @@ class GPUHybridTrainer:
     def check(self) -> None:
         self.runtime.check()
 
+    # ------------------------------------------------------------------ live reconfiguration
+    def reconfigure(self, leaving: list[int], *, store=None, store_addr=None, store_prefix: str | None = None) -> bool:
+        """Planned removal of the ranks ``leaving`` (e.g. a GPU evicted as fail-slow), between
+        steps; every current rank calls it.  Each rank first exports its slot's full
+        tensor-parallel-local state (ZeRO shards all-gathered inside each data-parallel group),
+        so every interval of every tensor is also held by a surviving replica; the planner
+        re-plans on the remaining devices (TP shrink of the weakened group or its eviction with
+        micro-batch migration, min-max layer repartition); the survivors rebuild the
+        communicators without the leavers (NCCL shrink, or a fresh world on ``store`` /
+        ``store_addr``), build the new generation's runtime and pull every slice of parameters
+        and Adam moments they now hold from the old holders (``state.transfer_plan`` /
+        ``state.transfer_engine``); the global batch, data order and step count are unchanged.
+        Returns False on a rank that leaves or becomes standby (it must not use the trainer
+        afterwards).  Phase timings land in ``last_reconfig``.  (Reference: the worker's
+        generation build and state migration, ``resihp/train/resilient_loop.py:113-160`` and
+        ``resihp/train/hetero_binding.py:95-130``.)"""
+        import time
+
+        from ..runtime.gpu_runtime import GPUHybridRuntime
+        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, gpu_tensor_specs, import_state
+        from ..state.layer_registry import device_layout, holdings
+        from ..state.transfer_engine import execute_transfers
+        from ..state.transfer_plan import plan_transfers
+
+        marks = [("start", time.perf_counter())]
+
+        def mark(name: str) -> None:
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            marks.append((name, time.perf_counter()))
+
+        rt, old_plan = self.runtime, self.plan
+        me = old_plan.world[self.comms.rank]
+        state, layout = export_state(rt)
+        step, iteration = rt.stage.shd.step, rt.iteration
+        mark("export")
+        gone = {old_plan.world[r] for r in leaving}
+        topo = self.topology.without(sorted(gone))
+        new_plan = self.planner.replan(old_plan, topo)
+        new_schedule, _ = self.planner.schedule(new_plan, topo)
+        active = {d for g in new_plan.stage_groups for d in g.devices}
+        mark("plan")
+        if me not in active:
+            rt.close()
+            self.runtime = None
+            return False
+        new_world = [d for d in new_plan.world if d in active]
+        if list(new_plan.world) != new_world:  # standby devices leave the job as well
+            new_plan = _without_standby(new_plan, new_world)
+            new_schedule, _ = self.planner.schedule(new_plan, topo)
+        comms = self.mgr.build(new_plan.generation, new_world, me, self._group_specs(new_plan, new_schedule),
+                               store=store, store_addr=store_addr, store_prefix=store_prefix)
+        mark("regroup")
+        new_rt = GPUHybridRuntime(self.cfg, new_plan, new_schedule, comms, self.mgr, device=self.device, init=False,
+                                  **self.opts)
+        mark("build")
+        specs = gpu_tensor_specs(self.cfg)
+        layer_of = gpu_layer_of(self.cfg.layers)
+        new_h = holdings(new_plan, specs, layer_of)
+        tplan = plan_transfers(holdings(old_plan, specs, layer_of), new_h, valid_sources=set(new_world),
+                               node_of={d: "n0" for d in old_plan.world})
+        if tplan.lost:
+            raise RuntimeError(f"{len(tplan.lost)} state slices have no surviving holder")
+        new_state = execute_transfers(tplan, me, comms, self.mgr, specs=specs, old_layout=layout, old_state=state,
+                                      new_layout=device_layout(new_h, me), kinds=KINDS, dtype=torch.float32,
+                                      device=str(self.device))
+        import_state(new_rt, new_state, step)
+        new_rt.iteration = iteration
+        moved = sum(t.numel() * t.element_size() for k in KINDS for t in new_state[k].values())
+        del new_state, state
+        mark("migrate")
+        rt.close()
+        self.runtime, self.plan, self.schedule, self.comms = new_rt, new_plan, new_schedule, comms
+        mark("commit")
+        self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
+        self.last_reconfig.update(bytes_loaded=moved, transfers=len(tplan.transfers),
+                                  layout=[(g.replica, g.stage, g.tp, list(g.layers)) for g in new_plan.stage_groups],
+                                  world=len(new_world))
+        return True
+
     def close(self) -> None:
-        self.runtime.close()
+        if self.runtime is not None:
+            self.runtime.close()
+            self.runtime = None
+
+
+def _without_standby(plan, world: list[str]):
+    """The same plan over a world without its standby devices."""
+    from dataclasses import replace
+
+    return replace(plan, world=tuple(world), standby=())

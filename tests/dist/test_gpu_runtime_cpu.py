@@ -131,3 +131,48 @@ def test_hybrid_trainer_plans_its_layout_and_matches_one_rank():
             assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], ref)
     # token rows are copied by the first (ids) and last (labels) stage ranks only
     assert sum(res["h2d"] for res in many.values()) == one[0]["h2d"]
+
+
+def _reconfig(rank, world, port, store_addr, layout, leaving, steps_before, steps_after):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tp, pp, dp = layout
+    tr = GPUHybridTrainer(_cfg(), tp=tp, pp=pp, dp=dp, global_batch=8, micro_batch=1, seq_len=S,
+                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2)
+    losses = [tr.train_step() for _ in range(steps_before)]
+    out = {"before": tr.plan.to_json()}
+    if leaving:
+        alive = tr.reconfigure(leaving, store_addr=store_addr, store_prefix="reconfig/gen2/")
+        out["alive"] = alive
+        if not alive:
+            out["losses"] = losses
+            return out
+        out["after"] = tr.plan.to_json()
+        out["phases"] = tr.last_reconfig
+    losses += [tr.train_step() for _ in range(steps_after)]
+    out["losses"] = losses
+    tr.close()
+    return out
+
+
+def test_live_eviction_replans_migrates_and_continues_the_same_run(store):
+    ref = spawn(_reconfig, 1, store, (1, 1, 1), [], 4, 0, timeout=240)[0]["losses"]
+    res = spawn(_reconfig, 8, store, (2, 2, 2), [7], 2, 2, timeout=400)
+    assert res[7]["alive"] is False
+    survivors = [r for r in range(7) if res[r]["alive"]]
+    assert survivors, res
+    after = res[survivors[0]]["after"]
+    devices = [d for g in after["stage_groups"] for d in g["devices"]]
+    assert "n0g7" not in devices
+    tps = sorted(len(g["devices"]) for g in after["stage_groups"])
+    assert tps != [2, 2, 2, 2]  # the weakened group shrank its TP degree or was evicted
+    for r in survivors:
+        for a, b in zip(res[r]["losses"], ref):
+            assert abs(a - b) <= 1e-2 * abs(b), (r, res[r]["losses"], ref)
+        assert res[r]["phases"]["migrate"] >= 0
