@@ -15,7 +15,9 @@ Hang causes designed out:
 
 ``abort()`` (called from the control-client thread) sets the abort flag, aborts every live NCCL
 group and sets the device abort word that the package's peer-memory kernels poll, so survivors
-leave in-flight fused kernels at once.  (Reference: ``resihp/comm/comm_manager.py:31-329``.)
+leave in-flight fused kernels at once.  Gloo groups are aborted when their generation is torn
+down: a gloo op that lost its peer stays in flight until its timeout, and destroying its group
+would otherwise wait for it while the next generation's rendezvous runs out of time.  (Reference: ``resihp/comm/comm_manager.py:31-329``.)
 """
 
 from __future__ import annotations
@@ -329,6 +331,15 @@ class ResilientCommManager:
             if self.backend == "nccl":
                 c10d._abort_process_group(None)
             else:
+                # a gloo op that lost its peer stays in flight until its timeout, and destroying
+                # its group would wait for it: abort the groups first (returns at once)
+                with self._lock:
+                    live = list(self._live)
+                for pg in live:
+                    try:
+                        pg.abort()
+                    except Exception:  # noqa: BLE001 - older gloo builds: fall back to the wait
+                        pass
                 dist.destroy_process_group()
         except Exception:  # noqa: BLE001
             log.exception("teardown of the previous generation failed; continuing")
