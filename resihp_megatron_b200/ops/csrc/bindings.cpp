@@ -416,6 +416,27 @@ void symm_copy(const std::vector<int64_t>& triples, int64_t device) {
                         static_cast<int>(pieces), num_sms(static_cast<int>(device)), cur_stream()), "symm_copy");
 }
 
+void symm_gather(const std::vector<int64_t>& src_ptrs, int64_t dst, int64_t chunk_bytes, int64_t self,
+                 int64_t device) {
+  std::vector<const void*> src(src_ptrs.size());
+  for (size_t c = 0; c < src_ptrs.size(); ++c) src[c] = reinterpret_cast<const void*>(src_ptrs[c]);
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  RB_CALL(rb::symm_gather(src.data(), reinterpret_cast<void*>(dst), chunk_bytes, static_cast<int>(src.size()),
+                          static_cast<int>(self), num_sms(static_cast<int>(device)), cur_stream()), "symm_gather");
+}
+
+void symm_copy2d(const std::vector<int64_t>& six, int64_t device) {
+  TORCH_CHECK(six.size() % 6 == 0, "symm_copy2d: sextuples");
+  const int n = static_cast<int>(six.size() / 6);
+  const long long pieces = rb::symm_copy2d_pieces(reinterpret_cast<const long long*>(six.data()), n);
+  if (pieces == 0) return;
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  auto scratch = torch::empty({pieces * rb::symm_copy2d_piece_bytes()},
+                              torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+  RB_CALL(rb::symm_copy2d(reinterpret_cast<const long long*>(six.data()), n, scratch.data_ptr(),
+                          static_cast<int>(pieces), num_sms(static_cast<int>(device)), cur_stream()), "symm_copy2d");
+}
+
 // Tensor parallel: all-gather -> GEMM (column-parallel) and GEMM -> reduce-scatter (row-parallel).
 void tp_ag_gemm(const torch::Tensor& x_full, const std::vector<int64_t>& src_ptrs, int64_t self, const torch::Tensor& w,
                 bool w_t, torch::Tensor& y, torch::Tensor& ready, int64_t abort_dev) {
@@ -562,6 +583,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &symm_barrier);
   m.def("dp_step_fused", &dp_step_fused);
   m.def("symm_copy", &symm_copy);
+  m.def("symm_gather", &symm_gather);
+  m.def("symm_copy2d", &symm_copy2d);
   m.def("host_register_mapped", &host_register_mapped);
   m.def("host_unregister", &host_unregister);
   m.def("ring_record_bytes", &ring_record_bytes);

@@ -82,6 +82,13 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
 int ring_record_bytes();
 int kernel_stamp_bytes();
 int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
+// All-gather of equal chunks from peers' buffers into this rank's buffer (no host staging).
+int symm_gather(const void* const* src, void* dst, long long chunk_bytes, int world, int self, int num_sms,
+                cudaStream_t s);
+// Strided slice copies (rows x row_bytes with source / destination pitches), pre-split on the host.
+int symm_copy2d(const long long* six, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
+long long symm_copy2d_pieces(const long long* six, int n);
+int symm_copy2d_piece_bytes();
 int symm_copy_piece_bytes();
 int rs_reduce(const void* recv, int world, long long n, void* out, const void* residual, cudaStream_t s);
 // Expert parallelism (moe.cu).

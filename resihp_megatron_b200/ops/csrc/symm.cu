@@ -242,10 +242,100 @@ __global__ void __launch_bounds__(256) symm_copy_kernel(const CopyPiece* __restr
   }
 }
 
+// Strided slice copy: piece = `rows` rows of `row16` 16-byte units, rows `src_pitch16` /
+// `dst_pitch16` units apart (a column block of a row-major tensor); pieces are pre-split on the
+// host so that each holds at most about 1 MB.
+struct CopyPiece2D {
+  const uint4* src;
+  uint4* dst;
+  int rows, row16;
+  long long src_pitch16, dst_pitch16;
+};
+
+__global__ void __launch_bounds__(256) symm_copy2d_kernel(const CopyPiece2D* __restrict__ pieces, int n_pieces) {
+  for (int pi = blockIdx.x; pi < n_pieces; pi += gridDim.x) {
+    const CopyPiece2D c = pieces[pi];
+    const long long total = static_cast<long long>(c.rows) * c.row16;
+    for (long long i = threadIdx.x; i < total; i += blockDim.x * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long g = i + u * blockDim.x;
+        if (g < total) {
+          const long long r = g / c.row16, q = g - r * c.row16;
+          v[u] = __ldcv(c.src + r * c.src_pitch16 + q);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long g = i + u * blockDim.x;
+        if (g < total) {
+          const long long r = g / c.row16, q = g - r * c.row16;
+          c.dst[r * c.dst_pitch16 + q] = v[u];
+        }
+      }
+    }
+  }
+}
+
+// All-gather of equal row chunks: chunk c of `dst` (this rank's buffer) is filled from `src[c]`
+// (chunk c in rank c's buffer) for every c != self; the work is cut into 1 MB slices spread over
+// the grid.  No piece table, so nothing is staged on the host.
+struct GatherArgs {
+  const uint4* src[kMaxWorld];
+  uint4* dst;
+  long long chunk16;
+  int world, self;
+};
+
+__global__ void __launch_bounds__(256) symm_gather_kernel(GatherArgs a) {
+  constexpr long long kSlice16 = (1 << 20) / 16;
+  const long long per_chunk = (a.chunk16 + kSlice16 - 1) / kSlice16;
+  const long long slices = per_chunk * (a.world - 1);
+  for (long long sl = blockIdx.x; sl < slices; sl += gridDim.x) {
+    const int k = static_cast<int>(sl / per_chunk);
+    const int c = (a.self + 1 + k) % a.world;
+    const long long lo = (sl - k * per_chunk) * kSlice16;
+    const long long hi = lo + kSlice16 < a.chunk16 ? lo + kSlice16 : a.chunk16;
+    const uint4* src = a.src[c];
+    uint4* dst = a.dst + c * a.chunk16;
+    for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * blockDim.x < hi) v[u] = __ldcv(src + i + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i + u * blockDim.x < hi) dst[i + u * blockDim.x] = v[u];
+    }
+  }
+}
+
 }  // namespace
 
 // ----------------------------------------------------------------------------------- host side
 int symm_signal_bytes(int world) { return world * kPadStride * 8; }
+
+int symm_gather(const void* const* src, void* dst, long long chunk_bytes, int world, int self, int num_sms,
+                cudaStream_t s) {
+  if (world < 1 || world > kMaxWorld || self < 0 || self >= world || (chunk_bytes & 15) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15))
+    return -1;
+  if (world == 1 || chunk_bytes == 0) return 0;
+  GatherArgs a{};
+  for (int c = 0; c < world; ++c) {
+    if (reinterpret_cast<uintptr_t>(src[c]) & 15) return -1;
+    a.src[c] = reinterpret_cast<const uint4*>(src[c]);
+  }
+  a.dst = reinterpret_cast<uint4*>(dst);
+  a.chunk16 = chunk_bytes / 16;
+  a.world = world;
+  a.self = self;
+  const long long slices = ((a.chunk16 + (1 << 16) - 1) >> 16) * (world - 1);
+  const int grid = slices < num_sms * 4 ? static_cast<int>(slices) : num_sms * 4;
+  symm_gather_kernel<<<grid, 256, 0, s>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
 
 int symm_barrier(unsigned long long* const* pads_dev, int rank, int world, unsigned long long epoch,
                  const int* abort_word, int* status, int* err, double budget_s, cudaStream_t s) {
@@ -334,6 +424,59 @@ int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces
 }
 
 int symm_copy_piece_bytes() { return static_cast<int>(sizeof(CopyPiece)); }
+
+// pieces: host array of (src, dst, rows, row_bytes, src_pitch, dst_pitch) sextuples, addresses,
+// row bytes and pitches 16-byte aligned; `dev_scratch` holds at least `max_pieces` records.
+int symm_copy2d(const long long* six, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s) {
+  constexpr long long kPieceBytes = 1 << 20;
+  std::vector<CopyPiece2D> pieces;
+  for (int i = 0; i < n; ++i) {
+    const long long src = six[6 * i], dst = six[6 * i + 1], rows = six[6 * i + 2], row_bytes = six[6 * i + 3];
+    const long long sp = six[6 * i + 4], dp = six[6 * i + 5];
+    if ((src | dst | row_bytes | sp | dp) & 15) return -1;
+    if (rows <= 0 || row_bytes <= 0) continue;
+    if (row_bytes > kPieceBytes) {  // long rows: one piece per (row, 1 MB column block)
+      for (long long r = 0; r < rows; ++r)
+        for (long long off = 0; off < row_bytes; off += kPieceBytes) {
+          const long long b = row_bytes - off < kPieceBytes ? row_bytes - off : kPieceBytes;
+          pieces.push_back({reinterpret_cast<const uint4*>(src + r * sp + off),
+                            reinterpret_cast<uint4*>(dst + r * dp + off), 1, static_cast<int>(b / 16), 0, 0});
+        }
+      continue;
+    }
+    const long long per = kPieceBytes / row_bytes;  // rows per piece (>= 1)
+    for (long long r = 0; r < rows; r += per) {
+      const long long nr = rows - r < per ? rows - r : per;
+      pieces.push_back({reinterpret_cast<const uint4*>(src + r * sp), reinterpret_cast<uint4*>(dst + r * dp),
+                        static_cast<int>(nr), static_cast<int>(row_bytes / 16), sp / 16, dp / 16});
+    }
+  }
+  if (pieces.empty()) return 0;
+  if (static_cast<int>(pieces.size()) > max_pieces) return -2;
+  cudaError_t e = cudaMemcpyAsync(dev_scratch, pieces.data(), pieces.size() * sizeof(CopyPiece2D),
+                                  cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaStreamSynchronize(s);  // the host vector must outlive the copy
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int grid = static_cast<int>(pieces.size()) < num_sms * 4 ? static_cast<int>(pieces.size()) : num_sms * 4;
+  symm_copy2d_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const CopyPiece2D*>(dev_scratch),
+                                          static_cast<int>(pieces.size()));
+  return static_cast<int>(cudaGetLastError());
+}
+
+long long symm_copy2d_pieces(const long long* six, int n) {
+  constexpr long long kPieceBytes = 1 << 20;
+  long long count = 0;
+  for (int i = 0; i < n; ++i) {
+    const long long rows = six[6 * i + 2], row_bytes = six[6 * i + 3];
+    if (rows <= 0 || row_bytes <= 0) continue;
+    if (row_bytes > kPieceBytes) count += rows * ((row_bytes + kPieceBytes - 1) / kPieceBytes);
+    else count += (rows + kPieceBytes / row_bytes - 1) / (kPieceBytes / row_bytes);
+  }
+  return count;
+}
+
+int symm_copy2d_piece_bytes() { return static_cast<int>(sizeof(CopyPiece2D)); }
 
 namespace {
 // Reduce-scatter finish: out[i] = sum over slots s (rank order) of recv[s][i], fp32 accumulate.

@@ -103,13 +103,8 @@ class TensorParallelComm:
         xf = self.gather_buffer(M, K, b)
         rows = M // self.world
         self._barrier()
-        src = self._sources(M, K, b)
-        dst = self.heap.peer_ptrs(f"x_full{b}")[self.rank]
-        triples = []
-        for c in range(self.world):
-            if c != self.rank:
-                triples += [src[c], dst + c * rows * K * 2, rows * K * 2]
-        ext().symm_copy(triples, xf.device.index if xf.device.index is not None else 0)
+        ext().symm_gather(self._sources(M, K, b), self.heap.peer_ptrs(f"x_full{b}")[self.rank], rows * K * 2,
+                          self.rank, xf.device.index if xf.device.index is not None else 0)
         count(2 if not self.emulated else 1)
         if advance:
             self._ag ^= 1

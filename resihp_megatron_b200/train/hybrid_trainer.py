@@ -52,7 +52,10 @@ class GPUHybridTrainer:
     def __init__(self, cfg: GPTConfig, *, tp: int, pp: int, dp: int, global_batch: int, micro_batch: int = 1,
                  seq_len: int | None = None, tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, device=None,
-                 data_seed: int = 1):
+                 data_seed: int = 1, migrate: str = "p2p"):
+        """``migrate``: how a reconfiguration moves state on GPUs -- ``"p2p"`` (one strided peer
+        copy launch per rank over NVLink, ``parallel.migration``) or ``"nccl"`` (one send/receive
+        per slice and kind, ``state.transfer_engine``)."""
         from ..comm.comm_manager import ResilientCommManager
         from ..runtime.gpu_executor import TokenSource
         from ..runtime.gpu_runtime import GPUHybridRuntime
@@ -63,6 +66,9 @@ class GPUHybridTrainer:
             raise ValueError(f"tp {tp} x pp {pp} x dp {dp} != world size {world}")
         if global_batch % micro_batch:
             raise ValueError("the global batch must be a multiple of the micro-batch")
+        if migrate not in ("p2p", "nccl"):
+            raise ValueError(migrate)
+        self.migrate = migrate
         self.cfg = cfg
         self.S = seq_len or cfg.seq_len
         self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
@@ -173,9 +179,20 @@ class GPUHybridTrainer:
                                node_of={d: "n0" for d in old_plan.world})
         if tplan.lost:
             raise RuntimeError(f"{len(tplan.lost)} state slices have no surviving holder")
-        new_state = execute_transfers(tplan, me, comms, self.mgr, specs=specs, old_layout=layout, old_state=state,
-                                      new_layout=device_layout(new_h, me), kinds=KINDS, dtype=torch.float32,
-                                      device=str(self.device))
+        new_layout = device_layout(new_h, me)
+        if self.device.type == "cuda" and self.migrate == "p2p":
+            from ..parallel.migration import migrate_p2p
+            from ..parallel.symm import exchange_via_group
+
+            new_state = {k: {key: torch.empty(specs[key].local_shape(iv), dtype=torch.float32, device=self.device)
+                             for key, iv in new_layout.items()} for k in KINDS}
+            migrate_p2p(tplan, me, new_world, specs=specs, old_h=holdings(old_plan, specs, layer_of), new_h=new_h,
+                        old_state=state, new_state=new_state, kinds=KINDS, device=self.device,
+                        exchange=exchange_via_group(None), abort=new_rt.abort)
+        else:
+            new_state = execute_transfers(tplan, me, comms, self.mgr, specs=specs, old_layout=layout,
+                                          old_state=state, new_layout=new_layout, kinds=KINDS, dtype=torch.float32,
+                                          device=str(self.device))
         import_state(new_rt, new_state, step)
         new_rt.iteration = iteration
         moved = sum(t.numel() * t.element_size() for k in KINDS for t in new_state[k].values())
