@@ -50,7 +50,9 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--seqs-per-gpu", type=int, default=SEQS_PER_GPU)
+    ap.add_argument("--seqs-per-gpu", type=int, default=None,
+                    help=f"sequences per GPU per step (default {SEQS_PER_GPU}; MoE models: 4, i.e. BASELINE config 3's "
+                         "global batch 32 at 8 GPUs)")
     ap.add_argument("--micro-batch", type=int, default=None,
                     help="sequences per micro-batch; default 1 on one GPU (the unsharded optimizer state leaves "
                          "room for one), 2 on more (bigger GEMMs, fewer partial waves)")
@@ -64,6 +66,8 @@ def _args():
     ap.add_argument("--parallelism", default="dp",
                     help="'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' with T*P*D = N: tensor (+ sequence) x "
                          "pipeline x data parallelism through the plan-driven runtime (BASELINE config 2: tp2pp2dp2)")
+    ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
+                    help="MoE models: expert dispatch / combine over NVLink peer memory, or NCCL all_to_all")
     ap.add_argument("--tp-impl", choices=["fused", "collective"], default="fused",
                     help="with --parallelism tp..: TP collectives fused into the GEMMs over NVLink, or NCCL")
     return ap.parse_args()
@@ -159,9 +163,16 @@ def main() -> None:
     from resihp_megatron_b200.models.config import get_config
     from resihp_megatron_b200.train.gpu_trainer import GPUTrainer, init_distributed
 
+    from resihp_megatron_b200.models.config import get_config as _get_config
+
+    if args.seqs_per_gpu is None:
+        args.seqs_per_gpu = 4 if _get_config(args.model).is_moe else SEQS_PER_GPU
     rank, world, local = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.parallelism == "ep" or get_config(args.model).is_moe:
+        run_moe(args, rank, world, local)
+        return
     if args.parallelism != "dp":
         run_hybrid(args, rank, world, local)
         return
@@ -328,12 +339,113 @@ def main() -> None:
         dist.destroy_process_group()
 
 
+def _timed_region(args, trainer, rank: int, world: int, local: int) -> dict:
+    """Warm-up, device-timed steps (max over ranks), clocks and the end-to-end steps through
+    ``trainer.train_step``; the common part of the MoE and hybrid-parallel runs."""
+    import torch
+    import torch.distributed as dist
+
+    from resihp_megatron_b200 import ops
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        trainer.step_device()
+    torch.cuda.synchronize()
+    trainer.check()
+    sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    l0 = ops.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    loss = None
+    for _ in range(args.steps):
+        loss = trainer.step_device()
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = ops.launches() - l0
+    clocks = sampler.stop() if sampler else None
+    trainer.check()
+    t = torch.tensor([start.elapsed_time(end)], device=trainer.device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = trainer.tokens_per_step * args.steps
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    h2d = 0
+    for _ in range(args.steps):
+        trainer.train_step()
+        h2d += trainer.h2d_bytes_last_step
+    torch.cuda.synchronize()
+    te = torch.tensor([time.perf_counter() - t0], device=trainer.device, dtype=torch.float64)
+    hb = torch.tensor([h2d / args.steps], device=trainer.device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.all_reduce(hb)
+    return {"ms": ms_max, "value": tokens / (ms_max / 1000.0), "loss": float(loss.item()), "launches": launches,
+            "clocks": clocks, "e2e": tokens / float(te.item()), "h2d": int(hb.item())}
+
+
+def _json_line(args, cfg, world: int, global_batch: int, mb: int, layout: str, r: dict, extra_config: dict) -> dict:
+    return {
+        "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (r["value"] / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None, "dtype": "bf16",
+        "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
+        "config": {"model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
+                   "global_batch": global_batch, "seq_len": args.seq, "micro_batch": mb, "parallelism": layout,
+                   "l2": "inputs larger than L2 (each step touches > 10 GB of weights/grads/optimizer state per GPU)",
+                   "params": cfg.num_params(),
+                   "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * r["value"] / world / 1e12, **extra_config},
+        "clocks": r["clocks"],
+        "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4 * world},
+        "gpu_launches": r["launches"], "loss": r["loss"], "impl": "ours",
+    }
+
+
+def run_moe(args, rank: int, world: int, local: int) -> None:
+    """Mixtral-shaped MoE step: dense weights data parallel, experts expert
+    parallel over the same ranks, through ``GPUMoETrainer``."""
+    import torch
+    import torch.distributed as dist
+
+    from resihp_megatron_b200.models.config import get_config
+    from resihp_megatron_b200.train.hybrid_trainer import ensure_process_group
+    from resihp_megatron_b200.train.moe_trainer import GPUMoETrainer
+
+    ensure_process_group(torch.device("cuda", local))
+    cfg = get_config(args.model, seq_len=args.seq)
+    if args.layers:
+        cfg = cfg.with_(layers=args.layers)
+    global_batch = args.seqs_per_gpu * world
+    mb = args.micro_batch or 1
+    trainer = GPUMoETrainer(cfg, global_batch=global_batch, micro_batch=mb, seq_len=args.seq,
+                            ep_impl="peer" if args.ep_impl == "peer" else "collective",
+                            dp_impl="fused" if args.dp_impl == "fused" else "collective")
+    r = _timed_region(args, trainer, rank, world, local)
+    if rank == 0:
+        out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r,
+                         {"experts": cfg.num_experts, "top_k": cfg.top_k})
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    trainer.close()
+    dist.barrier()
+
+
 def run_hybrid(args, rank: int, world: int, local: int) -> None:
     """TP x PP x DP step through ``GPUHybridTrainer`` (same metric, timing and JSON line)."""
     import torch
     import torch.distributed as dist
 
-    from resihp_megatron_b200 import ops
     from resihp_megatron_b200.models.config import get_config
     from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer, ensure_process_group
 
@@ -350,48 +462,8 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
     trainer = GPUHybridTrainer(cfg, tp=tp, pp=pp, dp=dp, global_batch=global_batch, micro_batch=mb,
                                seq_len=args.seq, tp_impl=args.tp_impl,
                                dp_impl="fused" if args.dp_impl == "fused" else "collective")
-    for _ in range(args.warmup):
-        trainer.step_device()
-    torch.cuda.synchronize()
-    trainer.check()
-    sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    dist.barrier()
-    torch.cuda.synchronize()
-    l0 = ops.launches()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    loss = None
-    for _ in range(args.steps):
-        loss = trainer.step_device()
-    end.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    launches = ops.launches() - l0
-    clocks = sampler.stop() if sampler else None
-    trainer.check()
-    t = torch.tensor([start.elapsed_time(end)], device=trainer.device, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    tokens = trainer.tokens_per_step * args.steps
-    value = tokens / (ms_max / 1000.0)
-    last_loss = float(loss.item())
-    # end to end through the public API: host tokens copied in by the consuming ranks, loss read back
-    dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    h2d = 0
-    for _ in range(args.steps):
-        trainer.train_step()
-        h2d += trainer.h2d_bytes_last_step
-    torch.cuda.synchronize()
-    te = torch.tensor([time.perf_counter() - t0, h2d / args.steps], device=trainer.device, dtype=torch.float64)
-    dist.all_reduce(te[:1], op=dist.ReduceOp.MAX)
-    hb = te[1:].clone()
-    dist.all_reduce(hb)
-    e2e_value = tokens / float(te[0].item())
+    parts = [b - a for a, b in trainer.plan.layer_partition()]
+    r = _timed_region(args, trainer, rank, world, local)
     # optional live reconfiguration: the last rank leaves; the planner re-plans the survivors
     # (TP shrink or eviction of its group, min-max layer repartition) and state migrates slice by slice
     recfg, alive = None, True
@@ -407,6 +479,7 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
             torch.cuda.synchronize()
             trainer.check()
             dist.barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
             for _ in range(args.steps):
                 loss2 = trainer.step_device()
@@ -416,29 +489,12 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
             post_ms, commit_max = vals.tolist()
             recfg = {"kind": "planned eviction of the last rank; re-planned layout, slice-level state migration",
-                     "n_gpus_post": dist.get_world_size(), "post_value": tokens / (post_ms / 1000),
+                     "n_gpus_post": dist.get_world_size(),
+                     "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
                      "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
                      "post_loss": float(loss2.item()), "phases_s_rank0": trainer.last_reconfig}
     if rank == 0:
-        out = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": (value / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None, "dtype": "bf16",
-            "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
-            "config": {
-                "model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
-                "global_batch": global_batch, "seq_len": args.seq, "micro_batch": mb,
-                "parallelism": trainer.layout,
-                "layers_per_stage": [b - a for a, b in trainer.plan.layer_partition()],
-                "l2": "inputs larger than L2 (each step touches > 10 GB of weights/grads/optimizer state per GPU)",
-                "params": cfg.num_params(),
-                "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * value / world / 1e12,
-            },
-            "clocks": clocks,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(hb.item()),
-                    "d2h_bytes_per_step": 4 * world},
-            "gpu_launches": launches, "loss": last_loss, "impl": "ours",
-        }
+        out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r, {"layers_per_stage": parts})
         if recfg is not None:
             out["reconfig"] = recfg
         print(json.dumps(out), flush=True)

@@ -536,15 +536,19 @@ void moe_grad_push(const torch::Tensor& dout, const torch::Tensor& gates, const 
           "moe_grad_push");
 }
 
-void moe_grad_pull(const torch::Tensor& dout, const torch::Tensor& gates, const torch::Tensor& dgate,
-                   const torch::Tensor& topi, const torch::Tensor& route_row, int64_t k, int64_t E,
-                   const std::vector<int64_t>& dxbuf, torch::Tensor& dx, torch::Tensor& dlogits) {
-  CHECK_BF16(dout);
-  const c10::cuda::CUDAGuard g(dout.device());
+// `residual_grad`: the gradient of the layer output, added to dx when the expert input is the
+// residual stream itself; None when the experts read a normalised copy (transformer blocks).
+void moe_grad_pull(const c10::optional<torch::Tensor>& residual_grad, const torch::Tensor& gates,
+                   const torch::Tensor& dgate, const torch::Tensor& topi, const torch::Tensor& route_row, int64_t k,
+                   int64_t E, const std::vector<int64_t>& dxbuf, torch::Tensor& dx, torch::Tensor& dlogits) {
+  CHECK_BF16(dx);
+  if (residual_grad.has_value()) CHECK_BF16((*residual_grad));
+  const c10::cuda::CUDAGuard g(dx.device());
   auto b = as_ptrs(dxbuf);
-  RB_CALL(rb::moe_grad_pull(dout.data_ptr(), gates.data_ptr<float>(), dgate.data_ptr<float>(), topi.data_ptr<int>(),
-                            reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), dout.size(0), k,
-                            dout.size(1), E, static_cast<int>(b.size()), b.data(), dx.data_ptr(),
+  RB_CALL(rb::moe_grad_pull(residual_grad.has_value() ? residual_grad->data_ptr() : nullptr, gates.data_ptr<float>(),
+                            dgate.data_ptr<float>(), topi.data_ptr<int>(),
+                            reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), dx.size(0), k,
+                            dx.size(1), E, static_cast<int>(b.size()), b.data(), dx.data_ptr(),
                             dlogits.data_ptr<float>(), cur_stream()), "moe_grad_pull");
 }
 

@@ -251,14 +251,16 @@ __global__ void moe_grad_pull_kernel(const __nv_bfloat16* __restrict__ dout, con
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
   for (int j = lane; j < H / 8; j += 32) {
-    float acc[8];
-    const uint4 dv = reinterpret_cast<const uint4*>(dout + static_cast<long long>(t) * H)[j];
-    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (dout != nullptr) {  // the residual path, when the experts' input is the residual stream
+      const uint4 dv = reinterpret_cast<const uint4*>(dout + static_cast<long long>(t) * H)[j];
+      const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = unpack_bf16x2(dw[q]);
-      acc[2 * q] = f.x;
-      acc[2 * q + 1] = f.y;
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(dw[q]);
+        acc[2 * q] = f.x;
+        acc[2 * q + 1] = f.y;
+      }
     }
     for (int s = 0; s < k; ++s) {
       const long long packed = route_row[t * k + s];

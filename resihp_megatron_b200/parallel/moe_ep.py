@@ -136,20 +136,33 @@ class ExpertParallelMoE:
         self._barrier()
 
     # ------------------------------------------------------------------ phase 4: experts
-    def experts_forward(self, weights: dict[int, tuple[torch.Tensor, torch.Tensor]]) -> None:
-        """``weights[e] = (w13 [2F, H], w2 [H, F])`` for this rank's experts."""
+    def experts_forward(self, weights: dict[int, tuple[torch.Tensor, torch.Tensor]], keep_input: bool = False) -> None:
+        """``weights[e] = (w13 [2F, H], w2 [H, F])`` for this rank's experts.  ``keep_input``
+        copies the received rows out of the shared receive buffer, so the backward still has
+        them after later layers reused the buffer (a multi-layer model keeps one ``saved`` state
+        per layer: ``take_state`` / ``put_state``)."""
         s = self.saved
         s["expert_cache"] = {}
         for e, (lo, n) in zip(self.local, s["local_ranges"]):
             if n == 0:
                 continue
             xin = self.rows("recv", lo + n)[lo:]
+            if keep_input:
+                xin = xin.clone()
             w13, w2 = weights[e]
             gu = ops.gemm(xin, w13)
             a = ops.swiglu_fwd(gu)
             ops.gemm(a, w2, out=self.rows("y", lo + n)[lo:])
-            s["expert_cache"][e] = (gu, a)
+            s["expert_cache"][e] = (gu, a, xin if keep_input else None)
         self._barrier()
+
+    def take_state(self) -> dict:
+        """Detach the routing / activation state of the layer just run (for its backward)."""
+        st, self.saved = self.saved, {}
+        return st
+
+    def put_state(self, state: dict) -> None:
+        self.saved = state
 
     # ------------------------------------------------------------------ phase 5: combine
     def combine(self, residual: torch.Tensor) -> torch.Tensor:
@@ -181,9 +194,9 @@ class ExpertParallelMoE:
             if n == 0:
                 continue
             w13, w2 = weights[e]
-            gu, a = s["expert_cache"][e]
+            gu, a, kept = s["expert_cache"][e]
             dy = self.rows("dyrecv", lo + n)[lo:]
-            xin = self.rows("recv", lo + n)[lo:]
+            xin = kept if kept is not None else self.rows("recv", lo + n)[lo:]
             da = ops.gemm(dy, w2, b_t=True)
             ops.gemm(dy, a, a_t=True, b_t=True, out=grads[e][1], accumulate=True)
             dgu = ops.swiglu_bwd(gu, da)
@@ -191,15 +204,18 @@ class ExpertParallelMoE:
             ops.gemm(dgu, w13, b_t=True, out=self.rows("dxrecv", lo + n)[lo:])
         self._barrier()
 
-    def grad_pull(self, router_w: torch.Tensor, router_grad: torch.Tensor) -> torch.Tensor:
-        """Input gradient of the layer (residual + expert paths + router path); accumulates the
-        router weight gradient (fp32) into ``router_grad``."""
+    def grad_pull(self, router_w: torch.Tensor, router_grad: torch.Tensor, residual: bool = True,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+        """Input gradient of the layer: expert paths + router path, plus the residual path when
+        ``residual`` (the experts read the residual stream itself; False when they read a
+        normalised copy, as in a transformer block); accumulates the router weight gradient
+        (fp32) into ``router_grad``."""
         s = self.saved
         T = s["T"]
-        dx = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
+        dx = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device) if out is None else out
         dlogits = torch.empty(T, self.E, dtype=torch.float32, device=self.device)
-        ext().moe_grad_pull(s["dout"], s["gates"], s["dgate"], s["topi"], s["route_row"], self.k, self.E,
-                            self.heap.peer_ptrs("dxrecv"), dx, dlogits)
+        ext().moe_grad_pull(s["dout"] if residual else None, s["gates"], s["dgate"], s["topi"], s["route_row"], self.k,
+                            self.E, self.heap.peer_ptrs("dxrecv"), dx, dlogits)
         ops.count(1)
         # router path: [T, E] x [E, H] products with E <= 16 (too narrow for the tensor-core tiles)
         router_grad.add_(dlogits.t() @ s["x"].float())

@@ -14,7 +14,7 @@ expert's gradient is summed over all its holders (``edp/`` groups derived from t
 Dropless routing and a per-token loss over the global token count make any placement -- with or
 without replicated experts, before or after a failure -- equal to the single-process reference
 up to reduction order.  On GPU the dispatch -> grouped expert GEMM -> combine path is the fused
-kernel of ``parallel/moe``.  (Reference: ``resihp/runtime/moe.py:29-269``.)
+kernels of ``parallel/moe_ep``.  (Reference: ``resihp/runtime/moe.py:29-269``.)
 """
 
 from __future__ import annotations

@@ -1,0 +1,61 @@
+"""Orchestration of the GPU MoE model (expert parallel over 4 gloo ranks with the all-to-all
+transport, PyTorch stand-ins for the kernels): gradients of every dense and expert tensor and
+the per-step losses must match one rank holding every expert."""
+
+import pytest
+import torch
+
+from tests.dist_utils import spawn
+
+pytestmark = pytest.mark.dist
+
+
+def _cfg():
+    from resihp_megatron_b200.models.config import GPTConfig
+
+    return GPTConfig(name="tmoe", vocab_size=64, hidden=64, layers=2, heads=4, kv_heads=2, ffn=64, seq_len=8,
+                     num_experts=4, top_k=2)
+
+
+def _worker(rank, world, port, steps):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.moe_trainer import GPUMoETrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tr = GPUMoETrainer(_cfg(), global_batch=8, micro_batch=1, seq_len=8, ep_impl="collective",
+                       dp_impl="collective", device="cpu", lr=1e-2)
+    m = tr.model
+    # step 0's gradients before any update
+    for j in range(tr.n_local):
+        ids, labels = tr.tokens.tokens(0, rank * tr.n_local + j)
+        m.forward_backward(ids, labels, 1.0 / tr.tokens_per_step)
+    dense = m.dense.grad.clone()
+    if world > 1:
+        dist.all_reduce(dense)
+    grads = {n: dense[m.dense.offsets[n]:m.dense.offsets[n] + m.dense.specs[n].numel].clone() for n in m.dense.order}
+    grads.update({n: m.experts.g(n).clone() for n in m.experts.order})
+    m.dense.grad.zero_()
+    m.experts.grad.zero_()
+    losses = [tr.train_step() for _ in range(steps)]
+    tr.close()
+    dist.destroy_process_group()
+    return {"grads": grads, "losses": losses}
+
+
+def test_expert_parallel_moe_matches_one_rank():
+    one = spawn(_worker, 1, 2, timeout=240)[0]
+    many = spawn(_worker, 4, 2, timeout=300)
+    got = {}
+    for r in many.values():
+        got.update(r["grads"])
+    assert set(got) == set(one["grads"])
+    for name, want in one["grads"].items():
+        err = (got[name] - want).abs().max().item()
+        assert err <= 2e-2 * (want.abs().max().item() + 1e-12), (name, err)
+    for r, res in many.items():
+        for a, b in zip(res["losses"], one["losses"]):
+            assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], one["losses"])
