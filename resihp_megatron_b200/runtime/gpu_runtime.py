@@ -136,7 +136,21 @@ class ParamSetSync:
         if self.impl == "collective" and self.zero:
             self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
 
-    def step(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+    def reduce(self) -> None:
+        """The gradient reduction of the step (nothing for the fused path, which reduces inside
+        ``apply``): an all-reduce (whole optimizer state) or a reduce-scatter into this rank's
+        gradient shard (ZeRO-1)."""
+        P = self.P
+        if self.impl in ("single", "fused"):
+            return
+        if not self.zero:
+            self.wait(dist.all_reduce(P.grad, group=self.group, async_op=True))
+            return
+        self.wait(dist.reduce_scatter_tensor(self.grad_shard, P.grad, group=self.group, async_op=True))
+        P.grad.zero_()
+
+    def apply(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+        """Adam on this rank's optimizer state (after ``reduce``) and the weight gather."""
         P = self.P
         P.step += 1
         if self.impl == "fused":
@@ -144,16 +158,20 @@ class ParamSetSync:
             return
         kw = dict(lr=lr, beta1=betas[0], beta2=betas[1], eps=eps, weight_decay=weight_decay, step=P.step)
         if self.impl == "single" or not self.zero:
-            if self.impl != "single":
-                self.wait(dist.all_reduce(P.grad, group=self.group, async_op=True))
             ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, zero_grad=True, **kw)
             return
-        self.wait(dist.reduce_scatter_tensor(self.grad_shard, P.grad, group=self.group, async_op=True))
-        P.grad.zero_()
         mine = P.shard_slice(P.bf16)
         ops.adam_step(P.master, self.grad_shard, P.exp_avg, P.exp_avg_sq, mine, zero_grad=False, **kw)
         src = mine if dist.get_backend(self.group) == "nccl" else mine.clone()
         self.wait(dist.all_gather_into_tensor(P.bf16, src, group=self.group, async_op=True))
+
+    def step(self, **kw) -> None:
+        self.reduce()
+        self.apply(**kw)
+
+    def discard(self) -> None:
+        """Drop this step's gradients (an aborted iteration)."""
+        self.P.grad.zero_()
 
     def check(self) -> None:
         if self.fdp is not None:
@@ -201,7 +219,7 @@ class HeteroParamSync:
                 self.slices.setdefault(holders, []).append((name, s.shard_dim, iv[0] - s.shard_range[0],
                                                             iv[1] - iv[0]))
 
-    def step(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+    def reduce(self) -> None:
         P = self.P
         for holders, pieces in self.slices.items():
             views = [P.g(name).narrow(dim, lo, ln) for name, dim, lo, ln in pieces]
@@ -212,9 +230,19 @@ class HeteroParamSync:
             for v in views:
                 v.copy_(flat[off:off + v.numel()].view(v.shape))
                 off += v.numel()
+
+    def apply(self, *, lr: float, betas, eps: float, weight_decay: float) -> None:
+        P = self.P
         P.step += 1
         ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, lr=lr, beta1=betas[0], beta2=betas[1],
                       eps=eps, weight_decay=weight_decay, step=P.step, zero_grad=True)
+
+    def step(self, **kw) -> None:
+        self.reduce()
+        self.apply(**kw)
+
+    def discard(self) -> None:
+        self.P.grad.zero_()
 
     def check(self) -> None:
         pass
@@ -307,14 +335,16 @@ class GPUHybridRuntime:
                                   tp_group=tp_pg, progress=progress, hook=hook)
         self.iteration = 0
 
-    def run_iteration(self, iteration: int | None = None) -> torch.Tensor:
+    def run_iteration(self, iteration: int | None = None, step: bool = True) -> torch.Tensor:
         """One training step of this slot; returns the global mean token loss as a 0-d device
-        tensor (no host synchronisation)."""
+        tensor (no host synchronisation).  ``step=False`` stops after the gradient reduction
+        (the resilient loop applies the optimizer step once the iteration is REDUCED)."""
         it = self.iteration if iteration is None else iteration
         self.interp.run(it)
-        kw = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)
-        self.shd_sync.step(**kw)
-        self.rep_sync.step(**kw)
+        self.shd_sync.reduce()
+        self.rep_sync.reduce()
+        if step:
+            self.apply_step()
         loss = self.stage.loss_acc.clone()
         work = dist.all_reduce(loss, async_op=True)
         if self.mgr is not None:
@@ -323,6 +353,15 @@ class GPUHybridRuntime:
             work.wait()
         self.iteration = it + 1
         return loss / self.tokens_per_step
+
+    def apply_step(self) -> None:
+        kw = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)
+        self.shd_sync.apply(**kw)
+        self.rep_sync.apply(**kw)
+
+    def discard_grads(self) -> None:
+        self.shd_sync.discard()
+        self.rep_sync.discard()
 
     def check(self) -> None:
         """Raise if a peer barrier of a fused collective timed out or was aborted."""
