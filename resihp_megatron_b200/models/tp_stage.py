@@ -148,6 +148,7 @@ class TPStage:
         self.loss_acc = torch.zeros((), dtype=torch.float32, device=self.device)
         self.slots: dict[object, _Slot] = {}
         self.free: list[_Slot] = []
+        self.deferred: dict[object, list] = {}
 
     # ------------------------------------------------------------------ parameter views
     def _check_adjacent(self, p: str, names) -> None:
@@ -230,17 +231,28 @@ class TPStage:
         return None
 
     # ------------------------------------------------------------------ backward
-    def backward(self, key, dx_top: torch.Tensor | None = None) -> torch.Tensor | None:
+    def _wgrad(self, deferred, a, b, out, *, copy_a: bool = False, copy_b: bool = False) -> None:
+        """``out += a^T b`` (fp32 accumulate): now, or -- for a zero-bubble schedule -- in the
+        micro-batch's W pass; operands that live in reused buffers (gathered inputs, workspaces)
+        are copied when deferred."""
+        if deferred is None:
+            ops.gemm(a, b, a_t=True, b_t=True, out=out, accumulate=True)
+            return
+        deferred.append((a.clone() if copy_a else a, b.clone() if copy_b else b, out))
+
+    def backward(self, key, dx_top: torch.Tensor | None = None, defer_w: bool = False) -> torch.Tensor | None:
         """Backward of micro-batch ``key`` (after its forward); accumulates both parameter
         sets' gradients and returns the gradient of the stage input rows (None on the first
-        stage)."""
+        stage).  ``defer_w`` (zero-bubble B/W split): only the input-gradient chain runs now;
+        the weight-gradient GEMMs wait for ``weight_backward(key)``."""
         cfg, R, P = self.cfg, self.rep, self.shd
         T, H, D = self.T, cfg.hidden, cfg.head_dim
         slot = self.slots[key]
         dx = self.ws_dx
+        w = [] if defer_w else None
         if self.last:
             ops.gemm(slot.logits, R.w("lm_head"), b_t=True, out=self.ws_dh)
-            ops.gemm(slot.logits, slot.hf, a_t=True, b_t=True, out=R.g("lm_head"), accumulate=True)
+            self._wgrad(w, slot.logits, slot.hf, R.g("lm_head"))
             ops.rmsnorm_bwd(slot.x[-1], R.w("final_norm"), slot.rstd_f, self.ws_dh, R.g("final_norm"), out=dx)
         else:
             dx.copy_(dx_top)
@@ -251,19 +263,19 @@ class TPStage:
             self.tp.chunk(T, H).copy_(dx)
             _, dy = self.tp.ag_gemm(T, P.w(p + "w2"), out=self.ws_da, w_t=True)
             ops.swiglu_fwd(slot.gu[i], out=self.ws_a)
-            ops.gemm(dy, self.ws_a, a_t=True, b_t=True, out=P.g(p + "w2"), accumulate=True)
+            self._wgrad(w, dy, self.ws_a, P.g(p + "w2"), copy_a=True, copy_b=True)
             dgu = ops.swiglu_bwd(slot.gu[i], self.ws_da, out=slot.gu[i])
             self.tp.gemm_rs(dgu, self.w13(p), out=self.ws_dh, w_t=True)
             self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), self.ws_rstd)
             h2 = self.tp.all_gather(T, H)
-            ops.gemm(dgu, h2, a_t=True, b_t=True, out=self.w13(p, grad=True), accumulate=True)
+            self._wgrad(w, dgu, h2, self.w13(p, grad=True), copy_b=True)
             ops.rmsnorm_bwd(slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.ws_dh, R.g(p + "mlp_norm"), dres=dx,
                             out=self.ws_dx2)
             dx2 = self.ws_dx2
             # attention
             self.tp.chunk(T, H).copy_(dx2)
             _, dy = self.tp.ag_gemm(T, P.w(p + "wo"), out=self.ws_do, w_t=True)
-            ops.gemm(dy, slot.o[i], a_t=True, b_t=True, out=P.g(p + "wo"), accumulate=True)
+            self._wgrad(w, dy, slot.o[i], P.g(p + "wo"), copy_a=True)
             q, k, v = self._qkv_views(slot.qkv[i])
             dq, dk, dv = self._qkv_views(self.ws_dqkv)
             ops.attention_bwd(q, k, v, slot.o[i], self.ws_do, slot.lse[i], dq, dk, dv, batch=self.mb, seq=self.S,
@@ -273,12 +285,19 @@ class TPStage:
             self.tp.gemm_rs(self.ws_dqkv, self.wqkv(p), out=self.ws_dh, w_t=True)
             self._rms(slot.x[i], R.w(p + "attn_norm"), self.tp.chunk(T, H), self.ws_rstd)
             h = self.tp.all_gather(T, H)
-            ops.gemm(self.ws_dqkv, h, a_t=True, b_t=True, out=self.wqkv(p, grad=True), accumulate=True)
+            self._wgrad(w, self.ws_dqkv, h, self.wqkv(p, grad=True), copy_a=True, copy_b=True)
             ops.rmsnorm_bwd(slot.x[i], R.w(p + "attn_norm"), slot.rstd1[i], self.ws_dh, R.g(p + "attn_norm"),
                             dres=dx2, out=dx)
         if self.first:
             ops.embedding_bwd(slot.ids, dx, R.g("embed"))
+        if w is None:
             self._release(key)
-            return None
+        else:
+            self.deferred[key] = w
+        return None if self.first else dx
+
+    def weight_backward(self, key) -> None:
+        """The deferred weight-gradient GEMMs of micro-batch ``key`` (zero-bubble W pass)."""
+        for a, b, out in self.deferred.pop(key):
+            ops.gemm(a, b, a_t=True, b_t=True, out=out, accumulate=True)
         self._release(key)
-        return dx

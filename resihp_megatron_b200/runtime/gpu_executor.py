@@ -1,4 +1,4 @@
-"""GPU stage executor for the pipeline IR interpreter: the Llama stage of ``models.tp_stage``.
+"""GPU stage executor for the pipeline IR interpreter: the Llama stages of ``models.tp_stage``.
 
 ``Interpreter`` (``runtime/interpreter.py``) walks this slot's instruction stream and calls
 ``forward`` / ``backward`` per micro-batch; the executor feeds the stage its token rows (first
@@ -39,13 +39,14 @@ class TokenSource:
 
 
 class GPUStageExecutor:
-    """``StageExecutor`` of one (replica, stage) slot running a ``TPStage``."""
+    """``StageExecutor`` of one physical slot running one ``TPStage`` per model chunk (virtual
+    stage); a plan without interleaving has one chunk."""
 
-    def __init__(self, stage, plan: HeteroParallelPlan, replica: int, stage_index: int, rank: int,
-                 tokens: TokenSource, grad_scale: float):
-        self.model = stage
+    def __init__(self, stages: dict, plan: HeteroParallelPlan, replica: int, rank: int, tokens: TokenSource,
+                 grad_scale: float):
+        self.models = dict(stages)
         self.plan = plan
-        self.group = plan.group(replica, stage_index)
+        self.group = plan.group(replica, min(self.models))
         if self.group.cp != 1:
             raise NotImplementedError("context parallelism is not wired into the GPU stage")
         self.ranks = plan.ranks(self.group)
@@ -53,19 +54,23 @@ class GPUStageExecutor:
         self.tokens = tokens
         self.grad_scale = grad_scale
         self.iteration = -1
-        self.device = stage.device
-        self.rows = local_rows(stage.T, self.ranks, rank)
+        first = next(iter(self.models.values()))
+        self.device = first.device
+        self.T = first.T
+        self.rows = local_rows(first.T, self.ranks, rank)
         self._host: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.h2d_bytes = 0
+        self.split_backward = False  # zero-bubble schedules: weight gradients in the W pass
 
     def begin_iteration(self, iteration: int) -> None:
         self.iteration = iteration
         self._host.clear()
-        self.model.loss_acc.zero_()
+        for m in self.models.values():
+            m.loss_acc.zero_()
         self.h2d_bytes = 0
 
     def n_rows(self, mb: int) -> int:
-        return self.model.T
+        return self.T
 
     def _device_rows(self, mb: int, which: int) -> torch.Tensor:
         if mb not in self._host:
@@ -76,19 +81,25 @@ class GPUStageExecutor:
         return host.to(self.device, non_blocking=True)
 
     def forward(self, mb: int, inp: torch.Tensor | None, stage: int) -> torch.Tensor | None:
-        m = self.model
+        m = self.models[stage]
         ids = self._device_rows(mb, 0) if m.first else None
         labels = self._device_rows(mb, 1) if m.last else None
-        return m.forward(mb, ids_local=ids, x_in=inp, labels_local=labels, grad_scale=self.grad_scale)
+        return m.forward((stage, mb), ids_local=ids, x_in=inp, labels_local=labels, grad_scale=self.grad_scale)
 
     def backward(self, mb: int, grad: torch.Tensor | None, stage: int) -> torch.Tensor | None:
-        dx = self.model.backward(mb, grad)
+        dx = self.models[stage].backward((stage, mb), grad, defer_w=self.split_backward)
         # the stage reuses its gradient workspace; the boundary send gets its own copy
         return None if dx is None else dx.clone()
 
     def weight_backward(self, mb: int, stage: int) -> None:
-        raise NotImplementedError("the GPU stage computes weight gradients inside backward (no B/W split)")
+        self.models[stage].weight_backward((stage, mb))
 
     @property
     def loss_sum(self) -> torch.Tensor:
-        return self.model.loss_acc
+        total = None
+        for m in self.models.values():
+            if m.last:
+                total = m.loss_acc if total is None else total + m.loss_acc
+        if total is None:
+            total = next(iter(self.models.values())).loss_acc  # zero: no chunk computes the loss
+        return total

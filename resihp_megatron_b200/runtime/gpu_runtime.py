@@ -58,8 +58,6 @@ def check_supported(plan: HeteroParallelPlan) -> None:
             r = plan.ranks(g)
             if list(r) != sorted(r):
                 raise NotImplementedError(f"group r{g.replica}/s{g.stage}: devices must be in rank order")
-    if plan.vpp != 1:
-        raise NotImplementedError("interleaved stages are not wired into the GPU runtime")
 
 
 def gpu_group_specs(plan: HeteroParallelPlan, schedule: Schedule, tokens_per_microbatch: int,
@@ -272,7 +270,7 @@ class GPUHybridRuntime:
         g: StageGroup = plan.group_of_device(me)
         if g is None:
             raise RuntimeError(f"{me} has no slot in generation {plan.generation} (standby)")
-        self.group, self.replica, self.stage_index = g, g.replica, g.stage
+        self.group, self.replica = g, g.replica
         ranks = plan.ranks(g)
         tp_rank = ranks.index(comms.rank)
         T = micro_batch * self.S
@@ -304,36 +302,64 @@ class GPUHybridRuntime:
                                               if mgr is not None else None)
         else:
             raise ValueError(tp_impl)
-        # data parallelism: the sharded set over the same TP rank of every replica, the
+        # one model chunk per virtual stage this device runs (one without interleaving); data
+        # parallelism per chunk: the sharded set over the same TP rank of every replica, the
         # replicated set over the whole stage
-        stage_groups = plan.groups_at(g.stage)
-        rep_ranks = tuple(sorted(r for h in stage_groups for r in plan.ranks(h)))
-        if stage_is_homogeneous(plan, g.stage):
-            shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
-            self.shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(g.stage, tp_rank)),
-                                         dp_impl, self.device, abort=self.abort, budget_s=budget_s, waiter=waiter,
-                                         zero=zero)
-        else:
-            self.shd_sync = HeteroParamSync(plan, g.stage, comms.rank, comms, self.device, waiter=waiter)
-        self.rep_sync = ParamSetSync(rep_ranks, comms.rank, comms.group(replicated_group_name(g.stage)), dp_impl,
-                                     self.device, abort=self.abort, budget_s=budget_s, waiter=waiter, zero=zero)
-        self.stage = TPStage(cfg, self.device, layers=range(*g.layers), first=g.stage == 0,
-                             last=g.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch,
-                             seq_len=self.S, seed=seed, rep_shard=self.rep_sync.shard, shd_shard=self.shd_sync.shard,
-                             rep_factories=self.rep_sync.factories, shd_factories=self.shd_sync.factories,
-                             init=init)
-        self.rep_sync.attach(self.stage.rep)
-        self.shd_sync.attach(self.stage.shd)
+        self.chunks: dict[int, tuple] = {}
+        for c in plan.groups_of_device(me):
+            stage_groups = plan.groups_at(c.stage)
+            rep_ranks = tuple(sorted(r for h in stage_groups for r in plan.ranks(h)))
+            if stage_is_homogeneous(plan, c.stage):
+                shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
+                shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(c.stage, tp_rank)), dp_impl,
+                                        self.device, abort=self.abort, budget_s=budget_s, waiter=waiter, zero=zero)
+            else:
+                shd_sync = HeteroParamSync(plan, c.stage, comms.rank, comms, self.device, waiter=waiter)
+            rep_sync = ParamSetSync(rep_ranks, comms.rank, comms.group(replicated_group_name(c.stage)), dp_impl,
+                                    self.device, abort=self.abort, budget_s=budget_s, waiter=waiter, zero=zero)
+            stage = TPStage(cfg, self.device, layers=range(*c.layers), first=c.stage == 0,
+                            last=c.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch, seq_len=self.S,
+                            seed=seed, rep_shard=rep_sync.shard, shd_shard=shd_sync.shard,
+                            rep_factories=rep_sync.factories, shd_factories=shd_sync.factories, init=init)
+            rep_sync.attach(stage.rep)
+            shd_sync.attach(stage.shd)
+            self.chunks[c.stage] = (stage, rep_sync, shd_sync)
         self.tokens = tokens or TokenSource(cfg.vocab_size, micro_batch, self.S)
-        self.executor = GPUStageExecutor(self.stage, plan, g.replica, g.stage, comms.rank, self.tokens,
-                                         grad_scale=1.0 / self.tokens_per_step)
+        self.executor = GPUStageExecutor({s_: ch[0] for s_, ch in self.chunks.items()}, plan, g.replica, comms.rank,
+                                         self.tokens, grad_scale=1.0 / self.tokens_per_step)
         stream = schedule[(g.replica, g.stage)]
-        if any(ins.op == Op.W for ins in stream):
-            raise NotImplementedError("zero-bubble (B/W split) schedules are not wired into the GPU stage")
+        self.executor.split_backward = any(ins.op == Op.W for ins in stream)
         p2p = P2PEngine(comms.rank, mgr, channels=channel_map(comms), device=str(self.device))
         self.interp = Interpreter(plan, stream, self.executor, p2p, g.replica, g.stage, (cfg.hidden,), torch.bfloat16,
                                   tp_group=tp_pg, progress=progress, hook=hook)
         self.iteration = 0
+
+    # ------------------------------------------------------------------ chunk views
+    @property
+    def stage(self):
+        """The model chunk (a device runs one unless the plan interleaves stages)."""
+        if len(self.chunks) != 1:
+            raise AttributeError("interleaved plan: use .chunks")
+        return next(iter(self.chunks.values()))[0]
+
+    def _syncs(self):
+        for _, rep_sync, shd_sync in self.chunks.values():
+            yield shd_sync
+            yield rep_sync
+
+    def param_sets(self) -> list[tuple]:
+        """``(FlatParams, sync)`` of every parameter set of every chunk."""
+        out = []
+        for stage, rep_sync, shd_sync in self.chunks.values():
+            out += [(stage.rep, rep_sync), (stage.shd, shd_sync)]
+        return out
+
+    @property
+    def step_count(self) -> int:
+        return next(iter(self.chunks.values()))[0].shd.step
+
+    def inflight(self) -> int:
+        return sum(ch[0].inflight() for ch in self.chunks.values())
 
     def run_iteration(self, iteration: int | None = None, step: bool = True) -> torch.Tensor:
         """One training step of this slot; returns the global mean token loss as a 0-d device
@@ -341,11 +367,11 @@ class GPUHybridRuntime:
         (the resilient loop applies the optimizer step once the iteration is REDUCED)."""
         it = self.iteration if iteration is None else iteration
         self.interp.run(it)
-        self.shd_sync.reduce()
-        self.rep_sync.reduce()
+        for sync in self._syncs():
+            sync.reduce()
         if step:
             self.apply_step()
-        loss = self.stage.loss_acc.clone()
+        loss = self.executor.loss_sum.clone()
         work = dist.all_reduce(loss, async_op=True)
         if self.mgr is not None:
             self.mgr.guarded_wait(work, what="loss all-reduce")
@@ -356,16 +382,16 @@ class GPUHybridRuntime:
 
     def apply_step(self) -> None:
         kw = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)
-        self.shd_sync.apply(**kw)
-        self.rep_sync.apply(**kw)
+        for sync in self._syncs():
+            sync.apply(**kw)
 
     def discard_grads(self) -> None:
-        self.shd_sync.discard()
-        self.rep_sync.discard()
+        for sync in self._syncs():
+            sync.discard()
 
     def check(self) -> None:
         """Raise if a peer barrier of a fused collective timed out or was aborted."""
-        for s in (self.shd_sync, self.rep_sync):
+        for s in self._syncs():
             s.check()
         if hasattr(self.tp, "check"):
             self.tp.check()
@@ -374,7 +400,7 @@ class GPUHybridRuntime:
         """Release the symmetric heaps (before the process groups are destroyed)."""
         if torch.cuda.is_available() and self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
-        for s in (self.shd_sync, self.rep_sync):
+        for s in self._syncs():
             s.close()
         self.tp.close()
         if self.abort is not None:

@@ -58,7 +58,7 @@ def partition_sizes(cfg: GPTConfig) -> tuple[int, ...]:
 
 
 def _sets(rt):
-    return ((rt.stage.rep, rt.rep_sync), (rt.stage.shd, rt.shd_sync))
+    return rt.param_sets()
 
 
 def export_state(rt) -> tuple[dict[str, dict[str, torch.Tensor]], dict[str, tuple[int, int]]]:

@@ -150,7 +150,7 @@ class GPUHybridTrainer:
         rt, old_plan = self.runtime, self.plan
         me = old_plan.world[self.comms.rank]
         state, layout = export_state(rt)
-        step, iteration = rt.stage.shd.step, rt.iteration
+        step, iteration = rt.step_count, rt.iteration
         mark("export")
         gone = {old_plan.world[r] for r in leaving}
         topo = self.topology.without(sorted(gone))

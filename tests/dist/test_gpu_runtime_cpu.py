@@ -20,9 +20,14 @@ def _cfg():
 
 
 def _plan(layout, ids):
-    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup
+    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup, interleave
 
-    if layout == "tp2pp2dp2":
+    if layout == "vpp":  # two physical stages, two chunks each (virtual stages of one layer)
+        groups = (StageGroup(0, 0, ids[0:2], (0, 2)), StageGroup(0, 1, ids[2:4], (2, 4)),
+                  StageGroup(1, 0, ids[4:6], (0, 2)), StageGroup(1, 1, ids[6:8], (2, 4)))
+        plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)), sequence_parallel=True)
+        plan = interleave(plan, 2)
+    elif layout in ("tp2pp2dp2", "zb"):
         groups = (StageGroup(0, 0, ids[0:2], (0, 2)), StageGroup(0, 1, ids[2:4], (2, 4)),
                   StageGroup(1, 0, ids[4:6], (0, 2)), StageGroup(1, 1, ids[6:8], (2, 4)))
         plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)), sequence_parallel=True)
@@ -47,9 +52,11 @@ def _worker(rank, world, port, store_addr, layout, iters):
     cfg = _cfg()
     ids = tuple(f"w{i}" for i in range(world))
     plan = _plan(layout, ids)
-    res = schedule_with_fallback(plan, lambda k, op, mb: 1.0 if op == "F" else 2.0, lambda a, b, kind: 0.1)
+    zb = layout == "zb"
+    res = schedule_with_fallback(plan, lambda k, op, mb: 1.0 if op == "F" else 2.0, lambda a, b, kind: 0.1,
+                                 split_backward=zb)
     schedule = compute_order_to_ir(plan, res.order)
-    validate(plan, schedule)
+    validate(plan, schedule, split_backward=zb)
     specs = gpu_group_specs(plan, schedule, MB * S)
     mgr = ResilientCommManager("gloo", timeout_s=60)
     comms = mgr.build(1, list(ids), ids[rank], specs, store_addr=store_addr, store_prefix=f"{layout}/gen1/")
@@ -58,7 +65,7 @@ def _worker(rank, world, port, store_addr, layout, iters):
     # iteration 0's gradients before any update, reduced over each set's data-parallel group
     rt.interp.run(0)
     grads = {}
-    for P, sync in ((rt.stage.rep, rt.rep_sync), (rt.stage.shd, rt.shd_sync)):
+    for P, sync in rt.param_sets():
         total = P.grad.clone()
         if sync.size > 1:
             dist.all_reduce(total, group=sync.group)
@@ -68,7 +75,7 @@ def _worker(rank, world, port, store_addr, layout, iters):
                            s.shard_range)
         P.grad.zero_()
     losses = [float(rt.run_iteration(it)) for it in range(iters)]
-    out = {"grads": grads, "losses": losses, "inflight": rt.stage.inflight(), "slots": len(rt.stage.free)}
+    out = {"grads": grads, "losses": losses, "inflight": rt.inflight()}
     rt.close()
     mgr.destroy()
     return out
@@ -86,9 +93,11 @@ def _assemble(results):
     return full
 
 
-def test_tp2_pp2_dp2_sequence_parallel_matches_single_rank(store):
+@pytest.mark.parametrize("layout", ["tp2pp2dp2", "zb", "vpp"])
+def test_tp2_pp2_dp2_sequence_parallel_matches_single_rank(store, layout):
+    """1F1B, zero-bubble (B/W split) and interleaved (two chunks per device) schedules."""
     one = spawn(_worker, 1, store, "single", 2, timeout=240)
-    many = spawn(_worker, 8, store, "tp2pp2dp2", 2, timeout=300)
+    many = spawn(_worker, 8, store, layout, 2, timeout=300)
     ref, got = _assemble(one), _assemble(many)
     assert set(ref) == set(got)
     for name in ref:
