@@ -71,7 +71,9 @@ def migrate_p2p(plan: TransferPlan, me: str, world: list[str], *, specs: dict[st
     if _stage:
         stage = heap.tensor("stage")
         for (key, kind), off in tables[me][0].items():
-            t = old_state[kind][key]
+            t = old_state.get(kind, {}).get(key)
+            if t is None:  # held under the old plan but not up to date: never chosen as a source
+                continue
             stage[off // 4: off // 4 + t.numel()].copy_(t.reshape(-1))
         if not emulated:
             heap.barrier(budget_s)

@@ -98,3 +98,35 @@ def import_state(rt, state: dict[str, dict[str, torch.Tensor]], step: int) -> No
             for kind, buf in zip(KINDS, (P.master, P.exp_avg, P.exp_avg_sq)):
                 buf[b:b + n].copy_(state[kind][name].reshape(-1)[a:a + n])
         P.step = step
+
+
+def local_layout(rt) -> dict[str, tuple[int, int]]:
+    """Interval of every key this rank holds (its TP dimension; ``FULL`` when replicated)."""
+    out = {}
+    for P, _ in _sets(rt):
+        for name in P.order:
+            s = P.specs[name]
+            out[name] = tuple(s.shard_range) if s.shard_dim is not None else FULL
+    return out
+
+
+def checkpoint_slices(rt, specs: dict[str, TensorSpec]):
+    """This rank's state as checkpoint slices ``[(SliceMeta, {kind: tensor})]`` (collective over
+    ZeRO-sharded data-parallel groups, like ``export_state``)."""
+    from ..state.checkpoint import SliceMeta
+
+    state, layout = export_state(rt)
+    return [(SliceMeta(key, specs[key].global_shape, specs[key].dim, tuple(iv)), {k: state[k][key] for k in KINDS})
+            for key, iv in layout.items()]
+
+
+def load_checkpoint_into(rt, checkpointer, iteration: int, specs: dict[str, TensorSpec]) -> None:
+    """Assemble this rank's slices of every key from checkpoint ``iteration`` (whatever layout
+    wrote it: reshard on load) and load them; the optimizer step count becomes ``iteration + 1``."""
+    from ..state.checkpoint import SliceMeta
+
+    wanted = [SliceMeta(key, specs[key].global_shape, specs[key].dim, iv) for key, iv in local_layout(rt).items()]
+    got = checkpointer.load(iteration, wanted, KINDS)
+    dev = rt.device
+    state = {k: {key: got[key][k].to(dev) for key in got} for k in KINDS}
+    import_state(rt, state, step=iteration + 1)

@@ -28,9 +28,11 @@ from ..state.transaction import TransactionManager
 class GPUHybridBinding:
     def __init__(self, cfg: GPTConfig, client, mgr, *, micro_batch: int = 1, seq_len: int | None = None,
                  device="cuda", tp_impl: str = "collective", lr: float = 3e-4, seed: int = 0, data_seed: int = 1,
-                 migrate: str = "auto", hook=None):
+                 migrate: str = "auto", hook=None, checkpointer=None, checkpoint_interval: int = 0):
         """``migrate``: ``"p2p"`` (peer copies over NVLink), ``"engine"`` (NCCL / gloo send-receive)
-        or ``"auto"`` (p2p on GPUs)."""
+        or ``"auto"`` (p2p on GPUs).  ``checkpointer`` (``state.checkpoint.SliceCheckpointer``):
+        every ``checkpoint_interval`` committed iterations each rank writes its slices; a plan
+        that asks to restore (no surviving holder of some slice) loads the newest complete one."""
         self.cfg, self.client, self.mgr = cfg, client, mgr
         self.micro_batch = micro_batch
         self.S = seq_len or cfg.seq_len
@@ -39,6 +41,7 @@ class GPUHybridBinding:
         self.tokens = TokenSource(cfg.vocab_size, micro_batch, self.S, seed=data_seed)
         self.migrate = ("p2p" if self.device.type == "cuda" else "engine") if migrate == "auto" else migrate
         self.hook = hook
+        self.checkpointer, self.checkpoint_interval = checkpointer, checkpoint_interval
         self.me = client.worker_id
         self.committed = None  # (plan, runtime)
         self.pending = None
@@ -82,7 +85,18 @@ class GPUHybridBinding:
             txm.discard()
         rt = self._runtime(plan, schedule, comms, init=old is None or target < 0)
         prev = payload.get("previous_plan")
-        if old is not None and prev is not None and target >= 0:
+        if rec.get("restore"):
+            from ..runtime.gpu_state import load_checkpoint_into
+
+            if self.checkpointer is None:
+                raise RuntimeError("restore requested but no checkpointer is configured")
+            specs = gpu_tensor_specs(self.cfg)
+            it = self.checkpointer.latest_complete({k: (sp.global_shape, sp.dim) for k, sp in specs.items()})
+            if it is None:
+                raise RuntimeError("no complete checkpoint to restore from")
+            load_checkpoint_into(rt, self.checkpointer, it, specs)
+            txm.adopt(it)
+        elif prev is not None and target >= 0:
             specs = gpu_tensor_specs(self.cfg)
             layer_of = gpu_layer_of(self.cfg.layers)
             old_plan = HeteroParallelPlan.from_json(prev)
@@ -91,7 +105,7 @@ class GPUHybridBinding:
             tplan = plan_transfers(old_h, new_h, valid_sources=valid, node_of=payload.get("nodes", {}))
             if tplan.lost:
                 raise RuntimeError(f"{len(tplan.lost)} state slices have no surviving holder")
-            mine_valid = self.me in valid
+            mine_valid = old is not None and self.me in valid
             state, layout = export_state(old[1]) if mine_valid else ({k: {} for k in KINDS}, {})
             t0 = time.monotonic()
             new_layout = device_layout(new_h, self.me)
@@ -139,7 +153,13 @@ class GPUHybridBinding:
         self.committed[1].discard_grads()
 
     def after_commit(self, iteration: int, comms) -> None:
-        pass
+        if not (self.checkpointer and self.checkpoint_interval and (iteration + 1) % self.checkpoint_interval == 0):
+            return
+        from ..runtime.gpu_state import checkpoint_slices, gpu_tensor_specs
+
+        rt = self.committed[1]
+        self.checkpointer.save(iteration, self.me, checkpoint_slices(rt, gpu_tensor_specs(self.cfg)),
+                               extra={"step_count": rt.step_count}, blocking=True)
 
     def try_resume(self, txm: TransactionManager) -> None:
         pass

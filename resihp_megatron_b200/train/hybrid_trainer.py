@@ -116,6 +116,37 @@ class GPUHybridTrainer:
     def check(self) -> None:
         self.runtime.check()
 
+    # ------------------------------------------------------------------ checkpoints (T2)
+    def save_checkpoint(self, directory) -> int:
+        """Write this rank's slices of the last completed step to ``directory`` in the shared
+        slice-checkpoint format (every rank calls it; collective inside ZeRO data-parallel
+        groups).  Returns the checkpoint's iteration."""
+        from ..runtime.gpu_state import checkpoint_slices, gpu_tensor_specs
+        from ..state.checkpoint import SliceCheckpointer
+
+        it = self.runtime.iteration - 1
+        me = self.plan.world[self.comms.rank]
+        ck = SliceCheckpointer(directory)
+        ck.save(it, me, checkpoint_slices(self.runtime, gpu_tensor_specs(self.cfg)),
+                extra={"step_count": self.runtime.step_count, "layout": self.layout}, blocking=True)
+        return it
+
+    def load_checkpoint(self, directory, iteration: int | None = None) -> int:
+        """Load the newest complete checkpoint (or ``iteration``) from ``directory``, whatever
+        layout wrote it, and continue from the step after it."""
+        from ..runtime.gpu_state import gpu_tensor_specs, load_checkpoint_into
+        from ..state.checkpoint import SliceCheckpointer
+
+        specs = gpu_tensor_specs(self.cfg)
+        ck = SliceCheckpointer(directory)
+        if iteration is None:
+            iteration = ck.latest_complete({k: (s.global_shape, s.dim) for k, s in specs.items()})
+            if iteration is None:
+                raise FileNotFoundError(f"no complete checkpoint under {directory}")
+        load_checkpoint_into(self.runtime, ck, iteration, specs)
+        self.runtime.iteration = iteration + 1
+        return iteration
+
     # ------------------------------------------------------------------ live reconfiguration
     def reconfigure(self, leaving: list[int], *, store=None, store_addr=None, store_prefix: str | None = None) -> bool:
         """Planned removal of the ranks ``leaving`` (e.g. a GPU evicted as fail-slow), between

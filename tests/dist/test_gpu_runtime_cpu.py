@@ -185,3 +185,39 @@ def test_live_eviction_replans_migrates_and_continues_the_same_run(store):
         for a, b in zip(res[r]["losses"], ref):
             assert abs(a - b) <= 1e-2 * abs(b), (r, res[r]["losses"], ref)
         assert res[r]["phases"]["migrate"] >= 0
+
+
+def _ckpt(rank, world, port, layout, directory, phase):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tp, pp, dp = layout
+    tr = GPUHybridTrainer(_cfg(), tp=tp, pp=pp, dp=dp, global_batch=4, micro_batch=1, seq_len=S,
+                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2)
+    if phase == "save":
+        losses = [tr.train_step() for _ in range(2)]
+        tr.save_checkpoint(directory)
+    elif phase == "load":
+        assert tr.load_checkpoint(directory) == 1
+        losses = [tr.train_step() for _ in range(2)]
+    else:
+        losses = [tr.train_step() for _ in range(4)]
+    tr.close()
+    dist.destroy_process_group()
+    return losses
+
+
+def test_checkpoint_written_by_one_layout_resumes_in_another(tmp_path):
+    """TP2 x PP2 x DP2 (ZeRO-sharded optimizer) writes slices; TP1 x PP2 x DP2 reads them
+    (reshard on load) and continues the run of one rank."""
+    ref = spawn(_ckpt, 1, (1, 1, 1), str(tmp_path), "ref", timeout=240)[0]
+    first = spawn(_ckpt, 8, (2, 2, 2), str(tmp_path), "save", timeout=300)
+    second = spawn(_ckpt, 4, (1, 2, 2), str(tmp_path), "load", timeout=300)
+    got = first[0] + second[0]
+    for a, b in zip(got, ref):
+        assert abs(a - b) <= 1e-2 * abs(b), (got, ref)
