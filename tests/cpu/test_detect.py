@@ -3,13 +3,12 @@ DetectorService with a fake coordinator, validation rounds, and the native NCCL 
 driven through its v5 ABI with ctypes (no NCCL needed)."""
 
 import ctypes
-import math
 
 import numpy as np
 import pytest
 
 from resihp_megatron_b200.detect.bocd import BOCD
-from resihp_megatron_b200.detect.failslow import FailSlowDetector, localize
+from resihp_megatron_b200.detect.failslow import localize
 from resihp_megatron_b200.detect.policy import SkiRentalPolicy
 from resihp_megatron_b200.detect.predictor import RLSPredictor, fit_least_squares
 from resihp_megatron_b200.detect.service import DetectorService

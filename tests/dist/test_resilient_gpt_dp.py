@@ -5,7 +5,6 @@ bitwise equal to single-process training."""
 
 import json
 import os
-import subprocess
 import sys
 import time
 from pathlib import Path
