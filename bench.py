@@ -432,9 +432,39 @@ def run_moe(args, rank: int, world: int, local: int) -> None:
                             ep_impl="peer" if args.ep_impl == "peer" else "collective",
                             dp_impl="fused" if args.dp_impl == "fused" else "collective")
     r = _timed_region(args, trainer, rank, world, local)
+    recfg = None
+    if args.reconfig and world > 1:
+        # fail-slow re-placement: the last rank is taken as 2x slower (its speed is given here; the
+        # residual-BOCD detector that would report it is exercised separately), the planner
+        # replicates / moves its experts and their state migrates peer to peer
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        info = trainer.replace_experts({world - 1: 0.5})
+        commit_s = time.perf_counter() - t0
+        for _ in range(max(2, min(args.warmup, 3))):
+            trainer.step_device()
+        torch.cuda.synchronize()
+        trainer.check()
+        dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            trainer.step_device()
+        end.record()
+        torch.cuda.synchronize()
+        vals = torch.tensor([start.elapsed_time(end), commit_s], device=trainer.device, dtype=torch.float64)
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        post_ms, commit_max = vals.tolist()
+        recfg = {"kind": "fail-slow expert re-placement (last rank at half speed), expert state migrated",
+                 "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
+                 "post_ms_per_step": post_ms / args.steps, "replace_to_commit_s": commit_max,
+                 "holders": info["holders"], "phases_s_rank0": {k: v for k, v in info.items() if k != "holders"}}
     if rank == 0:
         out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r,
                          {"experts": cfg.num_experts, "top_k": cfg.top_k})
+        if recfg is not None:
+            out["reconfig"] = recfg
         print(json.dumps(out), flush=True)
     dist.barrier()
     trainer.close()

@@ -43,15 +43,17 @@ def moe_param_specs(cfg: GPTConfig, local_experts: list[int]) -> tuple[list[Para
 
 
 class MoEModel:
-    def __init__(self, cfg: GPTConfig, device, *, ep, holder: list[int], rank: int, micro_batch: int = 1,
+    def __init__(self, cfg: GPTConfig, device, *, ep, holder: list, rank: int, micro_batch: int = 1,
                  seq_len: int | None = None, seed: int = 0, dense_shard: tuple[int, int] = (0, 1),
                  dense_factories=(None, None), init: bool = True):
+        """``holder[e]``: the rank of expert ``e`` or the list of its replicas' ranks."""
         if not cfg.is_moe:
             raise ValueError("MoEModel needs a config with experts")
         self.cfg, self.device = cfg, torch.device(device)
         self.ep = ep
-        self.holder = list(holder)
-        self.local = [e for e in range(cfg.num_experts) if holder[e] == rank]
+        self.seed = seed
+        self.holders = [list(h) if isinstance(h, (list, tuple)) else [int(h)] for h in holder]
+        self.local = [e for e in range(cfg.num_experts) if rank in self.holders[e]]
         self.mb = micro_batch
         self.S = seq_len or cfg.seq_len
         self.T = self.mb * self.S
@@ -64,6 +66,15 @@ class MoEModel:
             self.experts.initialize(seed, cfg.init_std)
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
         self._alloc()
+
+    def rebuild_experts(self, holders: list, rank: int, ep) -> None:
+        """Switch to a new expert placement: fresh (uninitialised) expert buffers for the experts
+        this rank now holds, to be filled with migrated state, and the new transport."""
+        self.holders = [list(h) if isinstance(h, (list, tuple)) else [int(h)] for h in holders]
+        self.local = [e for e in range(self.cfg.num_experts) if rank in self.holders[e]]
+        _, experts = moe_param_specs(self.cfg, self.local)
+        self.experts = FlatParams(experts, self.device)
+        self.ep = ep
 
     def _alloc(self) -> None:
         c, T, dev = self.cfg, self.T, self.device

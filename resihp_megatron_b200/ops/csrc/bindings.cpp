@@ -501,16 +501,29 @@ void moe_positions(const torch::Tensor& topi, int64_t E, torch::Tensor& pos, tor
                             cur_stream()), "moe_positions");
 }
 
+// `routes`: int32 [E, 2 * 64 + 16] = cycle (64) | cycle rank (64) | per-cycle slots per holder (16);
+// `period`: int32 [E]; `rowbase`: int64 [E, 16] (see MoeRoutes in moe.cu).
 void moe_dispatch(const torch::Tensor& x, const torch::Tensor& topi, const torch::Tensor& pos, int64_t k,
-                  int64_t me, const torch::Tensor& holder, const torch::Tensor& rowbase,
+                  int64_t me, const torch::Tensor& period, const torch::Tensor& routes, const torch::Tensor& rowbase,
                   const std::vector<int64_t>& recv, torch::Tensor& route_row) {
   CHECK_BF16(x);
+  const int E = static_cast<int>(period.numel());
+  TORCH_CHECK(routes.is_contiguous() && routes.scalar_type() == torch::kInt32 && routes.numel() == E * (2 * 64 + 16),
+              "moe_dispatch: routes must be int32 [E, 144]");
+  TORCH_CHECK(rowbase.is_contiguous() && rowbase.scalar_type() == torch::kInt64 && rowbase.numel() == E * 16,
+              "moe_dispatch: rowbase must be int64 [E, 16]");
   const c10::cuda::CUDAGuard g(x.device());
   auto r = as_ptrs(recv);
+  // split the packed table into its three [E, ...] arrays (device copies, row-major)
+  auto cyc = routes.view({E, 144});
+  auto cycle = cyc.narrow(1, 0, 64).contiguous();
+  auto cycle_rank = cyc.narrow(1, 64, 64).contiguous();
+  auto per_cycle = cyc.narrow(1, 128, 16).contiguous();
   RB_CALL(rb::moe_dispatch(x.data_ptr(), topi.data_ptr<int>(), pos.data_ptr<int>(), x.size(0), k, x.size(1),
-                           static_cast<int>(r.size()), me, holder.numel(), holder.data_ptr<int>(),
-                           rowbase.data_ptr<int64_t>() ? reinterpret_cast<const long long*>(rowbase.data_ptr<int64_t>()) : nullptr,
-                           r.data(), reinterpret_cast<long long*>(route_row.data_ptr<int64_t>()), cur_stream()),
+                           static_cast<int>(r.size()), me, E, period.data_ptr<int>(), cycle.data_ptr<int>(),
+                           cycle_rank.data_ptr<int>(), per_cycle.data_ptr<int>(),
+                           reinterpret_cast<const long long*>(rowbase.data_ptr<int64_t>()), r.data(),
+                           reinterpret_cast<long long*>(route_row.data_ptr<int64_t>()), cur_stream()),
           "moe_dispatch");
 }
 

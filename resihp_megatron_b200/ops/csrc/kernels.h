@@ -96,7 +96,8 @@ int moe_route(const void* x, const void* w, const float* bias, int T, int H, int
               float* gates, cudaStream_t s);
 int moe_positions(const int* topi, int n, int E, int* pos, int* counts, cudaStream_t s);
 int moe_dispatch(const void* x, const int* topi, const int* pos, int T, int k, int H, int world, int me, int E,
-                 const int* holder, const long long* rowbase, void* const* recv, long long* route_row, cudaStream_t s);
+                 const int* period, const int* cycle, const int* cycle_rank, const int* per_cycle,
+                 const long long* rowbase, void* const* recv, long long* route_row, cudaStream_t s);
 int moe_combine(const void* residual, const float* gates, const long long* route_row, int T, int k, int H, int world,
                 void* const* ybuf, void* out, void* ycache, cudaStream_t s);
 int moe_grad_push(const void* dout, const float* gates, const void* ycache, const long long* route_row, int T, int k,

@@ -146,11 +146,19 @@ __global__ void __launch_bounds__(kPosThreads) moe_positions_kernel(const int* _
   }
 }
 
+// An expert may have several holders (replicas); the (token, slot) pairs of expert e are dealt to
+// them in a fixed cycle: position p (the pair's rank among this source's pairs of e) goes to
+// cycle[e][p % period[e]] -- a speed-weighted round robin whose pattern repeats every period.
+constexpr int kMaxPeriod = 64;
+
 struct MoeRoutes {
   int world, me, E, k;
-  const int* holder;      // [E] rank holding expert e
-  const long long* rowbase;  // [E] first receive row of (expert e, source me) at its holder
-  void* peers[kMaxE];     // receive buffers of every rank ([rows, H] bf16)
+  const int* period;          // [E] cycle length (1: a single holder)
+  const int* cycle;           // [E][kMaxPeriod] holder rank of cycle slot j
+  const int* cycle_rank;      // [E][kMaxPeriod] rank of slot j among the slots with the same holder
+  const int* per_cycle;       // [E][kMaxE] slots of holder h in one cycle
+  const long long* rowbase;   // [E][kMaxE] first receive row of (expert e, source me) at holder h
+  void* peers[kMaxE];         // receive buffers of every rank ([rows, H] bf16)
 };
 
 __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ topi,
@@ -160,8 +168,11 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, const i
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
   const int t = i / k, e = topi[i];
-  const int h = r.holder[e];
-  const long long row = r.rowbase[e] + pos[i];
+  const int p = pos[i], L = r.period[e];
+  const int j = p % L;
+  const int h = r.cycle[e * kMaxPeriod + j];
+  const long long row = r.rowbase[e * kMaxE + h] + static_cast<long long>(p / L) * r.per_cycle[e * kMaxE + h] +
+                        r.cycle_rank[e * kMaxPeriod + j];
   if (lane == 0) route_row[i] = row * kMaxE + h;  // holder packed into the row index
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(t) * H);
   uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(r.peers[h]) + row * H);
@@ -292,15 +303,12 @@ __global__ void moe_grad_pull_kernel(const __nv_bfloat16* __restrict__ dout, con
   }
 }
 
-MoeRoutes make_routes(int world, int me, int E, int k, const int* holder, const long long* rowbase,
-                      void* const* peers) {
+MoeRoutes make_routes(int world, int me, int E, int k, void* const* peers) {
   MoeRoutes r{};
   r.world = world;
   r.me = me;
   r.E = E;
   r.k = k;
-  r.holder = holder;
-  r.rowbase = rowbase;
   for (int i = 0; i < world; ++i) r.peers[i] = peers[i];
   return r;
 }
@@ -323,9 +331,15 @@ int moe_positions(const int* topi, int n, int E, int* pos, int* counts, cudaStre
 }
 
 int moe_dispatch(const void* x, const int* topi, const int* pos, int T, int k, int H, int world, int me, int E,
-                 const int* holder, const long long* rowbase, void* const* recv, long long* route_row, cudaStream_t s) {
-  if (world > kMaxE || H % 8) return -1;
-  const MoeRoutes r = make_routes(world, me, E, k, holder, rowbase, recv);
+                 const int* period, const int* cycle, const int* cycle_rank, const int* per_cycle,
+                 const long long* rowbase, void* const* recv, long long* route_row, cudaStream_t s) {
+  if (world > kMaxE || E > kMaxE || H % 8) return -1;
+  MoeRoutes r = make_routes(world, me, E, k, recv);
+  r.period = period;
+  r.cycle = cycle;
+  r.cycle_rank = cycle_rank;
+  r.per_cycle = per_cycle;
+  r.rowbase = rowbase;
   const int n = T * k;
   moe_dispatch_kernel<<<(n * 32 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), topi, pos, n,
                                                          k, H, r, route_row);
@@ -335,7 +349,7 @@ int moe_dispatch(const void* x, const int* topi, const int* pos, int T, int k, i
 int moe_combine(const void* residual, const float* gates, const long long* route_row, int T, int k, int H, int world,
                 void* const* ybuf, void* out, void* ycache, cudaStream_t s) {
   if (world > kMaxE || H % 8) return -1;
-  const MoeRoutes r = make_routes(world, 0, 0, k, nullptr, nullptr, ybuf);
+  const MoeRoutes r = make_routes(world, 0, 0, k, ybuf);
   moe_combine_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(residual), gates,
                                                         route_row, T, k, H, r, reinterpret_cast<__nv_bfloat16*>(out),
                                                         reinterpret_cast<__nv_bfloat16*>(ycache));
@@ -345,7 +359,7 @@ int moe_combine(const void* residual, const float* gates, const long long* route
 int moe_grad_push(const void* dout, const float* gates, const void* ycache, const long long* route_row, int T, int k,
                   int H, int world, void* const* dyrecv, float* dgate, cudaStream_t s) {
   if (world > kMaxE || H % 8) return -1;
-  const MoeRoutes r = make_routes(world, 0, 0, k, nullptr, nullptr, dyrecv);
+  const MoeRoutes r = make_routes(world, 0, 0, k, dyrecv);
   const int n = T * k;
   moe_grad_push_kernel<<<(n * 32 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(dout), gates,
                                                           reinterpret_cast<const __nv_bfloat16*>(ycache), route_row,
@@ -357,7 +371,7 @@ int moe_grad_pull(const void* dout, const float* gates, const float* dgate, cons
                   const long long* route_row, int T, int k, int H, int E, int world, void* const* dxbuf, void* dx,
                   float* dlogits, cudaStream_t s) {
   if (world > kMaxE || H % 8) return -1;
-  const MoeRoutes r = make_routes(world, 0, E, k, nullptr, nullptr, dxbuf);
+  const MoeRoutes r = make_routes(world, 0, E, k, dxbuf);
   moe_grad_pull_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(dout), gates,
                                                           dgate, topi, route_row, T, k, H, E, r,
                                                           reinterpret_cast<__nv_bfloat16*>(dx), dlogits);

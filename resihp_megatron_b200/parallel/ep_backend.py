@@ -15,17 +15,22 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
-from .moe_ep import receive_layout
+from .moe_ep import replica_cycles, replica_layout, split_count
 
 
 class CollectiveEP:
     def __init__(self, rank: int, world: int, group, device, *, hidden: int, num_experts: int, top_k: int,
-                 holder: list[int], waiter=None):
+                 holder: list, waiter=None, speeds: dict[int, float] | None = None):
         self.rank, self.world, self.group = rank, world, group
         self.H, self.E, self.k = hidden, num_experts, top_k
-        self.holder = list(holder)
-        self.local = [e for e in range(num_experts) if holder[e] == rank]
+        self.holders = [list(h) if isinstance(h, (list, tuple)) else [int(h)] for h in holder]
+        self.cycles = replica_cycles(self.holders, speeds)
+        self.local = [e for e in range(num_experts) if rank in self.holders[e]]
         self.device = torch.device(device)
+        L = max(len(c) for c in self.cycles)
+        self._cycle_t = torch.tensor([c + [c[0]] * (L - len(c)) for c in self.cycles], dtype=torch.int64,
+                                     device=self.device)
+        self._period_t = torch.tensor([len(c) for c in self.cycles], dtype=torch.int64, device=self.device)
         self.wait = waiter or (lambda w: w.wait())
         self.saved: dict = {}
 
@@ -49,11 +54,17 @@ class CollectiveEP:
         topi = sel.topk(self.k, dim=-1).indices
         gates = torch.softmax(logits.gather(-1, topi), dim=-1)
         flat = topi.reshape(-1)
+        n = flat.numel()
+        idx = torch.arange(n, device=flat.device)
         counts = torch.bincount(flat, minlength=self.E).to(torch.int64)
-        # send order of the (token, slot) pairs: by holder, then expert, then token-major position
-        holder = torch.tensor(self.holder, dtype=torch.int64, device=flat.device)
-        key = (holder[flat] * self.E + flat) * (flat.numel() + 1) + torch.arange(flat.numel(), device=flat.device)
-        order = torch.argsort(key)
+        # position of every (token, slot) pair among this rank's pairs of its expert (token-major)
+        by_expert = torch.argsort(flat * (n + 1) + idx)
+        first = torch.cumsum(counts, 0) - counts
+        pos = torch.empty_like(flat)
+        pos[by_expert] = idx - first[flat[by_expert]]
+        holder = self._cycle_t[flat, pos % self._period_t[flat]]
+        # send order: by holder, then expert, then position
+        order = torch.argsort((holder * self.E + flat) * (n + 1) + idx)
         self.saved = {"x": x, "topi": topi, "gates": gates, "T": x.shape[0], "counts": counts, "order": order}
 
     def exchange_counts(self) -> None:
@@ -70,22 +81,27 @@ class CollectiveEP:
 
     def _layout(self, table: torch.Tensor) -> None:
         s = self.saved
+        tab = table.tolist()
         s["table"] = table
-        rowbase, ranges = receive_layout(table, self.holder, self.rank, self.world)
+        _, ranges = replica_layout(tab, self.cycles, self.rank, self.world)
         s["local_ranges"] = ranges
         s["recv_rows"] = sum(n for _, n in ranges)
-        # what this rank sends to holder h: its rows of h's experts, expert order, token-major
-        s["send_splits"] = [sum(int(table[self.rank][e]) for e in range(self.E) if self.holder[e] == h)
-                            for h in range(self.world)]
-        # what this rank receives from source r: r's rows of this rank's experts, in expert order
-        s["recv_splits"] = [sum(int(table[r][e]) for e in self.local) for r in range(self.world)]
+        me, W, E = self.rank, self.world, self.E
+
+        def cnt(src: int, e: int, h: int) -> int:
+            return split_count(tab[src][e], self.cycles[e], h)
+
+        # what this rank sends to holder h: its pairs dealt to h, expert order, position order
+        s["send_splits"] = [sum(cnt(me, e, h) for e in range(E)) for h in range(W)]
+        # what this rank receives from source r: r's pairs of this rank's experts, expert order
+        s["recv_splits"] = [sum(cnt(r, e, me) for e in self.local) for r in range(W)]
         # receive order (source-major, expert) -> expert-major rows of the layout
         perm = []
         starts = {e: lo for e, (lo, _) in zip(self.local, ranges)}
-        for r in range(self.world):
+        for r in range(W):
             for e in self.local:
-                base = starts[e] + sum(int(table[q][e]) for q in range(r))
-                perm.extend(range(base, base + int(table[r][e])))
+                base = starts[e] + sum(cnt(q, e, me) for q in range(r))
+                perm.extend(range(base, base + cnt(r, e, me)))
         s["perm"] = torch.tensor(perm, dtype=torch.int64, device=self.device)
 
     def dispatch(self) -> None:

@@ -28,33 +28,77 @@ from ..ops._build import ext
 from .symm import AbortWord, SymmetricHeap
 
 
-def receive_layout(table, holder: list[int], me: int, world: int) -> tuple[list[int], list[tuple[int, int]]]:
+PERIOD_MAX = 64  # longest replica cycle the dispatch kernel takes
+HOLDERS_MAX = 16
+
+
+def replica_cycles(holders: list[list[int]], speeds: dict[int, float] | None = None) -> list[list[int]]:
+    """Per expert, the holder of every slot of its dealing cycle: the (token, slot) pair at
+    position ``p`` of expert ``e`` on any source goes to ``cycle[e][p % len(cycle[e])]`` -- one
+    period of the speed-weighted smooth round robin the CPU runtime uses
+    (``plan.expert_placement.smooth_weighted_round_robin``, integer weights ``10 * speed``)."""
+    from ..plan.expert_placement import smooth_weighted_round_robin
+
+    speeds = speeds or {}
+    out = []
+    for hs in holders:
+        hs = list(hs)
+        if len(hs) == 1:
+            out.append(hs)
+            continue
+        period = sum(max(1, round(10 * speeds.get(h, 1.0))) for h in hs)
+        if period > PERIOD_MAX:
+            raise ValueError(f"replica cycle of {period} slots exceeds {PERIOD_MAX}")
+        out.append(smooth_weighted_round_robin(hs, speeds, period))
+    return out
+
+
+def split_count(count: int, cycle: list[int], holder: int) -> int:
+    """Pairs among the first ``count`` positions of an expert that its cycle deals to ``holder``."""
+    full, rem = divmod(int(count), len(cycle))
+    return full * cycle.count(holder) + cycle[:rem].count(holder)
+
+
+def replica_layout(table, cycles: list[list[int]], me: int, world: int):
     """Receive rows of a step from the count table ``table[source][expert]``: at every holder its
-    local experts in expert order, each expert's rows ordered by source rank.  Returns, for
-    source ``me``, the first row of each expert ``e`` at ``holder[e]`` (``rowbase[e]``), and for
-    ``me`` as a holder the (first row, rows) range of each of its experts."""
-    E = len(holder)
-    totals = [int(sum(int(table[s][e]) for s in range(world))) for e in range(E)]
-    start = [0] * E
+    experts in expert order, each expert's rows ordered by source rank, then by position.  Returns
+    ``rowbase[e][h]`` -- the first row, at holder ``h``, of this source's (``me``'s) pairs of
+    expert ``e`` -- and, for ``me`` as a holder, the ``(first row, rows)`` range of each expert it
+    holds (expert order)."""
+    E = len(cycles)
+    cnt = [[[split_count(table[s][e], cycles[e], h) for h in range(world)] for e in range(E)] for s in range(world)]
+    start: dict[tuple[int, int], int] = {}
     for h in range(world):
         off = 0
         for e in range(E):
-            if holder[e] == h:
-                start[e] = off
-                off += totals[e]
-    rowbase = [start[e] + sum(int(table[s][e]) for s in range(me)) for e in range(E)]
-    ranges = [(start[e], totals[e]) for e in range(E) if holder[e] == me]
+            if h in cycles[e]:
+                start[(e, h)] = off
+                off += sum(cnt[s][e][h] for s in range(world))
+    rowbase = [[0] * world for _ in range(E)]
+    for (e, h), lo in start.items():
+        rowbase[e][h] = lo + sum(cnt[s][e][h] for s in range(me))
+    ranges = [(start[(e, me)], sum(cnt[s][e][me] for s in range(world))) for e in range(E) if me in cycles[e]]
     return rowbase, ranges
+
+
+def receive_layout(table, holder: list[int], me: int, world: int) -> tuple[list[int], list[tuple[int, int]]]:
+    """``replica_layout`` for one holder per expert: ``rowbase[e]`` at ``holder[e]``."""
+    rowbase, ranges = replica_layout(table, [[h] for h in holder], me, world)
+    return [rowbase[e][holder[e]] for e in range(len(holder))], ranges
 
 
 class ExpertParallelMoE:
     def __init__(self, rank: int, world: int, exchange, device, *, hidden: int, num_experts: int, top_k: int,
-                 max_tokens: int, holder: list[int], abort: AbortWord | None = None, budget_s: float = 30.0,
-                 _heap: SymmetricHeap | None = None):
+                 max_tokens: int, holder: list, abort: AbortWord | None = None, budget_s: float = 30.0,
+                 speeds: dict[int, float] | None = None, _heap: SymmetricHeap | None = None):
+        """``holder[e]``: the rank of expert ``e``, or the list of its replicas' ranks (the pairs
+        routed to a replicated expert are dealt to its replicas by ``replica_cycles`` with
+        ``speeds``)."""
         self.rank, self.world = rank, world
         self.H, self.E, self.k = hidden, num_experts, top_k
-        self.holder = list(holder)
-        self.local = [e for e in range(num_experts) if holder[e] == rank]
+        self.holders = [list(h) if isinstance(h, (list, tuple)) else [int(h)] for h in holder]
+        self.cycles = replica_cycles(self.holders, speeds)
+        self.local = [e for e in range(num_experts) if rank in self.holders[e]]
         self.max_rows = max_tokens * world * max(1, len(self.local))
         self.device = torch.device(device)
         self.abort, self.budget = abort, budget_s
@@ -63,15 +107,23 @@ class ExpertParallelMoE:
                 "dyrecv": (self.max_rows * hidden, torch.bfloat16), "dxrecv": (self.max_rows * hidden, torch.bfloat16)}
         self.heap = _heap or SymmetricHeap(segs, rank, world, exchange, device, abort)
         self.emulated = _heap is not None
-        self.holder_t = torch.tensor(self.holder, dtype=torch.int32, device=self.device)
+        routes = torch.zeros(num_experts, 2 * PERIOD_MAX + HOLDERS_MAX, dtype=torch.int32)
+        for e, cyc in enumerate(self.cycles):
+            for j, h in enumerate(cyc):
+                routes[e, j] = h
+                routes[e, PERIOD_MAX + j] = cyc[:j].count(h)
+            for h in set(cyc):
+                routes[e, 2 * PERIOD_MAX + h] = cyc.count(h)
+        self.period_t = torch.tensor([len(c) for c in self.cycles], dtype=torch.int32, device=self.device)
+        self.routes_t = routes.to(self.device)
         self.saved: dict = {}
 
     @classmethod
     def emulated_group(cls, world: int, device, **kw) -> list["ExpertParallelMoE"]:
         """``world`` ranks in one process on one GPU (tests); call each phase on every rank in turn."""
         E = kw["num_experts"]
-        holder = kw["holder"]
-        local = max(sum(1 for e in range(E) if holder[e] == r) for r in range(world))
+        holders = [list(h) if isinstance(h, (list, tuple)) else [h] for h in kw["holder"]]
+        local = max(sum(1 for e in range(E) if r in holders[e]) for r in range(world))
         rows = kw["max_tokens"] * world * max(1, local)
         H = kw["hidden"]
         segs = {"counts": (world * 16, torch.int32), "recv": (rows * H, torch.bfloat16), "y": (rows * H, torch.bfloat16),
@@ -120,8 +172,10 @@ class ExpertParallelMoE:
         self._layout(table.to("cpu", torch.int64))
 
     def _layout(self, table: torch.Tensor) -> None:
-        rowbase, ranges = receive_layout(table, self.holder, self.rank, self.world)
-        self.saved["rowbase"] = torch.tensor(rowbase, dtype=torch.int64, device=self.device)
+        rowbase, ranges = replica_layout(table.tolist(), self.cycles, self.rank, self.world)
+        rb = torch.zeros(self.E, HOLDERS_MAX, dtype=torch.int64)
+        rb[:, : self.world] = torch.tensor(rowbase, dtype=torch.int64)
+        self.saved["rowbase"] = rb.to(self.device)
         self.saved["local_ranges"] = ranges
         self.saved["recv_rows"] = sum(n for _, n in ranges)
 
@@ -129,7 +183,7 @@ class ExpertParallelMoE:
     def dispatch(self) -> None:
         s = self.saved
         route_row = torch.empty(s["T"] * self.k, dtype=torch.int64, device=self.device)
-        ext().moe_dispatch(s["x"], s["topi"], s["pos"], self.k, self.rank, self.holder_t, s["rowbase"],
+        ext().moe_dispatch(s["x"], s["topi"], s["pos"], self.k, self.rank, self.period_t, self.routes_t, s["rowbase"],
                            self.heap.peer_ptrs("recv"), route_row)
         ops.count(1)
         s["route_row"] = route_row

@@ -59,3 +59,35 @@ def test_expert_parallel_moe_matches_one_rank():
     for r, res in many.items():
         for a, b in zip(res["losses"], one["losses"]):
             assert abs(a - b) <= 1e-2 * abs(b), (r, res["losses"], one["losses"])
+
+
+def _replace(rank, world, port, steps_before, steps_after):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.moe_trainer import GPUMoETrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tr = GPUMoETrainer(_cfg(), global_batch=8, micro_batch=1, seq_len=8, ep_impl="collective",
+                       dp_impl="collective", device="cpu", lr=1e-2)
+    losses = [tr.train_step() for _ in range(steps_before)]
+    info = None
+    if world > 1:
+        info = tr.replace_experts({world - 1: 0.5})  # the last rank runs at half speed
+    losses += [tr.train_step() for _ in range(steps_after)]
+    tr.close()
+    dist.destroy_process_group()
+    return {"losses": losses, "info": info}
+
+
+def test_fail_slow_expert_replacement_keeps_the_run():
+    ref = spawn(_replace, 1, 4, 0, timeout=240)[0]["losses"]
+    res = spawn(_replace, 4, 2, 2, timeout=300)
+    holders = res[0]["info"]["holders"]
+    assert any(len(h) > 1 for h in holders), holders  # the slow rank's expert got a replica
+    for r, out in res.items():
+        assert out["info"]["holders"] == holders
+        for a, b in zip(out["losses"], ref):
+            assert abs(a - b) <= 1e-2 * abs(b), (r, out["losses"], ref)
