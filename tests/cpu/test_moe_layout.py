@@ -27,3 +27,30 @@ def test_receive_rows_tile_each_holder_buffer():
             assert sum(n for _, n in ranges) == pos
             # expert-major, then source order
             assert [(e, src) for _, _, e, src in rows] == sorted((e, src) for _, _, e, src in rows)
+
+
+def test_replica_cycles_deal_positions_onto_disjoint_rows():
+    """Replicated experts: the dispatch kernel's row formula (rowbase[e][h] + (p // L) * slots of h
+    per cycle + rank of the slot) maps every position dealt to holder h onto its block exactly."""
+    from resihp_megatron_b200.parallel.moe_ep import replica_cycles, replica_layout
+
+    rng = random.Random(1)
+    world, E = 4, 5
+    holders = [[0, 1], [1], [2, 3, 0], [3], [0]]
+    cycles = replica_cycles(holders, {1: 0.5, 3: 1.5})
+    assert all(set(c) == set(h) for c, h in zip(cycles, holders))
+    table = [[rng.randrange(0, 40) for _ in range(E)] for _ in range(world)]
+    filled = {h: [] for h in range(world)}
+    for src in range(world):
+        rowbase, _ = replica_layout(table, cycles, src, world)
+        for e in range(E):
+            L = len(cycles[e])
+            for p in range(table[src][e]):
+                j = p % L
+                h = cycles[e][j]
+                row = rowbase[e][h] + (p // L) * cycles[e].count(h) + cycles[e][:j].count(h)
+                filled[h].append(row)
+    for h in range(world):
+        _, ranges = replica_layout(table, cycles, h, world)
+        total = sum(n for _, n in ranges)
+        assert sorted(filled[h]) == list(range(total)), h

@@ -30,16 +30,20 @@ def _reference(xs, router_w, w13s, w2s, k, douts):
     return out.detach(), x.grad, rw.grad, [w.grad for w in w13], [w.grad for w in w2], topi
 
 
-@pytest.mark.parametrize("world,E,k", [(4, 8, 2), (2, 4, 2), (8, 8, 2)])
-def test_expert_parallel_layer_forward_backward(world, E, k):
+@pytest.mark.parametrize("world,E,k,holder,speeds", [
+    (4, 8, 2, None, None), (2, 4, 2, None, None), (8, 8, 2, None, None),
+    # replicated experts: the pairs of experts 0 and 3 are dealt to two ranks by speed
+    (4, 4, 2, [[0, 1], [1], [2], [3, 0]], {1: 0.5}),
+])
+def test_expert_parallel_layer_forward_backward(world, E, k, holder, speeds):
     from resihp_megatron_b200.ops.gemm import error_state
     from resihp_megatron_b200.parallel.moe_ep import ExpertParallelMoE
 
     H, Fd, T = 256, 512, 96
     torch.manual_seed(0)
-    holder = [e * world // E for e in range(E)]
+    holder = holder or [e * world // E for e in range(E)]
     ranks = ExpertParallelMoE.emulated_group(world, "cuda", hidden=H, num_experts=E, top_k=k, max_tokens=T,
-                                             holder=holder)
+                                             holder=holder, speeds=speeds)
     xs = [torch.randn(T, H, device="cuda").bfloat16() for _ in range(world)]
     router_w = (torch.randn(E, H, device="cuda") / H ** 0.5).bfloat16()
     w13s = [(torch.randn(2 * Fd, H, device="cuda") / H ** 0.5).bfloat16() for _ in range(E)]
