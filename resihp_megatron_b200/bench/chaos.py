@@ -1,8 +1,12 @@
 """Real-process chaos benchmark on CPU (8 gloo workers, TP2 x PP2 x DP2): MTTR breakdown.
 
-Faults are injected from outside the workers at a recorded time ``t0``: ``kill`` (SIGKILL),
-``hang`` (SIGSTOP: alive, heartbeats and progress frozen) and ``slow`` (a 50 % SIGSTOP/SIGCONT
-duty cycle, i.e. a 2x fail-slow, found by the residual-BOCD detector service).  The
+Faults: ``kill`` (SIGKILL) and ``hang`` (SIGSTOP: alive, heartbeats and progress frozen) are
+injected from outside the workers at a recorded time ``t0``; ``slow`` is a 2x fail-slow of one
+rank's compute from the in-process injector (``slow@iter=...:factor=2``: each timed chunk is
+stretched by a busy wait), found by the residual-BOCD detector service, with ``t0`` the moment
+the coordinator sees the victim reach that iteration.  (A SIGSTOP/SIGCONT duty cycle is not used
+for ``slow``: with sub-millisecond compute chunks it mostly stretches communication waits, which
+the residual detector's predictor rightly does not read as a slower device.)  The
 coordinator's transaction marks split recovery into detection, abort, planning, generation
 build + state migration, and commit.  Each trial also checks that the survivors' losses and
 final shards equal single-process training.  The CPU harness bounds the absolute numbers
@@ -38,15 +42,11 @@ def _wait(pred, timeout: float, what: str) -> None:
         time.sleep(0.02)
 
 
-def _duty_cycle(pid: int, stop: threading.Event, period: float = 0.01) -> None:
-    while not stop.is_set():
-        try:
-            os.kill(pid, signal.SIGSTOP)
-            time.sleep(period / 2)
-            os.kill(pid, signal.SIGCONT)
-            time.sleep(period / 2)
-        except ProcessLookupError:
-            return
+def _progress(coord, worker_id: str) -> int:
+    for w in coord.membership.alive():
+        if w.worker_id == worker_id:
+            return w.progress.get("iteration", -1)
+    return -1
 
 
 def verify(out: Path, world: list[str]) -> bool:
@@ -100,6 +100,7 @@ def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None,
     # the detector calibrates its noise prior during warm-up: start a slowdown after it
     inject_after = inject_after if inject_after is not None else (20 if fault == "slow" else 8)
     out = Path(tempfile.mkdtemp(prefix=f"resihp-chaos-{fault}-"))
+    victim_id = "n0g0" if fault == "slow" else "n0g3"  # slow: a rank that reports its group's timings
     # gloo cannot abort an op blocked on a frozen peer, so the hang timeout must exceed the
     # communication timeout (10 s here) or the survivors' wait would look like a second hang
     coord = Coordinator(planner=make_hetero_planner(HETERO_REF), expected_workers=8, lease_timeout=2.0,
@@ -109,6 +110,8 @@ def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None,
         coord.report_handler = svc.handle
     coord.start()
     env = {"PYTHONPATH": str(ROOT), "RESIHP_LOG_LEVEL": "ERROR", "OMP_NUM_THREADS": "1"}
+    if fault == "slow":
+        env["RESIHP_FAULTS"] = f"slow@iter={inject_after}:target={victim_id}:factor=2"
     agents, stop = [], threading.Event()
     try:
         for n in range(2):
@@ -117,16 +120,15 @@ def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None,
                       "--iter-sleep", str(iter_sleep)], 4, env=env)
             agents.append(ag)
         _wait(lambda: coord.committed_generation >= 1, 60, "start")
-        _wait(lambda: min((w.progress.get("iteration", -1) for w in coord.membership.alive()), default=-1)
-              >= inject_after, 120, "warm-up")
-        victim = agents[0].workers["n0g3"].proc.pid
-        t0 = time.monotonic()
-        if fault == "kill":
-            os.kill(victim, signal.SIGKILL)
-        elif fault == "hang":
-            os.kill(victim, signal.SIGSTOP)
+        victim = agents[0].workers[victim_id].proc.pid
+        if fault == "slow":
+            _wait(lambda: _progress(coord, victim_id) >= inject_after, 120, "warm-up")
+            t0 = time.monotonic()
         else:
-            threading.Thread(target=_duty_cycle, args=(victim, stop), daemon=True).start()
+            _wait(lambda: min((w.progress.get("iteration", -1) for w in coord.membership.alive()), default=-1)
+                  >= inject_after, 120, "warm-up")
+            t0 = time.monotonic()
+            os.kill(victim, signal.SIGKILL if fault == "kill" else signal.SIGSTOP)
         _wait(lambda: coord.committed_generation >= 2, 240, "recovery commit")
         stop.set()
         procs = [w.proc for ag in agents for w in ag.workers.values()]
