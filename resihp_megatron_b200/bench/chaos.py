@@ -90,7 +90,8 @@ def breakdown(history: list[dict], t0: float) -> dict:
     return out
 
 
-def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None, iter_sleep: float = 0.05) -> dict:
+def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None, iter_sleep: float = 0.05,
+              slow_factor: float = 2.0) -> dict:
     from ..control.agent import NodeAgent
     from ..control.coordinator import Coordinator
     from ..detect.service import DetectorService
@@ -111,7 +112,7 @@ def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None,
     coord.start()
     env = {"PYTHONPATH": str(ROOT), "RESIHP_LOG_LEVEL": "ERROR", "OMP_NUM_THREADS": "1"}
     if fault == "slow":
-        env["RESIHP_FAULTS"] = f"slow@iter={inject_after}:target={victim_id}:factor=2"
+        env["RESIHP_FAULTS"] = f"slow@iter={inject_after}:target={victim_id}:factor={slow_factor}"
     agents, stop = [], threading.Event()
     try:
         for n in range(2):

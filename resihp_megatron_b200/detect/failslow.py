@@ -82,6 +82,8 @@ class FailSlowDetector:
         since = min(max(1, self.bocd.map_run_length() + 1), self.window)
         recent = self.xs[-since:]
         base = self.xs[-(since + 4 * self.window):-since] or self.xs[:-since]
+        if not base:  # the whole history is one segment: nothing to compare with yet
+            return None
         inc = math.exp(statistics.fmean(recent) - statistics.fmean(base)) - 1.0
         if inc < self.min_increase:
             return None

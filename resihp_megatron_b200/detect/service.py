@@ -8,11 +8,18 @@ reshaping, repartition, migration, exclusion) reuses the fail-stop machinery.  W
 ``what_if`` pricer the rent is (current plan - replanned plan) and the purchase price is the
 estimated migration + rebuild time, so a slowdown the planner cannot mitigate never triggers a
 reconfiguration.  (Reference: ``resihp/detect/service.py:30-114``.)
+
+Common-mode correction (``common_mode=True``): the reports of one iteration are processed
+together, and when at least three groups report, each group's time is divided by the median
+ratio observed / predicted over the groups before it reaches its detector and the shared
+predictor.  A slowdown of the whole node (contention, a thermal event, a noisy neighbour) moves
+every group alike and cancels; a fail-slow device moves only its group and stands out.
 """
 
 from __future__ import annotations
 
 import queue
+import statistics
 import threading
 
 from .failslow import FailSlowDetector
@@ -26,10 +33,12 @@ log = get_logger(__name__)
 class DetectorService:
     def __init__(self, coordinator, *, warmup: int = 6, threshold: float = 0.9, min_increase: float = 0.25,
                  reconfig_cost_s: float = 0.0, min_gain: float = 0.05, min_dwell: int = 0, token_scale: float = 1e3,
-                 what_if=None):
+                 what_if=None, common_mode: bool = True, window: int = 8):
         self.coord = coordinator
+        # a change is reported while it lies within the last ``window`` iterations: noisy timings
+        # may need several post-change samples before the posterior is confident
         self.detector_kw = dict(mode="residual", warmup=warmup, threshold=threshold, min_increase=min_increase,
-                                cooldown=warmup)
+                                cooldown=warmup, window=window)
         self.rls = RLSPredictor(scales=(token_scale, token_scale ** 2, 1.0), gate=0.3, warmup=32)
         self.detectors: dict[tuple, FailSlowDetector] = {}
         self.policy_kw = dict(min_gain=min_gain, min_dwell=min_dwell)
@@ -38,6 +47,9 @@ class DetectorService:
         self.what_if = what_if
         self.speeds: dict[str, float] = {}
         self.events: list[dict] = []
+        self.common_mode = common_mode
+        self._pending: dict[tuple, dict[tuple, tuple]] = {}  # (gen, iteration) -> {devices: (worker, report)}
+        self._groups: dict[object, set] = {}  # groups seen per generation
         self._suspects: dict[tuple, dict] = {}
         self._q: queue.Queue = queue.Queue()
         self._stop = threading.Event()
@@ -60,6 +72,7 @@ class DetectorService:
         end = time.monotonic() + timeout
         while not self._q.empty() and time.monotonic() < end:
             time.sleep(0.01)
+        time.sleep(0.05)  # the report being processed
 
     def _loop(self) -> None:
         while not self._stop.is_set():
@@ -67,15 +80,49 @@ class DetectorService:
             if item is None:
                 return
             try:
-                self._process(*item)
+                if self.common_mode:
+                    self._collect(*item)
+                else:
+                    self._process(*item)
             except Exception:  # noqa: BLE001 - detection must never take the coordinator down
                 log.exception("timing report processing failed")
 
-    def _process(self, worker_id: str, rep: dict) -> None:
+    def _collect(self, worker_id: str, rep: dict) -> None:
+        """Buffer the reports of an iteration; process one when every group of the generation has
+        reported it, or when a group is already two iterations further."""
+        gen, it = rep.get("gen"), rep["iteration"]
         devices = tuple(rep["devices"])
+        seen = self._groups.setdefault(gen, set())
+        seen.add(devices)
+        self._pending.setdefault((gen, it), {})[devices] = (worker_id, rep)
+        for key in sorted(k for k in self._pending if k[0] == gen):
+            batch = self._pending[key]
+            if set(batch) >= seen or key[1] <= it - 2:
+                del self._pending[key]
+                self._process_batch(list(batch.values()))
+
+    def _norm(self, rep: dict) -> list[tuple[float, float, float]]:
         layers = max(1, rep["layers"])
         share = max(1, rep["tp"]) * max(1, rep.get("cp", 1))  # one rank does 1/(tp*cp) of a layer
-        norm = [(n, s, sec * share / layers) for n, s, sec in rep["samples"]]
+        return [(n, s, sec * share / layers) for n, s, sec in rep["samples"]]
+
+    def _process_batch(self, batch: list[tuple[str, dict]]) -> None:
+        factor = 1.0
+        if self.rls.n >= self.rls.warmup:
+            ratios = []
+            for _, rep in batch:
+                norm = self._norm(rep)
+                if norm:
+                    pred = sum(max(self.rls.predict(n, s), 1e-9) for n, s, _ in norm)
+                    ratios.append(sum(sec for *_, sec in norm) / pred)
+            if len(ratios) >= 3:
+                factor = max(statistics.median(ratios), 1e-9)
+        for worker_id, rep in batch:
+            self._process(worker_id, rep, factor)
+
+    def _process(self, worker_id: str, rep: dict, common: float = 1.0) -> None:
+        devices = tuple(rep["devices"])
+        norm = [(n, s, sec / common) for n, s, sec in self._norm(rep)]
         if not norm:
             return
         observed = sum(sec for *_, sec in norm)

@@ -178,3 +178,45 @@ def test_nccl_profiler_plugin_records_coll_and_p2p(tmp_path, monkeypatch):
     assert all(r.end_ns >= r.start_ns for r in recs) and reader.poll() == []
     reader.close()
     assert prof.finalize(ctx) == 0
+
+
+def test_common_mode_noise_is_cancelled_and_the_slow_group_still_found():
+    """Four groups; iterations 20-29 slow every group 2.5x (node-wide contention: nobody is
+    flagged), group 3 alone runs 2x slower from iteration 60 (flagged)."""
+    coord = FakeCoord()
+    svc = DetectorService(coord, warmup=6, reconfig_cost_s=0.0, min_gain=0.05, token_scale=1e3)
+    rng = np.random.default_rng(7)
+    groups = [[f"g{g}a", f"g{g}b"] for g in range(4)]
+    for it in range(90):
+        for g, devs in enumerate(groups):
+            samples = []
+            for _ in range(4):
+                n = float(rng.integers(500, 2000))
+                s = float(n * rng.integers(50, 400))
+                sec = (2e-6 * n + 1e-9 * s) * 4 * (1.0 + rng.normal(0, 0.01))
+                if 20 <= it < 30:
+                    sec *= 2.5
+                if g == 3 and it >= 60:
+                    sec *= 2.0
+                samples.append((n, s, sec))
+            svc.handle("w", {"kind": "timing", "iteration": it, "gen": 1, "devices": devs, "layers": 4, "tp": 2,
+                             "cp": 1, "samples": samples})
+    svc.drain()
+    svc.stop()
+    assert coord.replans and all(r.startswith("failslow:g3a,g3b") for r in coord.replans), coord.replans
+    assert all(e["iteration"] >= 60 for e in svc.events)
+
+
+def test_a_change_that_needs_several_samples_to_be_sure_of_is_still_reported():
+    """Residuals recorded from a CPU job whose rank went 2x slow at sample 18: the first
+    post-change samples are ambiguous, so the posterior only becomes confident a few samples
+    later; the detector must still report the change (a 3-sample window missed it)."""
+    import math
+
+    from resihp_megatron_b200.detect.failslow import FailSlowDetector
+
+    xs = [-0.03, 0.34, -0.08, -0.01, -0.22, 0.09, -0.05, -0.25, 0.16, -0.24, -0.03, 0.07, -0.22, 0.02, 0.32, -0.03,
+          -0.04, 0.14, 0.48, 0.74, 0.63, 0.42, 0.61, 0.76, 0.49, 0.53, 0.67, 0.25, 0.86, 0.38, 0.62, 0.37, 0.72, 0.55]
+    d = FailSlowDetector("residual", warmup=6, threshold=0.9, min_increase=0.5, cooldown=6, window=8)
+    hits = [i for i, x in enumerate(xs) if d.observe(i, math.exp(x), 1.0)]
+    assert hits and 18 <= hits[0] <= 24, hits
