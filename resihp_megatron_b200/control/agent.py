@@ -102,12 +102,15 @@ class NodeAgent:
 
     # ------------------------------------------------------------------ workers
     def spawn(self, cmd: list[str], nproc: int, env: dict[str, str] | None = None,
-              devices: list[str] | None = None) -> list[LocalWorker]:
-        """Start ``nproc`` workers; each gets its identity through ``RESIHP_*`` variables."""
+              devices: list[str] | None = None, first_rank: int = 0) -> list[LocalWorker]:
+        """Start ``nproc`` workers (local ranks ``first_rank ..``); each gets its identity through
+        ``RESIHP_*`` variables.  A later call with a higher ``first_rank`` adds workers to a
+        running job (a replacement GPU, a grown node): they register and join at the next
+        generation."""
         started = []
-        for i in range(nproc):
+        for i in range(first_rank, first_rank + nproc):
             wid = f"{self.node_id}g{i}"
-            dev = devices[i] if devices else "cpu"
+            dev = devices[i - first_rank] if devices else "cpu"
             wenv = {**os.environ, **(env or {}),
                     "RESIHP_AGENT_ADDR": fmt_addr(self.address), "RESIHP_WORKER_ID": wid,
                     "RESIHP_NODE_ID": self.node_id, "RESIHP_LOCAL_RANK": str(i), "RESIHP_DEVICE": dev}

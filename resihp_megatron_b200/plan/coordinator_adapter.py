@@ -75,6 +75,23 @@ class HeteroPlannerFn:
         replicas = max(1, slots // self.cfg.num_stages)
         return HeteroPlanner(replace(self.cfg, num_replicas=replicas)).initial_plan(topo, generation=generation)
 
+    def _degraded_initial(self, topo: ClusterTopology, generation: int) -> HeteroParallelPlan:
+        """A job that starts with fewer devices than its nominal layout (a node short of a GPU):
+        plan the nominal layout on a topology padded with placeholder devices, then re-plan
+        without them, exactly as if they had failed (TP shrink, repartition, migration)."""
+        from .topology import Device
+
+        nodes = topo.nodes()
+        width = max(len(d) for d in nodes.values())
+        width = -(-width // self.cfg.tp) * self.cfg.tp
+        devs = list(topo.devices)
+        for node, have in nodes.items():
+            for k in range(len(have), width):
+                devs.append(Device(f"{node}~{k}", node, k, have[0].rack))
+        padded = ClusterTopology(tuple(devs))
+        nominal = self.planner.initial_plan(padded, generation=generation)
+        return self.planner.replan(nominal, topo, generation=generation)
+
     def __call__(self, view) -> tuple[list[str], dict]:
         t0 = time.monotonic()
         topo = topology_from_view(view)
@@ -82,7 +99,10 @@ class HeteroPlannerFn:
         restore = None
         hit = False
         if prev is None:
-            plan = self.planner.initial_plan(topo, generation=view.generation)
+            try:
+                plan = self.planner.initial_plan(topo, generation=view.generation)
+            except (ValueError, PlanInfeasible):
+                plan = self._degraded_initial(topo, view.generation)
         else:
             plan = self._from_cache(prev, topo, view)
             hit = plan is not None
