@@ -36,3 +36,13 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip_gpu)
         if "multigpu" in item.keywords and n < 2:
             item.add_marker(skip_multi)
+
+
+@pytest.fixture
+def store():
+    """A master ``TCPStore`` on 127.0.0.1 for multi-process tests; yields ``(host, port)``."""
+    import torch.distributed as dist
+
+    srv = dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False)
+    yield ("127.0.0.1", srv.port)
+    del srv
