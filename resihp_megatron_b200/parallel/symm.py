@@ -68,9 +68,12 @@ class Segment:
         return self.numel * torch.empty(0, dtype=self.dtype).element_size()
 
 
+SIGNAL_SLOT_BYTES = 128  # one 64-bit word per writer rank, each on its own 128-byte line (symm.cu)
+
+
 def layout(segments: dict[str, tuple[int, torch.dtype]], world: int) -> tuple[dict[str, Segment], int, int]:
     """Offsets of the signal pad and of every segment; returns (segments, pad bytes, total)."""
-    pad = (ext().symm_signal_bytes(world) + ALIGN - 1) // ALIGN * ALIGN
+    pad = (world * SIGNAL_SLOT_BYTES + ALIGN - 1) // ALIGN * ALIGN
     off = pad
     out = {}
     for name, (numel, dtype) in segments.items():
@@ -78,6 +81,21 @@ def layout(segments: dict[str, tuple[int, torch.dtype]], world: int) -> tuple[di
         out[name] = seg
         off += (seg.nbytes + ALIGN - 1) // ALIGN * ALIGN
     return out, pad, off
+
+
+def check_layout(segs: dict[str, Segment], pad: int, total: int, world: int) -> None:
+    """Invariants every rank's kernels rely on: the signal pad holds one slot per rank, every
+    segment starts on an ``ALIGN`` boundary after the pad, segments do not overlap and fit."""
+    if pad < world * SIGNAL_SLOT_BYTES or pad % ALIGN:
+        raise AssertionError(f"signal pad of {pad} bytes for {world} ranks")
+    spans = sorted((seg.offset, seg.offset + seg.nbytes, name) for name, seg in segs.items())
+    end = pad
+    for lo, hi, name in spans:
+        if lo % ALIGN or lo < end:
+            raise AssertionError(f"segment {name} at {lo} overlaps or is misaligned")
+        end = hi
+    if end > total:
+        raise AssertionError(f"segments end at {end} beyond the heap's {total} bytes")
 
 
 class SymmetricHeap:
@@ -91,6 +109,9 @@ class SymmetricHeap:
         self.device = torch.device(device)
         self.dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self.segments, self.pad_bytes, self.nbytes = layout(segments, world)
+        check_layout(self.segments, self.pad_bytes, self.nbytes, world)
+        if ext().symm_signal_bytes(world) != world * SIGNAL_SLOT_BYTES:
+            raise RuntimeError("signal pad layout differs between the extension and this module")
         self.abort = abort
         self.epoch = 0
         self._opened: list[int] = []
@@ -160,6 +181,16 @@ class SymmetricHeap:
         ext().symm_tensor(self.local_base, self.pad_bytes, "uint8", self.dev_index).zero_()
         self.status.zero_()
         self.epoch = 0
+
+    def validate(self) -> None:
+        """Host-side invariant check: layout, distinct peer regions, pad pointers, epoch."""
+        check_layout(self.segments, self.pad_bytes, self.nbytes, self.world)
+        if len(self.bases) != self.world or len(set(self.bases)) != self.world or self.bases[self.rank] != self.local_base:
+            raise AssertionError("peer bases are not one distinct region per rank")
+        if self.pads.tolist() != self.bases:
+            raise AssertionError("device pad pointers differ from the mapped bases")
+        if self.epoch < 0:
+            raise AssertionError("negative barrier epoch")
 
     def check(self) -> None:
         st = self.status.tolist()

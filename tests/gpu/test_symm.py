@@ -19,6 +19,8 @@ def test_fused_dp_step_emulated_ranks_matches_reference(tmp_path):
 
     W, n = 4, 1 << 16
     heaps = SymmetricHeap.emulated({"grad": (n, torch.float32), "weight": (n, torch.bfloat16)}, W, "cuda")
+    for h in heaps:
+        h.validate()
     import os
 
     ring_dir = tmp_path
