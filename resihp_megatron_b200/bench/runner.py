@@ -106,6 +106,15 @@ def cmd_megatron_log(args) -> None:
     megatron_log.main(args.rest)
 
 
+def cmd_gpu_sweep(args) -> None:
+    """The multi-GPU sweeps run one process per GPU: ``torchrun --nproc-per-node N -m
+    resihp_megatron_b200.bench.runner <sweep> ...`` (or the sweep module directly)."""
+    import importlib
+
+    mod = {"tp-sweep": "tp_sweep", "moe-sweep": "moe_sweep", "migration-sweep": "migration_sweep"}[args.cmd]
+    importlib.import_module(f"resihp_megatron_b200.bench.{mod}").main(args.rest)
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="resihp-bench", description=__doc__,
                                  formatter_class=argparse.RawTextHelpFormatter)
@@ -129,7 +138,7 @@ def build_parser() -> argparse.ArgumentParser:
     c = sub.add_parser("chaos")
     c.add_argument("--trials", type=int, default=3)
     c.add_argument("--faults", default="kill,hang,slow")
-    for name in ("kernels", "megatron-log"):
+    for name in PASS_THROUGH:
         k = sub.add_parser(name, add_help=False)
         k.add_argument("rest", nargs=argparse.REMAINDER)
     a = sub.add_parser("all")
@@ -137,8 +146,16 @@ def build_parser() -> argparse.ArgumentParser:
     return ap
 
 
+PASS_THROUGH = ("kernels", "megatron-log", "tp-sweep", "moe-sweep", "migration-sweep")
+
+
 def main(argv=None) -> None:
-    args = build_parser().parse_args(argv)
+    ap = build_parser()
+    args, unknown = ap.parse_known_args(argv)
+    if unknown:
+        if args.cmd not in PASS_THROUGH:
+            ap.error(f"unrecognized arguments: {' '.join(unknown)}")
+        args.rest = list(unknown) + list(args.rest)
     t0 = time.monotonic()
     if args.cmd == "all":
         q = args.quick
@@ -148,7 +165,8 @@ def main(argv=None) -> None:
             main(["--out", args.out, *sub_argv])
     else:
         {"detection": cmd_detection, "planner": cmd_planner, "calibrate": cmd_calibrate, "sim": cmd_sim,
-         "chaos": cmd_chaos, "kernels": cmd_kernels, "megatron-log": cmd_megatron_log}[args.cmd](args)
+         "chaos": cmd_chaos, "kernels": cmd_kernels, "megatron-log": cmd_megatron_log, "tp-sweep": cmd_gpu_sweep,
+         "moe-sweep": cmd_gpu_sweep, "migration-sweep": cmd_gpu_sweep}[args.cmd](args)
     print(f"[resihp-bench {args.cmd}] {time.monotonic() - t0:.1f}s")
 
 
