@@ -63,6 +63,9 @@ def _args():
                          "and the eviction-to-commit time)")
     ap.add_argument("--dp-impl", choices=["fused", "nccl"], default="fused",
                     help="N > 1: fused NVLink reduction + Adam + gather kernel, or NCCL reduce-scatter/all-gather")
+    ap.add_argument("--cuda-graph", action="store_true",
+                    help="one GPU: capture the whole step (every micro-batch and the update) in a CUDA graph after "
+                         "the warm-up and replay it")
     ap.add_argument("--parallelism", default="dp",
                     help="'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' with T*P*D = N: tensor (+ sequence) x "
                          "pipeline x data parallelism through the plan-driven runtime (BASELINE config 2: tp2pp2dp2)")
@@ -208,6 +211,10 @@ def main() -> None:
         trainer.step_device(*dev_batches[s % len(dev_batches)])
     torch.cuda.synchronize()
     trainer.check()  # a peer that never reached a barrier ends the run here, not after every step
+    if args.cuda_graph:
+        if world != 1:
+            raise SystemExit("--cuda-graph: one GPU only (the data-parallel step's collectives are not captured)")
+        trainer.capture_graphs()
 
     # ---- device-timed region
     sampler = ClockSampler([local] if world == 1 else range(world)) if rank == 0 else None
@@ -311,7 +318,8 @@ def main() -> None:
                 "global_batch": global_batch,
                 "seq_len": args.seq,
                 "micro_batch": args.micro_batch,
-                "parallelism": "tp1pp1dp1" if world == 1 else f"dp{world}-zero1-{args.dp_impl}",
+                "parallelism": ("tp1pp1dp1" + ("-cudagraph" if args.cuda_graph else "")) if world == 1
+                               else f"dp{world}-zero1-{args.dp_impl}",
                 "l2": "inputs larger than L2 (each step touches >100 GB of weights/grads/optimizer state)",
                 "params": cfg.num_params(),
                 "model_tflops_per_gpu": cfg.flops_per_token(args.seq) * value / world / 1e12,

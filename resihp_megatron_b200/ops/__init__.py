@@ -94,10 +94,12 @@ def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, dtable: torch.Tensor):
 
 
 def adam_step(p, grad, m, v, p_bf16=None, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0,
-              decoupled=False, step: int, grad_scale=1.0, zero_grad=False):
-    """Fused Adam(W) on flat fp32 buffers; optionally refreshes a bf16 copy of the weights."""
+              decoupled=False, step: int, grad_scale=1.0, zero_grad=False, bias_corr: torch.Tensor | None = None):
+    """Fused Adam(W) on flat fp32 buffers; optionally refreshes a bf16 copy of the weights.
+    ``bias_corr`` (fp32 device ``[1 - beta1^t, sqrt(1 - beta2^t)]``) is read by the kernel
+    instead of ``step``'s host values -- for CUDA graphs, whose replays keep launch arguments."""
     ext().adam_step(p, grad, m, v, p_bf16, float(lr), float(beta1), float(beta2), float(eps), float(weight_decay),
-                    bool(decoupled), int(step), float(grad_scale), bool(zero_grad))
+                    bool(decoupled), int(step), float(grad_scale), bool(zero_grad), bias_corr)
     count(1)
 
 

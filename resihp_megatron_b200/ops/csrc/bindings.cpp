@@ -172,22 +172,24 @@ void embedding_bwd(const torch::Tensor& ids, const torch::Tensor& dx, torch::Ten
   const c10::cuda::CUDAGuard g(dx.device());
   auto flat = ids.reshape({-1});
   auto sorted = torch::sort(flat, /*stable=*/true, /*dim=*/0, /*descending=*/false);
-  auto vals = std::get<0>(sorted);
+  auto vals = std::get<0>(sorted).contiguous();
   auto order = std::get<1>(sorted).contiguous();
-  auto uc = torch::unique_consecutive(vals, /*return_inverse=*/false, /*return_counts=*/true);
-  auto uniq = std::get<0>(uc).contiguous();
-  auto counts = std::get<2>(uc);
-  auto starts = torch::zeros({uniq.numel() + 1}, counts.options());
-  starts.narrow(0, 1, uniq.numel()).copy_(torch::cumsum(counts, 0));
-  RB_CALL(rb::embedding_bwd(order.data_ptr<int64_t>(), starts.data_ptr<int64_t>(), uniq.data_ptr<int64_t>(),
-                            uniq.numel(), dx.data_ptr(), dE.data_ptr<float>(), dE.size(1), cur_stream()),
+  RB_CALL(rb::embedding_bwd(vals.data_ptr<int64_t>(), order.data_ptr<int64_t>(), static_cast<int>(flat.numel()),
+                            dx.data_ptr(), dE.data_ptr<float>(), dE.size(1), cur_stream()),
           "embedding_bwd");
 }
 
 void adam_step(torch::Tensor& p, torch::Tensor& grad, torch::Tensor& m, torch::Tensor& v,
                const c10::optional<torch::Tensor>& p_bf16, double lr, double b1, double b2, double eps, double wd,
-               bool decoupled, int64_t step, double grad_scale, bool zero_grad) {
+               bool decoupled, int64_t step, double grad_scale, bool zero_grad,
+               const c10::optional<torch::Tensor>& bias_corr) {
   CHECK_F32(p); CHECK_F32(grad); CHECK_F32(m); CHECK_F32(v);
+  const float* bc_dev = nullptr;
+  if (bias_corr.has_value()) {
+    CHECK_F32((*bias_corr));
+    TORCH_CHECK(bias_corr->numel() >= 2, "adam_step: bias_corr holds (1 - b1^t, sqrt(1 - b2^t))");
+    bc_dev = bias_corr->data_ptr<float>();
+  }
   void* pb = nullptr;
   if (p_bf16.has_value()) { CHECK_BF16(*p_bf16); TORCH_CHECK(p_bf16->numel() == p.numel()); pb = p_bf16->data_ptr(); }
   const double bc1 = 1.0 - std::pow(b1, static_cast<double>(step));
@@ -196,7 +198,7 @@ void adam_step(torch::Tensor& p, torch::Tensor& grad, torch::Tensor& m, torch::T
   RB_CALL(rb::adam_step(p.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), pb,
                         p.numel(), lr, b1, b2, eps, wd, decoupled ? 1 : 0, static_cast<float>(bc1),
                         static_cast<float>(std::sqrt(bc2)), static_cast<float>(grad_scale), zero_grad ? 1 : 0,
-                        cur_stream()), "adam_step");
+                        cur_stream(), bc_dev), "adam_step");
 }
 
 // Deterministic sum of squares of a flat fp32 buffer (fixed 296-way split, fixed order).

@@ -255,18 +255,20 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
 }
 
-// Deterministic embedding gradient.  `order` lists token positions sorted by (id, position)
-// and `starts[k]..starts[k+1]` is the run of positions of the k-th distinct id `uniq[k]`.
-// dE[uniq[k], :] += sum over the run, in position order.
-__global__ void embedding_bwd_kernel(const int64_t* __restrict__ order, const int64_t* __restrict__ starts,
-                                     const int64_t* __restrict__ uniq, const __nv_bfloat16* __restrict__ dx,
-                                     float* __restrict__ dE, int H) {
-  const int k = blockIdx.x;
-  const long long s0 = starts[k], s1 = starts[k + 1];
-  const long long id = uniq[k];
+// Embedding backward on the ids sorted stably by value (`vals`, with original positions
+// `order`): block i owns position i; if it starts a run of equal ids it sums that run's rows of dx
+// in position order and adds them to dE[id, :] (fixed order: deterministic), else it returns.  No
+// data-dependent sizes reach the host, so the whole backward can be captured in a CUDA graph.
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ vals, const int64_t* __restrict__ order, int T,
+                                     const __nv_bfloat16* __restrict__ dx, float* __restrict__ dE, int H) {
+  const int i = blockIdx.x;
+  const long long id = vals[i];
+  if (i > 0 && vals[i - 1] == id) return;
+  int end = i + 1;
+  while (end < T && vals[end] == id) ++end;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (long long s = s0; s < s1; ++s) {
+    for (int s = i; s < end; ++s) {
       float v[8];
       load_bf16x8(dx + order[s] * H + c, v);
 #pragma unroll
@@ -288,9 +290,13 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ order, const in
 __global__ void adam_kernel(float* __restrict__ p, const float* __restrict__ grad, float* __restrict__ m,
                             float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, long long n, float lr,
                             float b1, float b2, float eps, float wd, int decoupled, float bc1, float bc2_sqrt,
-                            float grad_scale, int zero_grad) {
+                            float grad_scale, int zero_grad, const float* __restrict__ bc_dev) {
   const long long i4 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i4 >= n) return;
+  if (bc_dev != nullptr) {  // bias corrections of this step from device memory (replayed CUDA graphs)
+    bc1 = bc_dev[0];
+    bc2_sqrt = bc_dev[1];
+  }
   const float step_size = lr / bc1;
   const int cnt = (n - i4) >= 4 ? 4 : static_cast<int>(n - i4);
   float pp[4], gg[4], mm[4], vv[4];
@@ -412,17 +418,17 @@ int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int 
   return static_cast<int>(cudaGetLastError());
 }
 
-int embedding_bwd(const int64_t* order, const int64_t* starts, const int64_t* uniq, int n_uniq, const void* dx,
-                  float* dE, int H, cudaStream_t s) {
-  if (H % 8 || n_uniq <= 0) return n_uniq == 0 ? 0 : -1;
-  embedding_bwd_kernel<<<n_uniq, 128, 0, s>>>(order, starts, uniq, reinterpret_cast<const __nv_bfloat16*>(dx),
-                                              dE, H);
+int embedding_bwd(const int64_t* vals, const int64_t* order, int T, const void* dx, float* dE, int H,
+                  cudaStream_t s) {
+  if (H % 8 || T < 0) return -1;
+  if (T == 0) return 0;
+  embedding_bwd_kernel<<<T, 128, 0, s>>>(vals, order, T, reinterpret_cast<const __nv_bfloat16*>(dx), dE, H);
   return static_cast<int>(cudaGetLastError());
 }
 
 int adam_step(float* p, float* grad, float* m, float* v, void* p_bf16, long long n, float lr, float b1, float b2,
               float eps, float wd, int decoupled, float bc1, float bc2_sqrt, float grad_scale, int zero_grad,
-              cudaStream_t s) {
+              cudaStream_t s, const float* bc_dev) {
   if (n <= 0) return 0;
   if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(grad) | reinterpret_cast<uintptr_t>(m) |
        reinterpret_cast<uintptr_t>(v)) & 15)
@@ -431,7 +437,7 @@ int adam_step(float* p, float* grad, float* m, float* v, void* p_bf16, long long
   const long long nthreads = (n + 3) / 4;
   adam_kernel<<<cdiv_ll(nthreads, 256), 256, 0, s>>>(p, grad, m, v, reinterpret_cast<__nv_bfloat16*>(p_bf16), n,
                                                      lr, b1, b2, eps, wd, decoupled, bc1, bc2_sqrt, grad_scale,
-                                                     zero_grad);
+                                                     zero_grad, bc_dev);
   return static_cast<int>(cudaGetLastError());
 }
 

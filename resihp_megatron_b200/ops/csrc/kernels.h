@@ -23,11 +23,12 @@ int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos
 int swiglu_fwd(const void* gu, void* a, int T, int F, cudaStream_t s);
 int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStream_t s);
 int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int V, int* err, cudaStream_t s);
-int embedding_bwd(const int64_t* order, const int64_t* starts, const int64_t* uniq, int n_uniq, const void* dx,
-                  float* dE, int H, cudaStream_t s);
+int embedding_bwd(const int64_t* vals, const int64_t* order, int T, const void* dx, float* dE, int H,
+                  cudaStream_t s);
 int adam_step(float* p, float* grad, float* m, float* v, void* p_bf16, long long n, float lr, float b1, float b2,
               float eps, float wd, int decoupled, float bc1, float bc2_sqrt, float grad_scale, int zero_grad,
-              cudaStream_t s);
+              cudaStream_t s,
+              const float* bc_dev = nullptr);
 int sumsq_partial(const float* x, long long n, float* part, int nblocks, cudaStream_t s);
 int cross_entropy_fwd_bwd(void* logits, long long ld, const int64_t* labels, float* loss, float* lse, int T, int V,
                           long long v0, float grad_scale, long long ignore_index, int write_grad, cudaStream_t s);

@@ -76,10 +76,79 @@ class GPUTrainer:
             self.grad_shard = torch.empty(P.shard_numel, dtype=torch.float32, device=self.device)
         self.step_count = 0
 
+    # ------------------------------------------------------------------ CUDA graphs
+    def capture_graphs(self) -> None:
+        """Capture one whole device step -- every micro-batch's forward and backward and the
+        optimizer update -- into a CUDA graph; ``step_device`` then replays it (one launch from
+        the host per step instead of thousands).  Single GPU only (no collective in the step).
+        Call it after at least one eager step (allocator pools and kernel attributes settle)."""
+        if self.dp != 1:
+            raise NotImplementedError("graph capture of the data-parallel step (collectives) is not wired")
+        from .. import ops
+
+        self.drop_graphs()
+        self.bias_corr = torch.zeros(2, dtype=torch.float32, device=self.device)
+        # pinned staging ring: a slot is rewritten only after its previous copy ran (event), so the
+        # host can run ahead of the device without racing the asynchronous copies
+        self._bc_ring = torch.zeros(64, 2, dtype=torch.float32).pin_memory()
+        self._bc_events: list = [None] * 64
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        l0 = ops.launches()
+        with torch.cuda.graph(g):
+            self.graph_loss = self._step_body(self.ids_dev, self.labels_dev, self.bias_corr)
+        self.graph_launches = ops.launches() - l0
+        self.graph = g
+
+    def drop_graphs(self) -> None:
+        self.graph = None
+        self.graph_loss = None
+
+    def _step_body(self, ids: torch.Tensor, labels: torch.Tensor, bias_corr: torch.Tensor | None) -> torch.Tensor:
+        from .. import ops
+
+        m = self.model
+        m.loss_acc.zero_()
+        scale = 1.0 / self.tokens_per_step
+        mb = self.micro_batch
+        for i in range(self.n_micro):
+            m.forward_backward(ids[i * mb:(i + 1) * mb].reshape(-1), labels[i * mb:(i + 1) * mb].reshape(-1), scale)
+        P = self.model.params
+        ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, lr=self.lr, beta1=self.betas[0],
+                      beta2=self.betas[1], eps=self.eps, weight_decay=self.wd, step=max(P.step, 1), zero_grad=True,
+                      bias_corr=bias_corr)
+        return m.loss_acc / self.tokens_per_step
+
+    def _replay(self, ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+
+        if ids.data_ptr() != self.ids_dev.data_ptr():
+            self.ids_dev.copy_(ids)
+            self.labels_dev.copy_(labels)
+        import math
+
+        P = self.model.params
+        P.step += 1
+        k = P.step % len(self._bc_events)
+        if self._bc_events[k] is not None:
+            self._bc_events[k].synchronize()
+        self._bc_ring[k, 0] = 1.0 - self.betas[0] ** P.step
+        self._bc_ring[k, 1] = math.sqrt(1.0 - self.betas[1] ** P.step)
+        self.bias_corr.copy_(self._bc_ring[k], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._bc_events[k] = ev
+        self.graph.replay()
+        ops.count(self.graph_launches)
+        self.step_count += 1
+        return self.graph_loss
+
     # ------------------------------------------------------------------ device-resident step
     def step_device(self, ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         """One optimizer step on device-resident ``[local_batch, S]`` ids/labels; returns the
         global mean loss as a 0-d device tensor (no host synchronisation)."""
+        if getattr(self, "graph", None) is not None:
+            return self._replay(ids, labels)
         m = self.model
         m.loss_acc.zero_()
         scale = 1.0 / self.tokens_per_step

@@ -158,8 +158,10 @@ def attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, *, batch, seq, heads, kv_he
 
 
 def adam_step(p, grad, m, v, p_bf16=None, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0,
-              decoupled=False, step, grad_scale=1.0, zero_grad=False):
+              decoupled=False, step, grad_scale=1.0, zero_grad=False, bias_corr=None):
     bc1, bc2s = 1 - beta1 ** step, math.sqrt(1 - beta2 ** step)
+    if bias_corr is not None:
+        bc1, bc2s = float(bias_corr[0]), float(bias_corr[1])
     g = grad * grad_scale
     if weight_decay:
         if decoupled:
