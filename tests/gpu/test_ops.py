@@ -160,3 +160,22 @@ def test_attention_fwd_bwd(S, Hq, Hkv, D):
     ops.attention_bwd(q, k, v, o, do, lse, dqkv2[:, : Hq * D], dqkv2[:, Hq * D: (Hq + Hkv) * D],
                       dqkv2[:, (Hq + Hkv) * D:], batch=B, seq=S, heads=Hq, kv_heads=Hkv, head_dim=D)
     assert torch.equal(dqkv, dqkv2)
+
+
+def test_adam_bias_corrections_from_device_equal_the_host_step():
+    import math
+
+    from resihp_megatron_b200 import ops
+
+    n, step, b1, b2 = 4099, 7, 0.9, 0.95
+    torch.manual_seed(1)
+    p0, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
+    m0, v0 = torch.randn(n, device="cuda") * 0.1, torch.rand(n, device="cuda") * 0.1
+    outs = []
+    for dev in (False, True):
+        p, m, v = p0.clone(), m0.clone(), v0.clone()
+        bc = torch.tensor([1 - b1 ** step, math.sqrt(1 - b2 ** step)], dtype=torch.float32, device="cuda")
+        ops.adam_step(p, g, m, v, lr=1e-3, beta1=b1, beta2=b2, step=1 if dev else step, bias_corr=bc if dev else None)
+        outs.append((p, m, v))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
