@@ -18,8 +18,8 @@ from .counter import count, launches, reset_launches
 
 __all__ = [
     "gemm", "error_state", "rmsnorm_fwd", "rmsnorm_bwd", "rope_", "swiglu_fwd", "swiglu_bwd", "embedding_fwd",
-    "embedding_bwd", "adam_step", "sumsq", "cross_entropy_", "attention_fwd", "attention_bwd", "rope_tables",
-    "EPI_BF16", "EPI_BF16_RES", "EPI_F32", "EPI_F32_ACC", "launches", "reset_launches",
+    "embedding_bwd", "gelu_fwd", "gelu_bwd", "adam_step", "sumsq", "cross_entropy_", "attention_fwd",
+    "attention_bwd", "rope_tables", "EPI_BF16", "EPI_BF16_RES", "EPI_F32", "EPI_F32_ACC", "launches", "reset_launches",
 ]
 
 
@@ -76,6 +76,22 @@ def swiglu_bwd(gu: torch.Tensor, da: torch.Tensor, out: torch.Tensor | None = No
     ext().swiglu_bwd(gu, da, dgu)
     count(1)
     return dgu
+
+
+def gelu_fwd(h: torch.Tensor, out: torch.Tensor | None = None):
+    """GELU (tanh form) of a bf16 tensor."""
+    a = torch.empty_like(h) if out is None else out
+    ext().gelu_fwd(h, a)
+    count(1)
+    return a
+
+
+def gelu_bwd(h: torch.Tensor, da: torch.Tensor, out: torch.Tensor | None = None):
+    """``da * gelu'(h)``; ``out`` may alias ``h`` (in place)."""
+    dh = torch.empty_like(h) if out is None else out
+    ext().gelu_bwd(h, da, dh)
+    count(1)
+    return dh
 
 
 def embedding_fwd(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):

@@ -158,6 +158,20 @@ void swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& da, torch::Tensor&
   RB_CALL(rb::swiglu_bwd(gu.data_ptr(), da.data_ptr(), dgu.data_ptr(), T, F, cur_stream()), "swiglu_bwd");
 }
 
+void gelu_fwd(const torch::Tensor& h, torch::Tensor& a) {
+  CHECK_BF16(h); CHECK_BF16(a);
+  TORCH_CHECK(h.numel() == a.numel(), "gelu_fwd: sizes differ");
+  const c10::cuda::CUDAGuard g(h.device());
+  RB_CALL(rb::gelu_fwd(h.data_ptr(), a.data_ptr(), h.numel(), cur_stream()), "gelu_fwd");
+}
+
+void gelu_bwd(const torch::Tensor& h, const torch::Tensor& da, torch::Tensor& dh) {
+  CHECK_BF16(h); CHECK_BF16(da); CHECK_BF16(dh);
+  TORCH_CHECK(h.numel() == da.numel() && h.numel() == dh.numel(), "gelu_bwd: sizes differ");
+  const c10::cuda::CUDAGuard g(h.device());
+  RB_CALL(rb::gelu_bwd(h.data_ptr(), da.data_ptr(), dh.data_ptr(), h.numel(), cur_stream()), "gelu_bwd");
+}
+
 void embedding_fwd(const torch::Tensor& ids, const torch::Tensor& E, torch::Tensor& x) {
   TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.is_contiguous(), "ids must be contiguous int64");
   CHECK_BF16(E); CHECK_BF16(x);
@@ -567,6 +581,74 @@ void moe_grad_pull(const c10::optional<torch::Tensor>& residual_grad, const torc
                             dlogits.data_ptr<float>(), cur_stream()), "moe_grad_pull");
 }
 
+// ---------------------------------------------------------------- block-scaled fp8
+static void check_fp8(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.dim() == 2 && t.is_contiguous(), name,
+              " must be a contiguous 2-D CUDA tensor of 1-byte elements");
+}
+
+static float* opt_f32(const c10::optional<torch::Tensor>& t, const char* name) {
+  if (!t.has_value()) return nullptr;
+  CHECK_F32((*t));
+  return t->data_ptr<float>();
+}
+
+// Quantise bf16 x [R, C]; outputs are optional (rowwise q [R, C], colwise q [C, R]).
+void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::optional<torch::Tensor>& q_row,
+                  const c10::optional<torch::Tensor>& s_row, const c10::optional<torch::Tensor>& q_col,
+                  const c10::optional<torch::Tensor>& s_col, const c10::optional<torch::Tensor>& amax) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2, "x must be a 2-D CUDA bf16 tensor");
+  const long long ldx = ld_of(x, "x");
+  const int R = x.size(0), C = x.size(1);
+  const long long nr = (R / 128), nc = (C / 128);
+  if (q_row.has_value()) {
+    check_fp8(*q_row, "q_row");
+    TORCH_CHECK(q_row->size(0) == R && q_row->size(1) == C, "q_row must be [R, C]");
+  }
+  if (q_col.has_value()) {
+    check_fp8(*q_col, "q_col");
+    TORCH_CHECK(q_col->size(0) == C && q_col->size(1) == R, "q_col must be [C, R]");
+  }
+  if (s_row.has_value()) TORCH_CHECK(s_row->numel() == (two_d ? nr * nc : static_cast<long long>(R) * nc), "bad s_row size");
+  if (s_col.has_value()) TORCH_CHECK(s_col->numel() == nr * C, "bad s_col size");
+  if (amax.has_value()) TORCH_CHECK(amax->numel() >= 1, "amax needs one element");
+  const c10::cuda::CUDAGuard g(x.device());
+  RB_CALL(rb::fp8_quantize(x.data_ptr(), ldx, R, C, static_cast<int>(fmt), two_d ? 1 : 0,
+                           q_row.has_value() ? q_row->data_ptr() : nullptr, opt_f32(s_row, "s_row"),
+                           q_col.has_value() ? q_col->data_ptr() : nullptr, opt_f32(s_col, "s_col"),
+                           reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream()),
+          "fp8_quantize");
+}
+
+static void check_scale(const torch::Tensor& s, int64_t kb, int64_t row, int64_t shift, int rows, int K,
+                        const char* name) {
+  CHECK_F32(s);
+  TORCH_CHECK(kb >= 0 && row >= 0 && (shift == 0 || shift == 7), name, ": bad scale addressing");
+  const long long last = (static_cast<long long>(K / 128) - 1) * kb + static_cast<long long>((rows - 1) >> shift) * row;
+  TORCH_CHECK(last < s.numel(), name, ": scale tensor too small for its addressing");
+}
+
+// out[M, N] (+)= alpha * sum_kb sa(m, kb) sb(n, kb) (a[m, kb] . b[n, kb])
+void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, int64_t sa_kb, int64_t sa_row,
+              int64_t sa_shift, const torch::Tensor& b, int64_t b_fmt, const torch::Tensor& sb, int64_t sb_kb,
+              int64_t sb_row, int64_t sb_shift, torch::Tensor& out, int64_t epi, double alpha) {
+  check_fp8(a, "a");
+  check_fp8(b, "b");
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K, "gemm_fp8: contraction sizes differ");
+  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == N, "gemm_fp8: out must be [M, N]");
+  TORCH_CHECK(out.scalar_type() == (epi == 0 ? torch::kBFloat16 : torch::kFloat32), "gemm_fp8: out dtype");
+  check_scale(sa, sa_kb, sa_row, sa_shift, M, K, "sa");
+  check_scale(sb, sb_kb, sb_row, sb_shift, N, K, "sb");
+  const c10::cuda::CUDAGuard g(a.device());
+  RB_CALL(rb::gemm_fp8(a.data_ptr(), static_cast<int>(a_fmt), b.data_ptr(), static_cast<int>(b_fmt),
+                       sa.data_ptr<float>(), sa_kb, sa_row, static_cast<int>(sa_shift), sb.data_ptr<float>(), sb_kb,
+                       sb_row, static_cast<int>(sb_shift), out.data_ptr(), ld_of(out, "out"), M, N, K,
+                       static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a), num_sms(a.get_device()),
+                       cur_stream()),
+          "gemm_fp8");
+}
+
 torch::Tensor error_state(int64_t device) { return error_word(static_cast<int>(device)); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -582,6 +664,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
+  m.def("gelu_fwd", &gelu_fwd);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
+        py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"));
+  m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM");
   m.def("adam_step", &adam_step);
   m.def("sumsq", &sumsq);
   m.def("cross_entropy", &cross_entropy);

@@ -241,6 +241,39 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* 
   store_bf16x8(dgu + gofs + F, du);
 }
 
+// GELU, tanh form (the GPT MLP activation): gelu(h) = 0.5 h (1 + tanh(c (h + 0.044715 h^3))),
+// c = sqrt(2 / pi).  Elementwise over [n] (n % 8 == 0).
+constexpr float kGeluC = 0.7978845608028654f;
+constexpr float kGeluA = 0.044715f;
+
+__global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ a, long long n8) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float x[8], o[8];
+  load_bf16x8(h + i * 8, x);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = 0.5f * x[j] * (1.f + tanhf(kGeluC * (x[j] + kGeluA * x[j] * x[j] * x[j])));
+  store_bf16x8(a + i * 8, o);
+}
+
+// dh = da * gelu'(h).  May run in place (dh == h).
+__global__ void gelu_bwd_kernel(const __nv_bfloat16* h, const __nv_bfloat16* __restrict__ da, __nv_bfloat16* dh,
+                                long long n8) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  float x[8], d[8], o[8];
+  load_bf16x8(h + i * 8, x);
+  load_bf16x8(da + i * 8, d);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float x2 = x[j] * x[j];
+    const float t = tanhf(kGeluC * (x[j] + kGeluA * x2 * x[j]));
+    const float dg = 0.5f * (1.f + t) + 0.5f * x[j] * (1.f - t * t) * kGeluC * (1.f + 3.f * kGeluA * x2);
+    o[j] = d[j] * dg;
+  }
+  store_bf16x8(dh + i * 8, o);
+}
+
 // x[t, :] = E[ids[t], :]
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
                                      __nv_bfloat16* __restrict__ x, int T, int H, int V, int* err) {
@@ -408,6 +441,23 @@ int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStre
   swiglu_bwd_kernel<<<cdiv_ll(total, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
                                                         reinterpret_cast<const __nv_bfloat16*>(da),
                                                         reinterpret_cast<__nv_bfloat16*>(dgu), T, F);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gelu_fwd(const void* h, void* a, long long n, cudaStream_t s) {
+  if (n % 8) return -1;
+  if (n == 0) return 0;
+  gelu_fwd_kernel<<<cdiv_ll(n / 8, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(h),
+                                                      reinterpret_cast<__nv_bfloat16*>(a), n / 8);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gelu_bwd(const void* h, const void* da, void* dh, long long n, cudaStream_t s) {
+  if (n % 8) return -1;
+  if (n == 0) return 0;
+  gelu_bwd_kernel<<<cdiv_ll(n / 8, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(h),
+                                                      reinterpret_cast<const __nv_bfloat16*>(da),
+                                                      reinterpret_cast<__nv_bfloat16*>(dh), n / 8);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -1,0 +1,539 @@
+// Block-scaled fp8 (E4M3 / E5M2) quantisation and GEMM on the 5th-generation tensor cores.
+//
+// Quantisation (fp8_quantize_kernel).  A bf16 [R, C] tensor is cut into 128 x 128 tiles, one
+// CTA per tile.  Each 1 x 128 block -- a row segment along C ("rowwise") or a column segment
+// along R ("colwise") -- or, for weights, each whole 128 x 128 tile ("2-D") gets a power-of-two
+// scale s = 2^e, the smallest with amax / s <= the format's largest finite value, and its
+// values are stored as fp8(x / s), rounded to nearest even (x / s itself is exact).  The
+// colwise output is written transposed ([C, R]) so that every GEMM operand is K-major.  Scales
+// are stored K-block major: the scale of operand row r in K-block kb sits at
+// kb * kb_stride + (r >> shift) * row_stride, so a tile's scales for one K-block are
+// contiguous.  Each CTA folds the magnitude of its tile into one atomicMax on the tensor's amax
+// word (bit pattern of |x|, so NaN and inf win), the input of the delayed-scaling history.
+//
+// GEMM (gemm_fp8_sm100).  D[m, n] = alpha * sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A(m, k) B(n, k)
+// for A [M, K] and B [N, K], both K-major fp8, K-blocks of 128.  One persistent CTA per SM:
+//   warp 0     : TMA producer, 6-deep ring of 128 x 128-byte A and B tiles, 128B swizzle
+//   warp 1     : TMEM allocator and single-thread issuer: per K-block four
+//                tcgen05.mma.kind::f8f6f4 (K = 32 each) into one of four 128-column TMEM
+//                partial accumulators
+//   warps 2..9 : promotion and epilogue, two warps per TMEM lane quadrant, each owning 64 of
+//                the tile's 128 columns: tcgen05.ld of each finished partial, scaled by
+//                sa(row) * sb(column) and added into fp32 registers, then the partial is
+//                released -- the MMAs of later K-blocks overlap the scaling of this one.  After
+//                the last K-block the same warps store the tile (bf16, fp32 or fp32 accumulate).
+// Power-of-two scales make every scaling exact; the only roundings are the fp8 casts and the
+// fp32 accumulation, so a PyTorch emulation reproduces the quantised bytes bit for bit.
+//
+// New work: the reference framework's fp8 is Transformer Engine inside Megatron-Core
+// (`resihp/runtime/generation_hooks.py:83-112` only re-initialises TE buffers) and its
+// semantics oracle emulates delayed scaling in float64 (`resihp/runtime/reference_model.py:44-46,
+// 204-227`).
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace rb {
+namespace {
+
+constexpr int kFp8E4M3 = 0;
+constexpr int kFp8E5M2 = 1;
+enum : int { kF8EpiBF16 = 0, kF8EpiF32 = 1, kF8EpiF32Acc = 2 };
+
+// Largest finite value of the format = 1.75 * 2^F.
+__host__ __device__ constexpr int fp8_max_exp(int fmt) { return fmt == kFp8E4M3 ? 8 : 15; }
+
+// Exponent e of the power-of-two scale: the smallest e with amax * 2^-e <= 1.75 * 2^F, clamped
+// to [-126, 126] so that 2^e and 2^-e are normal floats.  `amax_bits` is the bit pattern of a
+// non-negative float; zero, inf and NaN blocks get e = 0.
+__device__ __forceinline__ int fp8_scale_exp(uint32_t amax_bits, int F) {
+  const int E = static_cast<int>(amax_bits >> 23);
+  if (amax_bits == 0 || E == 255) return 0;
+  const uint32_t mant = amax_bits & 0x7fffffu;
+  int e = (E - 127) - F + (mant > 0x600000u ? 1 : 0);  // 1.75 = 1 + 0x600000 / 2^23
+  e = e < -126 ? -126 : (e > 126 ? 126 : e);
+  return e;
+}
+
+__device__ __forceinline__ float exp2_int(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
+// |x| of a bf16 as the bit pattern of an fp32 (an unsigned compare orders magnitudes).
+__device__ __forceinline__ uint32_t abs_bits_bf16(uint16_t h) { return static_cast<uint32_t>(h & 0x7fffu) << 16; }
+
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t cvt4_fp8(float a, float b, float c, float d, int fmt) {
+  const __nv_fp8_interpretation_t kind = fmt == kFp8E4M3 ? __NV_E4M3 : __NV_E5M2;
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, kind);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, kind);
+  return (lo & 0xffffu) | (hi << 16);
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
+
+// ------------------------------------------------------------------------------ quantisation
+struct QuantArgs {
+  const uint16_t* x;  // bf16 bits
+  long long ldx;
+  int R, C, fmt, two_d;
+  uint8_t* q_row;  // [R, C] or null
+  float* s_row;    // 1x128: [C/128][R];  2-D: [C/128][R/128] (shared by both outputs)
+  uint8_t* q_col;  // [C, R] (transposed) or null
+  float* s_col;    // 1x128: [R/128][C]
+  unsigned int* amax;
+};
+
+constexpr int kQT = 128;
+constexpr int kQPitch = 136;  // bf16 per shared-memory row (272 bytes: 16-byte aligned, staggered banks)
+
+__global__ void __launch_bounds__(256) fp8_quantize_kernel(QuantArgs p) {
+  __shared__ __align__(16) uint16_t tile[kQT * kQPitch];
+  __shared__ uint32_t rowmax[kQT];
+  __shared__ uint32_t colmax[2][kQT];
+  __shared__ uint32_t tile_max;
+  const int cb = blockIdx.x, rb = blockIdx.y;
+  const int r0 = rb * kQT, c0 = cb * kQT;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int F = fp8_max_exp(p.fmt);
+
+  for (int i = t; i < kQT * 16; i += 256) {
+    const int r = i >> 4, c8 = i & 15;
+    const uint4 v = *reinterpret_cast<const uint4*>(p.x + static_cast<long long>(r0 + r) * p.ldx + c0 + c8 * 8);
+    *reinterpret_cast<uint4*>(tile + r * kQPitch + c8 * 8) = v;
+  }
+  __syncthreads();
+
+#pragma unroll 4
+  for (int rr = 0; rr < 16; ++rr) {
+    const int r = warp * 16 + rr;
+    const uint2 u = *reinterpret_cast<const uint2*>(tile + r * kQPitch + lane * 4);
+    uint32_t m = max(max(abs_bits_bf16(u.x & 0xffffu), abs_bits_bf16(u.x >> 16)),
+                     max(abs_bits_bf16(u.y & 0xffffu), abs_bits_bf16(u.y >> 16)));
+    m = warp_max_u32(m);
+    if (lane == 0) rowmax[r] = m;
+  }
+  {
+    const int c = t & 127, h = t >> 7;
+    uint32_t m = 0;
+#pragma unroll 8
+    for (int r = h * 64; r < h * 64 + 64; ++r) m = max(m, abs_bits_bf16(tile[r * kQPitch + c]));
+    colmax[h][c] = m;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t m = max(max(rowmax[lane], rowmax[lane + 32]), max(rowmax[lane + 64], rowmax[lane + 96]));
+    m = warp_max_u32(m);
+    if (lane == 0) {
+      tile_max = m;
+      if (p.amax != nullptr) atomicMax(p.amax, m);
+    }
+  }
+  __syncthreads();
+  const uint32_t tmax = tile_max;
+
+  if (p.q_row != nullptr) {
+#pragma unroll 4
+    for (int rr = 0; rr < 16; ++rr) {
+      const int r = warp * 16 + rr;
+      const int e = fp8_scale_exp(p.two_d ? tmax : rowmax[r], F);
+      const float inv = exp2_int(-e);
+      const uint2 u = *reinterpret_cast<const uint2*>(tile + r * kQPitch + lane * 4);
+      const uint32_t q = cvt4_fp8(bf16_bits_to_float(u.x & 0xffffu) * inv, bf16_bits_to_float(u.x >> 16) * inv,
+                                  bf16_bits_to_float(u.y & 0xffffu) * inv, bf16_bits_to_float(u.y >> 16) * inv, p.fmt);
+      *reinterpret_cast<uint32_t*>(p.q_row + static_cast<long long>(r0 + r) * p.C + c0 + lane * 4) = q;
+      if (!p.two_d && lane == 0) p.s_row[static_cast<long long>(cb) * p.R + r0 + r] = exp2_int(e);
+    }
+  }
+  if (p.q_col != nullptr) {
+    const int c = t & 127, h = t >> 7;
+    const int e = fp8_scale_exp(p.two_d ? tmax : max(colmax[0][c], colmax[1][c]), F);
+    const float inv = exp2_int(-e);
+    uint8_t* dst = p.q_col + static_cast<long long>(c0 + c) * p.R + r0 + h * 64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = h * 64 + j * 16 + i * 4;
+        w[i] = cvt4_fp8(bf16_bits_to_float(tile[r * kQPitch + c]) * inv,
+                        bf16_bits_to_float(tile[(r + 1) * kQPitch + c]) * inv,
+                        bf16_bits_to_float(tile[(r + 2) * kQPitch + c]) * inv,
+                        bf16_bits_to_float(tile[(r + 3) * kQPitch + c]) * inv, p.fmt);
+      }
+      *reinterpret_cast<uint4*>(dst + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    if (!p.two_d && h == 0) p.s_col[static_cast<long long>(rb) * p.C + c0 + c] = exp2_int(e);
+  }
+  if (p.two_d && t == 0) p.s_row[static_cast<long long>(cb) * (p.R / kQT) + rb] = exp2_int(fp8_scale_exp(tmax, F));
+}
+
+// ------------------------------------------------------------------------------ GEMM
+struct F8GemmArgs {
+  int M, N, K;
+  uint32_t idesc;
+  void* D;
+  long long ldd;
+  float alpha;
+  const float* sa;
+  long long sa_kb, sa_row;
+  int sa_shift;
+  const float* sb;
+  long long sb_kb, sb_row;
+  int sb_shift;
+  int* err;
+};
+
+struct F8Cfg {
+  static constexpr int BM = 128, BN = 128, BK = 128;  // BK fp8 = 128 bytes = one swizzle row
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int PARTS = 4;  // TMEM partial accumulators of BN columns
+  static constexpr int TMEM_COLS = PARTS * BN;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * PARTS + 1;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 320;
+  static constexpr int PROMO_WARPS = 8;
+  static constexpr int GROUP_M = 16;
+};
+
+// Instruction descriptor of kind::f8f6f4 (f32 accumulation, both operands K-major).
+__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, int b_fmt) {
+  return (1u << 4) | (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(b_fmt) << 10) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread t of the warp gets lane (base + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void f8_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = F8Cfg::GROUP_M * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * F8Cfg::GROUP_M;
+  const int gsize = min(num_m - first_m, F8Cfg::GROUP_M);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+__device__ __forceinline__ bool f8_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <int EPI>
+__device__ __forceinline__ void f8_store_row(const float (&acc)[64], int row, int col0, const F8GemmArgs& p) {
+  if (EPI == kF8EpiBF16) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 u;
+      u.x = pack_bf16x2(acc[8 * j + 0] * p.alpha, acc[8 * j + 1] * p.alpha);
+      u.y = pack_bf16x2(acc[8 * j + 2] * p.alpha, acc[8 * j + 3] * p.alpha);
+      u.z = pack_bf16x2(acc[8 * j + 4] * p.alpha, acc[8 * j + 5] * p.alpha);
+      u.w = pack_bf16x2(acc[8 * j + 6] * p.alpha, acc[8 * j + 7] * p.alpha);
+      *reinterpret_cast<uint4*>(dst + 8 * j) = u;
+    }
+  } else {
+    float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float4 o = make_float4(acc[4 * j] * p.alpha, acc[4 * j + 1] * p.alpha, acc[4 * j + 2] * p.alpha,
+                             acc[4 * j + 3] * p.alpha);
+      if (EPI == kF8EpiF32Acc) {
+        const float4 old = *reinterpret_cast<const float4*>(dst + 4 * j);
+        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+      }
+      *reinterpret_cast<float4*>(dst + 4 * j) = o;
+    }
+  }
+}
+
+// SB_VEC: B's scale differs per output column (1x128 blocks along K for every row of B, laid out
+// contiguously over rows); otherwise it is one value per 128-column tile (128 x 128 blocks).
+template <bool SB_VEC, int EPI>
+__global__ void __launch_bounds__(320, 1)
+    gemm_fp8_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, F8GemmArgs p) {
+  using C = F8Cfg;
+  constexpr int STAGES = C::STAGES, PARTS = C::PARTS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto pfull_bar = [&](int j) { return smem_u32(&bars[2 * STAGES + j]); };
+  auto pempty_bar = [&](int j) { return smem_u32(&bars[2 * STAGES + PARTS + j]); };
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 2 * PARTS]);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int j = 0; j < PARTS; ++j) {
+      mbar_init(pfull_bar(j), 1);
+      mbar_init(pempty_bar(j), C::PROMO_WARPS);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = p.M / C::BM;
+  const int num_n = p.N / C::BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = p.K / C::BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mb, nb;
+        f8_tile_coords(tile, num_m, num_n, mb, nb);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fb, kb * C::BK, mb * C::BM);
+          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * C::BK, nb * C::BN);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0, part = 0;
+      uint32_t phase = 0, pphase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(pempty_bar(part), pphase ^ 1, abort_flag, p.err) ||
+              !mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+          const uint32_t d_tmem = tmem_base + part * C::BN;
+#pragma unroll
+          for (int k = 0; k < C::BK / 32; ++k) {
+            const uint64_t ad = make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
+            umma_f8(d_tmem, ad, bd, p.idesc, k != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          umma_commit(pfull_bar(part));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++part == PARTS) {
+            part = 0;
+            pphase ^= 1;
+          }
+        }
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ promotion + epilogue (warps 2..9)
+    const int q = warp & 3;             // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;   // which 64 of the tile's 128 columns
+    int part = 0;
+    uint32_t pphase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      f8_tile_coords(tile, num_m, num_n, mb, nb);
+      const int row = mb * C::BM + q * 32 + lane;
+      const int col0 = nb * C::BN + half * 64;
+      float acc[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+      bool ok = true;
+#pragma unroll 1
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const float sa = __ldg(p.sa + kb * p.sa_kb + static_cast<long long>(row >> p.sa_shift) * p.sa_row);
+        float s_tile = 0.f;
+        if (!SB_VEC) s_tile = sa * __ldg(p.sb + kb * p.sb_kb + static_cast<long long>(col0 >> p.sb_shift) * p.sb_row);
+        if (!f8_warp_wait(pfull_bar(part), pphase, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + part * C::BN + half * 64;
+        if (SB_VEC) {
+          // 16 columns at a time: per-column scales cost 4 more registers per column group
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tbase + c * 16, r);
+            const float4* sbp = reinterpret_cast<const float4*>(p.sb + kb * p.sb_kb + col0 + c * 16);
+            float4 sv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sv[i] = __ldg(sbp + i);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              acc[c * 16 + 4 * i + 0] = fmaf(__uint_as_float(r[4 * i + 0]), sa * sv[i].x, acc[c * 16 + 4 * i + 0]);
+              acc[c * 16 + 4 * i + 1] = fmaf(__uint_as_float(r[4 * i + 1]), sa * sv[i].y, acc[c * 16 + 4 * i + 1]);
+              acc[c * 16 + 4 * i + 2] = fmaf(__uint_as_float(r[4 * i + 2]), sa * sv[i].z, acc[c * 16 + 4 * i + 2]);
+              acc[c * 16 + 4 * i + 3] = fmaf(__uint_as_float(r[4 * i + 3]), sa * sv[i].w, acc[c * 16 + 4 * i + 3]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tbase + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(r[j]), s_tile, acc[c * 32 + j]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pempty_bar(part));
+        if (++part == PARTS) {
+          part = 0;
+          pphase ^= 1;
+        }
+      }
+      if (!ok) break;
+      f8_store_row<EPI>(acc, row, col0, p);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <bool SB_VEC, int EPI>
+int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a, int num_sms, cudaStream_t s) {
+  auto kern = gemm_fp8_sm100<SB_VEC, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F8Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  const int tiles = (a.M / F8Cfg::BM) * (a.N / F8Cfg::BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kern<<<grid, F8Cfg::THREADS, F8Cfg::SMEM_BYTES, s>>>(ta, tb, a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
+                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s) {
+  if (R <= 0 || C <= 0 || R % kQT || C % kQT || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -3;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || ldx % 8 || ldx < C) return -4;
+  if ((q_row != nullptr && s_row == nullptr) || (q_col != nullptr && !two_d && s_col == nullptr)) return -5;
+  if (two_d && s_row == nullptr) return -5;
+  if ((q_row != nullptr && (reinterpret_cast<uintptr_t>(q_row) & 15)) ||
+      (q_col != nullptr && (reinterpret_cast<uintptr_t>(q_col) & 15)))
+    return -6;
+  QuantArgs p{static_cast<const uint16_t*>(x), ldx, R, C, fmt, two_d, static_cast<uint8_t*>(q_row), s_row,
+              static_cast<uint8_t*>(q_col), s_col, amax};
+  dim3 grid(C / kQT, R / kQT);
+  fp8_quantize_kernel<<<grid, 256, 0, s>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
+             int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
+             int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 128) return -3;
+  if ((a_fmt != kFp8E4M3 && a_fmt != kFp8E5M2) || (b_fmt != kFp8E4M3 && b_fmt != kFp8E5M2)) return -3;
+  if ((sa_shift != 0 && sa_shift != 7) || (sb_shift != 0 && sb_shift != 7)) return -3;
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
+  const int esz = epi == kF8EpiBF16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(D) & 15) || (ldd * esz) % 16 || ldd < N) return -6;
+  const bool sb_vec = sb_shift == 0;
+  if (sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;
+  CUtensorMap ta, tb;
+  if (int rc = make_tmap_2d_sw128(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, 128, 128)) return -100 - rc;
+  if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, 128)) return -100 - rc;
+  F8GemmArgs a{M, N, K, make_idesc_f8(128, 128, a_fmt, b_fmt), D, ldd, alpha, sa, sa_kb, sa_row, sa_shift,
+               sb, sb_kb, sb_row, sb_shift, err};
+  switch (epi) {
+    case kF8EpiBF16: return sb_vec ? launch_fp8<true, kF8EpiBF16>(ta, tb, a, num_sms, stream)
+                                   : launch_fp8<false, kF8EpiBF16>(ta, tb, a, num_sms, stream);
+    case kF8EpiF32: return sb_vec ? launch_fp8<true, kF8EpiF32>(ta, tb, a, num_sms, stream)
+                                  : launch_fp8<false, kF8EpiF32>(ta, tb, a, num_sms, stream);
+    case kF8EpiF32Acc: return sb_vec ? launch_fp8<true, kF8EpiF32Acc>(ta, tb, a, num_sms, stream)
+                                     : launch_fp8<false, kF8EpiF32Acc>(ta, tb, a, num_sms, stream);
+  }
+  return -2;
+}
+
+}  // namespace rb

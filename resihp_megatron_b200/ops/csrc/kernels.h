@@ -22,6 +22,8 @@ int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos
                int T, int inverse, cudaStream_t s);
 int swiglu_fwd(const void* gu, void* a, int T, int F, cudaStream_t s);
 int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStream_t s);
+int gelu_fwd(const void* h, void* a, long long n, cudaStream_t s);
+int gelu_bwd(const void* h, const void* da, void* dh, long long n, cudaStream_t s);
 int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int V, int* err, cudaStream_t s);
 int embedding_bwd(const int64_t* vals, const int64_t* order, int T, const void* dx, float* dE, int H,
                   cudaStream_t s);
@@ -114,6 +116,13 @@ int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int se
 int gemm_ag_ready_words(int M, int K);
 int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* recv, int world, int slot, int M, int N,
                          int K, int* err, int num_sms, cudaStream_t stream);
+// Block-scaled fp8 (fp8_sm100.cu).  fmt: 0 = E4M3, 1 = E5M2.  Scale of operand row r in K-block kb:
+// s[kb * kb_stride + (r >> shift) * row_stride] (shift 0: 1 x 128 blocks, 7: 128 x 128 blocks).
+int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
+                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s);
+int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
+             int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
+             int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
 int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
 }  // namespace rb

@@ -1,0 +1,102 @@
+"""Block-scaled fp8 kernels against their PyTorch emulation: the quantiser bit for bit (bytes,
+scales, amax), the tcgen05 GEMM (all three scale layouts of a linear layer, every epilogue)
+against the fp32 sum of the same block products, and GELU against PyTorch."""
+
+import pytest
+import torch
+
+from resihp_megatron_b200.ops import fp8
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(R, C, seed=0, spread=3.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(R, C, device="cuda", generator=g) * torch.logspace(-spread, spread, C, device="cuda")[None, :]
+    return x.bfloat16()
+
+
+@pytest.mark.parametrize("two_d", [False, True])
+@pytest.mark.parametrize("fmt", [fp8.E4M3, fp8.E5M2])
+def test_quantize_matches_emulation_bitwise(fmt, two_d):
+    x = _x(384, 640, seed=fmt)
+    x[7, 9] = 0.0
+    x[128:256, 256:384] = 0.0  # an all-zero block / tile
+    amax = torch.zeros(1, device="cuda")
+    got = fp8.quantize(x, fmt, two_d=two_d, rowwise=True, colwise=True, amax=amax)
+    ref_amax = torch.zeros(1, device="cuda")
+    ref = fp8.quantize_reference(x, fmt, two_d=two_d, rowwise=True, colwise=True, amax=ref_amax)
+    torch.cuda.synchronize()
+    assert torch.equal(got.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
+    assert torch.equal(got.q_col.view(torch.uint8), ref.q_col.view(torch.uint8))
+    assert torch.equal(got.s_row, ref.s_row)
+    if not two_d:
+        assert torch.equal(got.s_col, ref.s_col)
+    assert amax.item() == ref_amax.item() == x.float().abs().max().item()
+
+
+def test_quantize_strided_input_and_running_amax():
+    base = _x(256, 768, seed=3)
+    x = base[:, 128:640]  # row stride 768
+    amax = torch.full((1,), 1e6, device="cuda")
+    got = fp8.quantize(x, fp8.E4M3, rowwise=True, amax=amax)
+    ref = fp8.quantize_reference(x.contiguous(), fp8.E4M3, rowwise=True)
+    assert torch.equal(got.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
+    assert amax.item() == 1e6  # a running max keeps the larger value
+
+
+def _check(out, ref, tol):
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err <= tol * ref.float().abs().max().item() + 1e-30, err
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1024, 1024, 2048), (128, 128, 128)])
+def test_gemm_forward_dgrad_wgrad(M, N, K):
+    x = _x(M, K, seed=1, spread=1.0)
+    w = (_x(N, K, seed=2, spread=0.5).float() * 0.05).bfloat16()
+    dy = (_x(M, N, seed=4, spread=1.0).float() * 1e-3).bfloat16()
+    xq = fp8.quantize(x, fp8.E4M3, rowwise=True, colwise=True)
+    wq = fp8.quantize(w, fp8.E4M3, two_d=True, rowwise=True, colwise=True)
+    dyq = fp8.quantize(dy, fp8.E5M2, rowwise=True, colwise=True)
+    # forward: per-row A scales, 128 x 128 B scales
+    y = fp8.gemm(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32)
+    _check(y, fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32), 1e-5)
+    yb = fp8.gemm(xq.rowwise(), wq.rowwise())
+    _check(yb, fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32), 8e-3)
+    # dgrad: E5M2 x E4M3, transposed 2-D weight scales
+    dx = fp8.gemm(dyq.rowwise(), wq.colwise(), out_dtype=torch.float32)
+    _check(dx, fp8.gemm_reference(dyq.rowwise(), wq.colwise(), out_dtype=torch.float32), 1e-5)
+    # wgrad: per-column B scales, fp32 accumulate with alpha
+    g0 = torch.randn(N, K, device="cuda")
+    g = g0.clone()
+    fp8.gemm(dyq.colwise(), xq.colwise(), out=g, accumulate=True, alpha=0.5)
+    ref = g0.clone()
+    fp8.gemm_reference(dyq.colwise(), xq.colwise(), out=ref, accumulate=True, alpha=0.5)
+    _check(g - g0, ref - g0, 1e-5)
+    # and the whole thing tracks the bf16 product
+    full = (x.float() @ w.float().t())
+    assert ((y - full).norm() / full.norm()).item() < 0.05
+
+
+def test_gemm_rejects_unaligned():
+    a = fp8.quantize(_x(128, 128), fp8.E4M3)
+    with pytest.raises(RuntimeError):
+        bad = fp8.Fp8Operand(a.q_row[:, :64].contiguous(), a.s_row, 128, 1, 0, fp8.E4M3)
+        fp8.gemm(bad, bad)
+
+
+def test_gelu_fwd_bwd():
+    from resihp_megatron_b200 import ops
+
+    h = (torch.randn(300, 1024, device="cuda") * 3).bfloat16()
+    da = torch.randn(300, 1024, device="cuda").bfloat16()
+    a = ops.gelu_fwd(h)
+    hf = h.float().requires_grad_(True)
+    ref = torch.nn.functional.gelu(hf, approximate="tanh")
+    assert ((a.float() - ref).abs().max() / ref.abs().max()).item() < 1e-2
+    ref.backward(da.float())
+    dh = ops.gelu_bwd(h, da)
+    assert ((dh.float() - hf.grad).abs().max() / hf.grad.abs().max()).item() < 1e-2
+    h2 = h.clone()
+    ops.gelu_bwd(h2, da, out=h2)  # in place
+    assert torch.equal(h2, dh)
