@@ -631,21 +631,43 @@ static void check_scale(const torch::Tensor& s, int64_t kb, int64_t row, int64_t
 // out[M, N] (+)= alpha * sum_kb sa(m, kb) sb(n, kb) (a[m, kb] . b[n, kb])
 void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, int64_t sa_kb, int64_t sa_row,
               int64_t sa_shift, const torch::Tensor& b, int64_t b_fmt, const torch::Tensor& sb, int64_t sb_kb,
-              int64_t sb_row, int64_t sb_shift, torch::Tensor& out, int64_t epi, double alpha) {
+              int64_t sb_row, int64_t sb_shift, const c10::optional<torch::Tensor>& out, int64_t epi, double alpha,
+              const c10::optional<torch::Tensor>& residual, const std::vector<int64_t>& rs_ptrs, int64_t rs_slot) {
   check_fp8(a, "a");
   check_fp8(b, "b");
   const int M = a.size(0), K = a.size(1), N = b.size(0);
   TORCH_CHECK(b.size(1) == K, "gemm_fp8: contraction sizes differ");
-  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == N, "gemm_fp8: out must be [M, N]");
-  TORCH_CHECK(out.scalar_type() == (epi == 0 ? torch::kBFloat16 : torch::kFloat32), "gemm_fp8: out dtype");
+  void* dptr = nullptr;
+  long long ldd = 0;
+  std::vector<void*> dst;
+  if (epi == 4) {  // scatter into receive slots (peer memory); no local output
+    TORCH_CHECK(!rs_ptrs.empty(), "gemm_fp8: the scatter epilogue needs receive pointers");
+    for (auto p : rs_ptrs) dst.push_back(reinterpret_cast<void*>(p));
+  } else {
+    TORCH_CHECK(out.has_value(), "gemm_fp8: out is required");
+    const auto& o = *out;
+    TORCH_CHECK(o.is_cuda() && o.dim() == 2 && o.size(0) == M && o.size(1) == N, "gemm_fp8: out must be [M, N]");
+    TORCH_CHECK(o.scalar_type() == ((epi == 0 || epi == 3) ? torch::kBFloat16 : torch::kFloat32), "gemm_fp8: out dtype");
+    dptr = o.data_ptr();
+    ldd = ld_of(o, "out");
+  }
+  const void* rptr = nullptr;
+  long long ldr = 0;
+  if (epi == 3) {
+    TORCH_CHECK(residual.has_value(), "gemm_fp8: the residual epilogue needs a residual");
+    const auto& r = *residual;
+    TORCH_CHECK(r.is_cuda() && r.scalar_type() == torch::kBFloat16 && r.size(0) == M && r.size(1) == N, "bad residual");
+    rptr = r.data_ptr();
+    ldr = ld_of(r, "residual");
+  }
   check_scale(sa, sa_kb, sa_row, sa_shift, M, K, "sa");
   check_scale(sb, sb_kb, sb_row, sb_shift, N, K, "sb");
   const c10::cuda::CUDAGuard g(a.device());
   RB_CALL(rb::gemm_fp8(a.data_ptr(), static_cast<int>(a_fmt), b.data_ptr(), static_cast<int>(b_fmt),
                        sa.data_ptr<float>(), sa_kb, sa_row, static_cast<int>(sa_shift), sb.data_ptr<float>(), sb_kb,
-                       sb_row, static_cast<int>(sb_shift), out.data_ptr(), ld_of(out, "out"), M, N, K,
-                       static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a), num_sms(a.get_device()),
-                       cur_stream()),
+                       sb_row, static_cast<int>(sb_shift), dptr, ldd, M, N, K, static_cast<int>(epi),
+                       static_cast<float>(alpha), err_ptr(a), num_sms(a.get_device()), cur_stream(), rptr, ldr,
+                       dst.empty() ? nullptr : dst.data(), static_cast<int>(dst.size()), static_cast<int>(rs_slot)),
           "gemm_fp8");
 }
 
@@ -668,7 +690,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_bwd", &gelu_bwd);
   m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
         py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"));
-  m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM");
+  m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM", py::arg("a"), py::arg("a_fmt"), py::arg("sa"),
+        py::arg("sa_kb"), py::arg("sa_row"), py::arg("sa_shift"), py::arg("b"), py::arg("b_fmt"), py::arg("sb"),
+        py::arg("sb_kb"), py::arg("sb_row"), py::arg("sb_shift"), py::arg("out"), py::arg("epi"), py::arg("alpha"),
+        py::arg("residual") = py::none(), py::arg("rs_ptrs") = std::vector<int64_t>{}, py::arg("rs_slot") = 0);
   m.def("adam_step", &adam_step);
   m.def("sumsq", &sumsq);
   m.def("cross_entropy", &cross_entropy);

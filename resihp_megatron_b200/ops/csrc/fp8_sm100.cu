@@ -21,7 +21,10 @@
 //                the tile's 128 columns: tcgen05.ld of each finished partial, scaled by
 //                sa(row) * sb(column) and added into fp32 registers, then the partial is
 //                released -- the MMAs of later K-blocks overlap the scaling of this one.  After
-//                the last K-block the same warps store the tile (bf16, fp32 or fp32 accumulate).
+//                the last K-block the same warps store the tile: bf16 (optionally plus a
+//                residual), fp32, fp32 accumulate, or bf16 rows scattered to the receive slots of
+//                their owner ranks (peer stores over NVLink: the GEMM -> reduce-scatter of a
+//                row-parallel layer).
 // Power-of-two scales make every scaling exact; the only roundings are the fp8 casts and the
 // fp32 accumulation, so a PyTorch emulation reproduces the quantised bytes bit for bit.
 //
@@ -41,7 +44,8 @@ namespace {
 
 constexpr int kFp8E4M3 = 0;
 constexpr int kFp8E5M2 = 1;
-enum : int { kF8EpiBF16 = 0, kF8EpiF32 = 1, kF8EpiF32Acc = 2 };
+enum : int { kF8EpiBF16 = 0, kF8EpiF32 = 1, kF8EpiF32Acc = 2, kF8EpiBF16Res = 3, kF8EpiScatter = 4 };
+constexpr int kF8MaxTP = 8;
 
 // Largest finite value of the format = 1.75 * 2^F.
 __host__ __device__ constexpr int fp8_max_exp(int fmt) { return fmt == kFp8E4M3 ? 8 : 15; }
@@ -188,6 +192,13 @@ struct F8GemmArgs {
   long long sb_kb, sb_row;
   int sb_shift;
   int* err;
+  // kF8EpiBF16Res: D = alpha * acc + R (bf16, leading dimension ldr)
+  const __nv_bfloat16* R;
+  long long ldr;
+  // kF8EpiScatter (GEMM -> reduce-scatter): row m goes, as bf16, to rank q = m / rs_rows, into
+  // slot `rs_slot` of its receive buffer ([world][rs_rows][N], possibly another GPU's memory)
+  int rs_slot, rs_rows;
+  void* rs_dst[kF8MaxTP];
 };
 
 struct F8Cfg {
@@ -249,15 +260,30 @@ __device__ __forceinline__ bool f8_warp_wait(uint32_t bar, uint32_t parity, vola
 
 template <int EPI>
 __device__ __forceinline__ void f8_store_row(const float (&acc)[64], int row, int col0, const F8GemmArgs& p) {
-  if (EPI == kF8EpiBF16) {
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+  if (EPI == kF8EpiBF16 || EPI == kF8EpiBF16Res || EPI == kF8EpiScatter) {
+    __nv_bfloat16* dst;
+    if (EPI == kF8EpiScatter) {
+      const int q = row / p.rs_rows;
+      dst = reinterpret_cast<__nv_bfloat16*>(p.rs_dst[q]) +
+            (static_cast<long long>(p.rs_slot) * p.rs_rows + (row - q * p.rs_rows)) * p.N + col0;
+    } else {
+      dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = acc[8 * j + i] * p.alpha;
+      if (EPI == kF8EpiBF16Res) {
+        const uint4 r = *reinterpret_cast<const uint4*>(p.R + row * p.ldr + col0 + 8 * j);
+        const float2 f0 = unpack_bf16x2(r.x), f1 = unpack_bf16x2(r.y), f2 = unpack_bf16x2(r.z), f3 = unpack_bf16x2(r.w);
+        v[0] += f0.x; v[1] += f0.y; v[2] += f1.x; v[3] += f1.y; v[4] += f2.x; v[5] += f2.y; v[6] += f3.x; v[7] += f3.y;
+      }
       uint4 u;
-      u.x = pack_bf16x2(acc[8 * j + 0] * p.alpha, acc[8 * j + 1] * p.alpha);
-      u.y = pack_bf16x2(acc[8 * j + 2] * p.alpha, acc[8 * j + 3] * p.alpha);
-      u.z = pack_bf16x2(acc[8 * j + 4] * p.alpha, acc[8 * j + 5] * p.alpha);
-      u.w = pack_bf16x2(acc[8 * j + 6] * p.alpha, acc[8 * j + 7] * p.alpha);
+      u.x = pack_bf16x2(v[0], v[1]);
+      u.y = pack_bf16x2(v[2], v[3]);
+      u.z = pack_bf16x2(v[4], v[5]);
+      u.w = pack_bf16x2(v[6], v[7]);
       *reinterpret_cast<uint4*>(dst + 8 * j) = u;
     }
   } else {
@@ -511,20 +537,38 @@ int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d,
 
 int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
              int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
-             int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream) {
+             int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream, const void* R,
+             long long ldr, void* const* rs_dst, int world, int rs_slot) {
   if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 128) return -3;
   if ((a_fmt != kFp8E4M3 && a_fmt != kFp8E5M2) || (b_fmt != kFp8E4M3 && b_fmt != kFp8E5M2)) return -3;
   if ((sa_shift != 0 && sa_shift != 7) || (sb_shift != 0 && sb_shift != 7)) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
-  const int esz = epi == kF8EpiBF16 ? 2 : 4;
-  if ((reinterpret_cast<uintptr_t>(D) & 15) || (ldd * esz) % 16 || ldd < N) return -6;
+  F8GemmArgs a{};
+  if (epi == kF8EpiScatter) {
+    if (world < 1 || world > kF8MaxTP || M % world || rs_slot < 0) return -8;
+    for (int q = 0; q < world; ++q) {
+      if (rs_dst[q] == nullptr || (reinterpret_cast<uintptr_t>(rs_dst[q]) & 15)) return -8;
+      a.rs_dst[q] = rs_dst[q];
+    }
+    a.rs_slot = rs_slot;
+    a.rs_rows = M / world;
+  } else {
+    const int esz = (epi == kF8EpiBF16 || epi == kF8EpiBF16Res) ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(D) & 15) || (ldd * esz) % 16 || ldd < N) return -6;
+  }
+  if (epi == kF8EpiBF16Res && (R == nullptr || (reinterpret_cast<uintptr_t>(R) & 15) || ldr % 8 || ldr < N)) return -9;
   const bool sb_vec = sb_shift == 0;
   if (sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_2d_sw128(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, 128, 128)) return -100 - rc;
   if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, 128)) return -100 - rc;
-  F8GemmArgs a{M, N, K, make_idesc_f8(128, 128, a_fmt, b_fmt), D, ldd, alpha, sa, sa_kb, sa_row, sa_shift,
-               sb, sb_kb, sb_row, sb_shift, err};
+  a.M = M; a.N = N; a.K = K;
+  a.idesc = make_idesc_f8(128, 128, a_fmt, b_fmt);
+  a.D = D; a.ldd = ldd; a.alpha = alpha;
+  a.sa = sa; a.sa_kb = sa_kb; a.sa_row = sa_row; a.sa_shift = sa_shift;
+  a.sb = sb; a.sb_kb = sb_kb; a.sb_row = sb_row; a.sb_shift = sb_shift;
+  a.err = err;
+  a.R = static_cast<const __nv_bfloat16*>(R); a.ldr = ldr;
   switch (epi) {
     case kF8EpiBF16: return sb_vec ? launch_fp8<true, kF8EpiBF16>(ta, tb, a, num_sms, stream)
                                    : launch_fp8<false, kF8EpiBF16>(ta, tb, a, num_sms, stream);
@@ -532,6 +576,10 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
                                   : launch_fp8<false, kF8EpiF32>(ta, tb, a, num_sms, stream);
     case kF8EpiF32Acc: return sb_vec ? launch_fp8<true, kF8EpiF32Acc>(ta, tb, a, num_sms, stream)
                                      : launch_fp8<false, kF8EpiF32Acc>(ta, tb, a, num_sms, stream);
+    case kF8EpiBF16Res: return sb_vec ? launch_fp8<true, kF8EpiBF16Res>(ta, tb, a, num_sms, stream)
+                                      : launch_fp8<false, kF8EpiBF16Res>(ta, tb, a, num_sms, stream);
+    case kF8EpiScatter: return sb_vec ? launch_fp8<true, kF8EpiScatter>(ta, tb, a, num_sms, stream)
+                                      : launch_fp8<false, kF8EpiScatter>(ta, tb, a, num_sms, stream);
   }
   return -2;
 }

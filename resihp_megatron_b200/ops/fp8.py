@@ -39,7 +39,7 @@ E4M3, E5M2 = 0, 1
 DTYPES = {E4M3: torch.float8_e4m3fn, E5M2: torch.float8_e5m2}
 MAX_EXP = {E4M3: 8, E5M2: 15}  # largest finite value = 1.75 * 2^MAX_EXP
 BLOCK = 128
-EPI_BF16, EPI_F32, EPI_F32_ACC = 0, 1, 2
+EPI_BF16, EPI_F32, EPI_F32_ACC, EPI_BF16_RES, EPI_SCATTER = 0, 1, 2, 3, 4
 
 
 def fmt_of(name: str | int) -> int:
@@ -143,8 +143,27 @@ def _u8(t):
 
 
 def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-         accumulate: bool = False, alpha: float = 1.0) -> torch.Tensor:
-    """``out [a.rows, b.rows] (+)= alpha * block-scaled a @ b^T`` (all dims multiples of 128)."""
+         accumulate: bool = False, alpha: float = 1.0, residual: torch.Tensor | None = None,
+         scatter: tuple[list[int], int] | None = None) -> torch.Tensor | None:
+    """``out [a.rows, b.rows] (+)= alpha * block-scaled a @ b^T`` (all dims multiples of 128).
+    ``residual``: bf16 ``out = product + residual``.  ``scatter = (recv_ptrs, slot)``: no local
+    output; row ``m`` is stored (bf16) into rank ``m // (rows / world)``'s receive buffer
+    ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter."""
+    if scatter is not None:
+        ptrs, slot = scatter
+        ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
+                       b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, None, EPI_SCATTER,
+                       float(alpha), None, [int(p) for p in ptrs], int(slot))
+        count(1)
+        return None
+    if residual is not None:
+        if out is None:
+            out = torch.empty(a.rows, b.rows, dtype=torch.bfloat16, device=a.data.device)
+        ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
+                       b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, EPI_BF16_RES,
+                       float(alpha), residual)
+        count(1)
+        return out
     if accumulate:
         if out is None or out.dtype != torch.float32:
             raise ValueError("accumulate=True needs an fp32 `out`")
@@ -216,7 +235,8 @@ def quantize_reference(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = 
 
 
 def gemm_reference(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None,
-                   out_dtype: torch.dtype = torch.bfloat16, accumulate: bool = False, alpha: float = 1.0):
+                   out_dtype: torch.dtype = torch.bfloat16, accumulate: bool = False, alpha: float = 1.0,
+                   residual: torch.Tensor | None = None):
     """``gemm`` in PyTorch: block products summed in fp32 (the kernel's order of K-blocks)."""
     nk = a.K // BLOCK
     sa, sb = a.scale_matrix(), b.scale_matrix()
@@ -226,6 +246,8 @@ def gemm_reference(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = N
         sl = slice(kb * BLOCK, (kb + 1) * BLOCK)
         acc += (af[:, sl] @ bf[:, sl].t()) * (sa[:, kb:kb + 1] * sb[:, kb][None, :])
     acc = acc * alpha
+    if residual is not None:
+        acc = acc + residual.float()
     if accumulate:
         out += acc
         return out

@@ -100,3 +100,23 @@ def test_gelu_fwd_bwd():
     h2 = h.clone()
     ops.gelu_bwd(h2, da, out=h2)  # in place
     assert torch.equal(h2, dh)
+
+
+def test_gemm_residual_and_scatter_epilogues():
+    M, N, K, world = 512, 256, 384, 4
+    x = _x(M, K, seed=5, spread=1.0)
+    w = (_x(N, K, seed=6, spread=0.5).float() * 0.05).bfloat16()
+    res = _x(M, N, seed=7, spread=0.0)
+    xq = fp8.quantize(x, fp8.E4M3)
+    wq = fp8.quantize(w, fp8.E4M3, two_d=True)
+    ref = fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32)
+    y = fp8.gemm(xq.rowwise(), wq.rowwise(), residual=res)
+    _check(y, ref + res.float(), 8e-3)
+    # scatter: rows of rank q's share land in slot 1 of buffer q ([world][M / world][N])
+    rows = M // world
+    bufs = [torch.zeros(world, rows, N, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    fp8.gemm(xq.rowwise(), wq.rowwise(), scatter=([b.data_ptr() for b in bufs], 1))
+    full = fp8.gemm(xq.rowwise(), wq.rowwise())
+    for q in range(world):
+        assert torch.equal(bufs[q][1], full[q * rows:(q + 1) * rows])
+        assert bufs[q][0].abs().sum().item() == 0 and bufs[q][2:].abs().sum().item() == 0
