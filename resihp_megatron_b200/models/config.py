@@ -29,6 +29,8 @@ class GPTConfig:
     num_experts: int = 0
     top_k: int = 2
     moe_every: int = 1
+    # MLP: "swiglu" (w1, w3 -> silu(w1 x) * w3 x -> w2) or "gelu" (w1 -> gelu -> w2, the GPT MLP)
+    mlp: str = "swiglu"
 
     @property
     def head_dim(self) -> int:
@@ -42,10 +44,27 @@ class GPTConfig:
     def is_moe(self) -> bool:
         return self.num_experts > 0
 
+    @property
+    def gated(self) -> bool:
+        """Gated MLP (SwiGLU: two input projections) or plain (GELU: one)."""
+        if self.mlp not in ("swiglu", "gelu"):
+            raise ValueError(f"unknown mlp {self.mlp!r}")
+        return self.mlp == "swiglu"
+
+    @property
+    def mlp_in(self) -> int:
+        """Rows of the MLP's input projection (``2 * ffn`` gated, ``ffn`` plain)."""
+        return (2 if self.gated else 1) * self.ffn
+
+    @property
+    def mlp_mats(self) -> int:
+        return 3 if self.gated else 2
+
     def layer_params(self) -> int:
         H, F = self.hidden, self.ffn
         attn = self.qkv_rows * H + H * self.heads * self.head_dim + 2 * H
-        mlp = (3 * H * F) * (self.num_experts if self.is_moe else 1) + (H * self.num_experts if self.is_moe else 0)
+        experts = self.num_experts if self.is_moe else 1
+        mlp = self.mlp_mats * H * F * experts + (H * self.num_experts if self.is_moe else 0)
         return attn + mlp
 
     def num_params(self) -> int:
@@ -55,7 +74,8 @@ class GPTConfig:
         """Training FLOPs per token: 6 x matmul params + causal attention (fwd + bwd)."""
         S = seq_len or self.seq_len
         H, F = self.hidden, self.ffn
-        dense_mm = self.qkv_rows * H + H * self.heads * self.head_dim + (3 * H * F) * (self.top_k if self.is_moe else 1)
+        dense_mm = (self.qkv_rows * H + H * self.heads * self.head_dim
+                    + (self.mlp_mats * H * F) * (self.top_k if self.is_moe else 1))
         matmul = self.layers * dense_mm + self.vocab_size * H
         attn = self.layers * 4 * self.heads * self.head_dim * S / 2  # QK^T and PV, causal half, per token
         return 6.0 * matmul + 3.0 * attn
@@ -72,7 +92,7 @@ LLAMA3_8B = GPTConfig(name="llama3-8b", vocab_size=128256, hidden=4096, layers=3
 MIXTRAL_8X7B = GPTConfig(name="mixtral-8x7b", vocab_size=32000, hidden=4096, layers=32, heads=32, kv_heads=8,
                          ffn=14336, seq_len=4096, rope_theta=1000000.0, num_experts=8, top_k=2)
 GPT_1P3B = GPTConfig(name="gpt-1.3b", vocab_size=50304, hidden=2048, layers=24, heads=16, kv_heads=16, ffn=8192,
-                     seq_len=2048, rope_theta=10000.0)
+                     seq_len=2048, rope_theta=10000.0, mlp="gelu")
 TINY = GPTConfig(name="tiny", vocab_size=512, hidden=256, layers=2, heads=4, kv_heads=2, ffn=512, seq_len=128)
 
 PRESETS = {c.name: c for c in (LLAMA3_8B, MIXTRAL_8X7B, GPT_1P3B, TINY)}

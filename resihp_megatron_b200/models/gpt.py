@@ -13,6 +13,10 @@ Per layer (``T`` tokens of one micro-batch):
     h2  = rmsnorm(x2)                gu  = h2 W13^T          a = silu(gate) * up
     x'  = x2 + a W2^T
 
+With ``cfg.mlp == "gelu"`` (the GPT MLP) the input projection is ``w1`` alone and
+``a = gelu(h2 W1^T)``.  With an ``Fp8Recipe`` the four projections of every layer run as
+block-scaled fp8 GEMMs (``models.fp8_linear``); the LM head stays bf16.
+
 Saved for backward: x, x2, qkv (after RoPE), o, lse, gu and the two rstd vectors; h, h2 and
 ``a`` are recomputed (cheap, bandwidth bound), which keeps activations at ~23 bytes x hidden
 per token per layer.  Gradients of every GEMM use the MN-major operand modes of the GEMM
@@ -48,7 +52,7 @@ def layer_param_specs(cfg: GPTConfig, layer: int, tp_rank: int = 0, tp_size: int
             ParamSpec(p + "wqkv", ((cfg.heads + 2 * cfg.kv_heads) * D, H)),
             ParamSpec(p + "wo", (H, cfg.heads * D)),
             ParamSpec(p + "mlp_norm", (H,), init="ones"),
-            ParamSpec(p + "w13", (2 * F, H)),
+            ParamSpec(p + fc1_name(cfg), (cfg.mlp_in, H)),
             ParamSpec(p + "w2", (H, F)),
         ]
     # Sharded: q/k/v and gate/up are stored as separate logical tensors so each rank's slice
@@ -61,9 +65,22 @@ def layer_param_specs(cfg: GPTConfig, layer: int, tp_rank: int = 0, tp_size: int
         ParamSpec(p + "wo", (H, nq * D), (H, cfg.heads * D), 1, (qh[0] * D, qh[1] * D)),
         ParamSpec(p + "mlp_norm", (H,), init="ones"),
         ParamSpec(p + "w1", (nf, H), (F, H), 0, fr),
-        ParamSpec(p + "w3", (nf, H), (F, H), 0, fr),
+    ] + ([ParamSpec(p + "w3", (nf, H), (F, H), 0, fr)] if cfg.gated else []) + [
         ParamSpec(p + "w2", (H, nf), (H, F), 1, fr),
     ]
+
+
+def fc1_name(cfg: GPTConfig) -> str:
+    """The MLP's input projection in the unsharded layout: ``w13 = [w1; w3]`` (SwiGLU) or ``w1``."""
+    return "w13" if cfg.gated else "w1"
+
+
+def mlp_act_fwd(cfg: GPTConfig, gu: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    return ops.swiglu_fwd(gu, out=out) if cfg.gated else ops.gelu_fwd(gu, out=out)
+
+
+def mlp_act_bwd(cfg: GPTConfig, gu: torch.Tensor, da: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    return ops.swiglu_bwd(gu, da, out=out) if cfg.gated else ops.gelu_bwd(gu, da, out=out)
 
 
 def model_param_specs(cfg: GPTConfig, layers: range | None = None, first: bool = True, last: bool = True):
@@ -83,7 +100,9 @@ class LlamaModel:
 
     def __init__(self, cfg: GPTConfig, device="cuda", *, micro_batch: int = 1, seq_len: int | None = None,
                  seed: int = 0, layers: range | None = None, first: bool = True, last: bool = True,
-                 shard_rank: int = 0, shard_count: int = 1, buffer_factory=None, opt_factory=None):
+                 shard_rank: int = 0, shard_count: int = 1, buffer_factory=None, opt_factory=None, fp8=None):
+        """``fp8``: an ``Fp8Recipe`` to run the four linear layers of every decoder layer in
+        block-scaled fp8 (the LM head stays bf16)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.mb = micro_batch
@@ -96,6 +115,12 @@ class LlamaModel:
                                  buffer_factory=buffer_factory, opt_factory=opt_factory)
         self.params.initialize(seed, cfg.init_std)
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
+        self.fc1 = fc1_name(cfg)
+        self.f8 = None
+        if fp8 is not None:
+            from .fp8_linear import Fp8Linears
+
+            self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
         self._alloc()
 
     # ------------------------------------------------------------------ buffers
@@ -123,7 +148,7 @@ class LlamaModel:
         self.qkv = [torch.empty(T, cfg.qkv_rows, **bf) for _ in range(L)]
         self.o = [torch.empty(T, cfg.heads * cfg.head_dim, **bf) for _ in range(L)]
         self.lse = [torch.empty(self.mb, cfg.heads, self.S, **f32) for _ in range(L)]
-        self.gu = [torch.empty(T, 2 * F, **bf) for _ in range(L)]
+        self.gu = [torch.empty(T, cfg.mlp_in, **bf) for _ in range(L)]
         self.rstd1 = [torch.empty(T, **f32) for _ in range(L)]
         self.rstd2 = [torch.empty(T, **f32) for _ in range(L)]
         self.ws_h = torch.empty(T, H, **bf)
@@ -170,21 +195,47 @@ class LlamaModel:
             ops.embedding_fwd(ids, P.w("embed"), out=self.xs[0])
         else:
             self.xs[0].copy_(x_in)
+        if self.f8 is not None:
+            self.refresh_fp8_weights()
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = self.xs[i]
             h, r1 = self._rmsnorm(x, P.w(p + "attn_norm"), self.ws_h, self.rstd1[i])
-            ops.gemm(h, P.w(p + "wqkv"), out=self.qkv[i])
+            self._linear(l, "qkv", h, P.w(p + "wqkv"), self.qkv[i])
             q, k, v = self._views(i)
             ops.rope_(q, cfg.heads, cfg.head_dim, self.cos, self.sin, self.S)
             ops.rope_(k, cfg.kv_heads, cfg.head_dim, self.cos, self.sin, self.S)
             self._attention_fwd(i, q, k, v)
-            ops.gemm(self.o[i], P.w(p + "wo"), residual=x, out=self.x2[i])
+            self._linear(l, "o", self.o[i], P.w(p + "wo"), self.x2[i], residual=x)
             h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])
-            ops.gemm(h2, P.w(p + "w13"), out=self.gu[i])
-            ops.swiglu_fwd(self.gu[i], out=self.ws_a)
-            ops.gemm(self.ws_a, P.w(p + "w2"), residual=self.x2[i], out=self.xs[i + 1])
+            self._linear(l, "fc1", h2, P.w(p + self.fc1), self.gu[i])
+            mlp_act_fwd(cfg, self.gu[i], self.ws_a)
+            self._linear(l, "fc2", self.ws_a, P.w(p + "w2"), self.xs[i + 1], residual=self.x2[i])
         return self.xs[-1]
+
+    # ------------------------------------------------------------------ linear layers (bf16 or fp8)
+    def refresh_fp8_weights(self) -> None:
+        """Quantise the weights once per optimizer step (before the first forward after it)."""
+        P = self.params
+        ws = {}
+        for l in self.layer_ids:
+            p = f"layers.{l}."
+            for lin, name in (("qkv", "wqkv"), ("o", "wo"), ("fc1", self.fc1), ("fc2", "w2")):
+                ws[(l, lin)] = P.w(p + name)
+        self.f8.refresh_weights(ws, P.step)
+
+    def _linear(self, layer, lin, x, w, out, residual=None):
+        if self.f8 is not None:
+            return self.f8.forward(layer, lin, x, out, residual=residual)
+        return ops.gemm(x, w, out=out, residual=residual)
+
+    def _linear_bwd(self, layer, lin, dy, x, w, dx_out, grad):
+        """dgrad into ``dx_out``, wgrad accumulated into ``grad``."""
+        if self.f8 is not None:
+            return self.f8.backward(layer, lin, dy, x, dx_out, grad)
+        ops.gemm(dy, w, b_t=True, out=dx_out)
+        ops.gemm(dy, x, a_t=True, b_t=True, out=grad, accumulate=True)
+        return dx_out
 
     def _rmsnorm(self, x, w, out, rstd):
         return ops.rmsnorm_fwd(x, w, float(self.cfg.norm_eps), out=out, rstd=rstd)
@@ -217,20 +268,17 @@ class LlamaModel:
             l = self.layer_ids[i]
             p = f"layers.{l}."
             # MLP
-            ops.swiglu_fwd(self.gu[i], out=self.ws_a)
-            ops.gemm(dx, P.w(p + "w2"), b_t=True, out=self.ws_da)
-            ops.gemm(dx, self.ws_a, a_t=True, b_t=True, out=P.g(p + "w2"), accumulate=True)
-            ops.swiglu_bwd(self.gu[i], self.ws_da, out=self.gu[i])
+            mlp_act_fwd(cfg, self.gu[i], self.ws_a)
+            self._linear_bwd(l, "fc2", dx, self.ws_a, P.w(p + "w2"), self.ws_da, P.g(p + "w2"))
+            mlp_act_bwd(cfg, self.gu[i], self.ws_da, self.gu[i])
             dgu = self.gu[i]
             h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])
-            ops.gemm(dgu, P.w(p + "w13"), b_t=True, out=self.ws_dh)
-            ops.gemm(dgu, h2, a_t=True, b_t=True, out=P.g(p + "w13"), accumulate=True)
+            self._linear_bwd(l, "fc1", dgu, h2, P.w(p + self.fc1), self.ws_dh, P.g(p + self.fc1))
             ops.rmsnorm_bwd(self.x2[i], P.w(p + "mlp_norm"), self.rstd2[i], self.ws_dh, P.g(p + "mlp_norm"), dres=dx,
                             out=self.ws_dx2)
             dx2 = self.ws_dx2
             # attention
-            ops.gemm(dx2, P.w(p + "wo"), b_t=True, out=self.ws_do)
-            ops.gemm(dx2, self.o[i], a_t=True, b_t=True, out=P.g(p + "wo"), accumulate=True)
+            self._linear_bwd(l, "o", dx2, self.o[i], P.w(p + "wo"), self.ws_do, P.g(p + "wo"))
             q, k, v = self._views(i)
             D = cfg.head_dim
             dq = self.ws_dqkv[:, : cfg.heads * D]
@@ -240,8 +288,7 @@ class LlamaModel:
             ops.rope_(dq, cfg.heads, D, self.cos, self.sin, self.S, inverse=True)
             ops.rope_(dk, cfg.kv_heads, D, self.cos, self.sin, self.S, inverse=True)
             h, _ = self._rmsnorm(self.xs[i], P.w(p + "attn_norm"), self.ws_h, self.rstd1[i])
-            ops.gemm(self.ws_dqkv, P.w(p + "wqkv"), b_t=True, out=self.ws_dh)
-            ops.gemm(self.ws_dqkv, h, a_t=True, b_t=True, out=P.g(p + "wqkv"), accumulate=True)
+            self._linear_bwd(l, "qkv", self.ws_dqkv, h, P.w(p + "wqkv"), self.ws_dh, P.g(p + "wqkv"))
             ops.rmsnorm_bwd(self.xs[i], P.w(p + "attn_norm"), self.rstd1[i], self.ws_dh, P.g(p + "attn_norm"),
                             dres=dx2, out=dx)
         if self.first:

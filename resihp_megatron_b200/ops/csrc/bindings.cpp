@@ -158,6 +158,15 @@ void swiglu_bwd(const torch::Tensor& gu, const torch::Tensor& da, torch::Tensor&
   RB_CALL(rb::swiglu_bwd(gu.data_ptr(), da.data_ptr(), dgu.data_ptr(), T, F, cur_stream()), "swiglu_bwd");
 }
 
+// hist [n, len] fp32, pending [n] fp32: shift the history by one and move pending into slot 0
+void amax_history_push(torch::Tensor& hist, torch::Tensor& pending) {
+  CHECK_F32(hist); CHECK_F32(pending);
+  TORCH_CHECK(hist.dim() >= 1 && hist.numel() == pending.numel() * hist.size(-1), "amax_history_push: shapes");
+  const c10::cuda::CUDAGuard g(hist.device());
+  RB_CALL(rb::amax_history_push(hist.data_ptr<float>(), pending.data_ptr<float>(), pending.numel(), hist.size(-1),
+                                cur_stream()), "amax_history_push");
+}
+
 void gelu_fwd(const torch::Tensor& h, torch::Tensor& a) {
   CHECK_BF16(h); CHECK_BF16(a);
   TORCH_CHECK(h.numel() == a.numel(), "gelu_fwd: sizes differ");
@@ -687,6 +696,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("gelu_fwd", &gelu_fwd);
+  m.def("amax_history_push", &amax_history_push);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
         py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"));

@@ -274,6 +274,17 @@ __global__ void gelu_bwd_kernel(const __nv_bfloat16* h, const __nv_bfloat16* __r
   store_bf16x8(dh + i * 8, o);
 }
 
+// Delayed-scaling history update, one thread per recorded tensor: hist[i] = [pending[i],
+// hist[i][0 .. len-2]] and pending[i] = 0.
+__global__ void amax_history_push_kernel(float* __restrict__ hist, float* __restrict__ pending, int n, int len) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float* h = hist + static_cast<long long>(i) * len;
+  for (int j = len - 1; j > 0; --j) h[j] = h[j - 1];
+  h[0] = pending[i];
+  pending[i] = 0.f;
+}
+
 // x[t, :] = E[ids[t], :]
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
                                      __nv_bfloat16* __restrict__ x, int T, int H, int V, int* err) {
@@ -458,6 +469,13 @@ int gelu_bwd(const void* h, const void* da, void* dh, long long n, cudaStream_t 
   gelu_bwd_kernel<<<cdiv_ll(n / 8, 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(h),
                                                       reinterpret_cast<const __nv_bfloat16*>(da),
                                                       reinterpret_cast<__nv_bfloat16*>(dh), n / 8);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int amax_history_push(float* hist, float* pending, int n, int len, cudaStream_t s) {
+  if (n < 0 || len < 1) return -1;
+  if (n == 0) return 0;
+  amax_history_push_kernel<<<(n + 127) / 128, 128, 0, s>>>(hist, pending, n, len);
   return static_cast<int>(cudaGetLastError());
 }
 

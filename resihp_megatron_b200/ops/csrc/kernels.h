@@ -23,6 +23,7 @@ int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos
 int swiglu_fwd(const void* gu, void* a, int T, int F, cudaStream_t s);
 int swiglu_bwd(const void* gu, const void* da, void* dgu, int T, int F, cudaStream_t s);
 int gelu_fwd(const void* h, void* a, long long n, cudaStream_t s);
+int amax_history_push(float* hist, float* pending, int n, int len, cudaStream_t s);
 int gelu_bwd(const void* h, const void* da, void* dh, long long n, cudaStream_t s);
 int embedding_fwd(const int64_t* ids, const void* E, void* x, int T, int H, int V, int* err, cudaStream_t s);
 int embedding_bwd(const int64_t* vals, const int64_t* order, int T, const void* dx, float* dE, int H,

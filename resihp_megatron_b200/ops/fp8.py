@@ -138,6 +138,19 @@ def quantize(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = False, row
     return out
 
 
+def amax_history_push(history: torch.Tensor, pending: torch.Tensor) -> None:
+    """``history [..., len]`` (fp32): shift by one, ``pending`` (same leading shape) into slot 0,
+    then zero ``pending`` -- the delayed-scaling update after the amax reduction."""
+    ext().amax_history_push(history, pending)
+    count(1)
+
+
+def amax_history_push_reference(history: torch.Tensor, pending: torch.Tensor) -> None:
+    history[..., 1:] = history[..., :-1].clone()
+    history[..., 0] = pending
+    pending.zero_()
+
+
 def _u8(t):
     return None if t is None else t.view(torch.uint8)
 

@@ -31,7 +31,10 @@ class GPUTrainer:
     def __init__(self, cfg: GPTConfig, *, global_batch: int, micro_batch: int = 1, seq_len: int | None = None,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, seed: int = 0,
                  device=None, dp_group: dist.ProcessGroup | None = None, dp_impl: str = "fused",
-                 spare_bank: bool | None = None):
+                 spare_bank: bool | None = None, fp8=None):
+        """``fp8``: an ``Fp8Recipe`` -- block-scaled fp8 linear layers whose per-layer amax is
+        reduced with MAX over the data-parallel group and recorded in the amax history at the
+        end of every step."""
         self.cfg = cfg
         self.S = seq_len or cfg.seq_len
         self.group = dp_group
@@ -66,7 +69,7 @@ class GPUTrainer:
             factory, opt_factory = self.fused.buffer_factory, self.fused.opt_factory
         self.model = LlamaModel(cfg, self.device, micro_batch=micro_batch, seq_len=self.S, seed=seed,
                                 shard_rank=self.rank, shard_count=self.dp, buffer_factory=factory,
-                                opt_factory=opt_factory)
+                                opt_factory=opt_factory, fp8=fp8)
         self.tokens_per_step = global_batch * self.S
         self.batch_offset = self.rank * self.local_batch  # first sequence of this rank in the global batch
         self.ids_dev = torch.empty(self.local_batch, self.S, dtype=torch.int64, device=self.device)
@@ -92,6 +95,8 @@ class GPUTrainer:
         # host can run ahead of the device without racing the asynchronous copies
         self._bc_ring = torch.zeros(64, 2, dtype=torch.float32).pin_memory()
         self._bc_events: list = [None] * 64
+        if self.model.f8 is not None:
+            self.model.f8.version = None  # the weight quantisation is part of every replay
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         l0 = ops.launches()
@@ -113,6 +118,8 @@ class GPUTrainer:
         mb = self.micro_batch
         for i in range(self.n_micro):
             m.forward_backward(ids[i * mb:(i + 1) * mb].reshape(-1), labels[i * mb:(i + 1) * mb].reshape(-1), scale)
+        if m.f8 is not None:
+            m.f8.finish_iteration()
         P = self.model.params
         ops.adam_step(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.bf16, lr=self.lr, beta1=self.betas[0],
                       beta2=self.betas[1], eps=self.eps, weight_decay=self.wd, step=max(P.step, 1), zero_grad=True,
@@ -155,9 +162,14 @@ class GPUTrainer:
         mb = self.micro_batch
         for i in range(self.n_micro):
             m.forward_backward(ids[i * mb:(i + 1) * mb].reshape(-1), labels[i * mb:(i + 1) * mb].reshape(-1), scale)
+        if m.f8 is not None:  # the amax reduction (one MAX all-reduce) and the history update
+            m.f8.finish_iteration(self._reduce_max if self.dp > 1 else None)
         self._reduce_and_update()
         self.step_count += 1
         return m.loss_acc / self.tokens_per_step
+
+    def _reduce_max(self, t: torch.Tensor) -> None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
 
     def _reduce_and_update(self) -> None:
         from .. import ops

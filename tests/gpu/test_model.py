@@ -126,3 +126,53 @@ def test_cuda_graph_replay_trains_exactly_like_eager_steps():
     assert ops.launches() > l0
     assert eager == graphed, (eager, graphed)
     assert torch.equal(w_eager, w_graph)
+
+
+def test_gelu_mlp_step_matches_fp32_reference():
+    """GPT MLP (w1 -> gelu -> w2) against PyTorch autograd with the model's weights."""
+    from resihp_megatron_b200.models.config import TINY
+    from resihp_megatron_b200.models.gpt import LlamaModel
+
+    cfg = TINY.with_(hidden=256, heads=2, kv_heads=2, ffn=512, layers=2, vocab_size=512, mlp="gelu")
+    model = LlamaModel(cfg, "cuda", micro_batch=1, seq_len=128, seed=0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(0, cfg.vocab_size, (1, 128), device="cuda", generator=g)
+    labels = torch.roll(ids, -1, 1)
+    model.forward_backward(ids.view(-1), labels.view(-1), grad_scale=1.0 / ids.numel())
+    torch.cuda.synchronize()
+    P = model.params
+    W = {n: P.w(n).float().clone().requires_grad_(True) for n in P.order}
+
+    def rms(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * w
+
+    # compare the MLP of layer 0 in isolation: input x2 saved by the model
+    x2 = model.x2[0].float()
+    h2 = rms(x2, W["layers.0.mlp_norm"])
+    out = x2 + torch.nn.functional.gelu(h2 @ W["layers.0.w1"].t(), approximate="tanh") @ W["layers.0.w2"].t()
+    assert ((model.xs[1].float() - out).abs().max() / out.abs().max()).item() < 2e-2
+
+
+def test_fp8_training_tracks_bf16_and_reduces_loss():
+    """GPT-style model with block-scaled fp8 linear layers through the trainer: the first loss
+    matches the bf16 model's, training reduces it, and the amax history fills one slot per step."""
+    from resihp_megatron_b200.models.config import TINY
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.train.gpu_trainer import GPUTrainer
+
+    cfg = TINY.with_(hidden=256, heads=2, kv_heads=2, ffn=512, layers=2, vocab_size=512, mlp="gelu")
+    g = torch.Generator().manual_seed(6)
+    data = torch.randint(0, cfg.vocab_size, (2, 129), generator=g)
+    ids, lab = data[:, :-1].contiguous().cuda(), data[:, 1:].contiguous().cuda()
+
+    def run(fp8):
+        tr = GPUTrainer(cfg, global_batch=2, micro_batch=1, seq_len=128, lr=3e-3, device="cuda",
+                        fp8=Fp8Recipe() if fp8 else None)
+        return [tr.step_device(ids, lab).item() for _ in range(6)], tr
+
+    bf, _ = run(False)
+    f8, tr = run(True)
+    assert abs(f8[0] - bf[0]) < 0.02 * bf[0], (f8[0], bf[0])
+    assert f8[-1] < f8[0]
+    h = tr.model.f8.history
+    assert (h[:, :, :6] > 0).all() and (h[:, :, 6:] == 0).all() and not tr.model.f8.has_nonfinite()

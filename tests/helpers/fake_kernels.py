@@ -177,18 +177,65 @@ def adam_step(p, grad, m, v, p_bf16=None, *, lr, beta1=0.9, beta2=0.999, eps=1e-
         p_bf16.copy_(p)
 
 
+def gelu_fwd(h, out=None):
+    a = F.gelu(h.float(), approximate="tanh")
+    out = torch.empty_like(h) if out is None else out
+    out.copy_(a)
+    return out
+
+
+def gelu_bwd(h, da, out=None):
+    x = h.float().clone().requires_grad_(True)
+    F.gelu(x, approximate="tanh").backward(da.float())
+    out = torch.empty_like(h) if out is None else out
+    out.copy_(x.grad)
+    return out
+
+
+# block-scaled fp8: the PyTorch emulation of the kernels (bit-exact quantiser)
+def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=None, out=None):
+    from resihp_megatron_b200.ops import fp8
+
+    ref = fp8.quantize_reference(x, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, amax=amax)
+    if out is None:
+        return ref
+    for name in ("q_row", "s_row", "q_col", "s_col"):
+        src, dst = getattr(ref, name), getattr(out, name)
+        if src is not None and dst is not None:
+            dst.copy_(src)
+    return out
+
+
+def fp8_gemm(a, b, *, out=None, out_dtype=torch.bfloat16, accumulate=False, alpha=1.0, residual=None, scatter=None):
+    from resihp_megatron_b200.ops import fp8
+
+    if scatter is not None:
+        raise NotImplementedError("the scatter epilogue writes peer memory (GPU only)")
+    return fp8.gemm_reference(a, b, out=out, out_dtype=out_dtype, accumulate=accumulate, alpha=alpha,
+                              residual=residual)
+
+
+def fp8_amax_history_push(history, pending):
+    from resihp_megatron_b200.ops import fp8
+
+    fp8.amax_history_push_reference(history, pending)
+
+
 NAMES = ("gemm", "rmsnorm_fwd", "rmsnorm_bwd", "rope_tables", "rope_", "swiglu_fwd", "swiglu_bwd", "embedding_fwd",
-         "embedding_bwd", "cross_entropy_", "attention_fwd", "attention_bwd", "adam_step")
+         "embedding_bwd", "cross_entropy_", "attention_fwd", "attention_bwd", "adam_step", "gelu_fwd", "gelu_bwd")
+FP8_NAMES = {"quantize": fp8_quantize, "gemm": fp8_gemm, "amax_history_push": fp8_amax_history_push}
 
 
 def install(monkeypatch=None) -> None:
-    """Swap the stand-ins into ``resihp_megatron_b200.ops`` (with ``monkeypatch`` when given, so a
-    test undoes it; plain assignment in a spawned worker process)."""
+    """Swap the stand-ins into ``resihp_megatron_b200.ops`` and ``ops.fp8`` (with ``monkeypatch``
+    when given, so a test undoes it; plain assignment in a spawned worker process)."""
     from resihp_megatron_b200 import ops
+    from resihp_megatron_b200.ops import fp8
 
     g = globals()
-    for n in NAMES:
+    targets = [(ops, n, g[n]) for n in NAMES] + [(fp8, n, f) for n, f in FP8_NAMES.items()]
+    for mod, n, f in targets:
         if monkeypatch is not None:
-            monkeypatch.setattr(ops, n, g[n])
+            monkeypatch.setattr(mod, n, f)
         else:
-            setattr(ops, n, g[n])
+            setattr(mod, n, f)
