@@ -18,6 +18,13 @@ of ``wo`` / ``w2`` (whose gathered input also feeds the weight gradient), the gr
 all-gather is a reduce-scatter after the dgrad GEMM of ``wqkv`` / ``w13``, and the normalised
 inputs of the column-parallel weight gradients are recomputed and re-gathered.
 
+With the GPT MLP (``cfg.mlp == "gelu"``) the input projection is ``w1`` alone and
+``a = gelu(AllGather(h2) W1_r^T)``.  With an ``Fp8Recipe`` (``fp8=``) the four projections run as
+block-scaled fp8 GEMMs (``models.fp8_linear``): the column-parallel ones gather the bf16 rows
+and quantise the gathered input, the row-parallel ones store their partial products straight
+into the owners' receive slots from the fp8 GEMM's epilogue (``tp.gemm_rs_with``), and every
+rank records the amax of its operands for the per-layer history.
+
 Parameters live in two flat sets: ``shd`` (tensor-parallel shards: wq, wk, wv, wo, w1, w3, w2)
 and ``rep`` (replicated on every TP rank: the norms, the embedding on the first stage, the final
 norm and LM head on the last).  With sequence parallelism every TP rank computes the replicated
@@ -37,8 +44,10 @@ from __future__ import annotations
 import torch
 
 from .. import ops
+from ..ops import fp8 as fp8_ops
 from ..utils.intervals import even_split
 from .config import GPTConfig
+from .gpt import mlp_act_bwd, mlp_act_fwd
 from .params import FlatParams, ParamSpec
 
 SHARDED = ("wq", "wk", "wv", "wo", "w1", "w3", "w2")
@@ -68,7 +77,7 @@ def stage_param_specs(cfg: GPTConfig, layers, first: bool, last: bool, tp_rank: 
             ParamSpec(p + "wv", (nk * D, H), (cfg.kv_heads * D, H), 0, (kh[0] * D, kh[1] * D)),
             ParamSpec(p + "wo", (H, nq * D), (H, cfg.heads * D), 1, (qh[0] * D, qh[1] * D)),
             ParamSpec(p + "w1", (nf, H), (F, H), 0, fr),
-            ParamSpec(p + "w3", (nf, H), (F, H), 0, fr),
+        ] + ([ParamSpec(p + "w3", (nf, H), (F, H), 0, fr)] if cfg.gated else []) + [
             ParamSpec(p + "w2", (H, nf), (H, F), 1, fr),
         ]
     if last:
@@ -92,7 +101,7 @@ class _Slot:
         self.qkv = [torch.empty(T, stage.qkv_cols, **bf) for _ in range(L)]
         self.o = [torch.empty(T, stage.nq * c.head_dim, **bf) for _ in range(L)]
         self.lse = [torch.empty(stage.mb, stage.nq, stage.S, **f32) for _ in range(L)]
-        self.gu = [torch.empty(T, 2 * stage.nf, **bf) for _ in range(L)]
+        self.gu = [torch.empty(T, stage.mlp_in, **bf) for _ in range(L)]
         self.ids: torch.Tensor | None = None
         if stage.last:
             self.hf = torch.empty(Tl, H, **bf)
@@ -104,11 +113,12 @@ class TPStage:
     def __init__(self, cfg: GPTConfig, device, *, layers, first: bool, last: bool, tp, micro_batch: int = 1,
                  seq_len: int | None = None, seed: int = 0, rep_shard: tuple[int, int] = (0, 1),
                  shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None),
-                 init: bool = True):
+                 init: bool = True, fp8=None):
         """``tp``: the tensor-parallel backend (``parallel.tp_backend``); ``*_shard`` the
         (rank, count) of the ZeRO-1 optimizer shard of each parameter set over its
         data-parallel group; ``*_factories`` the (buffer, optimizer) factories of ``FlatParams``
-        (the fused data-parallel step's peer heap); ``init`` draws the initial weights."""
+        (the fused data-parallel step's peer heap); ``init`` draws the initial weights;
+        ``fp8`` an ``Fp8Recipe`` for block-scaled fp8 projections."""
         self.cfg, self.device = cfg, torch.device(device)
         self.tp = tp
         self.tp_rank, self.tp_size = tp.rank, tp.world
@@ -122,6 +132,7 @@ class TPStage:
         self.Tl = self.T // self.tp_size
         self.nq, self.nk = cfg.heads // self.tp_size, cfg.kv_heads // self.tp_size
         self.nf = cfg.ffn // self.tp_size
+        self.mlp_in = (2 if cfg.gated else 1) * self.nf
         self.qkv_cols = (self.nq + 2 * self.nk) * cfg.head_dim
         rep_specs, shd_specs = stage_param_specs(cfg, self.layer_ids, first, last, self.tp_rank, self.tp_size)
         self.rep = FlatParams(rep_specs, self.device, shard_rank=rep_shard[0], shard_count=rep_shard[1],
@@ -134,7 +145,8 @@ class TPStage:
         self.cos, self.sin = ops.rope_tables(self.S, cfg.head_dim, cfg.rope_theta, self.device)
         for l in self.layer_ids:  # fused projection weights are views over consecutive tensors
             self._check_adjacent(f"layers.{l}.", ("wq", "wk", "wv"))
-            self._check_adjacent(f"layers.{l}.", ("w1", "w3"))
+            if cfg.gated:
+                self._check_adjacent(f"layers.{l}.", ("w1", "w3"))
         bf = dict(dtype=torch.bfloat16, device=self.device)
         T, Tl, H = self.T, self.Tl, cfg.hidden
         self.ws_a = torch.empty(T, self.nf, **bf)
@@ -149,6 +161,11 @@ class TPStage:
         self.slots: dict[object, _Slot] = {}
         self.free: list[_Slot] = []
         self.deferred: dict[object, list] = {}
+        self.f8 = None
+        if fp8 is not None:
+            from .fp8_linear import Fp8Linears
+
+            self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
 
     # ------------------------------------------------------------------ parameter views
     def _check_adjacent(self, p: str, names) -> None:
@@ -167,7 +184,76 @@ class TPStage:
         return self._fused(self.shd.grad if grad else self.shd.bf16, p, ("wq", "wk", "wv"), self.qkv_cols)
 
     def w13(self, p: str, grad: bool = False) -> torch.Tensor:
-        return self._fused(self.shd.grad if grad else self.shd.bf16, p, ("w1", "w3"), 2 * self.nf)
+        """The MLP input projection's rows on this rank: ``[w1; w3]`` (gated) or ``w1``."""
+        names = ("w1", "w3") if self.cfg.gated else ("w1",)
+        return self._fused(self.shd.grad if grad else self.shd.bf16, p, names, self.mlp_in)
+
+    def refresh_fp8_weights(self) -> None:
+        """Quantise this rank's projection shards once per optimizer step."""
+        ws = {}
+        for l in self.layer_ids:
+            p = f"layers.{l}."
+            ws[(l, "qkv")], ws[(l, "o")] = self.wqkv(p), self.shd.w(p + "wo")
+            ws[(l, "fc1")], ws[(l, "fc2")] = self.w13(p), self.shd.w(p + "w2")
+        self.f8.refresh_weights(ws, self.shd.step)
+
+    # ------------------------------------------------------------------ projections (bf16 or fp8)
+    def _col_fwd(self, l: int, lin: str, w: torch.Tensor, out: torch.Tensor) -> None:
+        """Column-parallel projection of the gathered chunks (the caller wrote this rank's rows)."""
+        T, H = self.T, self.cfg.hidden
+        if self.f8 is None:
+            self.tp.ag_gemm(T, w, out=out)
+            return
+        self.f8.forward(l, lin, self.tp.all_gather(T, H), out)
+
+    def _row_fwd(self, l: int, lin: str, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
+                 residual: torch.Tensor) -> None:
+        """Row-parallel projection, reduce-scattered to the row shards, plus the residual."""
+        if self.f8 is None:
+            self.tp.gemm_rs(x, w, out=out, residual=residual)
+            return
+        xq = self.f8.quant_x(l, lin, x)
+        wq = self.f8.weight(l, lin)
+        self.tp.gemm_rs_with(x.shape[0], w.shape[0], lambda **kw: fp8_ops.gemm(xq.rowwise(), wq.rowwise(), **kw),
+                             out=out, residual=residual)
+
+    def _row_bwd(self, w_list, l: int, lin: str, w: torch.Tensor, x: torch.Tensor, dx_out: torch.Tensor,
+                 grad: torch.Tensor) -> None:
+        """Backward of a row-parallel projection: the output gradient rows (written into this
+        rank's chunk by the caller) are gathered; dgrad into ``dx_out`` and wgrad (``x`` is the
+        saved / recomputed full-width input) into ``grad``."""
+        T, H = self.T, self.cfg.hidden
+        if self.f8 is None:
+            _, dy = self.tp.ag_gemm(T, w, out=dx_out, w_t=True)
+            self._wgrad(w_list, dy, x, grad, copy_a=True, copy_b=x is self.ws_a)
+            return
+        dy = self.tp.all_gather(T, H)
+        dyq = self.f8.quant_dy(l, lin, dy)
+        fp8_ops.gemm(dyq.rowwise(), self.f8.weight(l, lin).colwise(), out=dx_out)
+        self._wgrad_f8(w_list, dyq, dy, x, grad, copy_x=x is self.ws_a)
+
+    def _col_bwd(self, w_list, l: int, lin: str, dy: torch.Tensor, w: torch.Tensor, dx_out: torch.Tensor,
+                 grad: torch.Tensor, x_full_fn) -> None:
+        """Backward of a column-parallel projection: dgrad reduce-scattered into ``dx_out`` (this
+        rank's rows); ``x_full_fn()`` recomputes and gathers the input for the wgrad."""
+        if self.f8 is None:
+            self.tp.gemm_rs(dy, w, out=dx_out, w_t=True)
+            self._wgrad(w_list, dy, x_full_fn(), grad, copy_a=dy is self.ws_dqkv, copy_b=True)
+            return
+        dyq = self.f8.quant_dy(l, lin, dy)
+        wq = self.f8.weight(l, lin)
+        self.tp.gemm_rs_with(dy.shape[0], self.cfg.hidden,
+                             lambda **kw: fp8_ops.gemm(dyq.rowwise(), wq.colwise(), **kw), out=dx_out)
+        self._wgrad_f8(w_list, dyq, dy, x_full_fn(), grad, copy_x=True)
+
+    def _wgrad_f8(self, deferred, dyq, dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, *,
+                  copy_x: bool) -> None:
+        """fp8 weight gradient ``out += dy^T x``: now (with ``dy``'s transposed layout already
+        quantised), or -- deferred -- from bf16 copies, re-quantised in the W pass."""
+        if deferred is None:
+            fp8_ops.gemm(dyq.colwise(), self.f8.quant_x_cols(x).colwise(), out=out, accumulate=True)
+            return
+        deferred.append(("f8", dy.clone(), x.clone() if copy_x else x, out))
 
     def param_sets(self) -> tuple[FlatParams, FlatParams]:
         return self.rep, self.shd
@@ -207,21 +293,23 @@ class TPStage:
             ops.embedding_fwd(ids_local, R.w("embed"), out=slot.x[0])
         else:
             slot.x[0] = x_in
+        if self.f8 is not None:
+            self.refresh_fp8_weights()
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = slot.x[i]
             self._rms(x, R.w(p + "attn_norm"), self.tp.chunk(T, H), slot.rstd1[i])
-            self.tp.ag_gemm(T, self.wqkv(p), out=slot.qkv[i])
+            self._col_fwd(l, "qkv", self.wqkv(p), slot.qkv[i])
             q, k, v = self._qkv_views(slot.qkv[i])
             ops.rope_(q, self.nq, D, self.cos, self.sin, self.S)
             ops.rope_(k, self.nk, D, self.cos, self.sin, self.S)
             ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.nq, kv_heads=self.nk, head_dim=D,
                               out=slot.o[i], lse=slot.lse[i])
-            self.tp.gemm_rs(slot.o[i], P.w(p + "wo"), out=slot.x2[i], residual=x)
+            self._row_fwd(l, "o", slot.o[i], P.w(p + "wo"), slot.x2[i], x)
             self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), slot.rstd2[i])
-            self.tp.ag_gemm(T, self.w13(p), out=slot.gu[i])
-            ops.swiglu_fwd(slot.gu[i], out=self.ws_a)
-            self.tp.gemm_rs(self.ws_a, P.w(p + "w2"), out=slot.x[i + 1], residual=slot.x2[i])
+            self._col_fwd(l, "fc1", self.w13(p), slot.gu[i])
+            mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
+            self._row_fwd(l, "fc2", self.ws_a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])
         if not self.last:
             return slot.x[-1]
         self._rms(slot.x[-1], R.w("final_norm"), slot.hf, slot.rstd_f)
@@ -261,31 +349,33 @@ class TPStage:
             p = f"layers.{l}."
             # MLP: the reduce-scatter's gradient is an all-gather feeding w2's dgrad and wgrad
             self.tp.chunk(T, H).copy_(dx)
-            _, dy = self.tp.ag_gemm(T, P.w(p + "w2"), out=self.ws_da, w_t=True)
-            ops.swiglu_fwd(slot.gu[i], out=self.ws_a)
-            self._wgrad(w, dy, self.ws_a, P.g(p + "w2"), copy_a=True, copy_b=True)
-            dgu = ops.swiglu_bwd(slot.gu[i], self.ws_da, out=slot.gu[i])
-            self.tp.gemm_rs(dgu, self.w13(p), out=self.ws_dh, w_t=True)
-            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), self.ws_rstd)
-            h2 = self.tp.all_gather(T, H)
-            self._wgrad(w, dgu, h2, self.w13(p, grad=True), copy_b=True)
+            mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
+            self._row_bwd(w, l, "fc2", P.w(p + "w2"), self.ws_a, self.ws_da, P.g(p + "w2"))
+            dgu = mlp_act_bwd(cfg, slot.gu[i], self.ws_da, slot.gu[i])
+
+            def h2_full(i=i, p=p):
+                self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), self.ws_rstd)
+                return self.tp.all_gather(T, H)
+
+            self._col_bwd(w, l, "fc1", dgu, self.w13(p), self.ws_dh, self.w13(p, grad=True), h2_full)
             ops.rmsnorm_bwd(slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.ws_dh, R.g(p + "mlp_norm"), dres=dx,
                             out=self.ws_dx2)
             dx2 = self.ws_dx2
             # attention
             self.tp.chunk(T, H).copy_(dx2)
-            _, dy = self.tp.ag_gemm(T, P.w(p + "wo"), out=self.ws_do, w_t=True)
-            self._wgrad(w, dy, slot.o[i], P.g(p + "wo"), copy_a=True)
+            self._row_bwd(w, l, "o", P.w(p + "wo"), slot.o[i], self.ws_do, P.g(p + "wo"))
             q, k, v = self._qkv_views(slot.qkv[i])
             dq, dk, dv = self._qkv_views(self.ws_dqkv)
             ops.attention_bwd(q, k, v, slot.o[i], self.ws_do, slot.lse[i], dq, dk, dv, batch=self.mb, seq=self.S,
                               heads=self.nq, kv_heads=self.nk, head_dim=D)
             ops.rope_(dq, self.nq, D, self.cos, self.sin, self.S, inverse=True)
             ops.rope_(dk, self.nk, D, self.cos, self.sin, self.S, inverse=True)
-            self.tp.gemm_rs(self.ws_dqkv, self.wqkv(p), out=self.ws_dh, w_t=True)
-            self._rms(slot.x[i], R.w(p + "attn_norm"), self.tp.chunk(T, H), self.ws_rstd)
-            h = self.tp.all_gather(T, H)
-            self._wgrad(w, self.ws_dqkv, h, self.wqkv(p, grad=True), copy_a=True, copy_b=True)
+
+            def h_full(i=i, p=p):
+                self._rms(slot.x[i], R.w(p + "attn_norm"), self.tp.chunk(T, H), self.ws_rstd)
+                return self.tp.all_gather(T, H)
+
+            self._col_bwd(w, l, "qkv", self.ws_dqkv, self.wqkv(p), self.ws_dh, self.wqkv(p, grad=True), h_full)
             ops.rmsnorm_bwd(slot.x[i], R.w(p + "attn_norm"), slot.rstd1[i], self.ws_dh, R.g(p + "attn_norm"),
                             dres=dx2, out=dx)
         if self.first:
@@ -298,6 +388,12 @@ class TPStage:
 
     def weight_backward(self, key) -> None:
         """The deferred weight-gradient GEMMs of micro-batch ``key`` (zero-bubble W pass)."""
-        for a, b, out in self.deferred.pop(key):
-            ops.gemm(a, b, a_t=True, b_t=True, out=out, accumulate=True)
+        for item in self.deferred.pop(key):
+            if item[0] == "f8":
+                _, dy, x, out = item
+                dyq = fp8_ops.quantize(dy, self.f8.recipe.bwd_fmt, rowwise=False, colwise=True)
+                fp8_ops.gemm(dyq.colwise(), self.f8.quant_x_cols(x).colwise(), out=out, accumulate=True)
+            else:
+                a, b, out = item
+                ops.gemm(a, b, a_t=True, b_t=True, out=out, accumulate=True)
         self._release(key)

@@ -18,7 +18,11 @@ Operations:
   producer (an RMSNorm, a copy) writes them in place;
 * ``ag_gemm(M, w, out, w_t)`` -> ``(AllGather(chunks) @ op(w)^T, gathered input)``;
 * ``all_gather(M, K)`` -> the gathered ``[M, K]`` chunks;
-* ``gemm_rs(x, w, out, w_t, residual)`` -> ``ReduceScatter_rows(x @ op(w)^T) (+ residual)``.
+* ``gemm_rs(x, w, out, w_t, residual)`` -> ``ReduceScatter_rows(x @ op(w)^T) (+ residual)``;
+* ``gemm_rs_with(M, N, gemm, out, residual)`` -> the same for any GEMM (the block-scaled fp8
+  one): ``gemm(out=..., residual=..., scatter=(recv_ptrs, slot))`` writes the ``[M, N]`` product
+  into a local buffer (optionally plus a residual) or, with ``scatter``, stores each row
+  straight into its owner's receive slot.
 
 ``op(w) = w`` (``[N, K]``) or, with ``w_t``, ``w.T`` (``w`` stored ``[K, N]``).  A gathered input
 stays valid until the gather after next (two buffers alternate), which is what the weight
@@ -77,6 +81,10 @@ class SoloTP:
                 residual: torch.Tensor | None = None) -> torch.Tensor:
         return ops.gemm(x, w, b_t=w_t, out=out, residual=residual)
 
+    def gemm_rs_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+        return gemm(out=out, residual=residual)
+
     def close(self) -> None:
         pass
 
@@ -115,6 +123,18 @@ class CollectiveTP:
         if part is None:
             part = self.partials[(M, N)] = torch.empty(M, N, dtype=torch.bfloat16, device=self.device)
         ops.gemm(x, w, b_t=w_t, out=part)
+        return self._reduce_scatter(part, out, residual)
+
+    def gemm_rs_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+        part = self.partials.get((M, N))
+        if part is None:
+            part = self.partials[(M, N)] = torch.empty(M, N, dtype=torch.bfloat16, device=self.device)
+        gemm(out=part)
+        return self._reduce_scatter(part, out, residual)
+
+    def _reduce_scatter(self, part: torch.Tensor, out, residual) -> torch.Tensor:
+        M, N = part.shape
         y = torch.empty(M // self.world, N, dtype=torch.bfloat16, device=self.device) if out is None else out
         self.wait(dist.reduce_scatter_tensor(y, part, group=self.group, async_op=True))
         if residual is not None:
@@ -146,6 +166,10 @@ class FusedTP:
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, w_t: bool = False,
                 residual: torch.Tensor | None = None) -> torch.Tensor:
         return self.comm.gemm_reduce_scatter(x, w, out=out, w_t=w_t, residual=residual)
+
+    def gemm_rs_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+        return self.comm.reduce_scatter_with(M, N, gemm, out=out, residual=residual)
 
     def check(self) -> None:
         self.comm.heap.check()

@@ -122,6 +122,18 @@ class TensorParallelComm:
         self._rs ^= 1
         return y
 
+    def reduce_scatter_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
+                            residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``gemm_reduce_scatter`` for another GEMM kernel (the block-scaled fp8 one) whose
+        epilogue stores row ``m`` into rank ``m // (M / world)``'s receive slot:
+        ``gemm(scatter=(recv_ptrs, slot))``."""
+        self._barrier()
+        gemm(scatter=(self.heap.peer_ptrs(f"rs_recv{self._rs}"), self.rank))
+        self._barrier()
+        y = self.reduce_received(M, N, out, residual)
+        self._rs ^= 1
+        return y
+
     def scatter_partials(self, x: torch.Tensor, w: torch.Tensor, w_t: bool = False) -> None:
         ext().tp_rs_gemm(x, w, bool(w_t), self.heap.peer_ptrs(f"rs_recv{self._rs}"), self.rank)
         count(1)

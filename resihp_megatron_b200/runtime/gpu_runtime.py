@@ -254,10 +254,12 @@ class GPUHybridRuntime:
                  micro_batch: int = 1, seq_len: int | None = None, tokens: TokenSource | None = None,
                  tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0, lr: float = 3e-4,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, budget_s: float = 60.0,
-                 progress=None, hook=None, zero: bool = True, init: bool = True):
+                 progress=None, hook=None, zero: bool = True, init: bool = True, fp8=None):
         """``zero``: shard the optimizer state over each data-parallel group (ZeRO-1) or keep it
         whole on every replica (redundant: survives a fail-stop); ``init``: draw the initial
-        weights (False when a migrated state is loaded next)."""
+        weights (False when a migrated state is loaded next); ``fp8``: an ``Fp8Recipe`` --
+        block-scaled fp8 projections whose per-layer amax is reduced with MAX over every rank at
+        the end of each iteration (one all-reduce) and pushed into the amax history."""
         from ..models.tp_stage import TPStage
 
         check_supported(plan)
@@ -320,7 +322,8 @@ class GPUHybridRuntime:
             stage = TPStage(cfg, self.device, layers=range(*c.layers), first=c.stage == 0,
                             last=c.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch, seq_len=self.S,
                             seed=seed, rep_shard=rep_sync.shard, shd_shard=shd_sync.shard,
-                            rep_factories=rep_sync.factories, shd_factories=shd_sync.factories, init=init)
+                            rep_factories=rep_sync.factories, shd_factories=shd_sync.factories, init=init,
+                            fp8=fp8)
             rep_sync.attach(stage.rep)
             shd_sync.attach(stage.shd)
             self.chunks[c.stage] = (stage, rep_sync, shd_sync)
@@ -333,6 +336,12 @@ class GPUHybridRuntime:
         self.interp = Interpreter(plan, stream, self.executor, p2p, g.replica, g.stage, (cfg.hidden,), torch.bfloat16,
                                   tp_group=tp_pg, progress=progress, hook=hook)
         self.iteration = 0
+        self.fp8 = fp8
+        self._amax = None
+        if fp8 is not None:
+            from ..models.fp8_linear import NSLOTS
+
+            self._amax = torch.zeros(cfg.layers, NSLOTS, dtype=torch.float32, device=self.device)
 
     # ------------------------------------------------------------------ chunk views
     @property
@@ -361,12 +370,40 @@ class GPUHybridRuntime:
     def inflight(self) -> int:
         return sum(ch[0].inflight() for ch in self.chunks.values())
 
+    def buffers(self) -> dict[str, torch.Tensor]:
+        """Non-trainable state an iteration mutates, by logical key (the fp8 amax histories of
+        this rank's layers): migrated with its layer, rolled back with an aborted iteration."""
+        out = {}
+        for stage, _, _ in self.chunks.values():
+            if stage.f8 is not None:
+                out.update(stage.f8.state())
+        return out
+
+    def _finish_fp8(self) -> None:
+        """Global per-layer amax (MAX over every rank's micro-batches and shards: one
+        all-reduce over the world for all layers), then each layer's history update.
+        (Reference: ``resihp/runtime/hetero_runtime.py:122-134``.)"""
+        stages = [ch[0] for ch in self.chunks.values() if ch[0].f8 is not None]
+        self._amax.zero_()
+        for st in stages:
+            self._amax[st.layer_ids] = st.f8.pending
+        work = dist.all_reduce(self._amax, op=dist.ReduceOp.MAX, async_op=True)
+        if self.mgr is not None:
+            self.mgr.guarded_wait(work, what="amax all-reduce")
+        else:
+            work.wait()
+        for st in stages:
+            st.f8.pending.copy_(self._amax[st.layer_ids])
+            st.f8.finish_iteration()
+
     def run_iteration(self, iteration: int | None = None, step: bool = True) -> torch.Tensor:
         """One training step of this slot; returns the global mean token loss as a 0-d device
         tensor (no host synchronisation).  ``step=False`` stops after the gradient reduction
         (the resilient loop applies the optimizer step once the iteration is REDUCED)."""
         it = self.iteration if iteration is None else iteration
         self.interp.run(it)
+        if self.fp8 is not None:
+            self._finish_fp8()
         for sync in self._syncs():
             sync.reduce()
         if step:

@@ -24,16 +24,22 @@ from ..state.layer_registry import FULL, TensorSpec
 KINDS = ("param", "exp_avg", "exp_avg_sq")
 
 
-def gpu_tensor_specs(cfg: GPTConfig) -> dict[str, TensorSpec]:
+def gpu_tensor_specs(cfg: GPTConfig, fp8_history: int = 0) -> dict[str, TensorSpec]:
+    """Every logical tensor; ``fp8_history`` > 0 adds each layer's fp8 amax history
+    (``layers.<l>.amax_history``, ``[12, fp8_history]``, replicated, no optimizer state)."""
+    from ..models.fp8_linear import NSLOTS
+
     H, D, F, V = cfg.hidden, cfg.head_dim, cfg.ffn, cfg.vocab_size
     q, kv = cfg.heads * D, cfg.kv_heads * D
     out = {"embed": TensorSpec("embed", (V, H), None)}
+    mlp = (("w1", (F, H), 0),) + ((("w3", (F, H), 0),) if cfg.gated else ()) + (("w2", (H, F), 1),)
     for l in range(cfg.layers):
         p = f"layers.{l}."
         for name, shape, dim in (("attn_norm", (H,), None), ("mlp_norm", (H,), None), ("wq", (q, H), 0),
-                                 ("wk", (kv, H), 0), ("wv", (kv, H), 0), ("wo", (H, q), 1), ("w1", (F, H), 0),
-                                 ("w3", (F, H), 0), ("w2", (H, F), 1)):
+                                 ("wk", (kv, H), 0), ("wv", (kv, H), 0), ("wo", (H, q), 1)) + mlp:
             out[p + name] = TensorSpec(p + name, shape, dim)
+        if fp8_history:
+            out[p + "amax_history"] = TensorSpec(p + "amax_history", (NSLOTS, fp8_history), None, trainable=False)
     out["final_norm"] = TensorSpec("final_norm", (H,), None)
     out["lm_head"] = TensorSpec("lm_head", (V, H), None)
     return out
@@ -61,6 +67,11 @@ def _sets(rt):
     return rt.param_sets()
 
 
+def _buffers(rt) -> dict[str, torch.Tensor]:
+    """Non-trainable per-layer state of the runtime (fp8 amax histories), by logical key."""
+    return rt.buffers() if hasattr(rt, "buffers") else {}
+
+
 def export_state(rt) -> tuple[dict[str, dict[str, torch.Tensor]], dict[str, tuple[int, int]]]:
     """``(state, layout)``: ``state[kind][key]`` fp32 tensors of this rank's local shape and
     ``layout[key]`` its interval along the key's TP dimension.  Collective over every
@@ -81,6 +92,9 @@ def export_state(rt) -> tuple[dict[str, dict[str, torch.Tensor]], dict[str, tupl
             for kind, b in zip(KINDS, bufs):
                 state[kind][name] = b[o:o + s.numel].view(s.shape)
             layout[name] = s.shard_range if s.shard_dim is not None else FULL
+    for key, t in _buffers(rt).items():
+        state["param"][key] = t.clone()
+        layout[key] = FULL
     return state, layout
 
 
@@ -98,6 +112,9 @@ def import_state(rt, state: dict[str, dict[str, torch.Tensor]], step: int) -> No
             for kind, buf in zip(KINDS, (P.master, P.exp_avg, P.exp_avg_sq)):
                 buf[b:b + n].copy_(state[kind][name].reshape(-1)[a:a + n])
         P.step = step
+    for key, t in _buffers(rt).items():
+        if key in state["param"]:
+            t.copy_(state["param"][key])
 
 
 def local_layout(rt) -> dict[str, tuple[int, int]]:
@@ -107,6 +124,8 @@ def local_layout(rt) -> dict[str, tuple[int, int]]:
         for name in P.order:
             s = P.specs[name]
             out[name] = tuple(s.shard_range) if s.shard_dim is not None else FULL
+    for key in _buffers(rt):
+        out[key] = FULL
     return out
 
 
@@ -116,7 +135,8 @@ def checkpoint_slices(rt, specs: dict[str, TensorSpec]):
     from ..state.checkpoint import SliceMeta
 
     state, layout = export_state(rt)
-    return [(SliceMeta(key, specs[key].global_shape, specs[key].dim, tuple(iv)), {k: state[k][key] for k in KINDS})
+    return [(SliceMeta(key, specs[key].global_shape, specs[key].dim, tuple(iv)),
+             {k: state[k][key] for k in (KINDS if specs[key].trainable else KINDS[:1])})
             for key, iv in layout.items()]
 
 
@@ -126,7 +146,8 @@ def load_checkpoint_into(rt, checkpointer, iteration: int, specs: dict[str, Tens
     from ..state.checkpoint import SliceMeta
 
     wanted = [SliceMeta(key, specs[key].global_shape, specs[key].dim, iv) for key, iv in local_layout(rt).items()]
-    got = checkpointer.load(iteration, wanted, KINDS)
+    got = checkpointer.load(iteration, [w for w in wanted if specs[w.key].trainable], KINDS)
+    got.update(checkpointer.load(iteration, [w for w in wanted if not specs[w.key].trainable], KINDS[:1]))
     dev = rt.device
-    state = {k: {key: got[key][k].to(dev) for key in got} for k in KINDS}
+    state = {k: {key: got[key][k].to(dev) for key in got if k in got[key]} for k in KINDS}
     import_state(rt, state, step=iteration + 1)

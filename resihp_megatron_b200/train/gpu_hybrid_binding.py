@@ -28,11 +28,13 @@ from ..state.transaction import TransactionManager
 class GPUHybridBinding:
     def __init__(self, cfg: GPTConfig, client, mgr, *, micro_batch: int = 1, seq_len: int | None = None,
                  device="cuda", tp_impl: str = "collective", lr: float = 3e-4, seed: int = 0, data_seed: int = 1,
-                 migrate: str = "auto", hook=None, checkpointer=None, checkpoint_interval: int = 0):
+                 migrate: str = "auto", hook=None, checkpointer=None, checkpoint_interval: int = 0, fp8=None):
         """``migrate``: ``"p2p"`` (peer copies over NVLink), ``"engine"`` (NCCL / gloo send-receive)
         or ``"auto"`` (p2p on GPUs).  ``checkpointer`` (``state.checkpoint.SliceCheckpointer``):
         every ``checkpoint_interval`` committed iterations each rank writes its slices; a plan
-        that asks to restore (no surviving holder of some slice) loads the newest complete one."""
+        that asks to restore (no surviving holder of some slice) loads the newest complete one.
+        ``fp8``: an ``Fp8Recipe``; the amax histories are the transactions' rollback buffers and
+        migrate with their layers."""
         self.cfg, self.client, self.mgr = cfg, client, mgr
         self.micro_batch = micro_batch
         self.S = seq_len or cfg.seq_len
@@ -42,6 +44,7 @@ class GPUHybridBinding:
         self.migrate = ("p2p" if self.device.type == "cuda" else "engine") if migrate == "auto" else migrate
         self.hook = hook
         self.checkpointer, self.checkpoint_interval = checkpointer, checkpoint_interval
+        self.fp8 = fp8
         self.me = client.worker_id
         self.committed = None  # (plan, runtime)
         self.pending = None
@@ -63,12 +66,17 @@ class GPUHybridBinding:
         return GPUHybridRuntime(self.cfg, plan, schedule, comms, self.mgr, device=self.device,
                                 micro_batch=self.micro_batch, seq_len=self.S, tokens=self.tokens,
                                 tp_impl=self.tp_impl, dp_impl="collective", seed=self.seed, lr=self.lr, zero=False,
-                                init=init, progress=self.client.set_progress, hook=self.hook)
+                                init=init, progress=self.client.set_progress, hook=self.hook, fp8=self.fp8)
+
+    def _specs(self):
+        from ..runtime.gpu_state import gpu_tensor_specs
+
+        return gpu_tensor_specs(self.cfg, self.fp8.history if self.fp8 is not None else 0)
 
     def recover(self, comms, payload: dict, txm: TransactionManager) -> None:
         import time
 
-        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, gpu_tensor_specs, import_state
+        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, import_state
         from ..state.layer_registry import device_layout, holdings
         from ..state.transfer_engine import execute_transfers
         from ..state.transfer_plan import plan_transfers
@@ -90,14 +98,14 @@ class GPUHybridBinding:
 
             if self.checkpointer is None:
                 raise RuntimeError("restore requested but no checkpointer is configured")
-            specs = gpu_tensor_specs(self.cfg)
+            specs = self._specs()
             it = self.checkpointer.latest_complete({k: (sp.global_shape, sp.dim) for k, sp in specs.items()})
             if it is None:
                 raise RuntimeError("no complete checkpoint to restore from")
             load_checkpoint_into(rt, self.checkpointer, it, specs)
             txm.adopt(it)
         elif prev is not None and target >= 0:
-            specs = gpu_tensor_specs(self.cfg)
+            specs = self._specs()
             layer_of = gpu_layer_of(self.cfg.layers)
             old_plan = HeteroParallelPlan.from_json(prev)
             old_h, new_h = holdings(old_plan, specs, layer_of), holdings(plan, specs, layer_of)
@@ -155,14 +163,16 @@ class GPUHybridBinding:
     def after_commit(self, iteration: int, comms) -> None:
         if not (self.checkpointer and self.checkpoint_interval and (iteration + 1) % self.checkpoint_interval == 0):
             return
-        from ..runtime.gpu_state import checkpoint_slices, gpu_tensor_specs
+        from ..runtime.gpu_state import checkpoint_slices
 
         rt = self.committed[1]
-        self.checkpointer.save(iteration, self.me, checkpoint_slices(rt, gpu_tensor_specs(self.cfg)),
+        self.checkpointer.save(iteration, self.me, checkpoint_slices(rt, self._specs()),
                                extra={"step_count": rt.step_count}, blocking=True)
 
     def try_resume(self, txm: TransactionManager) -> None:
         pass
 
     def buffers(self) -> dict[str, torch.Tensor]:
-        return {}
+        """The live fp8 amax histories (snapshotted by each transaction, restored on abort)."""
+        current = self.pending or self.committed
+        return current[1].buffers() if current is not None else {}

@@ -52,10 +52,11 @@ class GPUHybridTrainer:
     def __init__(self, cfg: GPTConfig, *, tp: int, pp: int, dp: int, global_batch: int, micro_batch: int = 1,
                  seq_len: int | None = None, tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, device=None,
-                 data_seed: int = 1, migrate: str = "p2p"):
+                 data_seed: int = 1, migrate: str = "p2p", fp8=None):
         """``migrate``: how a reconfiguration moves state on GPUs -- ``"p2p"`` (one strided peer
         copy launch per rank over NVLink, ``parallel.migration``) or ``"nccl"`` (one send/receive
-        per slice and kind, ``state.transfer_engine``)."""
+        per slice and kind, ``state.transfer_engine``).  ``fp8``: an ``Fp8Recipe`` (block-scaled
+        fp8 projections; the per-layer amax histories migrate and checkpoint with their layers)."""
         from ..comm.comm_manager import ResilientCommManager
         from ..runtime.gpu_executor import TokenSource
         from ..runtime.gpu_runtime import GPUHybridRuntime
@@ -83,14 +84,21 @@ class GPUHybridTrainer:
                                         subgroup_mode="local", timeout_s=120)
         self.comms = self.mgr.adopt(1, ids, ids[rank], self._group_specs(self.plan, self.schedule))
         self.tokens = TokenSource(cfg.vocab_size, micro_batch, self.S, seed=data_seed)
+        self.fp8 = fp8
         self.opts = dict(micro_batch=micro_batch, seq_len=self.S, tokens=self.tokens, tp_impl=tp_impl, dp_impl=dp_impl,
-                         seed=seed, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+                         seed=seed, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, fp8=fp8)
         self.runtime = GPUHybridRuntime(cfg, self.plan, self.schedule, self.comms, self.mgr, device=self.device,
                                         **self.opts)
         self.tokens_per_step = self.runtime.tokens_per_step
         self.global_batch = global_batch
-        self.layout = f"tp{tp}pp{pp}dp{dp}-sp-{tp_impl}tp-{dp_impl}dp"
+        self.layout = f"tp{tp}pp{pp}dp{dp}-sp-{tp_impl}tp-{dp_impl}dp" + ("-fp8" if fp8 is not None else "")
         self.last_reconfig: dict | None = None
+
+    def tensor_specs(self):
+        """Logical tensors of the job (with the fp8 amax histories when fp8 is on)."""
+        from ..runtime.gpu_state import gpu_tensor_specs
+
+        return gpu_tensor_specs(self.cfg, self.fp8.history if self.fp8 is not None else 0)
 
     def _group_specs(self, plan, schedule):
         from ..runtime.gpu_runtime import gpu_group_specs
@@ -121,23 +129,23 @@ class GPUHybridTrainer:
         """Write this rank's slices of the last completed step to ``directory`` in the shared
         slice-checkpoint format (every rank calls it; collective inside ZeRO data-parallel
         groups).  Returns the checkpoint's iteration."""
-        from ..runtime.gpu_state import checkpoint_slices, gpu_tensor_specs
+        from ..runtime.gpu_state import checkpoint_slices
         from ..state.checkpoint import SliceCheckpointer
 
         it = self.runtime.iteration - 1
         me = self.plan.world[self.comms.rank]
         ck = SliceCheckpointer(directory)
-        ck.save(it, me, checkpoint_slices(self.runtime, gpu_tensor_specs(self.cfg)),
+        ck.save(it, me, checkpoint_slices(self.runtime, self.tensor_specs()),
                 extra={"step_count": self.runtime.step_count, "layout": self.layout}, blocking=True)
         return it
 
     def load_checkpoint(self, directory, iteration: int | None = None) -> int:
         """Load the newest complete checkpoint (or ``iteration``) from ``directory``, whatever
         layout wrote it, and continue from the step after it."""
-        from ..runtime.gpu_state import gpu_tensor_specs, load_checkpoint_into
+        from ..runtime.gpu_state import load_checkpoint_into
         from ..state.checkpoint import SliceCheckpointer
 
-        specs = gpu_tensor_specs(self.cfg)
+        specs = self.tensor_specs()
         ck = SliceCheckpointer(directory)
         if iteration is None:
             iteration = ck.latest_complete({k: (s.global_shape, s.dim) for k, s in specs.items()})
@@ -166,7 +174,7 @@ class GPUHybridTrainer:
         import time
 
         from ..runtime.gpu_runtime import GPUHybridRuntime
-        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, gpu_tensor_specs, import_state
+        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, import_state
         from ..state.layer_registry import device_layout, holdings
         from ..state.transfer_engine import execute_transfers
         from ..state.transfer_plan import plan_transfers
@@ -203,7 +211,7 @@ class GPUHybridTrainer:
         new_rt = GPUHybridRuntime(self.cfg, new_plan, new_schedule, comms, self.mgr, device=self.device, init=False,
                                   **self.opts)
         mark("build")
-        specs = gpu_tensor_specs(self.cfg)
+        specs = self.tensor_specs()
         layer_of = gpu_layer_of(self.cfg.layers)
         new_h = holdings(new_plan, specs, layer_of)
         tplan = plan_transfers(holdings(old_plan, specs, layer_of), new_h, valid_sources=set(new_world),
@@ -226,7 +234,8 @@ class GPUHybridTrainer:
                                           device=str(self.device))
         import_state(new_rt, new_state, step)
         new_rt.iteration = iteration
-        moved = sum(t.numel() * t.element_size() for k in KINDS for t in new_state[k].values())
+        moved = sum(t.numel() * t.element_size() for k in KINDS for key, t in new_state[k].items()
+                    if k == KINDS[0] or specs[key].trainable)
         del new_state, state
         mark("migrate")
         rt.close()
