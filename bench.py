@@ -73,7 +73,26 @@ def _args():
                     help="MoE models: expert dispatch / combine over NVLink peer memory, or NCCL all_to_all")
     ap.add_argument("--tp-impl", choices=["fused", "collective"], default="fused",
                     help="with --parallelism tp..: TP collectives fused into the GEMMs over NVLink, or NCCL")
+    ap.add_argument("--fp8", action="store_true",
+                    help="block-scaled fp8 projections (E4M3 forward / E5M2 backward, 1x128 activation and 128x128 "
+                         "weight scales, amax history 16; BASELINE config 4 with --model gpt-1.3b)")
+    ap.add_argument("--reshard", default=None,
+                    help="with --parallelism tp..: after the timed steps change the layout live on the same GPUs "
+                         "(e.g. tp2pp1dp4 after tp4pp1dp2: BASELINE config 4's TP4 -> TP2), migrating parameters, "
+                         "Adam moments and amax histories, and time the same steps again")
     return ap.parse_args()
+
+
+def fp8_recipe(args):
+    if not args.fp8:
+        return None
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+
+    return Fp8Recipe()
+
+
+def dtype_of(args) -> str:
+    return "fp8 (E4M3 fwd / E5M2 bwd, block-scaled) + bf16" if args.fp8 else "bf16"
 
 
 def parse_layout(text: str) -> tuple[int, int, int] | None:
@@ -187,7 +206,7 @@ def main() -> None:
         args.micro_batch = 1 if world == 1 else 2
     group = dist.group.WORLD if world > 1 else None
     trainer = GPUTrainer(cfg, global_batch=global_batch, micro_batch=args.micro_batch, seq_len=args.seq, seed=0,
-                         dp_group=group, dp_impl=args.dp_impl)
+                         dp_group=group, dp_impl=args.dp_impl, fp8=fp8_recipe(args))
     dev = trainer.device
 
     # synthetic data: uniform random token ids, next-token labels, one batch per step
@@ -311,7 +330,7 @@ def main() -> None:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": (value / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None,
-            "dtype": "bf16",
+            "dtype": dtype_of(args),
             "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
             "config": {
                 "model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
@@ -407,7 +426,7 @@ def _json_line(args, cfg, world: int, global_batch: int, mb: int, layout: str, r
     return {
         "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": r["ms"] / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": (r["value"] / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None, "dtype": "bf16",
+        "vs_baseline": (r["value"] / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None, "dtype": dtype_of(args),
         "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
         "config": {"model": cfg.name + ("" if not args.layers else f"-{args.layers}L-INVALID"),
                    "global_batch": global_batch, "seq_len": args.seq, "micro_batch": mb, "parallelism": layout,
@@ -418,6 +437,26 @@ def _json_line(args, cfg, world: int, global_batch: int, mb: int, layout: str, r
         "e2e": {"value": r["e2e"], "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4 * world},
         "gpu_launches": r["launches"], "loss": r["loss"], "impl": "ours",
     }
+
+
+def _post_steps(args, trainer) -> dict:
+    """Warm-up and device-timed steps after a reconfiguration (this rank's time)."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(max(2, min(args.warmup, 3))):
+        trainer.step_device()
+    torch.cuda.synchronize()
+    trainer.check()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    loss = None
+    for _ in range(args.steps):
+        loss = trainer.step_device()
+    end.record()
+    torch.cuda.synchronize()
+    return {"ms": start.elapsed_time(end), "loss": float(loss.item())}
 
 
 def run_moe(args, rank: int, world: int, local: int) -> None:
@@ -499,13 +538,31 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
     mb = args.micro_batch or 1
     trainer = GPUHybridTrainer(cfg, tp=tp, pp=pp, dp=dp, global_batch=global_batch, micro_batch=mb,
                                seq_len=args.seq, tp_impl=args.tp_impl,
-                               dp_impl="fused" if args.dp_impl == "fused" else "collective")
+                               dp_impl="fused" if args.dp_impl == "fused" else "collective", fp8=fp8_recipe(args))
     parts = [b - a for a, b in trainer.plan.layer_partition()]
     r = _timed_region(args, trainer, rank, world, local)
     # optional live reconfiguration: the last rank leaves; the planner re-plans the survivors
     # (TP shrink or eviction of its group, min-max layer repartition) and state migrates slice by slice
     recfg, alive = None, True
-    if args.reconfig:
+    if args.reshard:
+        new = parse_layout(args.reshard)
+        if new is None or new[0] * new[1] * new[2] != world:
+            raise SystemExit(f"--reshard {args.reshard!r} is not tp{{T}}pp{{P}}dp{{D}} with T*P*D = {world}")
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        trainer.reshard(*new)
+        commit_s = time.perf_counter() - t0
+        post = _post_steps(args, trainer)
+        vals = torch.tensor([post["ms"], commit_s], device=trainer.device, dtype=torch.float64)
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        post_ms, commit_max = vals.tolist()
+        recfg = {"kind": f"live reshard {args.parallelism} -> {args.reshard} on the same GPUs (params, Adam moments"
+                         " and amax histories migrated slice by slice)",
+                 "layout_post": trainer.layout, "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
+                 "post_ms_per_step": post_ms / args.steps, "reshard_to_commit_s": commit_max,
+                 "post_loss": post["loss"], "phases_s_rank0": trainer.last_reconfig}
+    elif args.reconfig:
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()

@@ -173,11 +173,7 @@ class GPUHybridTrainer:
         ``resihp/train/hetero_binding.py:95-130``.)"""
         import time
 
-        from ..runtime.gpu_runtime import GPUHybridRuntime
-        from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, import_state
-        from ..state.layer_registry import device_layout, holdings
-        from ..state.transfer_engine import execute_transfers
-        from ..state.transfer_plan import plan_transfers
+        from ..runtime.gpu_state import export_state
 
         marks = [("start", time.perf_counter())]
 
@@ -208,6 +204,66 @@ class GPUHybridTrainer:
         comms = self.mgr.build(new_plan.generation, new_world, me, self._group_specs(new_plan, new_schedule),
                                store=store, store_addr=store_addr, store_prefix=store_prefix)
         mark("regroup")
+        self._migrate_to(old_plan, new_plan, new_schedule, comms, me, new_world, state, layout, step, iteration, mark)
+        self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
+        self.last_reconfig.update(self._moved, layout=[(g.replica, g.stage, g.tp, list(g.layers))
+                                                       for g in new_plan.stage_groups], world=len(new_world))
+        return True
+
+    def reshard(self, tp: int, pp: int, dp: int) -> None:
+        """Planned live change of the layout on the same GPUs between steps (e.g. TP4 x DP2 ->
+        TP2 x DP4): every rank exports its slot's state, the joint planner lays out the new
+        degrees, the plan's groups are created on the existing world, and parameters, Adam
+        moments and the fp8 amax histories move slice by slice into the new layout (peer copies
+        over NVLink on GPUs); global batch, data order and step count are unchanged.  Phase
+        timings land in ``last_reconfig``."""
+        import dataclasses
+        import time
+
+        from ..runtime.gpu_state import export_state
+
+        marks = [("start", time.perf_counter())]
+
+        def mark(name: str) -> None:
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            marks.append((name, time.perf_counter()))
+
+        rt, old_plan = self.runtime, self.plan
+        world = list(old_plan.world)
+        if tp * pp * dp != len(world):
+            raise ValueError(f"tp {tp} x pp {pp} x dp {dp} != {len(world)} GPUs")
+        me = world[self.comms.rank]
+        state, layout = export_state(rt)
+        step, iteration = rt.step_count, rt.iteration
+        mark("export")
+        planner, topo = layout_planner(self.cfg, tp=tp, pp=pp, dp=dp, num_microbatches=old_plan.num_microbatches,
+                                       micro_batch=self.micro_batch, seq_len=self.S)
+        new_plan = dataclasses.replace(planner.initial_plan(topo), generation=old_plan.generation + 1)
+        if list(new_plan.world) != world:
+            raise RuntimeError("the new layout names other devices than the current world")
+        new_schedule, _ = planner.schedule(new_plan, topo)
+        mark("plan")
+        comms = self.mgr.adopt(new_plan.generation, world, me, self._group_specs(new_plan, new_schedule))
+        mark("regroup")
+        self._migrate_to(old_plan, new_plan, new_schedule, comms, me, world, state, layout, step, iteration, mark)
+        self.planner, self.topology = planner, topo
+        self.layout = f"tp{tp}pp{pp}dp{dp}-" + self.layout.split("-", 1)[1]
+        self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
+        self.last_reconfig.update(self._moved, layout=[(g.replica, g.stage, g.tp, list(g.layers))
+                                                       for g in new_plan.stage_groups], world=len(world))
+
+    def _migrate_to(self, old_plan, new_plan, new_schedule, comms, me, new_world, state, layout, step, iteration,
+                    mark) -> None:
+        """Build the new generation's runtime, move every slice it needs from the old holders
+        and switch to it (the old runtime is closed)."""
+        from ..runtime.gpu_runtime import GPUHybridRuntime
+        from ..runtime.gpu_state import KINDS, gpu_layer_of, import_state
+        from ..state.layer_registry import device_layout, holdings
+        from ..state.transfer_engine import execute_transfers
+        from ..state.transfer_plan import plan_transfers
+
+        rt = self.runtime
         new_rt = GPUHybridRuntime(self.cfg, new_plan, new_schedule, comms, self.mgr, device=self.device, init=False,
                                   **self.opts)
         mark("build")
@@ -241,11 +297,7 @@ class GPUHybridTrainer:
         rt.close()
         self.runtime, self.plan, self.schedule, self.comms = new_rt, new_plan, new_schedule, comms
         mark("commit")
-        self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
-        self.last_reconfig.update(bytes_loaded=moved, transfers=len(tplan.transfers),
-                                  layout=[(g.replica, g.stage, g.tp, list(g.layers)) for g in new_plan.stage_groups],
-                                  world=len(new_world))
-        return True
+        self._moved = {"bytes_loaded": moved, "transfers": len(tplan.transfers)}
 
     def close(self) -> None:
         if self.runtime is not None:

@@ -112,3 +112,44 @@ def test_fp8_histories_checkpoint_in_one_layout_and_resume_in_another(store, tmp
     assert set(saved) == set(restored)
     for k in saved:
         assert torch.equal(saved[k], restored[k]), k
+
+
+def _reshard(rank, world, port, store_addr, layout, new_layout, steps_before, steps_after):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    tp, pp, dp = layout
+    tr = GPUHybridTrainer(_cfg(), tp=tp, pp=pp, dp=dp, global_batch=8, micro_batch=1, seq_len=S,
+                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2, fp8=Fp8Recipe())
+    losses = [tr.train_step() for _ in range(steps_before)]
+    out = {"hist": _histories(tr)}
+    if new_layout is not None:
+        tr.reshard(*new_layout)
+        out["migrated"] = _histories(tr)
+        out["layout"] = tr.layout
+        out["phases"] = tr.last_reconfig
+    losses += [tr.train_step() for _ in range(steps_after)]
+    out["losses"] = losses
+    tr.close()
+    return out
+
+
+def test_fp8_live_reshard_tp2_to_tp1_keeps_the_run(store):
+    """TP2 x DP2 -> TP1 x DP4 on the same four ranks between steps: parameters, Adam moments and
+    amax histories move into the new layout and the run continues like the one-rank run."""
+    ref = spawn(_reshard, 1, store, (1, 1, 1), None, 4, 0, timeout=300)[0]["losses"]
+    res = spawn(_reshard, 4, store, (2, 1, 2), (1, 1, 4), 2, 2, timeout=400)
+    before, after = _union(res, "hist"), _union(res, "migrated")
+    assert set(before) == set(after)
+    for k in before:
+        assert torch.equal(before[k], after[k]), k
+    for r, out in res.items():
+        assert out["layout"].startswith("tp1pp1dp4") and out["phases"]["transfers"] > 0
+        for a, b in zip(out["losses"], ref):
+            assert abs(a - b) <= 3e-2 * abs(b), (r, out["losses"], ref)
