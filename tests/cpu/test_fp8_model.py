@@ -82,3 +82,36 @@ def test_fp8_weights_requantised_after_each_optimizer_step(fakes):
     q1 = m.f8.weight(0, "fc1").q_row.float()
     assert not torch.equal(q0, q1)
     assert m.f8.version == m.params.step == 1
+
+
+def test_single_rank_tp_stage_equals_the_model_in_fp8(fakes):
+    """``TPStage`` with one TP rank runs the same fp8 operations as ``LlamaModel``."""
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.models.tp_stage import TPStage
+    from resihp_megatron_b200.parallel.tp_backend import SoloTP
+
+    ids, labels = _batch()
+    m = _model(True)
+    st = TPStage(CFG, "cpu", layers=range(CFG.layers), first=True, last=True, tp=SoloTP("cpu"), micro_batch=1,
+                 seq_len=128, seed=3, fp8=Fp8Recipe())
+    R, P, M = st.rep, st.shd, m.params
+    for n in ("embed", "final_norm", "lm_head"):
+        R.w(n).copy_(M.w(n))
+    for l in range(CFG.layers):
+        p = f"layers.{l}."
+        for n in ("attn_norm", "mlp_norm"):
+            R.w(p + n).copy_(M.w(p + n))
+        st.wqkv(p).copy_(M.w(p + "wqkv"))
+        st.w13(p).copy_(M.w(p + "w1"))
+        P.w(p + "wo").copy_(M.w(p + "wo"))
+        P.w(p + "w2").copy_(M.w(p + "w2"))
+    m.forward_backward(ids, labels, 1.0 / ids.numel())
+    st.forward("mb", ids_local=ids, labels_local=labels, grad_scale=1.0 / ids.numel())
+    st.backward("mb")
+    assert st.loss_acc.item() == m.loss_acc.item()
+    assert torch.equal(st.f8.pending, m.f8.pending)
+    for l in range(CFG.layers):
+        p = f"layers.{l}."
+        assert torch.equal(st.wqkv(p, grad=True), M.g(p + "wqkv"))
+        assert torch.equal(st.w13(p, grad=True), M.g(p + "w1"))
+        assert torch.equal(P.g(p + "w2"), M.g(p + "w2"))

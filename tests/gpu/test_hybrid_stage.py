@@ -78,3 +78,47 @@ def test_hybrid_trainer_trains_on_one_gpu():
         tr.close()
     finally:
         dist.destroy_process_group()
+
+
+def test_single_rank_stage_matches_llama_model_in_fp8_with_gelu():
+    """The GPT (GELU) MLP with block-scaled fp8 projections: one TP rank of the stage runs the same
+    fp8 kernels in the same order as ``LlamaModel`` -- same loss, gradients and recorded amax."""
+    from resihp_megatron_b200.models.config import TINY
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.models.gpt import LlamaModel
+    from resihp_megatron_b200.models.tp_stage import TPStage
+    from resihp_megatron_b200.parallel.tp_backend import SoloTP
+
+    cfg = TINY.with_(hidden=256, heads=2, kv_heads=2, ffn=512, layers=2, vocab_size=512, mlp="gelu")
+    S = 256
+    stage = TPStage(cfg, "cuda", layers=range(cfg.layers), first=True, last=True, tp=SoloTP("cuda"), micro_batch=1,
+                    seq_len=S, fp8=Fp8Recipe())
+    model = LlamaModel(cfg, "cuda", micro_batch=1, seq_len=S, fp8=Fp8Recipe())
+    R, P, M = stage.rep, stage.shd, model.params
+    for n in ("embed", "final_norm", "lm_head"):
+        M.w(n).copy_(R.w(n))
+    for l in model.layer_ids:
+        p = f"layers.{l}."
+        for n in ("attn_norm", "mlp_norm"):
+            M.w(p + n).copy_(R.w(p + n))
+        M.w(p + "wqkv").copy_(stage.wqkv(p))
+        M.w(p + "w1").copy_(stage.w13(p))
+        M.w(p + "wo").copy_(P.w(p + "wo"))
+        M.w(p + "w2").copy_(P.w(p + "w2"))
+    g = torch.Generator(device="cuda").manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (S,), device="cuda", generator=g)
+    labels = torch.roll(ids, -1)
+    stage.forward("mb0", ids_local=ids, labels_local=labels, grad_scale=1.0 / S)
+    stage.backward("mb0")
+    model.loss_acc.zero_()
+    model.forward_backward(ids, labels, 1.0 / S)
+    torch.cuda.synchronize()
+    a, b = stage.loss_acc.item(), model.loss_acc.item()
+    assert math.isfinite(a) and abs(a - b) <= 1e-5 * abs(b), (a, b)
+    assert torch.allclose(stage.f8.pending, model.f8.pending, rtol=1e-5, atol=0)
+    for l in model.layer_ids:
+        p = f"layers.{l}."
+        for got, want in ((stage.wqkv(p, grad=True), M.g(p + "wqkv")), (stage.w13(p, grad=True), M.g(p + "w1")),
+                          (P.g(p + "wo"), M.g(p + "wo")), (P.g(p + "w2"), M.g(p + "w2"))):
+            err = (got - want).abs().max().item()
+            assert err <= 1e-5 * (want.abs().max().item() + 1e-12), err
