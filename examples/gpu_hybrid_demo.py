@@ -39,6 +39,7 @@ def main(argv=None) -> None:
     ap.add_argument("--timeout", type=float, default=30.0)
     ap.add_argument("--device", default="cuda", help="cuda (this worker's GPU) or cpu (gloo ranks)")
     ap.add_argument("--tp-impl", default="collective", choices=["fused", "collective"])
+    ap.add_argument("--fp8", action="store_true", help="block-scaled fp8 projections with per-layer amax history")
     ap.add_argument("--out", required=True)
     args = ap.parse_args(argv)
     torch.set_num_threads(1)
@@ -51,8 +52,13 @@ def main(argv=None) -> None:
     mgr = ResilientCommManager(backend, device=device, timeout_s=args.timeout, validate_timeout_s=args.timeout,
                                subgroup_mode="local")
     injector = get_injector()
+    fp8 = None
+    if args.fp8:
+        from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+
+        fp8 = Fp8Recipe()
     binding = GPUHybridBinding(GPU_DEMO, client, mgr, micro_batch=1, seq_len=GPU_DEMO.seq_len, device=device,
-                               tp_impl=args.tp_impl, lr=args.lr, hook=injector.on_hook if injector else None)
+                               tp_impl=args.tp_impl, lr=args.lr, hook=injector.on_hook if injector else None, fp8=fp8)
     result = ResilientTrainer(client, mgr, binding).run(args.iterations)
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
@@ -66,6 +72,8 @@ def main(argv=None) -> None:
         info["slot"] = None if g is None else {"replica": g.replica, "stage": g.stage, "tp": g.tp,
                                                "layers": list(g.layers)}
         info["generation"] = plan.generation
+        # steps recorded in each layer's amax history (an aborted iteration's entry is rolled back)
+        info["amax_steps"] = {k: int((v.abs().sum(0) > 0).sum()) for k, v in binding.buffers().items()}
     (out / f"{me}.json").write_text(json.dumps(info))
     mgr.destroy()
     client.close()

@@ -336,6 +336,7 @@ class GPUHybridRuntime:
         self.interp = Interpreter(plan, stream, self.executor, p2p, g.replica, g.stage, (cfg.hidden,), torch.bfloat16,
                                   tp_group=tp_pg, progress=progress, hook=hook)
         self.iteration = 0
+        self.hook = hook
         self.fp8 = fp8
         self._amax = None
         if fp8 is not None:
@@ -404,6 +405,8 @@ class GPUHybridRuntime:
         self.interp.run(it)
         if self.fp8 is not None:
             self._finish_fp8()
+        if self.hook is not None:  # after the loss and the amax reduction, before the gradient reduction
+            self.hook(it, "loss")
         for sync in self._syncs():
             sync.reduce()
         if step:
