@@ -20,8 +20,9 @@ inputs of the column-parallel weight gradients are recomputed and re-gathered.
 
 With the GPT MLP (``cfg.mlp == "gelu"``) the input projection is ``w1`` alone and
 ``a = gelu(AllGather(h2) W1_r^T)``.  With an ``Fp8Recipe`` (``fp8=``) the four projections run as
-block-scaled fp8 GEMMs (``models.fp8_linear``): the column-parallel ones gather the bf16 rows
-and quantise the gathered input, the row-parallel ones store their partial products straight
+block-scaled fp8 GEMMs (``models.fp8_linear``): for the column-parallel ones each rank quantises
+its own rows and the gather moves fp8 rows with their scales (half the bytes of bf16), the
+row-parallel ones store their partial products straight
 into the owners' receive slots from the fp8 GEMM's epilogue (``tp.gemm_rs_with``), and every
 rank records the amax of its operands for the per-layer history.
 
@@ -166,6 +167,7 @@ class TPStage:
             from .fp8_linear import Fp8Linears
 
             self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
+            self.ws_hl = torch.empty(self.Tl, cfg.hidden, dtype=torch.bfloat16, device=self.device)
 
     # ------------------------------------------------------------------ parameter views
     def _check_adjacent(self, p: str, names) -> None:
@@ -198,13 +200,27 @@ class TPStage:
         self.f8.refresh_weights(ws, self.shd.step)
 
     # ------------------------------------------------------------------ projections (bf16 or fp8)
+    def _col_in(self) -> torch.Tensor:
+        """Where the normalised rows of this rank go before a column-parallel projection: the
+        gather buffer's chunk (bf16), or a workspace that the fp8 path quantises from."""
+        return self.tp.chunk(self.T, self.cfg.hidden) if self.f8 is None else self.ws_hl
+
     def _col_fwd(self, l: int, lin: str, w: torch.Tensor, out: torch.Tensor) -> None:
-        """Column-parallel projection of the gathered chunks (the caller wrote this rank's rows)."""
+        """Column-parallel projection of the gathered rows (the caller wrote this rank's rows into
+        ``_col_in()``).  fp8: this rank quantises its own rows (row-major 1 x 128 scales) straight
+        into the gather buffer, the gather moves fp8 rows and their scales, the GEMM reads them."""
         T, H = self.T, self.cfg.hidden
         if self.f8 is None:
             self.tp.ag_gemm(T, w, out=out)
             return
-        self.f8.forward(l, lin, self.tp.all_gather(T, H), out)
+        fmt = self.f8.recipe.fwd_fmt
+        dt = fp8_ops.DTYPES[fmt]
+        q, sc = self.tp.fp8_local(T, H)
+        local = fp8_ops.Fp8Tensor(self.Tl, H, fmt, False, q.view(dt), sc, None, None, True)
+        fp8_ops.quantize(self.ws_hl, fmt, rowwise=True, amax=self.f8.amax(l, lin, "x"), out=local)
+        qf, sf = self.tp.all_gather_fp8(T, H)
+        xq = fp8_ops.Fp8Operand(qf.view(dt), sf, 1, H // fp8_ops.BLOCK, 0, fmt)
+        fp8_ops.gemm(xq, self.f8.weight(l, lin).rowwise(), out=out)
 
     def _row_fwd(self, l: int, lin: str, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
                  residual: torch.Tensor) -> None:
@@ -298,7 +314,7 @@ class TPStage:
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = slot.x[i]
-            self._rms(x, R.w(p + "attn_norm"), self.tp.chunk(T, H), slot.rstd1[i])
+            self._rms(x, R.w(p + "attn_norm"), self._col_in(), slot.rstd1[i])
             self._col_fwd(l, "qkv", self.wqkv(p), slot.qkv[i])
             q, k, v = self._qkv_views(slot.qkv[i])
             ops.rope_(q, self.nq, D, self.cos, self.sin, self.S)
@@ -306,7 +322,7 @@ class TPStage:
             ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.nq, kv_heads=self.nk, head_dim=D,
                               out=slot.o[i], lse=slot.lse[i])
             self._row_fwd(l, "o", slot.o[i], P.w(p + "wo"), slot.x2[i], x)
-            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), slot.rstd2[i])
+            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self._col_in(), slot.rstd2[i])
             self._col_fwd(l, "fc1", self.w13(p), slot.gu[i])
             mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
             self._row_fwd(l, "fc2", self.ws_a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])

@@ -605,11 +605,12 @@ static float* opt_f32(const c10::optional<torch::Tensor>& t, const char* name) {
 // Quantise bf16 x [R, C]; outputs are optional (rowwise q [R, C], colwise q [C, R]).
 void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::optional<torch::Tensor>& q_row,
                   const c10::optional<torch::Tensor>& s_row, const c10::optional<torch::Tensor>& q_col,
-                  const c10::optional<torch::Tensor>& s_col, const c10::optional<torch::Tensor>& amax) {
+                  const c10::optional<torch::Tensor>& s_col, const c10::optional<torch::Tensor>& amax,
+                  bool row_major) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2, "x must be a 2-D CUDA bf16 tensor");
   const long long ldx = ld_of(x, "x");
   const int R = x.size(0), C = x.size(1);
-  const long long nr = (R / 128), nc = (C / 128);
+  const long long nr = (R / 128), nc = (C / 128);  // R need not be a multiple of 128 for rowwise-only output
   if (q_row.has_value()) {
     check_fp8(*q_row, "q_row");
     TORCH_CHECK(q_row->size(0) == R && q_row->size(1) == C, "q_row must be [R, C]");
@@ -625,7 +626,7 @@ void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::op
   RB_CALL(rb::fp8_quantize(x.data_ptr(), ldx, R, C, static_cast<int>(fmt), two_d ? 1 : 0,
                            q_row.has_value() ? q_row->data_ptr() : nullptr, opt_f32(s_row, "s_row"),
                            q_col.has_value() ? q_col->data_ptr() : nullptr, opt_f32(s_col, "s_col"),
-                           reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream()),
+                           reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream(), row_major ? 1 : 0),
           "fp8_quantize");
 }
 
@@ -699,7 +700,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("amax_history_push", &amax_history_push);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
-        py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"));
+        py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"),
+        py::arg("row_major") = false);
   m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM", py::arg("a"), py::arg("a_fmt"), py::arg("sa"),
         py::arg("sa_kb"), py::arg("sa_row"), py::arg("sa_shift"), py::arg("b"), py::arg("b_fmt"), py::arg("sb"),
         py::arg("sb_kb"), py::arg("sb_row"), py::arg("sb_shift"), py::arg("out"), py::arg("epi"), py::arg("alpha"),

@@ -7,8 +7,9 @@
 // values are stored as fp8(x / s), rounded to nearest even (x / s itself is exact).  The
 // colwise output is written transposed ([C, R]) so that every GEMM operand is K-major.  Scales
 // are stored K-block major: the scale of operand row r in K-block kb sits at
-// kb * kb_stride + (r >> shift) * row_stride, so a tile's scales for one K-block are
-// contiguous.  Each CTA folds the magnitude of its tile into one atomicMax on the tensor's amax
+// kb * kb_stride + (r >> shift) * row_stride: K-block major by default, so a tile's scales for
+// one K-block are contiguous, or (rowwise, on request) row major, so that a row's scales travel
+// with it when the rows are gathered from other ranks.  Each CTA folds the magnitude of its tile into one atomicMax on the tensor's amax
 // word (bit pattern of |x|, so NaN and inf win), the input of the delayed-scaling history.
 //
 // GEMM (gemm_fp8_sm100).  D[m, n] = alpha * sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A(m, k) B(n, k)
@@ -87,8 +88,9 @@ struct QuantArgs {
   const uint16_t* x;  // bf16 bits
   long long ldx;
   int R, C, fmt, two_d;
-  uint8_t* q_row;  // [R, C] or null
-  float* s_row;    // 1x128: [C/128][R];  2-D: [C/128][R/128] (shared by both outputs)
+  int s_row_major;  // 1x128 rowwise scales stored [R][C/128] (a row's scales contiguous) instead of [C/128][R]
+  uint8_t* q_row;   // [R, C] or null
+  float* s_row;     // 1x128: [C/128][R] (or [R][C/128]);  2-D: [C/128][R/128] (shared by both outputs)
   uint8_t* q_col;  // [C, R] (transposed) or null
   float* s_col;    // 1x128: [R/128][C]
   unsigned int* amax;
@@ -107,9 +109,11 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(QuantArgs p) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int F = fp8_max_exp(p.fmt);
 
+  const int rows = min(kQT, p.R - r0);  // a partial last row tile only in rowwise-only mode
   for (int i = t; i < kQT * 16; i += 256) {
     const int r = i >> 4, c8 = i & 15;
-    const uint4 v = *reinterpret_cast<const uint4*>(p.x + static_cast<long long>(r0 + r) * p.ldx + c0 + c8 * 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < rows) v = *reinterpret_cast<const uint4*>(p.x + static_cast<long long>(r0 + r) * p.ldx + c0 + c8 * 8);
     *reinterpret_cast<uint4*>(tile + r * kQPitch + c8 * 8) = v;
   }
   __syncthreads();
@@ -146,13 +150,18 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(QuantArgs p) {
 #pragma unroll 4
     for (int rr = 0; rr < 16; ++rr) {
       const int r = warp * 16 + rr;
+      if (r >= rows) break;  // uniform across the warp (one row per warp iteration)
       const int e = fp8_scale_exp(p.two_d ? tmax : rowmax[r], F);
       const float inv = exp2_int(-e);
       const uint2 u = *reinterpret_cast<const uint2*>(tile + r * kQPitch + lane * 4);
       const uint32_t q = cvt4_fp8(bf16_bits_to_float(u.x & 0xffffu) * inv, bf16_bits_to_float(u.x >> 16) * inv,
                                   bf16_bits_to_float(u.y & 0xffffu) * inv, bf16_bits_to_float(u.y >> 16) * inv, p.fmt);
       *reinterpret_cast<uint32_t*>(p.q_row + static_cast<long long>(r0 + r) * p.C + c0 + lane * 4) = q;
-      if (!p.two_d && lane == 0) p.s_row[static_cast<long long>(cb) * p.R + r0 + r] = exp2_int(e);
+      if (!p.two_d && lane == 0) {
+        const long long si = p.s_row_major ? static_cast<long long>(r0 + r) * (p.C / kQT) + cb
+                                           : static_cast<long long>(cb) * p.R + r0 + r;
+        p.s_row[si] = exp2_int(e);
+      }
     }
   }
   if (p.q_col != nullptr) {
@@ -520,17 +529,19 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
 }  // namespace
 
 int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
-                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s) {
-  if (R <= 0 || C <= 0 || R % kQT || C % kQT || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -3;
+                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major) {
+  if (R <= 0 || C <= 0 || C % kQT || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -3;
+  if (R % kQT && (two_d || q_col != nullptr)) return -3;  // 128-row blocks need whole row tiles
   if ((reinterpret_cast<uintptr_t>(x) & 15) || ldx % 8 || ldx < C) return -4;
   if ((q_row != nullptr && s_row == nullptr) || (q_col != nullptr && !two_d && s_col == nullptr)) return -5;
   if (two_d && s_row == nullptr) return -5;
   if ((q_row != nullptr && (reinterpret_cast<uintptr_t>(q_row) & 15)) ||
       (q_col != nullptr && (reinterpret_cast<uintptr_t>(q_col) & 15)))
     return -6;
-  QuantArgs p{static_cast<const uint16_t*>(x), ldx, R, C, fmt, two_d, static_cast<uint8_t*>(q_row), s_row,
-              static_cast<uint8_t*>(q_col), s_col, amax};
-  dim3 grid(C / kQT, R / kQT);
+  if (s_row_major && two_d) return -3;
+  QuantArgs p{static_cast<const uint16_t*>(x), ldx, R, C, fmt, two_d, s_row_major, static_cast<uint8_t*>(q_row),
+              s_row, static_cast<uint8_t*>(q_col), s_col, amax};
+  dim3 grid(C / kQT, (R + kQT - 1) / kQT);
   fp8_quantize_kernel<<<grid, 256, 0, s>>>(p);
   return static_cast<int>(cudaGetLastError());
 }

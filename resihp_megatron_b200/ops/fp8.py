@@ -82,8 +82,9 @@ class Fp8Operand:
 @dataclass
 class Fp8Tensor:
     """A quantised bf16 ``[R, C]`` tensor: rowwise data ``[R, C]`` and/or colwise data ``[C, R]``.
-    Scales: 1 x 128 rowwise ``s_row`` ``[C/128, R]``, colwise ``s_col`` ``[R/128, C]``; with
-    ``two_d`` one ``s_row`` ``[C/128, R/128]`` serves both layouts."""
+    Scales: 1 x 128 rowwise ``s_row`` ``[C/128, R]`` (``row_major``: ``[R, C/128]``, a row's
+    scales contiguous -- they travel with the row in a gather), colwise ``s_col`` ``[R/128, C]``;
+    with ``two_d`` one ``s_row`` ``[C/128, R/128]`` serves both layouts."""
 
     R: int
     C: int
@@ -93,12 +94,14 @@ class Fp8Tensor:
     s_row: torch.Tensor | None
     q_col: torch.Tensor | None
     s_col: torch.Tensor | None
+    row_major: bool = False
 
     @classmethod
     def empty(cls, R: int, C: int, fmt: int = E4M3, *, two_d: bool = False, rowwise: bool = True,
-              colwise: bool = False, device=None) -> "Fp8Tensor":
-        if R % BLOCK or C % BLOCK:
-            raise ValueError(f"fp8 tensors need both dims multiples of {BLOCK}, got [{R}, {C}]")
+              colwise: bool = False, device=None, row_major: bool = False) -> "Fp8Tensor":
+        if C % BLOCK or (R % BLOCK and (two_d or colwise)):
+            raise ValueError(f"fp8 tensors need dims multiples of {BLOCK} (rows too unless rowwise-only), "
+                             f"got [{R}, {C}]")
         dt = DTYPES[fmt]
         f32 = dict(dtype=torch.float32, device=device)
         q_row = torch.empty(R, C, dtype=dt, device=device) if rowwise else None
@@ -106,15 +109,18 @@ class Fp8Tensor:
         if two_d:
             s_row, s_col = torch.empty(C // BLOCK, R // BLOCK, **f32), None
         else:
-            s_row = torch.empty(C // BLOCK, R, **f32) if rowwise else None
+            s_row = (torch.empty(R, C // BLOCK, **f32) if row_major else torch.empty(C // BLOCK, R, **f32)) \
+                if rowwise else None
             s_col = torch.empty(R // BLOCK, C, **f32) if colwise else None
-        return cls(R, C, fmt, two_d, q_row, s_row, q_col, s_col)
+        return cls(R, C, fmt, two_d, q_row, s_row, q_col, s_col, row_major and not two_d)
 
     def rowwise(self) -> Fp8Operand:
         """Operand ``[R, K = C]`` (forward input, weight for the forward, dgrad's gradient)."""
         assert self.q_row is not None, "quantised without the rowwise layout"
         if self.two_d:
             return Fp8Operand(self.q_row, self.s_row, self.R // BLOCK, 1, 7, self.fmt)
+        if self.row_major:
+            return Fp8Operand(self.q_row, self.s_row, 1, self.C // BLOCK, 0, self.fmt)
         return Fp8Operand(self.q_row, self.s_row, self.R, 1, 0, self.fmt)
 
     def colwise(self) -> Fp8Operand:
@@ -126,14 +132,17 @@ class Fp8Tensor:
 
 
 def quantize(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = False, rowwise: bool = True,
-             colwise: bool = False, amax: torch.Tensor | None = None, out: Fp8Tensor | None = None) -> Fp8Tensor:
-    """Quantise bf16 ``x [R, C]`` (R, C multiples of 128).  ``amax`` (fp32, >= 1 element) receives
-    ``max(amax[0], max |x|)`` -- NaN and inf propagate."""
+             colwise: bool = False, amax: torch.Tensor | None = None, out: Fp8Tensor | None = None,
+             row_major: bool = False) -> Fp8Tensor:
+    """Quantise bf16 ``x [R, C]`` (C a multiple of 128; R too unless rowwise-only).  ``amax`` (fp32, >= 1 element) receives
+    ``max(amax[0], max |x|)`` -- NaN and inf propagate.  ``row_major``: rowwise scales stored
+    ``[R, C/128]`` (taken from ``out`` when given)."""
     fmt = fmt_of(fmt)
     R, C = x.shape
     if out is None:
-        out = Fp8Tensor.empty(R, C, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, device=x.device)
-    ext().fp8_quantize(x, fmt, two_d, _u8(out.q_row), out.s_row, _u8(out.q_col), out.s_col, amax)
+        out = Fp8Tensor.empty(R, C, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, device=x.device,
+                              row_major=row_major)
+    ext().fp8_quantize(x, fmt, two_d, _u8(out.q_row), out.s_row, _u8(out.q_col), out.s_col, amax, out.row_major)
     count(1)
     return out
 
@@ -211,16 +220,16 @@ def pow2(e: torch.Tensor) -> torch.Tensor:
 
 
 def quantize_reference(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = False, rowwise: bool = True,
-                       colwise: bool = False, amax: torch.Tensor | None = None) -> Fp8Tensor:
+                       colwise: bool = False, amax: torch.Tensor | None = None, row_major: bool = False) -> Fp8Tensor:
     """``quantize`` in PyTorch (any device): same bytes and scales for finite inputs."""
     fmt = fmt_of(fmt)
     R, C = x.shape
-    if R % BLOCK or C % BLOCK:
-        raise ValueError(f"fp8 tensors need both dims multiples of {BLOCK}, got [{R}, {C}]")
+    if C % BLOCK or (R % BLOCK and (two_d or colwise)):
+        raise ValueError(f"fp8 tensors need dims multiples of {BLOCK} (rows too unless rowwise-only), got [{R}, {C}]")
     xf = x.float()
     dt = DTYPES[fmt]
     nr, nc = R // BLOCK, C // BLOCK
-    out = Fp8Tensor(R, C, fmt, two_d, None, None, None, None)
+    out = Fp8Tensor(R, C, fmt, two_d, None, None, None, None, row_major and not two_d)
     if amax is not None:
         amax[0] = torch.maximum(amax[0], xf.abs().max())
     if two_d:
@@ -238,7 +247,7 @@ def quantize_reference(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = 
         bmax = xf.abs().reshape(R, nc, BLOCK).amax(-1)  # [R, nc]
         e = scale_exponent(bmax, fmt)
         out.q_row = (xf * pow2(-e).repeat_interleave(BLOCK, 1)).to(dt)
-        out.s_row = pow2(e).t().contiguous()
+        out.s_row = pow2(e).contiguous() if out.row_major else pow2(e).t().contiguous()
     if colwise:
         bmax = xf.abs().reshape(nr, BLOCK, C).amax(1)  # [nr, C]
         e = scale_exponent(bmax, fmt)

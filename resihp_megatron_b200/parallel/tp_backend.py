@@ -19,6 +19,11 @@ Operations:
 * ``ag_gemm(M, w, out, w_t)`` -> ``(AllGather(chunks) @ op(w)^T, gathered input)``;
 * ``all_gather(M, K)`` -> the gathered ``[M, K]`` chunks;
 * ``gemm_rs(x, w, out, w_t, residual)`` -> ``ReduceScatter_rows(x @ op(w)^T) (+ residual)``;
+* ``fp8_local(M, K)`` / ``all_gather_fp8(M, K)`` -- the gather of a block-scaled fp8 input: this
+  rank quantises its rows (1 x 128 row scales, row-major so a row's scales travel with it) into
+  ``fp8_local``'s ``(data [M / tp, K] uint8, scales [M / tp, K / 128])``; the gather returns the
+  ``[M, K]`` / ``[M, K / 128]`` views -- half the bytes of the bf16 gather, and no
+  quantisation pass over the gathered rows;
 * ``gemm_rs_with(M, N, gemm, out, residual)`` -> the same for any GEMM (the block-scaled fp8
   one): ``gemm(out=..., residual=..., scatter=(recv_ptrs, slot))`` writes the ``[M, N]`` product
   into a local buffer (optionally plus a residual) or, with ``scatter``, stores each row
@@ -57,11 +62,40 @@ class _Buffers:
         self.turn ^= 1
 
 
+class _Fp8Buffers:
+    """Two alternating ``([M, K] uint8, [M, K / 128] fp32)`` buffers per shape."""
+
+    def __init__(self, device):
+        self.device = device
+        self.bufs: dict[tuple[int, int], list] = {}
+        self.turn = 0
+
+    def current(self, M: int, K: int):
+        pair = self.bufs.get((M, K))
+        if pair is None:
+            pair = [(torch.empty(M, K, dtype=torch.uint8, device=self.device),
+                     torch.empty(M, K // 128, dtype=torch.float32, device=self.device)) for _ in range(2)]
+            self.bufs[(M, K)] = pair
+        return pair[self.turn]
+
+    def advance(self) -> None:
+        self.turn ^= 1
+
+
 class SoloTP:
     world, rank = 1, 0
 
     def __init__(self, device):
         self.buf = _Buffers(device)
+        self.f8 = _Fp8Buffers(device)
+
+    def fp8_local(self, M: int, K: int):
+        return self.f8.current(M, K)
+
+    def all_gather_fp8(self, M: int, K: int):
+        out = self.f8.current(M, K)
+        self.f8.advance()
+        return out
 
     def chunk(self, M: int, K: int) -> torch.Tensor:
         return self.buf.current(M, K)
@@ -96,12 +130,26 @@ class CollectiveTP:
         self.rank, self.world, self.group = rank, world, group
         self.device = torch.device(device)
         self.buf = _Buffers(self.device)
+        self.f8 = _Fp8Buffers(self.device)
         self.partials: dict[tuple[int, int], torch.Tensor] = {}
         self.wait = waiter or (lambda work: work.wait())
 
     def chunk(self, M: int, K: int) -> torch.Tensor:
         rows = M // self.world
         return self.buf.current(M, K)[self.rank * rows:(self.rank + 1) * rows]
+
+    def fp8_local(self, M: int, K: int):
+        q, s = self.f8.current(M, K)
+        rows = M // self.world
+        return q[self.rank * rows:(self.rank + 1) * rows], s[self.rank * rows:(self.rank + 1) * rows]
+
+    def all_gather_fp8(self, M: int, K: int):
+        q, s = self.f8.current(M, K)
+        self.f8.advance()
+        ql, sl = q.chunk(self.world)[self.rank], s.chunk(self.world)[self.rank]
+        self.wait(dist.all_gather_into_tensor(q, ql, group=self.group, async_op=True))
+        self.wait(dist.all_gather_into_tensor(s, sl, group=self.group, async_op=True))
+        return q, s
 
     def all_gather(self, M: int, K: int) -> torch.Tensor:
         full = self.buf.current(M, K)
@@ -162,6 +210,12 @@ class FusedTP:
 
     def all_gather(self, M: int, K: int) -> torch.Tensor:
         return self.comm.all_gather(M, K)
+
+    def fp8_local(self, M: int, K: int):
+        return self.comm.fp8_local(M, K)
+
+    def all_gather_fp8(self, M: int, K: int):
+        return self.comm.all_gather_fp8(M, K)
 
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, w_t: bool = False,
                 residual: torch.Tensor | None = None) -> torch.Tensor:

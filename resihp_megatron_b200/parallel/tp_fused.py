@@ -110,6 +110,45 @@ class TensorParallelComm:
             self._ag ^= 1
         return xf
 
+    # ------------------------------------------------------------------ fp8 all-gather
+    def _fp8_offset(self, M: int, K: int) -> int:
+        return (M * K + 255) // 256 * 256
+
+    def fp8_views(self, M: int, K: int, buf: int | None = None):
+        """The fp8 gather layout inside gather buffer ``buf``: ``[M, K]`` bytes, then row-major
+        ``[M, K / 128]`` fp32 scales (together at most half the bf16 ``[M, K]`` buffer + M K / 32)."""
+        b = self._ag if buf is None else buf
+        raw = self.heap.tensor(f"x_full{b}").view(torch.uint8)
+        off, nk = self._fp8_offset(M, K), K // 128
+        assert off + M * nk * 4 <= raw.numel(), "fp8 gather does not fit the gather buffer"
+        return raw[: M * K].view(M, K), raw[off: off + M * nk * 4].view(torch.float32).view(M, nk)
+
+    def fp8_local(self, M: int, K: int):
+        """Where this rank quantises its ``[M / tp, K]`` rows (and their scales) before the gather."""
+        q, s = self.fp8_views(M, K)
+        rows = M // self.world
+        return q[self.rank * rows:(self.rank + 1) * rows], s[self.rank * rows:(self.rank + 1) * rows]
+
+    def all_gather_fp8(self, M: int, K: int, advance: bool = True):
+        """Gather every rank's fp8 rows and row scales (peer pulls, two launches)."""
+        b = self._ag
+        q, s = self.fp8_views(M, K, b)
+        rows, nk = M // self.world, K // 128
+        off = self._fp8_offset(M, K)
+        if (rows * K) % 16 or (rows * nk * 4) % 16:
+            raise ValueError("fp8 gather chunks must be multiples of 16 bytes")
+        base = self.heap.peer_ptrs(f"x_full{b}")
+        dev = q.device.index if q.device.index is not None else 0
+        self._barrier()
+        ext().symm_gather([base[c] + c * rows * K for c in range(self.world)], base[self.rank], rows * K, self.rank,
+                          dev)
+        ext().symm_gather([base[c] + off + c * rows * nk * 4 for c in range(self.world)], base[self.rank] + off,
+                          rows * nk * 4, self.rank, dev)
+        count(3 if not self.emulated else 2)
+        if advance:
+            self._ag ^= 1
+        return q, s
+
     # ------------------------------------------------------------------ GEMM -> reduce-scatter
     def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
                             w_t: bool = False, residual: torch.Tensor | None = None) -> torch.Tensor:

@@ -92,7 +92,11 @@ def test_linear_layer_gemms_match_fp32():
 
 def test_rejects_unaligned_shapes():
     with pytest.raises(ValueError):
-        fp8.quantize_reference(torch.zeros(100, 128).bfloat16())
+        fp8.quantize_reference(torch.zeros(100, 128).bfloat16(), colwise=True)
+    with pytest.raises(ValueError):
+        fp8.quantize_reference(torch.zeros(128, 100).bfloat16())
+    part = fp8.quantize_reference(torch.ones(100, 128).bfloat16(), row_major=True)  # rowwise-only: any rows
+    assert part.rowwise().dequantize().eq(1).all() and part.s_row.shape == (100, 1)
     with pytest.raises(ValueError):
         fp8.Fp8Tensor.empty(128, 200)
     assert math.isclose(1.75 * 2 ** fp8.MAX_EXP[fp8.E4M3], 448.0)

@@ -87,3 +87,43 @@ def test_transposed_weight_variants(world):
         g = t.all_gather(M, K, advance=False)
         assert torch.equal(g, x_all.bfloat16())
     ranks[0].close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_fp8_all_gather_and_fp8_gemm_reduce_scatter(world):
+    """Block-scaled fp8 under tensor parallelism: every rank quantises its rows (row-major scales)
+    into the gather buffer and the fp8 gather moves rows and scales (bit-identical to quantising
+    the gathered tensor); the fp8 GEMM's scatter epilogue feeds the rank-ordered reduction."""
+    from resihp_megatron_b200.ops import fp8
+    from resihp_megatron_b200.parallel.tp_fused import TensorParallelComm
+
+    M, K, N = 1024, 512, 256
+    ranks = TensorParallelComm.emulated_group(world, "cuda", max_rows=M, max_k=K, max_n=N)
+    torch.manual_seed(2)
+    rows = M // world
+    xs = [torch.randn(rows, K, device="cuda").bfloat16() for _ in range(world)]
+    for r, t in enumerate(ranks):
+        q, s = t.fp8_local(M, K)
+        local = fp8.Fp8Tensor(rows, K, fp8.E4M3, False, q.view(fp8.DTYPES[fp8.E4M3]), s, None, None, True)
+        fp8.quantize(xs[r], fp8.E4M3, out=local)
+    torch.cuda.synchronize()
+    ref = fp8.quantize_reference(torch.cat(xs), fp8.E4M3, row_major=True)
+    for t in ranks:
+        q, s = t.all_gather_fp8(M, K, advance=False)
+        torch.cuda.synchronize()
+        assert torch.equal(q, ref.q_row.view(torch.uint8)) and torch.equal(s, ref.s_row)
+    # row-parallel fp8 GEMM -> reduce-scatter through the scatter epilogue
+    a = [fp8.quantize(torch.randn(M, K, device="cuda").bfloat16(), fp8.E4M3) for _ in range(world)]
+    w = [fp8.quantize((torch.randn(N, K, device="cuda") * 0.05).bfloat16(), fp8.E4M3, two_d=True)
+         for _ in range(world)]
+    for r, t in enumerate(ranks):
+        fp8.gemm(a[r].rowwise(), w[r].rowwise(), scatter=(t.heap.peer_ptrs(f"rs_recv{t._rs}"), r))
+    parts = [fp8.gemm_reference(a[r].rowwise(), w[r].rowwise(), out_dtype=torch.bfloat16).float()
+             for r in range(world)]
+    full = sum(parts)
+    outs = [t.reduce_received(M, N) for t in ranks]
+    torch.cuda.synchronize()
+    for q, y in enumerate(outs):
+        want = full[q * rows:(q + 1) * rows]
+        assert (y.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item() + 1e-3, q
+    ranks[0].close()

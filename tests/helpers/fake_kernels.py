@@ -193,10 +193,13 @@ def gelu_bwd(h, da, out=None):
 
 
 # block-scaled fp8: the PyTorch emulation of the kernels (bit-exact quantiser)
-def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=None, out=None):
+def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=None, out=None, row_major=False):
     from resihp_megatron_b200.ops import fp8
 
-    ref = fp8.quantize_reference(x, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, amax=amax)
+    if out is not None:
+        row_major = out.row_major
+    ref = fp8.quantize_reference(x, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, amax=amax,
+                                 row_major=row_major)
     if out is None:
         return ref
     for name in ("q_row", "s_row", "q_col", "s_col"):
