@@ -114,12 +114,14 @@ class TPStage:
     def __init__(self, cfg: GPTConfig, device, *, layers, first: bool, last: bool, tp, micro_batch: int = 1,
                  seq_len: int | None = None, seed: int = 0, rep_shard: tuple[int, int] = (0, 1),
                  shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None),
-                 init: bool = True, fp8=None):
+                 init: bool = True, fp8=None, sp: bool = True):
         """``tp``: the tensor-parallel backend (``parallel.tp_backend``); ``*_shard`` the
         (rank, count) of the ZeRO-1 optimizer shard of each parameter set over its
         data-parallel group; ``*_factories`` the (buffer, optimizer) factories of ``FlatParams``
         (the fused data-parallel step's peer heap); ``init`` draws the initial weights;
-        ``fp8`` an ``Fp8Recipe`` for block-scaled fp8 projections."""
+        ``fp8`` an ``Fp8Recipe`` for block-scaled fp8 projections; ``sp=False``: plain tensor
+        parallelism (every TP rank holds every token row; the backend all-reduces instead of
+        reduce-scattering)."""
         self.cfg, self.device = cfg, torch.device(device)
         self.tp = tp
         self.tp_rank, self.tp_size = tp.rank, tp.world
@@ -130,7 +132,10 @@ class TPStage:
         self.T = self.mb * self.S
         if self.T % self.tp_size:
             raise ValueError(f"{self.T} tokens per micro-batch do not split over tp={self.tp_size}")
-        self.Tl = self.T // self.tp_size
+        self.sp = sp
+        if getattr(tp, "sp", True) != sp:
+            raise ValueError("the stage and its TP backend disagree on sequence parallelism")
+        self.Tl = self.T // self.tp_size if sp else self.T
         self.nq, self.nk = cfg.heads // self.tp_size, cfg.kv_heads // self.tp_size
         self.nf = cfg.ffn // self.tp_size
         self.mlp_in = (2 if cfg.gated else 1) * self.nf

@@ -29,7 +29,12 @@ Operations:
   into a local buffer (optionally plus a residual) or, with ``scatter``, stores each row
   straight into its owner's receive slot.
 
-``op(w) = w`` (``[N, K]``) or, with ``w_t``, ``w.T`` (``w`` stored ``[K, N]``).  A gathered input
+``op(w) = w`` (``[N, K]``) or, with ``w_t``, ``w.T`` (``w`` stored ``[K, N]``).
+
+Without sequence parallelism (``sp=False``) the residual stream is replicated on every TP rank:
+``chunk`` is the whole ``[M, K]`` buffer, the gathers move nothing, and the reduce-scatter
+becomes an all-reduce (the GEMM -> all-reduce of Megatron's plain tensor parallelism; fused:
+the GEMM -> reduce-scatter kernel pair followed by a peer all-gather of the reduced rows).  A gathered input
 stays valid until the gather after next (two buffers alternate), which is what the weight
 gradients of a layer need.  (Reference: the sequence-parallel autograd functions
 ``_GatherFromSP`` / ``_ReduceScatterToSP``, ``resihp/runtime/reference_model.py:134-192``.)
@@ -84,6 +89,7 @@ class _Fp8Buffers:
 
 class SoloTP:
     world, rank = 1, 0
+    sp = True  # one rank: both modes coincide
 
     def __init__(self, device):
         self.buf = _Buffers(device)
@@ -126,8 +132,9 @@ class SoloTP:
 class CollectiveTP:
     """Library collectives on ``group`` (this rank is ``rank`` of ``world``)."""
 
-    def __init__(self, rank: int, world: int, group, device, waiter=None):
+    def __init__(self, rank: int, world: int, group, device, waiter=None, sp: bool = True):
         self.rank, self.world, self.group = rank, world, group
+        self.sp = sp
         self.device = torch.device(device)
         self.buf = _Buffers(self.device)
         self.f8 = _Fp8Buffers(self.device)
@@ -135,17 +142,23 @@ class CollectiveTP:
         self.wait = waiter or (lambda work: work.wait())
 
     def chunk(self, M: int, K: int) -> torch.Tensor:
+        if not self.sp:
+            return self.buf.current(M, K)
         rows = M // self.world
         return self.buf.current(M, K)[self.rank * rows:(self.rank + 1) * rows]
 
     def fp8_local(self, M: int, K: int):
         q, s = self.f8.current(M, K)
+        if not self.sp:
+            return q, s
         rows = M // self.world
         return q[self.rank * rows:(self.rank + 1) * rows], s[self.rank * rows:(self.rank + 1) * rows]
 
     def all_gather_fp8(self, M: int, K: int):
         q, s = self.f8.current(M, K)
         self.f8.advance()
+        if not self.sp:
+            return q, s
         ql, sl = q.chunk(self.world)[self.rank], s.chunk(self.world)[self.rank]
         self.wait(dist.all_gather_into_tensor(q, ql, group=self.group, async_op=True))
         self.wait(dist.all_gather_into_tensor(s, sl, group=self.group, async_op=True))
@@ -154,6 +167,8 @@ class CollectiveTP:
     def all_gather(self, M: int, K: int) -> torch.Tensor:
         full = self.buf.current(M, K)
         self.buf.advance()
+        if not self.sp:
+            return full
         rows = M // self.world
         mine = full[self.rank * rows:(self.rank + 1) * rows]
         self.wait(dist.all_gather_into_tensor(full, mine, group=self.group, async_op=True))
@@ -183,6 +198,13 @@ class CollectiveTP:
 
     def _reduce_scatter(self, part: torch.Tensor, out, residual) -> torch.Tensor:
         M, N = part.shape
+        if not self.sp:  # all-reduce: every rank keeps every row
+            self.wait(dist.all_reduce(part, group=self.group, async_op=True))
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=self.device) if out is None else out
+            y.copy_(part)
+            if residual is not None:
+                y.add_(residual)
+            return y
         y = torch.empty(M // self.world, N, dtype=torch.bfloat16, device=self.device) if out is None else out
         self.wait(dist.reduce_scatter_tensor(y, part, group=self.group, async_op=True))
         if residual is not None:
@@ -196,34 +218,65 @@ class CollectiveTP:
 class FusedTP:
     """``TensorParallelComm`` (symmetric heap of this TP group) behind the stage interface."""
 
-    def __init__(self, comm):
+    def __init__(self, comm, sp: bool = True):
         self.comm = comm
         self.rank, self.world = comm.rank, comm.world
+        self.sp = sp
 
     def chunk(self, M: int, K: int) -> torch.Tensor:
-        return self.comm.local_chunk(M, K)
+        return self.comm.local_chunk(M, K) if self.sp else self.comm.gather_buffer(M, K)
 
     def ag_gemm(self, M: int, w: torch.Tensor, out: torch.Tensor | None = None, w_t: bool = False):
         K = w.shape[0] if w_t else w.shape[1]
         x = self.comm.gather_buffer(M, K)
+        if not self.sp:
+            self.comm.advance_gather()
+            return ops.gemm(x, w, b_t=w_t, out=out), x
         return self.comm.all_gather_gemm(M, w, out=out, w_t=w_t), x
 
     def all_gather(self, M: int, K: int) -> torch.Tensor:
+        if not self.sp:
+            x = self.comm.gather_buffer(M, K)
+            self.comm.advance_gather()
+            return x
         return self.comm.all_gather(M, K)
 
     def fp8_local(self, M: int, K: int):
-        return self.comm.fp8_local(M, K)
+        return self.comm.fp8_local(M, K) if self.sp else self.comm.fp8_views(M, K)
 
     def all_gather_fp8(self, M: int, K: int):
+        if not self.sp:
+            out = self.comm.fp8_views(M, K)
+            self.comm.advance_gather()
+            return out
         return self.comm.all_gather_fp8(M, K)
 
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, w_t: bool = False,
                 residual: torch.Tensor | None = None) -> torch.Tensor:
+        if not self.sp:
+            N = w.shape[1] if w_t else w.shape[0]
+            return self._all_reduce(x.shape[0], N, lambda mine, res: self.comm.gemm_reduce_scatter(
+                x, w, out=mine, w_t=w_t, residual=res), out, residual)
         return self.comm.gemm_reduce_scatter(x, w, out=out, w_t=w_t, residual=residual)
 
     def gemm_rs_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
                      residual: torch.Tensor | None = None) -> torch.Tensor:
+        if not self.sp:
+            return self._all_reduce(M, N, lambda mine, res: self.comm.reduce_scatter_with(
+                M, N, gemm, out=mine, residual=res), out, residual)
         return self.comm.reduce_scatter_with(M, N, gemm, out=out, residual=residual)
+
+    def _all_reduce(self, M: int, N: int, reduce_scatter, out, residual) -> torch.Tensor:
+        """GEMM -> all-reduce as GEMM -> reduce-scatter (this rank's reduced rows, plus the
+        replicated residual's same rows, land in its gather chunk) and a peer all-gather."""
+        rows = M // self.world
+        mine = self.comm.local_chunk(M, N)
+        res = None if residual is None else residual[self.rank * rows:(self.rank + 1) * rows]
+        reduce_scatter(mine, res)
+        full = self.comm.all_gather(M, N)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=full.device) if out is None else out
+        y.copy_(full)
+        return y
 
     def check(self) -> None:
         self.comm.heap.check()

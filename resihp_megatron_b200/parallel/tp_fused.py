@@ -69,6 +69,10 @@ class TensorParallelComm:
         b = self._ag if buf is None else buf
         return self.heap.tensor(f"x_full{b}")[: M * K].view(M, K)
 
+    def advance_gather(self) -> None:
+        """Use the other gather buffer next (a gather that moved nothing still takes its turn)."""
+        self._ag ^= 1
+
     def local_chunk(self, M: int, K: int) -> torch.Tensor:
         """Where this rank writes its ``[M / tp, K]`` shard before the next gather."""
         rows = M // self.world

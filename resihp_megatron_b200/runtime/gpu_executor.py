@@ -43,7 +43,9 @@ class GPUStageExecutor:
     stage); a plan without interleaving has one chunk."""
 
     def __init__(self, stages: dict, plan: HeteroParallelPlan, replica: int, rank: int, tokens: TokenSource,
-                 grad_scale: float):
+                 grad_scale: float, sp: bool = True):
+        """``sp=False`` (plain TP): every TP rank takes every token row, and only the slot's first
+        TP rank counts the loss (the others compute the same value)."""
         self.models = dict(stages)
         self.plan = plan
         self.group = plan.group(replica, min(self.models))
@@ -57,7 +59,9 @@ class GPUStageExecutor:
         first = next(iter(self.models.values()))
         self.device = first.device
         self.T = first.T
-        self.rows = local_rows(first.T, self.ranks, rank)
+        self.sp = sp
+        self.rows = local_rows(first.T, self.ranks, rank) if sp else (0, first.T)
+        self.counts_loss = sp or self.ranks.index(rank) == 0
         self._host: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.h2d_bytes = 0
         self.split_backward = False  # zero-bubble schedules: weight gradients in the W pass
@@ -100,6 +104,6 @@ class GPUStageExecutor:
         for m in self.models.values():
             if m.last:
                 total = m.loss_acc if total is None else total + m.loss_acc
-        if total is None:
-            total = next(iter(self.models.values())).loss_acc  # zero: no chunk computes the loss
+        if total is None or not self.counts_loss:
+            total = torch.zeros((), dtype=torch.float32, device=self.device)  # no chunk here counts the loss
         return total

@@ -289,6 +289,7 @@ class GPUHybridRuntime:
         tp_pg = comms.group(tp_group_name(g.replica, g.stage)) if g.tp > 1 else None
         from ..parallel import tp_backend
 
+        self.sp = plan.sequence_parallel or g.tp == 1
         if g.tp == 1:
             self.tp = tp_backend.SoloTP(self.device)
         elif tp_impl == "fused":
@@ -297,11 +298,11 @@ class GPUHybridRuntime:
 
             comm = TensorParallelComm(tp_rank, g.tp, exchange_via_group(tp_pg), self.device, max_rows=T,
                                       max_k=cfg.hidden, max_n=cfg.hidden, abort=self.abort, budget_s=budget_s)
-            self.tp = tp_backend.FusedTP(comm)
+            self.tp = tp_backend.FusedTP(comm, sp=self.sp)
         elif tp_impl == "collective":
             self.tp = tp_backend.CollectiveTP(tp_rank, g.tp, tp_pg, self.device,
                                               waiter=(lambda w: mgr.guarded_wait(w, what="tp collective"))
-                                              if mgr is not None else None)
+                                              if mgr is not None else None, sp=self.sp)
         else:
             raise ValueError(tp_impl)
         # one model chunk per virtual stage this device runs (one without interleaving); data
@@ -323,13 +324,13 @@ class GPUHybridRuntime:
                             last=c.stage == plan.num_stages - 1, tp=self.tp, micro_batch=micro_batch, seq_len=self.S,
                             seed=seed, rep_shard=rep_sync.shard, shd_shard=shd_sync.shard,
                             rep_factories=rep_sync.factories, shd_factories=shd_sync.factories, init=init,
-                            fp8=fp8)
+                            fp8=fp8, sp=self.sp)
             rep_sync.attach(stage.rep)
             shd_sync.attach(stage.shd)
             self.chunks[c.stage] = (stage, rep_sync, shd_sync)
         self.tokens = tokens or TokenSource(cfg.vocab_size, micro_batch, self.S)
         self.executor = GPUStageExecutor({s_: ch[0] for s_, ch in self.chunks.items()}, plan, g.replica, comms.rank,
-                                         self.tokens, grad_scale=1.0 / self.tokens_per_step)
+                                         self.tokens, grad_scale=1.0 / self.tokens_per_step, sp=self.sp)
         stream = schedule[(g.replica, g.stage)]
         self.executor.split_backward = any(ins.op == Op.W for ins in stream)
         p2p = P2PEngine(comms.rank, mgr, channels=channel_map(comms), device=str(self.device))
@@ -397,16 +398,27 @@ class GPUHybridRuntime:
             st.f8.pending.copy_(self._amax[st.layer_ids])
             st.f8.finish_iteration()
 
+    def after_backward(self, iteration: int) -> None:
+        """Between the last backward of an iteration and the gradient reduction: the replicated
+        set's gradient share under plain TP, the fp8 amax reduction and history update, the
+        ``loss`` hook."""
+        if not self.sp:
+            # plain TP: every rank of a replica computed the replicated parameters' full gradient;
+            # the replicated set is reduced over all ranks of the stage, so each counts 1 / tp
+            for stage, _, _ in self.chunks.values():
+                stage.rep.grad.mul_(1.0 / self.group.tp)
+        if self.fp8 is not None:
+            self._finish_fp8()
+        if self.hook is not None:  # after the loss and the amax reduction, before the gradient reduction
+            self.hook(iteration, "loss")
+
     def run_iteration(self, iteration: int | None = None, step: bool = True) -> torch.Tensor:
         """One training step of this slot; returns the global mean token loss as a 0-d device
         tensor (no host synchronisation).  ``step=False`` stops after the gradient reduction
         (the resilient loop applies the optimizer step once the iteration is REDUCED)."""
         it = self.iteration if iteration is None else iteration
         self.interp.run(it)
-        if self.fp8 is not None:
-            self._finish_fp8()
-        if self.hook is not None:  # after the loss and the amax reduction, before the gradient reduction
-            self.hook(it, "loss")
+        self.after_backward(it)
         for sync in self._syncs():
             sync.reduce()
         if step:

@@ -34,7 +34,7 @@ def ensure_process_group(device: torch.device) -> None:
 
 
 def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatches: int, micro_batch: int,
-                   seq_len: int):
+                   seq_len: int, sequence_parallel: bool = True):
     """The joint planner for a ``tp x pp x dp`` layout of ``cfg`` on one node, and the node's
     topology (device ids ``n0g{i}``)."""
     from ..plan.model_spec import ModelProfile, ModelSpec
@@ -44,7 +44,7 @@ def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatche
     spec = ModelSpec(num_layers=cfg.layers, hidden=cfg.hidden, ffn=cfg.ffn, num_heads=cfg.heads,
                      num_kv_heads=cfg.kv_heads, vocab=cfg.vocab_size, seq_len=seq_len, micro_batch_size=micro_batch)
     pc = PlannerConfig(model=spec, profile=ModelProfile.b200(spec), num_stages=pp, num_replicas=dp, tp=tp,
-                       num_microbatches=num_microbatches, sequence_parallel=True, mem_capacity=math.inf)
+                       num_microbatches=num_microbatches, sequence_parallel=sequence_parallel, mem_capacity=math.inf)
     return HeteroPlanner(pc), ClusterTopology.uniform(1, tp * pp * dp)
 
 
@@ -52,11 +52,13 @@ class GPUHybridTrainer:
     def __init__(self, cfg: GPTConfig, *, tp: int, pp: int, dp: int, global_batch: int, micro_batch: int = 1,
                  seq_len: int | None = None, tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, device=None,
-                 data_seed: int = 1, migrate: str = "p2p", fp8=None):
+                 data_seed: int = 1, migrate: str = "p2p", fp8=None, sequence_parallel: bool = True):
         """``migrate``: how a reconfiguration moves state on GPUs -- ``"p2p"`` (one strided peer
         copy launch per rank over NVLink, ``parallel.migration``) or ``"nccl"`` (one send/receive
         per slice and kind, ``state.transfer_engine``).  ``fp8``: an ``Fp8Recipe`` (block-scaled
-        fp8 projections; the per-layer amax histories migrate and checkpoint with their layers)."""
+        fp8 projections; the per-layer amax histories migrate and checkpoint with their layers).
+        ``sequence_parallel=False``: plain tensor parallelism (replicated token rows, GEMM ->
+        all-reduce)."""
         from ..comm.comm_manager import ResilientCommManager
         from ..runtime.gpu_executor import TokenSource
         from ..runtime.gpu_runtime import GPUHybridRuntime
@@ -75,8 +77,10 @@ class GPUHybridTrainer:
         self.device = torch.device(device if device is not None else f"cuda:{torch.cuda.current_device()}")
         self.micro_batch = micro_batch
         n_micro = global_batch // micro_batch
+        self.sequence_parallel = sequence_parallel
         self.planner, self.topology = layout_planner(cfg, tp=tp, pp=pp, dp=dp, num_microbatches=n_micro,
-                                                     micro_batch=micro_batch, seq_len=self.S)
+                                                     micro_batch=micro_batch, seq_len=self.S,
+                                                     sequence_parallel=sequence_parallel)
         self.plan = self.planner.initial_plan(self.topology)
         self.schedule, _ = self.planner.schedule(self.plan, self.topology)
         ids = list(self.plan.world)
@@ -91,7 +95,8 @@ class GPUHybridTrainer:
                                         **self.opts)
         self.tokens_per_step = self.runtime.tokens_per_step
         self.global_batch = global_batch
-        self.layout = f"tp{tp}pp{pp}dp{dp}-sp-{tp_impl}tp-{dp_impl}dp" + ("-fp8" if fp8 is not None else "")
+        self.layout = (f"tp{tp}pp{pp}dp{dp}-{'sp' if sequence_parallel else 'nosp'}-{tp_impl}tp-{dp_impl}dp"
+                       + ("-fp8" if fp8 is not None else ""))
         self.last_reconfig: dict | None = None
 
     def tensor_specs(self):
@@ -238,7 +243,8 @@ class GPUHybridTrainer:
         step, iteration = rt.step_count, rt.iteration
         mark("export")
         planner, topo = layout_planner(self.cfg, tp=tp, pp=pp, dp=dp, num_microbatches=old_plan.num_microbatches,
-                                       micro_batch=self.micro_batch, seq_len=self.S)
+                                       micro_batch=self.micro_batch, seq_len=self.S,
+                                       sequence_parallel=self.sequence_parallel)
         new_plan = dataclasses.replace(planner.initial_plan(topo), generation=old_plan.generation + 1)
         if list(new_plan.world) != world:
             raise RuntimeError("the new layout names other devices than the current world")

@@ -27,10 +27,11 @@ def _plan(layout, ids):
                   StageGroup(1, 0, ids[4:6], (0, 2)), StageGroup(1, 1, ids[6:8], (2, 4)))
         plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)), sequence_parallel=True)
         plan = interleave(plan, 2)
-    elif layout in ("tp2pp2dp2", "zb"):
+    elif layout in ("tp2pp2dp2", "zb", "nosp"):
         groups = (StageGroup(0, 0, ids[0:2], (0, 2)), StageGroup(0, 1, ids[2:4], (2, 4)),
                   StageGroup(1, 0, ids[4:6], (0, 2)), StageGroup(1, 1, ids[6:8], (2, 4)))
-        plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)), sequence_parallel=True)
+        plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, MICRO, ((0, 0, 1, 1), (0, 0, 1, 1)),
+                                  sequence_parallel=layout != "nosp")
     else:
         groups = (StageGroup(0, 0, ids[0:1], (0, 4)),)
         plan = HeteroParallelPlan(1, ids, 4, 1, 1, groups, MICRO, ((0, 0, 0, 0),), sequence_parallel=True)
@@ -64,6 +65,7 @@ def _worker(rank, world, port, store_addr, layout, iters):
                           tp_impl="collective", dp_impl="collective", lr=1e-2)
     # iteration 0's gradients before any update, reduced over each set's data-parallel group
     rt.interp.run(0)
+    rt.after_backward(0)
     grads = {}
     for P, sync in rt.param_sets():
         total = P.grad.clone()
@@ -93,9 +95,10 @@ def _assemble(results):
     return full
 
 
-@pytest.mark.parametrize("layout", ["tp2pp2dp2", "zb", "vpp"])
+@pytest.mark.parametrize("layout", ["tp2pp2dp2", "zb", "vpp", "nosp"])
 def test_tp2_pp2_dp2_sequence_parallel_matches_single_rank(store, layout):
-    """1F1B, zero-bubble (B/W split) and interleaved (two chunks per device) schedules."""
+    """1F1B, zero-bubble (B/W split) and interleaved (two chunks per device) schedules, and plain
+    tensor parallelism without sequence parallelism (replicated rows, GEMM -> all-reduce)."""
     one = spawn(_worker, 1, store, "single", 2, timeout=240)
     many = spawn(_worker, 8, store, layout, 2, timeout=300)
     ref, got = _assemble(one), _assemble(many)
