@@ -128,6 +128,24 @@ class Fp8Linears:
         out = self._buf(R, C, self.recipe.fwd_fmt, False, True, False, "x")
         return fp8.quantize(x, self.recipe.fwd_fmt, rowwise=True, amax=self.amax(layer, lin, "x"), out=out)
 
+    def norm_quant_x(self, layer: int, lin: str, x: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                     rstd: torch.Tensor, out: fp8.Fp8Tensor | None = None) -> fp8.Fp8Tensor:
+        """Forward input that is an RMSNorm output: normalised and quantised in one kernel
+        (``rstd`` saved for the backward; amax recorded)."""
+        R, C = x.shape
+        if out is None:
+            out = self._buf(R, C, self.recipe.fwd_fmt, False, True, False, "x")
+        return fp8.rmsnorm_quantize(x, norm_w, eps, self.recipe.fwd_fmt, out=out, rstd=rstd,
+                                    amax=self.amax(layer, lin, "x"))
+
+    def act_quant_x(self, layer: int, lin: str, gu: torch.Tensor, gated: bool) -> fp8.Fp8Tensor:
+        """Forward input that is the MLP activation of ``gu``: activation and quantisation in one
+        kernel (amax recorded)."""
+        T = gu.shape[0]
+        F = gu.shape[1] // (2 if gated else 1)
+        out = self._buf(T, F, self.recipe.fwd_fmt, False, True, False, "x")
+        return fp8.act_quantize(gu, gated, self.recipe.fwd_fmt, out=out, amax=self.amax(layer, lin, "x"))
+
     def quant_x_cols(self, x: torch.Tensor) -> fp8.Fp8Tensor:
         """Weight-gradient input: blocks along the token dimension (transposed layout)."""
         R, C = x.shape

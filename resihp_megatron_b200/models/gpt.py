@@ -200,17 +200,22 @@ class LlamaModel:
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = self.xs[i]
-            h, r1 = self._rmsnorm(x, P.w(p + "attn_norm"), self.ws_h, self.rstd1[i])
-            self._linear(l, "qkv", h, P.w(p + "wqkv"), self.qkv[i])
+            self._norm_linear(l, "qkv", x, P.w(p + "attn_norm"), self.rstd1[i], P.w(p + "wqkv"), self.qkv[i])
             q, k, v = self._views(i)
             ops.rope_(q, cfg.heads, cfg.head_dim, self.cos, self.sin, self.S)
             ops.rope_(k, cfg.kv_heads, cfg.head_dim, self.cos, self.sin, self.S)
             self._attention_fwd(i, q, k, v)
             self._linear(l, "o", self.o[i], P.w(p + "wo"), self.x2[i], residual=x)
-            h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])
-            self._linear(l, "fc1", h2, P.w(p + self.fc1), self.gu[i])
-            mlp_act_fwd(cfg, self.gu[i], self.ws_a)
-            self._linear(l, "fc2", self.ws_a, P.w(p + "w2"), self.xs[i + 1], residual=self.x2[i])
+            self._norm_linear(l, "fc1", self.x2[i], P.w(p + "mlp_norm"), self.rstd2[i], P.w(p + self.fc1),
+                              self.gu[i])
+            if self.f8 is not None:  # activation written as the fp8 operand directly
+                from ..ops import fp8
+
+                aq = self.f8.act_quant_x(l, "fc2", self.gu[i], cfg.gated)
+                fp8.gemm(aq.rowwise(), self.f8.weight(l, "fc2").rowwise(), out=self.xs[i + 1], residual=self.x2[i])
+            else:
+                mlp_act_fwd(cfg, self.gu[i], self.ws_a)
+                self._linear(l, "fc2", self.ws_a, P.w(p + "w2"), self.xs[i + 1], residual=self.x2[i])
         return self.xs[-1]
 
     # ------------------------------------------------------------------ linear layers (bf16 or fp8)
@@ -223,6 +228,16 @@ class LlamaModel:
             for lin, name in (("qkv", "wqkv"), ("o", "wo"), ("fc1", self.fc1), ("fc2", "w2")):
                 ws[(l, lin)] = P.w(p + name)
         self.f8.refresh_weights(ws, P.step)
+
+    def _norm_linear(self, layer, lin, x, norm_w, rstd, w, out):
+        """``rmsnorm(x) @ w^T``; fp8: the norm writes the quantised operand directly."""
+        if self.f8 is not None:
+            from ..ops import fp8
+
+            xq = self.f8.norm_quant_x(layer, lin, x, norm_w, float(self.cfg.norm_eps), rstd)
+            return fp8.gemm(xq.rowwise(), self.f8.weight(layer, lin).rowwise(), out=out)
+        h, _ = self._rmsnorm(x, norm_w, self.ws_h, rstd)
+        return ops.gemm(h, w, out=out)
 
     def _linear(self, layer, lin, x, w, out, residual=None):
         if self.f8 is not None:

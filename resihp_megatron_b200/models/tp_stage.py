@@ -20,8 +20,8 @@ inputs of the column-parallel weight gradients are recomputed and re-gathered.
 
 With the GPT MLP (``cfg.mlp == "gelu"``) the input projection is ``w1`` alone and
 ``a = gelu(AllGather(h2) W1_r^T)``.  With an ``Fp8Recipe`` (``fp8=``) the four projections run as
-block-scaled fp8 GEMMs (``models.fp8_linear``): for the column-parallel ones each rank quantises
-its own rows and the gather moves fp8 rows with their scales (half the bytes of bf16), the
+block-scaled fp8 GEMMs (``models.fp8_linear``): for the column-parallel ones each rank's RMSNorm
+writes its rows as fp8 and the gather moves fp8 rows with their scales (half the bytes of bf16), the
 row-parallel ones store their partial products straight
 into the owners' receive slots from the fp8 GEMM's epilogue (``tp.gemm_rs_with``), and every
 rank records the amax of its operands for the per-layer history.
@@ -172,7 +172,6 @@ class TPStage:
             from .fp8_linear import Fp8Linears
 
             self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
-            self.ws_hl = torch.empty(self.Tl, cfg.hidden, dtype=torch.bfloat16, device=self.device)
 
     # ------------------------------------------------------------------ parameter views
     def _check_adjacent(self, p: str, names) -> None:
@@ -205,37 +204,37 @@ class TPStage:
         self.f8.refresh_weights(ws, self.shd.step)
 
     # ------------------------------------------------------------------ projections (bf16 or fp8)
-    def _col_in(self) -> torch.Tensor:
-        """Where the normalised rows of this rank go before a column-parallel projection: the
-        gather buffer's chunk (bf16), or a workspace that the fp8 path quantises from."""
-        return self.tp.chunk(self.T, self.cfg.hidden) if self.f8 is None else self.ws_hl
-
-    def _col_fwd(self, l: int, lin: str, w: torch.Tensor, out: torch.Tensor) -> None:
-        """Column-parallel projection of the gathered rows (the caller wrote this rank's rows into
-        ``_col_in()``).  fp8: this rank quantises its own rows (row-major 1 x 128 scales) straight
-        into the gather buffer, the gather moves fp8 rows and their scales, the GEMM reads them."""
+    def _norm_col_fwd(self, l: int, lin: str, x: torch.Tensor, norm_w: torch.Tensor, rstd: torch.Tensor,
+                      w: torch.Tensor, out: torch.Tensor) -> None:
+        """``AllGather(rmsnorm(x)) @ w^T`` for this rank's rows ``x``: bf16 -- the norm writes the
+        gather buffer's chunk and the fused all-gather -> GEMM runs; fp8 -- the norm writes this
+        rank's rows as fp8 (row-major 1 x 128 scales) straight into the gather buffer, the gather
+        moves fp8 rows and their scales, the fp8 GEMM reads them."""
         T, H = self.T, self.cfg.hidden
         if self.f8 is None:
+            self._rms(x, norm_w, self.tp.chunk(T, H), rstd)
             self.tp.ag_gemm(T, w, out=out)
             return
         fmt = self.f8.recipe.fwd_fmt
         dt = fp8_ops.DTYPES[fmt]
         q, sc = self.tp.fp8_local(T, H)
         local = fp8_ops.Fp8Tensor(self.Tl, H, fmt, False, q.view(dt), sc, None, None, True)
-        fp8_ops.quantize(self.ws_hl, fmt, rowwise=True, amax=self.f8.amax(l, lin, "x"), out=local)
+        self.f8.norm_quant_x(l, lin, x, norm_w, float(self.cfg.norm_eps), rstd, out=local)
         qf, sf = self.tp.all_gather_fp8(T, H)
         xq = fp8_ops.Fp8Operand(qf.view(dt), sf, 1, H // fp8_ops.BLOCK, 0, fmt)
         fp8_ops.gemm(xq, self.f8.weight(l, lin).rowwise(), out=out)
 
-    def _row_fwd(self, l: int, lin: str, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
-                 residual: torch.Tensor) -> None:
-        """Row-parallel projection, reduce-scattered to the row shards, plus the residual."""
+    def _row_fwd(self, l: int, lin: str, x: torch.Tensor | None, w: torch.Tensor, out: torch.Tensor,
+                 residual: torch.Tensor, xq=None) -> None:
+        """Row-parallel projection, reduce-scattered to the row shards, plus the residual (fp8:
+        ``xq`` is the already quantised input when given)."""
         if self.f8 is None:
             self.tp.gemm_rs(x, w, out=out, residual=residual)
             return
-        xq = self.f8.quant_x(l, lin, x)
+        if xq is None:
+            xq = self.f8.quant_x(l, lin, x)
         wq = self.f8.weight(l, lin)
-        self.tp.gemm_rs_with(x.shape[0], w.shape[0], lambda **kw: fp8_ops.gemm(xq.rowwise(), wq.rowwise(), **kw),
+        self.tp.gemm_rs_with(xq.R, w.shape[0], lambda **kw: fp8_ops.gemm(xq.rowwise(), wq.rowwise(), **kw),
                              out=out, residual=residual)
 
     def _row_bwd(self, w_list, l: int, lin: str, w: torch.Tensor, x: torch.Tensor, dx_out: torch.Tensor,
@@ -319,18 +318,20 @@ class TPStage:
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = slot.x[i]
-            self._rms(x, R.w(p + "attn_norm"), self._col_in(), slot.rstd1[i])
-            self._col_fwd(l, "qkv", self.wqkv(p), slot.qkv[i])
+            self._norm_col_fwd(l, "qkv", x, R.w(p + "attn_norm"), slot.rstd1[i], self.wqkv(p), slot.qkv[i])
             q, k, v = self._qkv_views(slot.qkv[i])
             ops.rope_(q, self.nq, D, self.cos, self.sin, self.S)
             ops.rope_(k, self.nk, D, self.cos, self.sin, self.S)
             ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.nq, kv_heads=self.nk, head_dim=D,
                               out=slot.o[i], lse=slot.lse[i])
             self._row_fwd(l, "o", slot.o[i], P.w(p + "wo"), slot.x2[i], x)
-            self._rms(slot.x2[i], R.w(p + "mlp_norm"), self._col_in(), slot.rstd2[i])
-            self._col_fwd(l, "fc1", self.w13(p), slot.gu[i])
-            mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
-            self._row_fwd(l, "fc2", self.ws_a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])
+            self._norm_col_fwd(l, "fc1", slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.w13(p), slot.gu[i])
+            if self.f8 is not None:  # the activation is written as the fp8 operand directly
+                aq = self.f8.act_quant_x(l, "fc2", slot.gu[i], cfg.gated)
+                self._row_fwd(l, "fc2", None, P.w(p + "w2"), slot.x[i + 1], slot.x2[i], xq=aq)
+            else:
+                mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
+                self._row_fwd(l, "fc2", self.ws_a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])
         if not self.last:
             return slot.x[-1]
         self._rms(slot.x[-1], R.w("final_norm"), slot.hf, slot.rstd_f)

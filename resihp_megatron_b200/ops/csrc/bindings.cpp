@@ -602,6 +602,37 @@ static float* opt_f32(const c10::optional<torch::Tensor>& t, const char* name) {
   return t->data_ptr<float>();
 }
 
+// RMSNorm of x [T, H] written as fp8 q [T, H] with 1x128 row-block scales s (addressing s_kb, s_row).
+void rmsnorm_fp8(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& rstd, double eps,
+                 int64_t fmt, const torch::Tensor& q, const torch::Tensor& s, int64_t s_kb, int64_t s_row,
+                 const c10::optional<torch::Tensor>& amax) {
+  CHECK_BF16(x); CHECK_BF16(w); CHECK_F32(s);
+  check_fp8(q, "q");
+  const int H = x.size(-1);
+  const int T = x.numel() / H;
+  TORCH_CHECK(q.size(0) == T && q.size(1) == H, "rmsnorm_fp8: q must be [T, H]");
+  TORCH_CHECK(w.numel() == H, "rmsnorm_fp8: w must be [H]");
+  TORCH_CHECK(T == 0 || (H / 128 - 1) * s_kb + static_cast<long long>(T - 1) * s_row < s.numel(), "rmsnorm_fp8: scales");
+  if (rstd.has_value()) TORCH_CHECK(rstd->numel() == T, "rmsnorm_fp8: rstd must be [T]");
+  const c10::cuda::CUDAGuard g(x.device());
+  RB_CALL(rb::rmsnorm_fp8(x.data_ptr(), w.data_ptr(), opt_f32(rstd, "rstd"), T, H, static_cast<float>(eps),
+                          static_cast<int>(fmt), q.data_ptr(), s.data_ptr<float>(), s_kb, s_row,
+                          reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream()), "rmsnorm_fp8");
+}
+
+// MLP activation of `in` ([T, F] GELU or [T, 2F] SwiGLU) written as fp8 q [T, F] with 1x128 row-block scales.
+void act_fp8(const torch::Tensor& in, bool gated, int64_t fmt, const torch::Tensor& q, const torch::Tensor& s,
+             int64_t s_kb, int64_t s_row, const c10::optional<torch::Tensor>& amax) {
+  CHECK_BF16(in); CHECK_F32(s);
+  check_fp8(q, "q");
+  const int T = q.size(0), F = q.size(1);
+  TORCH_CHECK(in.numel() == static_cast<long long>(T) * F * (gated ? 2 : 1), "act_fp8: input / output sizes");
+  TORCH_CHECK(T == 0 || (F / 128 - 1) * s_kb + static_cast<long long>(T - 1) * s_row < s.numel(), "act_fp8: scales");
+  const c10::cuda::CUDAGuard g(in.device());
+  RB_CALL(rb::act_fp8(in.data_ptr(), gated ? 1 : 0, T, F, static_cast<int>(fmt), q.data_ptr(), s.data_ptr<float>(),
+                      s_kb, s_row, reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream()), "act_fp8");
+}
+
 // Quantise bf16 x [R, C]; outputs are optional (rowwise q [R, C], colwise q [C, R]).
 void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::optional<torch::Tensor>& q_row,
                   const c10::optional<torch::Tensor>& s_row, const c10::optional<torch::Tensor>& q_col,
@@ -702,6 +733,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
         py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"),
         py::arg("row_major") = false);
+  m.def("act_fp8", &act_fp8, "MLP activation written as block-scaled fp8", py::arg("input"), py::arg("gated"),
+        py::arg("fmt"), py::arg("q"), py::arg("s"), py::arg("s_kb"), py::arg("s_row"), py::arg("amax"));
+  m.def("rmsnorm_fp8", &rmsnorm_fp8, "RMSNorm written as block-scaled fp8", py::arg("x"), py::arg("w"),
+        py::arg("rstd"), py::arg("eps"), py::arg("fmt"), py::arg("q"), py::arg("s"), py::arg("s_kb"), py::arg("s_row"),
+        py::arg("amax"));
   m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM", py::arg("a"), py::arg("a_fmt"), py::arg("sa"),
         py::arg("sa_kb"), py::arg("sa_row"), py::arg("sa_shift"), py::arg("b"), py::arg("b_fmt"), py::arg("sb"),
         py::arg("sb_kb"), py::arg("sb_row"), py::arg("sb_shift"), py::arg("out"), py::arg("epi"), py::arg("alpha"),

@@ -9,6 +9,7 @@
 
 #include <cstdint>
 
+#include "fp8_common.cuh"
 #include "sm100.cuh"
 
 namespace rb {
@@ -87,6 +88,77 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bf
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * r * wv[j];
       store_bf16x8(y + row * H + c * 8, o);
     }
+  }
+}
+
+// RMSNorm straight to block-scaled fp8 (the fp8 projections' input): the same arithmetic as
+// rmsnorm_fwd_kernel up to the bf16 output, then each 1 x 128 block of the bf16 row is quantised
+// exactly as fp8_quantize would (power-of-two scale from the block's amax, round to nearest even).
+// The 16 threads holding one block (16 x 8 consecutive features) reduce its amax with shuffles.
+// Scale of block cb of this row: s[cb * s_kb + row * s_row].  One atomicMax per row on `amax`.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fp8_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   float* __restrict__ rstd, int H, float eps,
+                                                                   int fmt, uint8_t* __restrict__ q, float* s,
+                                                                   long long s_kb, long long s_row,
+                                                                   unsigned int* amax) {
+  __shared__ float sh[32];
+  __shared__ uint32_t wmax[kNormThreads / 32];
+  const long long row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * H;
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+  const int nvec = H / 8;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (threadIdx.x + i * kNormThreads);
+    if (c < nvec) {
+      load_bf16x8(xr + c * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = block_sum<kNormThreads>(ss, sh);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0 && rstd != nullptr) rstd[row] = r;
+  const int F = fp8_max_exp(fmt);
+  uint32_t rmax = 0;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (threadIdx.x + i * kNormThreads);
+    const bool on = c < nvec;  // H % 128 == 0: a block's 16 threads are all on or all off
+    float o[8];
+    uint32_t m = 0;
+    if (on) {
+      float wv[8];
+      load_bf16x8(w + c * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o[j] = __bfloat162float(__float2bfloat16_rn(v[i][j] * r * wv[j]));
+        m = max(m, __float_as_uint(o[j]) & 0x7fffffffu);
+      }
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    rmax = max(rmax, m);
+    if (on) {
+      const int e = fp8_scale_exp(m, F);
+      const float inv = exp2_int(-e);
+      uint2 u;
+      u.x = cvt4_fp8(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv, fmt);
+      u.y = cvt4_fp8(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv, fmt);
+      *reinterpret_cast<uint2*>(q + row * H + c * 8) = u;
+      if ((threadIdx.x & 15) == 0) s[static_cast<long long>(c / 16) * s_kb + row * s_row] = exp2_int(e);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) rmax = max(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = rmax;
+  __syncthreads();
+  if (threadIdx.x == 0 && amax != nullptr) {
+    uint32_t m = 0;
+    for (int k = 0; k < kNormThreads / 32; ++k) m = max(m, wmax[k]);
+    atomicMax(amax, m);
   }
 }
 
@@ -285,6 +357,65 @@ __global__ void amax_history_push_kernel(float* __restrict__ hist, float* __rest
   pending[i] = 0.f;
 }
 
+// The MLP activation written straight as block-scaled fp8 (the fc2 input): GELU of h [T, F]
+// (GATED = false) or silu(gate) * up of gu [T, 2F] (GATED = true), rounded to bf16 exactly as
+// gelu_fwd_kernel / swiglu_fwd_kernel round it, then each 1 x 128 block of a row quantised as
+// fp8_quantize would.  Thread i covers features [8 i, 8 i + 8) of the flattened [T, F] output,
+// so the 16 consecutive threads of a block (F % 128 == 0) reduce its amax with shuffles.  Scale
+// of block cb of row t: s[cb * s_kb + t * s_row].  One atomicMax per CTA on `amax`.
+template <bool GATED>
+__global__ void __launch_bounds__(256) act_fp8_kernel(const __nv_bfloat16* __restrict__ in, int T, int F, int fmt,
+                                                      uint8_t* __restrict__ q, float* __restrict__ s, long long s_kb,
+                                                      long long s_row, unsigned int* amax) {
+  __shared__ uint32_t wmax[8];
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nv = F / 8;
+  const bool on = i < static_cast<long long>(T) * nv;  // whole 16-thread groups (T * nv % 16 == 0)
+  const long long t = on ? i / nv : 0;
+  const int c = on ? static_cast<int>(i % nv) : 0;
+  float o[8];
+  uint32_t m = 0;
+  if (on) {
+    if (GATED) {
+      float g[8], u[8];
+      load_bf16x8(in + t * 2 * F + c * 8, g);
+      load_bf16x8(in + t * 2 * F + F + c * 8, u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __bfloat162float(__float2bfloat16_rn(silu(g[j]) * u[j]));
+    } else {
+      float x[8];
+      load_bf16x8(in + t * F + c * 8, x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = __bfloat162float(
+            __float2bfloat16_rn(0.5f * x[j] * (1.f + tanhf(kGeluC * (x[j] + kGeluA * x[j] * x[j] * x[j])))));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = max(m, __float_as_uint(o[j]) & 0x7fffffffu);
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (on) {
+    const int e = fp8_scale_exp(m, fp8_max_exp(fmt));
+    const float inv = exp2_int(-e);
+    uint2 u;
+    u.x = cvt4_fp8(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv, fmt);
+    u.y = cvt4_fp8(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv, fmt);
+    *reinterpret_cast<uint2*>(q + t * F + c * 8) = u;
+    if ((threadIdx.x & 15) == 0) s[static_cast<long long>(c / 16) * s_kb + t * s_row] = exp2_int(e);
+  }
+  uint32_t bm = m;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) bm = max(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = bm;
+  __syncthreads();
+  if (threadIdx.x == 0 && amax != nullptr) {
+    uint32_t mm = 0;
+    for (int k = 0; k < 8; ++k) mm = max(mm, wmax[k]);
+    atomicMax(amax, mm);
+  }
+}
+
 // x[t, :] = E[ids[t], :]
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ E,
                                      __nv_bfloat16* __restrict__ x, int T, int H, int V, int* err) {
@@ -412,6 +543,32 @@ int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H
   rmsnorm_fwd_kernel<<<T, kNormThreads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x),
                                                 reinterpret_cast<const __nv_bfloat16*>(w),
                                                 reinterpret_cast<__nv_bfloat16*>(y), rstd, H, eps);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int rmsnorm_fp8(const void* x, const void* w, float* rstd, int T, int H, float eps, int fmt, void* q, float* s,
+                long long s_kb, long long s_row, unsigned int* amax, cudaStream_t st) {
+  if (H % 128 || H > kNormThreads * kNormMaxVec * 8 || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -1;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7) || s == nullptr) return -2;
+  if (T == 0) return 0;
+  rmsnorm_fp8_kernel<<<T, kNormThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
+                                                 reinterpret_cast<const __nv_bfloat16*>(w), rstd, H, eps, fmt,
+                                                 static_cast<uint8_t*>(q), s, s_kb, s_row, amax);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int act_fp8(const void* in, int gated, int T, int F, int fmt, void* q, float* s, long long s_kb, long long s_row,
+            unsigned int* amax, cudaStream_t st) {
+  if (F % 128 || T < 0 || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -1;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(q) & 7) || s == nullptr) return -2;
+  if (T == 0) return 0;
+  const long long n = static_cast<long long>(T) * (F / 8);
+  if (gated)
+    act_fp8_kernel<true><<<cdiv_ll(n, 256), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(in), T, F, fmt,
+                                                            static_cast<uint8_t*>(q), s, s_kb, s_row, amax);
+  else
+    act_fp8_kernel<false><<<cdiv_ll(n, 256), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(in), T, F, fmt,
+                                                             static_cast<uint8_t*>(q), s, s_kb, s_row, amax);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -37,33 +37,16 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include "fp8_common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
 
 namespace rb {
 namespace {
 
-constexpr int kFp8E4M3 = 0;
-constexpr int kFp8E5M2 = 1;
 enum : int { kF8EpiBF16 = 0, kF8EpiF32 = 1, kF8EpiF32Acc = 2, kF8EpiBF16Res = 3, kF8EpiScatter = 4 };
 constexpr int kF8MaxTP = 8;
 
-// Largest finite value of the format = 1.75 * 2^F.
-__host__ __device__ constexpr int fp8_max_exp(int fmt) { return fmt == kFp8E4M3 ? 8 : 15; }
-
-// Exponent e of the power-of-two scale: the smallest e with amax * 2^-e <= 1.75 * 2^F, clamped
-// to [-126, 126] so that 2^e and 2^-e are normal floats.  `amax_bits` is the bit pattern of a
-// non-negative float; zero, inf and NaN blocks get e = 0.
-__device__ __forceinline__ int fp8_scale_exp(uint32_t amax_bits, int F) {
-  const int E = static_cast<int>(amax_bits >> 23);
-  if (amax_bits == 0 || E == 255) return 0;
-  const uint32_t mant = amax_bits & 0x7fffffu;
-  int e = (E - 127) - F + (mant > 0x600000u ? 1 : 0);  // 1.75 = 1 + 0x600000 / 2^23
-  e = e < -126 ? -126 : (e > 126 ? 126 : e);
-  return e;
-}
-
-__device__ __forceinline__ float exp2_int(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
 
 // |x| of a bf16 as the bit pattern of an fp32 (an unsigned compare orders magnitudes).
 __device__ __forceinline__ uint32_t abs_bits_bf16(uint16_t h) { return static_cast<uint32_t>(h & 0x7fffu) << 16; }
@@ -74,12 +57,6 @@ __device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t cvt4_fp8(float a, float b, float c, float d, int fmt) {
-  const __nv_fp8_interpretation_t kind = fmt == kFp8E4M3 ? __NV_E4M3 : __NV_E5M2;
-  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, kind);
-  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, kind);
-  return (lo & 0xffffu) | (hi << 16);
-}
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
 

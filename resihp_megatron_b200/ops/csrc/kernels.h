@@ -16,6 +16,14 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
 
 int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s);
 int rmsnorm_bwd_blocks(int T);
+// RMSNorm whose output is written as block-scaled fp8 (1 x 128 row blocks; scale of block cb of
+// row t at s[cb * s_kb + t * s_row]); bit-identical to rmsnorm_fwd followed by fp8_quantize.
+// MLP activation (GELU of [T, F], or SwiGLU of [T, 2F]) written as block-scaled fp8 [T, F]; bit-identical
+// to gelu_fwd / swiglu_fwd followed by fp8_quantize.
+int act_fp8(const void* in, int gated, int T, int F, int fmt, void* q, float* s, long long s_kb, long long s_row,
+            unsigned int* amax, cudaStream_t st);
+int rmsnorm_fp8(const void* x, const void* w, float* rstd, int T, int H, float eps, int fmt, void* q, float* s,
+                long long s_kb, long long s_row, unsigned int* amax, cudaStream_t st);
 int rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres, void* dx,
                 float* dw, int accumulate, float* part, int T, int H, cudaStream_t s);
 int rope_apply(void* q, long long row_stride, int heads, int D, const float* cos_t, const float* sin_t, int S,

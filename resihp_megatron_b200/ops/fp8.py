@@ -147,6 +147,31 @@ def quantize(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = False, row
     return out
 
 
+def rmsnorm_quantize(x: torch.Tensor, w: torch.Tensor, eps: float, fmt: int | str = E4M3, *, out: Fp8Tensor,
+                     rstd: torch.Tensor | None = None, amax: torch.Tensor | None = None) -> Fp8Tensor:
+    """``quantize(rmsnorm(x) * w)`` in one pass (rowwise 1 x 128 blocks into ``out``, whose scale
+    layout -- K-block or row major -- is kept); ``rstd`` receives the per-row ``1 / rms``.
+    Bit-identical to ``ops.rmsnorm_fwd`` followed by ``quantize``."""
+    fmt = fmt_of(fmt)
+    op = out.rowwise()
+    ext().rmsnorm_fp8(x, w, rstd, float(eps), fmt, out.q_row.view(torch.uint8), out.s_row, op.kb_stride,
+                      op.row_stride, amax)
+    count(1)
+    return out
+
+
+def act_quantize(x: torch.Tensor, gated: bool, fmt: int | str = E4M3, *, out: Fp8Tensor,
+                 amax: torch.Tensor | None = None) -> Fp8Tensor:
+    """The MLP activation -- ``gelu(x)`` of ``[T, F]`` or ``silu(gate) * up`` of ``[T, 2F]``
+    (``gated``) -- quantised rowwise into ``out`` (``[T, F]``) in one pass; bit-identical to
+    ``ops.gelu_fwd`` / ``ops.swiglu_fwd`` followed by ``quantize``."""
+    fmt = fmt_of(fmt)
+    op = out.rowwise()
+    ext().act_fp8(x, bool(gated), fmt, out.q_row.view(torch.uint8), out.s_row, op.kb_stride, op.row_stride, amax)
+    count(1)
+    return out
+
+
 def amax_history_push(history: torch.Tensor, pending: torch.Tensor) -> None:
     """``history [..., len]`` (fp32): shift by one, ``pending`` (same leading shape) into slot 0,
     then zero ``pending`` -- the delayed-scaling update after the amax reduction."""

@@ -120,3 +120,42 @@ def test_gemm_residual_and_scatter_epilogues():
     for q in range(world):
         assert torch.equal(bufs[q][1], full[q * rows:(q + 1) * rows])
         assert bufs[q][0].abs().sum().item() == 0 and bufs[q][2:].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("row_major", [False, True])
+def test_rmsnorm_quantize_equals_norm_then_quantize(row_major):
+    """The fused RMSNorm -> fp8 kernel writes the same bytes, scales, rstd and amax as
+    ``rmsnorm_fwd`` followed by ``quantize`` (partial last row tile too)."""
+    from resihp_megatron_b200 import ops
+
+    T, H = 300, 2048
+    x = _x(T, H, seed=9, spread=1.0)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    y, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
+    a0 = torch.zeros(1, device="cuda")
+    ref = fp8.quantize(y, fp8.E4M3, amax=a0, row_major=row_major)
+    out = fp8.Fp8Tensor.empty(T, H, fp8.E4M3, device="cuda", row_major=row_major)
+    r2 = torch.empty(T, device="cuda")
+    a1 = torch.zeros(1, device="cuda")
+    fp8.rmsnorm_quantize(x, w, 1e-5, fp8.E4M3, out=out, rstd=r2, amax=a1)
+    torch.cuda.synchronize()
+    assert torch.equal(out.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
+    assert torch.equal(out.s_row, ref.s_row) and torch.equal(r2, rstd) and a0.item() == a1.item()
+
+
+@pytest.mark.parametrize("gated", [False, True])
+def test_act_quantize_equals_activation_then_quantize(gated):
+    """GELU / SwiGLU written straight as fp8: same bytes, scales and amax as the bf16 activation
+    kernel followed by ``quantize``."""
+    from resihp_megatron_b200 import ops
+
+    T, F = 257, 1024
+    gu = _x(T, 2 * F if gated else F, seed=11, spread=0.5)
+    y = ops.swiglu_fwd(gu) if gated else ops.gelu_fwd(gu)
+    a0, a1 = torch.zeros(1, device="cuda"), torch.zeros(1, device="cuda")
+    ref = fp8.quantize(y, fp8.E4M3, amax=a0)
+    out = fp8.Fp8Tensor.empty(T, F, fp8.E4M3, device="cuda")
+    fp8.act_quantize(gu, gated, fp8.E4M3, out=out, amax=a1)
+    torch.cuda.synchronize()
+    assert torch.equal(out.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
+    assert torch.equal(out.s_row, ref.s_row) and a0.item() == a1.item()

@@ -209,6 +209,16 @@ def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=Non
     return out
 
 
+def fp8_rmsnorm_quantize(x, w, eps, fmt=0, *, out, rstd=None, amax=None):
+    y, r = rmsnorm_fwd(x, w, eps, rstd=rstd)
+    return fp8_quantize(y, fmt, rowwise=True, amax=amax, out=out)
+
+
+def fp8_act_quantize(x, gated, fmt=0, *, out, amax=None):
+    y = swiglu_fwd(x) if gated else gelu_fwd(x)
+    return fp8_quantize(y, fmt, rowwise=True, amax=amax, out=out)
+
+
 def fp8_gemm(a, b, *, out=None, out_dtype=torch.bfloat16, accumulate=False, alpha=1.0, residual=None, scatter=None):
     from resihp_megatron_b200.ops import fp8
 
@@ -226,7 +236,8 @@ def fp8_amax_history_push(history, pending):
 
 NAMES = ("gemm", "rmsnorm_fwd", "rmsnorm_bwd", "rope_tables", "rope_", "swiglu_fwd", "swiglu_bwd", "embedding_fwd",
          "embedding_bwd", "cross_entropy_", "attention_fwd", "attention_bwd", "adam_step", "gelu_fwd", "gelu_bwd")
-FP8_NAMES = {"quantize": fp8_quantize, "gemm": fp8_gemm, "amax_history_push": fp8_amax_history_push}
+FP8_NAMES = {"quantize": fp8_quantize, "gemm": fp8_gemm, "amax_history_push": fp8_amax_history_push,
+             "rmsnorm_quantize": fp8_rmsnorm_quantize, "act_quantize": fp8_act_quantize}
 
 
 def install(monkeypatch=None) -> None:
