@@ -146,6 +146,15 @@ class Fp8Linears:
         out = self._buf(T, F, self.recipe.fwd_fmt, False, True, False, "x")
         return fp8.act_quantize(gu, gated, self.recipe.fwd_fmt, out=out, amax=self.amax(layer, lin, "x"))
 
+    def act_quant_cols(self, gu: torch.Tensor, gated: bool) -> fp8.Fp8Tensor:
+        """Weight-gradient input that is the MLP activation of ``gu``: recomputed and quantised
+        along tokens in one kernel (the bf16 activation is never written)."""
+        T = gu.shape[0]
+        F = gu.shape[1] // (2 if gated else 1)
+        out = self._buf(T, F, self.recipe.fwd_fmt, False, False, True, "xc")
+        return fp8.quantize(gu, self.recipe.fwd_fmt, rowwise=False, colwise=True, out=out,
+                            act="swiglu" if gated else "gelu")
+
     def quant_x_cols(self, x: torch.Tensor) -> fp8.Fp8Tensor:
         """Weight-gradient input: blocks along the token dimension (transposed layout)."""
         R, C = x.shape

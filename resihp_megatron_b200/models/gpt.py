@@ -283,8 +283,16 @@ class LlamaModel:
             l = self.layer_ids[i]
             p = f"layers.{l}."
             # MLP
-            mlp_act_fwd(cfg, self.gu[i], self.ws_a)
-            self._linear_bwd(l, "fc2", dx, self.ws_a, P.w(p + "w2"), self.ws_da, P.g(p + "w2"))
+            if self.f8 is not None:  # wgrad input: the activation recomputed and quantised in one pass
+                from ..ops import fp8
+
+                dyq = self.f8.quant_dy(l, "fc2", dx)
+                fp8.gemm(dyq.rowwise(), self.f8.weight(l, "fc2").colwise(), out=self.ws_da)
+                aq = self.f8.act_quant_cols(self.gu[i], cfg.gated)
+                fp8.gemm(dyq.colwise(), aq.colwise(), out=P.g(p + "w2"), accumulate=True)
+            else:
+                mlp_act_fwd(cfg, self.gu[i], self.ws_a)
+                self._linear_bwd(l, "fc2", dx, self.ws_a, P.w(p + "w2"), self.ws_da, P.g(p + "w2"))
             mlp_act_bwd(cfg, self.gu[i], self.ws_da, self.gu[i])
             dgu = self.gu[i]
             h2, _ = self._rmsnorm(self.x2[i], P.w(p + "mlp_norm"), self.ws_h, self.rstd2[i])

@@ -237,11 +237,12 @@ class TPStage:
         self.tp.gemm_rs_with(xq.R, w.shape[0], lambda **kw: fp8_ops.gemm(xq.rowwise(), wq.rowwise(), **kw),
                              out=out, residual=residual)
 
-    def _row_bwd(self, w_list, l: int, lin: str, w: torch.Tensor, x: torch.Tensor, dx_out: torch.Tensor,
-                 grad: torch.Tensor) -> None:
+    def _row_bwd(self, w_list, l: int, lin: str, w: torch.Tensor, x: torch.Tensor | None, dx_out: torch.Tensor,
+                 grad: torch.Tensor, xq_cols=None) -> None:
         """Backward of a row-parallel projection: the output gradient rows (written into this
         rank's chunk by the caller) are gathered; dgrad into ``dx_out`` and wgrad (``x`` is the
-        saved / recomputed full-width input) into ``grad``."""
+        saved / recomputed full-width input; fp8 without deferral: ``xq_cols()`` may give it
+        already quantised along tokens) into ``grad``."""
         T, H = self.T, self.cfg.hidden
         if self.f8 is None:
             _, dy = self.tp.ag_gemm(T, w, out=dx_out, w_t=True)
@@ -250,6 +251,9 @@ class TPStage:
         dy = self.tp.all_gather(T, H)
         dyq = self.f8.quant_dy(l, lin, dy)
         fp8_ops.gemm(dyq.rowwise(), self.f8.weight(l, lin).colwise(), out=dx_out)
+        if xq_cols is not None and w_list is None:
+            fp8_ops.gemm(dyq.colwise(), xq_cols().colwise(), out=grad, accumulate=True)
+            return
         self._wgrad_f8(w_list, dyq, dy, x, grad, copy_x=x is self.ws_a)
 
     def _col_bwd(self, w_list, l: int, lin: str, dy: torch.Tensor, w: torch.Tensor, dx_out: torch.Tensor,
@@ -371,8 +375,14 @@ class TPStage:
             p = f"layers.{l}."
             # MLP: the reduce-scatter's gradient is an all-gather feeding w2's dgrad and wgrad
             self.tp.chunk(T, H).copy_(dx)
-            mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
-            self._row_bwd(w, l, "fc2", P.w(p + "w2"), self.ws_a, self.ws_da, P.g(p + "w2"))
+            if self.f8 is not None and w is None:
+                # wgrad input: the activation recomputed and quantised in one pass (gu still holds
+                # the pre-activation: its gradient overwrites it only below)
+                self._row_bwd(w, l, "fc2", P.w(p + "w2"), None, self.ws_da, P.g(p + "w2"),
+                              xq_cols=lambda i=i: self.f8.act_quant_cols(slot.gu[i], cfg.gated))
+            else:
+                mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
+                self._row_bwd(w, l, "fc2", P.w(p + "w2"), self.ws_a, self.ws_da, P.g(p + "w2"))
             dgu = mlp_act_bwd(cfg, slot.gu[i], self.ws_da, slot.gu[i])
 
             def h2_full(i=i, p=p):

@@ -637,10 +637,11 @@ void act_fp8(const torch::Tensor& in, bool gated, int64_t fmt, const torch::Tens
 void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::optional<torch::Tensor>& q_row,
                   const c10::optional<torch::Tensor>& s_row, const c10::optional<torch::Tensor>& q_col,
                   const c10::optional<torch::Tensor>& s_col, const c10::optional<torch::Tensor>& amax,
-                  bool row_major) {
+                  bool row_major, int64_t act) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2, "x must be a 2-D CUDA bf16 tensor");
+  TORCH_CHECK(act >= 0 && act <= 2, "fp8_quantize: act is 0 (none), 1 (gelu) or 2 (swiglu)");
   const long long ldx = ld_of(x, "x");
-  const int R = x.size(0), C = x.size(1);
+  const int R = x.size(0), C = act == 2 ? x.size(1) / 2 : x.size(1);
   const long long nr = (R / 128), nc = (C / 128);  // R need not be a multiple of 128 for rowwise-only output
   if (q_row.has_value()) {
     check_fp8(*q_row, "q_row");
@@ -657,7 +658,8 @@ void fp8_quantize(const torch::Tensor& x, int64_t fmt, bool two_d, const c10::op
   RB_CALL(rb::fp8_quantize(x.data_ptr(), ldx, R, C, static_cast<int>(fmt), two_d ? 1 : 0,
                            q_row.has_value() ? q_row->data_ptr() : nullptr, opt_f32(s_row, "s_row"),
                            q_col.has_value() ? q_col->data_ptr() : nullptr, opt_f32(s_col, "s_col"),
-                           reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream(), row_major ? 1 : 0),
+                           reinterpret_cast<unsigned int*>(opt_f32(amax, "amax")), cur_stream(), row_major ? 1 : 0,
+                           static_cast<int>(act)),
           "fp8_quantize");
 }
 
@@ -732,7 +734,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_bwd", &gelu_bwd);
   m.def("fp8_quantize", &fp8_quantize, "block-scaled fp8 quantisation", py::arg("x"), py::arg("fmt"),
         py::arg("two_d"), py::arg("q_row"), py::arg("s_row"), py::arg("q_col"), py::arg("s_col"), py::arg("amax"),
-        py::arg("row_major") = false);
+        py::arg("row_major") = false, py::arg("act") = 0);
   m.def("act_fp8", &act_fp8, "MLP activation written as block-scaled fp8", py::arg("input"), py::arg("gated"),
         py::arg("fmt"), py::arg("q"), py::arg("s"), py::arg("s_kb"), py::arg("s_row"), py::arg("amax"));
   m.def("rmsnorm_fp8", &rmsnorm_fp8, "RMSNorm written as block-scaled fp8", py::arg("x"), py::arg("w"),

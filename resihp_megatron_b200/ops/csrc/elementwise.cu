@@ -9,6 +9,7 @@
 
 #include <cstdint>
 
+#include "act_common.cuh"
 #include "fp8_common.cuh"
 #include "sm100.cuh"
 
@@ -273,7 +274,6 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ q, long long row_stride,
   *reinterpret_cast<uint32_t*>(base + half + i) = pack_bf16x2(hi.x * c0 + lo.x * s0, hi.y * c1 + lo.y * s1);
 }
 
-__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
 
 // gu = [T, 2F] with gate in [:, :F] and up in [:, F:]; a = silu(gate) * up.
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ a, int T,
@@ -313,10 +313,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* 
   store_bf16x8(dgu + gofs + F, du);
 }
 
-// GELU, tanh form (the GPT MLP activation): gelu(h) = 0.5 h (1 + tanh(c (h + 0.044715 h^3))),
-// c = sqrt(2 / pi).  Elementwise over [n] (n % 8 == 0).
-constexpr float kGeluC = 0.7978845608028654f;
-constexpr float kGeluA = 0.044715f;
+// GELU (act_common.cuh), elementwise over [n] (n % 8 == 0).
 
 __global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ a, long long n8) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -324,7 +321,7 @@ __global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat
   float x[8], o[8];
   load_bf16x8(h + i * 8, x);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = 0.5f * x[j] * (1.f + tanhf(kGeluC * (x[j] + kGeluA * x[j] * x[j] * x[j])));
+  for (int j = 0; j < 8; ++j) o[j] = gelu_tanh(x[j]);
   store_bf16x8(a + i * 8, o);
 }
 
@@ -387,8 +384,7 @@ __global__ void __launch_bounds__(256) act_fp8_kernel(const __nv_bfloat16* __res
       load_bf16x8(in + t * F + c * 8, x);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        o[j] = __bfloat162float(
-            __float2bfloat16_rn(0.5f * x[j] * (1.f + tanhf(kGeluC * (x[j] + kGeluA * x[j] * x[j] * x[j])))));
+        o[j] = __bfloat162float(__float2bfloat16_rn(gelu_tanh(x[j])));
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = max(m, __float_as_uint(o[j]) & 0x7fffffffu);

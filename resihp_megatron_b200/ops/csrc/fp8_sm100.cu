@@ -37,6 +37,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include "act_common.cuh"
 #include "fp8_common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -65,6 +66,7 @@ struct QuantArgs {
   const uint16_t* x;  // bf16 bits
   long long ldx;
   int R, C, fmt, two_d;
+  int act;  // what is quantised: 0 x itself, 1 gelu(x), 2 silu(x[:, :C]) * x[:, C:] (bf16-rounded)
   int s_row_major;  // 1x128 rowwise scales stored [R][C/128] (a row's scales contiguous) instead of [C/128][R]
   uint8_t* q_row;   // [R, C] or null
   float* s_row;     // 1x128: [C/128][R] (or [R][C/128]);  2-D: [C/128][R/128] (shared by both outputs)
@@ -90,7 +92,29 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(QuantArgs p) {
   for (int i = t; i < kQT * 16; i += 256) {
     const int r = i >> 4, c8 = i & 15;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < rows) v = *reinterpret_cast<const uint4*>(p.x + static_cast<long long>(r0 + r) * p.ldx + c0 + c8 * 8);
+    if (r < rows) {
+      const uint16_t* xr = p.x + static_cast<long long>(r0 + r) * p.ldx + c0 + c8 * 8;
+      v = *reinterpret_cast<const uint4*>(xr);
+      if (p.act != 0) {  // the activation, rounded to bf16 as the bf16 activation kernels round it
+        const uint4 up = p.act == 2 ? *reinterpret_cast<const uint4*>(xr + p.C) : v;
+        const uint32_t* a = &v.x;
+        const uint32_t* b = &up.x;
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float lo = bf16_bits_to_float(a[k] & 0xffffu), hi = bf16_bits_to_float(a[k] >> 16);
+          if (p.act == 1) {
+            lo = gelu_tanh(lo);
+            hi = gelu_tanh(hi);
+          } else {
+            lo = silu(lo) * bf16_bits_to_float(b[k] & 0xffffu);
+            hi = silu(hi) * bf16_bits_to_float(b[k] >> 16);
+          }
+          o[k] = pack_bf16x2(lo, hi);
+        }
+        v = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
     *reinterpret_cast<uint4*>(tile + r * kQPitch + c8 * 8) = v;
   }
   __syncthreads();
@@ -506,17 +530,18 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
 }  // namespace
 
 int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
-                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major) {
+                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major, int act) {
   if (R <= 0 || C <= 0 || C % kQT || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -3;
   if (R % kQT && (two_d || q_col != nullptr)) return -3;  // 128-row blocks need whole row tiles
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || ldx % 8 || ldx < C) return -4;
+  if (act < 0 || act > 2) return -3;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || ldx % 8 || ldx < (act == 2 ? 2 * C : C)) return -4;
   if ((q_row != nullptr && s_row == nullptr) || (q_col != nullptr && !two_d && s_col == nullptr)) return -5;
   if (two_d && s_row == nullptr) return -5;
   if ((q_row != nullptr && (reinterpret_cast<uintptr_t>(q_row) & 15)) ||
       (q_col != nullptr && (reinterpret_cast<uintptr_t>(q_col) & 15)))
     return -6;
   if (s_row_major && two_d) return -3;
-  QuantArgs p{static_cast<const uint16_t*>(x), ldx, R, C, fmt, two_d, s_row_major, static_cast<uint8_t*>(q_row),
+  QuantArgs p{static_cast<const uint16_t*>(x), ldx, R, C, fmt, two_d, act, s_row_major, static_cast<uint8_t*>(q_row),
               s_row, static_cast<uint8_t*>(q_col), s_col, amax};
   dim3 grid(C / kQT, (R + kQT - 1) / kQT);
   fp8_quantize_kernel<<<grid, 256, 0, s>>>(p);

@@ -128,7 +128,7 @@ int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* r
 // Block-scaled fp8 (fp8_sm100.cu).  fmt: 0 = E4M3, 1 = E5M2.  Scale of operand row r in K-block kb:
 // s[kb * kb_stride + (r >> shift) * row_stride] (shift 0: 1 x 128 blocks, 7: 128 x 128 blocks).
 int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
-                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major = 0);
+                 void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major = 0, int act = 0);
 int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
              int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
              int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream,

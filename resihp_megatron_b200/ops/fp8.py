@@ -131,18 +131,26 @@ class Fp8Tensor:
         return Fp8Operand(self.q_col, self.s_col, self.C, 1, 0, self.fmt)
 
 
+ACTS = {None: 0, "gelu": 1, "swiglu": 2}
+
+
 def quantize(x: torch.Tensor, fmt: int | str = E4M3, *, two_d: bool = False, rowwise: bool = True,
              colwise: bool = False, amax: torch.Tensor | None = None, out: Fp8Tensor | None = None,
-             row_major: bool = False) -> Fp8Tensor:
-    """Quantise bf16 ``x [R, C]`` (C a multiple of 128; R too unless rowwise-only).  ``amax`` (fp32, >= 1 element) receives
-    ``max(amax[0], max |x|)`` -- NaN and inf propagate.  ``row_major``: rowwise scales stored
-    ``[R, C/128]`` (taken from ``out`` when given)."""
+             row_major: bool = False, act: str | None = None) -> Fp8Tensor:
+    """Quantise bf16 ``x [R, C]`` (C a multiple of 128; R too unless rowwise-only).  ``amax`` (fp32,
+    >= 1 element) receives ``max(amax[0], max |x|)`` -- NaN and inf propagate.  ``row_major``:
+    rowwise scales stored ``[R, C/128]`` (taken from ``out`` when given).  ``act``: quantise the
+    MLP activation of ``x`` instead -- ``"gelu"`` (``x`` is ``[R, C]``) or ``"swiglu"`` (``x`` is
+    ``[R, 2C]``: gate | up) -- computed and rounded to bf16 exactly as the activation kernels do."""
     fmt = fmt_of(fmt)
     R, C = x.shape
+    if act == "swiglu":
+        C //= 2
     if out is None:
         out = Fp8Tensor.empty(R, C, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, device=x.device,
                               row_major=row_major)
-    ext().fp8_quantize(x, fmt, two_d, _u8(out.q_row), out.s_row, _u8(out.q_col), out.s_col, amax, out.row_major)
+    ext().fp8_quantize(x, fmt, two_d, _u8(out.q_row), out.s_row, _u8(out.q_col), out.s_col, amax, out.row_major,
+                       ACTS[act])
     count(1)
     return out
 

@@ -159,3 +159,20 @@ def test_act_quantize_equals_activation_then_quantize(gated):
     torch.cuda.synchronize()
     assert torch.equal(out.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
     assert torch.equal(out.s_row, ref.s_row) and a0.item() == a1.item()
+
+
+@pytest.mark.parametrize("act", ["gelu", "swiglu"])
+def test_quantize_of_the_activation_equals_activation_then_quantize(act):
+    """The quantiser's activation option (the fp8 wgrad input of fc2, along tokens): same bytes and
+    scales as the bf16 activation kernel followed by ``quantize``."""
+    from resihp_megatron_b200 import ops
+
+    T, F = 384, 1024
+    gu = _x(T, 2 * F if act == "swiglu" else F, seed=12, spread=0.5)
+    y = ops.swiglu_fwd(gu) if act == "swiglu" else ops.gelu_fwd(gu)
+    ref = fp8.quantize(y, fp8.E4M3, rowwise=True, colwise=True)
+    got = fp8.quantize(gu, fp8.E4M3, rowwise=True, colwise=True, act=act)
+    torch.cuda.synchronize()
+    assert torch.equal(got.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
+    assert torch.equal(got.q_col.view(torch.uint8), ref.q_col.view(torch.uint8))
+    assert torch.equal(got.s_row, ref.s_row) and torch.equal(got.s_col, ref.s_col)

@@ -193,9 +193,12 @@ def gelu_bwd(h, da, out=None):
 
 
 # block-scaled fp8: the PyTorch emulation of the kernels (bit-exact quantiser)
-def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=None, out=None, row_major=False):
+def fp8_quantize(x, fmt=0, *, two_d=False, rowwise=True, colwise=False, amax=None, out=None, row_major=False,
+                 act=None):
     from resihp_megatron_b200.ops import fp8
 
+    if act is not None:
+        x = swiglu_fwd(x) if act == "swiglu" else gelu_fwd(x)
     if out is not None:
         row_major = out.row_major
     ref = fp8.quantize_reference(x, fmt, two_d=two_d, rowwise=rowwise, colwise=colwise, amax=amax,
