@@ -651,6 +651,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       __threadfence();
+      fence_proxy_async_global();  // this thread's generic writes -> the consumers' TMA (async proxy) reads
       named_bar_sync(1, 128);
       if (t == 0) st_release_gpu(p.ag_ready + 1 + mb * nseg + seg, 1);
     }
