@@ -1,6 +1,7 @@
 """Kernel microbenchmarks with roofline fractions (``resihp-bench kernels``).
 
     python -m resihp_megatron_b200.bench.kernels gemm --m 8192 --n 8192 --k 8192
+    python -m resihp_megatron_b200.bench.kernels fp8 --m 8192 --n 8192 --k 8192
     python -m resihp_megatron_b200.bench.kernels attention --batch 2 --seq 4096 --heads 32 --kv-heads 8
     python -m resihp_megatron_b200.bench.kernels adam --numel 1000000000
     python -m resihp_megatron_b200.bench.kernels all
@@ -90,6 +91,61 @@ def bench_gemm(a, t: Timer) -> None:
     assert int(ops.error_state()[0]) == 0
 
 
+def bench_fp8(a, t: Timer) -> None:
+    """Block-scaled fp8: the GEMM in its forward layout (1 x 128 row scales x 128 x 128 weight
+    tiles) and its weight-gradient layout (per-column scales), the quantiser and the fused
+    RMSNorm -> fp8, beside cuBLAS fp8 with one scale per tensor (``torch._scaled_mm``) when the
+    installed PyTorch offers it.  GEMM fractions are of twice the measured bf16 peak (the dense
+    fp8 rate is twice the bf16 rate)."""
+    from .. import ops
+    from ..ops import fp8
+
+    M, N, K = a.m, a.n, a.k
+    fl = 2.0 * M * N * K
+    pk = peaks()
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    xq = fp8.quantize(x, fp8.E4M3, rowwise=True, colwise=True)
+    wq = fp8.quantize(w, fp8.E4M3, two_d=True, rowwise=True, colwise=True)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+    def frac(row):
+        if "tflops" in row:
+            row["frac_of_2x_bf16_peak"] = round(row["tflops"] / (2 * pk["bf16_tflops"]), 3)
+            print(json.dumps({"kernel": row["kernel"], "frac_of_2x_bf16_peak": row["frac_of_2x_bf16_peak"]}),
+                  flush=True)
+
+    frac(emit("gemm_fp8_fwd_blockscaled", t(lambda: fp8.gemm(xq.rowwise(), wq.rowwise(), out=out)), flops=fl,
+              shape=[M, N, K]))
+    # weight-gradient layout: both operands scaled per row along K (per-column scales of B)
+    dy = torch.randn(K, M, device="cuda").bfloat16()
+    dyq = fp8.quantize(dy, fp8.E5M2, rowwise=True)
+    g = torch.zeros(K, N, device="cuda")
+    xq2 = fp8.quantize(torch.randn(N, M, device="cuda").bfloat16(), fp8.E4M3, rowwise=True)
+    frac(emit("gemm_fp8_wgrad_blockscaled", t(lambda: fp8.gemm(dyq.rowwise(), xq2.rowwise(), out=g, accumulate=True)),
+              flops=fl, shape=[K, N, M]))
+    try:
+        a8, b8 = x.to(torch.float8_e4m3fn), w.to(torch.float8_e4m3fn)
+        one = torch.ones((), device="cuda")
+        frac(emit("cublas_fp8_tensorwise", t(lambda: torch._scaled_mm(a8, b8.t(), scale_a=one, scale_b=one,
+                                                                         out_dtype=torch.bfloat16)),
+                  flops=fl, shape=[M, N, K]))
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"kernel": "cublas_fp8_tensorwise", "unavailable": str(e)[:200]}), flush=True)
+    # bandwidth-bound producers (bf16 in, fp8 + scales out)
+    T, H = a.tokens, a.hidden
+    xt = torch.randn(T, H, device="cuda").bfloat16()
+    buf = fp8.Fp8Tensor.empty(T, H, fp8.E4M3, rowwise=True, colwise=True, device="cuda")
+    emit("fp8_quantize_row_col", t(lambda: fp8.quantize(xt, fp8.E4M3, rowwise=True, colwise=True, out=buf)),
+         bytes_=T * H * (2 + 1 + 1), shape=[T, H])
+    nw = torch.ones(H, device="cuda").bfloat16()
+    rbuf = fp8.Fp8Tensor.empty(T, H, fp8.E4M3, device="cuda")
+    rstd = torch.empty(T, device="cuda")
+    emit("rmsnorm_fp8", t(lambda: fp8.rmsnorm_quantize(xt, nw, 1e-5, fp8.E4M3, out=rbuf, rstd=rstd)),
+         bytes_=T * H * (2 + 1), shape=[T, H])
+    assert int(ops.error_state()[0]) == 0
+
+
 def bench_attention(a, t: Timer) -> None:
     from .. import ops
 
@@ -158,7 +214,7 @@ def bench_ce(a, t: Timer) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(prog="resihp-bench kernels")
-    ap.add_argument("which", choices=["gemm", "attention", "adam", "norm", "ce", "all"])
+    ap.add_argument("which", choices=["gemm", "fp8", "attention", "adam", "norm", "ce", "all"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=8192)
@@ -179,8 +235,8 @@ def main(argv=None) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("kernel benchmarks need a GPU")
     t = Timer(a.warmup, a.iters, not a.no_flush)
-    table = {"gemm": bench_gemm, "attention": bench_attention, "adam": bench_adam, "norm": bench_norm,
-             "ce": bench_ce}
+    table = {"gemm": bench_gemm, "fp8": bench_fp8, "attention": bench_attention, "adam": bench_adam,
+             "norm": bench_norm, "ce": bench_ce}
     for name in (table if a.which == "all" else [a.which]):
         table[name](a, t)
 
