@@ -481,32 +481,34 @@ def run_moe(args, rank: int, world: int, local: int) -> None:
     r = _timed_region(args, trainer, rank, world, local)
     recfg = None
     if args.reconfig and world > 1:
-        # fail-slow re-placement: the last rank is taken as 2x slower (its speed is given here; the
-        # residual-BOCD detector that would report it is exercised separately), the planner
-        # replicates / moves its experts and their state migrates peer to peer
+        # fail-slow: the last rank's expert compute is stretched 2x from the host (no GPU setting is
+        # touched); every rank times its expert GEMMs, the residual-BOCD monitor flags the slow
+        # rank, the planner re-places its experts by speed and their state migrates peer to peer
+        trainer.enable_failslow(warmup=6)
+        dist.barrier()
+        for _ in range(8):  # healthy series for the detector's calibration
+            trainer.train_step()
+        if rank == world - 1:
+            trainer.set_slowdown(2.0)
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        info = trainer.replace_experts({world - 1: 0.5})
-        commit_s = time.perf_counter() - t0
-        for _ in range(max(2, min(args.warmup, 3))):
-            trainer.step_device()
-        torch.cuda.synchronize()
-        trainer.check()
-        dist.barrier()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(args.steps):
-            trainer.step_device()
-        end.record()
-        torch.cuda.synchronize()
-        vals = torch.tensor([start.elapsed_time(end), commit_s], device=trainer.device, dtype=torch.float64)
+        slowed_steps = 0
+        while not trainer.failslow_events and slowed_steps < 40:
+            trainer.train_step()
+            slowed_steps += 1
+        detect_s = time.perf_counter() - t0
+        event = trainer.failslow_events[0] if trainer.failslow_events else None
+        post = _post_steps(args, trainer)  # the slow rank stays slow
+        vals = torch.tensor([post["ms"], detect_s], device=trainer.device, dtype=torch.float64)
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        post_ms, commit_max = vals.tolist()
-        recfg = {"kind": "fail-slow expert re-placement (last rank at half speed), expert state migrated",
+        post_ms, detect_max = vals.tolist()
+        recfg = {"kind": "fail-slow (last rank's expert compute 2x slower, host-injected), detected by residual BOCD "
+                         "on per-rank expert time, experts re-placed by speed, expert state migrated",
+                 "detected": event is not None, "slowed_steps_to_replacement": slowed_steps,
+                 "slow_to_commit_s": detect_max, "event": event,
                  "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
-                 "post_ms_per_step": post_ms / args.steps, "replace_to_commit_s": commit_max,
-                 "holders": info["holders"], "phases_s_rank0": {k: v for k, v in info.items() if k != "holders"}}
+                 "post_ms_per_step": post_ms / args.steps, "phases_s_rank0": trainer.last_reconfig}
     if rank == 0:
         out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r,
                          {"experts": cfg.num_experts, "top_k": cfg.top_k})

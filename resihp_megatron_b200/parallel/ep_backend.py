@@ -117,6 +117,9 @@ class CollectiveEP:
         s = self.saved
         y = torch.empty_like(s["recv"])
         s["expert_cache"] = {}
+        clock = getattr(self, "clock", None)
+        if clock is not None:
+            clock.begin(s["recv_rows"])
         for e, (lo, n) in zip(self.local, s["local_ranges"]):
             if n == 0:
                 continue
@@ -126,6 +129,8 @@ class CollectiveEP:
             a = ops.swiglu_fwd(gu)
             ops.gemm(a, w2, out=y[lo:lo + n])
             s["expert_cache"][e] = (gu, a, xin)
+        if clock is not None:
+            clock.end()
         s["y"] = y
 
     def combine(self, residual: torch.Tensor) -> torch.Tensor:
@@ -158,6 +163,9 @@ class CollectiveEP:
     def experts_backward(self, weights, grads) -> None:
         s = self.saved
         dx = torch.zeros_like(s["dyrecv"])
+        clock = getattr(self, "clock", None)
+        if clock is not None:
+            clock.begin(s["recv_rows"])
         for e, (lo, n) in zip(self.local, s["local_ranges"]):
             if n == 0:
                 continue
@@ -169,6 +177,8 @@ class CollectiveEP:
             dgu = ops.swiglu_bwd(gu, da)
             ops.gemm(dgu, xin, a_t=True, b_t=True, out=grads[e][0], accumulate=True)
             ops.gemm(dgu, w13, b_t=True, out=dx[lo:lo + n])
+        if clock is not None:
+            clock.end()
         s["dxrecv"] = dx
 
     def grad_pull(self, router_w: torch.Tensor, router_grad: torch.Tensor, residual: bool = True,

@@ -197,6 +197,9 @@ class ExpertParallelMoE:
         per layer: ``take_state`` / ``put_state``)."""
         s = self.saved
         s["expert_cache"] = {}
+        clock = getattr(self, "clock", None)
+        if clock is not None:
+            clock.begin(s["recv_rows"])
         for e, (lo, n) in zip(self.local, s["local_ranges"]):
             if n == 0:
                 continue
@@ -208,6 +211,8 @@ class ExpertParallelMoE:
             a = ops.swiglu_fwd(gu)
             ops.gemm(a, w2, out=self.rows("y", lo + n)[lo:])
             s["expert_cache"][e] = (gu, a, xin if keep_input else None)
+        if clock is not None:
+            clock.end()  # before the barrier: a slow peer does not stretch this rank's time
         self._barrier()
 
     def take_state(self) -> dict:
@@ -244,6 +249,9 @@ class ExpertParallelMoE:
     def experts_backward(self, weights, grads) -> None:
         """``grads[e] = (dw13 fp32, dw2 fp32)`` accumulated (fixed row order)."""
         s = self.saved
+        clock = getattr(self, "clock", None)
+        if clock is not None:
+            clock.begin(s["recv_rows"])
         for e, (lo, n) in zip(self.local, s["local_ranges"]):
             if n == 0:
                 continue
@@ -256,6 +264,8 @@ class ExpertParallelMoE:
             dgu = ops.swiglu_bwd(gu, da)
             ops.gemm(dgu, xin, a_t=True, b_t=True, out=grads[e][0], accumulate=True)
             ops.gemm(dgu, w13, b_t=True, out=self.rows("dxrecv", lo + n)[lo:])
+        if clock is not None:
+            clock.end()
         self._barrier()
 
     def grad_pull(self, router_w: torch.Tensor, router_grad: torch.Tensor, residual: bool = True,

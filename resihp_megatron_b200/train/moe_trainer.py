@@ -117,6 +117,46 @@ class GPUMoETrainer:
         self.h2d_bytes = 0
         self.layout = f"ep{self.world}dp{self.world}-{ep_impl}ep-{dp_impl}dp"
         self.last_reconfig: dict | None = None
+        self.clock = None
+        self.monitor = None
+        self.failslow_events: list[dict] = []
+
+    # ------------------------------------------------------------------ fail-slow detection
+    def enable_failslow(self, *, slowdown: float = 1.0, model_ms_per_row: float | None = None,
+                        **detector_kw) -> None:
+        """Time this rank's expert compute every step and run the residual-BOCD monitor on every
+        rank's times after each ``train_step``; a rank flagged slow triggers ``replace_experts``
+        with its estimated speed.  ``slowdown`` > 1 emulates a slower GPU on this rank (host-side
+        idling inside its expert regions; no GPU setting is touched); ``model_ms_per_row``
+        replaces the measurement by a modelled time (CPU tests)."""
+        from .moe_failslow import ExpertClock, ExpertSlowMonitor
+
+        self.clock = ExpertClock(self.device, slowdown, model_ms_per_row, seed=self.rank)
+        self.ep.clock = self.clock
+        self.monitor = ExpertSlowMonitor(self.world, **detector_kw)
+
+    def set_slowdown(self, factor: float) -> None:
+        if self.clock is not None:
+            self.clock.slowdown = float(factor)
+
+    def _observe_failslow(self) -> dict | None:
+        ms, rows = self.clock.collect()
+        mine = torch.tensor([ms, float(rows)], dtype=torch.float64, device=self.device)
+        allv = torch.empty(self.world * 2, dtype=torch.float64, device=self.device)
+        if self.world > 1:
+            dist.all_gather_into_tensor(allv, mine)
+        else:
+            allv.copy_(mine)
+        v = allv.view(self.world, 2).tolist()
+        slow = self.monitor.observe(self.iteration - 1, [a for a, _ in v], [int(b) for _, b in v])
+        if not slow:
+            return None
+        speeds = {r: max(0.05, min(1.0, p)) for r, p in slow.items()}
+        info = self.replace_experts(speeds)
+        self.monitor.reset()
+        event = {"iteration": self.iteration - 1, "speeds": speeds, "holders": info["holders"]}
+        self.failslow_events.append(event)
+        return event
 
     def _make_ep(self, holders, speeds):
         cfg, T = self.cfg, self.micro_batch * self.S
@@ -158,8 +198,12 @@ class GPUMoETrainer:
         return self.h2d_bytes
 
     def train_step(self) -> float:
+        """One step through the public path; with fail-slow detection enabled, the step's expert
+        times are then exchanged and a flagged rank's experts re-placed before the next step."""
         value = float(self.step_device().item())
         self.check()
+        if self.monitor is not None:
+            self._observe_failslow()
         return value
 
     # ------------------------------------------------------------------ expert re-placement
@@ -243,6 +287,8 @@ class GPUMoETrainer:
         self.ep.close()
         self.holders, self.speeds = new_holders, dict(speeds)
         self.ep = self._make_ep(self.holders, self.speeds)
+        if self.clock is not None:
+            self.ep.clock = self.clock
         self.model.rebuild_experts(self.holders, self.rank, self.ep)
         Q = self.model.experts
         for name in Q.order:

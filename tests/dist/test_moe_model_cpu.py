@@ -91,3 +91,50 @@ def test_fail_slow_expert_replacement_keeps_the_run():
         assert out["info"]["holders"] == holders
         for a, b in zip(out["losses"], ref):
             assert abs(a - b) <= 1e-2 * abs(b), (r, out["losses"], ref)
+
+
+def _failslow(rank, world, port, steps, slow_rank, slow_from):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    import torch
+
+    from resihp_megatron_b200.models.config import GPTConfig
+    from resihp_megatron_b200.train.moe_trainer import GPUMoETrainer
+
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    cfg = GPTConfig(name="tmoe-fs", vocab_size=64, hidden=256, layers=1, heads=4, kv_heads=2, ffn=512, seq_len=64,
+                    num_experts=4, top_k=2)
+    tr = GPUMoETrainer(cfg, global_batch=8, micro_batch=1, seq_len=64, ep_impl="collective", dp_impl="collective",
+                       device="cpu", lr=1e-3)
+    tr.enable_failslow(warmup=5, model_ms_per_row=0.01)  # modelled device time: CPU timings are too noisy
+    holders0 = [list(h) for h in tr.holders]
+    losses = []
+    for it in range(steps):
+        if rank == slow_rank and it == slow_from:
+            tr.set_slowdown(3.0)  # this rank's expert compute now runs 3x slower
+        losses.append(tr.train_step())
+    out = {"events": tr.failslow_events, "holders0": holders0, "holders": tr.holders, "losses": losses}
+    tr.close()
+    dist.destroy_process_group()
+    return out
+
+
+def test_fail_slow_rank_is_detected_by_residual_bocd_and_its_experts_replaced():
+    """A rank whose expert compute slows 3x from step 14: every rank's per-row expert time (a
+    modelled device time with jitter: CPU process timings are far noisier than a GPU's) goes to
+    one residual-BOCD detector per rank (median rank = prediction); the slow rank -- and only it --
+    is flagged within a few steps on every rank, its experts are re-placed by speed, training
+    continues."""
+    res = spawn(_failslow, 4, 30, 3, 14, timeout=400)
+    firsts = {r: out["events"][0] if out["events"] else None for r, out in res.items()}
+    assert all(e is not None for e in firsts.values()), firsts
+    ev = firsts[0]
+    assert all(e == ev for e in firsts.values())  # every rank decided the same
+    assert set(ev["speeds"]) == {3} and ev["speeds"][3] < 0.8, ev
+    assert 14 <= ev["iteration"] <= 22, ev
+    assert res[0]["holders"] != res[0]["holders0"]
+    assert all(abs(l) < 100 for l in res[0]["losses"])
