@@ -49,7 +49,7 @@ def _args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="llama3-8b")
-    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the model's, 4096 for llama3-8b)")
     ap.add_argument("--seqs-per-gpu", type=int, default=None,
                     help=f"sequences per GPU per step (default {SEQS_PER_GPU}; MoE models: 4, i.e. BASELINE config 3's "
                          "global batch 32 at 8 GPUs)")
@@ -187,6 +187,8 @@ def main() -> None:
 
     from resihp_megatron_b200.models.config import get_config as _get_config
 
+    if args.seq is None:
+        args.seq = _get_config(args.model).seq_len
     if args.seqs_per_gpu is None:
         args.seqs_per_gpu = 4 if _get_config(args.model).is_moe else SEQS_PER_GPU
     rank, world, local = init_distributed()
