@@ -51,8 +51,8 @@ def _args():
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the model's, 4096 for llama3-8b)")
     ap.add_argument("--seqs-per-gpu", type=int, default=None,
-                    help=f"sequences per GPU per step (default {SEQS_PER_GPU}; MoE models: 4, i.e. BASELINE config 3's "
-                         "global batch 32 at 8 GPUs)")
+                    help=f"sequences per GPU per step (default {SEQS_PER_GPU}; MoE models: 4 and gpt-1.3b: 32, i.e. "
+                         "BASELINE config 3's global batch 32 and config 4's 256 at 8 GPUs)")
     ap.add_argument("--micro-batch", type=int, default=None,
                     help="sequences per micro-batch; default 1 on one GPU (the unsharded optimizer state leaves "
                          "room for one), 2 on more (bigger GEMMs, fewer partial waves)")
@@ -189,8 +189,8 @@ def main() -> None:
 
     if args.seq is None:
         args.seq = _get_config(args.model).seq_len
-    if args.seqs_per_gpu is None:
-        args.seqs_per_gpu = 4 if _get_config(args.model).is_moe else SEQS_PER_GPU
+    if args.seqs_per_gpu is None:  # the benchmark configs' global batches at 8 GPUs: 64, 32 (MoE), 256 (gpt-1.3b)
+        args.seqs_per_gpu = {"gpt-1.3b": 32}.get(args.model, 4 if _get_config(args.model).is_moe else SEQS_PER_GPU)
     rank, world, local = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
