@@ -39,7 +39,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "tokens/sec/box (device, max over ranks) pre/post reconfig; fault→commit s"
 SEQS_PER_GPU = 8
-BASELINE_PUBLISHED = None  # BASELINE.md publishes no GPU tokens/s for the reference
+BASELINE_PUBLISHED = None  # no published GPU tokens/s of the reference for this metric
 
 
 def _args():
