@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
 
-Config (BASELINE config 2 shape): 32 layers, hidden 4096, GQA 32q/8kv heads, SwiGLU FFN
+Config (benchmark config 2 shape): 32 layers, hidden 4096, GQA 32q/8kv heads, SwiGLU FFN
 14336, vocab 128256, seq 4096, bf16 compute with fp32 master weights and Adam, random
 N(0, 0.02) init, uniform random token ids (synthetic).  Weak scaling: 8 sequences per GPU
 per step (global batch 64 at 8 GPUs), micro-batch 1, gradient accumulation over the
@@ -52,7 +52,7 @@ def _args():
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the model's, 4096 for llama3-8b)")
     ap.add_argument("--seqs-per-gpu", type=int, default=None,
                     help=f"sequences per GPU per step (default {SEQS_PER_GPU}; MoE models: 4 and gpt-1.3b: 32, i.e. "
-                         "BASELINE config 3's global batch 32 and config 4's 256 at 8 GPUs)")
+                         "benchmark config 3's global batch 32 and config 4's 256 at 8 GPUs)")
     ap.add_argument("--micro-batch", type=int, default=None,
                     help="sequences per micro-batch; default 1 on one GPU (the unsharded optimizer state leaves "
                          "room for one), 2 on more (bigger GEMMs, fewer partial waves)")
@@ -68,17 +68,17 @@ def _args():
                          "the warm-up and replay it")
     ap.add_argument("--parallelism", default="dp",
                     help="'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' with T*P*D = N: tensor (+ sequence) x "
-                         "pipeline x data parallelism through the plan-driven runtime (BASELINE config 2: tp2pp2dp2)")
+                         "pipeline x data parallelism through the plan-driven runtime (benchmark config 2: tp2pp2dp2)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
                     help="MoE models: expert dispatch / combine over NVLink peer memory, or NCCL all_to_all")
     ap.add_argument("--tp-impl", choices=["fused", "collective"], default="fused",
                     help="with --parallelism tp..: TP collectives fused into the GEMMs over NVLink, or NCCL")
     ap.add_argument("--fp8", action="store_true",
                     help="block-scaled fp8 projections (E4M3 forward / E5M2 backward, 1x128 activation and 128x128 "
-                         "weight scales, amax history 16; BASELINE config 4 with --model gpt-1.3b)")
+                         "weight scales, amax history 16; benchmark config 4 with --model gpt-1.3b)")
     ap.add_argument("--reshard", default=None,
                     help="with --parallelism tp..: after the timed steps change the layout live on the same GPUs "
-                         "(e.g. tp2pp1dp4 after tp4pp1dp2: BASELINE config 4's TP4 -> TP2), migrating parameters, "
+                         "(e.g. tp2pp1dp4 after tp4pp1dp2: benchmark config 4's TP4 -> TP2), migrating parameters, "
                          "Adam moments and amax histories, and time the same steps again")
     return ap.parse_args()
 
@@ -462,7 +462,7 @@ def _post_steps(args, trainer) -> dict:
 
 
 def run_moe(args, rank: int, world: int, local: int) -> None:
-    """Mixtral-shaped MoE step: dense weights data parallel, experts expert
+    """Mixtral-shaped MoE step (benchmark config 3): dense weights data parallel, experts expert
     parallel over the same ranks, through ``GPUMoETrainer``."""
     import torch
     import torch.distributed as dist

@@ -1,6 +1,6 @@
 """Resilient replica-DP training of the float64 GPT decoder on CPU workers.
 
-8 workers on 2 simulated nodes, 8 micro-batches of 2 x 32 tokens, 4 layers,
+benchmark config 1: 8 workers on 2 simulated nodes, 8 micro-batches of 2 x 32 tokens, 4 layers,
 hidden 64, 4 heads, vocab 512, N(0, 0.02) init from seed 0, uniform tokens from seed 1::
 
     RESIHP_FAULTS="kill@iter=3:target=n0g3:phase=forward" \\

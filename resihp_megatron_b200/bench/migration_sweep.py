@@ -1,4 +1,4 @@
-"""Live-migration sweep (first half): reshard a bf16 ``[N, N]`` weight plus two
+"""Live-migration sweep (benchmark config 5, first half): reshard a bf16 ``[N, N]`` weight plus two
 fp32 Adam moments from TP8 -> TP4 -> TP2 (row shards, the column-parallel layout), N in {4096,
 8192, 16384}, values N(0, 1) from seed 0, on 8 GPUs of one node.
 

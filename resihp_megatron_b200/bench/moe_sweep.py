@@ -1,4 +1,4 @@
-"""Expert-parallel MoE layer on 8 GPUs (Mixtral-8x7B shapes, BASELINE config 3's layer): hidden 4096,
+"""Expert-parallel MoE layer on 8 GPUs (Mixtral-8x7B shapes, benchmark config 3's layer): hidden 4096,
 8 SwiGLU experts of FFN 14336, top-2, one expert per GPU, 4096 tokens per GPU, uniform random
 inputs.  Forward + backward of one layer:
 

@@ -1,4 +1,4 @@
-"""Fused tensor-parallel collective sweep (second half): all-gather -> GEMM and
+"""Fused tensor-parallel collective sweep (benchmark config 5, second half): all-gather -> GEMM and
 GEMM -> reduce-scatter for M = 8192 tokens, K = N = 8192, at tp = 2, 4, 8 GPUs of one node.
 
 * all-gather -> GEMM (column-parallel, sequence-parallel input): each rank holds ``[M / tp, K]``

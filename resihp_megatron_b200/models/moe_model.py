@@ -7,7 +7,7 @@ Each layer is the Llama attention block followed by a top-k mixture of SwiGLU ex
 
 Dense weights (embedding, attention, norms, router, LM head) are replicated on every rank and
 reduced data parallel; expert ``e`` lives on rank ``holder[e]`` only (expert parallelism over
-the same ranks, BASELINE config 3's EP8 x DP8).  The expert transport is a backend with the
+the same ranks, benchmark config 3's EP8 x DP8).  The expert transport is a backend with the
 phases of ``parallel.moe_ep.ExpertParallelMoE`` (peer-memory kernels over NVLink) or
 ``parallel.ep_backend.CollectiveEP`` (``all_to_all``); one routing state is kept per layer
 between the forward and the backward of a micro-batch.  The backward through a MoE block needs

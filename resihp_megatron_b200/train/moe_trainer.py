@@ -1,5 +1,5 @@
 """GPU training engine for Mixtral-style MoE models: data parallel dense weights, expert parallel
-experts over the same ranks (EP8 x DP8, TP1).
+experts over the same ranks (benchmark config 3: EP8 x DP8, TP1).
 
 ``GPUMoETrainer.train_step()`` runs one optimizer step of the global batch: rank ``r`` takes the
 micro-batches ``[r * n, (r + 1) * n)`` of the step (synthetic tokens from ``TokenSource``, copied

@@ -1,4 +1,4 @@
-"""BASELINE config 1 end to end: 8 CPU workers on 2 simulated nodes train the float64 GPT with
+"""benchmark config 1 end to end: 8 CPU workers on 2 simulated nodes train the float64 GPT with
 replica DP; ``kill -9`` of n0g3 in the forward pass of iteration 3; the 7 survivors re-plan,
 roll back / forward, and finish 20 iterations.  Every survivor's loss trajectory must be
 bitwise equal to single-process training."""
