@@ -462,6 +462,47 @@ void symm_copy2d(const std::vector<int64_t>& six, int64_t device) {
                           static_cast<int>(pieces), num_sms(static_cast<int>(device)), cur_stream()), "symm_copy2d");
 }
 
+// Resident piece tables: returns (device table, piece count) once; *_run launches it (no host sync).
+std::tuple<torch::Tensor, int64_t> symm_copy2d_build(const std::vector<int64_t>& six, int64_t device) {
+  TORCH_CHECK(six.size() % 6 == 0, "symm_copy2d_build: sextuples");
+  const int n = static_cast<int>(six.size() / 6);
+  const long long pieces = rb::symm_copy2d_pieces(reinterpret_cast<const long long*>(six.data()), n);
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  auto table = torch::empty({std::max<long long>(pieces, 1) * rb::symm_copy2d_piece_bytes()},
+                            torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+  int count = 0;
+  RB_CALL(rb::symm_copy2d_build(reinterpret_cast<const long long*>(six.data()), n, table.data_ptr(),
+                                static_cast<int>(std::max<long long>(pieces, 1)), &count, cur_stream()),
+          "symm_copy2d_build");
+  return {table, count};
+}
+
+void symm_copy2d_run(const torch::Tensor& table, int64_t count) {
+  const c10::cuda::CUDAGuard g(table.device());
+  RB_CALL(rb::symm_copy2d_run(table.data_ptr(), static_cast<int>(count), num_sms(table.get_device()), cur_stream()),
+          "symm_copy2d_run");
+}
+
+std::tuple<torch::Tensor, int64_t> symm_sum_build(const std::vector<int64_t>& entries, int64_t device) {
+  TORCH_CHECK(entries.size() % 11 == 0, "symm_sum_build: (dst, n, nsrc, src x 8) per piece");
+  const int n = static_cast<int>(entries.size() / 11);
+  const long long pieces = rb::symm_sum_pieces(reinterpret_cast<const long long*>(entries.data()), n);
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  auto table = torch::empty({std::max<long long>(pieces, 1) * rb::symm_sum_piece_bytes()},
+                            torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+  int count = 0;
+  RB_CALL(rb::symm_sum_build(reinterpret_cast<const long long*>(entries.data()), n, table.data_ptr(),
+                             static_cast<int>(std::max<long long>(pieces, 1)), &count, cur_stream()),
+          "symm_sum_build");
+  return {table, count};
+}
+
+void symm_sum_run(const torch::Tensor& table, int64_t count) {
+  const c10::cuda::CUDAGuard g(table.device());
+  RB_CALL(rb::symm_sum_run(table.data_ptr(), static_cast<int>(count), num_sms(table.get_device()), cur_stream()),
+          "symm_sum_run");
+}
+
 // Tensor parallel: all-gather -> GEMM (column-parallel) and GEMM -> reduce-scatter (row-parallel).
 void tp_ag_gemm(const torch::Tensor& x_full, const std::vector<int64_t>& src_ptrs, int64_t self, const torch::Tensor& w,
                 bool w_t, torch::Tensor& y, torch::Tensor& ready, int64_t abort_dev) {
@@ -778,6 +819,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_grad_push", &moe_grad_push);
   m.def("moe_grad_pull", &moe_grad_pull);
   m.def("tp_rs_gemm", &tp_rs_gemm);
+  m.def("symm_copy2d_build", &symm_copy2d_build);
+  m.def("symm_copy2d_run", &symm_copy2d_run);
+  m.def("symm_sum_build", &symm_sum_build);
+  m.def("symm_sum_run", &symm_sum_run);
   m.def("tp_rs_reduce", &tp_rs_reduce, py::arg("recv"), py::arg("world"), py::arg("out"),
         py::arg("residual") = py::none());
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),

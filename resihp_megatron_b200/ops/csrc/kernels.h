@@ -100,6 +100,13 @@ int symm_gather(const void* const* src, void* dst, long long chunk_bytes, int wo
 // Strided slice copies (rows x row_bytes with source / destination pitches), pre-split on the host.
 int symm_copy2d(const long long* six, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
 long long symm_copy2d_pieces(const long long* six, int n);
+// Resident piece tables (built once, launched per step): strided copies and rank-ordered fp32 sums.
+int symm_copy2d_build(const long long* six, int n, void* dev_table, int max_pieces, int* count, cudaStream_t s);
+int symm_copy2d_run(const void* dev_table, int count, int num_sms, cudaStream_t s);
+int symm_sum_piece_bytes();
+long long symm_sum_pieces(const long long* entries, int n);
+int symm_sum_build(const long long* entries, int n, void* dev_table, int max_pieces, int* count, cudaStream_t s);
+int symm_sum_run(const void* dev_table, int count, int num_sms, cudaStream_t s);
 int symm_copy2d_piece_bytes();
 int symm_copy_piece_bytes();
 int rs_reduce(const void* recv, int world, long long n, void* out, const void* residual, cudaStream_t s);

@@ -278,6 +278,41 @@ __global__ void __launch_bounds__(256) symm_copy2d_kernel(const CopyPiece2D* __r
   }
 }
 
+// Rank-ordered sums over peer memory: dst[i] = src[0][i] + src[1][i] + ... (fp32, in the given order,
+// so every rank that sums the same sources gets the same bits).  The piece table stays on the
+// device between launches.
+constexpr int kSumMaxSrc = 8;
+struct SumPiece {
+  float* dst;
+  const float* src[kSumMaxSrc];
+  long long n;
+  int nsrc;
+  int vec4;  // n % 4 == 0 and every pointer 16-byte aligned
+};
+
+__global__ void __launch_bounds__(256) symm_sum_kernel(const SumPiece* __restrict__ pieces, int n_pieces) {
+  for (int pi = blockIdx.x; pi < n_pieces; pi += gridDim.x) {
+    const SumPiece p = pieces[pi];
+    if (p.vec4) {
+      const long long n4 = p.n / 4;
+      for (long long i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 acc = __ldcv(reinterpret_cast<const float4*>(p.src[0]) + i);
+        for (int k = 1; k < p.nsrc; ++k) {
+          const float4 v = __ldcv(reinterpret_cast<const float4*>(p.src[k]) + i);
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        reinterpret_cast<float4*>(p.dst)[i] = acc;
+      }
+    } else {
+      for (long long i = threadIdx.x; i < p.n; i += blockDim.x) {
+        float acc = __ldcv(p.src[0] + i);
+        for (int k = 1; k < p.nsrc; ++k) acc += __ldcv(p.src[k] + i);
+        p.dst[i] = acc;
+      }
+    }
+  }
+}
+
 // All-gather of equal row chunks: chunk c of `dst` (this rank's buffer) is filled from `src[c]`
 // (chunk c in rank c's buffer) for every c != self; the work is cut into 1 MB slices spread over
 // the grid.  No piece table, so nothing is staged on the host.
@@ -462,6 +497,100 @@ int symm_copy2d(const long long* six, int n, void* dev_scratch, int max_pieces, 
   symm_copy2d_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const CopyPiece2D*>(dev_scratch),
                                           static_cast<int>(pieces.size()));
   return static_cast<int>(cudaGetLastError());
+}
+
+// Resident piece tables: built once (host -> device copy, one synchronisation), launched many times.
+int symm_copy2d_build(const long long* six, int n, void* dev_table, int max_pieces, int* count, cudaStream_t s) {
+  constexpr long long kPieceBytes = 1 << 20;
+  std::vector<CopyPiece2D> pieces;
+  for (int i = 0; i < n; ++i) {
+    const long long src = six[6 * i], dst = six[6 * i + 1], rows = six[6 * i + 2], row_bytes = six[6 * i + 3];
+    const long long sp = six[6 * i + 4], dp = six[6 * i + 5];
+    if ((src | dst | row_bytes | sp | dp) & 15) return -1;
+    if (rows <= 0 || row_bytes <= 0) continue;
+    if (row_bytes > kPieceBytes) {
+      for (long long r = 0; r < rows; ++r)
+        for (long long off = 0; off < row_bytes; off += kPieceBytes) {
+          const long long b = row_bytes - off < kPieceBytes ? row_bytes - off : kPieceBytes;
+          pieces.push_back({reinterpret_cast<const uint4*>(src + r * sp + off),
+                            reinterpret_cast<uint4*>(dst + r * dp + off), 1, static_cast<int>(b / 16), 0, 0});
+        }
+      continue;
+    }
+    const long long per = kPieceBytes / row_bytes;
+    for (long long r = 0; r < rows; r += per) {
+      const long long nr = rows - r < per ? rows - r : per;
+      pieces.push_back({reinterpret_cast<const uint4*>(src + r * sp), reinterpret_cast<uint4*>(dst + r * dp),
+                        static_cast<int>(nr), static_cast<int>(row_bytes / 16), sp / 16, dp / 16});
+    }
+  }
+  *count = static_cast<int>(pieces.size());
+  if (pieces.empty()) return 0;
+  if (static_cast<int>(pieces.size()) > max_pieces) return -2;
+  cudaError_t e = cudaMemcpyAsync(dev_table, pieces.data(), pieces.size() * sizeof(CopyPiece2D),
+                                  cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaStreamSynchronize(s);
+  return static_cast<int>(e);
+}
+
+int symm_copy2d_run(const void* dev_table, int count, int num_sms, cudaStream_t s) {
+  if (count <= 0) return 0;
+  const int grid = count < num_sms * 4 ? count : num_sms * 4;
+  symm_copy2d_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const CopyPiece2D*>(dev_table), count);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int symm_sum_piece_bytes() { return static_cast<int>(sizeof(SumPiece)); }
+
+// entries: per piece (dst, n, nsrc, src[0..7]) as 11 long longs; pieces are split into 1 MB runs.
+int symm_sum_build(const long long* entries, int n, void* dev_table, int max_pieces, int* count, cudaStream_t s) {
+  constexpr long long kRun = (1 << 20) / 4;
+  std::vector<SumPiece> pieces;
+  for (int i = 0; i < n; ++i) {
+    const long long* e = entries + 11 * i;
+    const long long len = e[1];
+    const int nsrc = static_cast<int>(e[2]);
+    if (len <= 0) continue;
+    if (nsrc < 1 || nsrc > kSumMaxSrc) return -1;
+    for (long long off = 0; off < len; off += kRun) {
+      SumPiece p{};
+      p.dst = reinterpret_cast<float*>(e[0]) + off;
+      p.n = len - off < kRun ? len - off : kRun;
+      p.nsrc = nsrc;
+      uintptr_t bits = reinterpret_cast<uintptr_t>(p.dst);
+      for (int k = 0; k < nsrc; ++k) {
+        p.src[k] = reinterpret_cast<const float*>(e[3 + k]) + off;
+        bits |= reinterpret_cast<uintptr_t>(p.src[k]);
+      }
+      p.vec4 = (p.n % 4 == 0) && (bits & 15) == 0;
+      pieces.push_back(p);
+    }
+  }
+  *count = static_cast<int>(pieces.size());
+  if (pieces.empty()) return 0;
+  if (static_cast<int>(pieces.size()) > max_pieces) return -2;
+  cudaError_t e = cudaMemcpyAsync(dev_table, pieces.data(), pieces.size() * sizeof(SumPiece), cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaStreamSynchronize(s);
+  return static_cast<int>(e);
+}
+
+int symm_sum_run(const void* dev_table, int count, int num_sms, cudaStream_t s) {
+  if (count <= 0) return 0;
+  const int grid = count < num_sms * 4 ? count : num_sms * 4;
+  symm_sum_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const SumPiece*>(dev_table), count);
+  return static_cast<int>(cudaGetLastError());
+}
+
+long long symm_sum_pieces(const long long* entries, int n) {
+  constexpr long long kRun = (1 << 20) / 4;
+  long long count = 0;
+  for (int i = 0; i < n; ++i) {
+    const long long len = entries[11 * i + 1];
+    if (len > 0) count += (len + kRun - 1) / kRun;
+  }
+  return count;
 }
 
 long long symm_copy2d_pieces(const long long* six, int n) {

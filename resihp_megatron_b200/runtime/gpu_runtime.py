@@ -249,6 +249,152 @@ class HeteroParamSync:
         pass
 
 
+class HeteroFusedSync(HeteroParamSync):
+    """``HeteroParamSync`` on NVLink peer memory: every rank packs its slices of each holder set
+    into its own region of a symmetric heap (one strided-copy launch), and after a bounded barrier
+    sums every slice of its sets from all holders' regions in rank order (one launch; every holder
+    computes the same bits), unpacks the sums into its gradient (one launch) and passes a second
+    barrier before its region may be rewritten.  The piece tables are built once and stay on the
+    device.  Region offsets of every rank follow from the plan (each rank's sets in sorted order),
+    so no layout is exchanged.  Falls back to the library path when a slice is not 16-byte aligned
+    or a set has more than 8 holders."""
+
+    impl = "hetero-fused"
+
+    def __init__(self, plan: HeteroParallelPlan, stage: int, me: int, comms, device, *, exchange=None, abort=None,
+                 budget_s: float = 60.0, waiter=None, _heap=None, _ranks=None):
+        super().__init__(plan, stage, me, comms, device, waiter)
+        self.exchange, self.abort, self.budget = exchange, abort, budget_s
+        self.ranks = _ranks or tuple(sorted(r for g in plan.groups_at(stage) for r in plan.ranks(g)))
+        self._heap_in = _heap
+        self.heap = None
+        self.fused = False
+
+    def _all_sets(self, P) -> dict[tuple[int, ...], list[tuple[str, int, int]]]:
+        """Every holder set of the stage with its pieces ``(name, global interval start, length)``."""
+        tp_slices = self.plan.tp_slices(self.stage)
+        out: dict[tuple[int, ...], list[tuple[str, int, int]]] = {}
+        for name in P.order:
+            sp = P.specs[name]
+            if sp.shard_dim is None:
+                continue
+            n = sp.full_shape[sp.shard_dim]
+            parts = [even_split(n, len(sl)) for sl in tp_slices]
+            for iv in refine(parts):
+                holders = tuple(sorted(self.plan.rank(sl[locate(part, iv)]) for sl, part in zip(tp_slices, parts)))
+                if len(holders) > 1:
+                    out.setdefault(holders, []).append((name, iv[0], iv[1] - iv[0]))
+        return out
+
+    def attach(self, P) -> None:
+        super().attach(P)
+        sets = self._all_sets(P)
+
+        def piece_numel(name: str, ln: int) -> int:
+            sp = P.specs[name]
+            other = 1
+            for d, v in enumerate(sp.full_shape):
+                if d != sp.shard_dim:
+                    other *= v
+            return ln * other
+
+        size = {h: sum(piece_numel(nm, ln) for nm, _, ln in pcs) for h, pcs in sets.items()}
+        offsets: dict[int, dict[tuple[int, ...], int]] = {}
+        totals = {}
+        for r in self.ranks:
+            off = 0
+            offsets[r] = {}
+            for h in sorted(sets):
+                if r in h:
+                    offsets[r][h] = off
+                    off += (size[h] + 3) // 4 * 4  # 16-byte aligned regions
+            totals[r] = off
+        mine = sorted(self.slices)
+        if not mine or any(len(h) > 8 for h in mine):
+            return
+        # piece geometry of this rank's slices: (grad pointer offset bytes, rows, row bytes, pitch bytes)
+        geo = []
+        for h in mine:
+            poff = 0
+            for name, dim, lo, ln in self.slices[h]:
+                g = P.g(name)
+                if dim == 0:
+                    row = g[0].numel() if g.dim() > 1 else 1
+                    item = (g.data_ptr() + lo * row * 4, 1, ln * row * 4, ln * row * 4)
+                else:
+                    item = (g.data_ptr() + lo * 4, g.shape[0], ln * 4, g.shape[1] * 4)
+                geo.append((h, poff, *item))
+                poff += piece_numel(name, ln)
+        if any((a | c | d) & 15 for _, _, a, _, c, d in geo) or any(o & 3 for _, o, *_ in geo):
+            return  # not 16-byte aligned: keep the library path
+        from ..parallel.symm import SymmetricHeap
+
+        cap = max(max(totals.values()), 64)
+        idx = self.ranks.index(self.me)
+        self.heap = self._heap_in or SymmetricHeap({"region": (cap, torch.float32)}, idx, len(self.ranks),
+                                                   self.exchange, self.device, self.abort)
+        base = self.heap.peer_ptrs("region")
+        self.scratch = torch.empty(max(totals[self.me], 4), dtype=torch.float32, device=self.device)
+        pack, unpack = [], []
+        for h, poff, src, rows, row_bytes, pitch in geo:
+            dst = base[idx] + (offsets[self.me][h] + poff) * 4
+            scr = self.scratch.data_ptr() + (offsets[self.me][h] + poff) * 4
+            pack += [src, dst, rows, row_bytes, pitch, row_bytes]
+            unpack += [scr, src, rows, row_bytes, row_bytes, pitch]
+        sums = []
+        for h in mine:
+            srcs = [base[self.ranks.index(r)] + offsets[r][h] * 4 for r in h]
+            sums += [self.scratch.data_ptr() + offsets[self.me][h] * 4, size[h], len(h)] + srcs + [0] * (8 - len(h))
+        dev = self.device.index if self.device.index is not None else 0
+        from ..ops._build import ext
+
+        self.pack_t, self.pack_n = ext().symm_copy2d_build(pack, dev)
+        self.unpack_t, self.unpack_n = ext().symm_copy2d_build(unpack, dev)
+        self.sum_t, self.sum_n = ext().symm_sum_build(sums, dev)
+        self.fused = True
+
+    # the three phases (emulated ranks in one process call them in turn, without barriers)
+    def pack(self) -> None:
+        from ..ops._build import ext
+
+        ext().symm_copy2d_run(self.pack_t, self.pack_n)
+        ops.count(1)
+
+    def sum(self) -> None:
+        from ..ops._build import ext
+
+        ext().symm_sum_run(self.sum_t, self.sum_n)
+        ops.count(1)
+
+    def unpack(self) -> None:
+        from ..ops._build import ext
+
+        ext().symm_copy2d_run(self.unpack_t, self.unpack_n)
+        ops.count(1)
+
+    def reduce(self) -> None:
+        if not self.fused:
+            return super().reduce()
+        self.pack()
+        self.heap.barrier(self.budget)  # every holder's slices are in its region
+        self.sum()
+        self.heap.barrier(self.budget)  # every region has been read: it may be rewritten next step
+        self.unpack()
+        ops.count(2)
+
+    def check(self) -> None:
+        if self.heap is not None and self._heap_in is None:
+            self.heap.check()
+
+    def close(self) -> None:
+        if self.heap is not None and self._heap_in is None:
+            self.heap.close()
+        self.heap = None
+
+    def close(self) -> None:
+        pass
+
+
 class GPUHybridRuntime:
     def __init__(self, cfg: GPTConfig, plan: HeteroParallelPlan, schedule: Schedule, comms, mgr, *, device,
                  micro_batch: int = 1, seq_len: int | None = None, tokens: TokenSource | None = None,
@@ -316,6 +462,12 @@ class GPUHybridRuntime:
                 shd_ranks = tuple(sorted(plan.ranks(h)[tp_rank] for h in stage_groups))
                 shd_sync = ParamSetSync(shd_ranks, comms.rank, comms.group(shard_group_name(c.stage, tp_rank)), dp_impl,
                                         self.device, abort=self.abort, budget_s=budget_s, waiter=waiter, zero=zero)
+            elif dp_impl == "fused" and self.device.type == "cuda":
+                from ..parallel.symm import exchange_via_group
+
+                shd_sync = HeteroFusedSync(plan, c.stage, comms.rank, comms, self.device,
+                                           exchange=exchange_via_group(comms.group(replicated_group_name(c.stage))),
+                                           abort=self.abort, budget_s=budget_s, waiter=waiter)
             else:
                 shd_sync = HeteroParamSync(plan, c.stage, comms.rank, comms, self.device, waiter=waiter)
             rep_sync = ParamSetSync(rep_ranks, comms.rank, comms.group(replicated_group_name(c.stage)), dp_impl,
