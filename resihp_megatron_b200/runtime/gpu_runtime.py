@@ -310,8 +310,6 @@ class HeteroFusedSync(HeteroParamSync):
                     off += (size[h] + 3) // 4 * 4  # 16-byte aligned regions
             totals[r] = off
         mine = sorted(self.slices)
-        if not mine or any(len(h) > 8 for h in mine):
-            return
         # piece geometry of this rank's slices: (grad pointer offset bytes, rows, row bytes, pitch bytes)
         geo = []
         for h in mine:
@@ -325,8 +323,15 @@ class HeteroFusedSync(HeteroParamSync):
                     item = (g.data_ptr() + lo * 4, g.shape[0], ln * 4, g.shape[1] * 4)
                 geo.append((h, poff, *item))
                 poff += piece_numel(name, ln)
-        if any((a | c | d) & 15 for _, _, a, _, c, d in geo) or any(o & 3 for _, o, *_ in geo):
-            return  # not 16-byte aligned: keep the library path
+        ok = bool(mine) and all(len(h) <= 8 for h in mine)
+        ok = ok and not any((a | c | d) & 15 for _, _, a, _, c, d in geo) and not any(o & 3 for _, o, *_ in geo)
+        if self.comms is not None:  # every rank of the stage takes the same path (the heap is collective)
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+            self.wait(dist.all_reduce(flag, op=dist.ReduceOp.MIN,
+                                      group=self.comms.group(replicated_group_name(self.stage)), async_op=True))
+            ok = bool(flag.item())
+        if not ok:
+            return  # a slice that is not 16-byte aligned or a set of more than 8 holders: library path
         from ..parallel.symm import SymmetricHeap
 
         cap = max(max(totals.values()), 64)
