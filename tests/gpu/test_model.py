@@ -176,3 +176,32 @@ def test_fp8_training_tracks_bf16_and_reduces_loss():
     assert f8[-1] < f8[0]
     h = tr.model.f8.history
     assert (h[:, :, :6] > 0).all() and (h[:, :, 6:] == 0).all() and not tr.model.f8.has_nonfinite()
+
+
+def test_fp8_step_replays_as_a_cuda_graph_exactly_like_eager():
+    """The fp8 step (weight quantisation, fused norm / activation producers, fp8 GEMMs, amax
+    reduction into the history, Adam) allocates nothing and never syncs, so it captures: replays
+    train bit for bit like eager steps, and the history keeps one entry per step."""
+    from resihp_megatron_b200.models.config import TINY
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.train.gpu_trainer import GPUTrainer
+
+    cfg = TINY.with_(hidden=256, heads=2, kv_heads=2, ffn=512, layers=2, vocab_size=512, mlp="gelu")
+    g = torch.Generator().manual_seed(8)
+    batches = [torch.randint(0, cfg.vocab_size, (2, 129), generator=g) for _ in range(5)]
+    dev = [(b[:, :-1].contiguous().cuda(), b[:, 1:].contiguous().cuda()) for b in batches]
+
+    def run(graph: bool):
+        tr = GPUTrainer(cfg, global_batch=2, micro_batch=1, seq_len=128, lr=3e-3, device="cuda", fp8=Fp8Recipe())
+        losses = []
+        for i, (ids, lab) in enumerate(dev):
+            if graph and i == 2:
+                tr.capture_graphs()
+            losses.append(tr.step_device(ids, lab).item())
+        return losses, tr.model.params.bf16.clone(), tr.model.f8.history.clone()
+
+    eager, w0, h0 = run(False)
+    graphed, w1, h1 = run(True)
+    assert eager == graphed, (eager, graphed)
+    assert torch.equal(w0, w1) and torch.equal(h0, h1)
+    assert (h0[:, :, :5] > 0).all() and (h0[:, :, 5:] == 0).all()
