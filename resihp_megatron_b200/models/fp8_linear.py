@@ -17,7 +17,8 @@ rank (one all-reduce for all layers) and pushed into a per-layer history of ``hi
 the delayed-scaling state of the reference (``resihp/runtime/reference_model.py:204-227``,
 reduced in ``resihp/runtime/hetero_runtime.py:122-134``), which migrates with its layer
 (``layers.<l>.amax_history``, ``[12, history]``) and rolls back with an aborted iteration.  A
-non-finite reduced amax marks the iteration's gradients as unusable (``has_nonfinite``).
+non-finite reduced amax marks the iteration's gradients as unusable (``has_nonfinite``); with
+``Fp8Recipe.skip_nonfinite`` the trainers then drop the iteration instead of applying it.
 """
 
 from __future__ import annotations
@@ -39,6 +40,7 @@ class Fp8Recipe:
     fwd: str = "e4m3"  # forward operands (activations, weights)
     bwd: str = "e5m2"  # output gradients
     history: int = 16  # amax history length per recorded tensor
+    skip_nonfinite: bool = False  # drop an iteration whose reduced amax is inf / NaN (one host read per step)
 
     @property
     def fwd_fmt(self) -> int:
@@ -75,9 +77,11 @@ class Fp8Linears:
         return self.pending[i, j:j + 1]
 
     def finish_iteration(self, reduce_max=None) -> None:
-        """``reduce_max(t)``: in-place MAX all-reduce over every rank (None: one rank)."""
+        """``reduce_max(t)``: in-place MAX all-reduce over every rank (None: one rank), given the
+        int32 view of the pending amaxes -- their bit patterns order like the magnitudes and a
+        NaN stays the largest, which a floating-point MAX would not guarantee."""
         if reduce_max is not None:
-            reduce_max(self.pending)
+            reduce_max(self.pending.view(torch.int32))
         fp8.amax_history_push(self.history, self.pending)
 
     def has_nonfinite(self) -> bool:

@@ -547,7 +547,8 @@ class GPUHybridRuntime:
         self._amax.zero_()
         for st in stages:
             self._amax[st.layer_ids] = st.f8.pending
-        work = dist.all_reduce(self._amax, op=dist.ReduceOp.MAX, async_op=True)
+        # MAX over the bit patterns (non-negative floats order like ints; NaN stays the largest)
+        work = dist.all_reduce(self._amax.view(torch.int32), op=dist.ReduceOp.MAX, async_op=True)
         if self.mgr is not None:
             self.mgr.guarded_wait(work, what="amax all-reduce")
         else:
@@ -555,6 +556,10 @@ class GPUHybridRuntime:
         for st in stages:
             st.f8.pending.copy_(self._amax[st.layer_ids])
             st.f8.finish_iteration()
+
+    def fp8_nonfinite(self) -> bool:
+        """Whether the iteration's reduced amax of any layer of this rank is inf / NaN."""
+        return any(ch[0].f8.has_nonfinite() for ch in self.chunks.values() if ch[0].f8 is not None)
 
     def after_backward(self, iteration: int) -> None:
         """Between the last backward of an iteration and the gradient reduction: the replicated
@@ -577,8 +582,14 @@ class GPUHybridRuntime:
         it = self.iteration if iteration is None else iteration
         self.interp.run(it)
         self.after_backward(it)
-        for sync in self._syncs():
-            sync.reduce()
+        if self.fp8 is not None and self.fp8.skip_nonfinite and self.fp8_nonfinite():
+            # every rank sees the same reduced amax, so every rank drops the iteration
+            self.discard_grads()
+            self.skipped_steps = getattr(self, "skipped_steps", 0) + 1
+            step = None
+        else:
+            for sync in self._syncs():
+                sync.reduce()
         if step:
             self.apply_step()
         loss = self.executor.loss_sum.clone()

@@ -164,6 +164,13 @@ class GPUTrainer:
             m.forward_backward(ids[i * mb:(i + 1) * mb].reshape(-1), labels[i * mb:(i + 1) * mb].reshape(-1), scale)
         if m.f8 is not None:  # the amax reduction (one MAX all-reduce) and the history update
             m.f8.finish_iteration(self._reduce_max if self.dp > 1 else None)
+            if m.f8.recipe.skip_nonfinite and m.f8.has_nonfinite():  # every rank sees the same amax
+                m.params.grad.zero_()
+                if self.dp > 1:
+                    dist.all_reduce(m.loss_acc, group=self.group)
+                self.skipped_steps = getattr(self, "skipped_steps", 0) + 1
+                self.step_count += 1
+                return m.loss_acc / self.tokens_per_step
         self._reduce_and_update()
         self.step_count += 1
         return m.loss_acc / self.tokens_per_step

@@ -115,3 +115,24 @@ def test_single_rank_tp_stage_equals_the_model_in_fp8(fakes):
         assert torch.equal(st.wqkv(p, grad=True), M.g(p + "wqkv"))
         assert torch.equal(st.w13(p, grad=True), M.g(p + "w1"))
         assert torch.equal(P.g(p + "w2"), M.g(p + "w2"))
+
+
+def test_nonfinite_amax_skips_the_step(fakes):
+    """With ``skip_nonfinite`` an iteration whose reduced amax is inf / NaN leaves the weights and
+    the optimizer untouched (every rank sees the same reduced amax, so every rank skips)."""
+    from resihp_megatron_b200.models.fp8_linear import Fp8Recipe
+    from resihp_megatron_b200.train.gpu_trainer import GPUTrainer
+
+    tr = GPUTrainer(CFG, global_batch=1, micro_batch=1, seq_len=128, device="cpu", lr=1e-2,
+                    fp8=Fp8Recipe(skip_nonfinite=True))
+    ids, labels = _batch()
+    ids, labels = ids.view(1, -1), labels.view(1, -1)
+    tr.step_device(ids, labels)
+    assert getattr(tr, "skipped_steps", 0) == 0 and tr.model.params.step == 1
+    P = tr.model.params
+    w = P.w("layers.1.w2")
+    w[0, 0] = float("inf")  # a diverged weight: its amax (and the step's outputs) are no longer finite
+    before = P.master.clone()
+    tr.step_device(ids, labels)
+    assert tr.skipped_steps == 1 and P.step == 1 and torch.equal(P.master, before)
+    assert tr.model.f8.has_nonfinite()
