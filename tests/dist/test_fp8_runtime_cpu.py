@@ -25,7 +25,7 @@ def _histories(tr):
     return {k: v.clone() for k, v in tr.runtime.buffers().items()}
 
 
-def _worker(rank, world, port, store_addr, layout, steps, leaving=None, directory=None, phase=None):
+def _worker(rank, world, port, store_addr, layout, steps, leaving=None, directory=None, phase=None, sp=True):
     import torch.distributed as dist
 
     from tests.helpers import fake_kernels
@@ -37,7 +37,8 @@ def _worker(rank, world, port, store_addr, layout, steps, leaving=None, director
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     tp, pp, dp = layout
     tr = GPUHybridTrainer(_cfg(), tp=tp, pp=pp, dp=dp, global_batch=8, micro_batch=1, seq_len=S,
-                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2, fp8=Fp8Recipe())
+                          tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2, fp8=Fp8Recipe(),
+                          sequence_parallel=sp)
     out = {}
     if phase == "load":
         out["loaded"] = tr.load_checkpoint(directory)
@@ -153,3 +154,14 @@ def test_fp8_live_reshard_tp2_to_tp1_keeps_the_run(store):
         assert out["layout"].startswith("tp1pp1dp4") and out["phases"]["transfers"] > 0
         for a, b in zip(out["losses"], ref):
             assert abs(a - b) <= 3e-2 * abs(b), (r, out["losses"], ref)
+
+
+def test_fp8_plain_tensor_parallelism_tracks_one_rank(store):
+    """fp8 without sequence parallelism: replicated rows, every rank quantises the whole input of
+    a column-parallel projection, row-parallel outputs all-reduced."""
+    one = spawn(_worker, 1, store, (1, 1, 1), 2, timeout=300)
+    many = spawn(_worker, 4, store, (2, 2, 1), 2, None, None, None, False, timeout=400)
+    ref = one[0]["losses"]
+    for r, res in many.items():
+        for a, b in zip(res["losses"], ref):
+            assert abs(a - b) <= 2e-2 * abs(b), (r, res["losses"], ref)
