@@ -107,6 +107,7 @@ class ExpertSlowMonitor:
         per = [t / n if n > 0 and t > 0 else None for t, n in zip(times_ms, rows)]
         seen = [p for p in per if p is not None]
         self.history.append(per)
+        del self.history[:-256]  # a bounded record of the recent series
         if len(seen) < max(2, self.world // 2 + 1):  # too few ranks did expert work this step
             return {}
         pred = statistics.median(seen)
