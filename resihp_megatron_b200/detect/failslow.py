@@ -69,6 +69,8 @@ class FailSlowDetector:
         before = self.bocd.snapshot()
         self.bocd.update(x)
         self.xs.append(x)
+        if len(self.xs) > 4096:  # long runs: only the recent series is ever compared
+            del self.xs[:-2048]
         if self.calibrate and len(self.xs) == self.warmup:
             mean = statistics.fmean(self.xs)
             sigma = max(statistics.pstdev(self.xs), self.sigma_floor)
