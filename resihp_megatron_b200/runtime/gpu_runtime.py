@@ -289,6 +289,14 @@ class HeteroFusedSync(HeteroParamSync):
 
     def attach(self, P) -> None:
         super().attach(P)
+        sets, size, offsets, totals, geo = self.layout(P)
+        self._build(P, sets, size, offsets, totals, geo)
+
+    def layout(self, P):
+        """``(sets, size, offsets, totals, geo)``: every holder set of the stage with its pieces,
+        each set's element count, every rank's region offset of each of its sets (elements), every
+        rank's region total, and this rank's pieces ``(set, offset in the set's region, grad
+        pointer, rows, row bytes, row pitch)`` -- pure index arithmetic from the plan and specs."""
         sets = self._all_sets(P)
 
         def piece_numel(name: str, ln: int) -> int:
@@ -324,6 +332,10 @@ class HeteroFusedSync(HeteroParamSync):
                     item = (g.data_ptr() + lo * 4, g.shape[0], ln * 4, g.shape[1] * 4)
                 geo.append((h, poff, *item))
                 poff += piece_numel(name, ln)
+        return sets, size, offsets, totals, geo
+
+    def _build(self, P, sets, size, offsets, totals, geo) -> None:
+        mine = sorted(self.slices)
         ok = bool(mine) and all(len(h) <= 8 for h in mine)
         ok = ok and not any((a | c | d) & 15 for _, _, a, _, c, d in geo) and not any(o & 3 for _, o, *_ in geo)
         if self.comms is not None:  # every rank of the stage takes the same path (the heap is collective)
