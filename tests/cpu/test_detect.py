@@ -220,3 +220,27 @@ def test_a_change_that_needs_several_samples_to_be_sure_of_is_still_reported():
     d = FailSlowDetector("residual", warmup=6, threshold=0.9, min_increase=0.5, cooldown=6, window=8)
     hits = [i for i, x in enumerate(xs) if d.observe(i, math.exp(x), 1.0)]
     assert hits and 18 <= hits[0] <= 24, hits
+
+
+def test_expert_slow_monitor_flags_only_the_slow_rank():
+    """Per-row expert times of 8 ranks with 3 % jitter and uneven routing (some ranks get no rows
+    in some steps): rank 5 slows 2x at step 20 and is the only one flagged, with a speed near 0.5."""
+    import random
+
+    from resihp_megatron_b200.train.moe_failslow import ExpertSlowMonitor
+
+    rng = random.Random(3)
+    mon = ExpertSlowMonitor(8, warmup=8)
+    flagged = []
+    for it in range(40):
+        rows = [0 if rng.random() < 0.1 else rng.randint(200, 900) for _ in range(8)]
+        times = [n * 0.01 * (1 + 0.03 * (2 * rng.random() - 1)) * (2.0 if r == 5 and it >= 20 else 1.0)
+                 for r, n in enumerate(rows)]
+        out = mon.observe(it, times, rows)
+        if out:
+            flagged.append((it, out))
+            mon.reset()
+    assert flagged, "the slow rank was not detected"
+    it, speeds = flagged[0]
+    assert 20 <= it <= 26 and set(speeds) == {5} and 0.4 < speeds[5] < 0.6, flagged
+    assert all(set(s) == {5} for _, s in flagged)
