@@ -55,6 +55,18 @@ def history_key(layer: int) -> str:
     return f"layers.{layer}.amax_history"
 
 
+def check_shapes(cfg, tokens: int, tp: int = 1) -> None:
+    """Every fp8 GEMM dimension must be a multiple of the 128-wide blocks: the tokens of a
+    micro-batch, the hidden size and each rank's share of the heads and of the FFN."""
+    D = cfg.head_dim
+    dims = {"tokens per micro-batch": tokens, "hidden": cfg.hidden,
+            "query heads x head dim per rank": cfg.heads * D // tp,
+            "q / k / v rows per rank": (cfg.heads + 2 * cfg.kv_heads) * D // tp, "ffn per rank": cfg.ffn // tp}
+    bad = {k: v for k, v in dims.items() if v % 128}
+    if bad:
+        raise ValueError(f"fp8 needs multiples of 128: {bad}")
+
+
 class Fp8Linears:
     """fp8 state of a contiguous set of decoder layers on one rank."""
 

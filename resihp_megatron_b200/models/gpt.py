@@ -118,8 +118,9 @@ class LlamaModel:
         self.fc1 = fc1_name(cfg)
         self.f8 = None
         if fp8 is not None:
-            from .fp8_linear import Fp8Linears
+            from .fp8_linear import Fp8Linears, check_shapes
 
+            check_shapes(cfg, self.T)
             self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
         self._alloc()
 

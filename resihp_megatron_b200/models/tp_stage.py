@@ -169,8 +169,9 @@ class TPStage:
         self.deferred: dict[object, list] = {}
         self.f8 = None
         if fp8 is not None:
-            from .fp8_linear import Fp8Linears
+            from .fp8_linear import Fp8Linears, check_shapes
 
+            check_shapes(cfg, self.T, self.tp_size)
             self.f8 = Fp8Linears(self.layer_ids, self.device, fp8)
 
     # ------------------------------------------------------------------ parameter views

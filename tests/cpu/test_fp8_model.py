@@ -136,3 +136,13 @@ def test_nonfinite_amax_skips_the_step(fakes):
     tr.step_device(ids, labels)
     assert tr.skipped_steps == 1 and P.step == 1 and torch.equal(P.master, before)
     assert tr.model.f8.has_nonfinite()
+
+
+def test_fp8_rejects_shapes_off_the_128_blocks():
+    from resihp_megatron_b200.models.fp8_linear import check_shapes
+
+    check_shapes(CFG, 128)
+    with pytest.raises(ValueError, match="tokens"):
+        check_shapes(CFG, 100)
+    with pytest.raises(ValueError, match="ffn"):
+        check_shapes(CFG.with_(ffn=640), 128, tp=2)  # 320 per rank
