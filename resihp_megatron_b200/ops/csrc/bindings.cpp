@@ -708,8 +708,9 @@ static void check_scale(const torch::Tensor& s, int64_t kb, int64_t row, int64_t
                         const char* name) {
   CHECK_F32(s);
   TORCH_CHECK(kb >= 0 && row >= 0 && (shift == 0 || shift == 7), name, ": bad scale addressing");
+  TORCH_CHECK(rows > 0 && K >= 128 && K % 128 == 0, name, ": needs rows > 0 and K a positive multiple of 128");
   const long long last = (static_cast<long long>(K / 128) - 1) * kb + static_cast<long long>((rows - 1) >> shift) * row;
-  TORCH_CHECK(last < s.numel(), name, ": scale tensor too small for its addressing");
+  TORCH_CHECK(last >= 0 && last < s.numel(), name, ": scale tensor too small for its addressing");
 }
 
 // out[M, N] (+)= alpha * sum_kb sa(m, kb) sb(n, kb) (a[m, kb] . b[n, kb])
@@ -719,6 +720,14 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
               const c10::optional<torch::Tensor>& residual, const std::vector<int64_t>& rs_ptrs, int64_t rs_slot) {
   check_fp8(a, "a");
   check_fp8(b, "b");
+  // Every shape rule of the kernel is checked here, before any pointer or tensor map is formed.
+  TORCH_CHECK(a.size(0) > 0 && a.size(1) > 0 && b.size(0) > 0 && a.size(0) % 128 == 0 && a.size(1) % 128 == 0 &&
+                  b.size(0) % 128 == 0,
+              "gemm_fp8: M, N and K must be positive multiples of 128");
+  TORCH_CHECK(a_fmt == 0 || a_fmt == 1, "gemm_fp8: a_fmt is 0 (E4M3) or 1 (E5M2)");
+  TORCH_CHECK(b_fmt == 0 || b_fmt == 1, "gemm_fp8: b_fmt is 0 (E4M3) or 1 (E5M2)");
+  TORCH_CHECK(epi >= 0 && epi <= 4, "gemm_fp8: epi is 0..4");
+  TORCH_CHECK(a.device() == b.device(), "gemm_fp8: a and b on different devices");
   const int M = a.size(0), K = a.size(1), N = b.size(0);
   TORCH_CHECK(b.size(1) == K, "gemm_fp8: contraction sizes differ");
   void* dptr = nullptr;

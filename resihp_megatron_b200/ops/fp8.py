@@ -197,13 +197,50 @@ def _u8(t):
     return None if t is None else t.view(torch.uint8)
 
 
+class Fp8ShapeError(ValueError, RuntimeError):
+    """A block-scaled GEMM was given operands the kernel cannot take (raised in Python, before
+    any native call)."""
+
+
+def _check_operand(op: Fp8Operand, name: str) -> None:
+    d = op.data
+    if d.dim() != 2 or d.element_size() != 1 or not d.is_contiguous():
+        raise Fp8ShapeError(f"{name}: data must be a contiguous 2-D tensor of 1-byte elements, got "
+                            f"{tuple(d.shape)} {d.dtype}")
+    rows, K = d.shape
+    if rows <= 0 or K <= 0 or rows % BLOCK or K % BLOCK:
+        raise Fp8ShapeError(f"{name}: rows and K must be positive multiples of {BLOCK}, got [{rows}, {K}]")
+    if op.shift not in (0, 7) or op.kb_stride < 0 or op.row_stride < 0:
+        raise Fp8ShapeError(f"{name}: bad scale addressing (kb_stride={op.kb_stride}, "
+                            f"row_stride={op.row_stride}, shift={op.shift})")
+    s = op.scale
+    if s.dtype != torch.float32 or not s.is_contiguous():
+        raise Fp8ShapeError(f"{name}: scales must be contiguous fp32")
+    last = (K // BLOCK - 1) * op.kb_stride + ((rows - 1) >> op.shift) * op.row_stride
+    if last >= s.numel():
+        raise Fp8ShapeError(f"{name}: {s.numel()} scales cannot cover index {last}")
+    if op.fmt not in DTYPES:
+        raise Fp8ShapeError(f"{name}: unknown fp8 format {op.fmt}")
+
+
+def _check_operands(a: Fp8Operand, b: Fp8Operand) -> None:
+    _check_operand(a, "a")
+    _check_operand(b, "b")
+    if a.K != b.K:
+        raise Fp8ShapeError(f"contraction sizes differ: a has K={a.K}, b has K={b.K}")
+    if a.data.device != b.data.device:
+        raise Fp8ShapeError("a and b live on different devices")
+
+
 def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
          accumulate: bool = False, alpha: float = 1.0, residual: torch.Tensor | None = None,
          scatter: tuple[list[int], int] | None = None) -> torch.Tensor | None:
     """``out [a.rows, b.rows] (+)= alpha * block-scaled a @ b^T`` (all dims multiples of 128).
     ``residual``: bf16 ``out = product + residual``.  ``scatter = (recv_ptrs, slot)``: no local
     output; row ``m`` is stored (bf16) into rank ``m // (rows / world)``'s receive buffer
-    ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter."""
+    ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter.
+    Shapes and scale addressing are validated here, before the extension is called."""
+    _check_operands(a, b)
     if scatter is not None:
         ptrs, slot = scatter
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,

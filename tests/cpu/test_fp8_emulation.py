@@ -101,3 +101,29 @@ def test_rejects_unaligned_shapes():
         fp8.Fp8Tensor.empty(128, 200)
     assert math.isclose(1.75 * 2 ** fp8.MAX_EXP[fp8.E4M3], 448.0)
     assert math.isclose(1.75 * 2 ** fp8.MAX_EXP[fp8.E5M2], 57344.0)
+
+
+def test_gemm_validates_shapes_and_scales_before_any_native_call(monkeypatch):
+    """Every operand rule of the fp8 GEMM is checked in Python: a bad shape or a scale vector too
+    short for its addressing never reaches the extension."""
+
+    def _no_native_call():
+        raise AssertionError("a bad operand reached the extension")
+
+    monkeypatch.setattr(fp8, "ext", _no_native_call)
+    q = fp8.quantize_reference(torch.ones(128, 256).bfloat16())
+    good = q.rowwise()
+    short_k = fp8.Fp8Operand(good.data[:, :64].contiguous(), good.scale, good.kb_stride, 1, 0, fp8.E4M3)
+    with pytest.raises(fp8.Fp8ShapeError, match="multiples of 128"):
+        fp8.gemm(short_k, short_k)
+    few_scales = fp8.Fp8Operand(good.data, good.scale[:1].contiguous(), good.kb_stride, 1, 0, fp8.E4M3)
+    with pytest.raises(fp8.Fp8ShapeError, match="cannot cover"):
+        fp8.gemm(few_scales, good)
+    bad_shift = fp8.Fp8Operand(good.data, good.scale, good.kb_stride, 1, 3, fp8.E4M3)
+    with pytest.raises(fp8.Fp8ShapeError, match="addressing"):
+        fp8.gemm(good, bad_shift)
+    other_k = fp8.quantize_reference(torch.ones(128, 384).bfloat16()).rowwise()
+    with pytest.raises(fp8.Fp8ShapeError, match="contraction"):
+        fp8.gemm(good, other_k)
+    # the error is both a ValueError and a RuntimeError (callers catching either keep working)
+    assert issubclass(fp8.Fp8ShapeError, ValueError) and issubclass(fp8.Fp8ShapeError, RuntimeError)

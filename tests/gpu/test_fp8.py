@@ -78,11 +78,21 @@ def test_gemm_forward_dgrad_wgrad(M, N, K):
     assert ((y - full).norm() / full.norm()).item() < 0.05
 
 
-def test_gemm_rejects_unaligned():
+def test_gemm_rejects_unaligned(monkeypatch):
     a = fp8.quantize(_x(128, 128), fp8.E4M3)
-    with pytest.raises(RuntimeError):
-        bad = fp8.Fp8Operand(a.q_row[:, :64].contiguous(), a.s_row, 128, 1, 0, fp8.E4M3)
+    torch.cuda.synchronize()
+    bad = fp8.Fp8Operand(a.q_row[:, :64].contiguous(), a.s_row, 128, 1, 0, fp8.E4M3)
+
+    def _no_native_call():
+        raise AssertionError("a bad shape reached the extension")
+
+    # the shape error is raised in Python, before the extension is touched
+    monkeypatch.setattr(fp8, "ext", _no_native_call)
+    with pytest.raises(fp8.Fp8ShapeError, match="multiples of 128"):
         fp8.gemm(bad, bad)
+    with pytest.raises(fp8.Fp8ShapeError, match="contraction"):
+        fp8.gemm(a.rowwise(), fp8.Fp8Operand(torch.zeros(128, 256, dtype=torch.uint8, device="cuda"),
+                                             torch.ones(256, device="cuda"), 128, 1, 0, fp8.E4M3))
 
 
 def test_gelu_fwd_bwd():
