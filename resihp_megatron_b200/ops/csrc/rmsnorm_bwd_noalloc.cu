@@ -17,19 +17,40 @@ static __device__ __align__(256) float g_rmsnorm_scratch[RB_NOALLOC_SCRATCH_FLOA
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 float* g_scratch_ptr[kMaxDevices] = {};
+void* g_scratch_ctx[kMaxDevices] = {};  // the context the cached address belongs to
 
-// Device address of the scratch array on the current device (looked up once per device).
+// The current driver context, through the runtime's driver entry point (no link to libcuda).
+void* current_context() {
+  using GetCurrentFn = int (*)(void**);
+  static GetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<GetCurrentFn>(f);
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+// Device address of the scratch array on the current device.  Looked up once per device and
+// context: after a cudaDeviceReset (or any re-creation of the device's primary context) the
+// context handle changes, and the address is looked up again instead of reusing a stale one.
 int scratch_on_current_device(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return RB_NOALLOC_ERR_SYMBOL;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  void* ctx = current_context();
+  if (g_scratch_ptr[dev] == nullptr || ctx == nullptr || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_rmsnorm_scratch);
     if (e != cudaSuccess || p == nullptr) return RB_NOALLOC_ERR_SYMBOL;
     g_scratch_ptr[dev] = static_cast<float*>(p);
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return 0;

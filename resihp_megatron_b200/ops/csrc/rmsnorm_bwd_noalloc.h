@@ -19,8 +19,10 @@
 //  * Scratch needed: ceil(T / 32) * H floats.  Calls that need more return
 //    RB_NOALLOC_ERR_TOO_LARGE and launch nothing (e.g. H = 4096 allows T <= 4096 rows).
 //  * The first call on a device (with that device current) looks up the array's device
-//    address with cudaGetSymbolAddress and caches it; make that first call before any
-//    stream capture on that device.
+//    address with cudaGetSymbolAddress and caches it with the device's current context; make
+//    that first call before any stream capture on that device.  If the context changes (a
+//    cudaDeviceReset, or the primary context released and created again), the next call looks
+//    the address up again, so that call too should come outside a stream capture.
 //  * Every call on a device shares the one array, and the array keeps the previous call's
 //    contents.  The kernels overwrite every scratch element they read, so nothing needs
 //    clearing between calls.  Calls that overlap on the GPU (different streams without

@@ -34,30 +34,50 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
 
 
-def test_noalloc_rmsnorm_bwd_matches_allocating_entry_point():
+def _rmsnorm_bwd_fp32(x, w, dy, dres, dw0, accumulate, eps=1e-5):
+    """fp32 PyTorch oracle: autograd through ``y = x * rsqrt(mean(x^2) + eps) * w``."""
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf
+    y.backward(dy.float())
+    dx = xf.grad + (dres.float() if dres is not None else 0)
+    dw = wf.grad + (dw0 if accumulate else 0)
+    return dx, dw
+
+
+@pytest.mark.parametrize("accumulate", [0, 1])
+@pytest.mark.parametrize("with_dres", [False, True])
+def test_noalloc_rmsnorm_bwd_matches_allocating_entry_point(accumulate, with_dres):
     from resihp_megatron_b200 import ops
 
     fn, cap = _entry()
     assert cap() == 512 * 1024
     T, H = 1000, 4096
     stream = torch.cuda.current_stream().cuda_stream
-    g = torch.Generator(device="cuda").manual_seed(7)
+    g = torch.Generator(device="cuda").manual_seed(7 + 2 * accumulate + int(with_dres))
     x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
     w = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).bfloat16()
     _, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
     for call in range(2):  # two calls in a row: the second sees the first call's scratch contents
         dy = torch.randn(T, H, device="cuda", generator=g).bfloat16()
-        dres = torch.randn(T, H, device="cuda", generator=g).bfloat16()
-        dw_ref = torch.full((H,), 0.25, device="cuda")
-        dx_ref = ops.rmsnorm_bwd(x, w, rstd, dy, dw_ref, dres=dres, accumulate=True)
+        dres = torch.randn(T, H, device="cuda", generator=g).bfloat16() if with_dres else None
+        dw0 = torch.full((H,), 0.25, device="cuda")
+        dw_ref = dw0.clone()
+        dx_ref = ops.rmsnorm_bwd(x, w, rstd, dy, dw_ref, dres=dres, accumulate=bool(accumulate))
         dx = torch.empty_like(x)
-        dw = torch.full((H,), 0.25, device="cuda")
-        rc = fn(x.data_ptr(), w.data_ptr(), rstd.data_ptr(), dy.data_ptr(), dres.data_ptr(), dx.data_ptr(),
-                dw.data_ptr(), 1, T, H, stream)
+        dw = torch.full((H,), -7.0 if not accumulate else 0.25, device="cuda")  # overwritten unless accumulating
+        rc = fn(x.data_ptr(), w.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+                dres.data_ptr() if dres is not None else None, dx.data_ptr(), dw.data_ptr(), accumulate, T, H,
+                stream)
         torch.cuda.synchronize()
         assert rc == 0, f"call {call}: rb_rmsnorm_bwd_noalloc returned {rc}"
-        assert _rel(dx, dx_ref) < 1e-2, call
-        assert _rel(dw, dw_ref) < 1e-3, call
+        # the same kernels as the allocating entry point: the same bits
+        assert torch.equal(dx, dx_ref), call
+        assert torch.equal(dw, dw_ref), call
+        # and both agree with an fp32 PyTorch RMSNorm backward
+        dx32, dw32 = _rmsnorm_bwd_fp32(x, w, dy, dres, dw0, accumulate)
+        assert _rel(dx, dx32) < 1e-2, (call, _rel(dx, dx32))
+        assert _rel(dw, dw32) < 1e-3, (call, _rel(dw, dw32))
 
 
 def test_noalloc_rejects_oversized_calls():
