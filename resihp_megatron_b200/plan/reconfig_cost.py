@@ -1,14 +1,17 @@
-"""Price of a plan transition -- the ``buy`` side of the ski-rental policy.
+"""What a plan transition costs -- the ``buy`` price of the ski-rental policy.
 
-Replays the slice-level transfer plan the workers would execute between two plans (local
-reuse, striping, locality), charges each device the time of the bytes it sends or receives,
-and adds the communicator rebuild time.  ``bytes_per_elem`` defaults to 14 (bf16 weight +
-fp32 master + two fp32 Adam moments).  (Reference: ``resihp/plan/reconfig_cost.py:28-73``.)
+The estimate replays the slice-level transfer plan the workers would execute between the two
+plans (with local reuse, striping across holders and locality), charges every device for the
+bytes it sends or receives at the intra- or inter-node bandwidth, takes the busiest device as
+the migration time and adds the communicator rebuild.  ``bytes_per_elem`` defaults to 14: a
+bf16 weight, its fp32 master copy and two fp32 Adam moments.
+Parity: ``resihp/plan/reconfig_cost.py:28-73`` (same pricing model).
 """
 
 from __future__ import annotations
 
-from collections import defaultdict
+import math
+from collections import Counter
 from dataclasses import dataclass
 
 from .hetero_plan import HeteroParallelPlan
@@ -25,20 +28,27 @@ class ReconfigEstimate:
     rebuild_s: float
 
 
+# (registry name, rows, cols, TP partition dim) of one decoder layer; None cols = a vector
+def _layer_tensors(model: ModelSpec):
+    h = model.hidden
+    kv = model.num_kv_heads * (h // model.num_heads)
+    up = model.ffn * (2 if model.swiglu else 1)
+    yield "attn.qkv.weight", (h + 2 * kv, h), 0
+    yield "attn.proj.weight", (h, h), 1
+    yield "mlp.fc1.weight", (up, h), 0
+    yield "mlp.fc2.weight", (h, model.ffn), 1
+    yield "ln1.weight", (h,), None
+    yield "ln2.weight", (h,), None
+
+
 def gpt_layer_specs(model: ModelSpec) -> dict[str, TensorSpec]:
-    """Per-layer tensors of a GPT layer with their TP partition dimension."""
-    h, f = model.hidden, model.ffn
-    hd = h // model.num_heads
-    qkv = h + 2 * model.num_kv_heads * hd
-    fc1 = (2 if model.swiglu else 1) * f
-    specs = {}
-    for l in range(model.num_layers):
-        for name, shape, dim in (("attn.qkv.weight", (qkv, h), 0), ("attn.proj.weight", (h, h), 1),
-                                 ("mlp.fc1.weight", (fc1, h), 0), ("mlp.fc2.weight", (h, f), 1),
-                                 ("ln1.weight", (h,), None), ("ln2.weight", (h,), None)):
-            key = f"layers.{l}.{name}"
-            specs[key] = TensorSpec(key, shape, dim)
-    return specs
+    """Registry specs of every layer's tensors, keyed ``layers.{l}.{name}``."""
+    out = {}
+    for layer in range(model.num_layers):
+        for name, shape, dim in _layer_tensors(model):
+            key = f"layers.{layer}.{name}"
+            out[key] = TensorSpec(key, shape, dim)
+    return out
 
 
 def layer_of_key(key: str) -> int:
@@ -48,24 +58,19 @@ def layer_of_key(key: str) -> int:
 def estimate_reconfig_cost(old: HeteroParallelPlan | None, new: HeteroParallelPlan, specs: dict[str, TensorSpec], *,
                            bytes_per_elem: int = 14, inter_bw: float = 25e9, intra_bw: float = 300e9,
                            rebuild_s: float = 2.0, node_of: dict[str, str] | None = None) -> ReconfigEstimate:
-    if old is None:
+    if old is None:  # a fresh start moves no state
         return ReconfigEstimate(rebuild_s, 0, 0, rebuild_s)
-    node_of = node_of or {}
-    plan = plan_transfers(holdings(old, specs, layer_of_key), holdings(new, specs, layer_of_key),
-                          valid_sources=set(old.world) & set(new.world), node_of=node_of)
-    busy_s: dict[str, float] = defaultdict(float)
-    busy_b: dict[str, int] = defaultdict(int)
-    total = 0
-    for t in plan.transfers:
-        n = 1
-        for d in specs[t.key].local_shape(t.interval):
-            n *= d
-        b = n * bytes_per_elem
-        local = node_of.get(t.src) is not None and node_of.get(t.src) == node_of.get(t.dst)
-        secs = b / (intra_bw if local else inter_bw)
-        for dev in (t.src, t.dst):
-            busy_s[dev] += secs
-            busy_b[dev] += b
-        total += b
-    return ReconfigEstimate(rebuild_s + max(busy_s.values(), default=0.0), total, max(busy_b.values(), default=0),
+    where = node_of or {}
+    transfers = plan_transfers(holdings(old, specs, layer_of_key), holdings(new, specs, layer_of_key),
+                               valid_sources=set(old.world) & set(new.world), node_of=where).transfers
+    seconds_of, bytes_of = Counter(), Counter()
+    for t in transfers:
+        nbytes = bytes_per_elem * math.prod(specs[t.key].local_shape(t.interval))
+        same_node = where.get(t.src) is not None and where.get(t.src) == where.get(t.dst)
+        secs = nbytes / (intra_bw if same_node else inter_bw)
+        for dev in (t.src, t.dst):  # a copy occupies both ends
+            seconds_of[dev] += secs
+            bytes_of[dev] += nbytes
+    busiest = max(seconds_of.values(), default=0.0)
+    return ReconfigEstimate(rebuild_s + busiest, sum(bytes_of.values()) // 2, max(bytes_of.values(), default=0),
                             rebuild_s)

@@ -1,11 +1,12 @@
-"""TP subgroup selection after failures / slowdowns, without the power-of-two restriction.
+"""TP subgroup selection after failures or slowdowns, any degree (no power-of-two rule).
 
-``select_subgroup`` maximises ``k * eff(k) * min_{i in S_k} p_i`` over TP degrees ``k`` where
-``S_k`` is the top-``k`` devices by normalised speed (Eq. 4 of ResiHP); ties go to the larger
-group (more memory headroom), and among equally fast devices incumbents are kept so the
-transition moves the least state.  With context parallelism a degree ``k`` takes ``k * cp``
-devices.  Memory helpers give the smallest TP degree that fits and the most layers a group can
-hold.  (Reference: ``resihp/plan/tp_select.py:19-81``.)
+``select_subgroup`` implements Eq. 4 of ResiHP: over the feasible degrees ``k``, take the ``k``
+fastest candidates (``k * cp`` with context parallelism) and score the group by its throughput
+``k * eff(k) * (slowest member's speed)``.  The best score wins; a near-tie goes to the larger
+degree (more memory headroom).  Among equally fast devices the incumbents of the old group rank
+first, so a transition moves as little state as possible.  The memory helpers give the smallest
+degree a stage fits in and the most layers a group can hold.
+Parity: ``resihp/plan/tp_select.py:19-81`` (same selection rule and memory tests).
 """
 
 from __future__ import annotations
@@ -14,6 +15,8 @@ import math
 from dataclasses import dataclass
 
 from .model_spec import ModelProfile, ModelSpec
+
+_TIE = 1e-12
 
 
 @dataclass(frozen=True)
@@ -24,59 +27,63 @@ class TPChoice:
     standby: tuple[str, ...]
 
 
+def _is_pow2(k: int) -> bool:
+    return k & (k - 1) == 0
+
+
 def feasible_degrees(model: ModelSpec | None, max_k: int, min_k: int = 1, power_of_two_only: bool = False) -> list[int]:
-    out = []
-    for k in range(max(1, min_k), max_k + 1):
-        if power_of_two_only and (k & (k - 1)):
-            continue
-        if model is None or model.tp_feasible(k):
-            out.append(k)
-    return out
+    """TP degrees in ``[min_k, max_k]`` the model's layout can be split by."""
+    ks = range(max(1, min_k), max_k + 1)
+    return [k for k in ks if (not power_of_two_only or _is_pow2(k)) and (model is None or model.tp_feasible(k))]
 
 
-def _fits(model: ModelSpec, layers: int, tp: int, capacity: float, inflight: int, dp_shard: int, sp: bool,
-          extra: int) -> bool:
-    need = model.static_bytes(layers, tp, dp_shard, extra) + inflight * model.activation_bytes(layers, tp, sp)
-    return need <= capacity
+def _per_gpu_bytes(model: ModelSpec, layers: int, tp: int, inflight: int, dp_shard: int, sp: bool,
+                   extra: int) -> float:
+    return model.static_bytes(layers, tp, dp_shard, extra) + inflight * model.activation_bytes(layers, tp, sp)
 
 
 def min_tp_for_memory(model: ModelSpec, layers: int, capacity_bytes: float, inflight: int, *, dp_shard: int = 1,
                       sequence_parallel: bool = True, extra_params: int = 0, max_k: int = 64) -> int | None:
+    """Smallest feasible TP degree at which ``layers`` layers fit ``capacity_bytes`` per GPU."""
     if math.isinf(capacity_bytes):
         return 1
-    for k in range(1, max_k + 1):
-        if model.tp_feasible(k) and _fits(model, layers, k, capacity_bytes, inflight, dp_shard, sequence_parallel,
-                                          extra_params):
-            return k
-    return None
+    fitting = (k for k in feasible_degrees(model, max_k)
+               if _per_gpu_bytes(model, layers, k, inflight, dp_shard, sequence_parallel, extra_params)
+               <= capacity_bytes)
+    return next(fitting, None)
 
 
 def max_layers_for_memory(model: ModelSpec, tp: int, capacity_bytes: float, inflight: int, *, dp_shard: int = 1,
                           sequence_parallel: bool = True, extra_params: int = 0) -> int:
+    """Most layers a TP-``tp`` group can hold (memory grows with the layer count)."""
     if math.isinf(capacity_bytes):
         return model.num_layers
-    best = 0
-    for layers in range(1, model.num_layers + 1):
-        if not _fits(model, layers, tp, capacity_bytes, inflight, dp_shard, sequence_parallel, extra_params):
-            break
-        best = layers
-    return best
+    layers = 0
+    while layers < model.num_layers and _per_gpu_bytes(model, layers + 1, tp, inflight, dp_shard,
+                                                       sequence_parallel, extra_params) <= capacity_bytes:
+        layers += 1
+    return layers
 
 
 def select_subgroup(candidates: list[tuple[str, float]], degrees: list[int], profile: ModelProfile | None = None,
                     incumbents: set[str] | None = None, cp: int = 1) -> TPChoice | None:
-    inc = incumbents or set()
-    ranked = sorted(candidates, key=lambda c: (-c[1], c[0] not in inc, c[0]))
-    best: TPChoice | None = None
-    for k in sorted(degrees):
-        n = k * cp
-        if k < 1 or n > len(ranked):
+    """Best ``TPChoice`` over ``degrees`` for ``(device, speed)`` candidates, or None."""
+    keep = incumbents or set()
+    order = sorted(candidates, key=lambda dv: (-dv[1], dv[0] not in keep, dv[0]))
+
+    def throughput(k: int, slowest: float) -> float:
+        return cp * (profile.group_speed(k, slowest) if profile is not None else k * slowest)
+
+    options = []
+    for k in sorted(set(degrees)):
+        width = k * cp
+        if k < 1 or width > len(order):
             continue
-        chosen = ranked[:n]
-        slowest = min(p for _, p in chosen)
-        if slowest <= 0:
-            continue
-        score = (profile.group_speed(k, slowest) if profile is not None else k * slowest) * cp
-        if best is None or score >= best.score - 1e-12:
-            best = TPChoice(tuple(d for d, _ in chosen), k, score, tuple(d for d, _ in ranked[n:]))
-    return best
+        slowest = order[width - 1][1]  # sorted by speed, descending
+        if slowest > 0:
+            options.append((k, width, throughput(k, slowest)))
+    if not options:
+        return None
+    top = max(score for _, _, score in options)
+    k, width, score = max((o for o in options if o[2] >= top - _TIE), key=lambda o: o[0])
+    return TPChoice(tuple(d for d, _ in order[:width]), k, score, tuple(d for d, _ in order[width:]))
