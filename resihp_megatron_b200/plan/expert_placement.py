@@ -1,21 +1,30 @@
 """Expert placement for resilient expert parallelism (EPLB / Lazarus style).
 
-Every EP group hosts each logical expert at least once; spare slots replicate the hottest
-experts (highest load per copy first).  Physical copies are packed most-constrained-first by
-(load / device speed), copies of one expert on distinct devices, incumbents kept while within a
-``stickiness`` margin of their speed share, so a reconfiguration moves as little expert state as
-possible.  The slot budget is searched and each candidate is scored by the exact
-speed-proportional expert time of the slowest device (ties: fewer moved copies, fewer copies).
-An expert's gradient is summed over all its holders, so expert-DP groups come from the placement.
-(Reference: ``resihp/plan/expert_placement.py:21-168``.)
+Within every EP group each logical expert has at least one physical copy; spare slots
+replicate the experts with the highest load per copy.  Copies are packed onto devices
+most-constrained first (experts with more copies, then heavier copies), never two copies of one
+expert on a device, each to the device whose speed-normalised work stays lowest -- except that a
+device which already held the expert keeps it while its work stays within ``stickiness`` of its
+speed share, so a re-placement moves little expert state.  The slot budget (how many copies in
+total) is searched; a budget is scored by the slowest device's expert time when every expert's
+tokens split across its holders in proportion to speed, then by copies moved, then by copies.
+
+An expert's gradient sums over all its holders, so expert-data-parallel groups follow from the
+placement (``expert_dp_groups``); tokens of a replicated expert are dealt to its holders by
+smooth weighted round robin (the nginx upstream balancing rule), deterministic on every rank.
+Parity: ``resihp/plan/expert_placement.py:21-168`` (same placement rules, JSON and token split).
 """
 
 from __future__ import annotations
 
+import heapq
 import math
+from collections import defaultdict
 from dataclasses import dataclass
 
 from .planner import PlanInfeasible
+
+_FLOOR = 1e-9
 
 
 @dataclass(frozen=True)
@@ -25,142 +34,162 @@ class ExpertPlacement:
     slots: dict[str, tuple[int, ...]]
 
     def holders(self, expert: int) -> list[str]:
-        return sorted(d for g in self.groups for d in g if expert in self.slots[d])
+        """Every device (in any group) hosting a copy of ``expert``, sorted."""
+        return sorted(d for d, hosted in self.slots.items() if expert in hosted and self._placed(d))
+
+    def _placed(self, device: str) -> bool:
+        return any(device in g for g in self.groups)
 
     def group_holders(self, group: int, expert: int) -> list[str]:
         return [d for d in self.groups[group] if expert in self.slots[d]]
 
     def group_of(self, device: str) -> int:
-        for i, g in enumerate(self.groups):
-            if device in g:
-                return i
-        raise KeyError(device)
+        found = [i for i, g in enumerate(self.groups) if device in g]
+        if not found:
+            raise KeyError(device)
+        return found[0]
 
     def validate(self) -> None:
-        every = set(range(self.num_experts))
+        want = frozenset(range(self.num_experts))
         for i, g in enumerate(self.groups):
-            hosted = {e for d in g for e in self.slots[d]}
-            if hosted != every:
-                raise ValueError(f"EP group {i} misses experts {sorted(every - hosted)}")
-            for d in g:
-                if len(set(self.slots[d])) != len(self.slots[d]):
-                    raise ValueError(f"{d} hosts duplicate copies")
+            lacking = want.difference(e for d in g for e in self.slots[d])
+            if lacking:
+                raise ValueError(f"EP group {i} misses experts {sorted(lacking)}")
+            doubled = [d for d in g if len(self.slots[d]) != len(frozenset(self.slots[d]))]
+            if doubled:
+                raise ValueError(f"{doubled[0]} hosts duplicate copies")
 
     def to_json(self) -> dict:
         return {"num_experts": self.num_experts, "groups": [list(g) for g in self.groups],
-                "slots": {d: list(v) for d, v in self.slots.items()}}
+                "slots": {d: list(es) for d, es in self.slots.items()}}
 
-    @staticmethod
-    def from_json(d: dict) -> "ExpertPlacement":
-        return ExpertPlacement(d["num_experts"], tuple(tuple(g) for g in d["groups"]),
-                               {k: tuple(v) for k, v in d["slots"].items()})
+    @classmethod
+    def from_json(cls, d: dict) -> "ExpertPlacement":
+        return cls(d["num_experts"], tuple(map(tuple, d["groups"])), {k: tuple(v) for k, v in d["slots"].items()})
 
 
 def replica_counts(loads: list[float], total_slots: int, max_copies: int | None = None) -> list[int]:
-    if total_slots < len(loads):
-        raise PlanInfeasible(f"{total_slots} slots cannot host {len(loads)} experts")
-    cap = max_copies or total_slots
-    counts = [1] * len(loads)
-    for _ in range(total_slots - len(loads)):
-        open_ = [i for i in range(len(loads)) if counts[i] < cap]
-        if not open_:
+    """Copies per expert for ``total_slots`` slots: one each, then every spare slot to the expert
+    with the highest load per copy (lower id on ties), at most ``max_copies`` each."""
+    E = len(loads)
+    if total_slots < E:
+        raise PlanInfeasible(f"{total_slots} slots cannot host {E} experts")
+    limit = max_copies or total_slots
+    counts = [1] * E
+    heap = [(-loads[e], e) for e in range(E) if limit > 1]  # key: -(load per copy), then id
+    heapq.heapify(heap)
+    for _ in range(total_slots - E):
+        if not heap:
             break
-        e = max(open_, key=lambda i: (loads[i] / counts[i], -i))
+        _, e = heapq.heappop(heap)
         counts[e] += 1
+        if counts[e] < limit:
+            heapq.heappush(heap, (-loads[e] / counts[e], e))
     return counts
 
 
 def group_time(slots: dict[str, tuple[int, ...]], loads: list[float], speeds: dict[str, float]) -> float:
-    """Expert time of the slowest device when each expert's tokens split across its holders in
-    proportion to speed (every holder of ``e`` spends ``load_e / sum(speed of holders)``)."""
-    cap: dict[int, float] = {}
-    for d, es in slots.items():
-        for e in es:
-            cap[e] = cap.get(e, 0.0) + max(speeds.get(d, 1.0), 1e-9)
-    return max((sum(loads[e] / cap[e] for e in es) for es in slots.values()), default=0.0)
+    """The slowest device's expert time when each expert's tokens split across its holders in
+    proportion to speed: every holder of ``e`` spends ``load_e / (sum of its holders' speeds)``."""
+    pooled: dict[int, float] = defaultdict(float)
+    for d, hosted in slots.items():
+        for e in hosted:
+            pooled[e] += max(speeds.get(d, 1.0), _FLOOR)
+    per_device = [sum(loads[e] / pooled[e] for e in hosted) for hosted in slots.values()]
+    return max(per_device, default=0.0)
 
 
-def _pack(devices, speed, loads, counts, per_device, prev, stickiness):
-    copies = sorted(((counts[e], loads[e] / counts[e], e) for e in range(len(loads)) for _ in range(counts[e])),
-                    key=lambda c: (-c[0], -c[1], c[2]))
-    total = sum(w for _, w, _ in copies)
-    fair = {d: total * speed[d] / sum(speed.values()) for d in devices}
-    hosted: dict[str, list[int]] = {d: [] for d in devices}
-    work = dict.fromkeys(devices, 0.0)
-    for _, w, e in copies:
-        cands = [d for d in devices if len(hosted[d]) < per_device and e not in hosted[d]]
-        if not cands:
-            return None
-        sticky = [d for d in cands if e in prev.get(d, ()) and work[d] + w <= fair[d] * (1 + stickiness) + 1e-12]
-        pick = min(sticky or cands, key=lambda d: ((work[d] + w) / speed[d], d))
-        hosted[pick].append(e)
-        work[pick] += w
-    return {d: tuple(sorted(v)) for d, v in hosted.items()}
+class _Packer:
+    """Greedy packing of one budget's copies onto one EP group's devices."""
+
+    def __init__(self, devices, speed, per_device, prev, stickiness):
+        self.devices, self.speed, self.cap = devices, speed, per_device
+        self.prev, self.slack = prev, 1.0 + stickiness
+
+    def pack(self, loads, counts):
+        copies = [(counts[e], loads[e] / counts[e], e) for e in range(len(loads)) for _ in range(counts[e])]
+        copies.sort(key=lambda c: (-c[0], -c[1], c[2]))
+        total_speed = sum(self.speed.values())
+        total_work = sum(w for _, w, _ in copies)
+        share = {d: total_work * self.speed[d] / total_speed for d in self.devices}
+        hosted = {d: [] for d in self.devices}
+        work = dict.fromkeys(self.devices, 0.0)
+        for _, w, e in copies:
+            open_ = [d for d in self.devices if len(hosted[d]) < self.cap and e not in hosted[d]]
+            if not open_:
+                return None
+            keepers = [d for d in open_ if e in self.prev.get(d, ()) and work[d] + w <= share[d] * self.slack + 1e-12]
+            dest = min(keepers or open_, key=lambda d: ((work[d] + w) / self.speed[d], d))
+            hosted[dest].append(e)
+            work[dest] += w
+        return {d: tuple(sorted(es)) for d, es in hosted.items()}
 
 
 def place_group(devices: list[str], speeds: dict[str, float], loads: list[float], slots_per_device: int,
                 prev: dict[str, tuple[int, ...]] | None = None, stickiness: float = 0.1) -> dict[str, tuple[int, ...]]:
-    prev = prev or {}
-    speed = {d: max(speeds.get(d, 1.0), 1e-9) for d in devices}
-    best = None
+    """Slots of one EP group's devices (see the module docstring)."""
+    before = prev or {}
+    speed = {d: max(speeds.get(d, 1.0), _FLOOR) for d in devices}
+    packer = _Packer(devices, speed, slots_per_device, before, stickiness)
+    scored = []
     for budget in range(len(loads), len(devices) * slots_per_device + 1):
-        counts = replica_counts(loads, budget, max_copies=len(devices))
-        slots = _pack(devices, speed, loads, counts, slots_per_device, prev, stickiness)
+        slots = packer.pack(loads, replica_counts(loads, budget, max_copies=len(devices)))
         if slots is None:
             continue
-        moved = sum(1 for d, es in slots.items() for e in es if e not in prev.get(d, ()))
-        key = (round(group_time(slots, loads, speed), 12), moved, budget)
-        if best is None or key < best[0]:
-            best = (key, slots)
-    if best is None:
+        fresh = sum(e not in before.get(d, ()) for d, es in slots.items() for e in es)
+        scored.append(((round(group_time(slots, loads, speed), 12), fresh, budget), slots))
+    if not scored:
         raise PlanInfeasible(f"cannot place {len(loads)} experts on {len(devices)} devices x {slots_per_device}")
-    return best[1]
+    return min(scored, key=lambda t: t[0])[1]
 
 
 def plan_expert_placement(ep_groups: list[list[str]], num_experts: int, *, speeds: dict[str, float] | None = None,
                           loads: list[float] | None = None, prev: ExpertPlacement | None = None,
                           max_slots: int | None = None, slots_per_device: int | None = None) -> ExpertPlacement:
-    speeds = speeds or {}
-    loads = loads or [1.0] * num_experts
-    prev_slots = prev.slots if prev else {}
+    """Placement over several EP groups (each hosts every expert), validated."""
+    load = list(loads) if loads else [1.0] * num_experts
+    earlier = prev.slots if prev else {}
     slots: dict[str, tuple[int, ...]] = {}
     for g in ep_groups:
         if max_slots is not None and len(g) * max_slots < num_experts:
             raise PlanInfeasible(f"EP group of {len(g)} devices x {max_slots} slots cannot host {num_experts}")
-        need = slots_per_device or math.ceil(num_experts / len(g))
+        per_device = slots_per_device or math.ceil(num_experts / len(g))
         if max_slots is not None:
-            need = min(need, max_slots)
-        slots.update(place_group(list(g), speeds, loads, need, prev_slots))
-    out = ExpertPlacement(num_experts, tuple(tuple(g) for g in ep_groups), slots)
-    out.validate()
-    return out
+            per_device = min(per_device, max_slots)
+        slots |= place_group(list(g), speeds or {}, load, per_device, earlier)
+    placement = ExpertPlacement(num_experts, tuple(map(tuple, ep_groups)), slots)
+    placement.validate()
+    return placement
 
 
 def expert_dp_groups(placement: ExpertPlacement) -> dict[tuple[str, ...], list[int]]:
     """Experts with identical holder sets share one gradient all-reduce group."""
-    out: dict[tuple[str, ...], list[int]] = {}
+    by_holders: dict[tuple[str, ...], list[int]] = {}
     for e in range(placement.num_experts):
-        out.setdefault(tuple(placement.holders(e)), []).append(e)
-    return out
+        by_holders.setdefault(tuple(placement.holders(e)), []).append(e)
+    return by_holders
 
 
 def smooth_weighted_round_robin(holders: list[str], speeds: dict[str, float], n: int) -> list[str]:
-    """Deterministic speed-proportional assignment of ``n`` tokens to an expert's replicas
-    (smooth weighted round robin with integer weights 10 * speed)."""
+    """Deal ``n`` tokens of an expert to its replicas in proportion to speed, interleaved.
+
+    Smooth weighted round robin (integer weights ``round(10 * speed)``, at least 1): every turn
+    each replica's credit grows by its weight, the replica with the most credit (larger name on
+    ties) takes the token and pays back the total weight."""
     if len(holders) == 1:
-        return holders * n
-    w = {h: max(1, round(10 * speeds.get(h, 1.0))) for h in holders}
-    total = sum(w.values())
-    cur = dict.fromkeys(holders, 0)
-    out = []
+        return [holders[0]] * n
+    weight = [max(1, round(10 * speeds.get(h, 1.0))) for h in holders]
+    total = sum(weight)
+    credit = [0] * len(holders)
+    dealt = []
     for _ in range(n):
-        for h in holders:
-            cur[h] += w[h]
-        pick = max(holders, key=lambda h: (cur[h], h))
-        cur[pick] -= total
-        out.append(pick)
-    return out
+        credit = [c + w for c, w in zip(credit, weight)]
+        k = max(range(len(holders)), key=lambda i: (credit[i], holders[i]))
+        credit[k] -= total
+        dealt.append(holders[k])
+    return dealt
 
 
 def moved_experts(old: ExpertPlacement, new: ExpertPlacement) -> int:
-    return sum(1 for d, es in new.slots.items() for e in es if e not in old.slots.get(d, ()))
+    """Copies in ``new`` that their device did not hold in ``old``."""
+    return sum(e not in old.slots.get(d, ()) for d, hosted in new.slots.items() for e in hosted)
