@@ -1,22 +1,28 @@
-"""Pipeline instruction IR run by the worker-side interpreter.
+"""Pipeline instruction IR, executed by the worker-side interpreter.
 
-One instruction stream per physical (replica, stage) slot; every TP rank of a slot runs the
-same stream.  Ops: ``F`` forward, ``B`` backward (input grad, or full backward), ``W`` weight
-grad (zero-bubble split), ``SA``/``RA`` send/receive activation, ``SG``/``RG`` send/receive
-gradient.  A communication instruction names its peer as a (replica, virtual stage) key; with
-interleaving an instruction also carries its own virtual stage.
+Each physical (replica, stage) slot runs one instruction stream; all TP ranks of the slot run
+the same stream.  Ops: ``F`` forward, ``B`` backward (input gradient only when the backward is
+split, else the full backward), ``W`` weight gradient (zero-bubble split), and the four
+transfers ``SA``/``RA`` (send / receive activation) and ``SG``/``RG`` (send / receive gradient).
+A transfer names its peer as a (replica, virtual stage) key; with interleaving every
+instruction also carries its own virtual stage.
 
-Safety conditions checked by ``validate`` (each direction of a rank pair is one FIFO channel,
-sends never block): completeness (one F and one B per (stage, mb) on the executing slot, B
-after F, W after B when split), per-channel receive order equal to send order, and deadlock
-freedom by an earliest-start evaluation of the streams.
+``validate`` proves a schedule safe under the runtime's channel model -- each direction between
+two slots is one FIFO channel and sends never block:
 
-The JSON encoding of an instruction is ``[op, mb]``, ``[op, mb, r, s]`` or
-``[op, mb, r|-1, s|-1, stage]`` -- the reference's format (``resihp/plan/ir.py:26-189``).
+* coverage: exactly one F and one B of every (stage, micro-batch) on the slot the plan assigns
+  it to, B after F, and one W after B exactly when the backward is split;
+* placement: no slot computes a (stage, micro-batch) assigned elsewhere;
+* FIFO: on every channel the receive order equals the send order;
+* progress: an earliest-start evaluation of all streams runs every instruction (no deadlock).
+
+The JSON encoding of an instruction, ``[op, mb]``, ``[op, mb, r, s]`` or
+``[op, mb, r|-1, s|-1, stage]``, is the reference's wire format (``resihp/plan/ir.py:26-189``).
 """
 
 from __future__ import annotations
 
+from collections import defaultdict, deque
 from dataclasses import dataclass
 from enum import Enum
 from typing import Callable
@@ -40,6 +46,9 @@ COMPUTE = frozenset({Op.F, Op.B, Op.W})
 SENDS = {Op.SEND_ACT: "act", Op.SEND_GRAD: "grad"}
 RECVS = {Op.RECV_ACT: "act", Op.RECV_GRAD: "grad"}
 
+# compute op -> (receive before it, offset of its source stage, send after it, offset of its target)
+_WIRING = {"F": (Op.RECV_ACT, -1, Op.SEND_ACT, +1), "B": (Op.RECV_GRAD, +1, Op.SEND_GRAD, -1)}
+
 
 @dataclass(frozen=True)
 class Instr:
@@ -49,19 +58,23 @@ class Instr:
     stage: int | None = None
 
     def stage_on(self, key: Key) -> int:
-        """Virtual stage of this instruction inside the stream of slot ``key``."""
-        return key[1] if self.stage is None else self.stage
+        """The virtual stage this instruction belongs to inside the stream of slot ``key``."""
+        return self.stage if self.stage is not None else key[1]
 
     def to_json(self) -> list:
-        head = [self.op.value, self.mb]
-        if self.stage is None:
-            return head + (list(self.peer) if self.peer is not None else [])
-        return head + (list(self.peer) if self.peer is not None else [-1, -1]) + [self.stage]
+        enc = [self.op.value, self.mb]
+        if self.peer is not None:
+            enc.extend(self.peer)
+        elif self.stage is not None:
+            enc.extend((-1, -1))
+        if self.stage is not None:
+            enc.append(self.stage)
+        return enc
 
-    @staticmethod
-    def from_json(d: list) -> "Instr":
-        peer = (d[2], d[3]) if len(d) > 2 and d[2] >= 0 else None
-        return Instr(Op(d[0]), d[1], peer, d[4] if len(d) > 4 else None)
+    @classmethod
+    def from_json(cls, d: list) -> "Instr":
+        has_peer = len(d) >= 4 and d[2] >= 0
+        return cls(Op(d[0]), d[1], (d[2], d[3]) if has_peer else None, d[4] if len(d) >= 5 else None)
 
 
 Schedule = dict[Key, list[Instr]]
@@ -72,84 +85,95 @@ class ScheduleError(ValueError):
 
 
 def compute_order_to_ir(plan: HeteroParallelPlan, order: dict[Key, list[tuple]]) -> Schedule:
-    """Expand per-slot compute orders (``(op, mb)`` or ``(op, mb, stage)``) into streams with
-    the receives before and the sends after each F / B."""
-    last = plan.num_stages - 1
-    out: Schedule = {}
+    """Expand per-slot compute orders -- entries ``(op, mb)`` or ``(op, mb, stage)`` -- into
+    instruction streams: a receive before and a send after every F and B that has a neighbour."""
+    first, last = 0, plan.num_stages - 1
+    streams: Schedule = {}
     for key, entries in order.items():
-        stream: list[Instr] = []
-        for e in entries:
-            op, mb = e[0], e[1]
-            s = e[2] if len(e) > 2 else key[1]
+        out = streams.setdefault(key, [])
+        for entry in entries:
+            op, mb = entry[0], entry[1]
+            s = entry[2] if len(entry) > 2 else key[1]
             tag = s if plan.vpp > 1 else None
-            if op == "F":
-                if s > 0:
-                    stream.append(Instr(Op.RECV_ACT, mb, (plan.executor(s - 1, mb), s - 1), tag))
-                stream.append(Instr(Op.F, mb, None, tag))
-                if s < last:
-                    stream.append(Instr(Op.SEND_ACT, mb, (plan.executor(s + 1, mb), s + 1), tag))
-            elif op == "B":
-                if s < last:
-                    stream.append(Instr(Op.RECV_GRAD, mb, (plan.executor(s + 1, mb), s + 1), tag))
-                stream.append(Instr(Op.B, mb, None, tag))
-                if s > 0:
-                    stream.append(Instr(Op.SEND_GRAD, mb, (plan.executor(s - 1, mb), s - 1), tag))
-            elif op == "W":
-                stream.append(Instr(Op.W, mb, None, tag))
-            else:
+            if op == "W":
+                out.append(Instr(Op.W, mb, None, tag))
+                continue
+            if op not in _WIRING:
                 raise ScheduleError(f"unknown compute op {op!r}")
-        out[key] = stream
-    return out
+            recv, src, send, dst = _WIRING[op]
+            if first <= s + src <= last:
+                out.append(Instr(recv, mb, (plan.executor(s + src, mb), s + src), tag))
+            out.append(Instr(Op(op), mb, None, tag))
+            if first <= s + dst <= last:
+                out.append(Instr(send, mb, (plan.executor(s + dst, mb), s + dst), tag))
+    return streams
 
 
 def schedule_to_json(schedule: Schedule) -> dict:
-    return {f"{r},{s}": [i.to_json() for i in stream] for (r, s), stream in schedule.items()}
+    return {"%d,%d" % key: [i.to_json() for i in stream] for key, stream in schedule.items()}
 
 
 def schedule_from_json(d: dict) -> Schedule:
-    out: Schedule = {}
-    for k, stream in d.items():
-        r, s = k.split(",")
-        out[(int(r), int(s))] = [Instr.from_json(i) for i in stream]
-    return out
+    def key(text: str) -> Key:
+        r, s = map(int, text.split(","))
+        return r, s
+
+    return {key(k): list(map(Instr.from_json, stream)) for k, stream in d.items()}
 
 
-def validate(plan: HeteroParallelPlan, schedule: Schedule, split_backward: bool = False) -> None:
-    phys = lambda k: plan.physical_key(*k)  # noqa: E731
+def _check_coverage(plan: HeteroParallelPlan, schedule: Schedule, split: bool, phys) -> None:
+    positions: dict[tuple, dict[Op, list[int]]] = defaultdict(lambda: defaultdict(list))
+    for key, stream in schedule.items():
+        for idx, ins in enumerate(stream):
+            if ins.op in COMPUTE:
+                positions[(key, ins.stage_on(key), ins.mb)][ins.op].append(idx)
     for s in range(plan.num_stages):
         for m in range(plan.num_microbatches):
             key = phys((plan.executor(s, m), s))
-            where: dict[Op, list[int]] = {op: [] for op in COMPUTE}
-            for idx, ins in enumerate(schedule.get(key, [])):
-                if ins.op in COMPUTE and ins.mb == m and ins.stage_on(key) == s:
-                    where[ins.op].append(idx)
-            if len(where[Op.F]) != 1 or len(where[Op.B]) != 1:
+            at = positions.get((key, s, m), {})
+            f, b, w = at.get(Op.F, []), at.get(Op.B, []), at.get(Op.W, [])
+            if len(f) != 1 or len(b) != 1:
                 raise ScheduleError(f"mb {m} stage {s}: expected exactly one F and one B on {key}")
-            if where[Op.F][0] > where[Op.B][0]:
+            if b[0] < f[0]:
                 raise ScheduleError(f"mb {m} stage {s}: B before F")
-            if split_backward:
-                if len(where[Op.W]) != 1 or where[Op.W][0] < where[Op.B][0]:
-                    raise ScheduleError(f"mb {m} stage {s}: W missing or before B")
-            elif where[Op.W]:
+            if split and (len(w) != 1 or w[0] < b[0]):
+                raise ScheduleError(f"mb {m} stage {s}: W missing or before B")
+            if not split and w:
                 raise ScheduleError(f"mb {m} stage {s}: unexpected W")
+
+
+def _check_placement(plan: HeteroParallelPlan, schedule: Schedule, phys) -> None:
     for key, stream in schedule.items():
-        for ins in stream:
-            if ins.op in COMPUTE:
-                s = ins.stage_on(key)
-                if phys((plan.executor(s, ins.mb), s)) != key:
-                    raise ScheduleError(f"{key} runs mb {ins.mb} of stage {s}, assigned to replica "
-                                        f"{plan.executor(s, ins.mb)}")
-    sent: dict[tuple, list[tuple[int, int]]] = {}
-    got: dict[tuple, list[tuple[int, int]]] = {}
+        for ins in filter(lambda i: i.op in COMPUTE, stream):
+            s = ins.stage_on(key)
+            owner = plan.executor(s, ins.mb)
+            if phys((owner, s)) != key:
+                raise ScheduleError(f"{key} runs mb {ins.mb} of stage {s}, assigned to replica {owner}")
+
+
+def _check_fifo(schedule: Schedule, phys) -> None:
+    posted, taken = defaultdict(list), defaultdict(list)
     for key, stream in schedule.items():
         for ins in stream:
             if ins.op in SENDS:
-                sent.setdefault((key, phys(ins.peer), SENDS[ins.op]), []).append((ins.mb, ins.peer[1]))
+                posted[(key, phys(ins.peer), SENDS[ins.op])].append((ins.mb, ins.peer[1]))
             elif ins.op in RECVS:
-                got.setdefault((phys(ins.peer), key, RECVS[ins.op]), []).append((ins.mb, ins.stage_on(key)))
-    for ch in sent.keys() | got.keys():
-        if sent.get(ch, []) != got.get(ch, []):
-            raise ScheduleError(f"channel {ch}: send order {sent.get(ch)} != receive order {got.get(ch)}")
+                taken[(phys(ins.peer), key, RECVS[ins.op])].append((ins.mb, ins.stage_on(key)))
+    for channel in set(posted) | set(taken):
+        if posted.get(channel, []) != taken.get(channel, []):
+            raise ScheduleError(f"channel {channel}: send order {posted.get(channel)} != receive order "
+                                f"{taken.get(channel)}")
+
+
+def validate(plan: HeteroParallelPlan, schedule: Schedule, split_backward: bool = False) -> None:
+    """Raise ``ScheduleError`` unless ``schedule`` is complete, FIFO-consistent and deadlock free."""
+
+    def phys(k: Key) -> Key:
+        return plan.physical_key(*k)
+
+    _check_coverage(plan, schedule, split_backward, phys)
+    _check_placement(plan, schedule, phys)
+    _check_fifo(schedule, phys)
     if not stream_simulation(schedule, phys=phys).complete:
         raise ScheduleError("schedule deadlocks")
 
@@ -167,29 +191,35 @@ def _unit(key, ins) -> float:
 
 def stream_simulation(schedule: Schedule, duration: Callable = _unit, transfer: Callable = lambda s, d, i: 0.0,
                       phys: Callable = lambda k: k) -> StreamSimResult:
-    """Earliest-start evaluation of fixed streams (DAG longest path): sends never block, a
-    receive starts once its matching send finished plus the transfer time."""
-    ptr = {k: 0 for k in schedule}
-    clock = {k: 0.0 for k in schedule}
-    arrivals: dict[tuple, float] = {}
-    moved = True
-    while moved:
-        moved = False
-        for key, stream in schedule.items():
-            while ptr[key] < len(stream):
-                ins = stream[ptr[key]]
-                t0 = clock[key]
-                if ins.op in RECVS:
-                    tag = (phys(ins.peer), key, RECVS[ins.op], ins.mb, ins.stage_on(key))
-                    if tag not in arrivals:
-                        break
-                    t0 = max(t0, arrivals[tag])
-                t1 = t0 + duration(key, ins)
-                if ins.op in SENDS:
-                    arrivals[(key, phys(ins.peer), SENDS[ins.op], ins.mb, ins.peer[1])] = t1 + transfer(key, ins.peer,
-                                                                                                       ins)
-                clock[key] = t1
-                ptr[key] += 1
-                moved = True
-    done = all(ptr[k] == len(s) for k, s in schedule.items())
-    return StreamSimResult(done, dict(clock), max(clock.values(), default=0.0))
+    """Earliest-start evaluation of fixed streams (the longest path of their DAG).  A stream
+    advances until it reaches a receive whose message was not sent yet; a send wakes the
+    receiving stream.  Sends never block; a receive starts at the later of its stream's clock
+    and its message's arrival (send end + ``transfer``)."""
+    pc = dict.fromkeys(schedule, 0)
+    now = dict.fromkeys(schedule, 0.0)
+    arrived: dict[tuple, float] = {}
+    waiting: dict[tuple, Key] = {}
+    ready = deque(schedule)
+    while ready:
+        key = ready.popleft()
+        stream = schedule[key]
+        while pc[key] < len(stream):
+            ins = stream[pc[key]]
+            start = now[key]
+            if ins.op in RECVS:
+                msg = (phys(ins.peer), key, RECVS[ins.op], ins.mb, ins.stage_on(key))
+                if msg not in arrived:
+                    waiting[msg] = key
+                    break
+                start = max(start, arrived[msg])
+            end = start + duration(key, ins)
+            if ins.op in SENDS:
+                dst = phys(ins.peer)
+                msg = (key, dst, SENDS[ins.op], ins.mb, ins.peer[1])
+                arrived[msg] = end + transfer(key, ins.peer, ins)
+                if waiting.get(msg) is not None:
+                    ready.append(waiting.pop(msg))
+            now[key] = end
+            pc[key] += 1
+    complete = all(pc[k] == len(s) for k, s in schedule.items())
+    return StreamSimResult(complete, dict(now), max(now.values(), default=0.0))
