@@ -1,25 +1,30 @@
-"""Progressive TP -> PP -> DP planner producing ``HeteroParallelPlan`` s and IR schedules.
+"""The joint TP -> PP -> DP planner: produces ``HeteroParallelPlan`` s and their IR schedules.
 
-``initial_plan``: place (replica, stage) TP groups (``spread`` by default), partition layers by
-min-max DP under memory caps, assign micro-batches, migrate, schedule.
+``initial_plan``: place the (replica, stage) TP groups (``spread`` by default), split the layers
+by the min-max partition under the memory caps, assign micro-batches, migrate, schedule.
 
-``replan`` after failures / slowdowns, per surviving group of the previous physical plan:
-  1. TP: choose a subgroup among the survivors plus free devices of the same node (Eq. 4 over
-     every feasible degree -- not only powers of two -- with a memory-derived minimum degree,
-     incumbents preferred);
-  2. fill missing groups from the free pool (rejoined / spare nodes) and optionally grow
-     whole replicas up to ``max_replicas``;
-  3. PP: repartition layers by aggregated stage capacity (min-max DP);
-  4. DP: progress-aware micro-batch migration (simulated moves);
-  5. joint keep-or-evict: for each weakened group, also try dropping it and letting peer
-     replicas absorb its work; keep whichever the simulator predicts faster.
-Ablation switches ``enable_tp_shrink`` / ``enable_repartition`` / ``enable_migration`` turn
-steps off.  (Reference: ``resihp/plan/planner.py:24-273``, ResiHP section 6.)
+``replan`` after failures or slowdowns works from the previous physical plan, group by group:
+
+1. **TP** -- for each group pick a subgroup among its survivors and the free devices of its
+   node: Eq. 4 over every feasible degree (not only powers of two), no smaller than the degree
+   the stage's memory needs, incumbents first.  A group with no survivor is rebuilt on the node
+   with the most free devices.
+2. **Pool** -- rebuild missing groups of the nominal layout from free devices (rejoined or spare
+   nodes), and optionally grow whole replicas up to ``max_replicas``.
+3. **PP** -- repartition the layers by each stage's aggregate capacity.
+4. **DP** -- progress-aware micro-batch migration, every move checked by simulation.
+5. **Keep or evict** -- for every weakened group (fewer devices or a slow member) also try
+   dropping it and letting its stage's other replicas absorb its work; keep the faster plan.
+
+``enable_tp_shrink`` / ``enable_repartition`` / ``enable_migration`` switch steps off for the
+ablation study.  Parity: ``resihp/plan/planner.py:24-273`` (ResiHP section 6; same steps and
+config fields).
 """
 
 from __future__ import annotations
 
 import math
+from collections import defaultdict
 from dataclasses import dataclass, replace
 
 from .cost_model import CostModel, Workload
@@ -65,222 +70,236 @@ class PlannerConfig:
     cp: int = 1
 
 
-class HeteroPlanner:
+class _Memory:
+    """The per-GPU memory model of one stage under a config."""
+
     def __init__(self, cfg: PlannerConfig):
         self.cfg = cfg
 
-    # ------------------------------------------------------------------ model helpers
+    def extra_params(self, stage: int) -> int:
+        emb = self.cfg.model.embedding_params()
+        return emb * ((stage == 0) + (stage == self.cfg.num_stages - 1))
+
+    def inflight(self, stage: int) -> int:
+        """Micro-batches stage ``stage`` holds at once (1F1B or interleaved warm-up), CP-split."""
+        P, v = self.cfg.num_stages, self.cfg.vpp
+        depth = max(1, P - stage) if v == 1 else math.ceil(((P - stage - 1) * 2 + (v - 1) * P) / v) + 1
+        return max(1, math.ceil(depth / self.cfg.cp))
+
+    def _kw(self, stage: int) -> dict:
+        return dict(dp_shard=self.cfg.dp_shard, sequence_parallel=self.cfg.sequence_parallel,
+                    extra_params=self.extra_params(stage))
+
+    def min_tp(self, layers: int, stage: int) -> int:
+        k = min_tp_for_memory(self.cfg.model, layers, self.cfg.mem_capacity, self.inflight(stage), **self._kw(stage))
+        return self.cfg.tp + 1 if k is None else k  # nothing fits: no degree is allowed
+
+    def max_layers(self, tp: int, stage: int) -> int:
+        return max_layers_for_memory(self.cfg.model, tp, self.cfg.mem_capacity, self.inflight(stage),
+                                     **self._kw(stage))
+
+    def slot_caps(self, plan: HeteroParallelPlan) -> dict[Key, float]:
+        """Per physical slot: how many micro-batches' activations fit beside its static state."""
+        c = self.cfg
+        if math.isinf(c.mem_capacity):
+            return {}
+        static, per_mb = defaultdict(float), defaultdict(float)
+        for g in plan.stage_groups:
+            slot = plan.physical_key(g.replica, g.stage)
+            static[slot] += c.model.static_bytes(g.num_layers, g.tp, c.dp_shard, self.extra_params(g.stage))
+            per_mb[slot] += c.model.activation_bytes(g.num_layers, g.tp, c.sequence_parallel) / g.cp
+        return {k: math.floor((c.mem_capacity - static[k]) / per_mb[k]) if per_mb[k] > 0 else math.inf
+                for k in static}
+
+
+class HeteroPlanner:
+    def __init__(self, cfg: PlannerConfig):
+        self.cfg = cfg
+        self.mem = _Memory(cfg)
+
+    # ------------------------------------------------------------------ pricing
     def workload(self) -> Workload:
         c = self.cfg
         return c.workload or Workload.uniform(c.num_microbatches, c.model.seq_len, c.model.micro_batch_size)
 
-    def _extra_params(self, s: int) -> int:
-        emb = self.cfg.model.embedding_params()
-        return (emb if s == 0 else 0) + (emb if s == self.cfg.num_stages - 1 else 0)
-
-    def _inflight(self, s: int) -> int:
-        """In-flight micro-batches at stage ``s`` for memory sizing (CP splits each one)."""
-        P, v = self.cfg.num_stages, self.cfg.vpp
-        n = max(1, P - s) if v == 1 else math.ceil(((P - s - 1) * 2 + (v - 1) * P) / v) + 1
-        return max(1, math.ceil(n / self.cfg.cp))
-
-    def _group_speed(self, devices, speed: dict[str, float]) -> float:
-        c = self.cfg
-        return c.profile.group_speed(len(devices) // c.cp, min(speed.get(d, 1.0) for d in devices)) * c.cp
-
-    def _k_min(self, layers: int, stage: int) -> int:
-        c = self.cfg
-        k = min_tp_for_memory(c.model, layers, c.mem_capacity, self._inflight(stage), dp_shard=c.dp_shard,
-                              sequence_parallel=c.sequence_parallel, extra_params=self._extra_params(stage))
-        return k if k is not None else c.tp + 1  # nothing fits: make every degree infeasible
-
-    def _max_layers(self, tp: int, stage: int) -> int:
-        c = self.cfg
-        return max_layers_for_memory(c.model, tp, c.mem_capacity, self._inflight(stage), dp_shard=c.dp_shard,
-                                     sequence_parallel=c.sequence_parallel, extra_params=self._extra_params(stage))
-
-    def _choose(self, cands: list[tuple[str, float]], max_tp: int, k_min: int, incumbents=None):
-        c = self.cfg
-        degrees = feasible_degrees(c.model, min(len(cands) // c.cp, max_tp), k_min, c.power_of_two_only)
-        return select_subgroup(cands, degrees, c.profile, incumbents=incumbents, cp=c.cp)
-
     def cost_model(self, plan: HeteroParallelPlan, topology: ClusterTopology) -> CostModel:
-        return CostModel(plan, self.cfg.model, self.cfg.profile, self.workload(),
-                         {d.id: d.speed for d in topology.devices}, {d.id: d.node for d in topology.devices},
+        speeds = {d.id: d.speed for d in topology.devices}
+        nodes = {d.id: d.node for d in topology.devices}
+        return CostModel(plan, self.cfg.model, self.cfg.profile, self.workload(), speeds, nodes,
                          split_backward=self.cfg.split_backward)
 
     def mem_caps(self, plan: HeteroParallelPlan) -> dict[Key, float]:
-        """Per physical slot: how many micro-batches' activations fit next to the static state."""
-        c = self.cfg
-        if math.isinf(c.mem_capacity):
-            return {}
-        static: dict[Key, float] = {}
-        act: dict[Key, float] = {}
-        last = plan.num_stages - 1
-        emb = c.model.embedding_params()
-        for g in plan.stage_groups:
-            k = plan.physical_key(g.replica, g.stage)
-            extra = (emb if g.stage == 0 else 0) + (emb if g.stage == last else 0)
-            static[k] = static.get(k, 0.0) + c.model.static_bytes(g.num_layers, g.tp, c.dp_shard, extra)
-            act[k] = act.get(k, 0.0) + c.model.activation_bytes(g.num_layers, g.tp, c.sequence_parallel) / g.cp
-        return {k: (math.floor((c.mem_capacity - static[k]) / act[k]) if act[k] > 0 else math.inf) for k in static}
+        return self.mem.slot_caps(plan)
 
-    def _partition(self, capacities: list[float], max_layers: list[int]) -> list[int]:
+    def _speed_of(self, devices, speed: dict[str, float]) -> float:
         c = self.cfg
-        if not c.enable_repartition:
-            q, r = divmod(c.model.num_layers, c.num_stages)
-            return [q + (1 if s < r else 0) for s in range(c.num_stages)]
-        return partition_layers(c.model.num_layers, capacities, first_extra=c.profile.first_stage_extra_layers,
-                                last_extra=c.profile.last_stage_extra_layers, max_layers=max_layers,
-                                min_layers=c.vpp)
+        return c.cp * c.profile.group_speed(len(devices) // c.cp, min(speed.get(d, 1.0) for d in devices))
 
-    # ------------------------------------------------------------------ plan assembly
-    def _assemble(self, generation: int, members: dict[Key, tuple[str, ...]], counts: list[int],
-                  world_order: list[str], standby: list[str], topology: ClusterTopology) -> HeteroParallelPlan:
+    def _subgroup(self, candidates, k_min: int, incumbents=None):
+        c = self.cfg
+        top = min(len(candidates) // c.cp, c.tp)
+        degrees = feasible_degrees(c.model, top, k_min, c.power_of_two_only)
+        return select_subgroup(candidates, degrees, c.profile, incumbents=incumbents, cp=c.cp)
+
+    def _layer_counts(self, capacities: list[float], max_layers: list[int]) -> list[int]:
+        c = self.cfg
+        if c.enable_repartition:
+            return partition_layers(c.model.num_layers, capacities, first_extra=c.profile.first_stage_extra_layers,
+                                    last_extra=c.profile.last_stage_extra_layers, max_layers=max_layers,
+                                    min_layers=c.vpp)
+        base, rest = divmod(c.model.num_layers, c.num_stages)
+        return [base + int(s < rest) for s in range(c.num_stages)]
+
+    # ------------------------------------------------------------------ assembly
+    def _build(self, generation: int, members: dict[Key, tuple[str, ...]], counts: list[int],
+               world_order: list[str], topology: ClusterTopology) -> HeteroParallelPlan:
         c = self.cfg
         used = {d for devs in members.values() for d in devs}
-        world = [d for d in world_order if d in used] + sorted(used - set(world_order))
-        rank = {d: i for i, d in enumerate(world)}
-        ranges = counts_to_ranges(counts)
-        groups = tuple(StageGroup(r, s, tuple(sorted(devs, key=rank.__getitem__)), ranges[s], c.cp)
-                       for (r, s), devs in sorted(members.items(), key=lambda kv: (kv[0][1], kv[0][0])))
+        world = [d for d in world_order if d in used]
+        world += sorted(used.difference(world_order))
+        pos = {d: i for i, d in enumerate(world)}
+        spans = counts_to_ranges(counts)
+        groups = tuple(StageGroup(r, s, tuple(sorted(members[(r, s)], key=pos.__getitem__)), spans[s], c.cp)
+                       for r, s in sorted(members, key=lambda k: (k[1], k[0])))
         speed = {d.id: d.speed for d in topology.devices}
-        assignment = initial_assignment(list(groups), c.num_stages, c.num_microbatches,
-                                        lambda key: self._group_speed(members[key], speed))
+        table = initial_assignment(list(groups), c.num_stages, c.num_microbatches,
+                                   lambda key: self._speed_of(members[key], speed))
         plan = HeteroParallelPlan(generation=generation, world=tuple(world), num_layers=c.model.num_layers,
-                                  num_stages=c.num_stages, num_replicas=max(r for r, _ in members) + 1,
-                                  stage_groups=groups, num_microbatches=c.num_microbatches, assignment=assignment,
-                                  standby=tuple(sorted(standby)), sequence_parallel=c.sequence_parallel)
+                                  num_stages=c.num_stages, num_replicas=1 + max(r for r, _ in members),
+                                  stage_groups=groups, num_microbatches=c.num_microbatches, assignment=table,
+                                  standby=tuple(sorted(d for d in topology.ids() if d not in used)),
+                                  sequence_parallel=c.sequence_parallel)
         plan = interleave(plan, c.vpp)
         plan.validate()
         cm = self.cost_model(plan, topology)
         if c.enable_migration:
-            res = progress_aware_migration(plan, cm, mem_cap=self.mem_caps(plan) or None, delta=c.delta,
-                                           max_rounds=c.migration_rounds, split_backward=c.split_backward)
-            plan = replace(plan, assignment=res.assignment)
-            makespan, initial = res.makespan, res.initial_makespan
+            moved = progress_aware_migration(plan, cm, mem_cap=self.mem_caps(plan) or None, delta=c.delta,
+                                             max_rounds=c.migration_rounds, split_backward=c.split_backward)
+            plan = replace(plan, assignment=moved.assignment)
+            predicted, before = moved.makespan, moved.initial_makespan
         else:
-            makespan = initial = simulate(plan, cm, c.split_backward).makespan
-        plan = replace(plan, meta={"predicted_iteration_s": makespan, "unmigrated_iteration_s": initial,
+            predicted = before = simulate(plan, cm, c.split_backward).makespan
+        plan = replace(plan, meta={"predicted_iteration_s": predicted, "unmigrated_iteration_s": before,
                                    "layer_counts": list(counts)})
         plan.validate()
         return plan
+
+    def _from_members(self, members: dict[Key, tuple[str, ...]], prev: HeteroParallelPlan,
+                      topology: ClusterTopology, generation: int) -> HeteroParallelPlan:
+        c = self.cfg
+        speed = {d.id: d.speed for d in topology.devices}
+        capacity, ceiling = [], []
+        for s in range(c.num_stages):
+            here = [devs for (r, st), devs in members.items() if st == s]
+            capacity.append(sum(self._speed_of(devs, speed) for devs in here))
+            ceiling.append(min(self.mem.max_layers(len(devs) // c.cp, s) for devs in here))
+        return self._build(generation, members, self._layer_counts(capacity, ceiling), list(prev.world), topology)
 
     # ------------------------------------------------------------------ entry points
     def initial_plan(self, topology: ClusterTopology, generation: int = 1) -> HeteroParallelPlan:
         c = self.cfg
         members = place_groups(topology, c.num_replicas, c.num_stages, c.tp * c.cp, c.placement)
-        caps = [c.num_replicas * c.profile.group_speed(c.tp, 1.0) * c.cp] * c.num_stages
-        counts = self._partition(caps, [self._max_layers(c.tp, s) for s in range(c.num_stages)])
-        used = {d for devs in members.values() for d in devs}
-        standby = [d for d in topology.ids() if d not in used]
-        return self._assemble(generation, members, counts, topology.ids(), standby, topology)
+        stage_capacity = c.num_replicas * c.cp * c.profile.group_speed(c.tp, 1.0)
+        counts = self._layer_counts([stage_capacity] * c.num_stages,
+                                    [self.mem.max_layers(c.tp, s) for s in range(c.num_stages)])
+        return self._build(generation, members, counts, topology.ids(), topology)
+
+    def _regroup(self, prev: HeteroParallelPlan, topology: ClusterTopology, counts: list[int]):
+        """Step 1: a subgroup per surviving group; returns the members and the free-device pool."""
+        c = self.cfg
+        alive = topology.by_id()
+        grouped = {d for g in prev.stage_groups for d in g.devices}
+        pool: dict[str, list[str]] = defaultdict(list)
+        for d in topology.devices:
+            if d.id in prev.standby or d.id not in grouped:
+                pool[d.node].append(d.id)
+        members: dict[Key, tuple[str, ...]] = {}
+        for g in sorted(prev.stage_groups, key=lambda g: (g.stage, g.replica)):
+            survivors = [d for d in g.devices if d in alive]
+            if survivors:
+                node = min(alive[d].node for d in survivors)
+            else:  # the whole group is gone: rebuild it where most devices are free
+                roomy = [n for n in pool if pool[n]]
+                node = max(roomy, key=lambda n: (len(pool[n]), n)) if roomy else None
+            candidates = [(d, alive[d].speed) for d in survivors + (list(pool[node]) if node else [])]
+            if not candidates:
+                continue
+            if not c.enable_tp_shrink:
+                if len(survivors) == len(g.devices):
+                    members[(g.replica, g.stage)] = tuple(survivors)
+                continue
+            pick = self._subgroup(candidates, self.mem.min_tp(counts[g.stage], g.stage), incumbents=set(survivors))
+            if pick is None:
+                continue
+            members[(g.replica, g.stage)] = pick.devices
+            if node:
+                pool[node] = [d for d in pool[node] + survivors if d not in pick.devices]
+        return members, pool
+
+    def _fill_from_pool(self, members: dict[Key, tuple[str, ...]], pool: dict[str, list[str]], alive: dict,
+                        prev_counts: list[int]) -> None:
+        """Step 2: rebuild missing groups of the nominal layout from free devices, then grow whole
+        replicas up to ``max_replicas``."""
+        c = self.cfg
+        width = c.tp * c.cp
+
+        def full_group(stage: int) -> tuple[str, ...] | None:
+            for node in sorted(pool, key=lambda n: (-len(pool[n]), n)):
+                if not pool[node]:
+                    continue
+                pick = self._subgroup([(d, alive[d].speed) for d in pool[node]],
+                                      self.mem.min_tp(prev_counts[stage], stage))
+                if pick is not None and pick.tp == c.tp:
+                    pool[node] = [d for d in pool[node] if d not in pick.devices]
+                    return pick.devices
+            return None
+
+        for r in range(max(c.num_replicas, c.max_replicas or 0)):
+            gaps = [s for s in range(c.num_stages) if (r, s) not in members]
+            if not gaps:
+                continue
+            if r >= c.num_replicas:  # growing: only whole new replicas, only if the pool can hold one
+                if len(gaps) < c.num_stages:
+                    continue
+                if sum(len(v) // width for v in pool.values()) < c.num_stages:
+                    break
+            for s in gaps:
+                devs = full_group(s)
+                if devs is not None:
+                    members[(r, s)] = devs
 
     def replan(self, prev: HeteroParallelPlan, topology: ClusterTopology,
                generation: int | None = None) -> HeteroParallelPlan:
         c = self.cfg
         prev = prev.physical()
         alive = topology.by_id()
-        node_of = {d.id: d.node for d in topology.devices}
-        grouped = {d for g in prev.stage_groups for d in g.devices}
-        pool: dict[str, list[str]] = {}
-        for d in topology.devices:
-            if d.id in prev.standby or d.id not in grouped:
-                pool.setdefault(d.node, []).append(d.id)
-        prev_counts = [b - a for a, b in prev.layer_partition()]
-        members: dict[Key, tuple[str, ...]] = {}
-        for g in sorted(prev.stage_groups, key=lambda g: (g.stage, g.replica)):
-            survivors = [d for d in g.devices if d in alive]
-            if survivors:
-                node = sorted({node_of[d] for d in survivors})[0]
-            else:  # the whole group is gone: rebuild on the node with the most free devices
-                node = max((n for n in pool if pool[n]), key=lambda n: (len(pool[n]), n), default=None)
-            local_free = pool.get(node, []) if node else []
-            cands = [(d, alive[d].speed) for d in survivors + local_free]
-            if not cands:
+        counts = [hi - lo for lo, hi in prev.layer_partition()]
+        members, pool = self._regroup(prev, topology, counts)
+        self._fill_from_pool(members, pool, alive, counts)
+        orphaned = [s for s in range(c.num_stages) if all(k[1] != s for k in members)]
+        if orphaned:
+            raise PlanInfeasible(f"no TP group can host stage {orphaned[0]}")
+        gen = generation if generation is not None else prev.generation + 1
+        best = self._from_members(members, prev, topology, gen)
+        # Step 5: Eq. 4 alone cannot see that a weakened group may slow its whole stage more than
+        # handing its micro-batches to the stage's other replicas would.
+        replicas_at = defaultdict(int)
+        for _, s in members:
+            replicas_at[s] += 1
+        for key, devs in list(members.items()):
+            weakened = len(devs) < c.tp * c.cp or min(alive[d].speed for d in devs) < 1.0
+            if not weakened or replicas_at[key[1]] < 2:
                 continue
-            if not c.enable_tp_shrink:
-                if len(survivors) == len(g.devices):
-                    members[(g.replica, g.stage)] = tuple(survivors)
-                continue
-            choice = self._choose(cands, c.tp, self._k_min(prev_counts[g.stage], g.stage),
-                                  incumbents=set(survivors))
-            if choice is None:
-                continue
-            members[(g.replica, g.stage)] = choice.devices
-            if node:
-                pool[node] = [d for d in pool.get(node, []) + survivors if d not in choice.devices]
-        self._fill_from_pool(members, pool, alive, prev_counts)
-        for s in range(c.num_stages):
-            if not any(k[1] == s for k in members):
-                raise PlanInfeasible(f"no TP group can host stage {s}")
-        gen = prev.generation + 1 if generation is None else generation
-        best = self._plan_from_members(members, prev, topology, gen)
-        # joint keep-or-evict: Eq. 4 alone cannot see that a weakened group may slow the whole
-        # stage more than handing its micro-batches to peer replicas would
-        weakened = [k for k, devs in members.items()
-                    if len(devs) < c.tp * c.cp or min(alive[d].speed for d in devs) < 1.0]
-        for key in weakened:
-            if sum(1 for k in members if k[1] == key[1]) < 2:
-                continue
-            variant = {k: v for k, v in members.items() if k != key}
             try:
-                cand = self._plan_from_members(variant, prev, topology, gen)
+                trial = self._from_members({k: v for k, v in members.items() if k != key}, prev, topology, gen)
             except ValueError:
                 continue
-            if cand.meta["predicted_iteration_s"] < best.meta["predicted_iteration_s"] - 1e-12:
-                best = cand
+            if trial.meta["predicted_iteration_s"] < best.meta["predicted_iteration_s"] - 1e-12:
+                best = trial
         return best
 
-    def _fill_from_pool(self, members: dict[Key, tuple[str, ...]], pool: dict[str, list[str]], alive: dict,
-                        prev_counts: list[int]) -> None:
-        """Rejoin / grow: rebuild missing (replica, stage) groups of the nominal layout from free
-        devices, then add whole replicas up to ``max_replicas``."""
-        c = self.cfg
-        target = max(c.num_replicas, c.max_replicas or 0)
-        slot = c.tp * c.cp
-
-        def take(stage: int) -> tuple[str, ...] | None:
-            for node in sorted(pool, key=lambda n: (-len(pool[n]), n)):
-                cands = [(d, alive[d].speed) for d in pool[node]]
-                if not cands:
-                    continue
-                choice = self._choose(cands, c.tp, self._k_min(prev_counts[stage], stage))
-                if choice is not None and choice.tp == c.tp:
-                    pool[node] = [d for d in pool[node] if d not in choice.devices]
-                    return choice.devices
-            return None
-
-        for r in range(target):
-            missing = [s for s in range(c.num_stages) if (r, s) not in members]
-            if not missing:
-                continue
-            if r >= c.num_replicas:
-                if len(missing) < c.num_stages:
-                    continue
-                if sum(len(v) // slot for v in pool.values()) < c.num_stages:
-                    break
-            for s in missing:
-                devs = take(s)
-                if devs is not None:
-                    members[(r, s)] = devs
-
-    def _plan_from_members(self, members: dict[Key, tuple[str, ...]], prev: HeteroParallelPlan,
-                           topology: ClusterTopology, gen: int) -> HeteroParallelPlan:
-        c = self.cfg
-        alive = topology.by_id()
-        speed = {d: alive[d].speed for devs in members.values() for d in devs}
-        caps, max_layers = [], []
-        for s in range(c.num_stages):
-            keys = [k for k in members if k[1] == s]
-            caps.append(sum(self._group_speed(members[k], speed) for k in keys))
-            max_layers.append(min(self._max_layers(len(members[k]) // c.cp, s) for k in keys))
-        counts = self._partition(caps, max_layers)
-        used = {d for devs in members.values() for d in devs}
-        standby = [d for d in topology.ids() if d not in used]
-        return self._assemble(gen, members, counts, list(prev.world), standby, topology)
-
     def schedule(self, plan: HeteroParallelPlan, topology: ClusterTopology) -> tuple[Schedule, SimResult]:
+        """The simulated order of ``plan`` as a validated IR, with its simulation."""
         sim = simulate(plan, self.cost_model(plan, topology), self.cfg.split_backward)
         ir = compute_order_to_ir(plan, sim.order)
         validate(plan, ir, self.cfg.split_backward)

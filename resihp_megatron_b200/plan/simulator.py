@@ -1,22 +1,24 @@
 """List-scheduling pipeline simulator, shared by the planner and the fail-slow detector.
 
-Given a plan and a cost model it builds a concrete compute order per physical slot
-(1F1B-like with an in-flight limit, optional zero-bubble W filling), the op timings, each
-slot's peak number of in-flight micro-batches, and the makespan.  Message channels are
-physical (src slot, dst slot, kind) FIFOs consumed strictly in send order -- the NCCL-safety
-discipline -- so every order it produces converts to a valid IR (``ir.compute_order_to_ir``).
+Given a plan and cost functions it produces, per physical slot, a concrete compute order
+(1F1B-like under an in-flight limit, with optional zero-bubble W ops), the timing of every op,
+each slot's peak number of in-flight micro-batches and the makespan.  Messages travel on
+physical ``(source slot, destination slot, kind)`` channels consumed strictly in send order --
+the discipline that keeps NCCL point-to-point safe -- so every order converts to a valid IR.
 
-Scheduling rule: repeatedly pick, over all slots, the candidate op with the earliest start
-time (ties: backward before forward before weight-grad, then lower micro-batch, then lower
-stage, then slot key).  Candidates of a slot: the next entry forward (if under the in-flight
-limit), the heads of the slot's incoming activation channels, the oldest pending last-stage
-backward, the heads of incoming gradient channels, and queued W ops.
-Semantics follow ``resihp/plan/simulator.py:45-251`` of the reference.
+Rule: repeatedly run, over all slots, the ready op with the earliest start time.  Ties go to
+backward before forward before weight-gradient, then the lower micro-batch, then the lower
+stage (within a slot) or the lower slot key (across slots).  A slot's ready ops are: the next
+micro-batch's first-stage forward (under the in-flight limit); forwards whose activation sits at
+the head of an incoming channel (the limit applies to the slot's first chunk); the oldest
+pending last-stage backward; backwards whose gradient heads an incoming channel; queued W ops.
+Parity: ``resihp/plan/simulator.py:45-251`` (same rule, limits and interleaved order).
 """
 
 from __future__ import annotations
 
 import math
+from collections import defaultdict
 from dataclasses import dataclass, field
 from typing import Callable
 
@@ -26,7 +28,7 @@ Key = tuple[int, int]
 CostFn = Callable[[Key, str, int], float]
 CommFn = Callable[[Key, Key, str], float]
 
-_PRIORITY = {"B": 0, "F": 1, "W": 2}
+_RANK = {"B": 0, "F": 1, "W": 2}
 
 
 @dataclass
@@ -52,205 +54,200 @@ class SimResult:
 
 
 def default_inflight_limit(plan: HeteroParallelPlan) -> dict[Key, float]:
-    """Micro-batches a physical slot may hold between its first forward and last backward.
+    """How many micro-batches a physical slot may hold between first forward and last backward.
 
-    Plain 1F1B: warm-up depth ``P - p``, scaled up by the slot's share of its stage's
-    micro-batches (a slot that absorbs migrated micro-batches needs proportionally more
-    warm-up).  Interleaved: only the pipeline entry is limited, to the interleaved warm-up
-    depth, which bounds every slot (a per-slot limit could block a chunk-0 message at a
-    channel head in front of a chunk-1 message)."""
+    Plain 1F1B: the warm-up depth ``P - p`` scaled by the slot's share of its stage's
+    micro-batches (a slot that absorbed migrated micro-batches needs proportionally deeper
+    warm-up).  Interleaved: only the pipeline entry is limited, to the interleaved warm-up depth;
+    that bounds every slot, whereas per-slot limits could stall a chunk-0 message at a channel
+    head in front of a chunk-1 message."""
     P, v = plan.num_physical_stages, plan.vpp
-    lim: dict[Key, float] = {}
+    entry_depth = math.ceil(((P - 1) * 2 + (v - 1) * P) / v) + 1
+    limits: dict[Key, float] = {}
     for g in plan.stage_groups:
-        r, p = plan.physical_key(g.replica, g.stage)
-        if v == 1:
-            share = len(plan.microbatches_of(r, p)) * plan.num_replicas / plan.num_microbatches
-            lim[(r, p)] = max(1, math.ceil((P - p) * max(1.0, share)))
-        else:
-            lim[(r, p)] = (math.ceil(((P - 1) * 2 + (v - 1) * P) / v) + 1) if p == 0 else math.inf
-    return lim
+        slot = plan.physical_key(g.replica, g.stage)
+        r, p = slot
+        if v > 1:
+            limits[slot] = entry_depth if p == 0 else math.inf
+            continue
+        share = len(plan.microbatches_of(r, p)) * plan.num_replicas / plan.num_microbatches
+        limits[slot] = max(1, math.ceil((P - p) * max(1.0, share)))
+    return limits
 
 
 def megatron_interleaved_order(plan: HeteroParallelPlan, split_backward: bool = False):
-    """The static interleaved 1F1B order per physical slot: forwards in groups of ``P``
-    micro-batches chunk by chunk, backwards with chunks reversed, warm-up
-    ``(P - p - 1) * 2 + (v - 1) * P``; with a split backward each W follows its B.  ``None``
-    when the chunks of a slot run different micro-batch sets."""
+    """Megatron's static interleaved 1F1B order per physical slot: forwards in rounds of ``P``
+    micro-batches chunk by chunk, backwards with the chunks reversed, a warm-up of
+    ``(P - p - 1) * 2 + (v - 1) * P`` forwards; a split backward puts each W right after its B.
+    ``None`` when the chunks of a slot run different micro-batch sets."""
     P, v = plan.num_physical_stages, plan.vpp
-    out: dict[Key, list[tuple]] = {}
+    orders: dict[Key, list[tuple]] = {}
     for g in plan.stage_groups:
-        r, p = plan.physical_key(g.replica, g.stage)
-        if (r, p) in out:
+        slot = plan.physical_key(g.replica, g.stage)
+        if slot in orders:
             continue
+        r, p = slot
         mbs = plan.microbatches_of(r, p)
-        for c in range(v):
-            if plan.group(r, p + c * P) is None or plan.microbatches_of(r, p + c * P) != mbs:
-                return None
+        same_set = all(plan.group(r, p + c * P) is not None and plan.microbatches_of(r, p + c * P) == mbs
+                       for c in range(v))
+        if not same_set:
+            return None
         n = len(mbs)
-
-        def nth(k: int, backward: bool) -> tuple[int, int]:
-            base = (k // (P * v)) * P
-            width = min(P, n - base)
-            c, i = divmod(k - base * v, width)
-            chunk = (v - 1 - c) if backward else c
-            return mbs[base + i], chunk * P + p
-
         total = n * v
+
+        def item(k: int, backward: bool) -> tuple[int, int]:
+            round_start = (k // (P * v)) * P
+            width = min(P, n - round_start)
+            chunk, i = divmod(k - round_start * v, width)
+            if backward:
+                chunk = v - 1 - chunk
+            return mbs[round_start + i], chunk * P + p
+
         warm = min(total, (P - p - 1) * 2 + (v - 1) * P)
-        seq: list[tuple] = [("F",) + nth(k, False) for k in range(warm)]
-
-        def push_back(i: int) -> None:
-            mb, s = nth(i, True)
-            seq.append(("B", mb, s))
-            if split_backward:
-                seq.append(("W", mb, s))
-
-        for i in range(total - warm):
-            seq.append(("F",) + nth(warm + i, False))
-            push_back(i)
-        for i in range(total - warm, total):
-            push_back(i)
-        out[(r, p)] = seq
-    return out
+        seq = [("F", *item(k, False)) for k in range(warm)]
+        backs = []
+        for k in range(total):
+            mb, s = item(k, True)
+            backs.append([("B", mb, s)] + ([("W", mb, s)] if split_backward else []))
+        for k in range(total - warm):
+            seq.append(("F", *item(warm + k, False)))
+            seq.extend(backs[k])
+        for k in range(total - warm, total):
+            seq.extend(backs[k])
+        orders[slot] = seq
+    return orders
 
 
-class _Channels:
-    """FIFO message channels keyed by (src slot, dst slot, kind)."""
+class _Scheduler:
+    def __init__(self, plan, cost, comm, split_backward, inflight_limit, fixed):
+        self.plan, self.cost, self.comm, self.split, self.fixed = plan, cost, comm, split_backward, fixed
+        self.S, self.interleaved = plan.num_stages, plan.vpp > 1
+        units = [(g.replica, g.stage) for g in plan.stage_groups]
+        self.slot_of = {u: plan.physical_key(*u) for u in units}
+        self.slots = sorted(set(self.slot_of.values()))
+        self.chunks = {k: sorted(u[1] for u in units if self.slot_of[u] == k) for k in self.slots}
+        self.limit = default_inflight_limit(plan) if inflight_limit is None else inflight_limit
+        self.entry_queue = {u: [m for m in range(plan.num_microbatches) if plan.executor(u[1], m) == u[0]]
+                            for u in units}
+        self.remaining = sum(map(len, self.entry_queue.values())) * (3 if split_backward else 2)
+        self.fwd_end = {u: {} for u in units}
+        self.bwd_end = {u: {} for u in units}
+        self.w_queue = {k: [] for k in self.slots}
+        self.clock = dict.fromkeys(self.slots, 0.0)
+        self.busy = dict.fromkeys(self.slots, 0.0)
+        self.holding = dict.fromkeys(self.slots, 0)
+        self.peak = dict.fromkeys(self.slots, 0)
+        self.order = {k: [] for k in self.slots}
+        self.ops: list[SimOp] = []
+        self.cursor = dict.fromkeys(self.slots, 0)
+        self.queues: dict[tuple, list] = defaultdict(list)  # channel -> [(mb, stage, arrival)]
+        self.taken: dict[tuple, int] = defaultdict(int)
 
-    def __init__(self):
-        self.msgs: dict[tuple, list[tuple[int, int, float]]] = {}
-        self.head: dict[tuple, int] = {}
+    def _heads(self, dst: Key, kind: str):
+        for ch, q in self.queues.items():
+            if ch[1] == dst and ch[2] == kind and self.taken[ch] < len(q):
+                mb, stage, t = q[self.taken[ch]]
+                yield mb, stage, t, ch
 
-    def push(self, ch: tuple, mb: int, stage: int, t: float) -> None:
-        self.msgs.setdefault(ch, []).append((mb, stage, t))
-        self.head.setdefault(ch, 0)
+    def _ready(self, k: Key) -> list[tuple]:
+        r, first = k[0], self.chunks[k][0]
+        t0 = self.clock[k]
+        room = self.holding[k] < self.limit.get(k, math.inf)
+        ready = []
+        if 0 in self.chunks[k] and room and self.entry_queue[(r, 0)]:
+            ready.append((t0, "F", self.entry_queue[(r, 0)][0], 0, None))
+        ready += [(max(t0, t), "F", mb, s, ch) for mb, s, t, ch in self._heads(k, "act") if room or s != first]
+        if self.S - 1 in self.chunks[k]:
+            tail = (r, self.S - 1)
+            open_mbs = [m for m in self.fwd_end[tail] if m not in self.bwd_end[tail]]
+            if open_mbs:
+                m = min(open_mbs)
+                ready.append((max(t0, self.fwd_end[tail][m]), "B", m, self.S - 1, None))
+        ready += [(max(t0, t, self.fwd_end[(r, s)][mb]), "B", mb, s, ch) for mb, s, t, ch in self._heads(k, "grad")]
+        if self.split and self.w_queue[k]:
+            for s, m in (self.w_queue[k] if self.fixed is not None else self.w_queue[k][:1]):
+                ready.append((max(t0, self.bwd_end[(r, s)][m]), "W", m, s, None))
+        if self.fixed is not None:
+            script = self.fixed[k]
+            nxt = tuple(script[self.cursor[k]]) if self.cursor[k] < len(script) else None
+            ready = [c for c in ready if (c[1], c[2], c[3]) == nxt]
+        return ready
 
-    def heads_into(self, dst: Key, kind: str):
-        for ch, q in self.msgs.items():
-            h = self.head[ch]
-            if ch[1] == dst and ch[2] == kind and h < len(q):
-                yield q[h] + (ch,)
+    def _emit(self, k: Key, choice: tuple) -> None:
+        start, op, mb, s, ch = choice
+        unit = (k[0], s)
+        end = start + self.cost(unit, op, mb)
+        self.busy[k] += end - start
+        self.clock[k] = end
+        self.order[k].append((op, mb, s) if self.interleaved else (op, mb))
+        self.ops.append(SimOp(k, op, mb, start, end, s if self.interleaved else None))
+        self.cursor[k] += 1
+        if ch is not None:
+            self.taken[ch] += 1
+        first = self.chunks[k][0]
+        if op == "W":
+            self.w_queue[k].remove((s, mb))
+            return
+        if op == "F":
+            if s == 0:
+                self.entry_queue[unit].remove(mb)
+            self.fwd_end[unit][mb] = end
+            if s == first:
+                self.holding[k] += 1
+                self.peak[k] = max(self.peak[k], self.holding[k])
+            nxt, kind = s + 1, "act"
+        else:
+            self.bwd_end[unit][mb] = end
+            if s == first:
+                self.holding[k] -= 1
+            if self.split:
+                self.w_queue[k].append((s, mb))
+            nxt, kind = s - 1, "grad"
+        if 0 <= nxt < self.S:
+            peer = (self.plan.executor(nxt, mb), nxt)
+            self.queues[(k, self.slot_of[peer], kind)].append((mb, nxt, end + self.comm(unit, peer, kind)))
 
-    def pop(self, ch: tuple) -> None:
-        self.head[ch] += 1
+    def run(self, sync_time, optimizer_time) -> SimResult:
+        for _ in range(self.remaining):
+            pick = None
+            for k in self.slots:
+                ready = self._ready(k)
+                if not ready:
+                    continue
+                c = min(ready, key=lambda c: (c[0], _RANK[c[1]], c[2], c[3]))
+                if pick is None or (c[0], _RANK[c[1]], k) < pick[0]:
+                    pick = ((c[0], _RANK[c[1]], k), k, c)
+            if pick is None:
+                return SimResult(self.order, self.ops, math.inf, dict(self.clock), self.busy, self.peak, deadlock=True)
+            self._emit(pick[1], pick[2])
+        finish = {}
+        for k in self.slots:
+            tail = sum(sync_time((k[0], s)) for s in self.chunks[k]) if sync_time else 0.0
+            finish[k] = self.clock[k] + tail
+        fwd_done = {k: max((t for s in self.chunks[k] for t in self.fwd_end[(k[0], s)].values()), default=0.0)
+                    for k in self.slots}
+        return SimResult(self.order, self.ops, max(finish.values(), default=0.0) + optimizer_time, finish,
+                         self.busy, self.peak, stage_forward_done=fwd_done)
 
 
 def list_schedule(plan: HeteroParallelPlan, cost: CostFn, comm: CommFn, *, split_backward: bool = False,
                   inflight_limit: dict[Key, float] | None = None, sync_time: Callable[[Key], float] | None = None,
                   optimizer_time: float = 0.0, fixed: dict[Key, list[tuple]] | None = None) -> SimResult:
-    """Greedy earliest-start scheduling of F/B/(W) over physical slots (see module docstring).
-    With ``fixed`` each slot follows the given ``(op, mb, stage)`` sequence and only timing is
-    computed."""
-    S, M = plan.num_stages, plan.num_microbatches
-    interleaved = plan.vpp > 1
-    units = [(g.replica, g.stage) for g in plan.stage_groups]
-    slot_of = {u: plan.physical_key(*u) for u in units}
-    slots = sorted(set(slot_of.values()))
-    chunks = {k: sorted(u[1] for u in units if slot_of[u] == k) for k in slots}
-    limit = inflight_limit if inflight_limit is not None else default_inflight_limit(plan)
-    todo_f0 = {u: [m for m in range(M) if plan.executor(u[1], m) == u[0]] for u in units}
-    n_ops = sum(len(v) for v in todo_f0.values()) * (3 if split_backward else 2)
-    f_end: dict[Key, dict[int, float]] = {u: {} for u in units}
-    b_end: dict[Key, dict[int, float]] = {u: {} for u in units}
-    w_queue: dict[Key, list[tuple[int, int]]] = {k: [] for k in slots}
-    free = {k: 0.0 for k in slots}
-    busy = {k: 0.0 for k in slots}
-    inflight = {k: 0 for k in slots}
-    peak = {k: 0 for k in slots}
-    order: dict[Key, list[tuple]] = {k: [] for k in slots}
-    ops: list[SimOp] = []
-    chans = _Channels()
-    cursor = {k: 0 for k in slots} if fixed is not None else None
-
-    def candidates(k: Key) -> list[tuple]:
-        r, first = k[0], chunks[k][0]
-        under = inflight[k] < limit.get(k, math.inf)
-        out = []
-        if 0 in chunks[k] and todo_f0[(r, 0)] and under:
-            out.append((free[k], "F", todo_f0[(r, 0)][0], 0, None))
-        for mb, s, t, ch in chans.heads_into(k, "act"):
-            if s != first or under:
-                out.append((max(free[k], t), "F", mb, s, ch))
-        if S - 1 in chunks[k]:
-            u = (r, S - 1)
-            pending = sorted(m for m in f_end[u] if m not in b_end[u])
-            if pending:
-                out.append((max(free[k], f_end[u][pending[0]]), "B", pending[0], S - 1, None))
-        for mb, s, t, ch in chans.heads_into(k, "grad"):
-            out.append((max(free[k], t, f_end[(r, s)][mb]), "B", mb, s, ch))
-        if split_backward and w_queue[k]:
-            queued = w_queue[k] if fixed is not None else w_queue[k][:1]
-            for s, m in queued:
-                out.append((max(free[k], b_end[(r, s)][m]), "W", m, s, None))
-        if fixed is not None:
-            seq = fixed[k]
-            want = tuple(seq[cursor[k]]) if cursor[k] < len(seq) else None
-            out = [c for c in out if want is not None and (c[1], c[2], c[3]) == want]
-        return out
-
-    for _ in range(n_ops):
-        best = None
-        for k in slots:
-            cands = candidates(k)
-            if not cands:
-                continue
-            c = min(cands, key=lambda c: (c[0], _PRIORITY[c[1]], c[2], c[3]))
-            rank = (c[0], _PRIORITY[c[1]], k)
-            if best is None or rank < best[0]:
-                best = (rank, k, c)
-        if best is None:
-            return SimResult(order, ops, math.inf, dict(free), busy, peak, deadlock=True)
-        _, k, (start, op, mb, s, ch) = best
-        u = (k[0], s)
-        end = start + cost(u, op, mb)
-        busy[k] += end - start
-        free[k] = end
-        order[k].append((op, mb, s) if interleaved else (op, mb))
-        ops.append(SimOp(k, op, mb, start, end, s if interleaved else None))
-        if cursor is not None:
-            cursor[k] += 1
-        if ch is not None:
-            chans.pop(ch)
-        if op == "F":
-            if s == 0:
-                todo_f0[u].remove(mb)
-            f_end[u][mb] = end
-            if s == chunks[k][0]:
-                inflight[k] += 1
-                peak[k] = max(peak[k], inflight[k])
-            if s < S - 1:
-                dst = (plan.executor(s + 1, mb), s + 1)
-                chans.push((k, slot_of[dst], "act"), mb, s + 1, end + comm(u, dst, "act"))
-        elif op == "B":
-            b_end[u][mb] = end
-            if s == chunks[k][0]:
-                inflight[k] -= 1
-            if split_backward:
-                w_queue[k].append((s, mb))
-            if s > 0:
-                dst = (plan.executor(s - 1, mb), s - 1)
-                chans.push((k, slot_of[dst], "grad"), mb, s - 1, end + comm(u, dst, "grad"))
-        else:
-            w_queue[k].remove((s, mb))
-
-    finish = {k: free[k] + (sum(sync_time((k[0], s)) for s in chunks[k]) if sync_time else 0.0) for k in slots}
-    fwd_done = {k: max((t for s in chunks[k] for t in f_end[(k[0], s)].values()), default=0.0) for k in slots}
-    return SimResult(order, ops, max(finish.values(), default=0.0) + optimizer_time, finish, busy, peak,
-                     stage_forward_done=fwd_done)
+    """Greedy earliest-start schedule of F/B/(W) over the physical slots (module docstring).
+    With ``fixed``, each slot follows its given ``(op, mb, stage)`` sequence and only the timing
+    is computed."""
+    return _Scheduler(plan, cost, comm, split_backward, inflight_limit, fixed).run(sync_time, optimizer_time)
 
 
 def schedule_with_fallback(plan: HeteroParallelPlan, cost: CostFn, comm: CommFn, **kw) -> SimResult:
-    """The in-flight-limited schedule (for interleaved plans also the static interleaved
-    order, whichever the simulation finds faster); unlimited in-flight -- always deadlock
-    free -- when the limited one deadlocks."""
-    unlimited = {plan.physical_key(g.replica, g.stage): math.inf for g in plan.stage_groups}
-    res = list_schedule(plan, cost, comm, **kw)
-    if plan.vpp > 1:
-        fixed = megatron_interleaved_order(plan, kw.get("split_backward", False))
-        if fixed is not None:
-            alt = list_schedule(plan, cost, comm, fixed=fixed, **{**kw, "inflight_limit": unlimited})
-            if not alt.deadlock and (res.deadlock or alt.makespan < res.makespan):
-                res = alt
-    if not res.deadlock:
-        return res
-    return list_schedule(plan, cost, comm, **{**kw, "inflight_limit": unlimited})
+    """The in-flight-limited schedule -- for interleaved plans the faster of it and Megatron's
+    static interleaved order -- or, if that deadlocks, the unlimited one (never deadlocks)."""
+    no_limit = {plan.physical_key(g.replica, g.stage): math.inf for g in plan.stage_groups}
+    unlimited = {**kw, "inflight_limit": no_limit}
+    best = list_schedule(plan, cost, comm, **kw)
+    static = megatron_interleaved_order(plan, kw.get("split_backward", False)) if plan.vpp > 1 else None
+    if static is not None:
+        alt = list_schedule(plan, cost, comm, fixed=static, **unlimited)
+        if not alt.deadlock and (best.deadlock or alt.makespan < best.makespan):
+            best = alt
+    return best if not best.deadlock else list_schedule(plan, cost, comm, **unlimited)
