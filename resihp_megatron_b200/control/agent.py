@@ -1,20 +1,20 @@
-"""NodeAgent: one per node.
+"""NodeAgent: one per node, between the node's workers and the coordinator.
 
-* Spawns (or adopts) the node's workers and never tears down healthy workers when a peer
-  dies (the opposite of an elastic launcher that restarts everyone).
-* Aggregates worker heartbeats into one node heartbeat, so coordinator load scales with
+* Starts (or adopts) the node's workers and never tears healthy ones down when a peer dies --
+  the opposite of an elastic launcher that restarts everybody.
+* Folds the workers' heartbeats into one node heartbeat, so the coordinator's load grows with
   nodes, not GPUs.
-* Detects local deaths immediately: process exit, lost control connection, stalled heartbeat
-  (hang) and fatal health events, and reports them.
-* Executes fencing (SIGKILL) on coordinator command.
-* Fails over between coordinator replicas; after ``self_fence_after`` seconds without any
-  coordinator it tells its workers to self-fence (abort their communicators).
-
-Behaviour follows ``resihp/control/agent.py:59-265`` of the reference.
+* Notices local deaths at once -- process exit, a lost control connection, a heartbeat that
+  stalled (a hang), a fatal health event -- and reports them.
+* Fences on command: SIGKILL of a worker the coordinator declared failed.
+* Fails over between coordinator replicas; after ``self_fence_after`` seconds with no
+  coordinator at all it tells its workers to self-fence (abort their communicators).
+Parity: ``resihp/control/agent.py:59-265`` (same duties, messages and environment variables).
 """
 
 from __future__ import annotations
 
+import contextlib
 import os
 import signal
 import subprocess
@@ -30,7 +30,7 @@ log = get_logger(__name__)
 
 
 def pid_alive(pid: int) -> bool:
-    """True while ``pid`` exists and is not a reaped/zombie child of this process."""
+    """Whether ``pid`` still runs (a zombie child of this process counts as gone)."""
     if pid <= 0:
         return False
     try:
@@ -38,12 +38,12 @@ def pid_alive(pid: int) -> bool:
     except ProcessLookupError:
         return False
     except PermissionError:
-        return True
+        return True  # exists, owned by someone else
     try:
-        done, _ = os.waitpid(pid, os.WNOHANG)
-        return done == 0
+        reaped, _status = os.waitpid(pid, os.WNOHANG)
     except ChildProcessError:
-        return True
+        return True  # not our child: existence is all we can know
+    return reaped == 0
 
 
 @dataclass
@@ -58,6 +58,64 @@ class LocalWorker:
     progress: dict = field(default_factory=dict)
     dead: bool = False
 
+    def death_reason(self, now: float, stall_after: float) -> str | None:
+        code = self.proc.poll() if self.proc is not None else None
+        if code is not None:
+            return f"exited with {code}"
+        if self.proc is None and self.pid and not pid_alive(self.pid):
+            return "process gone"
+        silent = now - self.last_hb
+        if self.conn is not None and silent > stall_after:
+            return f"heartbeat stalled {silent:.1f}s (hang)"
+        return None
+
+
+class _Uplink:
+    """The agent's link to the current coordinator replica."""
+
+    def __init__(self, agent: "NodeAgent", addrs):
+        self.agent, self.addrs = agent, list(addrs)
+        self.conn: Connection | None = None
+        self.lost_at: float | None = None
+        self.fenced = False
+
+    def send(self, message: dict) -> None:
+        link = self.conn
+        if link is None or not link.send(message):
+            log.warning("no coordinator; dropped %s", message.get("type"))
+
+    def dial(self, timeout: float) -> bool:
+        """Try every replica until one answers (or ``timeout``), then register this node."""
+        a = self.agent
+        give_up = time.monotonic() + timeout
+        while time.monotonic() < give_up and not a._stopped.is_set():
+            for addr in self.addrs:
+                try:
+                    link = connect(addr, a._from_coordinator, self._closed, timeout=0.5, name=f"agent-{a.node_id}")
+                except TimeoutError:
+                    continue
+                with a._lock:
+                    self.conn, self.lost_at, self.fenced = link, None, False
+                    known = [dict(worker_id=w.worker_id, node_id=a.node_id, local_rank=w.local_rank, pid=w.pid,
+                                  device=w.device) for w in a.workers.values() if not w.dead and w.conn is not None]
+                link.send(P.msg(P.AGENT_REGISTER, node_id=a.node_id, workers=known))
+                return True
+            time.sleep(0.1)
+        return False
+
+    def _closed(self, conn: Connection) -> None:
+        with self.agent._lock:
+            if self.conn is conn:
+                self.conn, self.lost_at = None, time.monotonic()
+
+    def overdue(self, after: float) -> bool:
+        """True once per outage, when no coordinator has answered for ``after`` seconds."""
+        since = self.lost_at if self.lost_at is not None else time.monotonic()
+        if self.fenced or time.monotonic() - since <= after:
+            return False
+        self.fenced = True
+        return True
+
 
 class NodeAgent:
     def __init__(self, node_id: str, coordinator_addrs: list[tuple[str, int]], *, host: str = "127.0.0.1",
@@ -65,18 +123,13 @@ class NodeAgent:
                  self_fence_after: float = 5.0, health_probe=None, health_every: int = 8):
         self.node_id = node_id
         self.coordinator_addrs = list(coordinator_addrs)
-        self.hb_interval = hb_interval
-        self.worker_timeout = worker_timeout
-        self.self_fence_after = self_fence_after
-        self.health_probe = health_probe
-        self.health_every = health_every
+        self.hb_interval, self.worker_timeout, self.self_fence_after = hb_interval, worker_timeout, self_fence_after
+        self.health_probe, self.health_every = health_probe, health_every
         self.workers: dict[str, LocalWorker] = {}
         self._lock = threading.RLock()
-        self._coord: Connection | None = None
-        self._coord_lost_at: float | None = None
-        self._fence_sent = False
         self._stopped = threading.Event()
-        self.server = Server(host, port, self._on_worker_message, on_close=self._on_worker_close)
+        self._up = _Uplink(self, coordinator_addrs)
+        self.server = Server(host, port, self._from_worker, on_close=self._worker_link_closed)
         self._threads: list[threading.Thread] = []
 
     @property
@@ -84,190 +137,146 @@ class NodeAgent:
         return self.server.address
 
     def start(self) -> "NodeAgent":
-        self._connect_coordinator()
-        for fn, name in ((self._heartbeat_loop, "agent-hb"), (self._monitor_loop, "agent-monitor")):
-            t = threading.Thread(target=fn, name=f"{name}-{self.node_id}", daemon=True)
-            t.start()
+        self._up.dial(timeout=10.0)
+        for loop, name in ((self._beat, "agent-hb"), (self._sweep, "agent-monitor")):
+            t = threading.Thread(target=loop, name=f"{name}-{self.node_id}", daemon=True)
             self._threads.append(t)
+            t.start()
         return self
 
     def stop(self, kill_workers: bool = False) -> None:
         self._stopped.set()
         if kill_workers:
             for w in list(self.workers.values()):
-                self._kill(w)
-        if self._coord is not None:
-            self._coord.close()
+                self._sigkill(w)
+        if self._up.conn is not None:
+            self._up.conn.close()
         self.server.stop()
 
-    # ------------------------------------------------------------------ workers
+    # ------------------------------------------------------------------ processes
     def spawn(self, cmd: list[str], nproc: int, env: dict[str, str] | None = None,
               devices: list[str] | None = None, first_rank: int = 0) -> list[LocalWorker]:
-        """Start ``nproc`` workers (local ranks ``first_rank ..``); each gets its identity through
-        ``RESIHP_*`` variables.  A later call with a higher ``first_rank`` adds workers to a
-        running job (a replacement GPU, a grown node): they register and join at the next
-        generation."""
-        started = []
-        for i in range(first_rank, first_rank + nproc):
-            wid = f"{self.node_id}g{i}"
-            dev = devices[i - first_rank] if devices else "cpu"
-            wenv = {**os.environ, **(env or {}),
-                    "RESIHP_AGENT_ADDR": fmt_addr(self.address), "RESIHP_WORKER_ID": wid,
-                    "RESIHP_NODE_ID": self.node_id, "RESIHP_LOCAL_RANK": str(i), "RESIHP_DEVICE": dev}
-            if dev.startswith("cuda:"):
-                wenv["CUDA_VISIBLE_DEVICES"] = dev.split(":", 1)[1]
-            proc = subprocess.Popen(cmd, env=wenv)
-            w = LocalWorker(worker_id=wid, local_rank=i, pid=proc.pid, device=dev, proc=proc)
+        """Start ``nproc`` workers with local ranks ``first_rank, first_rank + 1, ...``; each learns
+        its identity from ``RESIHP_*`` variables (and its GPU from ``CUDA_VISIBLE_DEVICES``).  A
+        later call with a higher ``first_rank`` adds workers to a running job -- a replacement GPU,
+        a grown node -- which register and join at the next generation."""
+        launched = []
+        for k in range(nproc):
+            rank = first_rank + k
+            device = devices[k] if devices else "cpu"
+            wid = f"{self.node_id}g{rank}"
+            child_env = dict(os.environ)
+            child_env.update(env or {})
+            child_env.update(RESIHP_AGENT_ADDR=fmt_addr(self.address), RESIHP_WORKER_ID=wid,
+                             RESIHP_NODE_ID=self.node_id, RESIHP_LOCAL_RANK=str(rank), RESIHP_DEVICE=device)
+            if device.startswith("cuda:"):
+                child_env["CUDA_VISIBLE_DEVICES"] = device.partition(":")[2]
+            proc = subprocess.Popen(cmd, env=child_env)
+            w = LocalWorker(wid, rank, pid=proc.pid, device=device, proc=proc)
             with self._lock:
                 self.workers[wid] = w
-            started.append(w)
-        return started
+            launched.append(w)
+        return launched
 
-    def _on_worker_message(self, conn: Connection, m: dict) -> None:
-        kind = m.get("type")
-        now = time.monotonic()
-        if kind == P.REGISTER:
-            wid = m["worker_id"]
-            with self._lock:
-                w = self.workers.get(wid)
-                if w is None or w.dead:
-                    w = LocalWorker(worker_id=wid, local_rank=m.get("local_rank", 0))
-                    self.workers[wid] = w
-                w.pid = m.get("pid", w.pid)
-                w.device = m.get("device", w.device)
-                w.conn = conn
-                w.last_hb = now
-                conn.meta["worker_id"] = wid
-            self._to_coord(P.msg(P.WORKER_REGISTER, worker_id=wid, node_id=self.node_id, local_rank=w.local_rank,
-                                 pid=w.pid, device=w.device))
-            return
-        wid = conn.meta.get("worker_id")
-        if wid is None:
+    def _sigkill(self, w: LocalWorker) -> None:
+        if w.pid > 0:
+            with contextlib.suppress(ProcessLookupError):
+                os.kill(w.pid, signal.SIGKILL)
+        if w.proc is not None:
+            with contextlib.suppress(subprocess.TimeoutExpired):
+                w.proc.wait(timeout=5)
+
+    def _declare_dead(self, w: LocalWorker, reason: str) -> None:
+        if not w.dead:
+            w.dead = True
+            log.warning("worker %s dead: %s", w.worker_id, reason)
+            self._up.send(P.msg(P.WORKER_FAILED, worker_id=w.worker_id, node_id=self.node_id, reason=reason))
+
+    # ------------------------------------------------------------------ worker side
+    def _from_worker(self, conn: Connection, m: dict) -> None:
+        if m.get("type") == P.REGISTER:
+            self._adopt(conn, m)
             return
         with self._lock:
-            w = self.workers.get(wid)
+            w = self.workers.get(conn.meta.get("worker_id"))
             if w is None or w.dead:
                 return
-            w.last_hb = now
-            if kind == P.HEARTBEAT:
+            w.last_hb = time.monotonic()
+            if m.get("type") == P.HEARTBEAT:
                 w.progress = m.get("progress", {})
                 return
-        self._to_coord(P.msg(P.WORKER_MSG, worker_id=wid, msg=m))
+        self._up.send(P.msg(P.WORKER_MSG, worker_id=w.worker_id, msg=m))
 
-    def _on_worker_close(self, conn: Connection) -> None:
+    def _adopt(self, conn: Connection, m: dict) -> None:
+        wid = m["worker_id"]
+        with self._lock:
+            w = self.workers.get(wid)
+            if w is None or w.dead:  # a worker this agent did not start (or a restarted one)
+                w = self.workers[wid] = LocalWorker(wid, m.get("local_rank", 0))
+            w.pid, w.device = m.get("pid", w.pid), m.get("device", w.device)
+            w.conn, w.last_hb = conn, time.monotonic()
+            conn.meta["worker_id"] = wid
+        self._up.send(P.msg(P.WORKER_REGISTER, worker_id=wid, node_id=self.node_id, local_rank=w.local_rank,
+                            pid=w.pid, device=w.device))
+
+    def _worker_link_closed(self, conn: Connection) -> None:
         wid = conn.meta.get("worker_id")
         if wid is None or self._stopped.is_set():
             return
         with self._lock:
             w = self.workers.get(wid)
             if w is not None and w.conn is conn:
-                self._mark_dead(w, "control connection lost")
+                self._declare_dead(w, "control connection lost")
 
-    def _mark_dead(self, w: LocalWorker, reason: str) -> None:
-        if w.dead:
-            return
-        w.dead = True
-        log.warning("worker %s dead: %s", w.worker_id, reason)
-        self._to_coord(P.msg(P.WORKER_FAILED, worker_id=w.worker_id, node_id=self.node_id, reason=reason))
-
-    def _kill(self, w: LocalWorker) -> None:
-        if w.pid > 0:
-            try:
-                os.kill(w.pid, signal.SIGKILL)
-            except ProcessLookupError:
-                pass
-        if w.proc is not None:
-            try:
-                w.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                pass
-
-    def _monitor_loop(self) -> None:
-        polls = 0
+    def _sweep(self) -> None:
+        """Liveness of every local worker, and (every ``health_every`` sweeps) the health probe."""
+        sweeps = 0
         while not self._stopped.is_set():
             now = time.monotonic()
             with self._lock:
-                for w in list(self.workers.values()):
-                    if w.dead:
-                        continue
-                    if w.proc is not None and w.proc.poll() is not None:
-                        self._mark_dead(w, f"exited with {w.proc.returncode}")
-                    elif w.proc is None and w.pid and not pid_alive(w.pid):
-                        self._mark_dead(w, "process gone")
-                    elif w.conn is not None and now - w.last_hb > self.worker_timeout:
-                        self._mark_dead(w, f"heartbeat stalled {now - w.last_hb:.1f}s (hang)")
-            polls += 1
-            if self.health_probe is not None and polls % self.health_every == 0:
-                for ev in self.health_probe.poll():
-                    if not ev.fatal:
-                        continue
-                    with self._lock:
-                        for w in self.workers.values():
-                            if not w.dead and ev.matches(w.device):
-                                self._mark_dead(w, f"health: {ev.describe()}")
+                for w in [w for w in self.workers.values() if not w.dead]:
+                    why = w.death_reason(now, self.worker_timeout)
+                    if why is not None:
+                        self._declare_dead(w, why)
+            sweeps += 1
+            if self.health_probe is not None and sweeps % self.health_every == 0:
+                self._apply_health(self.health_probe.poll())
             time.sleep(self.hb_interval / 2)
 
-    # ------------------------------------------------------------------ coordinator link
-    def _to_coord(self, message: dict) -> None:
-        conn = self._coord
-        if conn is None or not conn.send(message):
-            log.warning("no coordinator; dropped %s", message.get("type"))
+    def _apply_health(self, events) -> None:
+        for ev in filter(lambda e: e.fatal, events):
+            with self._lock:
+                for w in self.workers.values():
+                    if not w.dead and ev.matches(w.device):
+                        self._declare_dead(w, f"health: {ev.describe()}")
 
-    def _connect_coordinator(self, timeout: float = 10.0) -> bool:
-        deadline = time.monotonic() + timeout
-        while not self._stopped.is_set() and time.monotonic() < deadline:
-            for addr in self.coordinator_addrs:
-                try:
-                    conn = connect(addr, self._on_coord_message, self._on_coord_close, timeout=0.5,
-                                   name=f"agent-{self.node_id}")
-                except TimeoutError:
-                    continue
-                with self._lock:
-                    self._coord = conn
-                    self._coord_lost_at = None
-                    self._fence_sent = False
-                    live = [{"worker_id": w.worker_id, "node_id": self.node_id, "local_rank": w.local_rank,
-                             "pid": w.pid, "device": w.device}
-                            for w in self.workers.values() if not w.dead and w.conn is not None]
-                conn.send(P.msg(P.AGENT_REGISTER, node_id=self.node_id, workers=live))
-                return True
-            time.sleep(0.1)
-        return False
-
-    def _on_coord_close(self, conn: Connection) -> None:
-        with self._lock:
-            if self._coord is conn:
-                self._coord = None
-                self._coord_lost_at = time.monotonic()
-
-    def _on_coord_message(self, conn: Connection, m: dict) -> None:
+    # ------------------------------------------------------------------ coordinator side
+    def _from_coordinator(self, conn: Connection, m: dict) -> None:
         kind = m.get("type")
+        if kind not in (P.KILL, P.TO_WORKER):
+            return
+        with self._lock:
+            w = self.workers.get(m["worker_id"])
+        if w is None:
+            return
         if kind == P.KILL:
-            with self._lock:
-                w = self.workers.get(m["worker_id"])
-            if w is not None:
-                log.warning("fencing %s: %s", w.worker_id, m.get("reason"))
-                w.dead = True
-                self._kill(w)
-        elif kind == P.TO_WORKER:
-            with self._lock:
-                w = self.workers.get(m["worker_id"])
-            if w is not None and not w.dead and w.conn is not None:
-                w.conn.send(m["msg"])
+            log.warning("fencing %s: %s", w.worker_id, m.get("reason"))
+            w.dead = True
+            self._sigkill(w)
+        elif not w.dead and w.conn is not None:
+            w.conn.send(m["msg"])
 
-    def _heartbeat_loop(self) -> None:
+    def _beat(self) -> None:
         while not self._stopped.is_set():
-            if self._coord is None:
-                lost = self._coord_lost_at or time.monotonic()
-                if not self._fence_sent and time.monotonic() - lost > self.self_fence_after:
+            if self._up.conn is not None:
+                with self._lock:
+                    snapshot = {w.worker_id: w.progress for w in self.workers.values() if not w.dead}
+                self._up.send(P.msg(P.NODE_HEARTBEAT, node_id=self.node_id, progress=snapshot))
+            else:
+                if self._up.overdue(self.self_fence_after):
                     with self._lock:
                         for w in self.workers.values():
                             if not w.dead and w.conn is not None:
                                 w.conn.send(P.msg(P.SELF_FENCE, reason="coordinator unreachable"))
-                    self._fence_sent = True
-                self._connect_coordinator(timeout=self.hb_interval)
-            else:
-                with self._lock:
-                    progress = {w.worker_id: w.progress for w in self.workers.values() if not w.dead}
-                self._to_coord(P.msg(P.NODE_HEARTBEAT, node_id=self.node_id, progress=progress))
+                self._up.dial(timeout=self.hb_interval)
             time.sleep(self.hb_interval)

@@ -1,13 +1,16 @@
-"""Worker records kept by the coordinator (state, incarnation, progress, health).
+"""The coordinator's worker table: state, incarnation, pid, progress and health of every worker.
 
-``progress_changed_at`` moves only when ``(gen, iteration, op_seq)`` changes; the hang
-detector compares it with the clock (reference: ``resihp/control/membership.py:16-77``).
+A worker that registers again under the same id gets a new incarnation unless it is the same
+live process re-announced.  Hang detection reads ``progress_changed_at``: it moves only when the
+worker's position ``(gen, iteration, op_seq)`` moves, not on every heartbeat.
+Parity: ``resihp/control/membership.py:16-77`` (same record fields, persisted by the coordinator).
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass, field
 from enum import Enum
+from operator import attrgetter
 
 
 class WorkerState(str, Enum):
@@ -33,13 +36,15 @@ class WorkerRecord:
 
     @property
     def alive(self) -> bool:
-        return self.state is WorkerState.ALIVE
+        return self.state == WorkerState.ALIVE
 
     def sort_key(self) -> tuple:
-        return (self.node_id, self.local_rank, self.worker_id)
+        """Canonical order of workers: node, local rank, id."""
+        return self.node_id, self.local_rank, self.worker_id
 
 
-_PROGRESS_KEYS = ("gen", "iteration", "op_seq")
+def _position(progress: dict) -> tuple:
+    return progress.get("gen"), progress.get("iteration"), progress.get("op_seq")
 
 
 class Membership:
@@ -47,38 +52,40 @@ class Membership:
         self.workers: dict[str, WorkerRecord] = {}
 
     def register(self, rec: WorkerRecord, now: float) -> WorkerRecord:
-        prev = self.workers.get(rec.worker_id)
-        if prev is not None:
-            same_process = prev.alive and prev.pid == rec.pid
-            rec.incarnation = prev.incarnation + (0 if same_process else 1)
+        earlier = self.workers.get(rec.worker_id)
+        if earlier is not None:
+            restarted = not (earlier.alive and earlier.pid == rec.pid)
+            rec.incarnation = earlier.incarnation + int(restarted)
         rec.progress_changed_at = now
         self.workers[rec.worker_id] = rec
         return rec
 
     def alive(self) -> list[WorkerRecord]:
-        return sorted((w for w in self.workers.values() if w.alive), key=WorkerRecord.sort_key)
+        return sorted(filter(attrgetter("alive"), self.workers.values()), key=WorkerRecord.sort_key)
 
     def alive_ids(self) -> list[str]:
-        return [w.worker_id for w in self.alive()]
+        return list(map(attrgetter("worker_id"), self.alive()))
 
     def on_node(self, node_id: str) -> list[WorkerRecord]:
-        return [w for w in self.workers.values() if w.node_id == node_id]
+        return [rec for rec in self.workers.values() if rec.node_id == node_id]
 
     def mark(self, worker_ids, state: WorkerState) -> list[str]:
-        out = []
+        """Move the live ones among ``worker_ids`` to ``state``; returns those that changed."""
+        changed = []
         for wid in worker_ids:
-            w = self.workers.get(wid)
-            if w is not None and w.alive:
-                w.state = state
-                out.append(wid)
-        return out
+            rec = self.workers.get(wid)
+            if rec and rec.alive:
+                rec.state = state
+                changed.append(wid)
+        return changed
 
     def update_progress(self, worker_id: str, progress: dict, now: float) -> None:
-        w = self.workers.get(worker_id)
-        if w is None or not w.alive:
+        rec = self.workers.get(worker_id)
+        if not (rec and rec.alive):
             return
-        if any(progress.get(k) != w.progress.get(k) for k in _PROGRESS_KEYS):
-            w.progress_changed_at = now
-        w.progress = progress
-        if "p" in progress:
-            w.health["p"] = progress["p"]
+        if _position(progress) != _position(rec.progress):
+            rec.progress_changed_at = now
+        rec.progress = progress
+        speed = progress.get("p")
+        if speed is not None:
+            rec.health["p"] = speed
