@@ -1,19 +1,25 @@
-"""Framework-agnostic resilient training loop.
+"""The framework-agnostic resilient training loop of one worker.
 
-    begin txn -> run iteration (abortable) -> REDUCED -> optimizer step -> COMMIT
-    on any communication failure or reconfiguration notice:
-        abort txn (roll RNG + data cursor back) -> wait PREPARE(g) -> teardown hooks
-        -> build comms(g) -> recover state (roll-forward / peer copy / snapshot / checkpoint)
-        -> build runtime -> rebuild hooks -> READY(g) -> COMMIT(g)
-        -> replay the aborted iteration with the same global batch
+Per iteration::
 
-Survivor processes never restart.  The model, optimizer and runtime come from a
-``RuntimeBinding`` so one loop drives the replica-DP runtime, the heterogeneous hybrid-parallel
-runtime and the GPU engine.  (Reference: ``resihp/train/resilient_loop.py:28-160``.)
+    begin txn -> run the iteration (abortable) -> REDUCED -> optimizer step -> COMMIT
+
+On a communication failure or a reconfiguration notice the iteration's transaction is rolled
+back (RNG and data cursor included) and the worker joins the next generation::
+
+    wait PREPARE(g) -> generation hooks torn down -> comms(g) built -> state recovered
+    (roll-forward, peer copy, snapshot or checkpoint) -> runtime built -> hooks rebuilt
+    -> READY(g) -> COMMIT(g)
+
+after which the aborted iteration is replayed with the same global batch.  Survivors never
+restart.  Everything model-specific comes from a ``RuntimeBinding``, so the same loop drives
+the replica-DP runtime, the heterogeneous hybrid-parallel runtime and the GPU engines.
+Parity: ``resihp/train/resilient_loop.py:28-160`` (same sequence and binding protocol).
 """
 
 from __future__ import annotations
 
+import enum
 import time
 from dataclasses import dataclass, field
 from typing import Protocol
@@ -26,6 +32,7 @@ from ..utils.log import get_logger
 
 log = get_logger(__name__)
 
+# errors after which the worker rejoins at the next generation instead of dying
 RECOVERABLE = (CommAborted, CommTimeout, GenerationBuildError, RuntimeError, ReconfigInterrupted)
 
 
@@ -51,109 +58,139 @@ class TrainResult:
     standby: bool = False
 
 
+class _Join(enum.Enum):
+    MEMBER = "member"      # in the committed world, runtime ready
+    STANDBY = "standby"    # committed, but not in the world
+    RETRY = "retry"        # the generation was superseded or its build failed
+
+
 class ResilientTrainer:
     def __init__(self, client: WorkerClient, mgr: ResilientCommManager, binding: RuntimeBinding, *,
                  txm: TransactionManager | None = None, prepare_timeout: float = 600.0,
                  hooks: GenerationHooks | None = None):
-        self.client = client
-        self.mgr = mgr
-        self.binding = binding
-        self.txm = txm or TransactionManager()
+        self.client, self.mgr, self.binding = client, mgr, binding
+        self.txm = txm if txm is not None else TransactionManager()
         self.prepare_timeout = prepare_timeout
-        self.hooks = hooks or GenerationHooks()
+        self.hooks = hooks if hooks is not None else GenerationHooks()
         self.comms: GenerationComms | None = None
         self.runtime: Runtime | None = None
         self.result = TrainResult()
-        client.add_abort_callback(mgr.abort)
-        if hasattr(binding, "buffers"):
-            self.txm.track_buffers(binding.buffers)
+        client.add_abort_callback(mgr.abort)  # a notice aborts in-flight communication
+        buffers = getattr(binding, "buffers", None)
+        if buffers is not None:
+            self.txm.track_buffers(buffers)
 
     def run(self, num_iterations: int) -> TrainResult:
         self.binding.try_resume(self.txm)
         try:
-            self._reconfigure()
+            self._rejoin()
             while True:
-                self._train(num_iterations)
-                if self.client.finish(self.txm.committed_iteration, timeout=self.prepare_timeout) == "shutdown":
+                self._train_until(num_iterations)
+                verdict = self.client.finish(self.txm.committed_iteration, timeout=self.prepare_timeout)
+                if verdict == "shutdown":
                     break
-                self._reconfigure()  # peers need this worker again (e.g. as a state source)
+                self._rejoin()  # the others still need this worker (e.g. as a state source)
         except JobFinished:
             pass
         return self.result
 
-    def _train(self, num_iterations: int) -> None:
-        while self.txm.committed_iteration + 1 < num_iterations:
+    # ------------------------------------------------------------------ iterations
+    def _step(self, it: int) -> float:
+        """One transactional iteration; raises a RECOVERABLE error when it must be replayed."""
+        if self.client.immediate_abort_pending():
+            raise CommAborted("reconfiguration announced before the iteration started")
+        loss = self.runtime.run_iteration(it)
+        self.txm.on_reduced()
+        self.txm.on_step_begin()
+        self.binding.optimizer_step()
+        self.txm.on_commit()
+        return loss
+
+    def _publish(self, it: int, loss: float) -> None:
+        self.result.losses[it] = loss
+        self.client.set_progress(iteration=it, phase="committed", in_collective=False)
+        self.client.set_recovery_info(**self.txm.recovery_info())
+        self.binding.after_commit(it, self.comms)
+        self.hooks.after_iteration(it)
+
+    def _train_until(self, num_iterations: int) -> None:
+        while (it := self.txm.committed_iteration + 1) < num_iterations:
             if self.runtime is None:
-                self._reconfigure()
+                self._rejoin()
                 continue
-            it = self.txm.committed_iteration + 1
             self.txm.begin(it)
             try:
-                if self.client.immediate_abort_pending():
-                    raise CommAborted("reconfiguration announced before the iteration started")
-                loss = self.runtime.run_iteration(it)
-                self.txm.on_reduced()
-                self.txm.on_step_begin()
-                self.binding.optimizer_step()
-                self.txm.on_commit()
-                self.result.losses[it] = loss
-                self.client.set_progress(iteration=it, phase="committed", in_collective=False)
-                self.client.set_recovery_info(**self.txm.recovery_info())
-                self.binding.after_commit(it, self.comms)
-                self.hooks.after_iteration(it)
+                self._publish(it, self._step(it))
                 if self.client.reconfig_pending():
-                    self._reconfigure()
-            except RECOVERABLE as e:
-                log.warning("iteration %d interrupted: %s", it, e)
+                    self._rejoin()
+            except RECOVERABLE as err:
+                log.warning("iteration %d interrupted: %s", it, err)
                 self.txm.abort()
-                self._reconfigure()
+                self._rejoin()
 
-    def _reconfigure(self) -> None:
-        t0 = time.monotonic()
+    # ------------------------------------------------------------------ generations
+    def _rejoin(self) -> None:
+        started = time.monotonic()
         while True:
             self.client.set_recovery_info(**self.txm.recovery_info())
-            prep = self.client.wait_prepare(timeout=self.prepare_timeout)
-            gen, world, payload = prep["gen"], prep["world"], prep["payload"]
-            me = self.client.worker_id
+            prepare = self.client.wait_prepare(timeout=self.prepare_timeout)
             if self.comms is not None:
-                self.hooks.teardown()  # before the old communicators are destroyed
-            if me not in world:
-                self.mgr.destroy()
-                self.comms, self.runtime = None, None
-                self.client.send_ready(gen, standby=True)
-                try:
-                    self.client.wait_commit(gen, timeout=self.prepare_timeout)
-                except ReconfigInterrupted:
-                    continue
+                self.hooks.teardown()  # before the old communicators go away
+            outcome = self._enter(prepare)
+            if outcome is _Join.MEMBER:
+                self._record(prepare, started)
+                return
+            if outcome is _Join.STANDBY:
                 self.result.standby = True
-                self.result.generations.append(gen)
-                continue
-            try:
-                specs = self.binding.group_specs(world, payload)
-                store_addr = tuple(prep["store_addr"]) if prep.get("store_addr") else None
-                self.comms = None
-                comms = self.mgr.build(gen, world, me, specs, store_addr=store_addr, store_prefix=prep["store_prefix"])
-                self.binding.recover(comms, payload, self.txm)
-                self.runtime = self.binding.build_runtime(comms, payload)
-                self.hooks.rebuild(comms, payload)
-                self.comms = comms
-                self.client.send_ready(gen)
-                self.client.wait_commit(gen, timeout=self.prepare_timeout)
-                on_commit = getattr(self.binding, "on_generation_commit", None)
-                if on_commit is not None:
-                    on_commit()
-            except RECOVERABLE as e:
-                log.warning("generation %d build/recovery failed: %s", gen, e)
-                self.hooks.teardown()
-                self.client.report("build_failed", gen=gen, suspects=list(getattr(e, "suspects", ())),
-                                   detail=str(e)[:200])
-                self.runtime = None
-                continue
-            self.result.generations.append(gen)
-            self.result.standby = False
-            self.result.reconfigurations.append({"generation": gen, "world": list(world),
-                                                 "seconds": time.monotonic() - t0,
-                                                 "committed_iteration": self.txm.committed_iteration,
-                                                 "build_seconds": comms.build_seconds, "path": comms.path})
-            self.client.set_recovery_info(**self.txm.recovery_info())
-            return
+                self.result.generations.append(prepare["gen"])
+
+    def _enter(self, prepare: dict) -> _Join:
+        gen, world = prepare["gen"], prepare["world"]
+        if self.client.worker_id not in world:
+            return self._stand_by(gen)
+        try:
+            self._build(prepare)
+        except RECOVERABLE as err:
+            log.warning("generation %d build/recovery failed: %s", gen, err)
+            self.hooks.teardown()
+            self.client.report("build_failed", gen=gen, suspects=list(getattr(err, "suspects", ())),
+                               detail=str(err)[:200])
+            self.runtime = None
+            return _Join.RETRY
+        return _Join.MEMBER
+
+    def _stand_by(self, gen: int) -> _Join:
+        self.mgr.destroy()
+        self.comms = self.runtime = None
+        self.client.send_ready(gen, standby=True)
+        try:
+            self.client.wait_commit(gen, timeout=self.prepare_timeout)
+        except ReconfigInterrupted:
+            return _Join.RETRY
+        return _Join.STANDBY
+
+    def _build(self, prepare: dict) -> None:
+        gen, world, payload = prepare["gen"], prepare["world"], prepare["payload"]
+        store = tuple(prepare["store_addr"]) if prepare.get("store_addr") else None
+        self.comms = None
+        comms = self.mgr.build(gen, world, self.client.worker_id, self.binding.group_specs(world, payload),
+                               store_addr=store, store_prefix=prepare["store_prefix"])
+        self.binding.recover(comms, payload, self.txm)
+        self.runtime = self.binding.build_runtime(comms, payload)
+        self.hooks.rebuild(comms, payload)
+        self.comms = comms
+        self.client.send_ready(gen)
+        self.client.wait_commit(gen, timeout=self.prepare_timeout)
+        committed = getattr(self.binding, "on_generation_commit", None)
+        if committed is not None:
+            committed()
+
+    def _record(self, prepare: dict, started: float) -> None:
+        gen = prepare["gen"]
+        self.result.generations.append(gen)
+        self.result.standby = False
+        self.result.reconfigurations.append(dict(
+            generation=gen, world=list(prepare["world"]), seconds=time.monotonic() - started,
+            committed_iteration=self.txm.committed_iteration, build_seconds=self.comms.build_seconds,
+            path=self.comms.path))
+        self.client.set_recovery_info(**self.txm.recovery_info())
