@@ -1,11 +1,13 @@
-"""Reader of the shared-memory ring written by the NCCL profiler plugin
-(``detect/nccl_profiler/``, NCCL profiler ABI v5) -- and by the device timing ring of the fused
-kernels, which uses the same record format.
+"""Reads the shared-memory ring written by the NCCL profiler plugin (``detect/nccl_profiler/``,
+profiler ABI v5) and by the device timing ring of the fused kernels (same record format).
 
-Ring file ``<dir>/resihp_nccl_<pid>.ring``: header ``<IIII Q>`` = (magic 0x52455348 "RESH",
-version, capacity, record size, head); records ``<QQQQ iiii 24s Q>`` = (start_ns, end_ns,
-comm_id, count, rank, nranks, type, peer, func, seq) where ``seq == index + 1`` marks a complete
-record (seqlock).  Same format as the reference's (``resihp/detect/nccl_profile_reader.py``).
+Ring format (kept identical to the reference's, ``resihp/detect/nccl_profile_reader.py``, so
+the same tools read either): file ``<dir>/resihp_nccl_<pid>.ring``; a header ``<IIII Q>``
+(magic ``0x52455348`` "RESH", version, capacity, record size, head) followed by ``capacity``
+records ``<QQQQ iiii 24s Q>`` (start_ns, end_ns, comm_id, count, rank, nranks, type, peer,
+func, seq).  A record is complete when ``seq == index + 1`` (a seqlock), so a reader never
+returns a half-written record; a reader that falls more than ``capacity`` behind skips ahead
+and counts what it lost.
 """
 
 from __future__ import annotations
@@ -36,42 +38,50 @@ class CommRecord:
 
     @property
     def seconds(self) -> float:
-        return (self.end_ns - self.start_ns) / 1e9
+        return 1e-9 * (self.end_ns - self.start_ns)
+
+    @classmethod
+    def unpack(cls, fields: tuple) -> "CommRecord":
+        *numbers, name, _seq = fields
+        return cls(*numbers, name.partition(b"\0")[0].decode())
 
 
 class RingReader:
     def __init__(self, path: str | os.PathLike):
         self.path = Path(path)
-        self._f = open(self.path, "rb")
-        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
-        magic, _version, capacity, rsize, _ = HEADER.unpack_from(self._mm, 0)
-        if magic != MAGIC or rsize != RECORD.size:
-            raise ValueError(f"{path}: not a ResiHP ring (magic={magic:#x}, record={rsize} B)")
-        self.capacity = capacity
+        with open(self.path, "rb") as f:
+            self._mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        magic, _version, self.capacity, record_size, _head = HEADER.unpack_from(self._mm)
+        if (magic, record_size) != (MAGIC, RECORD.size):
+            self._mm.close()
+            raise ValueError(f"{path}: not a ResiHP ring (magic={magic:#x}, record={record_size} B)")
         self.cursor = 0
         self.dropped = 0
 
     def head(self) -> int:
-        return HEADER.unpack_from(self._mm, 0)[4]
+        return HEADER.unpack_from(self._mm)[-1]
+
+    def _slot(self, index: int) -> tuple:
+        return RECORD.unpack_from(self._mm, HEADER.size + RECORD.size * (index % self.capacity))
 
     def poll(self) -> list[CommRecord]:
+        """Every complete record written since the last poll (oldest first)."""
         head = self.head()
-        if head - self.cursor > self.capacity:  # overrun: the writer lapped us
-            self.dropped += head - self.cursor - self.capacity
-            self.cursor = head - self.capacity
-        out = []
-        while self.cursor < head:
-            v = RECORD.unpack_from(self._mm, HEADER.size + (self.cursor % self.capacity) * RECORD.size)
-            if v[-1] != self.cursor + 1:
-                break  # record still being written
-            s, e, comm, count, rank, nranks, typ, peer, func, _ = v
-            out.append(CommRecord(s, e, comm, count, rank, nranks, typ, peer, func.split(b"\0", 1)[0].decode()))
-            self.cursor += 1
-        return out
+        behind = head - self.cursor - self.capacity
+        if behind > 0:  # the writer lapped this reader
+            self.dropped += behind
+            self.cursor += behind
+        fresh = []
+        for index in range(self.cursor, head):
+            fields = self._slot(index)
+            if fields[-1] != index + 1:
+                break  # still being written
+            fresh.append(CommRecord.unpack(fields))
+        self.cursor += len(fresh)
+        return fresh
 
     def close(self) -> None:
         self._mm.close()
-        self._f.close()
 
 
 def find_rings(directory: str | os.PathLike = "/dev/shm") -> list[Path]:

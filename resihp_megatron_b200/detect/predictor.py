@@ -1,9 +1,12 @@
-"""Online workload-aware execution-time predictor: ``T = alpha * N + beta * sum(l_i^2) + gamma``
-per micro-batch chunk (``N`` packed tokens, ``l_i`` document lengths -- attention is block
-diagonal under packing), fitted by recursive least squares with a forgetting factor.
+"""Online, workload-aware execution-time predictor.
 
-Updates are gated: a sample whose log-residual exceeds ``gate`` is not learned from, otherwise
-the model would adapt to a fail-slow and hide it.  (Reference: ``resihp/detect/predictor.py``.)
+Per micro-batch chunk ``T = alpha * N + beta * sum(l_i^2) + gamma``: ``N`` packed tokens and
+``l_i`` the document lengths (attention is block-diagonal under packing).  The coefficients are
+fitted by recursive least squares with exponential forgetting (the standard Kalman-gain form,
+e.g. Haykin, *Adaptive Filter Theory*, ch. 10) on scaled features.  Updates are gated: once
+warmed up, a sample whose log residual exceeds ``gate`` is not learned from -- otherwise the
+model would adapt to a fail-slow GPU and hide it.
+Parity: ``resihp/detect/predictor.py`` (same model, gate and defaults).
 """
 
 from __future__ import annotations
@@ -18,10 +21,10 @@ class RLSPredictor:
                  gate: float = 0.15, warmup: int = 8):
         self.scales = np.asarray(scales, dtype=np.float64)
         self.lam = forgetting
-        self.theta = np.zeros(len(scales))
-        self.P = np.eye(len(scales)) * delta
-        self.gate = gate
-        self.warmup = warmup
+        self.gate, self.warmup = gate, warmup
+        dim = self.scales.size
+        self.theta = np.zeros(dim)
+        self.P = delta * np.eye(dim)  # inverse correlation matrix
         self.n = 0
         self.rejected = 0
 
@@ -29,30 +32,36 @@ class RLSPredictor:
         return np.array([tokens, sum_sq, 1.0]) / self.scales
 
     def predict(self, tokens: float, sum_sq: float) -> float:
-        return float(self.theta @ self.features(tokens, sum_sq))
+        return float(self.features(tokens, sum_sq) @ self.theta)
+
+    def _outlier(self, seconds: float, predicted: float) -> bool:
+        if self.n < self.warmup or predicted <= 0:
+            return False
+        return abs(math.log(max(seconds, 1e-12) / predicted)) > self.gate
 
     def update(self, tokens: float, sum_sq: float, seconds: float, force: bool = False) -> bool:
-        x = self.features(tokens, sum_sq)
-        pred = float(self.theta @ x)
-        if (not force and self.n >= self.warmup and pred > 0
-                and abs(math.log(max(seconds, 1e-12) / pred)) > self.gate):
+        """Learn from one sample; False when the gate rejected it."""
+        phi = self.features(tokens, sum_sq)
+        predicted = float(phi @ self.theta)
+        if not force and self._outlier(seconds, predicted):
             self.rejected += 1
             return False
-        Px = self.P @ x
-        gain = Px / (self.lam + x @ Px)
-        self.theta = self.theta + gain * (seconds - pred)
-        self.P = (self.P - np.outer(gain, Px)) / self.lam
+        p_phi = self.P @ phi
+        k = p_phi / (self.lam + float(phi @ p_phi))
+        self.theta = self.theta + (seconds - predicted) * k
+        self.P = (self.P - np.outer(k, p_phi)) / self.lam
         self.n += 1
         return True
 
     def coefficients(self) -> tuple[float, float, float]:
-        a, b, c = self.theta / self.scales
-        return float(a), float(b), float(c)
+        alpha, beta, gamma = (self.theta / self.scales).tolist()
+        return alpha, beta, gamma
 
 
 def fit_least_squares(samples: list[tuple[float, float, float]]) -> tuple[float, float, float]:
-    """Batch (alpha, beta, gamma) from (tokens, sum_sq, seconds) -- warm start / GPU profiling."""
-    X = np.array([[t, s, 1.0] for t, s, _ in samples])
-    y = np.array([sec for *_, sec in samples])
-    coef, *_ = np.linalg.lstsq(X, y, rcond=None)
-    return float(coef[0]), float(coef[1]), float(coef[2])
+    """Batch ``(alpha, beta, gamma)`` from ``(tokens, sum_sq, seconds)`` samples (warm start,
+    profiling from device timings)."""
+    data = np.asarray(samples, dtype=np.float64)
+    design = np.column_stack([data[:, 0], data[:, 1], np.ones(len(data))])
+    coef = np.linalg.lstsq(design, data[:, 2], rcond=None)[0]
+    return tuple(float(c) for c in coef)

@@ -1,14 +1,16 @@
-"""Per-chunk (F / B / W) timing with deferred readback.
+"""Per-chunk (F / B / W) timing that never stalls the training stream.
 
-On CUDA each chunk is bracketed by events that are read back once complete (one iteration
-later), so measuring never synchronises the training stream; on the CPU the wall clock is used
-and the fault injector's compute padding is added (fail-slow emulation).
-(Reference: ``resihp/detect/timing.py:25-58``.)
+On CUDA every timed chunk is bracketed by two events on the current stream; an event pair is
+read back only once the GPU has passed it (typically during the next iteration), so measuring
+adds no synchronisation.  On the CPU the wall clock is used, plus the fault injector's compute
+padding when one is installed (host-side fail-slow emulation).
+Parity: ``resihp/detect/timing.py:25-58`` (same records and deferred readback).
 """
 
 from __future__ import annotations
 
 import time
+from collections import deque
 from contextlib import contextmanager
 from dataclasses import dataclass
 
@@ -27,32 +29,38 @@ class ChunkTimer:
     def __init__(self, use_cuda: bool | None = None, injector=None):
         self.use_cuda = torch.cuda.is_available() if use_cuda is None else use_cuda
         self.injector = injector
-        self._pending: list[tuple] = []
-        self._done: list[ChunkRecord] = []
+        self._in_flight: deque = deque()      # (record without time, start event, end event)
+        self._ready: list[ChunkRecord] = []
+
+    def _wall(self, iteration: int, op: str, mb: int, started: float) -> None:
+        elapsed = time.perf_counter() - started
+        if self.injector is not None:
+            elapsed += self.injector.pad_compute(elapsed)
+        self._ready.append(ChunkRecord(iteration, op, mb, elapsed))
 
     @contextmanager
     def time(self, iteration: int, op: str, mb: int):
-        if self.use_cuda:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
+        if not self.use_cuda:
+            started = time.perf_counter()
             yield
-            b.record()
-            self._pending.append((iteration, op, mb, a, b))
-        else:
-            t0 = time.perf_counter()
-            yield
-            dt = time.perf_counter() - t0
-            if self.injector is not None:
-                dt += self.injector.pad_compute(dt)
-            self._done.append(ChunkRecord(iteration, op, mb, dt))
+            self._wall(iteration, op, mb, started)
+            return
+        begin, end = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+        begin.record()
+        yield
+        end.record()
+        self._in_flight.append(((iteration, op, mb), begin, end))
 
     def collect(self, upto_iteration: int | None = None) -> list[ChunkRecord]:
-        keep = []
-        for it, op, mb, a, b in self._pending:
-            if (upto_iteration is None or it <= upto_iteration) and b.query():
-                self._done.append(ChunkRecord(it, op, mb, a.elapsed_time(b) / 1e3))
+        """Records finished so far (CUDA pairs whose end event completed, up to an iteration)."""
+        waiting = deque()
+        while self._in_flight:
+            key, begin, end = self._in_flight.popleft()
+            eligible = upto_iteration is None or key[0] <= upto_iteration
+            if eligible and end.query():
+                self._ready.append(ChunkRecord(*key, begin.elapsed_time(end) / 1000.0))
             else:
-                keep.append((it, op, mb, a, b))
-        self._pending = keep
-        out, self._done = self._done, []
-        return out
+                waiting.append((key, begin, end))
+        self._in_flight = waiting
+        done, self._ready = self._ready, []
+        return done
