@@ -1,13 +1,17 @@
-"""T2: persistent checkpoints stored as logical slices, loadable by any later plan.
+"""T2: persistent checkpoints stored as logical slices, loadable into any later plan.
 
-On-disk format (kept identical to the reference, ``resihp/state/checkpoint.py:23-135``):
-``<root>/iter_<it:08d>/<owner>.pt`` written as ``.<owner>.pt.tmp`` then atomically renamed;
-content ``torch.save({"slices": [(SliceMeta.to_json(), {kind: cpu tensor})], "extra": {...}})``;
-``<owner>.done`` holds the JSON list of the owner's slice metas (written last = the commit
-marker).  A ``SliceMeta`` is ``{"key", "global_shape", "dim" (null = replicated), "interval"}``;
-replicated tensors use the interval ``[0, 1]``.  Loading assembles any requested interval from
-whichever saved slices overlap it (reshard on load for arbitrary TP / PP / DP changes).
-Saving runs on a background thread after a synchronous device-to-host copy.
+On-disk format -- kept identical to the reference's (``resihp/state/checkpoint.py:23-135``) so
+checkpoints move between the two frameworks:
+
+* ``<root>/iter_<it:08d>/<owner>.pt``, written as ``.<owner>.pt.tmp`` and renamed atomically,
+  holding ``torch.save({"slices": [(SliceMeta.to_json(), {kind: cpu tensor})], "extra": {...}})``;
+* ``<owner>.done``: the JSON list of that owner's slice metas, written last (the commit marker);
+* a ``SliceMeta`` is ``{"key", "global_shape", "dim" (null: replicated), "interval"}``, and a
+  replicated tensor uses the interval ``[0, 1]``.
+
+Loading assembles any requested interval from whichever saved slices overlap it, so a
+checkpoint reshards on load for arbitrary TP / PP / DP changes.  Saving copies to host memory
+synchronously and writes on a background thread.
 """
 
 from __future__ import annotations
@@ -31,110 +35,130 @@ class SliceMeta:
     interval: tuple[int, int]
 
     def to_json(self) -> dict:
-        return {"key": self.key, "global_shape": list(self.global_shape), "dim": self.dim,
-                "interval": list(self.interval)}
+        return dict(key=self.key, global_shape=list(self.global_shape), dim=self.dim, interval=list(self.interval))
 
-    @staticmethod
-    def from_json(d: dict) -> "SliceMeta":
-        return SliceMeta(d["key"], tuple(d["global_shape"]), d["dim"], tuple(d["interval"]))
+    @classmethod
+    def from_json(cls, d: dict) -> "SliceMeta":
+        return cls(d["key"], tuple(d["global_shape"]), d["dim"], tuple(d["interval"]))
+
+    @property
+    def length(self) -> int:
+        return 1 if self.dim is None else self.interval[1] - self.interval[0]
+
+    def local_shape(self) -> list[int]:
+        shape = list(self.global_shape)
+        if self.dim is not None:
+            shape[self.dim] = self.length
+        return shape
+
+
+def _covers(intervals, extent: int) -> bool:
+    """Whether the union of ``intervals`` contains ``[0, extent)``."""
+    reach = 0
+    for lo, hi in sorted(intervals):
+        if lo > reach:
+            break
+        reach = max(reach, hi)
+    return reach >= extent
+
+
+class _Iteration:
+    """The committed slices of one checkpoint iteration, with lazily loaded owner files."""
+
+    def __init__(self, folder: Path):
+        self.folder = folder
+        self.metas: list[tuple[str, SliceMeta]] = []
+        for marker in sorted(folder.glob("*.done")):
+            owner = marker.name.removesuffix(".done")
+            self.metas += [(owner, SliceMeta.from_json(m)) for m in json.loads(marker.read_text())]
+        self._files: dict[str, dict] = {}
+
+    def of_key(self, key: str) -> list[tuple[str, SliceMeta]]:
+        return [(owner, m) for owner, m in self.metas if m.key == key]
+
+    def tensors(self, owner: str, meta: SliceMeta) -> dict[str, torch.Tensor]:
+        if owner not in self._files:
+            saved = torch.load(self.folder / f"{owner}.pt", weights_only=False)["slices"]
+            self._files[owner] = {SliceMeta.from_json(m): t for m, t in saved}
+        return self._files[owner][meta]
 
 
 class SliceCheckpointer:
     def __init__(self, directory: str | os.PathLike):
         self.root = Path(directory)
-        self._thread: threading.Thread | None = None
+        self._writer: threading.Thread | None = None
 
     def _dir(self, iteration: int) -> Path:
         return self.root / f"iter_{iteration:08d}"
 
     def save(self, iteration: int, owner: str, slices: list[tuple[SliceMeta, dict[str, torch.Tensor]]],
              extra: dict | None = None, blocking: bool = False) -> None:
+        """Write ``owner``'s slices of ``iteration`` (device tensors are copied to host first)."""
         self.wait()
-        host = [(m, {k: v.detach().to("cpu", copy=True) for k, v in t.items()}) for m, t in slices]
+        on_host = [(meta, {kind: t.detach().to("cpu", copy=True) for kind, t in per_kind.items()})
+                   for meta, per_kind in slices]
+        folder = self._dir(iteration)
 
-        def write() -> None:
-            d = self._dir(iteration)
-            d.mkdir(parents=True, exist_ok=True)
-            tmp = d / f".{owner}.pt.tmp"
-            torch.save({"slices": [(m.to_json(), t) for m, t in host], "extra": extra or {}}, tmp)
-            os.replace(tmp, d / f"{owner}.pt")
-            (d / f"{owner}.done").write_text(json.dumps([m.to_json() for m, _ in host]))
+        def persist() -> None:
+            folder.mkdir(parents=True, exist_ok=True)
+            partial = folder / f".{owner}.pt.tmp"
+            torch.save({"slices": [(m.to_json(), t) for m, t in on_host], "extra": dict(extra or {})}, partial)
+            os.replace(partial, folder / f"{owner}.pt")
+            (folder / f"{owner}.done").write_text(json.dumps([m.to_json() for m, _ in on_host]))
 
         if blocking:
-            write()
+            persist()
         else:
-            self._thread = threading.Thread(target=write, name="ckpt-save", daemon=True)
-            self._thread.start()
+            self._writer = threading.Thread(target=persist, name="ckpt-save", daemon=True)
+            self._writer.start()
 
     def wait(self) -> None:
-        if self._thread is not None:
-            self._thread.join()
-            self._thread = None
-
-    def _index(self, iteration: int) -> list[tuple[str, SliceMeta]]:
-        out = []
-        for done in sorted(self._dir(iteration).glob("*.done")):
-            owner = done.name[: -len(".done")]
-            out.extend((owner, SliceMeta.from_json(m)) for m in json.loads(done.read_text()))
-        return out
+        writer, self._writer = self._writer, None
+        if writer is not None:
+            writer.join()
 
     def complete(self, iteration: int, required: dict[str, tuple[tuple[int, ...], int | None]]) -> bool:
-        idx = self._index(iteration)
+        """Every required key fully covered by committed slices of ``iteration``."""
+        found = _Iteration(self._dir(iteration))
         for key, (shape, dim) in required.items():
-            n = shape[dim] if dim is not None else 1
-            reach = 0
-            for a, b in sorted(m.interval for _, m in idx if m.key == key):
-                if a > reach:
-                    return False
-                reach = max(reach, b)
-            if reach < n:
+            extent = 1 if dim is None else shape[dim]
+            if not _covers([m.interval for _, m in found.of_key(key)], extent):
                 return False
         return True
 
     def latest_complete(self, required: dict[str, tuple[tuple[int, ...], int | None]]) -> int | None:
-        if not self.root.exists():
+        if not self.root.is_dir():
             return None
-        its = sorted((int(p.name[5:]) for p in self.root.glob("iter_*")), reverse=True)
-        for it in its:
-            if self.complete(it, required):
-                return it
-        return None
+        iterations = sorted((int(p.name.removeprefix("iter_")) for p in self.root.glob("iter_*")), reverse=True)
+        return next((it for it in iterations if self.complete(it, required)), None)
 
     def read_extra(self, iteration: int, owner: str) -> dict:
         return torch.load(self._dir(iteration) / f"{owner}.pt", weights_only=False).get("extra", {})
 
     def load(self, iteration: int, wanted: list[SliceMeta], kinds: tuple[str, ...]) -> dict[str, dict[str, torch.Tensor]]:
-        idx = self._index(iteration)
-        files: dict[str, list] = {}
-        out: dict[str, dict[str, torch.Tensor]] = {}
+        """Assemble every wanted slice from the saved slices that overlap it."""
+        found = _Iteration(self._dir(iteration))
+        assembled: dict[str, dict[str, torch.Tensor]] = {}
         for want in wanted:
-            dim = want.dim
-            shape = list(want.global_shape)
-            if dim is not None:
-                shape[dim] = want.interval[1] - want.interval[0]
-            got: dict[str, torch.Tensor | None] = dict.fromkeys(kinds)
-            covered = 0
-            for owner, meta in idx:
-                if meta.key != want.key:
+            parts: dict[str, torch.Tensor] = {}
+            filled = 0
+            for owner, meta in found.of_key(want.key):
+                overlap = (0, 1) if want.dim is None else intersect(meta.interval, want.interval)
+                if overlap is None:
                     continue
-                o = intersect(meta.interval, want.interval) if dim is not None else (0, 1)
-                if o is None:
-                    continue
-                if owner not in files:
-                    files[owner] = torch.load(self._dir(iteration) / f"{owner}.pt", weights_only=False)["slices"]
-                tensors = next(t for m, t in files[owner] if SliceMeta.from_json(m) == meta)
-                for k in kinds:
-                    if got[k] is None:
-                        got[k] = torch.empty(shape, dtype=tensors[k].dtype)
-                    if dim is None:
-                        got[k].copy_(tensors[k])
-                    else:
-                        got[k].narrow(dim, o[0] - want.interval[0], o[1] - o[0]).copy_(
-                            tensors[k].narrow(dim, o[0] - meta.interval[0], o[1] - o[0]))
-                covered += (o[1] - o[0]) if dim is not None else 1
-                if dim is None:
-                    break
-            if covered < ((want.interval[1] - want.interval[0]) if dim is not None else 1):
+                saved = found.tensors(owner, meta)
+                for kind in kinds:
+                    target = parts.setdefault(kind, torch.empty(want.local_shape(), dtype=saved[kind].dtype))
+                    if want.dim is None:
+                        target.copy_(saved[kind])
+                        continue
+                    width = overlap[1] - overlap[0]
+                    target.narrow(want.dim, overlap[0] - want.interval[0], width).copy_(
+                        saved[kind].narrow(want.dim, overlap[0] - meta.interval[0], width))
+                filled += overlap[1] - overlap[0] if want.dim is not None else 1
+                if want.dim is None:
+                    break  # one copy of a replicated tensor is enough
+            if filled < want.length:
                 raise KeyError(f"checkpoint {iteration} does not cover {want}")
-            out[want.key] = got
-        return out
+            assembled[want.key] = {kind: parts.get(kind) for kind in kinds}
+        return assembled

@@ -1,14 +1,16 @@
 """Stable tensor identities and plan-derived ownership.
 
-Every tensor is named by a key independent of stage boundaries (``layers.<global layer>.<param>``)
-with its global shape and TP partition dimension (``None`` = replicated).  ``holdings(plan)``
-says which device holds which interval of every key (replicated tensors use the interval
-``(0, 1)``; every CP slice holds a copy), so the old and new plans of a reconfiguration fully
-determine the state to move.  (Reference: ``resihp/state/layer_registry.py:21-79``.)
+A tensor is named independently of stage boundaries, ``layers.<global layer>.<param>``, and
+described by its global shape and TP partition dimension (``None``: replicated).
+``holdings(plan)`` lists which device holds which interval of every key -- a replicated tensor
+is held as the interval ``(0, 1)``, and every CP slice holds its own copy -- so the old and the
+new plan of a reconfiguration determine exactly which state has to move.
+Parity: ``resihp/state/layer_registry.py:21-79`` (same keys, specs and holdings).
 """
 
 from __future__ import annotations
 
+from collections import defaultdict
 from dataclasses import dataclass
 from typing import Callable
 
@@ -22,57 +24,68 @@ class TensorSpec:
     key: str
     global_shape: tuple[int, ...]
     dim: int | None
-    trainable: bool = True  # non-trainable tensors (amax history, router bias) have no optimizer state
+    trainable: bool = True  # non-trainable tensors (amax history, router bias) carry no optimizer state
 
     @property
     def extent(self) -> int:
-        return self.global_shape[self.dim] if self.dim is not None else 1
+        """Length of the partitioned dimension (1 for a replicated tensor)."""
+        return 1 if self.dim is None else self.global_shape[self.dim]
 
     def local_shape(self, interval: tuple[int, int]) -> tuple[int, ...]:
         if self.dim is None:
             return self.global_shape
-        shape = list(self.global_shape)
-        shape[self.dim] = interval[1] - interval[0]
-        return tuple(shape)
+        lo, hi = interval
+        return self.global_shape[:self.dim] + (hi - lo,) + self.global_shape[self.dim + 1:]
+
+    def split(self, parts: int) -> list[tuple[int, int]]:
+        """The interval each of ``parts`` TP ranks holds."""
+        return [FULL] * parts if self.dim is None else even_split(self.extent, parts)
 
 
 Holdings = dict[str, list[tuple[str, tuple[int, int]]]]
 
 
 def holdings(plan, specs: dict[str, TensorSpec], layer_of: Callable[[str], int]) -> Holdings:
-    out: Holdings = {}
+    """key -> sorted ``(device, interval)`` pairs of every holder under ``plan``."""
+    keys_of_layer: dict[int, list[str]] = defaultdict(list)
+    for key in specs:
+        keys_of_layer[layer_of(key)].append(key)
+    held: Holdings = defaultdict(list)
     for g in plan.stage_groups:
         lo, hi = g.layers
-        for key, spec in specs.items():
-            if not lo <= layer_of(key) < hi:
-                continue
-            parts = even_split(spec.extent, g.tp) if spec.dim is not None else [FULL] * g.tp
-            for i in range(g.cp):
-                for dev, iv in zip(g.slice(i), parts):
-                    out.setdefault(key, []).append((dev, iv))
-    for key in out:
-        out[key].sort()
-    return out
+        for layer in range(lo, hi):
+            for key in keys_of_layer.get(layer, ()):
+                pieces = specs[key].split(g.tp)
+                for c in range(g.cp):
+                    held[key].extend(zip(g.slice(c), pieces))
+    return {key: sorted(pairs) for key, pairs in held.items()}
 
 
 def device_layout(h: Holdings, device: str) -> dict[str, tuple[int, int]]:
-    return {key: iv for key, hs in h.items() for d, iv in hs if d == device}
+    """The interval of every key that ``device`` holds."""
+    mine = {}
+    for key, pairs in h.items():
+        for dev, interval in pairs:
+            if dev == device:
+                mine[key] = interval
+    return mine
 
 
 def reference_specs(cfg) -> dict[str, TensorSpec]:
-    """Specs of the CPU reference model (``runtime.reference_model``)."""
+    """Specs of the CPU reference model (``runtime.reference_model``), plus each layer's fp8 amax
+    history when the config keeps one."""
     from ..runtime.reference_model import PARAM_DIMS, full_layer_params
 
-    out = {}
+    specs = {}
     for layer in range(cfg.num_layers):
-        for name, t in full_layer_params(cfg, layer).items():
-            key = f"layers.{layer}.{name}"
-            out[key] = TensorSpec(key, tuple(t.shape), PARAM_DIMS[name])
+        prefix = f"layers.{layer}."
+        for name, tensor in full_layer_params(cfg, layer).items():
+            specs[prefix + name] = TensorSpec(prefix + name, tuple(tensor.shape), PARAM_DIMS[name])
         if cfg.amax_history:
-            key = f"layers.{layer}.amax_history"
-            out[key] = TensorSpec(key, (cfg.amax_history,), None, trainable=False)
-    return out
+            specs[prefix + "amax_history"] = TensorSpec(prefix + "amax_history", (cfg.amax_history,), None,
+                                                         trainable=False)
+    return specs
 
 
 def reference_layer_of(key: str) -> int:
-    return int(key.split(".")[1])
+    return int(key.split(".", 2)[1])

@@ -1,14 +1,14 @@
-"""State redundancy tiers.
+"""Redundancy tiers of training state.
 
-* T0 -- live replicas: parameters live on every DP replica of a stage; with a sharded optimizer
-  the optimizer shard has twin holders when the DP group is split into several optimizer
-  instances (``distopt_twin_holders``).  Zero rollback.
-* T1 -- host-memory snapshots every ``interval`` iterations (pinned host buffers filled on a
-  side stream; ``fence()`` orders the next in-place update after the copy), replicated to a
-  buddy on another node over a ring.  Rollback <= interval iterations; covers the loss of every
+* **T0, live replicas.**  Parameters live on every DP replica of a stage.  With a sharded
+  optimizer and the DP group split into several optimizer instances, every optimizer shard has
+  a twin holder in each instance (``distopt_twin_holders``).  No rollback.
+* **T1, host snapshots** every ``interval`` iterations: pinned host buffers filled on a side
+  stream (``fence()`` orders the next in-place update after the copy), mirrored to a buddy on the
+  next node of a ring.  Rolls back at most ``interval`` iterations; survives the loss of every
   live copy of a shard.
-* T2 -- persistent sliced checkpoints that reshard on load (``checkpoint.py``).
-(Reference: ``resihp/state/redundancy.py:21-163``.)
+* **T2, sliced checkpoints** that reshard on load (``checkpoint.py``).
+Parity: ``resihp/state/redundancy.py:21-163`` (same tiers, snapshot protocol and ring exchange).
 """
 
 from __future__ import annotations
@@ -21,13 +21,13 @@ import torch
 
 
 def distopt_twin_holders(dp_members: list[str], num_instances: int) -> dict[str, list[str]]:
-    """Holders of each optimizer shard when the DP group is cut into ``num_instances``
-    contiguous instances: shard ``j`` lives at position ``j`` of every instance."""
-    d = len(dp_members)
-    if num_instances < 1 or d % num_instances:
-        raise ValueError(f"DP size {d} is not divisible by {num_instances} instances")
-    per = d // num_instances
-    return {f"shard{j}": [dp_members[i * per + j] for i in range(num_instances)] for j in range(per)}
+    """Holders of every optimizer shard when the DP group is cut into ``num_instances``
+    consecutive instances: shard ``j`` sits at position ``j`` of each instance."""
+    if num_instances < 1 or len(dp_members) % num_instances:
+        raise ValueError(f"DP size {len(dp_members)} is not divisible by {num_instances} instances")
+    per = len(dp_members) // num_instances
+    instances = [dp_members[k:k + per] for k in range(0, len(dp_members), per)]
+    return {f"shard{j}": [inst[j] for inst in instances] for j in range(per)}
 
 
 @dataclass
@@ -35,127 +35,117 @@ class HolderMap:
     holders: dict[str, list[str]]
 
     def lost(self, failed: set[str]) -> list[str]:
-        return sorted(k for k, hs in self.holders.items() if all(h in failed for h in hs))
+        """Shards none of whose holders survived."""
+        return sorted(shard for shard, hs in self.holders.items() if set(hs) <= failed)
 
     def survivors(self, key: str, failed: set[str]) -> list[str]:
         return [h for h in self.holders[key] if h not in failed]
 
     def node_diverse(self, node_of: Callable[[str], str]) -> bool:
-        return all(len({node_of(h) for h in hs}) > 1 for hs in self.holders.values() if len(hs) > 1)
+        """Every shard with several holders has them on at least two nodes."""
+        return all(len(set(map(node_of, hs))) > 1 for hs in self.holders.values() if len(hs) > 1)
 
 
 class HostSnapshotManager:
     """Asynchronous host-memory snapshots of a flat ``name -> tensor`` state dict."""
 
     def __init__(self, interval: int, keep: int = 1):
-        self.interval = interval
-        self.keep = keep
-        self._snaps: list[tuple[int, dict[str, torch.Tensor]]] = []
-        self._held: dict[str, tuple[int, dict[str, torch.Tensor]]] = {}
-        self._thread: threading.Thread | None = None
-        self._lock = threading.Lock()
-        self._copy_done = None
-        self._pinned: dict[str, torch.Tensor] = {}
+        self.interval, self.keep = interval, keep
+        self._history: list[tuple[int, dict[str, torch.Tensor]]] = []  # oldest first, at most ``keep``
+        self._buddies: dict[str, tuple[int, dict[str, torch.Tensor]]] = {}
+        self._mu = threading.Lock()
+        self._publisher: threading.Thread | None = None
+        self._copied: torch.cuda.Event | None = None
 
     def due(self, iteration: int) -> bool:
         return self.interval > 0 and (iteration + 1) % self.interval == 0
 
-    def _host_buffer(self, k: str, v: torch.Tensor) -> torch.Tensor:
-        buf = self._pinned.get(k)
-        if buf is None or buf.shape != v.shape or buf.dtype != v.dtype:
-            buf = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
-        return buf
+    def _publish(self, iteration: int, staged: dict[str, torch.Tensor], side) -> None:
+        if side is not None:
+            side.synchronize()
+        with self._mu:
+            self._history = (self._history + [(iteration, staged)])[-self.keep:]
 
     def snapshot(self, iteration: int, state: dict[str, torch.Tensor], blocking: bool = False) -> None:
-        """CPU tensors are cloned now; CUDA tensors are copied to pinned host memory on a side
-        stream -- call ``fence()`` before the next in-place update of ``state``."""
+        """CPU tensors are cloned at once; CUDA tensors are copied into pinned host memory on a
+        side stream -- call ``fence()`` before the next in-place update of ``state``."""
         self.wait()
-        side = None
-        if any(v.is_cuda for v in state.values()):
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-        staged: dict[str, torch.Tensor] = {}
-        for k, v in state.items():
-            if v.is_cuda:
-                with torch.cuda.stream(side):
-                    buf = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
-                    buf.copy_(v.detach(), non_blocking=True)
-                staged[k] = buf
-            else:
-                staged[k] = v.detach().clone()
+        on_gpu = any(t.is_cuda for t in state.values())
+        side = torch.cuda.Stream() if on_gpu else None
         if side is not None:
-            self._copy_done = torch.cuda.Event()
-            self._copy_done.record(side)
-
-        def publish() -> None:
-            if side is not None:
-                side.synchronize()
-            with self._lock:
-                self._snaps.append((iteration, staged))
-                self._snaps = self._snaps[-self.keep:]
-
+            side.wait_stream(torch.cuda.current_stream())
+        staged = {}
+        for name, t in state.items():
+            if not t.is_cuda:
+                staged[name] = t.detach().clone()
+                continue
+            with torch.cuda.stream(side):
+                host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                host.copy_(t.detach(), non_blocking=True)
+            staged[name] = host
+        if side is not None:
+            self._copied = torch.cuda.Event()
+            self._copied.record(side)
         if blocking or side is None:
-            publish()
-        else:
-            self._thread = threading.Thread(target=publish, name="snapshot", daemon=True)
-            self._thread.start()
+            self._publish(iteration, staged, side)
+            return
+        self._publisher = threading.Thread(target=self._publish, args=(iteration, staged, side), name="snapshot",
+                                           daemon=True)
+        self._publisher.start()
 
     def fence(self) -> None:
-        if self._copy_done is not None:
-            torch.cuda.current_stream().wait_event(self._copy_done)
-            self._copy_done = None
+        """Make the current stream wait for the last snapshot's device-to-host copies."""
+        event, self._copied = self._copied, None
+        if event is not None:
+            torch.cuda.current_stream().wait_event(event)
 
     def maybe_snapshot(self, iteration: int, state_fn: Callable[[], dict[str, torch.Tensor]]) -> bool:
-        if not self.due(iteration):
-            return False
-        self.snapshot(iteration, state_fn(), blocking=True)
-        return True
+        if self.due(iteration):
+            self.snapshot(iteration, state_fn(), blocking=True)
+            return True
+        return False
 
     def wait(self) -> None:
-        if self._thread is not None:
-            self._thread.join()
-            self._thread = None
+        worker, self._publisher = self._publisher, None
+        if worker is not None:
+            worker.join()
 
     def latest(self) -> tuple[int, dict[str, torch.Tensor]] | None:
         self.wait()
-        with self._lock:
-            return self._snaps[-1] if self._snaps else None
+        with self._mu:
+            return self._history[-1] if self._history else None
 
     def at(self, iteration: int) -> dict[str, torch.Tensor] | None:
         self.wait()
-        with self._lock:
-            for it, s in self._snaps:
-                if it == iteration:
-                    return s
-        return None
+        with self._mu:
+            return next((snap for it, snap in self._history if it == iteration), None)
 
     def hold_for(self, owner: str, iteration: int, state: dict[str, torch.Tensor]) -> None:
         """Keep a buddy's snapshot (received over the replication ring)."""
-        with self._lock:
-            self._held[owner] = (iteration, state)
+        with self._mu:
+            self._buddies[owner] = (iteration, state)
 
     def held(self, owner: str) -> tuple[int, dict[str, torch.Tensor]] | None:
-        with self._lock:
-            return self._held.get(owner)
+        with self._mu:
+            return self._buddies.get(owner)
 
 
 def exchange_snapshot_with_buddy(mgr, comms, mine: tuple[int, dict[str, torch.Tensor]], send_to: str,
                                  recv_from: str, template: dict[str, torch.Tensor], group=None,
                                  timeout: float = 60.0) -> tuple[int, dict[str, torch.Tensor]]:
-    """Ring replication: send my snapshot to ``send_to``, receive ``recv_from``'s (shapes from
-    ``template``)."""
+    """Ring replication: send my newest snapshot to ``send_to`` and receive ``recv_from``'s
+    (its tensors shaped like ``template``); tag 0 carries the iteration, tags 1.. the tensors in
+    name order."""
     import torch.distributed as dist
 
-    it, state = mine
-    dst, src = comms.rank_of(send_to), comms.rank_of(recv_from)
-    hdr = torch.tensor([it], dtype=torch.int64)
-    rhdr = torch.zeros(1, dtype=torch.int64)
-    works = [dist.isend(hdr, dst, group=group, tag=0), dist.irecv(rhdr, src, group=group, tag=0)]
-    got = {k: torch.empty_like(v, device="cpu") for k, v in sorted(template.items())}
-    for i, k in enumerate(sorted(state)):
-        works.append(dist.isend(state[k].contiguous(), dst, group=group, tag=i + 1))
-    for i, k in enumerate(sorted(got)):
-        works.append(dist.irecv(got[k], src, group=group, tag=i + 1))
-    for w in works:
-        mgr.guarded_wait(w, timeout=timeout, what="snapshot replication")
-    return int(rhdr.item()), got
+    iteration, state = mine
+    to, frm = comms.rank_of(send_to), comms.rank_of(recv_from)
+    out_hdr, in_hdr = torch.tensor([iteration], dtype=torch.int64), torch.zeros(1, dtype=torch.int64)
+    received = {name: torch.empty_like(t, device="cpu") for name, t in sorted(template.items())}
+    works = [dist.isend(out_hdr, to, group=group, tag=0), dist.irecv(in_hdr, frm, group=group, tag=0)]
+    works += [dist.isend(state[name].contiguous(), to, group=group, tag=tag)
+              for tag, name in enumerate(sorted(state), start=1)]
+    works += [dist.irecv(received[name], frm, group=group, tag=tag) for tag, name in enumerate(received, start=1)]
+    for work in works:
+        mgr.guarded_wait(work, timeout=timeout, what="snapshot replication")
+    return int(in_hdr.item()), received

@@ -1,16 +1,16 @@
-"""Iteration-level transactions.
+"""Iteration-level transactions; the optimizer step is the commit point.
 
-The optimizer step is the commit point.  Phases: COMPUTE -> REDUCED (gradients all-reduced) ->
-STEPPING -> COMMITTED, or ABORTED.  Reduced gradients are kept until the step commits, which
-enables roll-forward recovery without a per-step consensus round: survivors report
-``(committed_iteration, has_reduced_grads)`` and the planner moves everyone to the newest
-committed iteration -- ranks that already hold the reduced gradients step locally (Adam is
-deterministic), the others copy state from a rank that committed.
+Phases: ``COMPUTE -> REDUCED`` (gradients all-reduced) ``-> STEPPING -> COMMITTED``, or
+``ABORTED``.  Reduced gradients are kept until the step commits, which allows roll-forward
+recovery without a per-step consensus round: survivors report ``(committed_iteration,
+has_reduced_grads)``, and the planner moves everyone to the newest committed iteration -- ranks
+that hold that iteration's reduced gradients step locally (Adam is deterministic), the others
+copy state from a rank that committed it.
 
-``buffers`` are the live non-trainable tensors an iteration mutates (FP8 amax history, MoE
-router bias / loads); they are snapshotted at ``begin`` and restored on rollback, except for an
-iteration that reached REDUCED, which may still roll forward.
-(Reference: ``resihp/state/transaction.py:22-142``.)
+``buffers`` are the non-trainable tensors an iteration mutates (fp8 amax history, MoE router
+bias and loads).  They are copied at ``begin`` and put back on rollback -- except after REDUCED,
+where the iteration may still roll forward.
+Parity: ``resihp/state/transaction.py:22-142`` (same phases, recovery report and roll-forward).
 """
 
 from __future__ import annotations
@@ -32,6 +32,10 @@ class TxnPhase(str, Enum):
     ABORTED = "aborted"
 
 
+_NEXT = {TxnPhase.COMPUTE: TxnPhase.REDUCED, TxnPhase.REDUCED: TxnPhase.STEPPING,
+         TxnPhase.STEPPING: TxnPhase.COMMITTED}
+
+
 @dataclass
 class IterationTransaction:
     iteration: int
@@ -45,7 +49,7 @@ class IterationTransaction:
 class TransactionManager:
     def __init__(self, cursor: DataCursor | None = None, committed_iteration: int = -1,
                  buffers: Callable[[], dict[str, torch.Tensor]] | None = None):
-        self.cursor = cursor or DataCursor(committed_iteration + 1)
+        self.cursor = cursor if cursor is not None else DataCursor(committed_iteration + 1)
         self.committed_iteration = committed_iteration
         self.current: IterationTransaction | None = None
         self.aborts = 0
@@ -54,91 +58,99 @@ class TransactionManager:
     def track_buffers(self, buffers: Callable[[], dict[str, torch.Tensor]] | None) -> None:
         self.buffers = buffers
 
-    def _live(self) -> dict[str, torch.Tensor]:
-        return self.buffers() if self.buffers is not None else {}
+    def _live_buffers(self) -> dict[str, torch.Tensor]:
+        return {} if self.buffers is None else self.buffers()
 
-    def _restore_buffers(self) -> None:
-        if self.current is None or not self.current.buffers:
+    def _put_back_buffers(self) -> None:
+        saved = self.current.buffers if self.current is not None else None
+        if not saved:
             return
         with torch.no_grad():
-            for k, t in self._live().items():
-                if k in self.current.buffers:
-                    t.copy_(self.current.buffers[k])
+            for key, live in self._live_buffers().items():
+                if key in saved:
+                    live.copy_(saved[key])
 
     def begin(self, iteration: int) -> IterationTransaction:
         if iteration != self.committed_iteration + 1:
             raise ValueError(f"iteration {iteration} does not follow committed {self.committed_iteration}")
         self.cursor.iteration = iteration
-        snap = {k: t.detach().clone() for k, t in self._live().items()}
-        self.current = IterationTransaction(iteration, capture_rng_state(), self.cursor.snapshot(), buffers=snap)
+        saved = {key: t.detach().clone() for key, t in self._live_buffers().items()}
+        self.current = IterationTransaction(iteration, capture_rng_state(), self.cursor.snapshot(), buffers=saved)
         return self.current
 
-    def _advance(self, expect: TxnPhase, to: TxnPhase) -> None:
-        if self.current is None or self.current.phase != expect:
-            raise RuntimeError(f"transaction not in {expect.value}")
-        self.current.phase = to
+    def _step_phase(self, expected: TxnPhase) -> None:
+        txn = self.current
+        if txn is None or txn.phase is not expected:
+            raise RuntimeError(f"transaction not in {expected.value}")
+        txn.phase = _NEXT[expected]
 
     def on_reduced(self) -> None:
-        self._advance(TxnPhase.COMPUTE, TxnPhase.REDUCED)
+        self._step_phase(TxnPhase.COMPUTE)
 
     def on_step_begin(self) -> None:
-        self._advance(TxnPhase.REDUCED, TxnPhase.STEPPING)
+        self._step_phase(TxnPhase.REDUCED)
 
     def on_commit(self) -> None:
-        self._advance(TxnPhase.STEPPING, TxnPhase.COMMITTED)
-        self.committed_iteration = self.current.iteration
-        self.cursor.iteration = self.committed_iteration + 1
-        self.current = None
+        self._step_phase(TxnPhase.STEPPING)
+        self._settle(self.current.iteration)
 
-    @property
-    def has_reduced_grads(self) -> bool:
-        return self.current is not None and self.current.phase == TxnPhase.REDUCED
-
-    def abort(self) -> dict:
-        """Roll RNG and the data cursor back to the start of the in-flight iteration."""
-        info = self.recovery_info()
-        if self.current is not None:
-            restore_rng_state(self.current.rng)
-            self.cursor.restore(self.current.cursor)
-            if self.current.phase != TxnPhase.REDUCED:
-                self.current.phase = TxnPhase.ABORTED
-                self._restore_buffers()
-            self.aborts += 1
-        return info
-
-    def discard(self) -> None:
-        """Drop the in-flight iteration (its gradients will not be used)."""
-        if self.current is not None:
-            self.cursor.restore(self.current.cursor)
-            self._restore_buffers()
-        self.current = None
-
-    def adopt(self, iteration: int) -> None:
-        """State was replaced by the state at ``iteration`` (peer copy, snapshot, checkpoint)."""
+    def _settle(self, iteration: int) -> None:
+        """The model now holds the state after ``iteration``; nothing is in flight."""
         self.committed_iteration = iteration
         self.cursor.iteration = iteration + 1
         self.current = None
 
+    @property
+    def has_reduced_grads(self) -> bool:
+        return self.current is not None and self.current.phase is TxnPhase.REDUCED
+
+    def abort(self) -> dict:
+        """Roll the RNG and data cursor back to the start of the in-flight iteration; returns
+        the recovery report as it was before the rollback."""
+        report = self.recovery_info()
+        txn = self.current
+        if txn is not None:
+            restore_rng_state(txn.rng)
+            self.cursor.restore(txn.cursor)
+            if txn.phase is not TxnPhase.REDUCED:  # a REDUCED iteration may still roll forward
+                txn.phase = TxnPhase.ABORTED
+                self._put_back_buffers()
+            self.aborts += 1
+        return report
+
+    def discard(self) -> None:
+        """Drop the in-flight iteration for good (its gradients will not be used)."""
+        if self.current is not None:
+            self.cursor.restore(self.current.cursor)
+            self._put_back_buffers()
+        self.current = None
+
+    def adopt(self, iteration: int) -> None:
+        """The state was replaced by the state after ``iteration`` (peer copy, snapshot, checkpoint)."""
+        self._settle(iteration)
+
     def recovery_info(self) -> dict:
+        inflight = None if self.current is None else self.current.iteration
         return {"committed_iteration": self.committed_iteration, "has_reduced_grads": self.has_reduced_grads,
-                "inflight_iteration": self.current.iteration if self.current is not None else None}
+                "inflight_iteration": inflight}
 
 
 def roll_forward_plan(recovery: dict[str, dict], world: list[str]) -> dict:
-    """Recovery target from the survivors' ABORTED reports: the newest committed iteration;
-    ``local_step`` = ranks one behind that hold reduced gradients of exactly that iteration,
-    ``up_to_date`` = ranks already there, ``needs_state`` = everyone else."""
-    default = {"committed_iteration": -1, "has_reduced_grads": False}
-    infos = {w: recovery.get(w, default) for w in world}
-    target = max((i.get("committed_iteration", -1) for i in infos.values()), default=-1)
-    out = {"target_iteration": target, "local_step": [], "needs_state": [], "up_to_date": []}
-    for w in world:
-        i = infos[w]
-        c = i.get("committed_iteration", -1)
-        if c == target:
-            out["up_to_date"].append(w)
-        elif c == target - 1 and i.get("has_reduced_grads") and i.get("inflight_iteration") == target:
-            out["local_step"].append(w)
-        else:
-            out["needs_state"].append(w)
-    return out
+    """The recovery target from the survivors' ABORTED reports: the newest committed iteration.
+    ``up_to_date``: ranks already there; ``local_step``: ranks one behind that hold the reduced
+    gradients of exactly the target; ``needs_state``: everyone else."""
+    blank = {"committed_iteration": -1, "has_reduced_grads": False}
+    reports = [(w, recovery.get(w, blank)) for w in world]
+    target = max((r.get("committed_iteration", -1) for _, r in reports), default=-1)
+    plan = {"target_iteration": target, "local_step": [], "needs_state": [], "up_to_date": []}
+
+    def bucket(r: dict) -> str:
+        at = r.get("committed_iteration", -1)
+        if at == target:
+            return "up_to_date"
+        steps_locally = at == target - 1 and r.get("has_reduced_grads") and r.get("inflight_iteration") == target
+        return "local_step" if steps_locally else "needs_state"
+
+    for w, r in reports:
+        plan[bucket(r)].append(w)
+    return plan
