@@ -1,11 +1,12 @@
-"""Worker-side interpreter of the pipeline IR (one stream per (replica, stage) slot).
+"""Worker-side interpreter of the pipeline IR (one instruction stream per (replica, stage) slot).
 
-Compute goes through a ``StageExecutor`` (the float64 reference model on CPU; the GPU model of
-``models/`` through ``runtime/gpu_executor.py``); communication goes through ``P2PEngine`` with
-heterogeneous-TP routing.  Sends are posted non-blocking and waited at the end of the iteration,
-which is what the IR validator assumes.  Progress (op index, in-collective flag) is reported on
-every instruction for hang detection, and fault-injection hooks fire at ``forward`` /
-``backward``.  (Reference: ``resihp/runtime/interpreter.py:23-214``.)
+Compute is delegated to a ``StageExecutor`` -- the float64 reference model on the CPU, the GPU
+decoder through ``runtime/gpu_executor.py`` -- and transfers to the ``P2PEngine`` with
+heterogeneous-TP routing.  Sends are posted non-blocking and waited for at the end of the
+iteration, the channel model the IR validator proves safe.  Every instruction reports progress
+(op index, whether it waits on a peer) for hang detection, and fault-injection hooks fire at
+``forward`` and ``backward``.
+Parity: ``resihp/runtime/interpreter.py:23-214`` (same ops, tags and progress reports).
 """
 
 from __future__ import annotations
@@ -24,7 +25,7 @@ from .reference_model import MicroBatch, RefModelConfig, RefStage, microbatch, t
 
 
 class StageExecutor(Protocol):
-    """``stage`` is the virtual stage (model chunk) the instruction belongs to."""
+    """``stage`` is the virtual stage (model chunk) an instruction belongs to."""
 
     def begin_iteration(self, iteration: int) -> None: ...
     def n_rows(self, mb: int) -> int: ...
@@ -34,102 +35,98 @@ class StageExecutor(Protocol):
 
 
 class RefStageExecutor:
+    """Runs the reference model's chunks of one slot on its rank's rows of each micro-batch."""
+
     def __init__(self, cfg: RefModelConfig, sampler: IndexAddressableSampler, module, plan: HeteroParallelPlan,
                  replica: int, stage: int, rank: int, weight_grad_store=None, timer=None):
-        self.cfg = cfg
-        self.sampler = sampler
-        self.module = module
+        self.cfg, self.sampler, self.module, self.plan, self.rank = cfg, sampler, module, plan, rank
         self.modules: dict[int, RefStage] = getattr(module, "chunks", None) or {stage: module}
-        self.plan = plan
         self.group = plan.group(replica, stage)
         self.cp_index = self.group.slice_of(plan.world[rank])
         self.ranks = plan.slice_ranks(self.group, self.cp_index)
-        self.rank = rank
         self.num_stages = plan.num_stages
         self.sp = plan.sequence_parallel and self.group.tp > 1
+        self.wgs, self.timer = weight_grad_store, timer
         self.iteration = -1
-        self.saved: dict[tuple[int, int], tuple] = {}
         self.loss_sum = 0.0
-        self._mbs: dict[int, MicroBatch] = {}
-        self.wgs = weight_grad_store
-        self.timer = timer
+        self.saved: dict[tuple[int, int], tuple] = {}
         self.fwd_docs: dict[int, list[int]] = {}
+        self._batches: dict[int, MicroBatch] = {}
 
     def begin_iteration(self, iteration: int) -> None:
-        self.iteration = iteration
+        self.iteration, self.loss_sum = iteration, 0.0
         self.saved.clear()
-        self._mbs.clear()
-        self.loss_sum = 0.0
+        self._batches.clear()
         self.fwd_docs = {}
 
     def timing_samples(self) -> list[tuple[float, float, float]]:
-        """(tokens, sum of squared doc lengths, forward seconds over local chunks) per micro-batch."""
+        """Per micro-batch: (tokens, sum of squared document lengths, forward seconds over this
+        slot's chunks)."""
         if self.timer is None:
             return []
-        secs: dict[int, float] = {}
+        seconds: dict[int, float] = {}
         for rec in self.timer.collect():
             if rec.op == "F" and rec.iteration == self.iteration and rec.mb in self.fwd_docs:
-                secs[rec.mb] = secs.get(rec.mb, 0.0) + rec.seconds
-        return [(float(sum(self.fwd_docs[mb])), float(sum(d * d for d in self.fwd_docs[mb])), s)
-                for mb, s in secs.items()]
+                seconds[rec.mb] = seconds.get(rec.mb, 0.0) + rec.seconds
+        out = []
+        for mb, secs in seconds.items():
+            docs = self.fwd_docs[mb]
+            out.append((float(sum(docs)), float(sum(d * d for d in docs)), secs))
+        return out
 
     def _timed(self, op: str, mb: int):
-        return self.timer.time(self.iteration, op, mb) if self.timer is not None else nullcontext()
+        return nullcontext() if self.timer is None else self.timer.time(self.iteration, op, mb)
 
-    def _mb(self, mb: int) -> MicroBatch:
-        m = self._mbs.get(mb)
-        if m is None:
-            m = microbatch(self.cfg, self.sampler, self.iteration, mb)
+    def _batch(self, mb: int) -> MicroBatch:
+        if mb not in self._batches:
+            b = microbatch(self.cfg, self.sampler, self.iteration, mb)
             if self.cfg.device != "cpu":
-                dev = self.cfg.device
-                m = MicroBatch(m.x.to(dev), m.y.to(dev), m.mask.to(dev), m.doc_lengths)
-            self._mbs[mb] = m
-        return m
+                d = self.cfg.device
+                b = MicroBatch(b.x.to(d), b.y.to(d), b.mask.to(d), b.doc_lengths)
+            self._batches[mb] = b
+        return self._batches[mb]
 
-    def _chunk(self, mb: int) -> tuple[int, int]:
-        """Token rows of this rank's context-parallel chunk of the micro-batch."""
-        return even_split(self._mb(mb).x.shape[0], self.group.cp)[self.cp_index]
+    def _cp_rows(self, mb: int) -> tuple[int, int]:
+        """Token rows of this rank's context-parallel chunk."""
+        return even_split(self._batch(mb).x.shape[0], self.group.cp)[self.cp_index]
 
     def n_rows(self, mb: int) -> int:
-        a, b = self._chunk(mb)
-        return b - a
+        lo, hi = self._cp_rows(mb)
+        return hi - lo
 
     def _rows(self, mb: int) -> tuple[int, int]:
-        a, b = self._chunk(mb)
+        lo, hi = self._cp_rows(mb)
         if not self.sp:
-            return a, b
-        s, e = local_rows(b - a, self.ranks, self.rank)
-        return a + s, a + e
+            return lo, hi
+        a, b = local_rows(hi - lo, self.ranks, self.rank)
+        return lo + a, lo + b
 
     def forward(self, mb: int, inp: torch.Tensor | None, stage: int) -> torch.Tensor | None:
-        first, last = stage == 0, stage == self.num_stages - 1
-        s, e = self._rows(mb)
-        x = self._mb(mb).x[s:e].clone() if first else inp.detach().requires_grad_(True)
+        lo, hi = self._rows(mb)
+        batch = self._batch(mb)
+        x = batch.x[lo:hi].clone() if stage == 0 else inp.detach().requires_grad_(True)
+        last = stage == self.num_stages - 1
         with self._timed("F", mb):
-            out = self.modules[stage](x)
+            y = self.modules[stage](x)
             if last:
-                m = self._mb(mb)
-                loss = token_loss(out, m.y[s:e], m.mask[s:e])
-        self.fwd_docs[mb] = self._mb(mb).doc_lengths
+                y = token_loss(y, batch.y[lo:hi], batch.mask[lo:hi])
+        self.fwd_docs[mb] = batch.doc_lengths
+        self.saved[(stage, mb)] = (x, y)
         if last:
-            self.loss_sum += loss.item()
-            self.saved[(stage, mb)] = (x, loss)
+            self.loss_sum += y.item()
             return None
-        self.saved[(stage, mb)] = (x, out)
-        return out.detach()
+        return y.detach()
 
     def backward(self, mb: int, grad: torch.Tensor | None, stage: int) -> torch.Tensor | None:
+        x, y = self.saved.pop((stage, mb))
         first, last = stage == 0, stage == self.num_stages - 1
-        x, out = self.saved.pop((stage, mb))
+        upstream = None if last else grad
         if self.wgs is not None and hasattr(self.wgs, "backward_input"):
             with self._timed("B", mb):
-                return self.wgs.backward_input((stage, mb), out, None if last else grad, None if first else x)
-        ctx = self.wgs.deferring((stage, mb)) if self.wgs is not None else nullcontext()
-        with ctx, self._timed("B", mb):
-            if last:
-                out.backward()
-            else:
-                torch.autograd.backward(out, grad)
+                return self.wgs.backward_input((stage, mb), y, upstream, None if first else x)
+        defer = self.wgs.deferring((stage, mb)) if self.wgs is not None else nullcontext()
+        with defer, self._timed("B", mb):
+            torch.autograd.backward(y, upstream)
         return None if first else x.grad
 
     def weight_backward(self, mb: int, stage: int) -> None:
@@ -138,72 +135,73 @@ class RefStageExecutor:
 
 
 def message_tag(mb: int, kind: str, dst_stage: int) -> int:
-    return (mb * 2 + (0 if kind == "act" else 1)) * 256 + dst_stage
+    """Tag of an activation / gradient message: micro-batch, kind and destination stage."""
+    return ((2 * mb + (kind != "act")) << 8) + dst_stage
 
 
 class Interpreter:
     def __init__(self, plan: HeteroParallelPlan, stream: list[Instr], executor: StageExecutor, p2p: P2PEngine,
                  replica: int, stage: int, row_shape: tuple[int, ...], dtype: torch.dtype, tp_group=None,
                  progress=None, hook=None):
-        self.plan = plan
-        self.stream = stream
-        self.executor = executor
-        self.p2p = p2p
+        self.plan, self.stream, self.executor, self.p2p = plan, stream, executor, p2p
         self.key = (replica, stage)
         self.group = plan.group(replica, stage)
-        # activations stay inside a context-parallel chunk: slice i only talks to slice i
+        # activations never leave a context-parallel chunk: slice i only talks to slice i
         self.cp_index = self.group.slice_of(plan.world[p2p.rank])
         self.ranks = plan.slice_ranks(self.group, self.cp_index)
-        self.row_shape = row_shape
-        self.dtype = dtype
-        self.tp_group = tp_group
+        self.row_shape, self.dtype, self.tp_group = row_shape, dtype, tp_group
         self.sp = plan.sequence_parallel
-        self.progress = progress or (lambda **kw: None)
-        self.hook = hook or (lambda it, phase: None)
+        self.progress = progress if progress is not None else (lambda **kw: None)
+        self.hook = hook if hook is not None else (lambda it, phase: None)
+        self._ops = {Op.RECV_ACT: self._recv_act, Op.F: self._forward, Op.SEND_ACT: self._send_act,
+                     Op.RECV_GRAD: self._recv_grad, Op.B: self._backward, Op.SEND_GRAD: self._send_grad,
+                     Op.W: self._weight}
 
     def peer_ranks(self, peer: tuple[int, int]) -> tuple[int, ...]:
         return self.plan.slice_ranks(self.plan.group(*peer), self.cp_index)
 
-    def _recv(self, mb: int, kind: str, stage: int, peer) -> torch.Tensor:
-        ex = self.executor
-        return self.p2p.recv(ex.n_rows(mb), self.row_shape, self.dtype, self.peer_ranks(peer), self.ranks, self.sp,
-                             message_tag(mb, kind, stage), self.tp_group)
+    def _receive(self, mb: int, kind: str, stage: int, peer) -> torch.Tensor:
+        return self.p2p.recv(self.executor.n_rows(mb), self.row_shape, self.dtype, self.peer_ranks(peer), self.ranks,
+                             self.sp, message_tag(mb, kind, stage), self.tp_group)
 
-    def _send(self, t: torch.Tensor, mb: int, kind: str, peer) -> list:
-        return self.p2p.send(t, self.ranks, self.peer_ranks(peer), self.executor.n_rows(mb), self.sp,
-                             message_tag(mb, kind, peer[1]))
+    def _post(self, t: torch.Tensor, mb: int, kind: str, peer) -> None:
+        self._sends += self.p2p.send(t, self.ranks, self.peer_ranks(peer), self.executor.n_rows(mb), self.sp,
+                                     message_tag(mb, kind, peer[1]))
+
+    # one handler per op; ``slot`` is (virtual stage, micro-batch)
+    def _recv_act(self, ins: Instr, slot, it: int) -> None:
+        self._box["act"][slot] = self._receive(ins.mb, "act", slot[0], ins.peer)
+
+    def _forward(self, ins: Instr, slot, it: int) -> None:
+        self.hook(it, "forward")
+        out = self.executor.forward(ins.mb, self._box["act"].pop(slot, None), slot[0])
+        if out is not None:
+            self._box["out"][slot] = out
+
+    def _send_act(self, ins: Instr, slot, it: int) -> None:
+        self._post(self._box["out"].pop(slot), ins.mb, "act", ins.peer)
+
+    def _recv_grad(self, ins: Instr, slot, it: int) -> None:
+        self._box["grad"][slot] = self._receive(ins.mb, "grad", slot[0], ins.peer)
+
+    def _backward(self, ins: Instr, slot, it: int) -> None:
+        self.hook(it, "backward")
+        g = self.executor.backward(ins.mb, self._box["grad"].pop(slot, None), slot[0])
+        if g is not None:
+            self._box["igrad"][slot] = g
+
+    def _send_grad(self, ins: Instr, slot, it: int) -> None:
+        self._post(self._box["igrad"].pop(slot), ins.mb, "grad", ins.peer)
+
+    def _weight(self, ins: Instr, slot, it: int) -> None:
+        self.executor.weight_backward(ins.mb, slot[0])
 
     def run(self, iteration: int) -> None:
-        ex = self.executor
-        ex.begin_iteration(iteration)
-        acts: dict = {}
-        grads: dict = {}
-        outs: dict = {}
-        igrads: dict = {}
-        sends: list = []
-        for i, ins in enumerate(self.stream):
-            self.progress(iteration=iteration, phase=f"{ins.op.value}{ins.mb}", op_seq=i,
-                          in_collective=ins.op in (Op.RECV_ACT, Op.RECV_GRAD))
-            mb, s = ins.mb, ins.stage_on(self.key)
-            k = (s, mb)
-            if ins.op == Op.RECV_ACT:
-                acts[k] = self._recv(mb, "act", s, ins.peer)
-            elif ins.op == Op.F:
-                self.hook(iteration, "forward")
-                out = ex.forward(mb, acts.pop(k, None), s)
-                if out is not None:
-                    outs[k] = out
-            elif ins.op == Op.SEND_ACT:
-                sends += self._send(outs.pop(k), mb, "act", ins.peer)
-            elif ins.op == Op.RECV_GRAD:
-                grads[k] = self._recv(mb, "grad", s, ins.peer)
-            elif ins.op == Op.B:
-                self.hook(iteration, "backward")
-                g = ex.backward(mb, grads.pop(k, None), s)
-                if g is not None:
-                    igrads[k] = g
-            elif ins.op == Op.SEND_GRAD:
-                sends += self._send(igrads.pop(k), mb, "grad", ins.peer)
-            elif ins.op == Op.W:
-                ex.weight_backward(mb, s)
-        self.p2p.wait_sends(sends)
+        self.executor.begin_iteration(iteration)
+        self._box = {"act": {}, "out": {}, "grad": {}, "igrad": {}}
+        self._sends: list = []
+        for index, ins in enumerate(self.stream):
+            waiting = ins.op in (Op.RECV_ACT, Op.RECV_GRAD)
+            self.progress(iteration=iteration, phase=f"{ins.op.value}{ins.mb}", op_seq=index, in_collective=waiting)
+            self._ops[ins.op](ins, (ins.stage_on(self.key), ins.mb), iteration)
+        self.p2p.wait_sends(self._sends)
