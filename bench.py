@@ -66,9 +66,14 @@ def _args():
     ap.add_argument("--cuda-graph", action="store_true",
                     help="one GPU: capture the whole step (every micro-batch and the update) in a CUDA graph after "
                          "the warm-up and replay it")
-    ap.add_argument("--parallelism", default="dp",
-                    help="'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' with T*P*D = N: tensor (+ sequence) x "
-                         "pipeline x data parallelism through the plan-driven runtime (benchmark config 2: tp2pp2dp2)")
+    ap.add_argument("--parallelism", default="auto",
+                    help="'auto' (benchmark config 2's layout where it fits N: tp2pp1dp1 at 2 GPUs, tp2pp2dp1 at 4, "
+                         "tp2pp2dp2 at 8; data parallel otherwise), 'dp' (data parallel, ZeRO-1) or 'tp{T}pp{P}dp{D}' "
+                         "with T*P*D = N: tensor (+ sequence) x pipeline x data parallelism through the plan-driven "
+                         "runtime")
+    ap.add_argument("--no-auto-reconfig", action="store_true",
+                    help="with --parallelism auto: do not run the live reconfiguration that 'auto' adds when the "
+                         "layout has a data-parallel replica (the evicted rank's slices need a surviving holder)")
     ap.add_argument("--ep-impl", choices=["peer", "nccl"], default="peer",
                     help="MoE models: expert dispatch / combine over NVLink peer memory, or NCCL all_to_all")
     ap.add_argument("--tp-impl", choices=["fused", "collective"], default="fused",
@@ -100,6 +105,25 @@ def parse_layout(text: str) -> tuple[int, int, int] | None:
 
     m = re.fullmatch(r"tp(\d+)pp(\d+)dp(\d+)", text)
     return None if m is None else tuple(int(x) for x in m.groups())
+
+
+CONFIG2_LAYOUTS = {2: "tp2pp1dp1", 4: "tp2pp2dp1", 8: "tp2pp2dp2"}  # benchmark config 2 scaled to N GPUs
+
+
+def resolve_auto_layout(args, world: int) -> None:
+    """``--parallelism auto``: benchmark config 2's TP2 x PP2 x DP2 (+ SP) layout, scaled down to
+    the GPUs present (its global batch, 8 sequences per GPU, scales with them); a live
+    reconfiguration (eviction of the last rank) is added when the layout has a data-parallel
+    replica to take over the evicted rank's slices."""
+    if args.parallelism != "auto":
+        return
+    from resihp_megatron_b200.models.config import get_config
+
+    dense_llama = not get_config(args.model).is_moe and args.model.startswith("llama")
+    args.parallelism = CONFIG2_LAYOUTS.get(world, "dp") if dense_llama else "dp"
+    layout = parse_layout(args.parallelism)
+    if layout is not None and layout[2] >= 2 and not args.no_auto_reconfig and not args.reshard:
+        args.reconfig = True
 
 
 def reference_unavailable(args) -> None:
@@ -194,6 +218,7 @@ def main() -> None:
     rank, world, local = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    resolve_auto_layout(args, world)
     if args.parallelism == "ep" or get_config(args.model).is_moe:
         run_moe(args, rank, world, local)
         return
@@ -566,32 +591,14 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
                  "layout_post": trainer.layout, "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
                  "post_ms_per_step": post_ms / args.steps, "reshard_to_commit_s": commit_max,
                  "post_loss": post["loss"], "phases_s_rank0": trainer.last_reconfig}
+    elif args.reconfig and layout[2] < 2:
+        recfg = {"skipped": "no data-parallel replica: the evicted rank's tensor-parallel slices would have no "
+                            "surviving holder (a fail-stop here restores from a checkpoint)"}
     elif args.reconfig:
-        dist.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        alive = trainer.reconfigure([world - 1])
-        commit_s = time.perf_counter() - t0
-        if alive:
-            for _ in range(max(2, min(args.warmup, 3))):
-                trainer.step_device()
-            torch.cuda.synchronize()
-            trainer.check()
-            dist.barrier()
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            for _ in range(args.steps):
-                loss2 = trainer.step_device()
-            end.record()
-            torch.cuda.synchronize()
-            vals = torch.tensor([start.elapsed_time(end), commit_s], device=trainer.device, dtype=torch.float64)
-            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-            post_ms, commit_max = vals.tolist()
-            recfg = {"kind": "planned eviction of the last rank; re-planned layout, slice-level state migration",
-                     "n_gpus_post": dist.get_world_size(),
-                     "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
-                     "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
-                     "post_loss": float(loss2.item()), "phases_s_rank0": trainer.last_reconfig}
+        try:
+            recfg, alive = _hybrid_reconfig(args, trainer, world)
+        except Exception as e:  # noqa: BLE001 -- the pre-reconfiguration line is still reported
+            recfg, alive = {"error": f"{type(e).__name__}: {e}"[:400]}, False
     if rank == 0:
         out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r, {"layers_per_stage": parts})
         if recfg is not None:
@@ -602,6 +609,41 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
     dist.barrier()
     trainer.close()
     dist.barrier()
+
+
+def _hybrid_reconfig(args, trainer, world: int):
+    """Planned eviction of the last rank; the survivors re-plan (TP shrink or eviction of its
+    group, min-max layer repartition), migrate state slice by slice and run timed steps.
+    Returns (record, whether this rank is still in the job)."""
+    import torch
+    import torch.distributed as dist
+
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    alive = trainer.reconfigure([world - 1])
+    commit_s = time.perf_counter() - t0
+    if not alive:
+        return None, False
+    for _ in range(max(2, min(args.warmup, 3))):
+        trainer.step_device()
+    torch.cuda.synchronize()
+    trainer.check()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        loss2 = trainer.step_device()
+    end.record()
+    torch.cuda.synchronize()
+    vals = torch.tensor([start.elapsed_time(end), commit_s], device=trainer.device, dtype=torch.float64)
+    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    post_ms, commit_max = vals.tolist()
+    return {"kind": "planned eviction of the last rank; re-planned layout, slice-level state migration",
+            "n_gpus_post": dist.get_world_size(), "post_value": trainer.tokens_per_step * args.steps / (post_ms / 1000),
+            "post_ms_per_step": post_ms / args.steps, "evict_to_commit_s": commit_max,
+            "post_loss": float(loss2.item()), "phases_s_rank0": trainer.last_reconfig,
+            "layout_post": trainer.layout}, True
 
 
 if __name__ == "__main__":
