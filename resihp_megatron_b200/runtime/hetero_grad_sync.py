@@ -1,14 +1,15 @@
 """Shard-aligned gradient reduction across DP replicas whose TP degrees differ.
 
-For a stage, every replica splits a partitioned dimension of length ``n`` evenly by its own TP
-degree; on the common refinement of those splits each interval has exactly one holder per
-replica, and those holders all-reduce exactly that slice (one ``dpshard/s{s}/{ranks}`` group
-per holder set).  With uniform TP this is the plain DP all-reduce; with TP 4 vs 3 it is the
-correct generalisation (pairing ranks by TP index would be wrong).  TP-replicated parameters
-are reduced through responsibility slices (rank ``t`` of a TP-``k`` replica reduces
-``even_split(numel, k)[t]``) and re-assembled with one all-gather in the TP group; under sequence
-parallelism their gradients are partial and are first summed inside the TP group.
-(Reference: ``resihp/runtime/hetero_grad_sync.py:34-126``.)
+For one stage, every replica splits a partitioned dimension of length ``n`` evenly by its own
+TP degree.  On the common refinement of those splits each interval has exactly one holder per
+replica, and exactly those holders all-reduce that interval (one ``dpshard/s{s}/{ranks}`` group
+per holder set).  With uniform TP this is the plain DP all-reduce; with, say, TP4 next to TP3 it
+is the correct generalisation (pairing ranks by TP index would not be).  A TP-replicated
+parameter is reduced through responsibility slices -- TP rank ``t`` of a TP-``k`` replica
+reduces ``even_split(numel, k)[t]`` -- and re-assembled with one all-gather in the TP group;
+under sequence parallelism its gradient is a partial sum over token shards and is first summed
+inside the TP group.
+Parity: ``resihp/runtime/hetero_grad_sync.py:34-126`` (same holder sets and reduction steps).
 """
 
 from __future__ import annotations
@@ -30,91 +31,88 @@ class ParamShard:
     sp_partial: bool = False
 
 
+def _packed_all_reduce(views: list[torch.Tensor], issue, what: str) -> None:
+    """All-reduce several tensor views as one flat buffer and write the sums back."""
+    flat = torch.cat([v.reshape(-1) for v in views])
+    issue(flat, what)
+    offset = 0
+    for v in views:
+        v.copy_(flat[offset:offset + v.numel()].view_as(v))
+        offset += v.numel()
+
+
 class HeteroGradSync:
     def __init__(self, plan: HeteroParallelPlan, comms, mgr, stage: int, replica: int,
                  params: dict[str, torch.Tensor], shards: dict[str, ParamShard], tp_group=None,
                  timeout: float = 120.0):
-        self.plan = plan
-        self.comms = comms
-        self.mgr = mgr
-        self.stage = stage
-        self.replica = replica
-        self.params = params
-        self.shards = shards
-        self.tp_group = tp_group
-        self.timeout = timeout
-        g = plan.group(replica, stage)
+        self.plan, self.comms, self.mgr = plan, comms, mgr
+        self.stage, self.replica = stage, replica
+        self.params, self.shards = params, shards
+        self.tp_group, self.timeout = tp_group, timeout
+        group = plan.group(replica, stage)
         me = plan.world[comms.rank]
-        self.tp = g.tp
-        self.tp_rank = g.slice(g.slice_of(me)).index(me)
+        self.tp = group.tp
+        self.tp_rank = group.slice(group.slice_of(me)).index(me)
         self.peers = plan.tp_slices(stage)
-        self._layout = self._build_layout()
+        self._buckets = self._plan_buckets()
 
-    def _build_layout(self) -> dict[str, list[tuple[str, tuple[int, int], tuple[int, int]]]]:
-        """group name -> [(key, global interval, local interval)] in a deterministic order."""
-        layout: dict[str, list] = {}
+    def _plan_buckets(self) -> dict[str, list[tuple[str, tuple[int, int], tuple[int, int]]]]:
+        """Reduction group name -> ``(key, global interval, local interval)`` of the pieces this rank
+        reduces in it, groups in name order (the same order on every member)."""
+        buckets: dict[str, list] = {}
         for key in sorted(self.params):
             info = self.shards[key]
-            parts = [even_split(info.full_size, len(sl)) for sl in self.peers]
-            mine = even_split(info.full_size, self.tp)[self.tp_rank]
-            base = mine[0] if info.dim is not None else 0
-            for iv in refine(parts):
-                if not (mine[0] <= iv[0] and iv[1] <= mine[1]):
-                    continue
-                holders = tuple(sorted(self.plan.rank(sl[locate(p, iv)]) for sl, p in zip(self.peers, parts)))
-                layout.setdefault(dpshard_group_name(self.stage, holders), []).append(
-                    (key, iv, (iv[0] - base, iv[1] - base)))
-        return dict(sorted(layout.items()))
+            splits = [even_split(info.full_size, len(peer)) for peer in self.peers]
+            lo, hi = even_split(info.full_size, self.tp)[self.tp_rank]
+            offset = lo if info.dim is not None else 0
+            for piece in refine(splits):
+                if piece[0] < lo or piece[1] > hi:
+                    continue  # another TP rank of this replica reduces it
+                holders = sorted(self.plan.rank(peer[locate(split, piece)]) for peer, split in zip(self.peers, splits))
+                name = dpshard_group_name(self.stage, tuple(holders))
+                buckets.setdefault(name, []).append((key, piece, (piece[0] - offset, piece[1] - offset)))
+        return {name: buckets[name] for name in sorted(buckets)}
 
-    def _rows_view(self, key: str) -> torch.Tensor:
-        g = self.params[key].grad
-        info = self.shards[key]
-        return g.reshape(-1) if info.dim is None else g.movedim(info.dim, 0)
+    def holder_groups(self) -> list[str]:
+        return list(self._buckets)
 
-    def _wait(self, work, what: str) -> None:
-        self.mgr.guarded_wait(work, timeout=self.timeout, what=what)
+    def _issue(self, group):
+        def run(flat: torch.Tensor, what: str) -> None:
+            self.mgr.guarded_wait(dist.all_reduce(flat, group=group, async_op=True), timeout=self.timeout, what=what)
+
+        return run
+
+    def _rows(self, key: str) -> torch.Tensor:
+        """The gradient with its partitioned dimension first (flattened when replicated)."""
+        grad, dim = self.params[key].grad, self.shards[key].dim
+        return grad.reshape(-1) if dim is None else grad.movedim(dim, 0)
 
     def sync(self) -> None:
         for p in self.params.values():
             if p.grad is None:
                 p.grad = torch.zeros_like(p)
+        partial = [self.params[k].grad for k in sorted(self.params) if self.shards[k].sp_partial]
+        if self.tp > 1 and partial:
+            _packed_all_reduce(partial, self._issue(self.tp_group), "tp partial-grad all-reduce")
+        for name, pieces in self._buckets.items():
+            group = self.comms.groups.get(name)
+            if group is None:
+                continue  # a holder set of one: nothing to reduce
+            views = [self._rows(key).narrow(0, a, b - a) for key, _, (a, b) in pieces]
+            _packed_all_reduce(views, self._issue(group), f"grad all-reduce {name}")
         if self.tp > 1:
-            partial = [k for k in sorted(self.params) if self.shards[k].sp_partial]
-            if partial:
-                flat = torch.cat([self.params[k].grad.reshape(-1) for k in partial])
-                self._wait(dist.all_reduce(flat, group=self.tp_group, async_op=True), "tp partial-grad all-reduce")
-                off = 0
-                for k in partial:
-                    g = self.params[k].grad
-                    g.copy_(flat[off:off + g.numel()].view_as(g))
-                    off += g.numel()
-        for name, entries in self._layout.items():
-            pg = self.comms.groups.get(name)
-            if pg is None:
-                continue
-            views = [self._rows_view(k).narrow(0, loc[0], loc[1] - loc[0]) for k, _, loc in entries]
-            flat = torch.cat([v.reshape(-1) for v in views])
-            self._wait(dist.all_reduce(flat, group=pg, async_op=True), f"grad all-reduce {name}")
-            off = 0
-            for v in views:
-                v.copy_(flat[off:off + v.numel()].view_as(v))
-                off += v.numel()
-        if self.tp > 1:
-            self._regather_replicated()
+            for key in (k for k in sorted(self.params) if self.shards[k].dim is None):
+                self._reassemble(self.params[key].grad.reshape(-1))
 
-    def _regather_replicated(self) -> None:
-        for k in sorted(self.params):
-            if self.shards[k].dim is not None:
-                continue
-            flat = self.params[k].grad.reshape(-1)
-            parts = even_split(flat.numel(), self.tp)
-            width = max(b - a for a, b in parts)
-            a, b = parts[self.tp_rank]
-            mine = torch.zeros(width, dtype=flat.dtype, device=flat.device)
-            mine[: b - a].copy_(flat[a:b])
-            bufs = [torch.empty_like(mine) for _ in range(self.tp)]
-            self._wait(dist.all_gather(bufs, mine, group=self.tp_group, async_op=True), "replicated grad all-gather")
-            flat.copy_(torch.cat([buf[: pb - pa] for buf, (pa, pb) in zip(bufs, parts)]))
-
-    def holder_groups(self) -> list[str]:
-        return list(self._layout)
+    def _reassemble(self, flat: torch.Tensor) -> None:
+        """Every TP rank reduced its responsibility slice of a replicated gradient: gather them."""
+        slices = even_split(flat.numel(), self.tp)
+        width = max(b - a for a, b in slices)
+        lo, hi = slices[self.tp_rank]
+        padded = torch.zeros(width, dtype=flat.dtype, device=flat.device)
+        padded[:hi - lo] = flat[lo:hi]
+        gathered = [torch.empty_like(padded) for _ in slices]
+        self.mgr.guarded_wait(dist.all_gather(gathered, padded, group=self.tp_group, async_op=True),
+                              timeout=self.timeout, what="replicated grad all-gather")
+        for part, (a, b) in zip(gathered, slices):
+            flat[a:b] = part[:b - a]
