@@ -1,19 +1,21 @@
-"""Per-generation rebuild of resources bound to one communicator layout.
+"""Per-generation rebuild of the resources bound to one communicator layout.
 
-Captured CUDA graphs bake in buffer addresses, communicator handles and the layer set; the
+A captured CUDA graph bakes in buffer addresses, communicator handles and the layer set; the
 symmetric peer-memory heap of the fused kernels maps the previous generation's peers.  Both must
-be released *before* the old generation's communicators are destroyed and re-created *after*
-the new generation's runtime exists (before READY), or the new generation replays stale
-pointers.  ``ResilientTrainer`` drives the hooks:
+be released *before* the old generation's communicators go away and re-created *after* the new
+generation's runtime exists (before READY), or the new generation would replay stale pointers.
+``ResilientTrainer`` drives the hooks:
 
-    teardown()                 before ResilientCommManager.build() replaces generation g
+    teardown()                 before the comm manager replaces generation g
     rebuild(comms, payload)    after the binding built generation g+1's runtime
     after_iteration(i)         after every committed iteration (deferred graph capture)
 
-Teardown is best effort (a failed release must not block recovery); a failed rebuild raises,
-which reports ``build_failed`` and retries the generation.
-(Reference: ``resihp/runtime/generation_hooks.py:32-162``, whose hooks manage Transformer Engine
-userbuffers and Megatron CUDA graphs.)
+Teardown is best effort -- hooks are released in reverse registration order and a failure is
+logged and returned, never raised, so it cannot block recovery; a failed rebuild raises, which
+reports ``build_failed`` and retries the generation.
+Parity: ``resihp/runtime/generation_hooks.py:32-162`` (same ordering contract; the reference's
+hooks manage Transformer Engine userbuffers and Megatron CUDA graphs, ours the peer-memory heap
+and the engine's step graphs).
 """
 
 from __future__ import annotations
@@ -39,49 +41,45 @@ class GenerationHooks:
         self.hooks.append(hook)
 
     def teardown(self) -> list[str]:
-        errors = []
-        for h in reversed(self.hooks):
+        """Release every hook, last registered first; returns the failures as text."""
+        failures = []
+        for hook in self.hooks[::-1]:
+            name = type(hook).__name__
             try:
-                h.teardown()
-            except Exception as e:  # noqa: BLE001
-                log.warning("teardown of %s failed: %s", type(h).__name__, e)
-                errors.append(f"{type(h).__name__}: {e}")
-        return errors
+                hook.teardown()
+            except Exception as err:  # noqa: BLE001 -- release is best effort
+                log.warning("teardown of %s failed: %s", name, err)
+                failures.append(f"{name}: {err}")
+        return failures
 
     def rebuild(self, comms, payload: dict) -> None:
-        for h in self.hooks:
-            h.rebuild(comms, payload)
+        for hook in self.hooks:
+            hook.rebuild(comms, payload)
 
     def after_iteration(self, iteration: int) -> None:
-        for h in self.hooks:
-            fn = getattr(h, "after_iteration", None)
-            if fn is not None:
-                fn(iteration)
+        for hook in filter(lambda h: hasattr(h, "after_iteration"), self.hooks):
+            hook.after_iteration(iteration)
 
 
 def uniform_contiguous_tp(plan: HeteroParallelPlan) -> int | None:
-    """The TP degree when every TP group of the plan is an aligned, rank-contiguous block of the
-    same size (the layout fixed-shape peer buffers are built for), else ``None``."""
-    tps = {g.tp for g in plan.stage_groups}
-    if len(tps) != 1:
+    """The TP degree if every TP group of the plan is an aligned block of consecutive ranks of one
+    common size (what fixed-shape peer buffers assume), else None."""
+    degrees = {g.tp for g in plan.stage_groups}
+    if len(degrees) != 1:
         return None
-    tp = tps.pop()
-    for g in plan.stage_groups:
-        for i in range(g.cp):
-            ranks = plan.slice_ranks(g, i)
-            if ranks != tuple(range(ranks[0], ranks[0] + tp)) or ranks[0] % tp:
-                return None
-    return tp
+    (tp,) = degrees
+    blocks = (plan.slice_ranks(g, c) for g in plan.stage_groups for c in range(g.cp))
+    aligned = all(b[0] % tp == 0 and list(b) == list(range(b[0], b[0] + tp)) for b in blocks)
+    return tp if aligned else None
 
 
 class SymmetricHeapHook:
-    """Per-generation symmetric peer-memory heap of the fused TP/DP/EP kernels.
+    """The per-generation symmetric peer-memory heap of the fused TP / DP / EP kernels.
 
-    ``factory(comms, payload)`` builds the heap for the new generation (exchanging handles over
-    the generation's store prefix); ``teardown`` raises the abort word, waits for in-flight
-    kernels and unmaps the peers.  Heterogeneous layouts are supported (the heap maps whatever
-    groups the plan names), so ``enabled`` is False only without a factory.
-    """
+    ``factory(comms, payload)`` builds the new generation's heap (exchanging handles under the
+    generation's store prefix); ``teardown`` closes the old one, which raises its abort word,
+    waits for kernels in flight and unmaps the peers.  Any layout the plan names is supported,
+    so the hook is disabled only when there is no factory."""
 
     def __init__(self, factory: Callable[[object, dict], object] | None):
         self.factory = factory
@@ -93,44 +91,43 @@ class SymmetricHeapHook:
         return self.factory is not None
 
     def teardown(self) -> None:
-        if self.heap is not None:
-            close = getattr(self.heap, "close", None)
-            if close is not None:
-                close()
-            self.heap = None
+        heap, self.heap = self.heap, None
+        closer = getattr(heap, "close", None)
+        if closer is not None:
+            closer()
 
     def rebuild(self, comms, payload: dict) -> None:
-        if self.factory is None:
-            return
-        self.heap = self.factory(comms, payload)
-        self.rebuilds += 1
+        if self.enabled:
+            self.heap = self.factory(comms, payload)
+            self.rebuilds += 1
 
 
 class CudaGraphHook:
-    """Graphs of the engine's step are dropped with the old generation and re-captured after
-    ``warmup`` eager iterations of the new one (the warm-up absorbs first-iteration allocator
-    growth).  ``engine`` exposes ``drop_graphs()`` and ``capture_graphs()``."""
+    """The engine's step graphs are dropped with the old generation and captured again after
+    ``warmup`` eager iterations of the new one (the eager steps absorb the allocator's first-use
+    growth).  The engine provides ``drop_graphs()`` and ``capture_graphs()``."""
 
     def __init__(self, engine_fn: Callable[[], object] | None = None, warmup: int = 1):
-        self.engine_fn = engine_fn
-        self.warmup = warmup
+        self.engine_fn, self.warmup = engine_fn, warmup
         self.eager_left = 0
         self.captures = 0
 
+    def _engine_call(self, method: str) -> None:
+        engine = self.engine_fn() if self.engine_fn is not None else None
+        fn = getattr(engine, method, None)
+        if fn is not None:
+            fn()
+
     def teardown(self) -> None:
-        eng = self.engine_fn() if self.engine_fn else None
-        if eng is not None and hasattr(eng, "drop_graphs"):
-            eng.drop_graphs()
+        self._engine_call("drop_graphs")
 
     def rebuild(self, comms, payload: dict) -> None:
         self.eager_left = self.warmup
 
     def after_iteration(self, iteration: int) -> None:
-        if self.eager_left <= 0:
+        if self.eager_left == 0:
             return
         self.eager_left -= 1
         if self.eager_left == 0:
-            eng = self.engine_fn() if self.engine_fn else None
-            if eng is not None and hasattr(eng, "capture_graphs"):
-                eng.capture_graphs()
+            self._engine_call("capture_graphs")
             self.captures += 1
