@@ -1,20 +1,21 @@
-"""Reference MoE block and a dropless expert-parallel runtime over arbitrary placements.
+"""The float64 MoE block and a dropless expert-parallel runtime over arbitrary placements.
 
-``y = x + sum_k g_k(x) * E_{e_k}(x)``: top-k routing with the softmax taken over the selected
+``y = x + sum_k g_k(x) * E_{e_k}(x)``: top-k routing whose softmax runs over the selected
 logits; a non-trainable per-expert bias is added to the logits for *selection only*
-(aux-loss-free balancing, moved by ``rate * sign(mean load - load)`` each iteration).  Experts
-are two-layer GELU MLPs.  Parameters are a pure function of ``(seed, key)``, so every placement
-sees the same model.
+(aux-loss-free balancing, moved by ``rate * sign(mean load - load)`` after every iteration).
+Experts are two-layer GELU MLPs.  Parameters are a pure function of ``(seed, key)``, so every
+placement trains the same model.
 
-``EPRuntime``: router replicated (data parallel over all ranks), the token copies for each
-expert are split over its replicas in the EP group by speed-weighted smooth round-robin, a
-counts all-to-all precedes an autograd-aware all-to-all dispatch, local expert copies run, a
-reverse all-to-all returns the outputs and they are combined with the gate weights.  Each
-expert's gradient is summed over all its holders (``edp/`` groups derived from the placement).
-Dropless routing and a per-token loss over the global token count make any placement -- with or
-without replicated experts, before or after a failure -- equal to the single-process reference
-up to reduction order.  On GPU the dispatch -> grouped expert GEMM -> combine path is the fused
-kernels of ``parallel/moe_ep``.  (Reference: ``resihp/runtime/moe.py:29-269``.)
+``EPRuntime`` replicates the router (data parallel over all ranks).  The (token, slot) pairs of
+each expert are dealt to its replicas inside the EP group by speed-weighted smooth round robin;
+a counts all-to-all precedes an autograd-aware all-to-all of the token rows, the local expert
+copies run, a reverse all-to-all returns their outputs, and the outputs are combined with the
+gate weights.  Each expert's gradient is summed over all its holders (``edp/`` groups that
+follow from the placement).  Dropless routing and a per-token loss over the global token count
+make any placement -- replicated experts or not, before or after a failure -- equal to the
+single-process reference up to reduction order.  On GPUs the dispatch, expert GEMMs and combine
+are the peer-memory kernels of ``parallel/moe_ep``.
+Parity: ``resihp/runtime/moe.py:29-269`` (same model, routing, placement use and group names).
 """
 
 from __future__ import annotations
@@ -31,6 +32,8 @@ from ..state.layer_registry import FULL, Holdings, TensorSpec
 from ..state.rng_data import generator
 from ..utils.intervals import even_split
 
+_EXPERT_MATS = ("fc1.weight", "fc2.weight")
+
 
 @dataclass(frozen=True)
 class MoEConfig:
@@ -44,31 +47,40 @@ class MoEConfig:
     bias_update_rate: float = 0.0
 
 
+def _expert_key(e: int, mat: str) -> str:
+    return f"experts.{e}.{mat}"
+
+
 def moe_specs(cfg: MoEConfig) -> dict[str, TensorSpec]:
-    h, f = cfg.hidden, cfg.ffn
-    out = {"router.weight": TensorSpec("router.weight", (cfg.num_experts, h), None)}
+    """Registry specs: the router, the optional selection bias and every expert's two matrices."""
+    shapes = {"fc1.weight": (cfg.ffn, cfg.hidden), "fc2.weight": (cfg.hidden, cfg.ffn)}
+    specs = {"router.weight": TensorSpec("router.weight", (cfg.num_experts, cfg.hidden), None)}
     if cfg.bias_update_rate:
-        out["router.expert_bias"] = TensorSpec("router.expert_bias", (cfg.num_experts,), None, trainable=False)
+        specs["router.expert_bias"] = TensorSpec("router.expert_bias", (cfg.num_experts,), None, trainable=False)
     for e in range(cfg.num_experts):
-        out[f"experts.{e}.fc1.weight"] = TensorSpec(f"experts.{e}.fc1.weight", (f, h), None)
-        out[f"experts.{e}.fc2.weight"] = TensorSpec(f"experts.{e}.fc2.weight", (h, f), None)
-    return out
+        for mat in _EXPERT_MATS:
+            key = _expert_key(e, mat)
+            specs[key] = TensorSpec(key, shapes[mat], None)
+    return specs
 
 
 def expert_of(key: str) -> int | None:
-    return int(key.split(".")[1]) if key.startswith("experts.") else None
+    head, _, rest = key.partition(".")
+    return int(rest.partition(".")[0]) if head == "experts" else None
 
 
 def init_param(cfg: MoEConfig, spec: TensorSpec) -> torch.Tensor:
     if not spec.trainable:
         return torch.zeros(spec.global_shape, dtype=cfg.dtype)
     g = generator(cfg.seed, zlib.crc32(spec.key.encode()))
-    return torch.randn(spec.global_shape, generator=g, dtype=cfg.dtype) / spec.global_shape[-1] ** 0.5
+    fan_in = spec.global_shape[-1]
+    return torch.randn(spec.global_shape, generator=g, dtype=cfg.dtype) / fan_in ** 0.5
 
 
 def update_expert_bias(cfg: MoEConfig, bias: torch.Tensor, loads: torch.Tensor) -> None:
+    """Aux-loss-free balancing: underloaded experts' bias rises, overloaded ones' falls."""
     with torch.no_grad():
-        bias.add_(cfg.bias_update_rate * torch.sign(loads.mean() - loads))
+        bias += cfg.bias_update_rate * (loads.mean() - loads).sign()
 
 
 def batch(cfg: MoEConfig, iteration: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -78,10 +90,11 @@ def batch(cfg: MoEConfig, iteration: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def route(cfg: MoEConfig, x: torch.Tensor, router: torch.Tensor, bias: torch.Tensor | None = None):
-    """Top-k expert ids (selected on logits + bias) and softmax gates over the selected logits."""
+    """Top-k expert ids (chosen on logits + bias) and the softmax gates of the chosen logits."""
     logits = x @ router.t()
-    topi = (logits if bias is None else logits + bias).topk(cfg.top_k, dim=-1).indices
-    return topi, torch.softmax(logits.gather(-1, topi), dim=-1)
+    chooser = logits if bias is None else logits + bias
+    chosen = chooser.topk(cfg.top_k, dim=-1).indices
+    return chosen, logits.gather(-1, chosen).softmax(dim=-1)
 
 
 def expert_ffn(x: torch.Tensor, fc1: torch.Tensor, fc2: torch.Tensor) -> torch.Tensor:
@@ -89,47 +102,53 @@ def expert_ffn(x: torch.Tensor, fc1: torch.Tensor, fc2: torch.Tensor) -> torch.T
 
 
 def token_loss(out: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-    return ((out - y) ** 2).mean(dim=-1).sum()
+    return (out - y).pow(2).mean(dim=-1).sum()
 
 
 def reference_forward(cfg: MoEConfig, params: dict[str, torch.Tensor], x: torch.Tensor) -> torch.Tensor:
-    topi, gates = route(cfg, x, params["router.weight"], params.get("router.expert_bias"))
-    if "router.expert_bias" in params:
-        loads = torch.bincount(topi.reshape(-1), minlength=cfg.num_experts).to(cfg.dtype)
-        update_expert_bias(cfg, params["router.expert_bias"], loads)
-    out = torch.zeros_like(x)
+    chosen, gates = route(cfg, x, params["router.weight"], params.get("router.expert_bias"))
+    bias = params.get("router.expert_bias")
+    if bias is not None:
+        update_expert_bias(cfg, bias, torch.bincount(chosen.flatten(), minlength=cfg.num_experts).to(cfg.dtype))
+    mixed = torch.zeros_like(x)
     for e in range(cfg.num_experts):
-        rows, slot = (topi == e).nonzero(as_tuple=True)
-        if rows.numel():
-            y = expert_ffn(x[rows], params[f"experts.{e}.fc1.weight"], params[f"experts.{e}.fc2.weight"])
-            out = out.index_add(0, rows, gates[rows, slot].unsqueeze(1) * y)
-    return x + out
+        tok, slot = torch.nonzero(chosen == e, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        y = expert_ffn(x[tok], params[_expert_key(e, "fc1.weight")], params[_expert_key(e, "fc2.weight")])
+        mixed = mixed.index_add(0, tok, gates[tok, slot, None] * y)
+    return x + mixed
 
 
 def reference_train(cfg: MoEConfig, iterations: int, lr: float = 1e-2):
+    """Single-process ground truth: losses per iteration and the final parameters and buffers."""
     from .optim import Adam
 
     specs = moe_specs(cfg)
     params = {k: torch.nn.Parameter(init_param(cfg, s)) for k, s in specs.items() if s.trainable}
     buffers = {k: init_param(cfg, s) for k, s in specs.items() if not s.trainable}
     opt = Adam(params, lr=lr)
-    losses = []
+    history = []
     for it in range(iterations):
         opt.zero_grad()
         x, y = batch(cfg, it)
-        loss = token_loss(reference_forward(cfg, {**params, **buffers}, x), y)
+        loss = token_loss(reference_forward(cfg, params | buffers, x), y)
         (loss / cfg.tokens).backward()
         opt.step()
-        losses.append(loss.item() / cfg.tokens)
-    state = {k: v.detach().clone() for k, v in params.items()}
-    state.update({k: v.clone() for k, v in buffers.items()})
-    return losses, state
+        history.append(loss.item() / cfg.tokens)
+    final = {k: v.detach().clone() for k, v in params.items()} | {k: v.clone() for k, v in buffers.items()}
+    return history, final
 
 
 def moe_holdings(placement: ExpertPlacement, specs: dict[str, TensorSpec]) -> Holdings:
-    devices = sorted(d for g in placement.groups for d in g)
-    return {key: [(d, FULL) for d in (devices if expert_of(key) is None else placement.holders(expert_of(key)))]
-            for key in specs}
+    """Dense keys on every device, an expert's keys on its holders."""
+    everyone = sorted(d for g in placement.groups for d in g)
+
+    def holders(key: str) -> list[str]:
+        e = expert_of(key)
+        return everyone if e is None else placement.holders(e)
+
+    return {key: [(d, FULL) for d in holders(key)] for key in specs}
 
 
 def edp_group_name(holders: tuple[str, ...]) -> str:
@@ -137,23 +156,25 @@ def edp_group_name(holders: tuple[str, ...]) -> str:
 
 
 def moe_group_specs(placement: ExpertPlacement, world: list[str]):
+    """``dp`` over everyone, ``ep/<i>`` per EP group, ``edp/<holders>`` per replicated expert set."""
     from ..comm.group_spec import GroupSpec
 
-    rank = {d: i for i, d in enumerate(world)}
+    rank_of = {d: r for r, d in enumerate(world)}
+
+    def ranks(devices) -> tuple[int, ...]:
+        return tuple(sorted(rank_of[d] for d in devices))
+
     specs = [GroupSpec("dp", tuple(range(len(world))), kind="dp")]
-    for i, g in enumerate(placement.groups):
-        specs.append(GroupSpec(f"ep/{i}", tuple(sorted(rank[d] for d in g)), kind="ep"))
-    for holders in expert_dp_groups(placement):
-        if len(holders) > 1:
-            specs.append(GroupSpec(edp_group_name(holders), tuple(sorted(rank[d] for d in holders)), kind="edp"))
+    specs += [GroupSpec(f"ep/{i}", ranks(g), kind="ep") for i, g in enumerate(placement.groups)]
+    specs += [GroupSpec(edp_group_name(h), ranks(h), kind="edp") for h in expert_dp_groups(placement) if len(h) > 1]
     return specs
 
 
-def _all_to_all(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group, wait) -> torch.Tensor:
+def _exchange(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group, wait) -> torch.Tensor:
+    """``all_to_all_single`` (a plain copy without a group)."""
     if group is None:
-        out.copy_(inp)
-    else:
-        wait(dist.all_to_all_single(out, inp.contiguous(), out_splits, in_splits, group=group, async_op=True))
+        return out.copy_(inp)
+    wait(dist.all_to_all_single(out, inp.contiguous(), out_splits, in_splits, group=group, async_op=True))
     return out
 
 
@@ -163,18 +184,17 @@ class _AllToAll(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, out_splits, in_splits, group, wait):
         ctx.meta = (out_splits, in_splits, group, wait)
-        out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
-        return _all_to_all(out, x, out_splits, in_splits, group, wait)
+        return _exchange(x.new_empty((sum(out_splits), *x.shape[1:])), x, out_splits, in_splits, group, wait)
 
     @staticmethod
     def backward(ctx, g):
         out_splits, in_splits, group, wait = ctx.meta
-        grad = g.new_empty((sum(in_splits),) + tuple(g.shape[1:]))
-        return _all_to_all(grad, g, in_splits, out_splits, group, wait), None, None, None, None
+        back = _exchange(g.new_empty((sum(in_splits), *g.shape[1:])), g, in_splits, out_splits, group, wait)
+        return back, None, None, None, None
 
 
 class EPRuntime:
-    """One MoE block on one device: the replicated router plus the expert copies placed here."""
+    """One MoE block on one device: the replicated router and the expert copies placed here."""
 
     def __init__(self, cfg: MoEConfig, placement: ExpertPlacement, me: str, world: list[str], comms, mgr,
                  params: dict[str, torch.Tensor], speeds: dict[str, float] | None = None, timeout: float = 60.0,
@@ -182,61 +202,67 @@ class EPRuntime:
         self.cfg, self.placement, self.me, self.world = cfg, placement, me, list(world)
         self.comms, self.mgr, self.timeout = comms, mgr, timeout
         self.speeds = speeds or {}
+        self.params, self.buffers = params, buffers or {}
         self.gidx = placement.group_of(me)
         self.ep = sorted(placement.groups[self.gidx], key=self.world.index)
-        self.params = params
-        self.buffers = buffers or {}
         self.local_experts = placement.slots[me]
-        self.wait = lambda w: mgr.guarded_wait(w, timeout=timeout, what="moe")
         self.tokens_per_expert = None
+
+    def wait(self, work) -> None:
+        self.mgr.guarded_wait(work, timeout=self.timeout, what="moe")
 
     def token_range(self) -> tuple[int, int]:
         return even_split(self.cfg.tokens, len(self.world))[self.world.index(self.me)]
 
+    def _destinations(self, chosen: torch.Tensor) -> torch.Tensor:
+        """EP-group index of the holder each (token, slot) pair goes to (smooth weighted round
+        robin over an expert's holders, pairs in token-major order)."""
+        dest = torch.empty_like(chosen)
+        where = {d: i for i, d in enumerate(self.ep)}
+        for e in range(self.cfg.num_experts):
+            tok, slot = torch.nonzero(chosen == e, as_tuple=True)
+            if tok.numel():
+                picks = smooth_weighted_round_robin(self.placement.group_holders(self.gidx, e), self.speeds, tok.numel())
+                dest[tok, slot] = torch.tensor([where[p] for p in picks], dtype=dest.dtype)
+        return dest
+
+    def _pack(self, chosen: torch.Tensor, dest: torch.Tensor):
+        """Send order (destination, expert, token, slot) and the ``[ep, experts]`` counts."""
+        T, K = chosen.shape
+        E = self.cfg.num_experts
+        flat = torch.arange(T * K)
+        key = (dest.flatten() * E + chosen.flatten()) * (T * K) + flat
+        order = key.argsort()
+        counts = torch.bincount(dest.flatten() * E + chosen.flatten(), minlength=len(self.ep) * E)
+        return order // K, order % K, counts.view(len(self.ep), E)
+
+    def _run_experts(self, recv: torch.Tensor, recv_counts: torch.Tensor) -> torch.Tensor:
+        outputs, at = [], 0
+        for src, e in ((s, e) for s in range(len(self.ep)) for e in range(self.cfg.num_experts)):
+            n = int(recv_counts[src, e])
+            if n == 0:
+                continue
+            if e not in self.local_experts:
+                raise RuntimeError(f"{self.me} received tokens for expert {e} it does not host")
+            w1, w2 = (self.params[_expert_key(e, m)] for m in _EXPERT_MATS)
+            outputs.append(expert_ffn(recv[at:at + n], w1, w2))
+            at += n
+        return torch.cat(outputs) if outputs else recv.new_zeros((0, self.cfg.hidden))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        cfg, E = self.cfg, self.cfg.num_experts
-        topi, gates = route(cfg, x, self.params["router.weight"], self.buffers.get("router.expert_bias"))
-        self.tokens_per_expert = torch.bincount(topi.reshape(-1), minlength=E).to(torch.float64)
-        # choose a replica for every (token, slot) pair
-        dest: dict[tuple[int, int], str] = {}
-        for e in range(E):
-            pairs = [tuple(p) for p in (topi == e).nonzero().tolist()]
-            if pairs:
-                picks = smooth_weighted_round_robin(self.placement.group_holders(self.gidx, e), self.speeds,
-                                                    len(pairs))
-                dest.update(zip(pairs, picks))
-        # send buffer ordered by (destination, expert, token)
-        order: list[tuple[int, int]] = []
-        counts = torch.zeros(len(self.ep), E, dtype=torch.int64)
-        for di, d in enumerate(self.ep):
-            for e in range(E):
-                rows = sorted(p for p, h in dest.items() if h == d and int(topi[p]) == e)
-                order += rows
-                counts[di, e] = len(rows)
-        rows_i = torch.tensor([i for i, _ in order], dtype=torch.long)
-        slot_j = torch.tensor([j for _, j in order], dtype=torch.long)
+        cfg = self.cfg
+        chosen, gates = route(cfg, x, self.params["router.weight"], self.buffers.get("router.expert_bias"))
+        self.tokens_per_expert = torch.bincount(chosen.flatten(), minlength=cfg.num_experts).to(torch.float64)
+        tok, slot, counts = self._pack(chosen, self._destinations(chosen))
         group = self.comms.group(f"ep/{self.gidx}")
-        recv_counts = _all_to_all(torch.empty_like(counts), counts, None, None, group, self.wait)
-        in_splits, out_splits = counts.sum(1).tolist(), recv_counts.sum(1).tolist()
-        recv = _AllToAll.apply(x.index_select(0, rows_i), out_splits, in_splits, group, self.wait)
-        outs, off = [], 0
-        for src in range(len(self.ep)):
-            for e in range(E):
-                c = int(recv_counts[src, e])
-                if not c:
-                    continue
-                if e not in self.local_experts:
-                    raise RuntimeError(f"{self.me} received tokens for expert {e} it does not host")
-                outs.append(expert_ffn(recv[off:off + c], self.params[f"experts.{e}.fc1.weight"],
-                                       self.params[f"experts.{e}.fc2.weight"]))
-                off += c
-        y = torch.cat(outs) if outs else recv.new_zeros((0, cfg.hidden))
-        back = _AllToAll.apply(y, in_splits, out_splits, group, self.wait)
-        combined = torch.zeros_like(x).index_add(0, rows_i, gates[rows_i, slot_j].unsqueeze(1) * back)
-        return x + combined
+        recv_counts = _exchange(torch.empty_like(counts), counts, None, None, group, self.wait)
+        sent, got = counts.sum(1).tolist(), recv_counts.sum(1).tolist()
+        recv = _AllToAll.apply(x.index_select(0, tok), got, sent, group, self.wait)
+        back = _AllToAll.apply(self._run_experts(recv, recv_counts), sent, got, group, self.wait)
+        return x + torch.zeros_like(x).index_add(0, tok, gates[tok, slot, None] * back)
 
     def global_loads(self) -> list[float]:
-        """Tokens routed to each expert in the last forward, summed over all data-parallel ranks."""
+        """Tokens routed to each expert in the last forward, summed over the data-parallel ranks."""
         loads = self.tokens_per_expert.clone()
         group = self.comms.group("dp")
         if group is not None:
@@ -248,31 +274,26 @@ class EPRuntime:
         if bias is not None:
             update_expert_bias(self.cfg, bias, torch.tensor(self.global_loads(), dtype=bias.dtype))
 
+    def _reduce(self, group_name: str, keys: list[str]) -> None:
+        group = self.comms.group(group_name)
+        if group is None:
+            return
+        grads = [self.params[k].grad if self.params[k].grad is not None else torch.zeros_like(self.params[k])
+                 for k in keys]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        self.wait(dist.all_reduce(flat, group=group, async_op=True))
+        for k, piece in zip(keys, flat.split([self.params[k].numel() for k in keys])):
+            self.params[k].grad = piece.view_as(self.params[k]).clone()
+
     def sync_grads(self) -> None:
-        def flat(keys):
-            return torch.cat([(self.params[k].grad if self.params[k].grad is not None
-                               else torch.zeros_like(self.params[k])).reshape(-1) for k in keys])
-
-        def unflat(buf, keys):
-            off = 0
-            for k in keys:
-                p = self.params[k]
-                p.grad = buf[off:off + p.numel()].view_as(p).clone()
-                off += p.numel()
-
-        jobs = [("dp", ["router.weight"])]
+        """Router gradient over all ranks; every replicated expert's over its holders."""
+        self._reduce("dp", ["router.weight"])
         for holders, experts in sorted(expert_dp_groups(self.placement).items()):
             if self.me in holders and len(holders) > 1:
-                jobs.append((edp_group_name(holders),
-                             [f"experts.{e}.{n}" for e in experts for n in ("fc1.weight", "fc2.weight")]))
-        for name, keys in jobs:
-            group = self.comms.group(name)
-            if group is None:
-                continue
-            buf = flat(keys)
-            self.wait(dist.all_reduce(buf, group=group, async_op=True))
-            unflat(buf, keys)
+                self._reduce(edp_group_name(holders), [_expert_key(e, m) for e in experts for m in _EXPERT_MATS])
 
 
 def local_keys(placement: ExpertPlacement, me: str, specs: dict[str, TensorSpec]) -> list[str]:
-    return [k for k in specs if expert_of(k) is None or expert_of(k) in placement.slots[me]]
+    """The keys ``me`` holds: every dense key and its experts' keys."""
+    hosted = set(placement.slots[me])
+    return [k for k in specs if expert_of(k) is None or expert_of(k) in hosted]
