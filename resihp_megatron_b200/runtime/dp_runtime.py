@@ -1,13 +1,16 @@
-"""Replica-level data-parallel runtime (every worker holds the whole model).
+"""Replica-level data-parallel runtime: every worker holds the whole model.
 
-Each worker runs its assigned micro-batches and keeps a *sum* of gradients; one flat
-all-reduce covers gradients plus the loss scalar, then gradients are divided by the global
-token count.  ``canonical=True`` makes the result independent of the DP layout: every worker
-keeps one gradient vector per micro-batch, the per-micro-batch vectors are all-gathered and
-summed in global micro-batch order on every rank -- exactly the order single-process training
-accumulates them -- so the loss trajectory is bit-identical before and after a
-reconfiguration.  ``sync_full_state`` copies model + optimizer state from a source worker to a
-lagging or new one.  (Reference: ``resihp/runtime/dp_runtime.py:14-85``.)
+A worker runs the micro-batches assigned to it and keeps a *sum* of gradients; one flat
+all-reduce carries the gradients and the loss, after which the gradients are divided by the
+global token count.  ``canonical=True`` makes the result independent of the DP layout: each
+worker keeps one gradient vector per micro-batch, the zero-padded ``[micro-batches, numel]``
+table is summed over the workers (every row has exactly one non-zero contributor, so the sum is
+exact), and every rank adds the rows in global micro-batch order -- the order single-process
+training accumulates them -- so the loss trajectory stays bit-identical across
+reconfigurations.  ``sync_full_state`` copies model and optimizer state from a source worker to
+a lagging or new one.
+Parity: ``resihp/runtime/dp_runtime.py:14-85`` (same iteration contract and state sync; the
+canonical micro-batch-order reduction is ours).
 """
 
 from __future__ import annotations
@@ -20,87 +23,84 @@ from ..state.rng_data import IndexAddressableSampler
 from .optim import Adam
 
 
+def _flat_grads(params, extra: torch.Tensor) -> torch.Tensor:
+    parts = [(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in params]
+    return torch.cat(parts + [extra.reshape(-1)])
+
+
 class DataParallelRuntime:
     def __init__(self, cfg, sampler: IndexAddressableSampler, model, comms: GenerationComms,
                  mgr: ResilientCommManager, assignment: list[int], *, hook=None, progress=None,
                  timeout: float = 120.0, canonical: bool = False, num_microbatches: int | None = None,
                  batch_fn=None, loss_fn=None, tokens_fn=None):
-        self.cfg = cfg
-        self.sampler = sampler
-        self.model = model
-        self.comms = comms
-        self.mgr = mgr
+        self.cfg, self.sampler, self.model, self.comms, self.mgr = cfg, sampler, model, comms, mgr
         self.assignment = assignment
         self.hook = hook or (lambda it, phase: None)
         self.progress = progress or (lambda **kw: None)
-        self.timeout = timeout
-        self.canonical = canonical
+        self.timeout, self.canonical = timeout, canonical
         self.num_microbatches = num_microbatches or sampler.num_microbatches
-        # model-specific pieces (defaults: the MLP reference model)
-        if batch_fn is None:
+        if batch_fn is None:  # the MLP reference model
             from .reference_model import global_tokens, microbatch, token_loss
 
-            batch_fn = lambda it, mb: microbatch(cfg, sampler, it, mb)  # noqa: E731
-            loss_fn = lambda model, m: token_loss(model(m.x), m.y, m.mask)  # noqa: E731
-            tokens_fn = lambda it: global_tokens(cfg, sampler, it)  # noqa: E731
+            def batch_fn(it, mb):
+                return microbatch(cfg, sampler, it, mb)
+
+            def loss_fn(model_, m):
+                return token_loss(model_(m.x), m.y, m.mask)
+
+            def tokens_fn(it):
+                return global_tokens(cfg, sampler, it)
         self.batch_fn, self.loss_fn, self.tokens_fn = batch_fn, loss_fn, tokens_fn
 
-    def _params(self):
-        return list(self.model.named_state().items())
+    def _all_reduce(self, t: torch.Tensor, what: str) -> None:
+        self.mgr.guarded_wait(dist.all_reduce(t, async_op=True), timeout=self.timeout, what=what)
 
     def run_iteration(self, iteration: int) -> float:
-        params = self._params()
-        dtype = params[0][1].dtype
-        for _, p in params:
+        params = [p for _, p in self.model.named_state().items()]
+        dtype = params[0].dtype
+        for p in params:
             p.grad = None
-        per_mb: dict[int, torch.Tensor] = {}
-        local = 0.0
+        rows: dict[int, torch.Tensor] = {}
+        loss_sum = 0.0
         for mb in self.assignment:
             self.hook(iteration, "forward")
             self.progress(iteration=iteration, phase=f"mb{mb}", in_collective=False)
             loss = self.loss_fn(self.model, self.batch_fn(iteration, mb))
             if self.canonical:
-                grads = torch.autograd.grad(loss, [p for _, p in params], allow_unused=True)
-                per_mb[mb] = torch.cat([(g if g is not None else torch.zeros_like(p)).reshape(-1)
-                                        for g, (_, p) in zip(grads, params)] + [loss.detach().reshape(1)])
+                grads = torch.autograd.grad(loss, params, allow_unused=True)
+                rows[mb] = torch.cat([(g if g is not None else torch.zeros_like(p)).reshape(-1)
+                                      for g, p in zip(grads, params)] + [loss.detach().reshape(1)])
             else:
                 loss.backward()
-            local += loss.item()
+            loss_sum += loss.item()
         self.hook(iteration, "reduce")
-        total = self.tokens_fn(iteration)
+        tokens = self.tokens_fn(iteration)
         if self.canonical:
-            flat = self._canonical_reduce(per_mb, params, dtype)
+            flat = self._canonical_reduce(rows, params, dtype)
         else:
-            flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for _, p in params]
-                             + [torch.tensor([local], dtype=dtype)])
+            flat = _flat_grads(params, torch.tensor([loss_sum], dtype=dtype))
             if self.comms.world_size > 1:
                 self.progress(iteration=iteration, phase="grad_allreduce", in_collective=True)
-                self.mgr.guarded_wait(dist.all_reduce(flat, async_op=True), timeout=self.timeout,
-                                      what="grad all-reduce")
-        off = 0
-        for _, p in params:
-            n = p.numel()
-            p.grad = (flat[off:off + n].view_as(p) / total).clone()
-            off += n
+                self._all_reduce(flat, "grad all-reduce")
+        sizes = [p.numel() for p in params]
+        for p, piece in zip(params, flat[:sum(sizes)].split(sizes)):
+            p.grad = (piece.view_as(p) / tokens).clone()
         self.hook(iteration, "step")
-        return flat[-1].item() / total
+        return flat[-1].item() / tokens
 
-    def _canonical_reduce(self, per_mb: dict[int, torch.Tensor], params, dtype) -> torch.Tensor:
-        """Sum per-micro-batch vectors in global micro-batch order (layout-invariant)."""
-        n = sum(p.numel() for _, p in params) + 1
-        M = self.num_microbatches
-        mine = torch.zeros(M, n, dtype=dtype)
-        for mb, v in per_mb.items():
-            mine[mb] = v
+    def _canonical_reduce(self, rows: dict[int, torch.Tensor], params, dtype) -> torch.Tensor:
+        """Per-micro-batch vectors summed in global micro-batch order (layout-invariant)."""
+        width = 1 + sum(p.numel() for p in params)
+        table = torch.zeros(self.num_microbatches, width, dtype=dtype)
+        for mb, row in rows.items():
+            table[mb] = row
         if self.comms.world_size > 1:
             self.progress(in_collective=True, phase="grad_gather")
-            # each micro-batch is computed by exactly one worker, so a SUM all-reduce of the
-            # zero-padded [M, n] table reproduces every row exactly (x + 0 is exact)
-            self.mgr.guarded_wait(dist.all_reduce(mine, async_op=True), timeout=self.timeout, what="grad gather")
-        acc = torch.zeros(n, dtype=dtype)
-        for mb in range(M):
-            acc = acc + mine[mb]
-        return acc
+            self._all_reduce(table, "grad gather")  # x + 0 is exact: every row is reproduced bit for bit
+        total = torch.zeros(width, dtype=dtype)
+        for row in table:
+            total = total + row
+        return total
 
 
 def full_state(opt: Adam, committed_iteration: int) -> tuple[dict[str, torch.Tensor], torch.Tensor]:
@@ -109,28 +109,25 @@ def full_state(opt: Adam, committed_iteration: int) -> tuple[dict[str, torch.Ten
 
 def sync_full_state(mgr: ResilientCommManager, comms: GenerationComms, my_id: str, sources: dict[str, str], opt: Adam,
                     committed_iteration: int, timeout: float = 120.0) -> int | None:
-    """Copy model + optimizer state to each receiver from its source; returns the adopted
-    iteration on receivers, ``None`` elsewhere."""
-    tensors, meta = full_state(opt, committed_iteration)
-    keys = sorted(tensors)
-    works = []
-    got = None
-    rmeta = torch.zeros(2, dtype=torch.int64)
-    rbuf: dict[str, torch.Tensor] = {}
+    """Copy model and optimizer state from each receiver's source to it; returns the adopted
+    iteration on receivers and None elsewhere.  Tag 0 carries (iteration, step count), tags 1..
+    the state tensors in name order."""
+    tensors, header = full_state(opt, committed_iteration)
+    names = sorted(tensors)
+    works, incoming, in_header = [], None, torch.zeros(2, dtype=torch.int64)
     for dst, src in sorted(sources.items()):
         if my_id == src:
-            peer = comms.rank_of(dst)
-            works.append(dist.isend(meta, peer, tag=0))
-            works.extend(dist.isend(tensors[k].contiguous(), peer, tag=i + 1) for i, k in enumerate(keys))
+            to = comms.rank_of(dst)
+            works.append(dist.isend(header, to, tag=0))
+            works += [dist.isend(tensors[n].contiguous(), to, tag=t) for t, n in enumerate(names, start=1)]
         if my_id == dst:
-            peer = comms.rank_of(src)
-            rbuf = {k: torch.empty_like(tensors[k]) for k in keys}
-            works.append(dist.irecv(rmeta, peer, tag=0))
-            works.extend(dist.irecv(rbuf[k], peer, tag=i + 1) for i, k in enumerate(keys))
-            got = True
-    for w in works:
-        mgr.guarded_wait(w, timeout=timeout, what="state sync")
-    if got:
-        opt.load_state_tensors(rbuf, int(rmeta[1].item()))
-        return int(rmeta[0].item())
-    return None
+            frm = comms.rank_of(src)
+            incoming = {n: torch.empty_like(tensors[n]) for n in names}
+            works.append(dist.irecv(in_header, frm, tag=0))
+            works += [dist.irecv(incoming[n], frm, tag=t) for t, n in enumerate(names, start=1)]
+    for work in works:
+        mgr.guarded_wait(work, timeout=timeout, what="state sync")
+    if incoming is None:
+        return None
+    opt.load_state_tensors(incoming, int(in_header[1].item()))
+    return int(in_header[0].item())
