@@ -1,27 +1,30 @@
 """ResilientCommManager: generation-scoped communicators that are rebuilt without hanging.
 
-Hang causes designed out:
-* dead ranks taking part in group creation -> survivors-only creation: NCCL ``shrink_group``
-  (with abort of whatever the dead ranks left in flight) when the new world is an
-  order-preserving subset of the old one and NCCL >= 2.27.3, else a fresh world on a
-  generation-scoped ``PrefixStore`` of the coordinator-hosted ``TCPStore``;
-* creation order depending on local state -> plan-derived canonical order: one ``split_group``
-  per layer of disjoint groups on NCCL, or ``new_group`` for every group on every rank in that
-  order on gloo;
-* a rendezvous store on a training rank -> the store lives on the coordinator;
-* blocking forever in a collective -> ``guarded_wait`` (abortable, deadline) and a validation
-  all-reduce of ones on every group under a deadline before the generation may report READY
-  (failure raises ``GenerationBuildError`` naming the suspect ranks).
+Each way a rebuild could hang is designed out:
 
-``abort()`` (called from the control-client thread) sets the abort flag, aborts every live NCCL
-group and sets the device abort word that the package's peer-memory kernels poll, so survivors
-leave in-flight fused kernels at once.  Gloo groups are aborted when their generation is torn
-down: a gloo op that lost its peer stays in flight until its timeout, and destroying its group
-would otherwise wait for it while the next generation's rendezvous runs out of time.  (Reference: ``resihp/comm/comm_manager.py:31-329``.)
+* **Dead ranks in group creation** -- only survivors create: NCCL ``shrink_group`` (aborting
+  what the dead ranks left in flight) when the new world keeps the old ranks' order and NCCL is
+  >= 2.27.3; otherwise a fresh world on the generation's ``PrefixStore`` of the coordinator's
+  ``TCPStore``.
+* **Creation order depending on local state** -- a plan-derived canonical order: one
+  ``split_group`` per layer of disjoint groups on NCCL, ``new_group`` for every group on every
+  rank (in the same order) on gloo.
+* **A rendezvous store on a training rank** -- the store lives on the coordinator.
+* **Blocking forever in a collective** -- ``guarded_wait`` (abortable, with a deadline), and a
+  validation all-reduce of ones on every group, under a deadline, before the generation may
+  report READY; a failure raises ``GenerationBuildError`` naming the suspect ranks.
+
+``abort()`` (called from the control-client thread) raises the abort flag, runs the abort hooks
+(the device abort word that this package's peer-memory kernels poll, so survivors leave fused
+kernels in flight at once) and aborts every live NCCL group.  Gloo groups are aborted when their
+generation is torn down: a gloo op that lost its peer stays in flight until its timeout, and
+destroying its group would wait for it while the next generation's rendezvous runs out of time.
+Parity: ``resihp/comm/comm_manager.py:31-329`` (same build paths, validation and abort semantics).
 """
 
 from __future__ import annotations
 
+import contextlib
 import datetime
 import threading
 import time
@@ -68,7 +71,7 @@ class GenerationComms:
         return len(self.world)
 
     def group(self, name: str):
-        """Process group for ``name``; ``None`` if this rank is not a member or it has one rank."""
+        """The process group of ``name``; None when this rank is not a member or it has one rank."""
         if name not in self.specs:
             raise KeyError(f"unknown group {name}")
         return self.groups.get(name)
@@ -84,11 +87,14 @@ class GenerationComms:
 
 
 def is_order_preserving_subset(new: list[str], old: tuple[str, ...]) -> bool:
-    pos = {w: i for i, w in enumerate(old)}
-    if any(w not in pos for w in new):
-        return False
-    idx = [pos[w] for w in new]
-    return idx == sorted(idx)
+    """Every member of ``new`` was in ``old``, in the same relative order."""
+    where = {w: i for i, w in enumerate(old)}
+    positions = [where.get(w) for w in new]
+    return None not in positions and positions == sorted(positions)
+
+
+def _nccl_at_least(version, wanted: tuple[int, ...]) -> bool:
+    return version is not None and tuple(version) >= wanted
 
 
 class ResilientCommManager:
@@ -99,252 +105,226 @@ class ResilientCommManager:
             raise ValueError(shrink)
         if subgroup_mode not in ("split", "local"):
             raise ValueError(subgroup_mode)
-        self.backend = backend
-        self.device = device
+        self.backend, self.device = backend, device
         self.timeout = datetime.timedelta(seconds=timeout_s)
-        self.validate_timeout_s = validate_timeout_s
-        self.validate = validate
-        self.shrink = shrink
-        self.subgroup_mode = subgroup_mode
-        self.nccl_nonblocking = nccl_nonblocking
+        self.validate_timeout_s, self.validate = validate_timeout_s, validate
+        self.shrink, self.subgroup_mode, self.nccl_nonblocking = shrink, subgroup_mode, nccl_nonblocking
         self.poll_interval_s = poll_interval_s or 0.0005
         self.current: GenerationComms | None = None
-        self._abort = threading.Event()
-        self._lock = threading.Lock()
-        self._live: list[Any] = []
-        self._store_client = None
-        self._store_addr: tuple[str, int] | None = None
+        self._aborted = threading.Event()
+        self._mu = threading.Lock()
+        self._groups_alive: list[Any] = []
+        self._store: tuple[tuple[str, int], Any] | None = None
         self._abort_hooks: list[Callable[[], None]] = []
 
     # ------------------------------------------------------------------ capabilities
     @staticmethod
     def capabilities() -> dict:
-        caps = {"shrink_group": hasattr(dist, "shrink_group"), "split_group": hasattr(dist, "split_group"),
-                "nccl": dist.is_nccl_available(), "gloo": dist.is_gloo_available(), "nccl_version": None}
-        if torch.cuda.is_available() and dist.is_nccl_available():
-            try:
+        caps = dict(shrink_group=hasattr(dist, "shrink_group"), split_group=hasattr(dist, "split_group"),
+                    nccl=dist.is_nccl_available(), gloo=dist.is_gloo_available(), nccl_version=None)
+        if dist.is_nccl_available() and torch.cuda.is_available():
+            with contextlib.suppress(Exception):
                 caps["nccl_version"] = torch.cuda.nccl.version()
-            except Exception:  # noqa: BLE001
-                pass
         return caps
 
     def can_shrink(self, new_world: list[str]) -> bool:
-        if self.shrink == "never" or self.current is None or self.backend != "nccl":
+        """Whether the transition to ``new_world`` can use NCCL's in-place shrink."""
+        if self.shrink == "never" or self.backend != "nccl" or self.current is None:
             return False
         caps = self.capabilities()
-        nccl_ok = caps["nccl_version"] is not None and tuple(caps["nccl_version"]) >= (2, 27, 3)
-        if not (caps["shrink_group"] and nccl_ok and hasattr(c10d, "SHRINK_ABORT")):
-            return False
-        return len(new_world) < self.current.world_size and is_order_preserving_subset(new_world,
-                                                                                       self.current.world)
+        supported = caps["shrink_group"] and hasattr(c10d, "SHRINK_ABORT") and _nccl_at_least(caps["nccl_version"],
+                                                                                              (2, 27, 3))
+        smaller = len(new_world) < self.current.world_size
+        return bool(supported and smaller and is_order_preserving_subset(new_world, self.current.world))
 
     def add_abort_hook(self, fn: Callable[[], None]) -> None:
-        """Extra action on abort (e.g. raising the device abort word of the symmetric heap)."""
+        """An extra action on abort (e.g. raising the symmetric heap's device abort word)."""
         self._abort_hooks.append(fn)
 
     # ------------------------------------------------------------------ building
     def store_for(self, store_addr: tuple[str, int], prefix: str):
-        if self._store_client is None or self._store_addr != tuple(store_addr):
-            self._store_client = dist.TCPStore(store_addr[0], int(store_addr[1]), is_master=False,
-                                               timeout=self.timeout, wait_for_workers=False)
-            self._store_addr = tuple(store_addr)
-        return dist.PrefixStore(prefix, self._store_client)
+        """The generation's view (``prefix``) of the coordinator's store; one client per address."""
+        addr = (store_addr[0], int(store_addr[1]))
+        if self._store is None or self._store[0] != addr:
+            client = dist.TCPStore(addr[0], addr[1], is_master=False, timeout=self.timeout, wait_for_workers=False)
+            self._store = (addr, client)
+        return dist.PrefixStore(prefix, self._store[1])
 
-    def build(self, generation: int, world: list[str], my_id: str, specs: list[GroupSpec], *, store=None,
-              store_addr: tuple[str, int] | None = None, store_prefix: str | None = None) -> GenerationComms:
-        t0 = time.monotonic()
-        self._abort.clear()
-        rank = world.index(my_id)
-        for s in specs:
-            if any(r >= len(world) for r in s.ranks):
-                raise ValueError(f"group {s.name} names a rank outside a world of {len(world)}")
-        path = "shrink" if self.can_shrink(world) else "fresh"
-        if self.shrink == "always" and path != "shrink":
-            raise RuntimeError("shrink requested but this transition cannot shrink")
-        if path == "shrink":
-            keep = set(world)
-            excluded = [i for i, w in enumerate(self.current.world) if w not in keep]
-            dist.shrink_group(excluded, group=None, shrink_flags=c10d.SHRINK_ABORT)
-        else:
-            if store is None:
-                if store_addr is None or store_prefix is None:
-                    raise ValueError("a fresh world needs a store (or store_addr + store_prefix)")
-                store = self.store_for(store_addr, store_prefix)
-            self._teardown()
-            self._init_world(rank, len(world), store)
-        with self._lock:
-            self._live = [c10d._get_default_group()]
-        groups = self._make_subgroups(rank, specs)
+    def _finish(self, generation: int, world: list[str], rank: int, specs: list[GroupSpec], path: str,
+                started: float) -> GenerationComms:
+        with self._mu:
+            self._groups_alive = [c10d._get_default_group()]
+        groups = self._subgroups(rank, specs)
         if self.validate:
             self._validate(len(world), groups, specs)
         comms = GenerationComms(generation, rank, tuple(world), {s.name: s for s in specs}, groups, path,
-                                time.monotonic() - t0)
+                                time.monotonic() - started)
         self.current = comms
         log.info("generation %d built (%s) in %.3fs with %d groups", generation, path, comms.build_seconds,
                  len(groups))
         return comms
 
-    def adopt(self, generation: int, world: list[str], my_id: str, specs: list[GroupSpec]) -> GenerationComms:
-        """Use the already initialised default process group (a launcher's environment, e.g.
-        ``torchrun``) as this generation's world and create the plan's subgroups on it."""
-        t0 = time.monotonic()
-        self._abort.clear()
+    def build(self, generation: int, world: list[str], my_id: str, specs: list[GroupSpec], *, store=None,
+              store_addr: tuple[str, int] | None = None, store_prefix: str | None = None) -> GenerationComms:
+        started = time.monotonic()
+        self._aborted.clear()
         rank = world.index(my_id)
-        if not dist.is_initialized() or dist.get_world_size() != len(world) or dist.get_rank() != rank:
+        outside = [s.name for s in specs if s.ranks and max(s.ranks) >= len(world)]
+        if outside:
+            raise ValueError(f"group {outside[0]} names a rank outside a world of {len(world)}")
+        if self.can_shrink(world):
+            dropped = [i for i, w in enumerate(self.current.world) if w not in set(world)]
+            dist.shrink_group(dropped, group=None, shrink_flags=c10d.SHRINK_ABORT)
+            return self._finish(generation, world, rank, specs, "shrink", started)
+        if self.shrink == "always":
+            raise RuntimeError("shrink requested but this transition cannot shrink")
+        if store is None:
+            if store_addr is None or store_prefix is None:
+                raise ValueError("a fresh world needs a store (or store_addr + store_prefix)")
+            store = self.store_for(store_addr, store_prefix)
+        self._teardown()
+        self._init_world(rank, len(world), store)
+        return self._finish(generation, world, rank, specs, "fresh", started)
+
+    def adopt(self, generation: int, world: list[str], my_id: str, specs: list[GroupSpec]) -> GenerationComms:
+        """Take the already initialised default process group (a launcher's, e.g. ``torchrun``) as
+        this generation's world and create the plan's subgroups on it."""
+        started = time.monotonic()
+        self._aborted.clear()
+        rank = world.index(my_id)
+        matches = dist.is_initialized() and dist.get_world_size() == len(world) and dist.get_rank() == rank
+        if not matches:
             raise RuntimeError("adopt() needs an initialised default group matching the world")
-        with self._lock:
-            self._live = [c10d._get_default_group()]
-        groups = self._make_subgroups(rank, specs)
-        if self.validate:
-            self._validate(len(world), groups, specs)
-        comms = GenerationComms(generation, rank, tuple(world), {s.name: s for s in specs}, groups, "adopted",
-                                time.monotonic() - t0)
-        self.current = comms
-        return comms
+        return self._finish(generation, world, rank, specs, "adopted", started)
 
     def _init_world(self, rank: int, world_size: int, store) -> None:
-        kw: dict = {"backend": self.backend, "store": store, "rank": rank, "world_size": world_size,
-                    "timeout": self.timeout}
+        options: dict = dict(backend=self.backend, store=store, rank=rank, world_size=world_size, timeout=self.timeout)
         if self.backend == "nccl":
             if self.device is not None:
-                kw["device_id"] = torch.device(self.device)
+                options["device_id"] = torch.device(self.device)
             if self.nccl_nonblocking:
-                opts = dist.ProcessGroupNCCL.Options()
-                opts.config.blocking = 0
-                kw["pg_options"] = opts
-        dist.init_process_group(**kw)
+                nccl_opts = dist.ProcessGroupNCCL.Options()
+                nccl_opts.config.blocking = 0
+                options["pg_options"] = nccl_opts
+        dist.init_process_group(**options)
 
-    def _make_subgroups(self, rank: int, specs: list[GroupSpec]) -> dict[str, Any]:
-        by_ranks: dict[tuple[int, ...], Any] = {}
-        # split_group needs a device bound to the default group (NCCL with device_id); gloo
-        # worlds use canonical-order new_group instead
-        use_split = self.subgroup_mode == "split" and self.backend == "nccl" and self.device is not None
-        if use_split:
+    def _subgroups(self, rank: int, specs: list[GroupSpec]) -> dict[str, Any]:
+        """Create the plan's groups in canonical order; name -> group for the groups this rank is in."""
+        mine: dict[tuple[int, ...], Any] = {}
+        # split_group needs a device bound to the default group (NCCL with device_id); gloo uses new_group
+        if self.subgroup_mode == "split" and self.backend == "nccl" and self.device is not None:
             for layer in split_layers(specs):
-                self._check_abort()
+                self._raise_if_aborted()
                 pg = dist.split_group(split_ranks=[list(s.ranks) for s in layer], timeout=self.timeout,
                                       group_desc=f"resihp:{layer[0].kind}:{len(layer)}")
-                for s in layer:
-                    if rank in s.ranks:
-                        by_ranks[s.ranks] = pg
+                mine.update((s.ranks, pg) for s in layer if rank in s.ranks)
         else:
-            # every rank creates every group in the same canonical order (non-members too), so
-            # c10d derives identical group names everywhere and creation cannot deadlock
-            made: set[tuple[int, ...]] = set()
-            for s in canonical_order(specs):
-                if not s.materialized or s.ranks in made:
-                    continue
-                made.add(s.ranks)
-                self._check_abort()
-                pg = dist.new_group(list(s.ranks), timeout=self.timeout, group_desc=f"resihp:{s.name}")
-                if rank in s.ranks:
-                    by_ranks[s.ranks] = pg
-        groups = {s.name: (by_ranks.get(s.ranks) if rank in s.ranks and s.materialized else None) for s in specs}
-        with self._lock:
-            self._live.extend(pg for pg in by_ranks.values() if pg not in self._live)
-        return groups
+            # every rank (member or not) creates every group in the same order, so c10d derives the
+            # same group names everywhere and creation cannot deadlock
+            for ranks in dict.fromkeys(s.ranks for s in canonical_order(specs) if s.materialized):
+                self._raise_if_aborted()
+                pg = dist.new_group(list(ranks), timeout=self.timeout, group_desc=f"resihp:{ranks}")
+                if rank in ranks:
+                    mine[ranks] = pg
+        with self._mu:
+            self._groups_alive += [pg for pg in mine.values() if pg not in self._groups_alive]
+        return {s.name: mine.get(s.ranks) if (s.materialized and rank in s.ranks) else None for s in specs}
 
     def _validate(self, world_size: int, groups: dict[str, Any], specs: list[GroupSpec]) -> None:
-        dev = torch.device(self.device) if (self.backend == "nccl" and self.device) else torch.device("cpu")
-        seen: set[int] = set()
-        targets = [(c10d._get_default_group(), tuple(range(world_size)), "world")]
-        targets += [(groups[s.name], s.ranks, s.name) for s in canonical_order(specs) if groups.get(s.name) is not None]
-        for pg, ranks, name in targets:
-            if id(pg) in seen:
+        """An all-reduce of ones under a deadline on the world and on every group of this rank."""
+        on_gpu = self.backend == "nccl" and self.device
+        device = torch.device(self.device) if on_gpu else torch.device("cpu")
+        checks = [("world", c10d._get_default_group(), tuple(range(world_size)))]
+        checks += [(s.name, groups[s.name], s.ranks) for s in canonical_order(specs) if groups.get(s.name) is not None]
+        done: set[int] = set()
+        for name, pg, ranks in checks:
+            if id(pg) in done:
                 continue
-            seen.add(id(pg))
-            t = torch.ones(1, device=dev)
+            done.add(id(pg))
+            ones = torch.ones(1, device=device)
             try:
-                self.guarded_wait(dist.all_reduce(t, group=pg, async_op=True), timeout=self.validate_timeout_s,
+                self.guarded_wait(dist.all_reduce(ones, group=pg, async_op=True), timeout=self.validate_timeout_s,
                                   what=f"validate {name}")
             except CommAborted:
                 raise
-            except (CommTimeout, RuntimeError) as e:
-                raise GenerationBuildError(f"group {name} failed validation: {e}", suspects=tuple(ranks)) from e
-            if int(t.item()) != pg.size():
-                raise GenerationBuildError(f"group {name}: validation sum {t.item()} != {pg.size()}", tuple(ranks))
+            except (CommTimeout, RuntimeError) as err:
+                raise GenerationBuildError(f"group {name} failed validation: {err}", suspects=tuple(ranks)) from err
+            if int(ones.item()) != pg.size():
+                raise GenerationBuildError(f"group {name}: validation sum {ones.item()} != {pg.size()}", tuple(ranks))
 
     # ------------------------------------------------------------------ waiting / aborting
-    def _check_abort(self) -> None:
-        if self._abort.is_set():
+    def _raise_if_aborted(self) -> None:
+        if self._aborted.is_set():
             raise CommAborted("communicators aborted by the control plane")
 
     def guarded_wait(self, work, timeout: float | None = None, what: str = "collective") -> None:
-        """Wait for ``work`` while honouring aborts and a deadline.  Gloo cannot interrupt an
-        in-flight op, so its blocking wait runs on a helper thread while this thread polls; on
-        NCCL ``wait()`` only orders streams and hangs are broken by ``abort()``."""
+        """Wait for ``work`` honouring aborts and a deadline.  On NCCL ``wait()`` only orders
+        streams and a hang is broken by ``abort()``; gloo cannot interrupt an op in flight, so its
+        blocking wait runs on a helper thread while this thread polls."""
         if self.backend == "nccl":
-            self._check_abort()
+            self._raise_if_aborted()
             work.wait()
             return
         if work.is_completed():
             work.wait()
             return
-        done = threading.Event()
-        failure: list[BaseException] = []
+        finished = threading.Event()
+        errors: list[BaseException] = []
 
-        def waiter() -> None:
+        def block() -> None:
             try:
                 work.wait()
-            except BaseException as e:  # noqa: BLE001 - re-raised on the caller's thread
-                failure.append(e)
+            except BaseException as err:  # noqa: BLE001 -- handed to the caller's thread
+                errors.append(err)
             finally:
-                done.set()
+                finished.set()
 
-        threading.Thread(target=waiter, name="guarded-wait", daemon=True).start()
-        deadline = None if timeout is None else time.monotonic() + timeout
-        while not done.wait(self.poll_interval_s):
-            if self._abort.is_set():
+        threading.Thread(target=block, name="guarded-wait", daemon=True).start()
+        give_up = None if timeout is None else time.monotonic() + timeout
+        while not finished.wait(self.poll_interval_s):
+            if self._aborted.is_set():
                 raise CommAborted(f"{what} aborted by the control plane")
-            if deadline is not None and time.monotonic() > deadline:
+            if give_up is not None and time.monotonic() > give_up:
                 raise CommTimeout(f"{what} timed out after {timeout}s")
-        if failure:
-            raise failure[0]
+        if errors:
+            raise errors[0]
 
     def abort(self) -> None:
-        """Thread safe; called from the control-client thread on RECONFIG_NOTICE."""
-        self._abort.set()
-        for fn in self._abort_hooks:
+        """Thread safe; the control client calls it on RECONFIG_NOTICE."""
+        self._aborted.set()
+        for hook in self._abort_hooks:
             try:
-                fn()
-            except Exception:  # noqa: BLE001 - best effort
+                hook()
+            except Exception:  # noqa: BLE001 -- best effort
                 log.exception("abort hook raised")
-        if self.backend != "nccl":
-            return
-        with self._lock:
-            live = list(self._live)
-        for pg in live:
-            try:
-                pg.abort()
-            except Exception:  # noqa: BLE001 - the NCCL watchdog is the backstop
-                pass
+        if self.backend == "nccl":
+            with self._mu:
+                groups = list(self._groups_alive)
+            for pg in groups:
+                with contextlib.suppress(Exception):  # the NCCL watchdog is the backstop
+                    pg.abort()
 
     @property
     def aborted(self) -> bool:
-        return self._abort.is_set()
+        return self._aborted.is_set()
 
     def _teardown(self) -> None:
-        if not dist.is_initialized():
-            self.current = None
-            return
-        try:
-            if self.backend == "nccl":
-                c10d._abort_process_group(None)
-            else:
-                # a gloo op that lost its peer stays in flight until its timeout, and destroying
-                # its group would wait for it: abort the groups first (returns at once)
-                with self._lock:
-                    live = list(self._live)
-                for pg in live:
-                    try:
-                        pg.abort()
-                    except Exception:  # noqa: BLE001 - older gloo builds: fall back to the wait
-                        pass
-                dist.destroy_process_group()
-        except Exception:  # noqa: BLE001
-            log.exception("teardown of the previous generation failed; continuing")
-        with self._lock:
-            self._live = []
+        if dist.is_initialized():
+            try:
+                if self.backend == "nccl":
+                    c10d._abort_process_group(None)
+                else:
+                    # abort first: a gloo op that lost its peer would make the destroy wait
+                    with self._mu:
+                        groups = list(self._groups_alive)
+                    for pg in groups:
+                        with contextlib.suppress(Exception):  # older gloo builds: fall back to the wait
+                            pg.abort()
+                    dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                log.exception("teardown of the previous generation failed; continuing")
+        with self._mu:
+            self._groups_alive = []
         self.current = None
 
     def destroy(self) -> None:
