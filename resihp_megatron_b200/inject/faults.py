@@ -1,20 +1,22 @@
 """Fault injection.
 
-* ``FaultInjector`` runs inside a worker and fires at deterministic hook points
-  ``(iteration >= iter, phase)`` with phases ``forward``, ``backward``, ``reduce``, ``step``,
-  ``loss``: SIGKILL itself, SIGSTOP itself (optionally resumed by a SIGCONT timer), pad compute by
-  busy-waiting (fail-slow), or delay a link.  All of it happens on the host: a killed or stopped
-  process leaves between kernel launches, never in the middle of a GPU operation.
+* ``FaultInjector`` lives inside a worker and fires at deterministic hook points
+  ``(iteration >= iter, phase)`` -- phases ``forward``, ``backward``, ``reduce``, ``step``,
+  ``loss`` -- or after a wall-clock offset: SIGKILL itself, SIGSTOP itself (optionally resumed by
+  a SIGCONT timer), pad its compute by busy waiting (fail-slow) or delay a link.  All of it happens
+  on the host: a killed or stopped process leaves between kernel launches, never inside a GPU
+  operation.
 * ``ExternalInjector`` builds (and, when allowed, runs) host commands that emulate hardware
-  faults on a cluster: kill / stop, NIC down, bandwidth contention, and -- only with
+  faults on a cluster: kill / stop, NIC down, bandwidth contention and -- only with
   ``allow_device_settings=True`` -- SM clock locks, power caps and DCGM XID injection.  It is a
-  dry run by default; on shared GPUs the device-setting faults stay dry-run only.
+  dry run by default; on shared GPUs the device-setting faults stay dry runs.
 
-Spec grammar (``RESIHP_FAULTS`` or ``parse_faults``), same as the reference
-(``resihp/inject/faults.py:35-287``)::
+Spec grammar (``RESIHP_FAULTS`` or ``parse_faults``), kept from the reference
+(``resihp/inject/faults.py:35-287``) because users write it::
 
-    kind@key=value:key=value;kind@...      e.g.  kill@iter=5:target=n0g1;slow@iter=10:target=n1g0:factor=2
-Reserved keys: target, iter, time, duration, factor, phase; the rest go to ``params``.
+    kind@key=value:key=value;kind@...     e.g.  kill@iter=5:target=n0g1;slow@iter=10:target=n1g0:factor=2
+
+Reserved keys: target, iter, time, duration, factor, phase; any other key goes to ``params``.
 """
 
 from __future__ import annotations
@@ -45,6 +47,10 @@ class FaultKind(str, Enum):
 
 DEVICE_SETTING_KINDS = frozenset({FaultKind.XID, FaultKind.POWER_CAP})
 
+# reserved key -> (FaultSpec field, parser); the field order is the order ``to_spec`` writes
+_FIELDS = {"target": ("target", str), "iter": ("at_iteration", int), "time": ("at_time", float),
+           "duration": ("duration", float), "factor": ("factor", float), "phase": ("phase", str)}
+
 
 @dataclass(frozen=True)
 class FaultSpec:
@@ -61,92 +67,86 @@ class FaultSpec:
         return dict(self.params).get(key, default)
 
     def to_spec(self) -> str:
-        kv = [f"target={self.target}"]
-        if self.at_iteration is not None:
-            kv.append(f"iter={self.at_iteration}")
-        if self.at_time is not None:
-            kv.append(f"time={self.at_time}")
-        if self.duration is not None:
-            kv.append(f"duration={self.duration}")
-        if self.factor != 1.0:
-            kv.append(f"factor={self.factor}")
-        if self.phase != "forward":
-            kv.append(f"phase={self.phase}")
-        kv += [f"{k}={v}" for k, v in self.params]
-        return f"{self.kind.value}@" + ":".join(kv)
+        """The grammar form; fields at their defaults are left out."""
+        defaults = {"at_iteration": None, "at_time": None, "duration": None, "factor": 1.0, "phase": "forward"}
+        pairs = []
+        for key, (attr, _) in _FIELDS.items():
+            value = getattr(self, attr)
+            if attr == "target" or value != defaults[attr]:
+                pairs.append(f"{key}={value}")
+        pairs += [f"{k}={v}" for k, v in self.params]
+        return f"{self.kind.value}@{':'.join(pairs)}"
 
 
-_RESERVED = {"target", "iter", "time", "duration", "factor", "phase"}
+def _parse_one(item: str) -> FaultSpec:
+    kind, at, body = item.partition("@")
+    if not at:
+        raise ValueError(f"fault {item!r} must look like kind@key=value:...")
+    values: dict[str, str] = {}
+    for token in filter(None, body.split(":")):
+        key, eq, value = token.partition("=")
+        if not eq:
+            raise ValueError(f"bad token {token!r} in fault {item!r}")
+        values[key.strip()] = value.strip()
+    if "target" not in values:
+        raise ValueError(f"fault {item!r} has no target")
+    fields = {attr: cast(values[key]) for key, (attr, cast) in _FIELDS.items() if key in values}
+    extra = tuple(sorted((k, v) for k, v in values.items() if k not in _FIELDS))
+    return FaultSpec(kind=FaultKind(kind.strip()), params=extra, **fields)
 
 
 def parse_faults(spec: str | None) -> list[FaultSpec]:
-    if not spec:
-        return []
-    out = []
-    for item in (s.strip() for s in spec.split(";")):
-        if not item:
-            continue
-        kind, sep, rest = item.partition("@")
-        if not sep:
-            raise ValueError(f"fault {item!r} must look like kind@key=value:...")
-        kv: dict[str, str] = {}
-        for tok in rest.split(":"):
-            if not tok:
-                continue
-            k, eq, v = tok.partition("=")
-            if not eq:
-                raise ValueError(f"bad token {tok!r} in fault {item!r}")
-            kv[k.strip()] = v.strip()
-        if "target" not in kv:
-            raise ValueError(f"fault {item!r} has no target")
-        out.append(FaultSpec(kind=FaultKind(kind.strip()), target=kv["target"],
-                             at_iteration=int(kv["iter"]) if "iter" in kv else None,
-                             at_time=float(kv["time"]) if "time" in kv else None,
-                             duration=float(kv["duration"]) if "duration" in kv else None,
-                             factor=float(kv.get("factor", 1.0)), phase=kv.get("phase", "forward"),
-                             params=tuple(sorted((k, v) for k, v in kv.items() if k not in _RESERVED))))
-    return out
+    return [_parse_one(item) for item in (s.strip() for s in (spec or "").split(";")) if item]
 
 
 class FaultInjector:
     def __init__(self, worker_id: str, faults: list[FaultSpec], *, start_time: float | None = None,
                  kill_fn: Callable[[], None] | None = None):
         self.worker_id = worker_id
-        self.faults = [f for f in faults if f.target in (worker_id, "*")]
+        self.faults = [f for f in faults if f.target in ("*", worker_id)]
         self.fired: set[int] = set()
-        self.start_time = time.monotonic() if start_time is None else start_time
+        self.start_time = start_time if start_time is not None else time.monotonic()
         self._kill_fn = kill_fn
-        self._slow_until: float | None = None
-        self._slow_factor = 1.0
+        self._slow_factor, self._slow_until = 1.0, None
         self._link_delay: dict[str, float] = {}
+        self._actions = {FaultKind.KILL: self._kill, FaultKind.HANG: self._hang,
+                         FaultKind.SLOW_COMPUTE: self._slow, FaultKind.SLOW_LINK: self._slow_link}
+
+    def _due(self, f: FaultSpec, iteration: int, phase: str, now: float) -> bool:
+        if f.at_iteration is None and f.at_time is None:
+            return False
+        if f.at_iteration is not None and (iteration < f.at_iteration or phase != f.phase):
+            return False
+        return f.at_time is None or now - self.start_time >= f.at_time
 
     def on_hook(self, iteration: int, phase: str) -> None:
         now = time.monotonic()
         for i, f in enumerate(self.faults):
-            if i in self.fired or (f.at_iteration is None and f.at_time is None):
-                continue
-            if f.at_iteration is not None and (iteration < f.at_iteration or phase != f.phase):
-                continue
-            if f.at_time is not None and now - self.start_time < f.at_time:
-                continue
-            self.fired.add(i)
-            self._fire(f, now)
+            if i not in self.fired and self._due(f, iteration, phase, now):
+                self.fired.add(i)
+                log.warning("injecting %s on %s", f.to_spec(), self.worker_id)
+                action = self._actions.get(f.kind)
+                if action is None:
+                    raise ValueError(f"{f.kind.value} cannot be injected in-process; use ExternalInjector")
+                action(f, now)
 
-    def _fire(self, f: FaultSpec, now: float) -> None:
-        log.warning("injecting %s on %s", f.to_spec(), self.worker_id)
-        if f.kind == FaultKind.KILL:
-            (self._kill_fn or (lambda: os.kill(os.getpid(), signal.SIGKILL)))()
-        elif f.kind == FaultKind.HANG:
-            if f.duration is not None:
-                subprocess.Popen(["sh", "-c", f"sleep {f.duration}; kill -CONT {os.getpid()}"])
-            os.kill(os.getpid(), signal.SIGSTOP)
-        elif f.kind == FaultKind.SLOW_COMPUTE:
-            self._slow_factor = max(1.0, f.factor)
-            self._slow_until = None if f.duration is None else now + f.duration
-        elif f.kind == FaultKind.SLOW_LINK:
-            self._link_delay[f.param("peer", "*")] = float(f.param("delay_s", "0.01"))
+    def _kill(self, f: FaultSpec, now: float) -> None:
+        if self._kill_fn is not None:
+            self._kill_fn()
         else:
-            raise ValueError(f"{f.kind.value} cannot be injected in-process; use ExternalInjector")
+            os.kill(os.getpid(), signal.SIGKILL)
+
+    def _hang(self, f: FaultSpec, now: float) -> None:
+        if f.duration is not None:  # a helper wakes this process up again
+            subprocess.Popen(["sh", "-c", f"sleep {f.duration}; kill -CONT {os.getpid()}"])
+        os.kill(os.getpid(), signal.SIGSTOP)
+
+    def _slow(self, f: FaultSpec, now: float) -> None:
+        self._slow_factor = max(1.0, f.factor)
+        self._slow_until = now + f.duration if f.duration is not None else None
+
+    def _slow_link(self, f: FaultSpec, now: float) -> None:
+        self._link_delay[f.param("peer", "*")] = float(f.param("delay_s", "0.01"))
 
     def compute_factor(self) -> float:
         if self._slow_until is not None and time.monotonic() > self._slow_until:
@@ -154,28 +154,27 @@ class FaultInjector:
         return self._slow_factor
 
     def pad_compute(self, elapsed_s: float) -> float:
-        """Busy-wait so a chunk that took ``elapsed_s`` looks ``factor`` times slower."""
-        factor = self.compute_factor()
-        if factor <= 1.0 or elapsed_s <= 0:
+        """Busy-wait so that a chunk which took ``elapsed_s`` looks ``factor`` times slower."""
+        extra = (self.compute_factor() - 1.0) * max(elapsed_s, 0.0)
+        if extra <= 0.0:
             return 0.0
-        pad = (factor - 1.0) * elapsed_s
-        end = time.perf_counter() + pad
-        while time.perf_counter() < end:
+        until = time.perf_counter() + extra
+        while time.perf_counter() < until:
             pass
-        return pad
+        return extra
 
     def link_delay(self, peer: str) -> float:
-        d = self._link_delay.get(peer, self._link_delay.get("*", 0.0))
-        if d > 0:
-            time.sleep(d)
-        return d
+        delay = self._link_delay.get(peer, self._link_delay.get("*", 0.0))
+        if delay > 0:
+            time.sleep(delay)
+        return delay
 
 
 _INJECTOR: FaultInjector | None = None
 
 
 def get_injector() -> FaultInjector:
-    """Process-wide injector from ``RESIHP_FAULTS`` and ``RESIHP_WORKER_ID``."""
+    """The process-wide injector built from ``RESIHP_FAULTS`` and ``RESIHP_WORKER_ID``."""
     global _INJECTOR
     if _INJECTOR is None:
         _INJECTOR = FaultInjector(os.environ.get("RESIHP_WORKER_ID", ""), parse_faults(os.environ.get("RESIHP_FAULTS")))
@@ -193,49 +192,70 @@ class ExternalCommand:
     revert: list[str] | None = None
 
 
+def _cmd_kill(f):
+    return ExternalCommand(["kill", "-9", f.param("pid", "0")])
+
+
+def _cmd_hang(f):
+    pid = f.param("pid", "0")
+    return ExternalCommand(["kill", "-STOP", pid], ["kill", "-CONT", pid])
+
+
+def _cmd_slow(f):
+    locked = str(int(float(f.param("base_mhz", "1965")) / max(f.factor, 1.0)))
+    gpu = f.param("gpu", "0")
+    return ExternalCommand(["nvidia-smi", "-i", gpu, "-lgc", f"{locked},{locked}"], ["nvidia-smi", "-i", gpu, "-rgc"])
+
+
+def _cmd_power_cap(f):
+    gpu = f.param("gpu", "0")
+    return ExternalCommand(["nvidia-smi", "-i", gpu, "-pl", f.param("watts", "500")],
+                           ["nvidia-smi", "-i", gpu, "-pl", f.param("default_watts", "1000")])
+
+
+def _cmd_xid(f):
+    # DCGM field 230 carries XID errors: this exercises the agents' health-probe path
+    return ExternalCommand(["dcgmi", "test", "--inject", "--gpuid", f.param("gpu", "0"), "-f", "230", "-v",
+                            f.param("xid", "79")])
+
+
+def _cmd_nic_down(f):
+    iface = f.param("iface", "ib0")
+    return ExternalCommand(["ip", "link", "set", "dev", iface, "down"], ["ip", "link", "set", "dev", iface, "up"])
+
+
+def _cmd_slow_link(f):
+    return ExternalCommand(["python", "-m", "resihp_megatron_b200.inject.contention", "--host",
+                            f.param("peer", "127.0.0.1"), "--port", f.param("port", "29700"), "--seconds",
+                            str(f.duration or 60)])
+
+
+_COMMANDS = {FaultKind.KILL: _cmd_kill, FaultKind.HANG: _cmd_hang, FaultKind.SLOW_COMPUTE: _cmd_slow,
+             FaultKind.POWER_CAP: _cmd_power_cap, FaultKind.XID: _cmd_xid, FaultKind.NIC_DOWN: _cmd_nic_down,
+             FaultKind.SLOW_LINK: _cmd_slow_link}
+
+
 class ExternalInjector:
-    """Host-level fault emulation; dry run unless ``dry_run=False``.  Commands that change a
-    GPU's settings (clock lock, power cap, XID injection) additionally need
-    ``allow_device_settings=True`` and are refused otherwise."""
+    """Host-level fault emulation, a dry run unless ``dry_run=False``.  Commands that change a
+    GPU's settings (clock lock, power cap, XID injection) also need ``allow_device_settings=True``
+    and are refused otherwise."""
 
     def __init__(self, dry_run: bool = True, runner: Callable[[list[str]], int] | None = None,
                  allow_device_settings: bool = False):
-        self.dry_run = dry_run
-        self.allow_device_settings = allow_device_settings
+        self.dry_run, self.allow_device_settings = dry_run, allow_device_settings
         self.executed: list[list[str]] = []
-        self._runner = runner or (lambda cmd: subprocess.call(cmd))
+        self._runner = runner if runner is not None else subprocess.call
 
     @staticmethod
     def commands(f: FaultSpec) -> ExternalCommand:
-        gpu = f.param("gpu", "0")
-        if f.kind == FaultKind.KILL:
-            return ExternalCommand(["kill", "-9", f.param("pid", "0")])
-        if f.kind == FaultKind.HANG:
-            pid = f.param("pid", "0")
-            return ExternalCommand(["kill", "-STOP", pid], ["kill", "-CONT", pid])
-        if f.kind == FaultKind.SLOW_COMPUTE:
-            base = float(f.param("base_mhz", "1965"))
-            mhz = str(int(base / max(f.factor, 1.0)))
-            return ExternalCommand(["nvidia-smi", "-i", gpu, "-lgc", f"{mhz},{mhz}"], ["nvidia-smi", "-i", gpu, "-rgc"])
-        if f.kind == FaultKind.POWER_CAP:
-            return ExternalCommand(["nvidia-smi", "-i", gpu, "-pl", f.param("watts", "500")],
-                                   ["nvidia-smi", "-i", gpu, "-pl", f.param("default_watts", "1000")])
-        if f.kind == FaultKind.XID:
-            # DCGM field 230 (XID errors): exercises the health-monitor path
-            return ExternalCommand(["dcgmi", "test", "--inject", "--gpuid", gpu, "-f", "230", "-v",
-                                    f.param("xid", "79")])
-        if f.kind == FaultKind.NIC_DOWN:
-            iface = f.param("iface", "ib0")
-            return ExternalCommand(["ip", "link", "set", "dev", iface, "down"], ["ip", "link", "set", "dev", iface, "up"])
-        if f.kind == FaultKind.SLOW_LINK:
-            return ExternalCommand(["python", "-m", "resihp_megatron_b200.inject.contention", "--host",
-                                    f.param("peer", "127.0.0.1"), "--port", f.param("port", "29700"), "--seconds",
-                                    str(f.duration or 60)])
-        raise ValueError(f"unsupported external fault {f.kind}")
+        build = _COMMANDS.get(f.kind)
+        if build is None:
+            raise ValueError(f"unsupported external fault {f.kind}")
+        return build(f)
 
     @staticmethod
     def changes_device_settings(f: FaultSpec) -> bool:
-        return f.kind in DEVICE_SETTING_KINDS or f.kind == FaultKind.SLOW_COMPUTE
+        return f.kind == FaultKind.SLOW_COMPUTE or f.kind in DEVICE_SETTING_KINDS
 
     def apply(self, f: FaultSpec) -> ExternalCommand:
         cmd = self.commands(f)
@@ -243,9 +263,9 @@ class ExternalInjector:
         return cmd
 
     def revert(self, f: FaultSpec) -> None:
-        cmd = self.commands(f)
-        if cmd.revert:
-            self._run(cmd.revert, f)
+        undo = self.commands(f).revert
+        if undo:
+            self._run(undo, f)
 
     def _run(self, argv: list[str], f: FaultSpec) -> None:
         self.executed.append(argv)
@@ -254,28 +274,27 @@ class ExternalInjector:
             return
         if self.changes_device_settings(f) and not self.allow_device_settings:
             raise PermissionError(f"{f.kind.value} changes GPU settings; pass allow_device_settings=True")
-        rc = self._runner(argv)
-        if rc != 0:
-            raise RuntimeError(f"fault command failed ({rc}): {shlex.join(argv)}")
+        code = self._runner(argv)
+        if code != 0:
+            raise RuntimeError(f"fault command failed ({code}): {shlex.join(argv)}")
 
 
 def run_schedule(faults: list[FaultSpec], injector: ExternalInjector, *, clock: Callable[[], float] = time.monotonic,
                  sleep: Callable[[float], None] = time.sleep) -> list[tuple[float, FaultSpec, str]]:
-    """Run time-triggered faults and their reverts in time order; returns the event log."""
-    t0 = clock()
-    events: list[tuple[float, str, FaultSpec]] = []
-    for f in faults:
-        if f.at_time is None:
-            continue
-        events.append((f.at_time, "apply", f))
+    """Apply the time-triggered faults and their reverts in time order (a revert first when both
+    fall on the same instant); returns ``(time, fault, action)`` per event."""
+    timeline = []
+    for f in filter(lambda f: f.at_time is not None, faults):
+        timeline.append((f.at_time, 1, "apply", f))
         if f.duration is not None:
-            events.append((f.at_time + f.duration, "revert", f))
-    events.sort(key=lambda e: (e[0], e[1] != "revert"))
-    log_ = []
-    for at, action, f in events:
-        wait = at - (clock() - t0)
-        if wait > 0:
-            sleep(wait)
-        (injector.apply if action == "apply" else injector.revert)(f)
-        log_.append((at, f, action))
-    return log_
+            timeline.append((f.at_time + f.duration, 0, "revert", f))
+    timeline.sort(key=lambda e: (e[0], e[1]))
+    started = clock()
+    done = []
+    for at, _, action, f in timeline:
+        pause = at - (clock() - started)
+        if pause > 0:
+            sleep(pause)
+        getattr(injector, action)(f)
+        done.append((at, f, action))
+    return done
