@@ -1,13 +1,14 @@
-"""Cluster-scale experiments: ETTR across scales and policies, loss breakdown, sensitivity.
+"""Cluster-scale experiments: ETTR across scales and policies, the loss breakdown, sensitivity.
 
 The job is a 405B-class dense model on TP8 x PP16 (128 GPUs per replica) with 16 micro-batches
 per replica, on the Llama 3 failure trace scaled to the cluster size.
-(Reference: ``resihp/sim/experiments.py:20-100``.)
+Parity: ``resihp/sim/experiments.py:20-100`` (same job, sweeps and tables).
 """
 
 from __future__ import annotations
 
 import statistics
+from collections import defaultdict
 
 from .calibrate import PROFILE
 from .cluster import JobConfig, baseline_params, ideal_params, resihp_params, simulate
@@ -22,76 +23,77 @@ def job_for(gpus: int, **kw) -> JobConfig:
 
 
 def policies(job: JobConfig, calib: dict, *, restart_s: float = 300.0, checkpoint_interval_s: float = 1200.0):
-    return [ideal_params(), resihp_params(job, beta=calib["beta"], overhead=calib["overhead"]),
-            *baseline_params(job, restart_s=restart_s, checkpoint_interval_s=checkpoint_interval_s)]
+    baselines = baseline_params(job, restart_s=restart_s, checkpoint_interval_s=checkpoint_interval_s)
+    return [ideal_params(), resihp_params(job, beta=calib["beta"], overhead=calib["overhead"]), *baselines]
+
+
+def _mean_row(rows: list[dict]) -> dict:
+    numeric = [k for k, v in rows[0].items() if isinstance(v, (int, float))]
+    mean = {k: statistics.fmean(r[k] for r in rows) for k in numeric}
+    mean["ettr_std"] = statistics.pstdev(r["ettr"] for r in rows)
+    return mean
 
 
 def run_cell(gpus: int, days: float, seeds: int, calib: dict, trace_kw=None, policy_kw=None,
              spare_frac: float = 0.0) -> dict:
-    trace_kw, policy_kw = trace_kw or {}, policy_kw or {}
+    """Every policy on ``seeds`` traces of one cluster size; per-policy means over the seeds."""
     job = job_for(gpus, spare_nodes=int(round(spare_frac * gpus / 8)))
-    per_policy: dict[str, list[dict]] = {}
-    traces = []
+    rows: dict[str, list[dict]] = defaultdict(list)
+    summaries = []
     for seed in range(seeds):
-        cfg = TraceConfig(gpus=gpus, days=days, seed=seed, **trace_kw)
+        cfg = TraceConfig(gpus=gpus, days=days, seed=seed, **(trace_kw or {}))
         events = generate(cfg)
-        traces.append(summarize(events, cfg))
-        for p in policies(job, calib, **policy_kw):
-            per_policy.setdefault(p.name, []).append(simulate(events, job, p, days * 86400.0).to_json())
-    cell = {"gpus": gpus, "days": days, "seeds": seeds, "trace": traces[0] if traces else {},
-            "fail_stop_mean": statistics.fmean(t["fail_stop"] for t in traces), "policies": {}}
-    for name, rows in per_policy.items():
-        agg = {k: statistics.fmean(r[k] for r in rows) for k, v in rows[0].items() if isinstance(v, (int, float))}
-        agg["ettr_std"] = statistics.pstdev(r["ettr"] for r in rows)
-        cell["policies"][name] = agg
-    return cell
+        summaries.append(summarize(events, cfg))
+        for policy in policies(job, calib, **(policy_kw or {})):
+            rows[policy.name].append(simulate(events, job, policy, 86400.0 * days).to_json())
+    return {"gpus": gpus, "days": days, "seeds": seeds, "trace": summaries[0] if summaries else {},
+            "fail_stop_mean": statistics.fmean(s["fail_stop"] for s in summaries),
+            "policies": {name: _mean_row(r) for name, r in rows.items()}}
 
 
 def scale_sweep(calib: dict, scales=DEFAULT_SCALES, days: float = 30.0, seeds: int = 5) -> list[dict]:
-    return [run_cell(g, days, seeds, calib) for g in scales]
+    return [run_cell(gpus, days, seeds, calib) for gpus in scales]
 
 
 def sensitivity(calib: dict, gpus: int = 16384, days: float = 30.0, seeds: int = 3) -> dict:
+    """ETTR per policy while one assumption moves: restart time, GPU repair time, failure rate,
+    fail-slow rate."""
     base = TraceConfig(gpus=gpus)
-    out: dict[str, dict] = {"restart_s": {}, "gpu_repair_h": {}, "fail_rate_x": {}, "slow_rate_x": {}}
-    for r in (300.0, 600.0, 1200.0, 1800.0):
-        out["restart_s"][str(int(r))] = run_cell(gpus, days, seeds, calib, policy_kw={"restart_s": r})["policies"]
-    for h in (6.0, 24.0, 72.0):
-        repair = dict(base.repair_median_s, gpu=h * 3600.0)
-        out["gpu_repair_h"][str(int(h))] = run_cell(gpus, days, seeds, calib,
-                                                    trace_kw={"repair_median_s": repair})["policies"]
-    for x in (0.5, 1.0, 2.0, 4.0):
-        out["fail_rate_x"][str(x)] = run_cell(gpus, days, seeds, calib, trace_kw={"rate_scale": x})["policies"]
-    for x in (0.0, 1.0, 4.0):
-        out["slow_rate_x"][str(x)] = run_cell(gpus, days, seeds, calib,
-                                              trace_kw={"slow_per_gpu_day": base.slow_per_gpu_day * x})["policies"]
-    return out
+
+    def cell(**kw):
+        return run_cell(gpus, days, seeds, calib, **kw)["policies"]
+
+    knobs = {
+        "restart_s": {str(int(r)): dict(policy_kw={"restart_s": r}) for r in (300.0, 600.0, 1200.0, 1800.0)},
+        "gpu_repair_h": {str(int(h)): dict(trace_kw={"repair_median_s": dict(base.repair_median_s, gpu=h * 3600.0)})
+                         for h in (6.0, 24.0, 72.0)},
+        "fail_rate_x": {str(x): dict(trace_kw={"rate_scale": x}) for x in (0.5, 1.0, 2.0, 4.0)},
+        "slow_rate_x": {str(x): dict(trace_kw={"slow_per_gpu_day": base.slow_per_gpu_day * x}) for x in (0.0, 1.0, 4.0)},
+    }
+    return {knob: {label: cell(**kw) for label, kw in settings.items()} for knob, settings in knobs.items()}
 
 
 def scale_table(cells: list[dict]) -> str:
     names = list(cells[0]["policies"])
-    lines = ["| policy | " + " | ".join(f"{c['gpus']:,} GPUs" for c in cells) + " |",
-             "|---|" + "---|" * len(cells)]
-    for n in names:
-        lines.append(f"| {n} | " + " | ".join(f"{c['policies'][n]['ettr'] * 100:.1f}%" for c in cells) + " |")
-    lines.append("| fail-stop events | " + " | ".join(f"{c['fail_stop_mean']:.0f}" for c in cells) + " |")
-    return "\n".join(lines)
+    rows = ["| policy | " + " | ".join(f"{c['gpus']:,} GPUs" for c in cells) + " |", "|---|" + "---|" * len(cells)]
+    rows += [f"| {n} | " + " | ".join(f"{c['policies'][n]['ettr'] * 100:.1f}%" for c in cells) + " |" for n in names]
+    rows.append("| fail-stop events | " + " | ".join(f"{c['fail_stop_mean']:.0f}" for c in cells) + " |")
+    return "\n".join(rows)
 
 
 def breakdown_table(cell: dict) -> str:
-    lines = [f"| policy ({cell['gpus']:,} GPUs, {cell['days']:.0f} days) | ETTR | downtime | rollback | "
-             "degraded throughput | mean MTTR (s) | p99 MTTR (s) |", "|---|---|---|---|---|---|---|"]
-    for n, a in cell["policies"].items():
-        lines.append(f"| {n} | {a['ettr'] * 100:.2f}% | {a['downtime_frac'] * 100:.2f}% | {a['lost_frac'] * 100:.2f}% | "
-                     f"{a['degraded_frac'] * 100:.2f}% | {a['mttr_mean_s']:.0f} | {a['mttr_p99_s']:.0f} |")
-    return "\n".join(lines)
+    rows = [f"| policy ({cell['gpus']:,} GPUs, {cell['days']:.0f} days) | ETTR | downtime | rollback | "
+            "degraded throughput | mean MTTR (s) | p99 MTTR (s) |", "|---|---|---|---|---|---|---|"]
+    for name, a in cell["policies"].items():
+        pct = [f"{a[k] * 100:.2f}%" for k in ("ettr", "downtime_frac", "lost_frac", "degraded_frac")]
+        rows.append(f"| {name} | " + " | ".join(pct) + f" | {a['mttr_mean_s']:.0f} | {a['mttr_p99_s']:.0f} |")
+    return "\n".join(rows)
 
 
 def sensitivity_table(sens: dict) -> str:
-    out = []
+    lines = []
     for knob, cells in sens.items():
         names = list(next(iter(cells.values())))
-        out += [f"\n**{knob}**\n", "| policy | " + " | ".join(cells) + " |", "|---|" + "---|" * len(cells)]
-        for n in names:
-            out.append(f"| {n} | " + " | ".join(f"{cells[k][n]['ettr'] * 100:.1f}%" for k in cells) + " |")
-    return "\n".join(out)
+        lines += [f"\n**{knob}**\n", "| policy | " + " | ".join(cells) + " |", "|---|" + "---|" * len(cells)]
+        lines += [f"| {n} | " + " | ".join(f"{cells[k][n]['ettr'] * 100:.1f}%" for k in cells) + " |" for n in names]
+    return "\n".join(lines)
