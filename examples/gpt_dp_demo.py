@@ -1,14 +1,14 @@
-"""Resilient replica-DP training of the float64 GPT decoder on CPU workers.
+"""Worker main: resilient replica-DP training of the float64 GPT decoder on CPU workers.
 
-benchmark config 1: 8 workers on 2 simulated nodes, 8 micro-batches of 2 x 32 tokens, 4 layers,
-hidden 64, 4 heads, vocab 512, N(0, 0.02) init from seed 0, uniform tokens from seed 1::
+Benchmark config 1 -- 8 workers on 2 simulated nodes, 8 micro-batches of 2 x 32 tokens, 4
+layers, hidden 64, 4 heads, vocab 512, N(0, 0.02) init from seed 0, uniform tokens from seed 1::
 
     RESIHP_FAULTS="kill@iter=3:target=n0g3:phase=forward" \\
     resihp-run local --nnodes 2 --nproc-per-node 4 \\
         --planner resihp_megatron_b200.train.demo_planners:dp_8mb -- python examples/gpt_dp_demo.py --out /tmp/gpt
 
-With the canonical micro-batch-order reduction, every survivor's loss trajectory is bitwise
-equal to ``runtime.reference_gpt.train_single_process``.
+The gradients are reduced per micro-batch in global micro-batch order, so every survivor's loss
+trajectory is bit for bit that of ``runtime.reference_gpt.train_single_process``, failure or not.
 """
 
 from __future__ import annotations
@@ -32,36 +32,40 @@ from resihp_megatron_b200.train.dp_binding import DPBinding  # noqa: E402
 from resihp_megatron_b200.train.resilient_loop import ResilientTrainer  # noqa: E402
 
 
+def _gpt_runtime_hooks(cfg: GPTRefConfig) -> dict:
+    """How the DP runtime batches, scores and counts tokens for the GPT oracle."""
+    return {"batch_fn": lambda it, mb: batch(cfg, it, mb),
+            "loss_fn": lambda model, b: forward_loss(cfg, model.params, b[0], b[1]),
+            "tokens_fn": lambda it: cfg.tokens_per_iteration}
+
+
 def main(argv=None) -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--iterations", type=int, default=20)
-    ap.add_argument("--lr", type=float, default=1e-3)
-    ap.add_argument("--timeout", type=float, default=30.0)
-    ap.add_argument("--out", required=True)
-    args = ap.parse_args(argv)
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--iterations", type=int, default=20)
+    parser.add_argument("--lr", type=float, default=1e-3)
+    parser.add_argument("--timeout", type=float, default=30.0)
+    parser.add_argument("--out", required=True)
+    args = parser.parse_args(argv)
     torch.set_num_threads(1)
+
     cfg = GPTRefConfig()
+    model = GPTRefModel(cfg)
+    optimizer = Adam(model.params, lr=args.lr, betas=(0.9, 0.95))
     client = WorkerClient(hb_interval=0.1).connect()
     mgr = ResilientCommManager("gloo", timeout_s=args.timeout, validate_timeout_s=args.timeout)
-    model = GPTRefModel(cfg)
-    opt = Adam(model.params, lr=args.lr, betas=(0.9, 0.95))
-    rt_kw = dict(batch_fn=lambda it, mb: batch(cfg, it, mb),
-                 loss_fn=lambda m, b: forward_loss(cfg, m.params, b[0], b[1]),
-                 tokens_fn=lambda it: cfg.tokens_per_iteration)
-    binding = DPBinding(cfg, None, model, opt, mgr, client, injector=get_injector(), timeout=args.timeout,
-                        canonical=True, runtime_kwargs=rt_kw)
+    binding = DPBinding(cfg, None, model, optimizer, mgr, client, injector=get_injector(), timeout=args.timeout,
+                        canonical=True, runtime_kwargs=_gpt_runtime_hooks(cfg))
     result = ResilientTrainer(client, mgr, binding).run(args.iterations)
-    out = Path(args.out)
+
+    out, me = Path(args.out), client.worker_id
     out.mkdir(parents=True, exist_ok=True)
-    me = client.worker_id
-    (out / f"{me}.json").write_text(json.dumps({"worker": me, "losses": {str(k): v for k, v in result.losses.items()},
-                                                "generations": result.generations,
-                                                "reconfigurations": result.reconfigurations,
-                                                "step_count": opt.step_count}))
-    torch.save({k: v.detach() for k, v in model.params.items()}, out / f"{me}.pt")
+    (out / f"{me}.json").write_text(json.dumps(dict(
+        worker=me, losses={str(it): loss for it, loss in result.losses.items()}, generations=result.generations,
+        reconfigurations=result.reconfigurations, step_count=optimizer.step_count)))
+    torch.save({name: p.detach() for name, p in model.params.items()}, out / f"{me}.pt")
     mgr.destroy()
     client.close()
-    os._exit(0)
+    os._exit(0)  # skip interpreter teardown: helper threads may still hold sockets
 
 
 if __name__ == "__main__":

@@ -1,15 +1,17 @@
-"""Dynamic hybrid parallelism with live state migration (reference model, CPU or GPU ranks).
+"""Worker main: dynamic hybrid parallelism with live state migration on the float64 reference
+model (CPU ranks, or one GPU per rank).
 
-The coordinator runs the progressive TP -> PP -> DP planner (``plan.coordinator_adapter``);
-each worker runs the float64 reference model with heterogeneous TP, uneven PP and stage-level
-migration, and migrates parameters plus Adam state slice by slice whenever the plan changes::
+The coordinator runs the joint TP -> PP -> DP planner (``plan.coordinator_adapter``); each
+worker trains its slice of the reference model with heterogeneous TP, uneven PP and stage-level
+micro-batch migration, and moves parameters plus Adam state slice by slice whenever the plan
+changes::
 
     resihp-run local --nnodes 2 --nproc-per-node 4 \\
         --planner resihp_megatron_b200.train.demo_planners:hetero_tp2_pp2_dp2 \\
         -- python examples/hetero_demo.py --out /tmp/hetero
 
-``--backend gloo`` runs on CPU; ``--backend nccl`` puts the same model and instruction streams on
-this worker's GPU.  Parameters and batches come from counter-based seeds, so both backends train
+``--backend gloo`` runs on the CPU; ``--backend nccl`` puts the same model and instruction streams
+on this worker's GPU.  Parameters and batches come from counter-based seeds, so both backends train
 the identical model.  Each worker writes ``<id>.json`` (losses, generations, last transfer) and
 ``<id>.pt`` (its final shards) under ``--out``.
 """
@@ -34,51 +36,55 @@ from resihp_megatron_b200.state.rng_data import IndexAddressableSampler  # noqa:
 from resihp_megatron_b200.train.hetero_binding import HeteroBinding  # noqa: E402
 from resihp_megatron_b200.train.resilient_loop import ResilientTrainer  # noqa: E402
 
+OPTIONS = [("--iterations", dict(type=int, default=6)), ("--gbs", dict(type=int, default=16)),
+           ("--mbs", dict(type=int, default=2)), ("--lr", dict(type=float, default=1e-2)),
+           ("--timeout", dict(type=float, default=30.0)),
+           ("--channels", dict(action="store_true", help="dedicated 2-rank groups per pipeline direction")),
+           ("--iter-sleep", dict(type=float, default=0.0, help="stretch iterations (demos and chaos runs)")),
+           ("--amax-history", dict(type=int, default=0, help="fp8-style delayed-scaling history length")),
+           ("--backend", dict(default="gloo", choices=["gloo", "nccl"])), ("--out", dict(required=True))]
+
+
+def _device(backend: str) -> str:
+    if backend != "nccl":
+        return "cpu"
+    torch.cuda.set_device(int(os.environ.get("RESIHP_LOCAL_RANK", "0")))
+    return f"cuda:{torch.cuda.current_device()}"
+
+
+def _write_result(out: Path, me: str, result, binding: HeteroBinding) -> None:
+    out.mkdir(parents=True, exist_ok=True)
+    report = dict(worker=me, losses={str(it): loss for it, loss in result.losses.items()},
+                  generations=result.generations, standby=result.standby, reconfigurations=result.reconfigurations,
+                  last_transfer=binding.last_transfer)
+    gen = binding.committed
+    if gen is not None and not result.standby:
+        report["layout"] = {key: list(span) for key, span in gen.layout.items()}
+        report["generation"] = gen.plan.generation
+        shards = {k: v.detach().cpu() for k, v in gen.module.named_state().items()}
+        shards |= {k: v.cpu() for k, v in gen.module.named_buffer_state().items()}
+        torch.save(shards, out / f"{me}.pt")
+    (out / f"{me}.json").write_text(json.dumps(report))
+
 
 def main(argv=None) -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--iterations", type=int, default=6)
-    ap.add_argument("--gbs", type=int, default=16)
-    ap.add_argument("--mbs", type=int, default=2)
-    ap.add_argument("--lr", type=float, default=1e-2)
-    ap.add_argument("--timeout", type=float, default=30.0)
-    ap.add_argument("--channels", action="store_true", help="dedicated 2-rank groups per pipeline direction")
-    ap.add_argument("--iter-sleep", type=float, default=0.0, help="stretch iterations (demos and chaos runs)")
-    ap.add_argument("--amax-history", type=int, default=0, help="FP8-style delayed-scaling history length")
-    ap.add_argument("--backend", default="gloo", choices=["gloo", "nccl"])
-    ap.add_argument("--out", required=True)
-    args = ap.parse_args(argv)
+    parser = argparse.ArgumentParser()
+    for flag, kw in OPTIONS:
+        parser.add_argument(flag, **kw)
+    args = parser.parse_args(argv)
     torch.set_num_threads(1)
-
     client = WorkerClient(hb_interval=0.1).connect()
-    device = "cpu"
-    if args.backend == "nccl":
-        torch.cuda.set_device(int(os.environ.get("RESIHP_LOCAL_RANK", "0")))
-        device = f"cuda:{torch.cuda.current_device()}"
+    device = _device(args.backend)
     mgr = ResilientCommManager(args.backend, device=device, timeout_s=args.timeout, validate_timeout_s=args.timeout)
-    cfg = RefModelConfig(amax_history=args.amax_history, device=device)
-    sampler = IndexAddressableSampler(256, args.gbs, args.mbs, seed=7)
-    binding = HeteroBinding(cfg, sampler, mgr, client, lr=args.lr, use_channels=args.channels,
-                            injector=get_injector(), timeout=args.timeout, chunk=4, iter_sleep=args.iter_sleep)
+    binding = HeteroBinding(RefModelConfig(amax_history=args.amax_history, device=device),
+                            IndexAddressableSampler(256, args.gbs, args.mbs, seed=7), mgr, client, lr=args.lr,
+                            use_channels=args.channels, injector=get_injector(), timeout=args.timeout, chunk=4,
+                            iter_sleep=args.iter_sleep)
     result = ResilientTrainer(client, mgr, binding).run(args.iterations)
-
-    out = Path(args.out)
-    out.mkdir(parents=True, exist_ok=True)
-    me = client.worker_id
-    info = {"worker": me, "losses": {str(k): v for k, v in result.losses.items()}, "generations": result.generations,
-            "standby": result.standby, "reconfigurations": result.reconfigurations,
-            "last_transfer": binding.last_transfer}
-    if binding.committed is not None and not result.standby:
-        a = binding.committed
-        info["layout"] = {k: list(v) for k, v in a.layout.items()}
-        info["generation"] = a.plan.generation
-        state = {k: v.detach().cpu() for k, v in a.module.named_state().items()}
-        state.update({k: v.cpu() for k, v in a.module.named_buffer_state().items()})
-        torch.save(state, out / f"{me}.pt")
-    (out / f"{me}.json").write_text(json.dumps(info))
+    _write_result(Path(args.out), client.worker_id, result, binding)
     mgr.destroy()
     client.close()
-    os._exit(0)
+    os._exit(0)  # skip interpreter teardown: helper threads may still hold sockets
 
 
 if __name__ == "__main__":

@@ -1,17 +1,17 @@
-"""Real-process chaos benchmark on CPU (8 gloo workers, TP2 x PP2 x DP2): MTTR breakdown.
+"""Real-process chaos benchmark on the CPU (8 gloo workers, TP2 x PP2 x DP2): MTTR breakdown.
 
-Faults: ``kill`` (SIGKILL) and ``hang`` (SIGSTOP: alive, heartbeats and progress frozen) are
-injected from outside the workers at a recorded time ``t0``; ``slow`` is a 2x fail-slow of one
-rank's compute from the in-process injector (``slow@iter=...:factor=2``: each timed chunk is
+Faults: ``kill`` (SIGKILL) and ``hang`` (SIGSTOP: alive, with heartbeats and progress frozen) are
+injected from outside the workers at a recorded instant ``t0``; ``slow`` is a 2x fail-slow of
+one rank's compute from the in-process injector (``slow@iter=...:factor=2``: each timed chunk is
 stretched by a busy wait), found by the residual-BOCD detector service, with ``t0`` the moment
-the coordinator sees the victim reach that iteration.  (A SIGSTOP/SIGCONT duty cycle is not used
-for ``slow``: with sub-millisecond compute chunks it mostly stretches communication waits, which
-the residual detector's predictor rightly does not read as a slower device.)  The
-coordinator's transaction marks split recovery into detection, abort, planning, generation
-build + state migration, and commit.  Each trial also checks that the survivors' losses and
-final shards equal single-process training.  The CPU harness bounds the absolute numbers
-(gloo, process start-up, Python); the breakdown is what carries over to GPUs.
-(Reference: ``resihp/bench/chaos.py:84-186``.)
+the coordinator sees the victim reach that iteration.  (A SIGSTOP / SIGCONT duty cycle is not
+used for ``slow``: with sub-millisecond compute chunks it mostly stretches communication waits,
+which the residual detector's predictor rightly does not read as a slower device.)  The
+coordinator's transaction marks split a recovery into detection, abort, planning, generation
+build with state migration, and commit.  Every trial also checks that the survivors' losses and
+final shards equal single-process training.  The CPU harness bounds the absolute numbers (gloo,
+process start-up, Python); the breakdown is what carries over to GPUs.
+Parity: ``resihp/bench/chaos.py:84-186`` (same faults, phases and exactness check).
 """
 
 from __future__ import annotations
@@ -22,7 +22,6 @@ import signal
 import statistics
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 
@@ -34,138 +33,161 @@ FAULTS = ("kill", "hang", "slow")
 PHASES = ("detect", "abort", "plan", "build_migrate", "commit")
 
 
-def _wait(pred, timeout: float, what: str) -> None:
-    deadline = time.monotonic() + timeout
-    while not pred():
-        if time.monotonic() > deadline:
+def _until(condition, timeout: float, what: str) -> None:
+    give_up = time.monotonic() + timeout
+    while not condition():
+        if time.monotonic() > give_up:
             raise TimeoutError(what)
         time.sleep(0.02)
 
 
-def _progress(coord, worker_id: str) -> int:
-    for w in coord.membership.alive():
-        if w.worker_id == worker_id:
-            return w.progress.get("iteration", -1)
-    return -1
+def _iteration_of(coord, worker_id: str) -> int:
+    rec = next((w for w in coord.membership.alive() if w.worker_id == worker_id), None)
+    return -1 if rec is None else rec.progress.get("iteration", -1)
+
+
+def _slowest_iteration(coord) -> int:
+    return min((w.progress.get("iteration", -1) for w in coord.membership.alive()), default=-1)
 
 
 def verify(out: Path, world: list[str]) -> bool:
+    """Every survivor's losses (rtol 1e-9) and final shards equal single-process training."""
     from ..runtime.reference_model import RefModelConfig, reference_train
     from ..state.layer_registry import reference_specs
     from ..state.rng_data import IndexAddressableSampler
 
-    infos = {w: json.loads((out / f"{w}.json").read_text()) for w in world if (out / f"{w}.json").exists()}
-    iterations = 1 + max(int(i) for info in infos.values() for i in info["losses"])
+    reports = {w: json.loads((out / f"{w}.json").read_text()) for w in world if (out / f"{w}.json").exists()}
+    steps = 1 + max(int(i) for r in reports.values() for i in r["losses"])
     cfg = RefModelConfig()
-    ref_losses, ref_params = reference_train(cfg, IndexAddressableSampler(256, 16, 2, seed=7), iterations)
+    want_losses, want_params = reference_train(cfg, IndexAddressableSampler(256, 16, 2, seed=7), steps)
     specs = reference_specs(cfg)
-    for w, info in infos.items():
-        if info.get("standby"):
+    for worker, report in reports.items():
+        if report.get("standby"):
             continue
-        if any(abs(v - ref_losses[int(i)]) > 1e-9 * abs(ref_losses[int(i)]) for i, v in info["losses"].items()):
-            return False
-        shards = torch.load(out / f"{w}.pt")
-        for key, iv in info["layout"].items():
+        for it, loss in report["losses"].items():
+            if abs(loss - want_losses[int(it)]) > 1e-9 * abs(want_losses[int(it)]):
+                return False
+        shards = torch.load(out / f"{worker}.pt")
+        for key, (lo, hi) in report["layout"].items():
             spec = specs[key]
-            want = ref_params[key] if spec.dim is None else ref_params[key].narrow(spec.dim, iv[0], iv[1] - iv[0])
-            if not torch.allclose(shards[key], want, rtol=1e-9, atol=1e-11):
+            full = want_params[key]
+            expected = full if spec.dim is None else full.narrow(spec.dim, lo, hi - lo)
+            if not torch.allclose(shards[key], expected, rtol=1e-9, atol=1e-11):
                 return False
     return True
 
 
 def breakdown(history: list[dict], t0: float) -> dict:
-    """Phase durations of the first transaction that followed the fault."""
-    after = [h for h in history if h["t"] >= t0]
-    fail = next((h for h in after if h["event"] == "failure" or h["event"] == "notice"), None)
-    if fail is None:
+    """Phase durations of the first transaction after the fault (empty if it never committed)."""
+    later = [h for h in history if h["t"] >= t0]
+    first = next((h for h in later if h["event"] in ("failure", "notice")), None)
+    if first is None:
         return {}
-    gen = next(h["generation"] for h in after if h["event"] == "notice" and h["t"] >= fail["t"])
-    mark = {h["event"]: h["t"] for h in after if h.get("generation") == gen}
-    if "commit" not in mark:
+    gen = next(h["generation"] for h in later if h["event"] == "notice" and h["t"] >= first["t"])
+    at = {h["event"]: h["t"] for h in later if h.get("generation") == gen}
+    if "commit" not in at:
         return {}
-    steps = [t0, fail["t"], mark.get("aborted", fail["t"]), mark.get("planned", fail["t"]),
-             mark.get("ready", mark["commit"]), mark["commit"]]
-    out = {p: max(0.0, b - a) for p, a, b in zip(PHASES, steps, steps[1:])}
-    out["total"] = mark["commit"] - t0
-    return out
+    edges = [t0, first["t"], at.get("aborted", first["t"]), at.get("planned", first["t"]),
+             at.get("ready", at["commit"]), at["commit"]]
+    phases = {name: max(0.0, end - start) for name, start, end in zip(PHASES, edges, edges[1:])}
+    phases["total"] = at["commit"] - t0
+    return phases
+
+
+class _Trial:
+    """Coordinator, two simulated nodes of four workers, one fault, one recovery."""
+
+    def __init__(self, fault: str, iterations: int, inject_after: int, iter_sleep: float, slow_factor: float):
+        self.fault, self.iterations, self.inject_after = fault, iterations, inject_after
+        self.iter_sleep, self.slow_factor = iter_sleep, slow_factor
+        self.out = Path(tempfile.mkdtemp(prefix=f"resihp-chaos-{fault}-"))
+        self.victim_id = "n0g0" if fault == "slow" else "n0g3"  # slow: a rank that reports its group's timings
+        self.coord, self.agents = None, []
+
+    def start(self) -> None:
+        from ..control.agent import NodeAgent
+        from ..control.coordinator import Coordinator
+        from ..detect.service import DetectorService
+        from ..plan.coordinator_adapter import make_hetero_planner
+        from ..train.demo_planners import HETERO_REF
+
+        # gloo cannot abort an op blocked on a frozen peer, so the hang timeout must exceed the
+        # communication timeout (10 s) or the survivors' wait would look like a second hang
+        self.coord = Coordinator(planner=make_hetero_planner(HETERO_REF), expected_workers=8, lease_timeout=2.0,
+                                 hang_timeout=30.0, abort_timeout=30.0, ready_timeout=120.0)
+        if self.fault == "slow":
+            self.coord.report_handler = DetectorService(self.coord, warmup=6, min_increase=0.5).handle
+        self.coord.start()
+        env = {"PYTHONPATH": str(ROOT), "RESIHP_LOG_LEVEL": "ERROR", "OMP_NUM_THREADS": "1"}
+        if self.fault == "slow":
+            env["RESIHP_FAULTS"] = f"slow@iter={self.inject_after}:target={self.victim_id}:factor={self.slow_factor}"
+        cmd = [sys.executable, DEMO, "--iterations", str(self.iterations), "--out", str(self.out), "--timeout", "10",
+               "--iter-sleep", str(self.iter_sleep)]
+        for n in range(2):
+            agent = NodeAgent(f"n{n}", [self.coord.address], hb_interval=0.1, worker_timeout=3.0).start()
+            agent.spawn(cmd, 4, env=env)
+            self.agents.append(agent)
+
+    def inject(self) -> float:
+        """Wait for the warm-up, inject, return the fault instant."""
+        coord = self.coord
+        _until(lambda: coord.committed_generation >= 1, 60, "start")
+        if self.fault == "slow":  # the injector fires itself at iteration ``inject_after``
+            _until(lambda: _iteration_of(coord, self.victim_id) >= self.inject_after, 120, "warm-up")
+            return time.monotonic()
+        _until(lambda: _slowest_iteration(coord) >= self.inject_after, 120, "warm-up")
+        t0 = time.monotonic()
+        os.kill(self.victim_pid, signal.SIGKILL if self.fault == "kill" else signal.SIGSTOP)
+        return t0
+
+    @property
+    def victim_pid(self) -> int:
+        return self.agents[0].workers[self.victim_id].proc.pid
+
+    def finish(self, t0: float) -> dict:
+        coord = self.coord
+        _until(lambda: coord.committed_generation >= 2, 240, "recovery commit")
+        others = [w.proc for a in self.agents for w in a.workers.values() if w.proc.pid != self.victim_pid]
+        _until(lambda: all(p.poll() is not None for p in others) or coord.phase == "finished", 600, "job end")
+        _until(lambda: all(p.poll() is not None for p in others), 60, "workers to exit")
+        reason = next((h.get("reason") for h in coord.history if h["event"] == "commit" and h["t"] >= t0), None)
+        return {"fault": self.fault, "breakdown": breakdown(coord.history, t0), "world": list(coord.world),
+                "exact": verify(self.out, list(coord.world)), "reason": reason}
+
+    def close(self) -> None:
+        for agent in self.agents:
+            agent.stop(kill_workers=True)
+        if self.coord is not None:
+            self.coord.stop()
 
 
 def run_trial(fault: str, iterations: int = 80, inject_after: int | None = None, iter_sleep: float = 0.05,
               slow_factor: float = 2.0) -> dict:
-    from ..control.agent import NodeAgent
-    from ..control.coordinator import Coordinator
-    from ..detect.service import DetectorService
-    from ..plan.coordinator_adapter import make_hetero_planner
-    from ..train.demo_planners import HETERO_REF
-
-    # the detector calibrates its noise prior during warm-up: start a slowdown after it
-    inject_after = inject_after if inject_after is not None else (20 if fault == "slow" else 8)
-    out = Path(tempfile.mkdtemp(prefix=f"resihp-chaos-{fault}-"))
-    victim_id = "n0g0" if fault == "slow" else "n0g3"  # slow: a rank that reports its group's timings
-    # gloo cannot abort an op blocked on a frozen peer, so the hang timeout must exceed the
-    # communication timeout (10 s here) or the survivors' wait would look like a second hang
-    coord = Coordinator(planner=make_hetero_planner(HETERO_REF), expected_workers=8, lease_timeout=2.0,
-                        hang_timeout=30.0, abort_timeout=30.0, ready_timeout=120.0)
-    svc = DetectorService(coord, warmup=6, min_increase=0.5) if fault == "slow" else None
-    if svc is not None:
-        coord.report_handler = svc.handle
-    coord.start()
-    env = {"PYTHONPATH": str(ROOT), "RESIHP_LOG_LEVEL": "ERROR", "OMP_NUM_THREADS": "1"}
-    if fault == "slow":
-        env["RESIHP_FAULTS"] = f"slow@iter={inject_after}:target={victim_id}:factor={slow_factor}"
-    agents, stop = [], threading.Event()
+    # the detector calibrates its noise prior during its warm-up: a slowdown starts after it
+    after = inject_after if inject_after is not None else (20 if fault == "slow" else 8)
+    trial = _Trial(fault, iterations, after, iter_sleep, slow_factor)
     try:
-        for n in range(2):
-            ag = NodeAgent(f"n{n}", [coord.address], hb_interval=0.1, worker_timeout=3.0).start()
-            ag.spawn([sys.executable, DEMO, "--iterations", str(iterations), "--out", str(out), "--timeout", "10",
-                      "--iter-sleep", str(iter_sleep)], 4, env=env)
-            agents.append(ag)
-        _wait(lambda: coord.committed_generation >= 1, 60, "start")
-        victim = agents[0].workers[victim_id].proc.pid
-        if fault == "slow":
-            _wait(lambda: _progress(coord, victim_id) >= inject_after, 120, "warm-up")
-            t0 = time.monotonic()
-        else:
-            _wait(lambda: min((w.progress.get("iteration", -1) for w in coord.membership.alive()), default=-1)
-                  >= inject_after, 120, "warm-up")
-            t0 = time.monotonic()
-            os.kill(victim, signal.SIGKILL if fault == "kill" else signal.SIGSTOP)
-        _wait(lambda: coord.committed_generation >= 2, 240, "recovery commit")
-        stop.set()
-        procs = [w.proc for ag in agents for w in ag.workers.values()]
-        _wait(lambda: all(p.poll() is not None for p in procs if p.pid != victim) or coord.phase == "finished",
-              600, "job end")
-        _wait(lambda: all(p.poll() is not None for p in procs if p.pid != victim), 60, "workers to exit")
-        res = {"fault": fault, "breakdown": breakdown(coord.history, t0), "world": list(coord.world),
-               "exact": verify(out, list(coord.world)),
-               "reason": next((h.get("reason") for h in coord.history if h["event"] == "commit" and h["t"] >= t0),
-                              None)}
-        return res
+        trial.start()
+        return trial.finish(trial.inject())
     finally:
-        stop.set()
-        for ag in agents:
-            ag.stop(kill_workers=True)
-        coord.stop()
+        trial.close()
 
 
 def run(trials: int = 3, faults=FAULTS) -> dict:
-    out: dict = {"trials": {}, "summary": {}}
-    for f in faults:
-        rows = [run_trial(f) for _ in range(trials)]
-        out["trials"][f] = rows
-        ok = [r for r in rows if r["breakdown"]]
-        out["summary"][f] = {k: statistics.fmean(r["breakdown"][k] for r in ok) for k in (*PHASES, "total")} if ok \
-            else {}
-        out["summary"][f]["exact"] = all(r["exact"] for r in rows)
-    return out
+    result: dict = {"trials": {}, "summary": {}}
+    for fault in faults:
+        rows = result["trials"][fault] = [run_trial(fault) for _ in range(trials)]
+        timed = [r["breakdown"] for r in rows if r["breakdown"]]
+        summary = {k: statistics.fmean(b[k] for b in timed) for k in (*PHASES, "total")} if timed else {}
+        summary["exact"] = all(r["exact"] for r in rows)
+        result["summary"][fault] = summary
+    return result
 
 
 def to_markdown(res: dict) -> str:
-    lines = ["| fault | detect (s) | abort | plan | build + migrate | commit | total MTTR | exact |",
+    table = ["| fault | detect (s) | abort | plan | build + migrate | commit | total MTTR | exact |",
              "|---|---|---|---|---|---|---|---|"]
-    for f, s in res["summary"].items():
-        if "total" not in s:
-            lines.append(f"| {f} | - | - | - | - | - | - | {s.get('exact')} |")
-            continue
-        lines.append(f"| {f} | " + " | ".join(f"{s[k]:.2f}" for k in (*PHASES, "total")) + f" | {s['exact']} |")
-    return "\n".join(lines)
+    for fault, s in res["summary"].items():
+        cells = [f"{s[k]:.2f}" for k in (*PHASES, "total")] if "total" in s else ["-"] * (len(PHASES) + 1)
+        table.append(f"| {fault} | " + " | ".join(cells) + f" | {s.get('exact')} |")
+    return "\n".join(table)

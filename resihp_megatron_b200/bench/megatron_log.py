@@ -1,6 +1,6 @@
-"""Parse Megatron-LM training logs into per-iteration records, for comparing a Megatron-Core
-run of the same model/config on the same box (``resihp-bench megatron-log <file>``).
-(Reference: ``resihp/bench/megatron_log.py:1-70``; the log line format is Megatron's.)
+"""Parses Megatron-LM training logs into per-iteration records, to compare a Megatron-Core run
+of the same model and config on the same box (``resihp-bench megatron-log <file> [seq_len]``).
+Parity: ``resihp/bench/megatron_log.py:1-70`` (the log line format is Megatron's).
 """
 
 from __future__ import annotations
@@ -11,8 +11,11 @@ import statistics
 import sys
 from dataclasses import asdict, dataclass
 
-_ITER = re.compile(r"iteration\s+(\d+)/\s*(\d+)")
-_FIELD = re.compile(r"\|\s*([^|:]+?):\s*([-+0-9.eE]+)")
+_ITERATION = re.compile(r"iteration\s+(\d+)/\s*(\d+)")
+_PAIR = re.compile(r"\|\s*([^|:]+?):\s*([-+0-9.eE]+)")
+# record field -> the label Megatron prints before the value
+_LABELS = {"iter_time_ms": "elapsed time per iteration (ms)", "tflops_per_gpu": "throughput per GPU (TFLOP/s/GPU)",
+           "lm_loss": "lm loss", "global_batch_size": "global batch size"}
 
 
 @dataclass
@@ -25,40 +28,47 @@ class IterRecord:
 
 
 def parse_line(line: str) -> IterRecord | None:
-    m = _ITER.search(line)
-    if m is None or "elapsed time per iteration" not in line:
+    """One training-iteration line, or None for any other line."""
+    found = _ITERATION.search(line)
+    if found is None or _LABELS["iter_time_ms"] not in line:
         return None
-    fields = {k.strip(): float(v) for k, v in _FIELD.findall(line)}
-    gbs = fields.get("global batch size")
-    return IterRecord(int(m.group(1)), fields.get("elapsed time per iteration (ms)"),
-                      fields.get("throughput per GPU (TFLOP/s/GPU)"), fields.get("lm loss"),
-                      int(gbs) if gbs is not None else None)
+    values = {label.strip(): float(number) for label, number in _PAIR.findall(line)}
+    fields = {name: values.get(label) for name, label in _LABELS.items()}
+    if fields["global_batch_size"] is not None:
+        fields["global_batch_size"] = int(fields["global_batch_size"])
+    return IterRecord(iteration=int(found.group(1)), **fields)
 
 
 def parse_log(text: str) -> list[IterRecord]:
-    return [r for r in map(parse_line, text.splitlines()) if r is not None]
+    return [rec for rec in (parse_line(line) for line in text.splitlines()) if rec is not None]
+
+
+def _median(values) -> float | None:
+    values = [v for v in values if v is not None]
+    return statistics.median(values) if values else None
 
 
 def summarize(records: list[IterRecord], skip_first: int = 2, seq_len: int | None = None) -> dict:
+    """Medians over the steady iterations (after ``skip_first``), the loss curve, and tokens/s
+    when the sequence length is given."""
     steady = [r for r in records[skip_first:] if r.iter_time_ms is not None] or records
-    times = [r.iter_time_ms for r in steady if r.iter_time_ms is not None]
-    tflops = [r.tflops_per_gpu for r in steady if r.tflops_per_gpu is not None]
-    losses = [(r.iteration, r.lm_loss) for r in records if r.lm_loss is not None]
-    out = {"iterations": len(records), "median_iter_time_ms": statistics.median(times) if times else None,
-           "median_tflops_per_gpu": statistics.median(tflops) if tflops else None,
-           "final_loss": losses[-1][1] if losses else None, "loss_curve": losses}
-    gbs = next((r.global_batch_size for r in steady if r.global_batch_size), None)
-    if seq_len and gbs and out["median_iter_time_ms"]:
-        out["tokens_per_s"] = gbs * seq_len / (out["median_iter_time_ms"] / 1000.0)
-    return out
+    curve = [(r.iteration, r.lm_loss) for r in records if r.lm_loss is not None]
+    summary = {"iterations": len(records), "median_iter_time_ms": _median(r.iter_time_ms for r in steady),
+               "median_tflops_per_gpu": _median(r.tflops_per_gpu for r in steady),
+               "final_loss": curve[-1][1] if curve else None, "loss_curve": curve}
+    batch = next((r.global_batch_size for r in steady if r.global_batch_size), None)
+    if seq_len and batch and summary["median_iter_time_ms"]:
+        summary["tokens_per_s"] = batch * seq_len * 1000.0 / summary["median_iter_time_ms"]
+    return summary
 
 
 def main(argv: list[str] | None = None) -> int:
-    argv = sys.argv[1:] if argv is None else argv
-    text = open(argv[0]).read() if argv else sys.stdin.read()
-    seq = int(argv[1]) if len(argv) > 1 else None
-    recs = parse_log(text)
-    print(json.dumps({"summary": summarize(recs, seq_len=seq), "records": [asdict(r) for r in recs]}, indent=2))
+    args = sys.argv[1:] if argv is None else argv
+    text = open(args[0]).read() if args else sys.stdin.read()
+    records = parse_log(text)
+    seq_len = int(args[1]) if len(args) > 1 else None
+    print(json.dumps({"summary": summarize(records, seq_len=seq_len), "records": list(map(asdict, records))},
+                     indent=2))
     return 0
 
 

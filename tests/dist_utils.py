@@ -1,7 +1,8 @@
-"""Multi-process gloo helpers for tests on localhost (127.0.0.1)."""
+"""Runs a function in several spawned processes that talk over gloo on 127.0.0.1."""
 
 from __future__ import annotations
 
+import io
 import multiprocessing as mp
 import os
 import queue
@@ -13,62 +14,64 @@ from typing import Any, Callable
 
 
 def free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+    """A TCP port on 127.0.0.1 that was free a moment ago."""
+    probe = socket.socket()
+    try:
+        probe.bind(("127.0.0.1", 0))
+        return probe.getsockname()[1]
+    finally:
+        probe.close()
 
 
-def _worker(fn: Callable, rank: int, world: int, port: int, q, args: tuple) -> None:
+def _child(fn: Callable, rank: int, world: int, port: int, results, args: tuple) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo0" if sys.platform == "darwin" else "lo")
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    import io
-
     import torch
 
     torch.set_num_threads(1)
     try:
-        buf = io.BytesIO()
-        torch.save(fn(rank, world, port, *args), buf)  # bytes, not shared-memory tensors
-        q.put((rank, True, buf.getvalue()))
-    except BaseException as e:  # noqa: BLE001 - report every failure to the test process
-        q.put((rank, False, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+        value = fn(rank, world, port, *args)
+    except BaseException as err:  # noqa: BLE001 -- every failure goes back to the test
+        results.put((rank, "error", f"{type(err).__name__}: {err}\n{traceback.format_exc()}"))
+        return
+    packed = io.BytesIO()
+    torch.save(value, packed)  # plain bytes: no shared-memory tensors cross the queue
+    results.put((rank, "ok", packed.getvalue()))
 
 
 def spawn(fn: Callable, world: int, *args: Any, timeout: float = 120.0,
           expect_dead: set[int] | None = None) -> dict[int, Any]:
-    """Run ``fn(rank, world, port, *args)`` in ``world`` processes and return ``{rank: result}``;
-    ranks in ``expect_dead`` may exit without reporting (killed on purpose)."""
+    """``fn(rank, world, port, *args)`` in ``world`` processes; returns ``{rank: result}``.
+    Ranks in ``expect_dead`` may exit without a result (killed on purpose)."""
+    import torch
+
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    results = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(fn, r, world, port, q, args), daemon=True) for r in range(world)]
-    for p in procs:
-        p.start()
-    dead = expect_dead or set()
-    ok: dict[int, Any] = {}
-    bad: dict[int, str] = {}
-    deadline = time.monotonic() + timeout
-    while len(ok) + len(bad) < world - len(dead) and time.monotonic() < deadline:
+    children = [ctx.Process(target=_child, args=(fn, r, world, port, results, args), daemon=True)
+                for r in range(world)]
+    for child in children:
+        child.start()
+    silent = set(expect_dead or ())
+    values: dict[int, Any] = {}
+    errors: dict[int, str] = {}
+    give_up = time.monotonic() + timeout
+    while len(values) + len(errors) < world - len(silent) and time.monotonic() < give_up:
         try:
-            r, success, payload = q.get(timeout=0.5)
+            rank, status, payload = results.get(timeout=0.5)
         except queue.Empty:
             continue
-        if success:
-            import io
-
-            import torch
-
-            ok[r] = torch.load(io.BytesIO(payload), weights_only=False)
+        if status == "ok":
+            values[rank] = torch.load(io.BytesIO(payload), weights_only=False)
         else:
-            bad[r] = payload
-    for p in procs:
-        p.join(timeout=2)
-        if p.is_alive():
-            p.kill()
-    if bad:
-        raise AssertionError("worker failures:\n" + "\n".join(f"[rank {r}] {e}" for r, e in sorted(bad.items())))
-    missing = set(range(world)) - set(ok) - dead
-    if missing:
-        raise AssertionError(f"ranks {sorted(missing)} did not report within {timeout}s")
-    return ok
+            errors[rank] = payload
+    for child in children:
+        child.join(timeout=2)
+        if child.is_alive():
+            child.kill()
+    if errors:
+        raise AssertionError("worker failures:\n" + "\n".join(f"[rank {r}] {e}" for r, e in sorted(errors.items())))
+    unheard = sorted(set(range(world)) - set(values) - silent)
+    if unheard:
+        raise AssertionError(f"ranks {unheard} did not report within {timeout}s")
+    return values

@@ -1,11 +1,12 @@
-"""Stand-in worker for control-plane tests, steered by files in ``$TEST_TRIGGER_DIR``:
+"""A stand-in worker for the control-plane tests, steered by files in ``$TEST_TRIGGER_DIR``:
 
-* ``stall_<id>``            the main loop sleeps forever (heartbeat thread stays alive);
-* ``collective``            every worker reports being inside a collective at op 10**6 and waits
-                            for the next notice (so only the stalled one is behind);
-* ``die_on_prepare_<id>``   the worker exits as soon as it sees a PREPARE.
+* ``stall_<id>`` -- the main loop sleeps for good (its heartbeat thread stays alive);
+* ``collective`` -- every worker reports sitting inside a collective at op 10**6 and waits for
+  the next notice, so only a stalled worker is behind;
+* ``die_on_prepare_<id>`` -- the worker exits as soon as it sees a PREPARE.
 
-Each committed generation (and each abort callback) is appended to ``$TEST_EVENT_LOG`` as one JSON line."""
+Every committed generation, and every abort callback, is appended to ``$TEST_EVENT_LOG`` as one
+JSON line."""
 
 import json
 import os
@@ -18,50 +19,63 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
 from resihp_megatron_b200.control.worker_client import JobFinished, ReconfigInterrupted, WorkerClient  # noqa: E402
 
 
-def main() -> None:
-    log = open(os.environ["TEST_EVENT_LOG"], "a")
-    triggers = Path(os.environ["TEST_TRIGGER_DIR"])
-    client = WorkerClient(hb_interval=0.1).connect()
-    me = client.worker_id
+class _StandIn:
+    def __init__(self):
+        self.log = open(os.environ["TEST_EVENT_LOG"], "a")
+        self.triggers = Path(os.environ["TEST_TRIGGER_DIR"])
+        self.client = WorkerClient(hb_interval=0.1).connect()
+        self.me = self.client.worker_id
+        self.iteration = 0
+        self.parked = False
+        self.client.add_abort_callback(lambda: self.record(abort=True))
 
-    def on_abort():
-        log.write(json.dumps({"worker": me, "abort": True, "t": time.time()}) + "\n")
-        log.flush()
+    def record(self, **fields) -> None:
+        self.log.write(json.dumps({"worker": self.me, "t": time.time(), **fields}) + "\n")
+        self.log.flush()
 
-    client.add_abort_callback(on_abort)
-    it = 0
-    parked = False
-    while True:
-        try:
-            prep = client.wait_prepare(timeout=60)
-        except (TimeoutError, JobFinished):
-            return
-        gen = prep["gen"]
-        if (triggers / f"die_on_prepare_{me}").exists():
-            os._exit(3)
-        if me in prep["world"]:
-            client.send_ready(gen)
-        try:
-            client.wait_commit(gen, timeout=60)
-        except ReconfigInterrupted:
-            continue
-        log.write(json.dumps({"worker": me, "gen": gen, "world": prep["world"], "t": time.time()}) + "\n")
-        log.flush()
-        if me not in prep["world"]:
-            continue
-        while not client.reconfig_pending():
-            if (triggers / f"stall_{me}").exists():
+    def triggered(self, name: str) -> bool:
+        return (self.triggers / name).exists()
+
+    def join(self) -> dict | None:
+        """One generation: PREPARE, READY (members only), COMMIT.  None when the job ended."""
+        while True:
+            try:
+                prepare = self.client.wait_prepare(timeout=60)
+            except (TimeoutError, JobFinished):
+                return None
+            if self.triggered(f"die_on_prepare_{self.me}"):
+                os._exit(3)
+            if self.me in prepare["world"]:
+                self.client.send_ready(prepare["gen"])
+            try:
+                self.client.wait_commit(prepare["gen"], timeout=60)
+            except ReconfigInterrupted:
+                continue
+            self.record(gen=prepare["gen"], world=prepare["world"])
+            return prepare
+
+    def work(self) -> None:
+        """Make progress until the next notice (or stall / park as the triggers say)."""
+        while not self.client.reconfig_pending():
+            if self.triggered(f"stall_{self.me}"):
                 time.sleep(3600)
-            if not parked and (triggers / "collective").exists():
-                parked = True
-                client.set_progress(iteration=it, in_collective=True, op_seq=10 ** 6)
-                while not client.reconfig_pending():
+            if not self.parked and self.triggered("collective"):
+                self.parked = True
+                self.client.set_progress(iteration=self.iteration, in_collective=True, op_seq=10 ** 6)
+                while not self.client.reconfig_pending():
                     time.sleep(0.02)
-                break
-            client.set_progress(iteration=it, in_collective=False, op_seq=it)
-            client.set_recovery_info(committed_iteration=it)
-            it += 1
+                return
+            self.client.set_progress(iteration=self.iteration, in_collective=False, op_seq=self.iteration)
+            self.client.set_recovery_info(committed_iteration=self.iteration)
+            self.iteration += 1
             time.sleep(0.02)
+
+
+def main() -> None:
+    worker = _StandIn()
+    while (prepare := worker.join()) is not None:
+        if worker.me in prepare["world"]:
+            worker.work()
 
 
 if __name__ == "__main__":
