@@ -1,6 +1,10 @@
-"""Heterogeneous-TP boundary transfers, shard-aligned gradient sync and full heterogeneous
-pipelines (with stage-level migration, SP, zero-bubble, interleaving and CP), checked against
-the single-process float64 reference on gloo ranks."""
+"""The heterogeneous hybrid runtime on gloo ranks, each path checked against an independent
+ground truth: pipeline-boundary routing against the rows a brute force says each receiver
+needs, shard-aligned gradient sync against the dense sum of every replica's gradient, and whole
+heterogeneous pipelines (stage-level migration, SP, zero bubble, interleaving, CP) against the
+single-process float64 reference model."""
+
+import itertools
 
 import pytest
 import torch
@@ -9,50 +13,53 @@ from tests.dist_utils import spawn
 
 pytestmark = pytest.mark.dist
 
-COMBOS = [(1, 1), (2, 1), (1, 3), (4, 2), (2, 3), (3, 4), (4, 3)]
+PAIRS = [(1, 1), (2, 1), (1, 3), (4, 2), (2, 3), (3, 4), (4, 3)]  # (sender TP, receiver TP)
+ROWS = 24
 
 
-def _p2p(rank, world, port, store_addr):
+def _routing(rank, world, port, store_addr):
     from resihp_megatron_b200.comm.comm_manager import ResilientCommManager
     from resihp_megatron_b200.comm.group_spec import GroupSpec
-    from resihp_megatron_b200.comm.p2p import P2PEngine, boundary_routes, channel_name, local_rows
+    from resihp_megatron_b200.comm.p2p import P2PEngine, boundary_routes, channel_name
+    from resihp_megatron_b200.utils.intervals import even_split
 
     ids = [f"w{i}" for i in range(world)]
-    specs = [GroupSpec(f"tp/{a}-{b}", tuple(range(a, a + b)), "tp") for a, b in COMBOS if b > 1]
-    pairs = sorted({(r.src, r.dst) for r in boundary_routes((0, 1, 2, 3), (4, 5, 6), 24)})
-    specs += [GroupSpec(channel_name(a, b), tuple(sorted((a, b))), "p2p") for a, b in pairs]
+    specs = [GroupSpec(f"recv/{a}-{b}", tuple(range(a, a + b)), "tp") for a, b in PAIRS if b > 1]
+    channel_pairs = sorted({(r.src, r.dst) for r in boundary_routes((0, 1, 2, 3), (4, 5, 6), ROWS)})
+    specs += [GroupSpec(channel_name(s, d), (min(s, d), max(s, d)), "p2p") for s, d in channel_pairs]
     mgr = ResilientCommManager("gloo", timeout_s=30)
-    comms = mgr.build(1, ids, ids[rank], specs, store_addr=store_addr, store_prefix="p2p/gen1/")
-    full = torch.arange(24 * 5, dtype=torch.float64).reshape(24, 5)
-    ok = []
-    for a, b in COMBOS:
-        src, dst = tuple(range(a)), tuple(range(a, a + b))
-        tp = comms.group(f"tp/{a}-{b}") if b > 1 else None
-        for sp in (False, True):
-            eng = P2PEngine(rank, mgr)
-            tag = a * 10 + b + (100 if sp else 0)
-            works = []
-            if rank in src:
-                works = eng.send(full[slice(*local_rows(24, src, rank))] if sp else full, src, dst, 24, sp, tag)
-            if rank in dst:
-                got = eng.recv(24, (5,), torch.float64, src, dst, sp, tag, tp_group=tp)
-                ok.append(bool(torch.equal(got, full[slice(*local_rows(24, dst, rank))] if sp else full)))
-            eng.wait_sends(works)
-    chans = {(a, b): comms.group(channel_name(a, b)) for a, b in pairs if rank in (a, b)}
-    eng = P2PEngine(rank, mgr, channels=chans)
-    works = eng.send(full, (0, 1, 2, 3), (4, 5, 6), 24, False, 7) if rank < 4 else []
+    comms = mgr.build(1, ids, ids[rank], specs, store_addr=store_addr, store_prefix="routing/gen1/")
+    payload = torch.randn(ROWS, 5, generator=torch.Generator().manual_seed(3), dtype=torch.float64)
+    checks = []
+
+    def rows_of(ranks, r):  # brute force: which rows rank r owns in a group of len(ranks)
+        return slice(*even_split(ROWS, len(ranks))[ranks.index(r)])
+
+    for (a, b), sp in itertools.product(PAIRS, (False, True)):
+        senders, receivers = tuple(range(a)), tuple(range(a, a + b))
+        engine = P2PEngine(rank, mgr)
+        tag = 1000 * sp + 10 * a + b
+        posted = engine.send(payload[rows_of(senders, rank)] if sp else payload, senders, receivers, ROWS, sp,
+                             tag) if rank in senders else []
+        if rank in receivers:
+            got = engine.recv(ROWS, (5,), torch.float64, senders, receivers, sp, tag,
+                              tp_group=comms.group(f"recv/{a}-{b}") if b > 1 else None)
+            checks.append(torch.equal(got, payload[rows_of(receivers, rank)] if sp else payload))
+        engine.wait_sends(posted)
+    channels = {(s, d): comms.group(channel_name(s, d)) for s, d in channel_pairs if rank in (s, d)}
+    engine = P2PEngine(rank, mgr, channels=channels)
+    posted = engine.send(payload, (0, 1, 2, 3), (4, 5, 6), ROWS, False, 7) if rank < 4 else []
     if 4 <= rank < 7:
-        got = eng.recv(24, (5,), torch.float64, (0, 1, 2, 3), (4, 5, 6), False, 7, tp_group=comms.group("tp/4-3"))
-        ok.append(bool(torch.equal(got, full)))
-    eng.wait_sends(works)
+        checks.append(torch.equal(engine.recv(ROWS, (5,), torch.float64, (0, 1, 2, 3), (4, 5, 6), False, 7,
+                                              tp_group=comms.group("recv/4-3")), payload))
+    engine.wait_sends(posted)
     mgr.destroy()
-    return ok
+    return checks
 
 
-def test_boundary_routing_for_every_tp_pair(store):
-    out = spawn(_p2p, 7, store, timeout=180)
-    assert all(all(v) for v in out.values())
-    assert sum(len(v) for v in out.values()) > 20
+def test_boundary_routing_delivers_exactly_the_needed_rows(store):
+    results = spawn(_routing, 7, store, timeout=180)
+    assert all(all(r) for r in results.values()) and sum(map(len, results.values())) > 20
 
 
 def _grad_sync(rank, world, port, store_addr, sp):
@@ -68,46 +75,67 @@ def _grad_sync(rank, world, port, store_addr, sp):
 
     cfg = RefModelConfig()
     ids = [f"w{i}" for i in range(world)]
-    groups = (StageGroup(0, 0, tuple(ids[0:4]), (0, 1)), StageGroup(1, 0, tuple(ids[4:7]), (0, 1)))
-    plan = HeteroParallelPlan(1, tuple(ids), 1, 1, 2, groups, 2, ((0, 1),), sequence_parallel=sp)
+    tp4, tp3 = StageGroup(0, 0, tuple(ids[:4]), (0, 1)), StageGroup(1, 0, tuple(ids[4:]), (0, 1))
+    plan = HeteroParallelPlan(1, tuple(ids), 1, 1, 2, (tp4, tp3), 2, ((0, 1),), sequence_parallel=sp)
     mgr = ResilientCommManager("gloo", timeout_s=30)
     comms = mgr.build(1, ids, ids[rank], plan.group_specs(reference_partition_sizes(cfg)), store_addr=store_addr,
-                      store_prefix=f"gs{int(sp)}/gen1/")
-    r = 0 if rank < 4 else 1
-    g = groups[r]
-    tp_rank = g.devices.index(ids[rank])
-    tp = TPContext(group=comms.group(f"tp/r{r}/s0"), rank=tp_rank, size=g.tp, sequence_parallel=sp,
-                   waiter=lambda w: mgr.guarded_wait(w))
+                      store_prefix=f"sync{int(sp)}/gen1/")
+    replica = 0 if rank < 4 else 1
+    group = (tp4, tp3)[replica]
+    tp_rank = group.devices.index(ids[rank])
+    tp = TPContext(group=comms.group(f"tp/r{replica}/s0"), rank=tp_rank, size=group.tp, sequence_parallel=sp,
+                   waiter=mgr.guarded_wait)
     module = RefStage(cfg, 0, 1, tp)
-    params = module.named_state()
-    want = {}
-    for key, p in params.items():
+    expected = {}
+    for key, param in module.named_state().items():
         name = key.split(".", 2)[2]
-        crc = zlib.crc32(name.encode())
-        total = torch.zeros_like(full_layer_params(cfg, 0)[name])
-        for rep in (0, 1):
-            total += torch.randn(total.shape, generator=generator(rep, crc), dtype=cfg.dtype)
-        mine = torch.randn(total.shape, generator=generator(r, crc), dtype=cfg.dtype)
-        if module.sp_partial(key):
-            others = [torch.randn(total.shape, generator=generator(r, t, 5, crc), dtype=cfg.dtype)
-                      for t in range(1, g.tp)]
-            p.grad = (mine - sum(others)) if tp_rank == 0 else others[tp_rank - 1].clone()
+        seed = zlib.crc32(name.encode())
+        shape = full_layer_params(cfg, 0)[name].shape
+
+        def dense(*parts):
+            return torch.randn(shape, generator=generator(*parts, seed), dtype=cfg.dtype)
+
+        # every replica's full gradient; the synced shard must be the sum over the replicas
+        expected[key] = shard(dense(0) + dense(1), PARAM_DIMS[name], tp_rank, group.tp)
+        mine = dense(replica)
+        if module.sp_partial(key):  # partial sums over token shards that add up to ``mine``
+            parts = [dense(replica, t, 5) for t in range(1, group.tp)]
+            param.grad = mine - sum(parts) if tp_rank == 0 else parts[tp_rank - 1].clone()
         else:
-            p.grad = shard(mine, PARAM_DIMS[name], tp_rank, g.tp)
-        want[key] = shard(total, PARAM_DIMS[name], tp_rank, g.tp)
-    HeteroGradSync(plan, comms, mgr, 0, r, params, reference_shards(cfg, module), tp_group=tp.group).sync()
-    errs = {k: float((p.grad - want[k]).abs().max()) for k, p in params.items()}
+            param.grad = shard(mine, PARAM_DIMS[name], tp_rank, group.tp)
+    HeteroGradSync(plan, comms, mgr, 0, replica, module.named_state(), reference_shards(cfg, module),
+                   tp_group=tp.group).sync()
+    worst = max(float((p.grad - expected[k]).abs().max()) for k, p in module.named_state().items())
     mgr.destroy()
-    return errs
+    return worst
 
 
 @pytest.mark.parametrize("sp", [False, True])
-def test_shard_aligned_grad_sync_tp4_vs_tp3(store, sp):
-    for rank, errs in spawn(_grad_sync, 7, store, sp, timeout=180).items():
-        assert max(errs.values()) < 1e-12, (rank, errs)
+def test_shard_aligned_sync_equals_the_dense_sum_tp4_with_tp3(store, sp):
+    assert max(spawn(_grad_sync, 7, store, sp, timeout=180).values()) < 1e-12
 
 
-def _run(rank, world, store_addr, cfg, plan, prefix, iterations, zb=False, fixed=False):
+# ---------------------------------------------------------------------- whole pipelines
+def _scenario(name: str, ids: tuple, sp: bool):
+    """(plan, model config) of a named heterogeneous layout."""
+    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup, interleave
+    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
+
+    migrated = ((0, 0, 0, 0, 0, 1, 1, 1), (0, 0, 1, 1, 1, 1, 1, 1))  # stage-level micro-batch migration
+    if name == "cp":  # cp = 2 everywhere; stage 0 has TP2 and TP1 replicas; replica 1 lost stage 1
+        groups = (StageGroup(0, 0, ids[0:4], (0, 3), 2), StageGroup(1, 0, ids[4:6], (0, 3), 2),
+                  StageGroup(0, 1, ids[6:8], (3, 4), 2))
+        return HeteroParallelPlan(1, ids, 4, 2, 2, groups, 8, (migrated[0], (0,) * 8), sequence_parallel=sp), \
+            RefModelConfig()
+    split = 3 if name == "pipeline" else 5
+    layers = 4 if name == "pipeline" else 8
+    groups = (StageGroup(0, 0, ids[0:2], (0, split)), StageGroup(1, 0, ids[2:3], (0, split)),
+              StageGroup(0, 1, ids[3:4], (split, layers)), StageGroup(1, 1, ids[4:7], (split, layers)))
+    plan = HeteroParallelPlan(1, ids, layers, 2, 2, groups, 8, migrated, sequence_parallel=sp)
+    return (interleave(plan, 2) if name == "interleaved" else plan), RefModelConfig(num_layers=layers)
+
+
+def _train(rank, world, port, store_addr, name, sp, zb, iterations):
     from resihp_megatron_b200.comm.comm_manager import ResilientCommManager
     from resihp_megatron_b200.plan.ir import compute_order_to_ir, validate
     from resihp_megatron_b200.plan.simulator import schedule_with_fallback
@@ -116,112 +144,63 @@ def _run(rank, world, store_addr, cfg, plan, prefix, iterations, zb=False, fixed
     from resihp_megatron_b200.runtime.optim import Adam
     from resihp_megatron_b200.state.rng_data import IndexAddressableSampler
 
-    sampler = IndexAddressableSampler(256, 16, 2, seed=7)
-    res = schedule_with_fallback(plan, lambda k, op, mb: 1.0 if op == "F" else 2.0, lambda a, b, kind: 0.1,
-                                 split_backward=zb)
-    schedule = compute_order_to_ir(plan, res.order)
+    ids = tuple(f"w{i}" for i in range(world))
+    plan, cfg = _scenario(name, ids, sp)
+    plan.validate()
+    order = schedule_with_fallback(plan, lambda k, op, mb: 2.0 if op != "F" else 1.0, lambda a, b, kind: 0.1,
+                                   split_backward=zb).order
+    schedule = compute_order_to_ir(plan, order)
     validate(plan, schedule, split_backward=zb)
-    specs = plan.group_specs(reference_partition_sizes(cfg)) + channel_specs(plan, schedule, 48)
     mgr = ResilientCommManager("gloo", timeout_s=60)
-    ids = list(plan.world)
-    comms = mgr.build(1, ids, ids[rank], specs, store_addr=store_addr, store_prefix=prefix)
+    comms = mgr.build(1, list(ids), ids[rank], plan.group_specs(reference_partition_sizes(cfg))
+                      + channel_specs(plan, schedule, 48), store_addr=store_addr,
+                      store_prefix=f"{name}{int(sp)}{int(zb)}/gen1/")
     module = build_stage_module(cfg, plan, comms, mgr)
-    opt = Adam(module.named_state(), lr=1e-2)
-    rt = HeteroRuntime(cfg, sampler, plan, schedule, comms, mgr, module, use_channels=True)
+    optimizer = Adam(module.named_state(), lr=1e-2)
+    runtime = HeteroRuntime(cfg, IndexAddressableSampler(256, 16, 2, seed=7), plan, schedule, comms, mgr, module,
+                            use_channels=True)
     losses = []
     for it in range(iterations):
-        losses.append(rt.run_iteration(it))
-        opt.step()
+        losses.append(runtime.run_iteration(it))
+        optimizer.step()
     me = ids[rank]
-    g = plan.group_of_device(me)
-    out = {"losses": losses, "replica": g.replica, "stage": g.stage, "slice": g.slice_of(me),
-           "tp_rank": g.slice(g.slice_of(me)).index(me), "chunks": len(plan.groups_of_device(me)),
-           "shards": {k: v.detach().clone() for k, v in module.named_state().items()}}
+    group = plan.group_of_device(me)
+    cp_slice = group.slice_of(me)
+    result = {"losses": losses, "key": (group.replica, group.stage, cp_slice),
+              "tp_rank": group.slice(cp_slice).index(me), "chunks": len(plan.groups_of_device(me)),
+              "shards": {k: v.detach().clone() for k, v in module.named_state().items()}}
     mgr.destroy()
-    return out
+    return result
 
 
-def _pipeline(rank, world, port, store_addr, sp, zb, iterations):
-    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup
-    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
-
-    ids = tuple(f"w{i}" for i in range(world))
-    groups = (StageGroup(0, 0, ("w0", "w1"), (0, 3)), StageGroup(1, 0, ("w2",), (0, 3)),
-              StageGroup(0, 1, ("w3",), (3, 4)), StageGroup(1, 1, ("w4", "w5", "w6"), (3, 4)))
-    assign = ((0, 0, 0, 0, 0, 1, 1, 1), (0, 0, 1, 1, 1, 1, 1, 1))  # stage-level migration at stage 1
-    plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, 8, assign, sequence_parallel=sp)
-    plan.validate()
-    return _run(rank, world, store_addr, RefModelConfig(), plan, f"pipe{int(sp)}{int(zb)}/gen1/", iterations, zb)
-
-
-def _vpp(rank, world, port, store_addr, sp, zb, iterations):
-    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup, interleave
-    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
-
-    ids = tuple(f"w{i}" for i in range(world))
-    groups = (StageGroup(0, 0, ("w0", "w1"), (0, 5)), StageGroup(1, 0, ("w2",), (0, 5)),
-              StageGroup(0, 1, ("w3",), (5, 8)), StageGroup(1, 1, ("w4", "w5", "w6"), (5, 8)))
-    assign = ((0, 0, 0, 0, 0, 1, 1, 1), (0, 0, 1, 1, 1, 1, 1, 1))
-    plan = interleave(HeteroParallelPlan(1, ids, 8, 2, 2, groups, 8, assign, sequence_parallel=sp), 2)
-    plan.validate()
-    return _run(rank, world, store_addr, RefModelConfig(num_layers=8), plan, f"vpp{int(sp)}{int(zb)}/gen1/",
-                iterations, zb)
-
-
-def _cp(rank, world, port, store_addr, sp, iterations):
-    from resihp_megatron_b200.plan.hetero_plan import HeteroParallelPlan, StageGroup
-    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
-
-    ids = tuple(f"w{i}" for i in range(world))
-    # cp = 2 everywhere; stage 0 has TP2 and TP1 replicas; replica 1 lost stage 1
-    groups = (StageGroup(0, 0, ids[0:4], (0, 3), 2), StageGroup(1, 0, ids[4:6], (0, 3), 2),
-              StageGroup(0, 1, ids[6:8], (3, 4), 2))
-    plan = HeteroParallelPlan(1, ids, 4, 2, 2, groups, 8, ((0, 0, 0, 0, 0, 1, 1, 1), (0,) * 8),
-                              sequence_parallel=sp)
-    plan.validate()
-    return _run(rank, world, store_addr, RefModelConfig(), plan, f"cp{int(sp)}/gen1/", iterations)
-
-
-def _check_against_reference(out, cfg, iterations, key=lambda r: (r["replica"], r["stage"], r["slice"])):
+def _assert_matches_reference(results, cfg, iterations):
     from resihp_megatron_b200.runtime.reference_model import PARAM_DIMS, reference_train
     from resihp_megatron_b200.state.rng_data import IndexAddressableSampler
 
-    ref_losses, ref_params = reference_train(cfg, IndexAddressableSampler(256, 16, 2, seed=7), iterations)
-    for res in out.values():
-        assert res["losses"] == pytest.approx(ref_losses, rel=1e-10)
-    groups: dict = {}
-    for res in out.values():
-        groups.setdefault(key(res), []).append(res)
-    covered = set()
-    for members in groups.values():
+    losses, params = reference_train(cfg, IndexAddressableSampler(256, 16, 2, seed=7), iterations)
+    assert all(r["losses"] == pytest.approx(losses, rel=1e-10) for r in results.values())
+    by_group: dict = {}
+    for r in results.values():
+        by_group.setdefault(r["key"], []).append(r)
+    seen = set()
+    for members in by_group.values():  # reassemble each TP group's shards and compare to the full tensor
         members.sort(key=lambda r: r["tp_rank"])
-        for name in members[0]["shards"]:
-            dim = PARAM_DIMS[name.split(".", 2)[2]]
-            full = members[0]["shards"][name] if dim is None else torch.cat([m["shards"][name] for m in members],
-                                                                            dim=dim)
-            torch.testing.assert_close(full, ref_params[name], rtol=1e-10, atol=1e-12)
-            covered.add(name)
-    assert covered == set(ref_params)
+        for key, first in members[0]["shards"].items():
+            dim = PARAM_DIMS[key.split(".", 2)[2]]
+            whole = first if dim is None else torch.cat([m["shards"][key] for m in members], dim=dim)
+            torch.testing.assert_close(whole, params[key], rtol=1e-10, atol=1e-12)
+            seen.add(key)
+    assert seen == set(params)
 
 
-@pytest.mark.parametrize("sp,zb", [(False, False), (True, False), (False, True), (True, True)])
-def test_hetero_pipeline_with_migration_matches_reference(store, sp, zb):
+@pytest.mark.parametrize("name,world,sp,zb", [
+    ("pipeline", 7, False, False), ("pipeline", 7, True, False), ("pipeline", 7, False, True),
+    ("pipeline", 7, True, True), ("interleaved", 7, False, False), ("interleaved", 7, True, True),
+    ("cp", 8, False, False), ("cp", 8, True, False)])
+def test_heterogeneous_pipeline_matches_the_float64_reference(store, name, world, sp, zb):
     from resihp_megatron_b200.runtime.reference_model import RefModelConfig
 
-    _check_against_reference(spawn(_pipeline, 7, store, sp, zb, 3, timeout=240), RefModelConfig(), 3)
-
-
-@pytest.mark.parametrize("sp,zb", [(False, False), (True, True)])
-def test_interleaved_pipeline_matches_reference(store, sp, zb):
-    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
-
-    out = spawn(_vpp, 7, store, sp, zb, 3, timeout=240)
-    assert {r["chunks"] for r in out.values()} == {2}
-    _check_against_reference(out, RefModelConfig(num_layers=8), 3)
-
-
-@pytest.mark.parametrize("sp", [False, True])
-def test_context_parallel_pipeline_matches_reference(store, sp):
-    from resihp_megatron_b200.runtime.reference_model import RefModelConfig
-
-    _check_against_reference(spawn(_cp, 8, store, sp, 3, timeout=240), RefModelConfig(), 3)
+    results = spawn(_train, world, store, name, sp, zb, 3, timeout=240)
+    if name == "interleaved":
+        assert {r["chunks"] for r in results.values()} == {2}
+    _assert_matches_reference(results, RefModelConfig(num_layers=8 if name == "interleaved" else 4), 3)
