@@ -81,6 +81,10 @@ def _args():
     ap.add_argument("--fp8", action="store_true",
                     help="block-scaled fp8 projections (E4M3 forward / E5M2 backward, 1x128 activation and 128x128 "
                          "weight scales, amax history 16; benchmark config 4 with --model gpt-1.3b)")
+    ap.add_argument("--chaos", choices=["auto", "on", "off"], default="auto",
+                    help="after the timed steps, run one real-process kill trial of the CPU chaos harness (8 gloo "
+                         "workers, coordinator + 2 agents; fault->commit seconds and its phases) through this arm's "
+                         "own code; 'auto' runs it at --gpus 1 only")
     ap.add_argument("--reshard", default=None,
                     help="with --parallelism tp..: after the timed steps change the layout live on the same GPUs "
                          "(e.g. tp2pp1dp4 after tp4pp1dp2: benchmark config 4's TP4 -> TP2), migrating parameters, "
@@ -126,6 +130,67 @@ def resolve_auto_layout(args, world: int) -> None:
         args.reconfig = True
 
 
+CHAOS_ITERATIONS = 40
+# The reference's chaos trial, preceded by a one-rank build of its communicator manager with the
+# defaults its demo worker uses: when that build raises, every worker of the trial fails the same
+# way at generation 1, and the error is the reason the trial cannot run.
+REFERENCE_CHAOS = """
+import json, sys
+import torch.distributed as dist
+from resihp.comm.comm_manager import ResilientCommManager
+from resihp.comm.group_spec import GroupSpec
+try:
+    store = dist.TCPStore("127.0.0.1", 0, 1, True)
+    ResilientCommManager("gloo", timeout_s=10).build(1, ["w0"], "w0", [GroupSpec("tp", (0,), "tp", True)], store=store)
+    dist.destroy_process_group()
+except Exception as e:
+    print("ResilientCommManager('gloo').build raised " + type(e).__name__ + ": " + str(e), file=sys.stderr)
+    sys.exit(3)
+from resihp.bench import chaos
+print(json.dumps(chaos.run_trial("kill", iterations={iterations})), flush=True)
+"""
+
+
+def chaos_trial(impl: str, timeout_s: float = 300.0) -> dict:
+    """One SIGKILL trial of the chaos harness of ``impl`` (``ours``: this package's
+    ``bench.chaos``; ``reference``: the installed reference's own ``resihp.bench.chaos``, stock
+    code, run from ``baseline/_ref``) in a child process; returns its fault->commit time and phases
+    or an ``unavailable`` reason.  The workers are CPU-only (gloo) and see no GPU."""
+    if impl == "ours":
+        path, code = ROOT, (f"from resihp_megatron_b200.bench import chaos; "
+                            f"chaos.main(['--fault', 'kill', '--iterations', '{CHAOS_ITERATIONS}'])")
+    else:
+        path = os.path.join(ROOT, "baseline", "_ref")
+        code = REFERENCE_CHAOS.format(iterations=CHAOS_ITERATIONS)
+    env = dict(os.environ, PYTHONPATH=path, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        proc = subprocess.run([sys.executable, "-c", code], cwd=path, env=env, capture_output=True, text=True,
+                              timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"chaos trial did not finish within {timeout_s:.0f} s"}
+    rows = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+    if proc.returncode != 0 or not rows:
+        tail = [ln for ln in (proc.stderr or "").splitlines() if ln.strip() and not ln.startswith(" ")]
+        return {"unavailable": f"chaos trial exited {proc.returncode}: " + (" | ".join(tail[-2:]) or "no output")[:400]}
+    res = json.loads(rows[-1])
+    if "breakdown" in res:  # this package's result layout
+        phases, total, exact = res["breakdown"], res["breakdown"].get("total"), res.get("exact")
+    else:  # the reference's
+        phases = {k: v for k, v in res.items() if k.endswith("_s")}
+        total, exact = res.get("total_s"), res.get("correct")
+        if not res.get("recovered", True):
+            return {"unavailable": "the reference's chaos trial did not recover", "result": res}
+    return {"metric": "fault->commit (SIGKILL of 1 of 8 CPU gloo workers, TP2xPP2xDP2 reference MLP)",
+            "value": total, "unit": "s", "higher_is_better": False, "phases_s": phases, "exact": exact,
+            "iterations": CHAOS_ITERATIONS}
+
+
+def want_chaos(args, world: int) -> bool:
+    return args.chaos == "on" or (args.chaos == "auto" and world == 1)
+
+
 def reference_unavailable(args) -> None:
     """The reference's GPU training path is Megatron-Core + Transformer Engine
     (resihp/train/megatron_binding.py); neither is installed nor fetchable offline
@@ -145,7 +210,10 @@ def reference_unavailable(args) -> None:
     if why is None:
         why = "reference Megatron path present but not wired into this bench"
     if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        out = {"impl": "reference", "unavailable": why}
+        if want_chaos(args, int(os.environ.get("WORLD_SIZE", "1"))):
+            out["chaos"] = chaos_trial("reference")
+        print(json.dumps(out), flush=True)
 
 
 class ClockSampler:
@@ -379,6 +447,8 @@ def main() -> None:
         }
         if recfg is not None:
             out["reconfig"] = recfg
+        if want_chaos(args, world):
+            out["chaos"] = chaos_trial("ours")
         print(json.dumps(out), flush=True)
     if world > 1:
         if post_group is not None:
@@ -541,6 +611,8 @@ def run_moe(args, rank: int, world: int, local: int) -> None:
                          {"experts": cfg.num_experts, "top_k": cfg.top_k})
         if recfg is not None:
             out["reconfig"] = recfg
+        if want_chaos(args, world):
+            out["chaos"] = chaos_trial("ours")
         print(json.dumps(out), flush=True)
     dist.barrier()
     trainer.close()
@@ -603,6 +675,8 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
         out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r, {"layers_per_stage": parts})
         if recfg is not None:
             out["reconfig"] = recfg
+        if want_chaos(args, world):
+            out["chaos"] = chaos_trial("ours")
         print(json.dumps(out), flush=True)
     if not alive:
         return

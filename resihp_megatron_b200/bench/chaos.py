@@ -191,3 +191,18 @@ def to_markdown(res: dict) -> str:
         cells = [f"{s[k]:.2f}" for k in (*PHASES, "total")] if "total" in s else ["-"] * (len(PHASES) + 1)
         table.append(f"| {fault} | " + " | ".join(cells) + f" | {s.get('exact')} |")
     return "\n".join(table)
+
+
+def main(argv=None) -> None:
+    """One trial, printed as one JSON line (what ``bench.py`` reads for its fault->commit key)."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--fault", choices=FAULTS, default="kill")
+    ap.add_argument("--iterations", type=int, default=40)
+    args = ap.parse_args(argv)
+    print(json.dumps(run_trial(args.fault, iterations=args.iterations)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -41,3 +41,36 @@ def test_megatron_log_parser(capsys):
     s = megatron_log.summarize(recs, skip_first=1, seq_len=4096)
     assert s["median_iter_time_ms"] == pytest.approx(4050.0) and s["final_loss"] == 10.0
     assert s["tokens_per_s"] == pytest.approx(64 * 4096 / 4.05)
+
+
+def _bench_module():
+    import importlib.util
+    import os
+
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "bench.py")
+    spec = importlib.util.spec_from_file_location("bench_root", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_bench_chaos_key_of_our_arm_is_an_exact_recovery():
+    """The ``chaos`` key of the headline line: one SIGKILL trial through this package's harness
+    recovers, reports the fault->commit phases, and the survivors stay bit-exact."""
+    bench = _bench_module()
+    res = bench.chaos_trial("ours", timeout_s=240)
+    assert "unavailable" not in res, res
+    assert res["unit"] == "s" and res["higher_is_better"] is False and res["exact"] is True
+    phases = res["phases_s"]
+    assert set(phases) >= {"detect", "abort", "plan", "build_migrate", "commit", "total"}
+    assert 0 < res["value"] == phases["total"] < 30
+
+
+def test_bench_chaos_key_of_the_reference_arm_names_a_reason_or_a_time():
+    import os
+
+    bench = _bench_module()
+    if not os.path.isdir(os.path.join(bench.ROOT, "baseline", "_ref", "resihp")):
+        pytest.skip("reference not installed under baseline/_ref")
+    res = bench.chaos_trial("reference", timeout_s=240)
+    assert ("unavailable" in res and res["unavailable"]) or res["value"] > 0
