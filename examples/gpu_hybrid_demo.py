@@ -45,7 +45,9 @@ def main(argv=None) -> None:
     torch.set_num_threads(1)
     client = WorkerClient(hb_interval=0.1).connect()
     if args.device == "cuda":
-        torch.cuda.set_device(int(os.environ.get("RESIHP_LOCAL_RANK", "0")))
+        local = int(os.environ.get("RESIHP_LOCAL_RANK", "0"))
+        # an agent that pins each worker to one GPU (CUDA_VISIBLE_DEVICES) leaves it device 0
+        torch.cuda.set_device(local if local < torch.cuda.device_count() else 0)
         device, backend = f"cuda:{torch.cuda.current_device()}", "nccl"
     else:
         device, backend = "cpu", "gloo"

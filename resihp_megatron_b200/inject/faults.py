@@ -2,7 +2,8 @@
 
 * ``FaultInjector`` lives inside a worker and fires at deterministic hook points
   ``(iteration >= iter, phase)`` -- phases ``forward``, ``backward``, ``reduce``, ``step``,
-  ``loss`` -- or after a wall-clock offset: SIGKILL itself, SIGSTOP itself (optionally resumed by
+  ``loss``, and ``boundary`` (after an iteration committed, with the GPU synchronised, so a
+  killed GPU worker leaves no kernel or collective in flight) -- or after a wall-clock offset: SIGKILL itself, SIGSTOP itself (optionally resumed by
   a SIGCONT timer), pad its compute by busy waiting (fail-slow) or delay a link.  All of it happens
   on the host: a killed or stopped process leaves between kernel launches, never inside a GPU
   operation.
@@ -131,6 +132,10 @@ class FaultInjector:
                 action(f, now)
 
     def _kill(self, f: FaultSpec, now: float) -> None:
+        stamp = os.environ.get("RESIHP_FAULT_STAMP")
+        if stamp:  # the fault instant on the machine-wide monotonic clock, for recovery timing
+            with open(stamp, "a") as fh:
+                fh.write(f"{self.worker_id} {time.monotonic():.6f}\n")
         if self._kill_fn is not None:
             self._kill_fn()
         else:

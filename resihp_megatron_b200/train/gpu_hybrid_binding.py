@@ -161,6 +161,11 @@ class GPUHybridBinding:
         self.committed[1].discard_grads()
 
     def after_commit(self, iteration: int, comms) -> None:
+        if self.hook is not None:
+            # an injected fault at the iteration boundary fires with no kernel of this worker in flight
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            self.hook(iteration, "boundary")
         if not (self.checkpointer and self.checkpoint_interval and (iteration + 1) % self.checkpoint_interval == 0):
             return
         from ..runtime.gpu_state import checkpoint_slices
