@@ -76,6 +76,44 @@ def emit(kind: str, ms: float, *, flops: float = 0.0, bytes_: float = 0.0, **ext
     return row
 
 
+# (name, N, K) of the Llama-3-8B projections; M is the token count of a micro-batch
+LLAMA3_8B_PROJ = (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336),
+                  ("head", 128256, 4096))
+
+
+def bench_gemm_llama(a, t: Timer) -> None:
+    """Every GEMM of a Llama-3-8B training step at ``--tokens`` tokens per micro-batch in the three
+    layouts of a linear layer (forward NT, dgrad with B MN-major, wgrad with both MN-major and
+    fp32 accumulation), beside cuBLAS on the same operands (``torch.matmul``; its wgrad writes
+    bf16, so it does slightly less work); the forward also without split-K."""
+    from .. import ops
+
+    M = a.tokens
+    for name, N, K in LLAMA3_8B_PROJ:
+        fl = 2.0 * M * N * K
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = torch.randn(N, K, device="cuda").bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+        dw = torch.zeros(N, K, device="cuda")
+        dwb = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+        rows = [("fwd", lambda: ops.gemm(x, w, out=y), lambda: torch.matmul(x, w.t(), out=y), [M, N, K]),
+                ("dgrad", lambda: ops.gemm(dy, w, b_t=True, out=dx), lambda: torch.matmul(dy, w, out=dx), [M, K, N]),
+                ("wgrad", lambda: ops.gemm(dy, x, a_t=True, b_t=True, out=dw, accumulate=True),
+                 lambda: torch.matmul(dy.t(), x, out=dwb), [N, K, M]),
+                ("fwd_nosplit", lambda: ops.gemm(x, w, out=y, variant=2), None, [M, N, K])]
+        for layout, ours, cublas, shape in rows:
+            r1 = emit(f"gemm_llama_{name}_{layout}", t(ours), flops=fl, shape=shape)
+            if cublas is None:
+                continue
+            r2 = emit(f"cublas_llama_{name}_{layout}", t(cublas), flops=fl, shape=shape)
+            print(json.dumps({"kernel": f"ratio_llama_{name}_{layout}", "ours_over_cublas":
+                              round(r1["tflops"] / r2["tflops"], 3)}), flush=True)
+        del x, w, dy, y, dx, dw, dwb
+    assert int(ops.error_state()[0]) == 0
+
+
 def bench_gemm(a, t: Timer) -> None:
     from .. import ops
 
@@ -85,6 +123,8 @@ def bench_gemm(a, t: Timer) -> None:
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     fl = 2.0 * M * N * K
     emit("gemm_tcgen05_nt", t(lambda: ops.gemm(x, w, out=out)), flops=fl, shape=[M, N, K])
+    emit("gemm_tcgen05_nt_pair_nosplit", t(lambda: ops.gemm(x, w, out=out, variant=2)), flops=fl, shape=[M, N, K])
+    emit("gemm_tcgen05_nt_pair_split2", t(lambda: ops.gemm(x, w, out=out, variant=3)), flops=fl, shape=[M, N, K])
     xt = x.t().contiguous()
     emit("gemm_tcgen05_tn", t(lambda: ops.gemm(xt, w, a_t=True, out=out)), flops=fl, shape=[M, N, K])
     emit("cublas", t(lambda: torch.matmul(x, w.t(), out=out)), flops=fl, shape=[M, N, K])
@@ -158,6 +198,18 @@ def bench_attention(a, t: Timer) -> None:
     o, lse = ops.attention_fwd(q, k, v, **kw)
     dout = torch.randn_like(o)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if a.fwd_variants:  # share of the softmax exponentials on the FMA pipe, 0..3 of every 8
+        ref = ops.attention_fwd(q, k, v, impl=ops.ATTN_TCGEN05, variant=0, **kw)[0].float()
+        for var in range(4):
+            o_var = ops.attention_fwd(q, k, v, impl=ops.ATTN_TCGEN05, variant=var, **kw)[0]
+            emit(f"attention_fwd_tcgen05_fma{var}of8",
+                 t(lambda: ops.attention_fwd(q, k, v, out=o, lse=lse, impl=ops.ATTN_TCGEN05, variant=var, **kw)),
+                 flops=fwd_flops, shape=[B, S, Hq, Hkv, D],
+                 max_abs_diff_vs_mufu=float((o_var.float() - ref).abs().max()))
+            emit(f"attention_bwd_tcgen05_fma{var}of8",
+                 t(lambda: ops.attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, impl=ops.ATTN_TCGEN05, variant=var,
+                                             **kw)),
+                 flops=2.5 * fwd_flops, shape=[B, S, Hq, Hkv, D])
     for name, impl in impls:
         emit(f"attention_fwd_{name}", t(lambda: ops.attention_fwd(q, k, v, out=o, lse=lse, impl=impl, **kw)),
              flops=fwd_flops, shape=[B, S, Hq, Hkv, D])
@@ -214,7 +266,7 @@ def bench_ce(a, t: Timer) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(prog="resihp-bench kernels")
-    ap.add_argument("which", choices=["gemm", "fp8", "attention", "adam", "norm", "ce", "all"])
+    ap.add_argument("which", choices=["gemm", "gemm-llama", "fp8", "attention", "adam", "norm", "ce", "all"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=8192)
@@ -223,6 +275,8 @@ def main(argv=None) -> None:
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--with-mma", action="store_true", help="also time the mma.sync attention kernels")
+    ap.add_argument("--fwd-variants", action="store_true",
+                    help="attention: also time 0-3 of every 8 softmax exponentials on the FMA pipe")
     ap.add_argument("--numel", type=int, default=1 << 28)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--hidden", type=int, default=4096)
@@ -235,7 +289,7 @@ def main(argv=None) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("kernel benchmarks need a GPU")
     t = Timer(a.warmup, a.iters, not a.no_flush)
-    table = {"gemm": bench_gemm, "fp8": bench_fp8, "attention": bench_attention, "adam": bench_adam,
+    table = {"gemm": bench_gemm, "gemm-llama": bench_gemm_llama, "fp8": bench_fp8, "attention": bench_attention, "adam": bench_adam,
              "norm": bench_norm, "ce": bench_ce}
     for name in (table if a.which == "all" else [a.which]):
         table[name](a, t)

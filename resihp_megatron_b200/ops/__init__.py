@@ -140,26 +140,30 @@ ATTN_AUTO, ATTN_MMA, ATTN_TCGEN05 = 0, 1, 2
 
 def attention_fwd(q, k, v, *, batch: int, seq: int, heads: int, kv_heads: int, head_dim: int, causal: bool = True,
                   scale: float | None = None, out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-                  impl: int = ATTN_AUTO):
+                  impl: int = ATTN_AUTO, variant: int = -1):
     """Causal GQA attention on token-major 2-D views; returns ``(o, lse)``.  ``impl``: the
     tcgen05 kernel (head dim 128, causal, seq % 256 == 0) with the mma.sync kernel for other
-    shapes (``ATTN_AUTO``), or one of them explicitly."""
+    shapes (``ATTN_AUTO``), or one of them explicitly.  ``variant`` (tcgen05 kernel, tuning):
+    how many of every 8 softmax exponentials run as an FMA-pipe polynomial instead of on the
+    MUFU unit (0-3; -1 = the built-in default)."""
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
     o = torch.empty((q.shape[0], heads * head_dim), dtype=q.dtype, device=q.device) if out is None else out
     if lse is None:
         lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
-    ext().attention_fwd(q, k, v, o, lse, batch, seq, heads, kv_heads, head_dim, float(scale), bool(causal), int(impl))
+    ext().attention_fwd(q, k, v, o, lse, batch, seq, heads, kv_heads, head_dim, float(scale), bool(causal), int(impl),
+                        int(variant))
     count(1)
     return o, lse
 
 
 def attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, *, batch: int, seq: int, heads: int, kv_heads: int,
-                  head_dim: int, causal: bool = True, scale: float | None = None, impl: int = ATTN_AUTO):
+                  head_dim: int, causal: bool = True, scale: float | None = None, impl: int = ATTN_AUTO,
+                  variant: int = -1):
     """Writes dq/dk/dv (token-major 2-D views, may be column slices of one buffer).  ``impl`` as
     in ``attention_fwd``: the tcgen05 kernels (head dim 128, causal, seq % 128 == 0) or the
     mma.sync kernels."""
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
     delta = torch.empty((batch, heads, seq), dtype=torch.float32, device=q.device)
     ext().attention_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, batch, seq, heads, kv_heads, head_dim, float(scale),
-                        bool(causal), int(impl))
+                        bool(causal), int(impl), int(variant))
     count(3)

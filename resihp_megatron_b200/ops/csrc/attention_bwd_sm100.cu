@@ -33,6 +33,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "exp2_fma.cuh"
 #include "sm100.cuh"
 
 namespace rb {
@@ -63,12 +64,6 @@ struct BwdParams {
   int* err;
 };
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 __device__ __forceinline__ bool warp_wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
@@ -88,15 +83,14 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int s) {
 __device__ __forceinline__ uint32_t packed_col(int s) { return (s >> 2) * 64 + (s & 3) * 8; }
 
 // Load 64 fp32 columns of this thread's TMEM lane.
+// Both 32-column loads are in flight before the one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t addr, float (&v)[64]) {
-  uint32_t t[32];
+  uint32_t t[2][32];
+  tmem_ld_32x32b_x32(addr, t[0]);
+  tmem_ld_32x32b_x32(addr + 32, t[1]);
+  tmem_ld_wait();
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    tmem_ld_32x32b_x32(addr + c * 32, t);
-    tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[i]);
-  }
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(t[i >> 5][i & 31]);
 }
 
 // Write 64 fp32 values of this thread's row as bf16 to global memory (128 contiguous bytes).
@@ -144,6 +138,7 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, long l
 }
 
 // ------------------------------------------------------------------------------ dK / dV
+template <int kFma>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -310,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int c = c4 * 4 + e;
-          float x = ex2(fmaf(pv[c], p.scale_log2, lv[e]));
+          float x = ex2_mixed<kFma>(fmaf(pv[c], p.scale_log2, lv[e]), c);
           if (diag && X * 64 + c < r) x = 0.f;  // query before key: masked
           pv[c] = x;
         }
@@ -370,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------ dQ
+template <int kFma>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -517,22 +513,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool diag = jj == i;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        float x = ex2(fmaf(pv[c], p.scale_log2, nl));
+        float x = ex2_mixed<kFma>(fmaf(pv[c], p.scale_log2, nl), c);
         if (diag && X * 64 + c > r) x = 0.f;  // key after query: masked
         pv[c] = x;
       }
       if (!(ok = warp_wait_bar(bar_dp, jj & 1, abort_flag, p.err))) break;
       tc_fence_after();
       {
-        uint32_t t[32], out[32];
+        uint32_t t[2][32], out[32];
+        tmem_ld_32x32b_x32(tdP + lane_off + X * 64, t[0]);
+        tmem_ld_32x32b_x32(tdP + lane_off + X * 64 + 32, t[1]);
+        tmem_ld_wait();
 #pragma unroll
         for (int c32 = 0; c32 < 2; ++c32) {
-          tmem_ld_32x32b_x32(tdP + lane_off + X * 64 + c32 * 32, t);
-          tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float a0 = pv[c32 * 32 + 2 * c] * (__uint_as_float(t[2 * c]) - dl);
-            const float a1 = pv[c32 * 32 + 2 * c + 1] * (__uint_as_float(t[2 * c + 1]) - dl);
+            const float a0 = pv[c32 * 32 + 2 * c] * (__uint_as_float(t[c32][2 * c]) - dl);
+            const float a1 = pv[c32 * 32 + 2 * c + 1] * (__uint_as_float(t[c32][2 * c + 1]) - dl);
             out[c32 * 16 + c] = pack_bf16x2(a0, a1);
           }
         }
@@ -560,11 +557,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool misaligned(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 
+// Exponentials per 8 score columns evaluated on the FMA pipe (ex2_fma) by default.
+constexpr int kDefaultFmaShare = 2;
+
+template <int kFma>
+int launch_bwd(dim3 grid_dkdv, dim3 grid_dq, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const CUtensorMap& tdo, const BwdParams& p, cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_dkdv_sm100_kernel<kFma>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDkdv);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_bwd_dq_sm100_kernel<kFma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSmemDq);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr = true;
+  }
+  attn_bwd_dkdv_sm100_kernel<kFma><<<grid_dkdv, kThreads, kSmemDkdv, stream>>>(tq, tk, tv, tdo, p);
+  attn_bwd_dq_sm100_kernel<kFma><<<grid_dq, kThreads, kSmemDq, stream>>>(tq, tk, tv, tdo, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 // Returns 1 when the shape is not handled here (the caller uses the mma.sync path).
-// `nl2` is scratch of B * Hq * S floats; `a.delta` receives rowsum(dO * O).
-int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t stream) {
+// `nl2` is scratch of B * Hq * S floats; `a.delta` receives rowsum(dO * O).  ``variant``:
+// exponentials per 8 score columns on the FMA pipe (0-3), or -1 for the default.
+int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t stream, int variant) {
   if (D != 128 || !a.causal || a.S % kTile != 0 || a.Hq % a.Hkv != 0) return 1;
   if (misaligned(a.q) || misaligned(a.k) || misaligned(a.v) || misaligned(a.o) || misaligned(a.dout) ||
       misaligned(a.dq) || misaligned(a.dk) || misaligned(a.dv) || misaligned(a.lse) || misaligned(a.delta) ||
@@ -585,15 +604,6 @@ int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaS
   if (make_tmap_bf16_2d(&tk, a.k, static_cast<uint64_t>(a.Hkv) * kTile, T, a.k_stride, 64, kTile)) return -21;
   if (make_tmap_bf16_2d(&tv, a.v, static_cast<uint64_t>(a.Hkv) * kTile, T, a.v_stride, 64, kTile)) return -22;
   if (make_tmap_bf16_2d(&tdo, a.dout, static_cast<uint64_t>(a.Hq) * kTile, T, a.do_stride, 64, kTile)) return -23;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_bwd_dkdv_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDkdv);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_bwd_dq_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    attr = true;
-  }
   BwdParams p{nl2,
               a.delta,
               reinterpret_cast<__nv_bfloat16*>(a.dq),
@@ -610,9 +620,14 @@ int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaS
               a.scale * kLog2e,
               err};
   const int nb = a.S / kTile;
-  attn_bwd_dkdv_sm100_kernel<<<nb * a.Hkv * a.B, kThreads, kSmemDkdv, stream>>>(tq, tk, tv, tdo, p);
-  attn_bwd_dq_sm100_kernel<<<nb * a.Hq * a.B, kThreads, kSmemDq, stream>>>(tq, tk, tv, tdo, p);
-  return static_cast<int>(cudaGetLastError());
+  const dim3 grid_dkdv(nb * a.Hkv * a.B), grid_dq(nb * a.Hq * a.B);
+  switch (variant < 0 ? kDefaultFmaShare : variant) {
+    case 0: return launch_bwd<0>(grid_dkdv, grid_dq, tq, tk, tv, tdo, p, stream);
+    case 1: return launch_bwd<1>(grid_dkdv, grid_dq, tq, tk, tv, tdo, p, stream);
+    case 2: return launch_bwd<2>(grid_dkdv, grid_dq, tq, tk, tv, tdo, p, stream);
+    case 3: return launch_bwd<3>(grid_dkdv, grid_dq, tq, tk, tv, tdo, p, stream);
+    default: return -24;
+  }
 }
 
 }  // namespace rb

@@ -25,6 +25,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "exp2_fma.cuh"
 #include "sm100.cuh"
 
 namespace rb {
@@ -56,11 +57,7 @@ __device__ __forceinline__ bool warp_wait_bar(uint32_t bar, uint32_t parity, vol
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+__device__ __forceinline__ float ex2(float x) { return ex2_mufu(x); }
 
 // K-major operand descriptor for k-step s (16 columns) of a [128 x 128] tile stored as two
 // 128B-swizzled halves of 64 columns.
@@ -73,6 +70,7 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int s) {
   return make_smem_desc(base + s * 2048, kHalf, 1024, kSwizzle128B);
 }
 
+template <int kFma>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, FwdParams p) {
@@ -244,28 +242,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j <= jmax; ++j) {
       if (!(ok = warp_wait_bar(bar_s(X), j & 1, abort_flag, p.err))) break;
       tc_fence_after();
-      float v[128];
-      {
-        uint32_t t[32];
+      // Two passes over S in 64-column halves (two 32-column loads in flight per wait): the row max
+      // first, then P.  Re-reading S from TMEM is cheap and keeps 64 scores, not 128, in registers.
+      // The diagonal block masks key > query to -inf.
+      const bool diag = j == jmax;
+      float m8[8];  // 8 independent max chains: one chain of dependent max operations is latency bound
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld_32x32b_x32(s_addr + c * 32, t);
-          tmem_ld_wait();
+      for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(t[i]) * p.scale_log2;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t t[2][32];
+        tmem_ld_32x32b_x32(s_addr + half * 64, t[0]);
+        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, t[1]);
+        tmem_ld_wait();
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (half * 64 + c > r) t[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-      }
-      float mx = -INFINITY;
-      if (j == jmax) {  // diagonal block: key index > query index is masked
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          if (c > r) v[c] = -INFINITY;
-          mx = fmaxf(mx, v[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, v[c]);
+        for (int c = 0; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(t[c >> 5][c & 31]));
       }
+      // the scale is positive, so the max of scaled scores is the scaled raw max
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
       const bool need = mx > m_ref + kRescaleThreshold;
       float alpha = 1.f;
       if (need) {
@@ -277,30 +277,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         // O is rescaled in place once the previous PV finished writing it
         if (!(ok = warp_wait_bar(bar_o(X), (j - 1) & 1, abort_flag, p.err))) break;
         tc_fence_after();
-        uint32_t t[32];
+        uint32_t o[32];
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld_32x32b_x32(o_addr + c * 32, t);
+          tmem_ld_32x32b_x32(o_addr + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-          tmem_st_32x32b_x32(o_addr + c * 32, t);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(o_addr + c * 32, o);
         }
         tmem_st_wait();
       }
-      float sum = 0.f;
+      // P = 2^(s * scale_log2 - m): one FFMA + one exp2 per score.  bf16 pairs overwrite the first
+      // half of S's columns: half h's pairs land on columns [32h, 32h + 32), all of which hold
+      // scores already read into registers.
+      const float neg_m = -m_ref;
+      float s8[8];
 #pragma unroll
-      for (int c32 = 0; c32 < 2; ++c32) {
-        uint32_t packed[32];
+      for (int k = 0; k < 8; ++k) s8[k] = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e0 = ex2(v[c32 * 64 + 2 * i] - m_ref);
-          const float e1 = ex2(v[c32 * 64 + 2 * i + 1] - m_ref);
-          sum += e0 + e1;
-          packed[i] = pack_bf16x2(e0, e1);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t t[2][32];
+        tmem_ld_32x32b_x32(s_addr + half * 64, t[0]);
+        tmem_ld_32x32b_x32(s_addr + half * 64 + 32, t[1]);
+        tmem_ld_wait();
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (half * 64 + c > r) t[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-        tmem_st_32x32b_x32(s_addr + c32 * 32, packed);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // 16 scores -> 8 packed columns per store
+          uint32_t packed[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int c0 = g * 16 + 2 * i, c1 = c0 + 1;
+            const float e0 = ex2_mixed<kFma>(fmaf(__uint_as_float(t[c0 >> 5][c0 & 31]), p.scale_log2, neg_m), c0);
+            const float e1 = ex2_mixed<kFma>(fmaf(__uint_as_float(t[c1 >> 5][c1 & 31]), p.scale_log2, neg_m), c1);
+            s8[c0 & 7] += e0;
+            s8[c1 & 7] += e1;
+            packed[i] = pack_bf16x2(e0, e1);
+          }
+          tmem_st_32x32b_x8(s_addr + half * 32 + g * 8, packed);
+        }
       }
+      const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       tmem_st_wait();
       l += sum;
       tc_fence_before();
@@ -339,10 +360,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Exponentials per 8 score columns evaluated on the FMA pipe (ex2_fma) by default.
+constexpr int kDefaultFmaShare = 2;
+
+template <int kFma>
+int launch_fwd(int grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
+               cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_sm100_kernel<kFma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr = true;
+  }
+  attn_fwd_sm100_kernel<kFma><<<grid, kThreads, kSmem, stream>>>(tq, tk, tv, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 // Returns 1 when the shape is not handled by this kernel (the caller uses the mma.sync path).
-int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t stream) {
+// ``variant``: exponentials per 8 score columns on the FMA pipe (0-3), or -1 for the default.
+int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t stream, int variant) {
   if (D != 128 || !a.causal || a.S % 256 != 0 || a.Hq % a.Hkv != 0) return 1;
   if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
        reinterpret_cast<uintptr_t>(a.o)) & 15)
@@ -353,16 +392,16 @@ int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t stream)
   if (make_tmap_bf16_2d(&tq, a.q, static_cast<uint64_t>(a.Hq) * 128, T, a.q_stride, 64, 128)) return -20;
   if (make_tmap_bf16_2d(&tk, a.k, static_cast<uint64_t>(a.Hkv) * 128, T, a.k_stride, 64, 128)) return -21;
   if (make_tmap_bf16_2d(&tv, a.v, static_cast<uint64_t>(a.Hkv) * 128, T, a.v_stride, 64, 128)) return -22;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    attr = true;
-  }
   FwdParams p{reinterpret_cast<__nv_bfloat16*>(a.o), a.o_stride, a.lse, a.B, a.S, a.Hq, a.Hkv,
               a.scale * 1.4426950408889634f, err};
-  attn_fwd_sm100_kernel<<<(a.S / 256) * a.Hq * a.B, kThreads, kSmem, stream>>>(tq, tk, tv, p);
-  return static_cast<int>(cudaGetLastError());
+  const int grid = (a.S / 256) * a.Hq * a.B;
+  switch (variant < 0 ? kDefaultFmaShare : variant) {
+    case 0: return launch_fwd<0>(grid, tq, tk, tv, p, stream);
+    case 1: return launch_fwd<1>(grid, tq, tk, tv, p, stream);
+    case 2: return launch_fwd<2>(grid, tq, tk, tv, p, stream);
+    case 3: return launch_fwd<3>(grid, tq, tk, tv, p, stream);
+    default: return -23;
+  }
 }
 
 }  // namespace rb

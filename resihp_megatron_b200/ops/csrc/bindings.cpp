@@ -89,10 +89,16 @@ void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, to
     if (epi == 3) out.copy_(*residual);
     return;
   }
+  const int sms = num_sms(a.get_device());
+  const int splits = rb::gemm_pair_splits(M, N, K, static_cast<int>(variant), sms);
+  // split-K workspace from the caching allocator: stream-ordered, so it is reused only after this
+  // launch
+  torch::Tensor ws;
+  if (splits > 1) ws = torch::empty({rb::gemm_split_ws_bytes(M, N, splits)}, a.options().dtype(torch::kUInt8));
   const int rc = rb::gemm_bf16(a.data_ptr(), lda, a_t, b.data_ptr(), ldb, b_t, out.data_ptr(), ldd, rptr, ldr,
-                               M, N, K, static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a),
-                               num_sms(a.get_device()), at::cuda::getCurrentCUDAStream(),
-                               static_cast<int>(variant));
+                               M, N, K, static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a), sms,
+                               at::cuda::getCurrentCUDAStream(), static_cast<int>(variant),
+                               splits > 1 ? ws.data_ptr() : nullptr, splits);
   TORCH_CHECK(rc == 0, "gemm_bf16 failed with code ", rc);
 }
 
@@ -264,9 +270,10 @@ static rb::AttnArgs attn_args(const torch::Tensor& q, const torch::Tensor& k, co
 
 // q/k/v/o: 2-D [B*S, heads*D] views with contiguous rows (row stride may exceed heads*D).
 // impl: 0 = tcgen05 kernel when the shape allows, else mma.sync; 1 = mma.sync; 2 = tcgen05 only.
+// variant (tcgen05 kernels): exponentials per 8 score columns on the FMA pipe, -1 = default.
 void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, torch::Tensor& o,
                    torch::Tensor& lse, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, double scale,
-                   bool causal, int64_t impl) {
+                   bool causal, int64_t impl, int64_t variant) {
   for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "attention operands must be 2-D bf16 CUDA views with contiguous rows");
@@ -274,7 +281,7 @@ void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
   const c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k, v, o, lse, B, S, Hq, Hkv, scale, causal);
   if (impl != 1) {
-    const int rc = rb::attention_fwd_sm100(a, D, err_ptr(q), cur_stream());
+    const int rc = rb::attention_fwd_sm100(a, D, err_ptr(q), cur_stream(), static_cast<int>(variant));
     if (rc == 0) return;
     TORCH_CHECK(rc == 1 && impl == 0, "attention_fwd (tcgen05) failed with code ", rc);
   }
@@ -284,7 +291,7 @@ void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
 void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& o,
                    const torch::Tensor& dout, const torch::Tensor& lse, torch::Tensor& delta, torch::Tensor& dq,
                    torch::Tensor& dk, torch::Tensor& dv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
-                   double scale, bool causal, int64_t impl) {
+                   double scale, bool causal, int64_t impl, int64_t variant) {
   for (const torch::Tensor* t : std::initializer_list<const torch::Tensor*>{&q, &k, &v, &o, &dout, &dq, &dk, &dv})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                 "attention operands must be 2-D bf16 CUDA views with contiguous rows");
@@ -301,7 +308,8 @@ void attention_bwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
   TORCH_CHECK(delta.numel() >= B * Hq * S, "delta needs B * Hq * S floats");
   if (impl != 1) {
     auto nl2 = torch::empty_like(delta);
-    const int rc = rb::attention_bwd_sm100(a, D, nl2.data_ptr<float>(), err_ptr(q), cur_stream());
+    const int rc = rb::attention_bwd_sm100(a, D, nl2.data_ptr<float>(), err_ptr(q), cur_stream(),
+                                           static_cast<int>(variant));
     if (rc == 0) return;
     TORCH_CHECK(rc == 1 && impl == 0, "attention_bwd (tcgen05) failed with code ", rc);
   }
@@ -799,7 +807,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy", &cross_entropy);
   m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"),
-        py::arg("impl") = 0);
+        py::arg("impl") = 0, py::arg("variant") = -1);
   m.def("tp_ag_ready_words", [](int64_t M, int64_t K) { return rb::gemm_ag_ready_words(M, K); });
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
@@ -836,5 +844,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("residual") = py::none());
   m.def("attention_bwd", &attention_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"),
         py::arg("lse"), py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("S"),
-        py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0);
+        py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("scale"), py::arg("causal"), py::arg("impl") = 0,
+        py::arg("variant") = -1);
 }

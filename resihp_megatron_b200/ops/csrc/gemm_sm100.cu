@@ -54,6 +54,14 @@ struct GemmArgs {
   void* ag_dst;
   int* ag_ready;
   const int* abort_word;
+  // split-K of the CTA-pair kernel: `splits` (1 or 2) work units per output tile, each over its
+  // share of the k-blocks.  Every unit's epilogue warp stores its 32 x 256 fp32 partial into its
+  // own workspace slot and counts itself on the tile's (CTA, warp) counter; the last to arrive
+  // adds the slots in a fixed order and runs the epilogue (so the result does not depend on which
+  // unit finishes first).
+  int splits;
+  float* split_ws;
+  int* split_cnt;
 };
 
 template <int BN>
@@ -748,6 +756,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const int kblocks = (p.K + BK - 1) / BK;
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int num_units = num_tiles * splits;       // unit u: tile u / splits, k share u % splits
+  const int kb_share = (kblocks + splits - 1) / splits;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -755,13 +766,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
-      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += num_pairs) {
+      for (int u = pair; u < num_units && !*abort_flag; u += num_pairs) {
+        const int tile = u / splits;
+        const int kb_lo = (u - tile * splits) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
         int mb, nb;
         tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
         const int m0 = mb * 2 * BM + static_cast<int>(cta) * BM;
         const int n0 = nb * C::BN + static_cast<int>(cta) * C::BNH;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
             ok = false;
             break;
@@ -807,12 +820,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
-      for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+      for (int u = pair; u < num_units; u += num_pairs) {
+        const int kb_lo = (u % splits) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
         if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
             ok = false;
             break;
@@ -826,7 +840,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                                      : make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd = B_MN ? make_smem_desc(b_base + k * 2048, 8192, 1024, kSwizzle128B)
                                      : make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
-            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_bar(stage));
           umma_commit_pair(mapa_shared(empty_bar(stage), 1));
@@ -850,27 +864,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const uint32_t release = leader ? 0u : mapa_shared(tempty_bar(0), 0);  // peer: leader's barrier
     int acc = 0;
     uint32_t aphase = 0;
-    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+    for (int u = pair; u < num_units; u += num_pairs) {
+      const int tile = u / splits, share = u - tile * splits;
       int mb, nb;
       tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
       if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = mb * 2 * BM + static_cast<int>(cta) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
+      const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::BN;
+      // workspace slots of this (tile, CTA, warp): `splits` consecutive 32 x 256 fp32 blocks
+      const long long slot0 = static_cast<long long>((tile * 2 + static_cast<int>(cta)) * 4 + q) * splits;
+      if (splits == 1) {
 #pragma unroll 1
-      for (int c = 0; c < C::BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::BN + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nb * C::BN + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        store_chunk<EPI>(r, row, col0, p);
+        for (int c = 0; c < C::BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_acc + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * C::BN + c * 32;
+          if (!row_ok || col0 >= p.N) continue;
+          store_chunk<EPI>(r, row, col0, p);
+        }
+      } else {
+        // this unit's partial -> its slot, column-major (each store is one coalesced 128-byte row)
+        float* mine = p.split_ws + (slot0 + share) * (32 * C::BN);
+#pragma unroll 1
+        for (int c = 0; c < C::BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_acc + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mine[(c * 32 + i) * 32 + lane] = __uint_as_float(r[i]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         if (leader) mbar_arrive(tempty_bar(acc));
         else mbar_arrive_cluster(release + acc * 8);
+      }
+      if (splits > 1) {
+        // the accumulator is released already; the unit that arrives last reduces the slots
+        __threadfence();
+        __syncwarp();
+        int* cnt = p.split_cnt + (tile * 2 + static_cast<int>(cta)) * 4 + q;
+        int last = 0;
+        if (lane == 0) last = atomicAdd(cnt, 1) == splits - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          const float* s0 = p.split_ws + slot0 * (32 * C::BN);
+#pragma unroll 1
+          for (int c = 0; c < C::BN / 32; ++c) {
+            const int col0 = nb * C::BN + c * 32;
+            uint32_t r[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float v = __ldcg(s0 + (c * 32 + i) * 32 + lane);
+              for (int sh = 1; sh < splits; ++sh) v += __ldcg(s0 + sh * (32 * C::BN) + (c * 32 + i) * 32 + lane);
+              r[i] = __float_as_uint(v);
+            }
+            if (row_ok && col0 < p.N) store_chunk<EPI>(r, row, col0, p);
+          }
+          if (lane == 0) *cnt = 0;  // ready for the next launch (the host also clears it first)
+        }
       }
       acc ^= 1;
       if (acc == 0) aphase ^= 1;
@@ -959,7 +1016,8 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   }
   const int tiles = ((a.M + 2 * C::BM - 1) / (2 * C::BM)) * ((a.N + C::BN - 1) / C::BN);
   int pairs = num_sms / 2;
-  if (tiles < pairs) pairs = tiles;
+  const int units = tiles * (a.splits > 1 ? a.splits : 1);
+  if (units < pairs) pairs = units;
   kern<<<2 * pairs, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, a);
   return static_cast<int>(cudaGetLastError());
 }
@@ -1052,11 +1110,42 @@ int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* r
               : launch_gemm<256, false, false, kEpiScatterBF16>(ta, tb, a, num_sms, stream);
 }
 
+static bool use_pair_kernel(int M, int N, int variant) {
+  return variant == 2 || variant == 3 || (variant == 0 && M >= 512 && N >= 256);
+}
+
+// Work units per output tile of the CTA-pair kernel.  Split-K in two shares pays when the tile
+// count leaves the last wave of SM pairs mostly idle (e.g. 256 tiles = 3.46 waves on 74 pairs ->
+// 512 units = 6.92 waves) and each share keeps >= 32 k-blocks; tile counts above 6 waves (where
+// the tail matters little) keep one unit per tile, which also bounds the workspace.
+int gemm_pair_splits(int M, int N, int K, int variant, int num_sms) {
+  if (!use_pair_kernel(M, N, variant) || variant == 2) return 1;
+  const int kblocks = (K + 63) / 64;
+  if (variant == 3) return kblocks >= 2 ? 2 : 1;
+  const long long pairs = num_sms / 2;
+  const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  if (pairs <= 0 || kblocks < 64 || tiles > 6 * pairs) return 1;
+  auto efficiency = [&](long long units) {
+    const long long waves = (units + pairs - 1) / pairs;
+    return static_cast<double>(units) / static_cast<double>(waves * pairs);
+  };
+  return efficiency(2 * tiles) > efficiency(tiles) + 0.04 ? 2 : 1;
+}
+
+// Workspace of a split launch: one 32 x 256 fp32 slot per (tile, CTA, epilogue warp, share),
+// then one counter per (tile, CTA, epilogue warp).
+long long gemm_split_ws_bytes(int M, int N, int splits) {
+  const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  return tiles * 8 * splits * (32LL * 256 * 4) + tiles * 8 * 4;
+}
+
 // A(m,k) = a_mn ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_mn ? B[k*ldb + n] : B[n*ldb + k].
 // Returns 0 on success, a negative value for a bad argument, else a CUDA error code.
+// `split_ws` (gemm_split_ws_bytes(M, N, splits) bytes, 16-byte aligned) is needed when
+// `splits` (gemm_pair_splits) is above 1.
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn,
               void* D, long long ldd, const void* R, long long ldr, int M, int N, int K, int epi,
-              float alpha, int* err, int num_sms, cudaStream_t stream, int variant) {
+              float alpha, int* err, int num_sms, cudaStream_t stream, int variant, void* split_ws, int splits) {
   if (M <= 0 || N <= 0 || K <= 0) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
   if ((lda * 2) % 16 || (ldb * 2) % 16) return -5;
@@ -1066,8 +1155,9 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
   const int BN = (N <= 128) ? 128 : 256;
   CUtensorMap ta, tb;
   int rc;
-  // variant: 0 auto (CTA pair for large tiles), 1 single CTA, 2 CTA pair
-  const bool use_pair = variant == 2 || (variant == 0 && M >= 512 && N >= 256);
+  // variant: 0 auto (CTA pair for large tiles, split-K where it fills the last wave), 1 single
+  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced
+  const bool use_pair = use_pair_kernel(M, N, variant);
   if (use_pair) {
     if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
     else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
@@ -1076,6 +1166,16 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
     else rc = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, 64);
     if (rc) return -100 - rc;
     GemmArgs ga{M, N, K, D, ldd, reinterpret_cast<const __nv_bfloat16*>(R), ldr, alpha, err};
+    ga.splits = 1;
+    if (splits > 1) {
+      if (split_ws == nullptr || (reinterpret_cast<uintptr_t>(split_ws) & 15)) return -8;
+      const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+      ga.splits = splits;
+      ga.split_ws = reinterpret_cast<float*>(split_ws);
+      ga.split_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(split_ws) + tiles * 8 * splits * (32LL * 256 * 4));
+      const cudaError_t e = cudaMemsetAsync(ga.split_cnt, 0, static_cast<size_t>(tiles * 8 * 4), stream);
+      if (e != cudaSuccess) return static_cast<int>(e);
+    }
     switch (epi) {
       case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
       case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream);

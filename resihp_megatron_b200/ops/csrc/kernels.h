@@ -12,7 +12,10 @@ namespace rb {
 
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* D,
               long long ldd, const void* R, long long ldr, int M, int N, int K, int epi, float alpha,
-              int* err, int num_sms, cudaStream_t stream, int variant = 0);
+              int* err, int num_sms, cudaStream_t stream, int variant = 0, void* split_ws = nullptr, int splits = 1);
+// Split-K plan of the CTA-pair GEMM (1 = none) and the workspace bytes a split launch needs.
+int gemm_pair_splits(int M, int N, int K, int variant, int num_sms);
+long long gemm_split_ws_bytes(int M, int N, int splits);
 
 int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s);
 int rmsnorm_bwd_blocks(int T);
@@ -81,7 +84,7 @@ struct AttnBwdArgs {
   int causal;
 };
 int attention_fwd_mma(const AttnArgs& a, int D, cudaStream_t s);
-int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t s);
+int attention_fwd_sm100(const AttnArgs& a, int D, int* err, cudaStream_t s, int variant = -1);
 int attention_bwd_mma(const AttnBwdArgs& a, int D, cudaStream_t s);
 // Symmetric peer memory (symm.cu).
 int symm_signal_bytes(int world);
@@ -142,5 +145,5 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
              const void* R = nullptr, long long ldr = 0, void* const* rs_dst = nullptr, int world = 0,
              int rs_slot = 0);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
-int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s);
+int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s, int variant = -1);
 }  // namespace rb

@@ -38,6 +38,30 @@ def test_tcgen05_attention_forward(B, S, Hq, Hkv, amp):
     assert (o.float() - o2.float()).abs().max().item() < 3e-2 * ref.abs().max().item() + 1e-2
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+def test_tcgen05_attention_forward_fma_exp2_shares(variant):
+    """Every share of softmax exponentials on the FMA-pipe polynomial (0-3 of 8) against the fp32
+    reference; the polynomial's relative error (8.6e-5) is below bf16 resolution, so the outputs
+    stay within a bf16 rounding of the all-MUFU kernel."""
+    from resihp_megatron_b200 import ops
+
+    B, S, Hq, Hkv, D = 1, 768, 4, 2, 128
+    torch.manual_seed(2)
+    qkv = (torch.randn(B * S, (Hq + 2 * Hkv) * D, device="cuda") * 2.0).bfloat16()
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D:]
+    kw = dict(batch=B, seq=S, heads=Hq, kv_heads=Hkv, head_dim=D)
+    o, lse = ops.attention_fwd(q, k, v, impl=ops.ATTN_TCGEN05, variant=variant, **kw)
+    o0, lse0 = ops.attention_fwd(q, k, v, impl=ops.ATTN_TCGEN05, variant=0, **kw)
+    ref, ref_lse = _ref(q, k, v, B, S, Hq, Hkv, D)
+    torch.cuda.synchronize()
+    assert int(ops.error_state()[0]) == 0
+    scale = ref.abs().max().item()
+    assert (o.float() - ref).abs().max().item() < 2e-2 * scale + 1e-2
+    assert (lse.view(B, Hq, S) - ref_lse).abs().max().item() < 1e-2
+    assert (o.float() - o0.float()).abs().max().item() < 1e-2 * scale + 4e-3
+    assert (lse - lse0).abs().max().item() < 1e-3
+
+
 def _ref_grads(q, k, v, dout, B, S, Hq, Hkv, D):
     qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
     o, _ = _ref(qf, kf, vf, B, S, Hq, Hkv, D)
@@ -74,3 +98,32 @@ def test_tcgen05_attention_backward(B, S, Hq, Hkv):
         assert (got.float() - mma.float()).abs().max().item() < 3e-2 * scale + 1e-2, name
     for a, b in zip(outs["tc"], outs["tc2"]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+def test_tcgen05_attention_backward_fma_exp2_shares(variant):
+    """dQ/dK/dV with 0-3 of every 8 probability exponentials on the FMA-pipe polynomial against
+    fp32 autograd and the all-MUFU kernels; each variant stays bitwise deterministic."""
+    from resihp_megatron_b200 import ops
+
+    B, S, Hq, Hkv, D = 1, 512, 4, 2, 128
+    torch.manual_seed(3)
+    q = torch.randn(B * S, Hq * D, device="cuda").bfloat16()
+    k = torch.randn(B * S, Hkv * D, device="cuda").bfloat16()
+    v = torch.randn(B * S, Hkv * D, device="cuda").bfloat16()
+    dout = torch.randn(B * S, Hq * D, device="cuda").bfloat16()
+    kw = dict(batch=B, seq=S, heads=Hq, kv_heads=Hkv, head_dim=D)
+    o, lse = ops.attention_fwd(q, k, v, impl=ops.ATTN_TCGEN05, variant=0, **kw)
+    outs = []
+    for var in (variant, variant, 0):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        ops.attention_bwd(q, k, v, o, dout, lse, dq, dk, dv, impl=ops.ATTN_TCGEN05, variant=var, **kw)
+        outs.append((dq, dk, dv))
+    torch.cuda.synchronize()
+    assert int(ops.error_state()[0]) == 0
+    ref = _ref_grads(q, k, v, dout, B, S, Hq, Hkv, D)
+    for got, again, mufu, want, name in zip(outs[0], outs[1], outs[2], ref, ("dq", "dk", "dv")):
+        scale = want.abs().max().item()
+        assert (got.float() - want).abs().max().item() < 2e-2 * scale + 1e-2, name
+        assert (got.float() - mufu.float()).abs().max().item() < 1e-2 * scale + 4e-3, name
+        assert torch.equal(got, again), name

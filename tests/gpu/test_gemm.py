@@ -102,3 +102,48 @@ def test_gemm_cta_pair_variant(M, N, K, a_t, b_t):
     assert torch.allclose(f32, ref, rtol=1e-4, atol=1e-3)
     assert torch.allclose(acc, base + ref, rtol=1e-4, atol=1e-3)
     assert (res.float() - (ref + r.float())).abs().max().item() <= 1e-2 * scale + 2e-2
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 1024), (1000, 520, 1000), (256, 256, 192)])
+def test_gemm_split_k_variant(M, N, K, a_t, b_t):
+    """Split-K of the CTA-pair kernel (variant 3: two k shares per tile, partials reduced by the
+    last-arriving unit) against fp32 with every epilogue, against the unsplit pair kernel, and
+    bitwise equal from run to run (the reduction order does not depend on arrival order)."""
+    from resihp_megatron_b200.ops.gemm import error_state, gemm
+
+    a, b = _mk(M, N, K, a_t, b_t, seed=11)
+    ref = _ref(a, b, a_t, b_t)
+    scale = ref.abs().max().item()
+    split = gemm(a, b, a_t=a_t, b_t=b_t, variant=3)
+    again = gemm(a, b, a_t=a_t, b_t=b_t, variant=3)
+    whole = gemm(a, b, a_t=a_t, b_t=b_t, variant=2)
+    f32 = gemm(a, b, a_t=a_t, b_t=b_t, out_dtype=torch.float32, variant=3)
+    base = torch.randn(M, N, device="cuda")
+    acc = base.clone()
+    gemm(a, b, a_t=a_t, b_t=b_t, out=acc, accumulate=True, variant=3)
+    r = torch.randn(M, N, device="cuda").bfloat16()
+    res = gemm(a, b, a_t=a_t, b_t=b_t, residual=r, variant=3, alpha=0.5)
+    torch.cuda.synchronize()
+    assert int(error_state()[0]) == 0
+    assert (split.float() - ref).abs().max().item() <= 1e-2 * scale + 1e-2
+    assert torch.equal(split, again)
+    assert (split.float() - whole.float()).abs().max().item() <= 1e-2 * scale + 1e-2
+    assert torch.allclose(f32, ref, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(acc, base + ref, rtol=1e-4, atol=1e-3)
+    assert (res.float() - (0.5 * ref + r.float())).abs().max().item() <= 1e-2 * scale + 2e-2
+
+
+def test_gemm_auto_split_on_a_partial_wave_shape():
+    """M = N = K = 4096 is 256 pair tiles (3.46 waves on 74 pairs), which the default variant
+    splits in two k shares; results stay within bf16 rounding of fp32 and deterministic."""
+    from resihp_megatron_b200.ops.gemm import error_state, gemm
+
+    a, b = _mk(4096, 4096, 4096, False, True, seed=12)
+    out = gemm(a, b, b_t=True)
+    out2 = gemm(a, b, b_t=True)
+    ref = _ref(a, b, False, True)
+    torch.cuda.synchronize()
+    assert int(error_state()[0]) == 0
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+    assert torch.equal(out, out2)
