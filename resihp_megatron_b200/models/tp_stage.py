@@ -103,6 +103,12 @@ class _Slot:
         self.o = [torch.empty(T, stage.nq * c.head_dim, **bf) for _ in range(L)]
         self.lse = [torch.empty(stage.mb, stage.nq, stage.S, **f32) for _ in range(L)]
         self.gu = [torch.empty(T, stage.mlp_in, **bf) for _ in range(L)]
+        # bf16 stages keep what the weight gradients read instead of recomputing it in the backward:
+        # the gathered normalised inputs of the QKV and MLP-input projections and the MLP activation
+        keep = stage.keep_inputs
+        self.h1 = [torch.empty(T, H, **bf) for _ in range(L)] if keep else None
+        self.h2 = [torch.empty(T, H, **bf) for _ in range(L)] if keep else None
+        self.act = [torch.empty(T, stage.nf, **bf) for _ in range(L)] if keep else None
         self.ids: torch.Tensor | None = None
         if stage.last:
             self.hf = torch.empty(Tl, H, **bf)
@@ -114,14 +120,17 @@ class TPStage:
     def __init__(self, cfg: GPTConfig, device, *, layers, first: bool, last: bool, tp, micro_batch: int = 1,
                  seq_len: int | None = None, seed: int = 0, rep_shard: tuple[int, int] = (0, 1),
                  shd_shard: tuple[int, int] = (0, 1), rep_factories=(None, None), shd_factories=(None, None),
-                 init: bool = True, fp8=None, sp: bool = True):
+                 init: bool = True, fp8=None, sp: bool = True, recompute: bool = False):
         """``tp``: the tensor-parallel backend (``parallel.tp_backend``); ``*_shard`` the
         (rank, count) of the ZeRO-1 optimizer shard of each parameter set over its
         data-parallel group; ``*_factories`` the (buffer, optimizer) factories of ``FlatParams``
         (the fused data-parallel step's peer heap); ``init`` draws the initial weights;
         ``fp8`` an ``Fp8Recipe`` for block-scaled fp8 projections; ``sp=False``: plain tensor
         parallelism (every TP rank holds every token row; the backend all-reduces instead of
-        reduce-scattering)."""
+        reduce-scattering).  ``recompute=True`` (bf16 only) re-derives the weight gradients'
+        inputs in the backward (RMSNorm + all-gather of the QKV / MLP inputs, the MLP activation)
+        instead of keeping them per in-flight micro-batch: less memory, two more all-gathers per
+        layer."""
         self.cfg, self.device = cfg, torch.device(device)
         self.tp = tp
         self.tp_rank, self.tp_size = tp.rank, tp.world
@@ -168,6 +177,7 @@ class TPStage:
         self.free: list[_Slot] = []
         self.deferred: dict[object, list] = {}
         self.f8 = None
+        self.keep_inputs = not recompute and fp8 is None
         if fp8 is not None:
             from .fp8_linear import Fp8Linears, check_shapes
 
@@ -206,7 +216,7 @@ class TPStage:
 
     # ------------------------------------------------------------------ projections (bf16 or fp8)
     def _norm_col_fwd(self, l: int, lin: str, x: torch.Tensor, norm_w: torch.Tensor, rstd: torch.Tensor,
-                      w: torch.Tensor, out: torch.Tensor) -> None:
+                      w: torch.Tensor, out: torch.Tensor, keep: torch.Tensor | None = None) -> None:
         """``AllGather(rmsnorm(x)) @ w^T`` for this rank's rows ``x``: bf16 -- the norm writes the
         gather buffer's chunk and the fused all-gather -> GEMM runs; fp8 -- the norm writes this
         rank's rows as fp8 (row-major 1 x 128 scales) straight into the gather buffer, the gather
@@ -214,7 +224,9 @@ class TPStage:
         T, H = self.T, self.cfg.hidden
         if self.f8 is None:
             self._rms(x, norm_w, self.tp.chunk(T, H), rstd)
-            self.tp.ag_gemm(T, w, out=out)
+            _, gathered = self.tp.ag_gemm(T, w, out=out)
+            if keep is not None:
+                keep.copy_(gathered)
             return
         fmt = self.f8.recipe.fwd_fmt
         dt = fp8_ops.DTYPES[fmt]
@@ -263,7 +275,8 @@ class TPStage:
         rank's rows); ``x_full_fn()`` recomputes and gathers the input for the wgrad."""
         if self.f8 is None:
             self.tp.gemm_rs(dy, w, out=dx_out, w_t=True)
-            self._wgrad(w_list, dy, x_full_fn(), grad, copy_a=dy is self.ws_dqkv, copy_b=True)
+            # a kept input lives in the micro-batch's slot until its W pass; a re-gathered one does not
+            self._wgrad(w_list, dy, x_full_fn(), grad, copy_a=dy is self.ws_dqkv, copy_b=not self.keep_inputs)
             return
         dyq = self.f8.quant_dy(l, lin, dy)
         wq = self.f8.weight(l, lin)
@@ -323,20 +336,23 @@ class TPStage:
         for i, l in enumerate(self.layer_ids):
             p = f"layers.{l}."
             x = slot.x[i]
-            self._norm_col_fwd(l, "qkv", x, R.w(p + "attn_norm"), slot.rstd1[i], self.wqkv(p), slot.qkv[i])
+            self._norm_col_fwd(l, "qkv", x, R.w(p + "attn_norm"), slot.rstd1[i], self.wqkv(p), slot.qkv[i],
+                               keep=slot.h1[i] if slot.h1 is not None else None)
             q, k, v = self._qkv_views(slot.qkv[i])
             ops.rope_(q, self.nq, D, self.cos, self.sin, self.S)
             ops.rope_(k, self.nk, D, self.cos, self.sin, self.S)
             ops.attention_fwd(q, k, v, batch=self.mb, seq=self.S, heads=self.nq, kv_heads=self.nk, head_dim=D,
                               out=slot.o[i], lse=slot.lse[i])
             self._row_fwd(l, "o", slot.o[i], P.w(p + "wo"), slot.x2[i], x)
-            self._norm_col_fwd(l, "fc1", slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.w13(p), slot.gu[i])
+            self._norm_col_fwd(l, "fc1", slot.x2[i], R.w(p + "mlp_norm"), slot.rstd2[i], self.w13(p), slot.gu[i],
+                               keep=slot.h2[i] if slot.h2 is not None else None)
             if self.f8 is not None:  # the activation is written as the fp8 operand directly
                 aq = self.f8.act_quant_x(l, "fc2", slot.gu[i], cfg.gated)
                 self._row_fwd(l, "fc2", None, P.w(p + "w2"), slot.x[i + 1], slot.x2[i], xq=aq)
             else:
-                mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
-                self._row_fwd(l, "fc2", self.ws_a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])
+                a = slot.act[i] if slot.act is not None else self.ws_a
+                mlp_act_fwd(cfg, slot.gu[i], a)
+                self._row_fwd(l, "fc2", a, P.w(p + "w2"), slot.x[i + 1], slot.x2[i])
         if not self.last:
             return slot.x[-1]
         self._rms(slot.x[-1], R.w("final_norm"), slot.hf, slot.rstd_f)
@@ -381,12 +397,16 @@ class TPStage:
                 # the pre-activation: its gradient overwrites it only below)
                 self._row_bwd(w, l, "fc2", P.w(p + "w2"), None, self.ws_da, P.g(p + "w2"),
                               xq_cols=lambda i=i: self.f8.act_quant_cols(slot.gu[i], cfg.gated))
+            elif slot.act is not None:  # the activation kept from the forward
+                self._row_bwd(w, l, "fc2", P.w(p + "w2"), slot.act[i], self.ws_da, P.g(p + "w2"))
             else:
                 mlp_act_fwd(cfg, slot.gu[i], self.ws_a)
                 self._row_bwd(w, l, "fc2", P.w(p + "w2"), self.ws_a, self.ws_da, P.g(p + "w2"))
             dgu = mlp_act_bwd(cfg, slot.gu[i], self.ws_da, slot.gu[i])
 
             def h2_full(i=i, p=p):
+                if slot.h2 is not None:
+                    return slot.h2[i]
                 self._rms(slot.x2[i], R.w(p + "mlp_norm"), self.tp.chunk(T, H), self.ws_rstd)
                 return self.tp.all_gather(T, H)
 
@@ -405,6 +425,8 @@ class TPStage:
             ops.rope_(dk, self.nk, D, self.cos, self.sin, self.S, inverse=True)
 
             def h_full(i=i, p=p):
+                if slot.h1 is not None:
+                    return slot.h1[i]
                 self._rms(slot.x[i], R.w(p + "attn_norm"), self.tp.chunk(T, H), self.ws_rstd)
                 return self.tp.all_gather(T, H)
 

@@ -557,8 +557,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool misaligned(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 
-// Exponentials per 8 score columns evaluated on the FMA pipe (ex2_fma) by default.
-constexpr int kDefaultFmaShare = 2;
+// Exponentials per 8 score columns evaluated on the FMA pipe (ex2_fma) by default.  Measured on
+// B200 at B=2 S=4096 (forward / backward TFLOP/s for shares 0..3): 797/585, 768/581, 751/572,
+// 732/561 -- with the softmax's dependency chains broken up the MUFU unit is not the limit, so
+// every exponential stays on MUFU; the other shares remain selectable for tuning.
+constexpr int kDefaultFmaShare = 0;
 
 template <int kFma>
 int launch_bwd(dim3 grid_dkdv, dim3 grid_dq, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,

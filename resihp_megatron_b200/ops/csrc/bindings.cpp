@@ -6,6 +6,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <unordered_map>
 
@@ -53,6 +54,18 @@ long long ld_of(const torch::Tensor& t, const char* name) {
 
 }  // namespace
 
+// Split-K workspace: one grow-only buffer per (device, stream), so launches on one stream reuse it
+// in stream order and launches on different streams never share it.  The map is never destroyed
+// (its tensors must not be freed after the CUDA context is gone at exit).
+static torch::Tensor split_workspace(const torch::Tensor& like, long long bytes) {
+  static std::mutex mu;
+  static auto* pool = new std::map<std::pair<int, cudaStream_t>, torch::Tensor>();
+  std::lock_guard<std::mutex> lock(mu);
+  auto& t = (*pool)[{static_cast<int>(like.get_device()), at::cuda::getCurrentCUDAStream().stream()}];
+  if (!t.defined() || t.numel() < bytes) t = torch::empty({bytes}, like.options().dtype(torch::kUInt8));
+  return t;
+}
+
 // out[M,N] (+)= alpha * op(a) @ op(b)^T ; a is [M,K] (or [K,M] if a_t), b is [N,K] (or [K,N] if b_t)
 void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, torch::Tensor& out,
           int64_t epi, double alpha, const c10::optional<torch::Tensor>& residual, int64_t variant) {
@@ -91,10 +104,8 @@ void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, to
   }
   const int sms = num_sms(a.get_device());
   const int splits = rb::gemm_pair_splits(M, N, K, static_cast<int>(variant), sms);
-  // split-K workspace from the caching allocator: stream-ordered, so it is reused only after this
-  // launch
   torch::Tensor ws;
-  if (splits > 1) ws = torch::empty({rb::gemm_split_ws_bytes(M, N, splits)}, a.options().dtype(torch::kUInt8));
+  if (splits > 1) ws = split_workspace(a, rb::gemm_split_ws_bytes(M, N, splits));
   const int rc = rb::gemm_bf16(a.data_ptr(), lda, a_t, b.data_ptr(), ldb, b_t, out.data_ptr(), ldd, rptr, ldr,
                                M, N, K, static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a), sms,
                                at::cuda::getCurrentCUDAStream(), static_cast<int>(variant),
