@@ -125,6 +125,7 @@ def bench_gemm(a, t: Timer) -> None:
     emit("gemm_tcgen05_nt", t(lambda: ops.gemm(x, w, out=out)), flops=fl, shape=[M, N, K])
     emit("gemm_tcgen05_nt_pair_nosplit", t(lambda: ops.gemm(x, w, out=out, variant=2)), flops=fl, shape=[M, N, K])
     emit("gemm_tcgen05_nt_pair_split2", t(lambda: ops.gemm(x, w, out=out, variant=3)), flops=fl, shape=[M, N, K])
+    emit("gemm_tcgen05_nt_pair_7stages", t(lambda: ops.gemm(x, w, out=out, variant=4)), flops=fl, shape=[M, N, K])
     xt = x.t().contiguous()
     emit("gemm_tcgen05_tn", t(lambda: ops.gemm(xt, w, a_t=True, out=out)), flops=fl, shape=[M, N, K])
     emit("cublas", t(lambda: torch.matmul(x, w.t(), out=out)), flops=fl, shape=[M, N, K])

@@ -682,6 +682,7 @@ __global__ void __launch_bounds__(320, 1)
 //   * the leader issues the MMAs and commits separately to each CTA's empty / accumulator-full
 //     barriers (no multicast);
 //   * epilogue warps of both CTAs release the accumulator on the leader's barrier (8 arrivals).
+template <int kStages>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA (the pair covers 256)
   static constexpr int BN = 256;  // columns of the pair's tile
@@ -690,19 +691,20 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BNH * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
+  static constexpr int STAGES = kStages;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 192;
   static constexpr int GROUP_M = 8;  // in 256-row pair tiles
+  static_assert(SMEM_BYTES <= 232448, "over the 227 KB of dynamic shared memory a CTA may have");
 };
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int kStages>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          GemmArgs p) {
-  using C = PairCfg;
+  using C = PairCfg<kStages>;
   constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -756,7 +758,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const int kblocks = (p.K + BK - 1) / BK;
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  const int splits = p.splits > 1 ? p.splits : 1;
+  const int splits = p.splits > 1 ? 2 : 1;  // the reduction below handles two shares
   const int num_units = num_tiles * splits;       // unit u: tile u / splits, k share u % splits
   const int kb_share = (kblocks + splits - 1) / splits;
 
@@ -909,21 +911,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         __syncwarp();
         int* cnt = p.split_cnt + (tile * 2 + static_cast<int>(cta)) * 4 + q;
         int last = 0;
-        if (lane == 0) last = atomicAdd(cnt, 1) == splits - 1;
+        if (lane == 0) last = atomicAdd(cnt, 1) == 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence();
+          // exactly two shares (the host plans 1 or 2): all 64 loads of a chunk are independent and
+          // in flight together -- a per-term loop over the shares serialised them, one L2 round
+          // trip per column, and made the split kernel ~10x slower than the unsplit one
           const float* s0 = p.split_ws + slot0 * (32 * C::BN);
+          const float* s1 = s0 + 32 * C::BN;
 #pragma unroll 1
           for (int c = 0; c < C::BN / 32; ++c) {
             const int col0 = nb * C::BN + c * 32;
+            float a0[32], a1[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) a0[i] = __ldcg(s0 + (c * 32 + i) * 32 + lane);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) a1[i] = __ldcg(s1 + (c * 32 + i) * 32 + lane);
             uint32_t r[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              float v = __ldcg(s0 + (c * 32 + i) * 32 + lane);
-              for (int sh = 1; sh < splits; ++sh) v += __ldcg(s0 + sh * (32 * C::BN) + (c * 32 + i) * 32 + lane);
-              r[i] = __float_as_uint(v);
-            }
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(a0[i] + a1[i]);
             if (row_ok && col0 < p.N) store_chunk<EPI>(r, row, col0, p);
           }
           if (lane == 0) *cnt = 0;  // ready for the next launch (the host also clears it first)
@@ -1003,11 +1010,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   return static_cast<int>(cudaGetLastError());
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int kStages>
 static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
                             cudaStream_t stream) {
-  using C = PairCfg;
-  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI>;
+  using C = PairCfg<kStages>;
+  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI, kStages>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -1022,13 +1029,21 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return static_cast<int>(cudaGetLastError());
 }
 
+template <int EPI, int kStages>
+static int dispatch_major_pair_stages(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                                      const GemmArgs& a, int num_sms, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI, kStages>(ta, tb, a, num_sms, s);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI, kStages>(ta, tb, a, num_sms, s);
+  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI, kStages>(ta, tb, a, num_sms, s);
+  return launch_gemm_pair<true, true, EPI, kStages>(ta, tb, a, num_sms, s);
+}
+
+// `stages`: depth of the operand ring (6 by default; 7 fills the 227 KB of shared memory)
 template <int EPI>
 static int dispatch_major_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                               const GemmArgs& a, int num_sms, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, a, num_sms, s);
-  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, a, num_sms, s);
-  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI>(ta, tb, a, num_sms, s);
-  return launch_gemm_pair<true, true, EPI>(ta, tb, a, num_sms, s);
+                               const GemmArgs& a, int num_sms, cudaStream_t s, int stages) {
+  if (stages == 7) return dispatch_major_pair_stages<EPI, 7>(a_mn, b_mn, ta, tb, a, num_sms, s);
+  return dispatch_major_pair_stages<EPI, 6>(a_mn, b_mn, ta, tb, a, num_sms, s);
 }
 
 template <int BN, int EPI>
@@ -1110,13 +1125,18 @@ int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* r
               : launch_gemm<256, false, false, kEpiScatterBF16>(ta, tb, a, num_sms, stream);
 }
 
-// Split-K chosen automatically by variant 0.  Off: its first measurement on B200 ran ~10x slower
-// than the unsplit kernel (time growing with the workspace size), so it stays opt-in (variant 3)
-// until that is understood.
+// Operand-ring depth of the CTA-pair kernel for variants 0, 2 and 3.
+constexpr int kPairStages = 6;
+
+// Split-K chosen automatically by variant 0.  Off: measured on B200 (events, 20 launches), the
+// unsplit pair kernel is faster or equal on every Llama-3-8B shape that split-K targets -- 4096^3
+// 0.103 vs 0.137 ms, 4096 x 6144 x 4096 0.155 vs 0.210, 4096 x 4096 x 14336 0.358 vs 0.377,
+// 4096 x 4096 x 28672 0.715 vs 0.710 -- the partial-tile traffic costs more than the idle part
+// of the last wave.  It stays selectable (variant 3).
 constexpr bool kAutoSplit = false;
 
 static bool use_pair_kernel(int M, int N, int variant) {
-  return variant == 2 || variant == 3 || (variant == 0 && M >= 512 && N >= 256);
+  return variant == 2 || variant == 3 || variant == 4 || (variant == 0 && M >= 512 && N >= 256);
 }
 
 // Work units per output tile of the CTA-pair kernel.  Split-K in two shares pays when the tile
@@ -1124,7 +1144,7 @@ static bool use_pair_kernel(int M, int N, int variant) {
 // 512 units = 6.92 waves) and each share keeps >= 32 k-blocks; tile counts above 6 waves (where
 // the tail matters little) keep one unit per tile, which also bounds the workspace.
 int gemm_pair_splits(int M, int N, int K, int variant, int num_sms) {
-  if (!use_pair_kernel(M, N, variant) || variant == 2) return 1;
+  if (!use_pair_kernel(M, N, variant) || variant == 2 || variant == 4) return 1;
   const int kblocks = (K + 63) / 64;
   if (variant == 3) return kblocks >= 2 ? 2 : 1;
   const long long pairs = num_sms / 2;
@@ -1161,8 +1181,9 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
   CUtensorMap ta, tb;
   int rc;
   // variant: 0 auto (CTA pair for large tiles, split-K where it fills the last wave), 1 single
-  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced
+  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced, 4 CTA pair with a 7-stage ring
   const bool use_pair = use_pair_kernel(M, N, variant);
+  const int stages = variant == 4 ? 7 : kPairStages;
   if (use_pair) {
     if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
     else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
@@ -1182,10 +1203,10 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
       if (e != cudaSuccess) return static_cast<int>(e);
     }
     switch (epi) {
-      case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
-      case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
-      case kEpiF32Acc: return dispatch_major_pair<kEpiF32Acc>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
-      case kEpiBF16Res: return dispatch_major_pair<kEpiBF16Res>(a_mn, b_mn, ta, tb, ga, num_sms, stream);
+      case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
+      case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
+      case kEpiF32Acc: return dispatch_major_pair<kEpiF32Acc>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
+      case kEpiBF16Res: return dispatch_major_pair<kEpiBF16Res>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
     }
     return -2;
   }
