@@ -274,9 +274,11 @@ class TPStage:
         """Backward of a column-parallel projection: dgrad reduce-scattered into ``dx_out`` (this
         rank's rows); ``x_full_fn()`` recomputes and gathers the input for the wgrad."""
         if self.f8 is None:
-            self.tp.gemm_rs(dy, w, out=dx_out, w_t=True)
+            # the dgrad's reduce-scatter runs while the weight-gradient GEMM computes
+            finish = self.tp.gemm_rs_async(dy, w, out=dx_out, w_t=True)
             # a kept input lives in the micro-batch's slot until its W pass; a re-gathered one does not
             self._wgrad(w_list, dy, x_full_fn(), grad, copy_a=dy is self.ws_dqkv, copy_b=not self.keep_inputs)
+            finish()
             return
         dyq = self.f8.quant_dy(l, lin, dy)
         wq = self.f8.weight(l, lin)

@@ -19,6 +19,9 @@ Operations:
 * ``ag_gemm(M, w, out, w_t)`` -> ``(AllGather(chunks) @ op(w)^T, gathered input)``;
 * ``all_gather(M, K)`` -> the gathered ``[M, K]`` chunks;
 * ``gemm_rs(x, w, out, w_t, residual)`` -> ``ReduceScatter_rows(x @ op(w)^T) (+ residual)``;
+* ``gemm_rs_async(x, w, out, w_t)`` -> a ``finish()`` callable: the GEMM and the start of the
+  reduce-scatter are enqueued now, ``out`` holds the reduced rows once ``finish()`` returned, and
+  work enqueued in between (a weight-gradient GEMM) overlaps the transfer;
 * ``fp8_local(M, K)`` / ``all_gather_fp8(M, K)`` -- the gather of a block-scaled fp8 input: this
   rank quantises its rows (1 x 128 row scales, row-major so a row's scales travel with it) into
   ``fp8_local``'s ``(data [M / tp, K] uint8, scales [M / tp, K / 128])``; the gather returns the
@@ -46,6 +49,10 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+
+
+def _done() -> None:
+    pass
 
 
 class _Buffers:
@@ -125,6 +132,10 @@ class SoloTP:
                      residual: torch.Tensor | None = None) -> torch.Tensor:
         return gemm(out=out, residual=residual)
 
+    def gemm_rs_async(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, w_t: bool = False):
+        self.gemm_rs(x, w, out=out, w_t=w_t)
+        return _done
+
     def close(self) -> None:
         pass
 
@@ -196,6 +207,18 @@ class CollectiveTP:
         gemm(out=part)
         return self._reduce_scatter(part, out, residual)
 
+    def gemm_rs_async(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, w_t: bool = False):
+        if not self.sp:
+            self.gemm_rs(x, w, out=out, w_t=w_t)
+            return _done
+        M, N = x.shape[0], (w.shape[1] if w_t else w.shape[0])
+        part = self.partials.get((M, N))
+        if part is None:
+            part = self.partials[(M, N)] = torch.empty(M, N, dtype=torch.bfloat16, device=self.device)
+        ops.gemm(x, w, b_t=w_t, out=part)
+        work = dist.reduce_scatter_tensor(out, part, group=self.group, async_op=True)
+        return lambda: self.wait(work)
+
     def _reduce_scatter(self, part: torch.Tensor, out, residual) -> torch.Tensor:
         M, N = part.shape
         if not self.sp:  # all-reduce: every rank keeps every row
@@ -265,6 +288,12 @@ class FusedTP:
             return self._all_reduce(M, N, lambda mine, res: self.comm.reduce_scatter_with(
                 M, N, gemm, out=mine, residual=res), out, residual)
         return self.comm.reduce_scatter_with(M, N, gemm, out=out, residual=residual)
+
+    def gemm_rs_async(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, w_t: bool = False):
+        if not self.sp:
+            self.gemm_rs(x, w, out=out, w_t=w_t)
+            return _done
+        return self.comm.gemm_reduce_scatter_begin(x, w, out, w_t=w_t)
 
     def _all_reduce(self, M: int, N: int, reduce_scatter, out, residual) -> torch.Tensor:
         """GEMM -> all-reduce as GEMM -> reduce-scatter (this rank's reduced rows, plus the

@@ -165,6 +165,21 @@ class TensorParallelComm:
         self._rs ^= 1
         return y
 
+    def gemm_reduce_scatter_begin(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, w_t: bool = False):
+        """``gemm_reduce_scatter`` in two halves: the partials are scattered now; the returned
+        ``finish()`` waits (bounded barrier) for every rank's partials and reduces them into
+        ``out``.  Work enqueued before ``finish()`` runs while the peers catch up."""
+        self._barrier()
+        self.scatter_partials(x, w, w_t)
+        M, N = x.shape[0], (w.shape[1] if w_t else w.shape[0])
+
+        def finish() -> None:
+            self._barrier()
+            self.reduce_received(M, N, out, None)
+            self._rs ^= 1
+
+        return finish
+
     def reduce_scatter_with(self, M: int, N: int, gemm, out: torch.Tensor | None = None,
                             residual: torch.Tensor | None = None) -> torch.Tensor:
         """``gemm_reduce_scatter`` for another GEMM kernel (the block-scaled fp8 one) whose
