@@ -52,7 +52,7 @@ def main(argv=None) -> None:
     else:
         device, backend = "cpu", "gloo"
     mgr = ResilientCommManager(backend, device=device, timeout_s=args.timeout, validate_timeout_s=args.timeout,
-                               subgroup_mode="local")
+                               subgroup_mode="split" if backend == "nccl" else "local")
     injector = get_injector()
     fp8 = None
     if args.fp8:

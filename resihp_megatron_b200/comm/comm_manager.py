@@ -154,11 +154,19 @@ class ResilientCommManager:
                 started: float) -> GenerationComms:
         with self._mu:
             self._groups_alive = [c10d._get_default_group()]
+        t_world = time.monotonic()
         groups = self._subgroups(rank, specs)
+        t_groups = time.monotonic()
         if self.validate:
             self._validate(len(world), groups, specs)
+        t_end = time.monotonic()
         comms = GenerationComms(generation, rank, tuple(world), {s.name: s for s in specs}, groups, path,
-                                time.monotonic() - started)
+                                t_end - started)
+        # where a generation build spends its time: the world (init / shrink / adopt), the plan's
+        # groups, their validation collectives
+        comms.stats["phases_s"] = {"world": round(t_world - started, 4), "groups": round(t_groups - t_world, 4),
+                                   "validate": round(t_end - t_groups, 4),
+                                   "groups_created": len({id(g) for g in groups.values() if g is not None})}
         self.current = comms
         log.info("generation %d built (%s) in %.3fs with %d groups", generation, path, comms.build_seconds,
                  len(groups))
@@ -197,6 +205,16 @@ class ResilientCommManager:
             raise RuntimeError("adopt() needs an initialised default group matching the world")
         return self._finish(generation, world, rank, specs, "adopted", started)
 
+    def _nccl_options(self):
+        """Options of every NCCL communicator this manager creates: non-blocking, so that
+        ``abort()`` from the control thread returns promptly even while a collective that lost
+        its peer is in flight (a blocking communicator's abort waited for the watchdog)."""
+        if self.backend != "nccl" or not self.nccl_nonblocking:
+            return None
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.blocking = 0
+        return opts
+
     def _init_world(self, rank: int, world_size: int, store) -> None:
         options: dict = dict(backend=self.backend, store=store, rank=rank, world_size=world_size, timeout=self.timeout)
         if self.backend == "nccl":
@@ -216,6 +234,7 @@ class ResilientCommManager:
             for layer in split_layers(specs):
                 self._raise_if_aborted()
                 pg = dist.split_group(split_ranks=[list(s.ranks) for s in layer], timeout=self.timeout,
+                                      pg_options=self._nccl_options(),
                                       group_desc=f"resihp:{layer[0].kind}:{len(layer)}")
                 mine.update((s.ranks, pg) for s in layer if rank in s.ranks)
         else:
@@ -223,7 +242,8 @@ class ResilientCommManager:
             # same group names everywhere and creation cannot deadlock
             for ranks in dict.fromkeys(s.ranks for s in canonical_order(specs) if s.materialized):
                 self._raise_if_aborted()
-                pg = dist.new_group(list(ranks), timeout=self.timeout, group_desc=f"resihp:{ranks}")
+                pg = dist.new_group(list(ranks), timeout=self.timeout, group_desc=f"resihp:{ranks}",
+                                    pg_options=self._nccl_options())
                 if rank in ranks:
                     mine[ranks] = pg
         with self._mu:

@@ -84,8 +84,11 @@ class GPUHybridTrainer:
         self.plan = self.planner.initial_plan(self.topology)
         self.schedule, _ = self.planner.schedule(self.plan, self.topology)
         ids = list(self.plan.world)
+        # NCCL: the plan's groups come from one ncclCommSplit per layer of disjoint groups
+        # ("split"), not one communicator creation per group; gloo creates them one by one
         self.mgr = ResilientCommManager("nccl" if self.device.type == "cuda" else "gloo", device=str(self.device),
-                                        subgroup_mode="local", timeout_s=120)
+                                        subgroup_mode="split" if self.device.type == "cuda" else "local",
+                                        timeout_s=120)
         self.comms = self.mgr.adopt(1, ids, ids[rank], self._group_specs(self.plan, self.schedule))
         self.tokens = TokenSource(cfg.vocab_size, micro_batch, self.S, seed=data_seed)
         self.fp8 = fp8
@@ -212,7 +215,8 @@ class GPUHybridTrainer:
         self._migrate_to(old_plan, new_plan, new_schedule, comms, me, new_world, state, layout, step, iteration, mark)
         self.last_reconfig = {name: round(t - marks[i][1], 4) for i, (name, t) in enumerate(marks[1:])}
         self.last_reconfig.update(self._moved, layout=[(g.replica, g.stage, g.tp, list(g.layers))
-                                                       for g in new_plan.stage_groups], world=len(new_world))
+                                                       for g in new_plan.stage_groups], world=len(new_world),
+                                  regroup_phases=comms.stats.get("phases_s"), regroup_path=comms.path)
         return True
 
     def reshard(self, tp: int, pp: int, dp: int) -> None:

@@ -59,9 +59,9 @@ def test_kill_at_boundary_recovers_on_gpus(tmp_path):
     env = {"RESIHP_FAULTS": f"kill@iter=2:target={victim}:phase=boundary", "RESIHP_FAULT_STAMP": str(stamp),
            "PYTHONPATH": str(ROOT), "OMP_NUM_THREADS": "1", "NCCL_NVLS_ENABLE": "0", "RESIHP_LOG_LEVEL": "WARNING"}
     coord = Coordinator(planner=make_hetero_planner(gpu_planner_config(tp=tp, pp=pp, dp=dp)), expected_workers=n,
-                        lease_timeout=3.0, hang_timeout=120.0, abort_timeout=30.0, ready_timeout=240.0).start()
+                        lease_timeout=3.0, hang_timeout=120.0, abort_timeout=60.0, ready_timeout=240.0).start()
     cmd = [sys.executable, str(ROOT / "examples" / "gpu_hybrid_demo.py"), "--iterations", str(ITERS), "--out",
-           str(tmp_path), "--timeout", "30", "--device", "cuda", "--tp-impl", "collective"]
+           str(tmp_path), "--timeout", "20", "--device", "cuda", "--tp-impl", "collective"]
     agent = None
     try:
         agent = NodeAgent("n0", [coord.address], hb_interval=0.1, worker_timeout=5.0).start()
