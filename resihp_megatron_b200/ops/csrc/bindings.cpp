@@ -356,6 +356,34 @@ void symm_close(int64_t ptr, int64_t device) {
   cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
 }
 
+// cuMem region of at least `bytes` on `device`, zeroed: (pointer, exported fd, mapped size).  The
+// caller owns the fd (close it once every peer imported it).
+py::tuple vmm_alloc(int64_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  TORCH_CHECK(rb::vmm_available(), "vmm_alloc: the driver's cuMem entry points are unavailable");
+  const long long size = rb::vmm_round(static_cast<int>(device), bytes);
+  void* p = nullptr;
+  int fd = -1;
+  const int rc = rb::vmm_alloc(static_cast<int>(device), size, &p, &fd);
+  TORCH_CHECK(rc == 0, "vmm_alloc of ", size, " bytes failed with code ", rc);
+  TORCH_CHECK(cudaMemset(p, 0, static_cast<size_t>(size)) == cudaSuccess, "vmm_alloc: memset failed");
+  return py::make_tuple(reinterpret_cast<int64_t>(p), static_cast<int64_t>(fd), static_cast<int64_t>(size));
+}
+// Map a peer's exported region (its fd, received over a Unix socket) for access from `device`.
+int64_t vmm_import(int64_t fd, int64_t size, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  void* p = nullptr;
+  const int rc = rb::vmm_import(static_cast<int>(device), static_cast<int>(fd), size, &p);
+  TORCH_CHECK(rc == 0, "vmm_import failed with code ", rc);
+  return reinterpret_cast<int64_t>(p);
+}
+void vmm_free(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  const int rc = rb::vmm_free(reinterpret_cast<void*>(ptr));
+  TORCH_CHECK(rc == 0, "vmm_free failed with code ", rc);
+}
+bool vmm_available() { return rb::vmm_available() != 0; }
+
 void symm_free(int64_t ptr, int64_t device) {
   const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
   cudaFree(reinterpret_cast<void*>(ptr));
@@ -824,6 +852,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
+  m.def("vmm_alloc", &vmm_alloc);
+  m.def("vmm_import", &vmm_import);
+  m.def("vmm_free", &vmm_free);
+  m.def("vmm_available", &vmm_available);
   m.def("symm_tensor", &symm_tensor);
   m.def("host_words_alloc", &host_words_alloc);
   m.def("host_words_free", &host_words_free);

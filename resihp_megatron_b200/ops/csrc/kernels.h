@@ -95,6 +95,12 @@ int dp_step_fused(const float* const* grads, __nv_bfloat16* const* weights, int 
                   int decoupled, float bc1, float bc2_sqrt, float grad_scale, const int* abort_word, int num_sms,
                   cudaStream_t s, void* ring_base = nullptr, int ring_capacity = 0, void* stamp = nullptr);
 int ring_record_bytes();
+// cuMem regions shared as POSIX file descriptors (vmm_heap.cu).
+int vmm_available();
+long long vmm_round(int device, long long bytes);
+int vmm_alloc(int device, long long bytes, void** ptr, int* fd);
+int vmm_import(int device, int fd, long long bytes, void** ptr);
+int vmm_free(void* ptr);
 int kernel_stamp_bytes();
 int symm_copy(const long long* triples, int n, void* dev_scratch, int max_pieces, int num_sms, cudaStream_t s);
 // All-gather of equal chunks from peers' buffers into this rank's buffer (no host staging).

@@ -1,8 +1,11 @@
 """Per-generation symmetric peer memory on one NVLink/NVSwitch node.
 
 Each rank allocates one device region holding a signal pad and named segments at identical
-offsets, exports a CUDA IPC handle, and maps every peer's region; kernels then read and write
-peers' segments directly over NVLink.  A reconfiguration tears the heap down (``close``) and
+offsets, shares it, and maps every peer's region; kernels then read and write peers' segments
+directly over NVLink.  Two ways to share a region: ``"vmm"`` -- a cuMem allocation exported as a POSIX file descriptor, which each peer receives over a
+Unix socket (``SCM_RIGHTS``) and maps into its own reserved range; the imported handle keeps the
+physical memory alive, so a departed peer's region stays mapped for the survivors until they drop
+it -- or ``"ipc"`` (the default): ``cudaMalloc`` plus a CUDA IPC handle.  A reconfiguration tears the heap down (``close``) and
 builds the next generation's heap over the new world -- the counterpart of rebuilding NCCL
 communicators (reference: ``resihp/comm/comm_manager.py:138-251``).
 
@@ -15,6 +18,12 @@ timeout.  ``barrier`` is a bounded cross-GPU barrier on the signal pad; its outc
 
 from __future__ import annotations
 
+import json
+import os
+import socket
+import threading
+import time
+import uuid
 from dataclasses import dataclass
 from typing import Callable
 
@@ -98,14 +107,70 @@ def check_layout(segs: dict[str, Segment], pad: int, total: int, world: int) -> 
         raise AssertionError(f"segments end at {end} beyond the heap's {total} bytes")
 
 
+class _FdServer:
+    """Hands this rank's region descriptor to ``peers`` connecting processes over an
+    abstract-namespace Unix socket (``SCM_RIGHTS``), then stops."""
+
+    def __init__(self, fd: int, peers: int, timeout_s: float = 60.0):
+        self.fd, self.peers = fd, peers
+        self.name = f"resihp-symm-{os.getpid()}-{uuid.uuid4().hex}"
+        self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.sock.bind("\0" + self.name)
+        self.sock.listen(max(1, peers))
+        self.sock.settimeout(timeout_s)
+        self.error: BaseException | None = None
+        self.thread = threading.Thread(target=self._serve, name="symm-fd-server", daemon=True)
+        self.thread.start()
+
+    def _serve(self) -> None:
+        try:
+            for _ in range(self.peers):
+                conn, _ = self.sock.accept()
+                with conn:
+                    socket.send_fds(conn, [b"f"], [self.fd])
+        except BaseException as e:  # noqa: BLE001 -- reported by join()
+            self.error = e
+        finally:
+            self.sock.close()
+
+    def join(self, timeout_s: float = 60.0) -> None:
+        self.thread.join(timeout_s)
+        if self.thread.is_alive() or self.error is not None:
+            raise RuntimeError(f"symmetric heap descriptor exchange did not finish: {self.error}")
+
+
+def _receive_fd(name: str, timeout_s: float = 60.0) -> int:
+    deadline = time.monotonic() + timeout_s
+    while True:
+        try:
+            with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as sock:
+                sock.settimeout(max(1.0, deadline - time.monotonic()))
+                sock.connect("\0" + name)
+                _, fds, _, _ = socket.recv_fds(sock, 16, 1)
+            if not fds:
+                raise RuntimeError(f"no descriptor from {name}")
+            return fds[0]
+        except (ConnectionRefusedError, FileNotFoundError):
+            if time.monotonic() > deadline:
+                raise
+            time.sleep(0.01)
+
+
+def default_alloc() -> str:
+    """``RESIHP_SYMM_ALLOC`` (``vmm`` / ``ipc``), else ``ipc``."""
+    want = os.environ.get("RESIHP_SYMM_ALLOC", "")
+    return want if want in ("vmm", "ipc") else "ipc"
+
+
 class SymmetricHeap:
     """``exchange(handle: bytes) -> list[bytes]`` all-gathers the IPC handles in rank order
     (``exchange_via_group`` / ``exchange_via_store``)."""
 
     def __init__(self, segments: dict[str, tuple[int, torch.dtype]], rank: int, world: int,
                  exchange: Callable[[bytes], list[bytes]] | None, device, abort: AbortWord | None = None,
-                 _bases: list[int] | None = None):
+                 _bases: list[int] | None = None, alloc: str | None = None):
         self.rank, self.world = rank, world
+        self.alloc = "ipc"
         self.device = torch.device(device)
         self.dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self.segments, self.pad_bytes, self.nbytes = layout(segments, world)
@@ -120,20 +185,55 @@ class SymmetricHeap:
             self.local_base = self.bases[rank]
             self._owns_local = False
         else:
-            self.local_base, handle = ext().symm_alloc(self.nbytes, self.dev_index)
+            self.alloc = alloc or default_alloc()
             self._owns_local = True
-            handles = exchange(handle) if world > 1 else [handle]
+            if self.alloc == "vmm":
+                self._map_vmm(rank, world, exchange)
+            else:
+                self.local_base, handle = ext().symm_alloc(self.nbytes, self.dev_index)
+                handles = exchange(handle) if world > 1 else [handle]
+                assert len(handles) == world
+                self.bases = []
+                for r, h in enumerate(handles):
+                    if r == rank:
+                        self.bases.append(self.local_base)
+                    else:
+                        p = ext().symm_open(h, self.dev_index)
+                        self._opened.append(p)
+                        self.bases.append(p)
+        self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    def _map_vmm(self, rank: int, world: int, exchange) -> None:
+        self.local_base, fd, size = ext().vmm_alloc(self.nbytes, self.dev_index)
+        server = _FdServer(fd, world - 1) if world > 1 else None
+        try:
+            mine = json.dumps({"sock": server.name if server else "", "size": size}).encode()
+            handles = exchange(mine) if world > 1 else [mine]
             assert len(handles) == world
             self.bases = []
             for r, h in enumerate(handles):
                 if r == rank:
                     self.bases.append(self.local_base)
-                else:
-                    p = ext().symm_open(h, self.dev_index)
-                    self._opened.append(p)
-                    self.bases.append(p)
-        self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
-        self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+                    continue
+                peer = json.loads(bytes(h).decode())
+                peer_fd = _receive_fd(peer["sock"])
+                try:
+                    p = ext().vmm_import(peer_fd, peer["size"], self.dev_index)
+                finally:
+                    os.close(peer_fd)
+                self._opened.append(p)
+                self.bases.append(p)
+            if server is not None:
+                server.join()
+        finally:
+            os.close(fd)
+
+    def _unmap(self, ptr: int) -> None:
+        if self.alloc == "vmm":
+            ext().vmm_free(ptr, self.dev_index)
+        else:
+            ext().symm_close(ptr, self.dev_index)
 
     @classmethod
     def emulated(cls, segments: dict[str, tuple[int, torch.dtype]], world: int, device) -> list["SymmetricHeap"]:
@@ -174,7 +274,7 @@ class SymmetricHeap:
         for r, b in enumerate(self.bases):
             if r not in keep and b in self._opened:
                 torch.cuda.synchronize(self.device)
-                ext().symm_close(b, self.dev_index)
+                self._unmap(b)
                 self._opened.remove(b)
         self.rank, self.world, self.bases = keep.index(self.rank), len(keep), bases
         self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
@@ -202,10 +302,13 @@ class SymmetricHeap:
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
         for p in self._opened:
-            ext().symm_close(p, self.dev_index)
+            self._unmap(p)
         self._opened = []
         if self._owns_local and self.local_base:
-            ext().symm_free(self.local_base, self.dev_index)
+            if self.alloc == "vmm":
+                ext().vmm_free(self.local_base, self.dev_index)
+            else:
+                ext().symm_free(self.local_base, self.dev_index)
         for b in getattr(self, "_emulated_bases", []):
             ext().symm_free(b, self.dev_index)
         self._emulated_bases = []

@@ -103,3 +103,77 @@ def test_barrier_single_rank_then_timeout_and_abort_paths():
     x = torch.ones(4, device="cuda") * 2  # context still usable
     assert x.sum().item() == 8
     pair[0].close()
+
+
+def test_vmm_region_exported_and_imported_aliases_the_same_memory():
+    """A cuMem region exported as a file descriptor and imported again maps the same physical
+    memory: writes through either mapping are seen through the other."""
+    import os
+
+    from resihp_megatron_b200.ops._build import ext
+
+    p, fd, size = ext().vmm_alloc(1 << 20, 0)
+    try:
+        q = ext().vmm_import(fd, size, 0)
+    finally:
+        os.close(fd)
+    n = size // 4
+    a = ext().symm_tensor(p, n, "float32", 0)
+    b = ext().symm_tensor(q, n, "float32", 0)
+    assert p != q and int(a.abs().sum()) == 0  # zeroed at allocation
+    a.copy_(torch.arange(n, device="cuda", dtype=torch.float32))
+    torch.cuda.synchronize()
+    assert torch.equal(b, a)
+    b.fill_(3.0)
+    torch.cuda.synchronize()
+    assert bool((a == 3.0).all())
+    del a, b
+    ext().vmm_free(q, 0)
+    ext().vmm_free(p, 0)
+
+
+def test_vmm_heap_descriptor_exchange_between_two_ranks_in_threads():
+    """Two heaps of one world built concurrently (threads standing in for processes) exchange
+    their regions' descriptors over Unix sockets; each maps the other's region, a write by one is
+    read through the other's mapping, and ``restrict`` drops the departed rank's mapping."""
+    import threading
+
+    from resihp_megatron_b200.parallel.symm import SymmetricHeap
+
+    slots: list = [None, None]
+    ready = threading.Barrier(2)
+
+    def exchange_for(rank):
+        def exchange(handle: bytes) -> list[bytes]:
+            slots[rank] = handle
+            ready.wait(timeout=30)
+            return list(slots)
+        return exchange
+
+    heaps: list = [None, None]
+    errors: list = []
+
+    def build(rank):
+        try:
+            torch.cuda.set_device(0)
+            heaps[rank] = SymmetricHeap({"x": (4096, torch.float32)}, rank, 2, exchange_for(rank), "cuda", alloc="vmm")
+        except BaseException as e:  # noqa: BLE001
+            errors.append(e)
+
+    threads = [threading.Thread(target=build, args=(r,)) for r in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(60)
+    assert not errors, errors
+    h0, h1 = heaps
+    h0.tensor("x").fill_(7.0)
+    torch.cuda.synchronize()
+    assert bool((h1.tensor("x", rank=0) == 7.0).all())
+    h1.tensor("x").fill_(-1.0)
+    torch.cuda.synchronize()
+    assert bool((h0.tensor("x", rank=1) == -1.0).all())
+    h0.restrict([0])
+    assert h0.world == 1 and h0.bases == [h0.local_base]
+    h0.close()
+    h1.close()
