@@ -759,7 +759,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int splits = p.splits > 1 ? 2 : 1;  // the reduction below handles two shares
-  const int num_units = num_tiles * splits;       // unit u: tile u / splits, k share u % splits
+  // unit u: tile u % num_tiles, k share u / num_tiles -- every tile's first share runs before any
+  // second share, so the units of a wave share A / B panels in L2 exactly as unsplit tiles do
+  const int num_units = num_tiles * splits;
   const int kb_share = (kblocks + splits - 1) / splits;
 
   if (warp == 0) {
@@ -769,8 +771,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       for (int u = pair; u < num_units && !*abort_flag; u += num_pairs) {
-        const int tile = u / splits;
-        const int kb_lo = (u - tile * splits) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
+        const int tile = u % num_tiles;
+        const int kb_lo = (u / num_tiles) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
         int mb, nb;
         tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
         const int m0 = mb * 2 * BM + static_cast<int>(cta) * BM;
@@ -823,7 +825,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int acc = 0;
       uint32_t aphase = 0;
       for (int u = pair; u < num_units; u += num_pairs) {
-        const int kb_lo = (u % splits) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
+        const int kb_lo = (u / num_tiles) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
         if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
@@ -867,7 +869,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t aphase = 0;
     for (int u = pair; u < num_units; u += num_pairs) {
-      const int tile = u / splits, share = u - tile * splits;
+      const int tile = u % num_tiles, share = u / num_tiles;
       int mb, nb;
       tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
       if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
