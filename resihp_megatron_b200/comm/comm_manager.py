@@ -97,6 +97,11 @@ def _nccl_at_least(version, wanted: tuple[int, ...]) -> bool:
     return version is not None and tuple(version) >= wanted
 
 
+def _abort_quietly(pg) -> None:
+    with contextlib.suppress(Exception):  # the NCCL watchdog is the backstop
+        pg.abort()
+
+
 class ResilientCommManager:
     def __init__(self, backend: str = "gloo", *, device: str | None = None, timeout_s: float = 60.0,
                  validate_timeout_s: float = 30.0, validate: bool = True, shrink: str = "auto",
@@ -320,9 +325,17 @@ class ResilientCommManager:
         if self.backend == "nccl":
             with self._mu:
                 groups = list(self._groups_alive)
-            for pg in groups:
-                with contextlib.suppress(Exception):  # the NCCL watchdog is the backstop
-                    pg.abort()
+            # Every communicator is aborted on its own thread, subgroups first: a subgroup split
+            # from the world communicator shares its proxy, and on B200 the world's abort waited
+            # (until the watchdog timeout) while a subgroup's collective was stuck on a dead peer,
+            # so aborting them one after another in creation order never reached the stuck one.
+            threads = [threading.Thread(target=_abort_quietly, args=(pg,), name="nccl-abort", daemon=True)
+                       for pg in reversed(groups)]
+            for t in threads:
+                t.start()
+            deadline = time.monotonic() + 2.0  # the control thread must not stall on a slow abort
+            for t in threads:
+                t.join(max(0.0, deadline - time.monotonic()))
 
     @property
     def aborted(self) -> bool:

@@ -682,11 +682,11 @@ __global__ void __launch_bounds__(320, 1)
 //   * the leader issues the MMAs and commits separately to each CTA's empty / accumulator-full
 //     barriers (no multicast);
 //   * epilogue warps of both CTAs release the accumulator on the leader's barrier (8 arrivals).
-template <int kStages>
+template <int kStages, int kBN = 256>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA (the pair covers 256)
-  static constexpr int BN = 256;  // columns of the pair's tile
-  static constexpr int BNH = 128; // B rows held per CTA
+  static constexpr int BN = kBN;  // columns of the pair's tile (256, or 128 for more tiles per wave)
+  static constexpr int BNH = kBN / 2;  // B rows held per CTA
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BNH * BK * 2;
@@ -700,11 +700,11 @@ struct PairCfg {
   static_assert(SMEM_BYTES <= 232448, "over the 227 KB of dynamic shared memory a CTA may have");
 };
 
-template <bool A_MN, bool B_MN, int EPI, int kStages>
+template <bool A_MN, bool B_MN, int EPI, int kStages, int kBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          GemmArgs p) {
-  using C = PairCfg<kStages>;
+  using C = PairCfg<kStages, kBN>;
   constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1012,11 +1012,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   return static_cast<int>(cudaGetLastError());
 }
 
-template <bool A_MN, bool B_MN, int EPI, int kStages>
+template <bool A_MN, bool B_MN, int EPI, int kStages, int kBN>
 static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
                             cudaStream_t stream) {
-  using C = PairCfg<kStages>;
-  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI, kStages>;
+  using C = PairCfg<kStages, kBN>;
+  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI, kStages, kBN>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -1031,21 +1031,23 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int EPI, int kStages>
+template <int EPI, int kStages, int kBN>
 static int dispatch_major_pair_stages(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                                       const GemmArgs& a, int num_sms, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI, kStages>(ta, tb, a, num_sms, s);
-  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI, kStages>(ta, tb, a, num_sms, s);
-  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI, kStages>(ta, tb, a, num_sms, s);
-  return launch_gemm_pair<true, true, EPI, kStages>(ta, tb, a, num_sms, s);
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI, kStages, kBN>(ta, tb, a, num_sms, s);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI, kStages, kBN>(ta, tb, a, num_sms, s);
+  if (a_mn && !b_mn) return launch_gemm_pair<true, false, EPI, kStages, kBN>(ta, tb, a, num_sms, s);
+  return launch_gemm_pair<true, true, EPI, kStages, kBN>(ta, tb, a, num_sms, s);
 }
 
-// `stages`: depth of the operand ring (6 by default; 7 fills the 227 KB of shared memory)
+// `stages`: depth of the operand ring (6 by default; 7 fills the 227 KB of shared memory);
+// `bn`: pair tile width, 256, or 128 (8 stages) for twice the tiles per wave
 template <int EPI>
 static int dispatch_major_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                               const GemmArgs& a, int num_sms, cudaStream_t s, int stages) {
-  if (stages == 7) return dispatch_major_pair_stages<EPI, 7>(a_mn, b_mn, ta, tb, a, num_sms, s);
-  return dispatch_major_pair_stages<EPI, 6>(a_mn, b_mn, ta, tb, a, num_sms, s);
+                               const GemmArgs& a, int num_sms, cudaStream_t s, int stages, int bn) {
+  if (bn == 128) return dispatch_major_pair_stages<EPI, 8, 128>(a_mn, b_mn, ta, tb, a, num_sms, s);
+  if (stages == 7) return dispatch_major_pair_stages<EPI, 7, 256>(a_mn, b_mn, ta, tb, a, num_sms, s);
+  return dispatch_major_pair_stages<EPI, 6, 256>(a_mn, b_mn, ta, tb, a, num_sms, s);
 }
 
 template <int BN, int EPI>
@@ -1138,7 +1140,7 @@ constexpr int kPairStages = 6;
 constexpr bool kAutoSplit = false;
 
 static bool use_pair_kernel(int M, int N, int variant) {
-  return variant == 2 || variant == 3 || variant == 4 || (variant == 0 && M >= 512 && N >= 256);
+  return (variant >= 2 && variant <= 5) || (variant == 0 && M >= 512 && N >= 256);
 }
 
 // Work units per output tile of the CTA-pair kernel.  Split-K in two shares pays when the tile
@@ -1146,7 +1148,7 @@ static bool use_pair_kernel(int M, int N, int variant) {
 // 512 units = 6.92 waves) and each share keeps >= 32 k-blocks; tile counts above 6 waves (where
 // the tail matters little) keep one unit per tile, which also bounds the workspace.
 int gemm_pair_splits(int M, int N, int K, int variant, int num_sms) {
-  if (!use_pair_kernel(M, N, variant) || variant == 2 || variant == 4) return 1;
+  if (!use_pair_kernel(M, N, variant) || variant == 2 || variant == 4 || variant == 5) return 1;
   const int kblocks = (K + 63) / 64;
   if (variant == 3) return kblocks >= 2 ? 2 : 1;
   const long long pairs = num_sms / 2;
@@ -1183,14 +1185,16 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
   CUtensorMap ta, tb;
   int rc;
   // variant: 0 auto (CTA pair for large tiles, split-K where it fills the last wave), 1 single
-  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced, 4 CTA pair with a 7-stage ring
+  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced, 4 CTA pair with a 7-stage ring,
+  // 5 CTA pair with 256 x 128 tiles
   const bool use_pair = use_pair_kernel(M, N, variant);
   const int stages = variant == 4 ? 7 : kPairStages;
+  const int pair_bn = variant == 5 ? 128 : 256;
   if (use_pair) {
     if (!a_mn) rc = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, 128);
     else rc = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, 64);
     if (rc) return -100 - rc;
-    if (!b_mn) rc = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, 128);
+    if (!b_mn) rc = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, pair_bn / 2);
     else rc = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, 64);
     if (rc) return -100 - rc;
     GemmArgs ga{M, N, K, D, ldd, reinterpret_cast<const __nv_bfloat16*>(R), ldr, alpha, err};
@@ -1205,10 +1209,10 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
       if (e != cudaSuccess) return static_cast<int>(e);
     }
     switch (epi) {
-      case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
-      case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
-      case kEpiF32Acc: return dispatch_major_pair<kEpiF32Acc>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
-      case kEpiBF16Res: return dispatch_major_pair<kEpiBF16Res>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages);
+      case kEpiBF16: return dispatch_major_pair<kEpiBF16>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages, pair_bn);
+      case kEpiF32: return dispatch_major_pair<kEpiF32>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages, pair_bn);
+      case kEpiF32Acc: return dispatch_major_pair<kEpiF32Acc>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages, pair_bn);
+      case kEpiBF16Res: return dispatch_major_pair<kEpiBF16Res>(a_mn, b_mn, ta, tb, ga, num_sms, stream, stages, pair_bn);
     }
     return -2;
   }

@@ -81,6 +81,16 @@ def replica_layout(table, cycles: list[list[int]], me: int, world: int):
     return rowbase, ranges
 
 
+def receive_capacity(holders: list[list[int]], world: int, max_tokens: int) -> int:
+    """Rows of every rank's receive segments.  The heap is symmetric: every rank must lay out the
+    same segment sizes, or a peer's segment offsets differ from this rank's and stores meant for
+    a peer's buffer land outside it.  So the size is the same on every rank -- that of the rank
+    holding the most experts (a speed-weighted placement gives ranks different expert counts);
+    each source rank sends at most ``max_tokens`` rows per expert."""
+    most_local = max(sum(1 for h in holders if r in h) for r in range(world))
+    return max_tokens * world * max(1, most_local)
+
+
 def receive_layout(table, holder: list[int], me: int, world: int) -> tuple[list[int], list[tuple[int, int]]]:
     """``replica_layout`` for one holder per expert: ``rowbase[e]`` at ``holder[e]``."""
     rowbase, ranges = replica_layout(table, [[h] for h in holder], me, world)
@@ -99,7 +109,7 @@ class ExpertParallelMoE:
         self.holders = [list(h) if isinstance(h, (list, tuple)) else [int(h)] for h in holder]
         self.cycles = replica_cycles(self.holders, speeds)
         self.local = [e for e in range(num_experts) if rank in self.holders[e]]
-        self.max_rows = max_tokens * world * max(1, len(self.local))
+        self.max_rows = receive_capacity(self.holders, world, max_tokens)
         self.device = torch.device(device)
         self.abort, self.budget = abort, budget_s
         segs = {"counts": (world * 16, torch.int32),
@@ -123,8 +133,7 @@ class ExpertParallelMoE:
         """``world`` ranks in one process on one GPU (tests); call each phase on every rank in turn."""
         E = kw["num_experts"]
         holders = [list(h) if isinstance(h, (list, tuple)) else [h] for h in kw["holder"]]
-        local = max(sum(1 for e in range(E) if r in holders[e]) for r in range(world))
-        rows = kw["max_tokens"] * world * max(1, local)
+        rows = receive_capacity(holders, world, kw["max_tokens"])
         H = kw["hidden"]
         segs = {"counts": (world * 16, torch.int32), "recv": (rows * H, torch.bfloat16), "y": (rows * H, torch.bfloat16),
                 "dyrecv": (rows * H, torch.bfloat16), "dxrecv": (rows * H, torch.bfloat16)}

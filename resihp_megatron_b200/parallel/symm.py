@@ -2,10 +2,11 @@
 
 Each rank allocates one device region holding a signal pad and named segments at identical
 offsets, shares it, and maps every peer's region; kernels then read and write peers' segments
-directly over NVLink.  Two ways to share a region: ``"vmm"`` -- a cuMem allocation exported as a POSIX file descriptor, which each peer receives over a
+directly over NVLink.  Two ways to share a region: ``"vmm"`` (the default where the driver offers
+it) -- a cuMem allocation exported as a POSIX file descriptor, which each peer receives over a
 Unix socket (``SCM_RIGHTS``) and maps into its own reserved range; the imported handle keeps the
 physical memory alive, so a departed peer's region stays mapped for the survivors until they drop
-it -- or ``"ipc"`` (the default): ``cudaMalloc`` plus a CUDA IPC handle.  A reconfiguration tears the heap down (``close``) and
+it -- or ``"ipc"``: ``cudaMalloc`` plus a CUDA IPC handle.  A reconfiguration tears the heap down (``close``) and
 builds the next generation's heap over the new world -- the counterpart of rebuilding NCCL
 communicators (reference: ``resihp/comm/comm_manager.py:138-251``).
 
@@ -157,9 +158,11 @@ def _receive_fd(name: str, timeout_s: float = 60.0) -> int:
 
 
 def default_alloc() -> str:
-    """``RESIHP_SYMM_ALLOC`` (``vmm`` / ``ipc``), else ``ipc``."""
+    """``RESIHP_SYMM_ALLOC`` (``vmm`` / ``ipc``), else ``vmm`` where the driver offers it."""
     want = os.environ.get("RESIHP_SYMM_ALLOC", "")
-    return want if want in ("vmm", "ipc") else "ipc"
+    if want in ("vmm", "ipc"):
+        return want
+    return "vmm" if ext().vmm_available() else "ipc"
 
 
 class SymmetricHeap:
@@ -191,8 +194,10 @@ class SymmetricHeap:
                 self._map_vmm(rank, world, exchange)
             else:
                 self.local_base, handle = ext().symm_alloc(self.nbytes, self.dev_index)
-                handles = exchange(handle) if world > 1 else [handle]
+                handles = exchange(handle + self.signature()) if world > 1 else [handle + self.signature()]
                 assert len(handles) == world
+                self._check_signatures([bytes(h)[-len(self.signature()):] for h in handles])
+                handles = [bytes(h)[: -len(self.signature())] for h in handles]
                 self.bases = []
                 for r, h in enumerate(handles):
                     if r == rank:
@@ -204,13 +209,30 @@ class SymmetricHeap:
         self.pads = torch.tensor(self.bases, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
 
+    def signature(self) -> bytes:
+        """16 bytes naming this heap's layout (segment names, offsets, sizes, total): every rank's
+        kernels address a peer's segment at this rank's offset, so all ranks must agree."""
+        import hashlib
+
+        desc = repr((self.nbytes, self.pad_bytes, sorted((n, g.offset, g.numel, str(g.dtype))
+                                                          for n, g in self.segments.items())))
+        return hashlib.sha256(desc.encode()).digest()[:16]
+
+    def _check_signatures(self, sigs: list[bytes]) -> None:
+        if any(sg != sigs[self.rank] for sg in sigs):
+            differ = [r for r, sg in enumerate(sigs) if sg != sigs[self.rank]]
+            raise RuntimeError(f"rank {self.rank}: symmetric heap layout differs on ranks {differ}; peer "
+                               "addresses would not match the peers' segments")
+
     def _map_vmm(self, rank: int, world: int, exchange) -> None:
         self.local_base, fd, size = ext().vmm_alloc(self.nbytes, self.dev_index)
         server = _FdServer(fd, world - 1) if world > 1 else None
         try:
-            mine = json.dumps({"sock": server.name if server else "", "size": size}).encode()
+            mine = json.dumps({"sock": server.name if server else "", "size": size,
+                               "sig": self.signature().hex()}).encode()
             handles = exchange(mine) if world > 1 else [mine]
             assert len(handles) == world
+            self._check_signatures([bytes.fromhex(json.loads(bytes(h).decode())["sig"]) for h in handles])
             self.bases = []
             for r, h in enumerate(handles):
                 if r == rank:

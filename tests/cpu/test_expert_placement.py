@@ -100,3 +100,28 @@ def test_smooth_round_robin_is_proportional_and_smooth(weights):
 def test_infeasible_slot_budget_raises():
     with pytest.raises(PlanInfeasible):
         plan_expert_placement([["a"]], 4, max_slots=3)
+
+
+def test_receive_capacity_is_rank_independent_and_bounds_every_layout():
+    """The symmetric heap's receive segments have one size on every rank, also when a
+    speed-weighted placement gives ranks different expert counts, and that size bounds what any
+    rank can receive: for every count table where each source routes at most T rows to each
+    expert, the rows landing on a rank fit."""
+    import random
+
+    from resihp_megatron_b200.parallel.moe_ep import receive_capacity, replica_cycles, replica_layout
+
+    rng = random.Random(0)
+    for _ in range(200):
+        world, E, T = rng.choice([2, 4, 8]), 8, rng.randint(1, 64)
+        holders = [[rng.randrange(world)] for _ in range(E)]
+        if rng.random() < 0.5:  # a replicated expert
+            e = rng.randrange(E)
+            holders[e] = sorted(set(holders[e] + [rng.randrange(world)]))
+        cap = receive_capacity(holders, world, T)
+        assert all(cap == receive_capacity(holders, world, T) for _ in range(world))
+        cycles = replica_cycles(holders)
+        table = [[rng.randint(0, T) for _ in range(E)] for _ in range(world)]
+        for me in range(world):
+            _, ranges = replica_layout(table, cycles, me, world)
+            assert sum(n for _, n in ranges) <= cap

@@ -149,19 +149,21 @@ def test_gemm_auto_split_on_a_partial_wave_shape():
     assert torch.equal(out, out2)
 
 
-@pytest.mark.parametrize("a_t,b_t", [(False, False), (True, True)])
+@pytest.mark.parametrize("variant", [4, 5])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("M,N,K", [(512, 1024, 1024), (1000, 520, 1000)])
-def test_gemm_seven_stage_ring_matches_six(M, N, K, a_t, b_t):
-    """The CTA-pair kernel with a 7-stage operand ring (variant 4) computes the same sums in the
-    same k order as the 6-stage one: bitwise equal, every epilogue."""
+def test_gemm_pair_ring_and_tile_variants_match(M, N, K, a_t, b_t, variant):
+    """The CTA-pair kernel with a 7-stage operand ring (variant 4) or 256 x 128 tiles (variant 5)
+    computes the same sums in the same k order as the default 6-stage 256 x 256 one: bitwise
+    equal, every operand layout, bf16 and fp32-accumulate epilogues."""
     from resihp_megatron_b200.ops.gemm import error_state, gemm
 
     a, b = _mk(M, N, K, a_t, b_t, seed=13)
-    assert torch.equal(gemm(a, b, a_t=a_t, b_t=b_t, variant=4), gemm(a, b, a_t=a_t, b_t=b_t, variant=2))
+    assert torch.equal(gemm(a, b, a_t=a_t, b_t=b_t, variant=variant), gemm(a, b, a_t=a_t, b_t=b_t, variant=2))
     base = torch.randn(M, N, device="cuda")
     acc6, acc7 = base.clone(), base.clone()
     gemm(a, b, a_t=a_t, b_t=b_t, out=acc6, accumulate=True, variant=2)
-    gemm(a, b, a_t=a_t, b_t=b_t, out=acc7, accumulate=True, variant=4)
+    gemm(a, b, a_t=a_t, b_t=b_t, out=acc7, accumulate=True, variant=variant)
     torch.cuda.synchronize()
     assert int(error_state()[0]) == 0
     assert torch.equal(acc6, acc7)
