@@ -121,6 +121,7 @@ class ResilientCommManager:
         self._groups_alive: list[Any] = []
         self._store: tuple[tuple[str, int], Any] | None = None
         self._abort_hooks: list[Callable[[], None]] = []
+        self._comms_aborted = False  # this generation's NCCL communicators were aborted
 
     # ------------------------------------------------------------------ capabilities
     @staticmethod
@@ -135,6 +136,8 @@ class ResilientCommManager:
     def can_shrink(self, new_world: list[str]) -> bool:
         """Whether the transition to ``new_world`` can use NCCL's in-place shrink."""
         if self.shrink == "never" or self.backend != "nccl" or self.current is None:
+            return False
+        if self._comms_aborted:  # aborted communicators cannot be shrunk: the next world starts fresh
             return False
         caps = self.capabilities()
         supported = caps["shrink_group"] and hasattr(c10d, "SHRINK_ABORT") and _nccl_at_least(caps["nccl_version"],
@@ -325,6 +328,7 @@ class ResilientCommManager:
         if self.backend == "nccl":
             with self._mu:
                 groups = list(self._groups_alive)
+                self._comms_aborted = bool(groups)
             # Every communicator is aborted on its own thread, subgroups first: a subgroup split
             # from the world communicator shares its proxy, and on B200 the world's abort waited
             # (until the watchdog timeout) while a subgroup's collective was stuck on a dead peer,
@@ -358,6 +362,7 @@ class ResilientCommManager:
                 log.exception("teardown of the previous generation failed; continuing")
         with self._mu:
             self._groups_alive = []
+            self._comms_aborted = False
         self.current = None
 
     def destroy(self) -> None:
