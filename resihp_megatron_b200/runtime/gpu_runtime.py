@@ -604,14 +604,18 @@ class GPUHybridRuntime:
                 sync.reduce()
         if step:
             self.apply_step()
-        loss = self.executor.loss_sum.clone()
-        work = dist.all_reduce(loss, async_op=True)
+        # the loss travels with a count of the ranks that took part: an NCCL collective cut short
+        # by a dead peer or an abort looks complete to the host, but its count falls short
+        loss_and_count = torch.stack([self.executor.loss_sum.reshape(()).float(),
+                                      torch.ones((), dtype=torch.float32, device=self.device)])
+        work = dist.all_reduce(loss_and_count, async_op=True)
         if self.mgr is not None:
             self.mgr.guarded_wait(work, what="loss all-reduce")
         else:
             work.wait()
         self.iteration = it + 1
-        return loss / self.tokens_per_step
+        self.last_participants = loss_and_count[1]
+        return loss_and_count[0] / self.tokens_per_step
 
     def apply_step(self) -> None:
         kw = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd)

@@ -25,6 +25,12 @@ from ..runtime.gpu_executor import TokenSource
 from ..state.transaction import TransactionManager
 
 
+def dist_world_size() -> int:
+    import torch.distributed as dist
+
+    return dist.get_world_size() if dist.is_initialized() else 1
+
+
 class GPUHybridBinding:
     def __init__(self, cfg: GPTConfig, client, mgr, *, micro_batch: int = 1, seq_len: int | None = None,
                  device="cuda", tp_impl: str = "collective", lr: float = 3e-4, seed: int = 0, data_seed: int = 1,
@@ -142,9 +148,24 @@ class GPUHybridBinding:
 
         class _Iteration:
             def run_iteration(self, iteration: int) -> float:
-                return float(binding.pending_or_committed().run_iteration(iteration, step=False).item())
+                rt = binding.pending_or_committed()
+                loss = float(rt.run_iteration(iteration, step=False).item())  # host synchronisation
+                binding.check_collectives(rt)
+                return loss
 
         return _Iteration()
+
+    def check_collectives(self, rt) -> None:
+        """After the iteration's host synchronisation: NCCL collectives that a dead peer or an
+        abort cut short return as if complete, so the iteration is only REDUCED if no abort came
+        and every rank was counted in its last all-reduce (otherwise it is replayed)."""
+        from ..comm.comm_manager import CommAborted
+
+        if self.mgr.aborted:
+            raise CommAborted("aborted while the iteration's collectives were in flight")
+        counted = int(round(float(rt.last_participants.item())))
+        if counted != dist_world_size():
+            raise CommAborted(f"the iteration's last all-reduce counted {counted} of {dist_world_size()} ranks")
 
     def pending_or_committed(self):
         return (self.pending or self.committed)[1]
