@@ -82,6 +82,10 @@ def _args():
     ap.add_argument("--fp8", action="store_true",
                     help="block-scaled fp8 projections (E4M3 forward / E5M2 backward, 1x128 activation and 128x128 "
                          "weight scales, amax history 16; benchmark config 4 with --model gpt-1.3b)")
+    ap.add_argument("--failstop", choices=["auto", "on", "off"], default="auto",
+                    help="hybrid layouts: after the timed steps and the teardown, run a real fail-stop on the same "
+                         "GPUs through the control plane (small demo model, one worker SIGKILLed at a step "
+                         "boundary) and report its fault->commit phases; 'auto' runs it at --gpus 2 or more")
     ap.add_argument("--chaos", choices=["auto", "on", "off"], default="auto",
                     help="after the timed steps, run one real-process kill trial of the CPU chaos harness (8 gloo "
                          "workers, coordinator + 2 agents; fault->commit seconds and its phases) through this arm's "
@@ -186,6 +190,42 @@ def chaos_trial(impl: str, timeout_s: float = 300.0) -> dict:
     return {"metric": "fault->commit (SIGKILL of 1 of 8 CPU gloo workers, TP2xPP2xDP2 reference MLP)",
             "value": total, "unit": "s", "higher_is_better": False, "phases_s": phases, "exact": exact,
             "iterations": CHAOS_ITERATIONS}
+
+
+def failstop_trial(world: int, timeout_s: float = 300.0) -> dict:
+    """Fault->commit of a real fail-stop on ``world`` GPUs through the control plane
+    (``resihp_megatron_b200.bench.gpu_failstop``: the small demo model at benchmark config 2's
+    layout scaled to ``world``; a worker is SIGKILLed at an iteration boundary), run in its own
+    process group and bounded in time."""
+    import signal
+
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    proc = subprocess.Popen([sys.executable, "-m", "resihp_megatron_b200.bench.gpu_failstop", "--gpus", str(world)],
+                            cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                            start_new_session=True)
+    try:
+        stdout, _ = proc.communicate(timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        os.killpg(proc.pid, signal.SIGKILL)  # the trial's own process group: its coordinator, agent, workers
+        proc.communicate()
+        return {"unavailable": f"GPU fail-stop trial did not finish within {timeout_s:.0f} s"}
+    rows = [ln for ln in stdout.splitlines() if ln.startswith("{")]
+    if proc.returncode != 0 or not rows:
+        return {"unavailable": f"GPU fail-stop trial exited {proc.returncode}"}
+    res = json.loads(rows[-1])
+    victim = res["victim"]
+    recovered = res["codes"].get(victim) == -9 and all(c == 0 for w, c in res["codes"].items() if w != victim)
+    phases = res.get("phases_s") or {}
+    return {"metric": "fault->commit (SIGKILL of 1 GPU worker at a step boundary, control plane, NCCL)",
+            "value": phases.get("total"), "unit": "s", "higher_is_better": False, "recovered": recovered,
+            "phases_s": phases, "gpus": res["gpus"], "layout": res["layout"], "model": "gpu-demo (4 layers)",
+            "iterations_completed": {w: len(v) for w, v in res.get("losses", {}).items()}}
+
+
+def want_failstop(args, world: int) -> bool:
+    return args.failstop == "on" or (args.failstop == "auto" and world >= 2)
 
 
 def want_chaos(args, world: int) -> bool:
@@ -672,18 +712,22 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
             recfg, alive = _hybrid_reconfig(args, trainer, world)
         except Exception as e:  # noqa: BLE001 -- the pre-reconfiguration line is still reported
             recfg, alive = {"error": f"{type(e).__name__}: {e}"[:400]}, False
+    out = None
     if rank == 0:
         out = _json_line(args, cfg, world, global_batch, mb, trainer.layout, r, {"layers_per_stage": parts})
         if recfg is not None:
             out["reconfig"] = recfg
         if want_chaos(args, world):
             out["chaos"] = chaos_trial("ours")
+    if alive:
+        dist.barrier()
+        trainer.close()
+        dist.barrier()
+    if rank == 0:
+        # after every rank released its collectives: the GPU fail-stop trial runs its own job
+        if want_failstop(args, world):
+            out["failstop"] = failstop_trial(world)
         print(json.dumps(out), flush=True)
-    if not alive:
-        return
-    dist.barrier()
-    trainer.close()
-    dist.barrier()
 
 
 def _hybrid_reconfig(args, trainer, world: int):
