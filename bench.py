@@ -221,7 +221,8 @@ def failstop_trial(world: int, timeout_s: float = 300.0) -> dict:
     return {"metric": "fault->commit (SIGKILL of 1 GPU worker at a step boundary, control plane, NCCL)",
             "value": phases.get("total"), "unit": "s", "higher_is_better": False, "recovered": recovered,
             "phases_s": phases, "gpus": res["gpus"], "layout": res["layout"], "model": "gpu-demo (4 layers)",
-            "iterations_completed": {w: len(v) for w, v in res.get("losses", {}).items()}}
+            "iterations_completed": {w: len(v) for w, v in res.get("losses", {}).items()},
+            "rebuild_s": next(iter((res.get("rebuild_s") or {}).values()), None)}
 
 
 def want_failstop(args, world: int) -> bool:

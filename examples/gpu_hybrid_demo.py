@@ -67,7 +67,7 @@ def main(argv=None) -> None:
     me = client.worker_id
     info = {"worker": me, "losses": {str(k): v for k, v in result.losses.items()}, "generations": result.generations,
             "standby": result.standby, "reconfigurations": result.reconfigurations,
-            "last_transfer": binding.last_transfer}
+            "last_transfer": binding.last_transfer, "last_recovery": binding.last_recovery}
     if binding.committed is not None and not result.standby:
         plan, _ = binding.committed
         g = plan.group_of_device(me)

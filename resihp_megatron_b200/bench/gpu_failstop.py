@@ -76,15 +76,16 @@ def run_trial(n: int, iterations: int = 6, kill_iteration: int = 2, out: str | N
     phases = None
     if stamp.exists():
         phases = breakdown(history, float(stamp.read_text().split()[1]))
-    losses = {}
+    losses, rebuild = {}, {}
     for w in codes:
         f = outdir / f"{w}.json"
         if w != victim and f.exists():
             info = json.loads(f.read_text())
             if not info["standby"]:
                 losses[w] = {int(k): v for k, v in info["losses"].items()}
+                rebuild[w] = info.get("last_recovery")
     return {"gpus": n, "layout": f"tp{tp}pp{pp}dp{dp}", "victim": victim, "codes": codes, "phases_s": phases,
-            "losses": losses, "out": str(outdir)}
+            "losses": losses, "rebuild_s": rebuild, "out": str(outdir)}
 
 
 def main(argv=None) -> None:

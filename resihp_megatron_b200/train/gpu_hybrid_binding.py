@@ -16,6 +16,8 @@ binding is Megatron's, ``resihp/train/megatron_binding.py``.)
 
 from __future__ import annotations
 
+import time
+
 import torch
 
 from ..models.config import GPTConfig
@@ -55,6 +57,7 @@ class GPUHybridBinding:
         self.committed = None  # (plan, runtime)
         self.pending = None
         self.last_transfer: dict = {}
+        self.last_recovery: dict = {}
 
     def _plan(self, payload: dict) -> tuple[HeteroParallelPlan, dict]:
         return HeteroParallelPlan.from_json(payload["plan"]), schedule_from_json(payload["schedule"])
@@ -80,13 +83,12 @@ class GPUHybridBinding:
         return gpu_tensor_specs(self.cfg, self.fp8.history if self.fp8 is not None else 0)
 
     def recover(self, comms, payload: dict, txm: TransactionManager) -> None:
-        import time
-
         from ..runtime.gpu_state import KINDS, export_state, gpu_layer_of, import_state
         from ..state.layer_registry import device_layout, holdings
         from ..state.transfer_engine import execute_transfers
         from ..state.transfer_plan import plan_transfers
 
+        started = time.monotonic()
         plan, schedule = self._plan(payload)
         rec = payload["recovery"]
         target = rec["target_iteration"]
@@ -98,6 +100,7 @@ class GPUHybridBinding:
             old[1].discard_grads()
             txm.discard()
         rt = self._runtime(plan, schedule, comms, init=old is None or target < 0)
+        built = time.monotonic()
         prev = payload.get("previous_plan")
         if rec.get("restore"):
             from ..runtime.gpu_state import load_checkpoint_into
@@ -142,6 +145,10 @@ class GPUHybridBinding:
                                   "seconds": time.monotonic() - t0}
         txm.discard()
         self.pending = (plan, rt)
+        # where a recovery's build time goes (the communicators were built just before)
+        self.last_recovery = {"comms_s": comms.build_seconds, "comms_phases_s": comms.stats.get("phases_s"),
+                              "runtime_build_s": round(built - started, 4),
+                              "state_s": round(time.monotonic() - built, 4)}
 
     def build_runtime(self, comms, payload: dict):
         binding = self
