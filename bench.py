@@ -85,7 +85,7 @@ def _args():
     ap.add_argument("--failstop", choices=["auto", "on", "off"], default="auto",
                     help="hybrid layouts: after the timed steps and the teardown, run a real fail-stop on the same "
                          "GPUs through the control plane (small demo model, one worker SIGKILLed at a step "
-                         "boundary) and report its fault->commit phases; 'auto' runs it at --gpus 2 or more")
+                         "boundary) and report its fault->commit phases; 'auto' runs it at --gpus 2 and 4")
     ap.add_argument("--chaos", choices=["auto", "on", "off"], default="auto",
                     help="after the timed steps, run one real-process kill trial of the CPU chaos harness (8 gloo "
                          "workers, coordinator + 2 agents; fault->commit seconds and its phases) through this arm's "
@@ -192,7 +192,7 @@ def chaos_trial(impl: str, timeout_s: float = 300.0) -> dict:
             "iterations": CHAOS_ITERATIONS}
 
 
-def failstop_trial(world: int, timeout_s: float = 300.0) -> dict:
+def failstop_trial(world: int, timeout_s: float = 150.0) -> dict:
     """Fault->commit of a real fail-stop on ``world`` GPUs through the control plane
     (``resihp_megatron_b200.bench.gpu_failstop``: the small demo model at benchmark config 2's
     layout scaled to ``world``; a worker is SIGKILLed at an iteration boundary), run in its own
@@ -226,7 +226,8 @@ def failstop_trial(world: int, timeout_s: float = 300.0) -> dict:
 
 
 def want_failstop(args, world: int) -> bool:
-    return args.failstop == "on" or (args.failstop == "auto" and world >= 2)
+    """``auto``: at the GPU counts where the trial has been run (2 and 4); ``on`` anywhere."""
+    return args.failstop == "on" or (args.failstop == "auto" and world in (2, 4))
 
 
 def want_chaos(args, world: int) -> bool:

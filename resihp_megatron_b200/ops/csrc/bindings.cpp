@@ -103,13 +103,14 @@ void gemm(const torch::Tensor& a, bool a_t, const torch::Tensor& b, bool b_t, to
     return;
   }
   const int sms = num_sms(a.get_device());
-  const int splits = rb::gemm_pair_splits(M, N, K, static_cast<int>(variant), sms);
+  int split_full = 0;
+  const int splits = rb::gemm_pair_splits(M, N, K, static_cast<int>(variant), sms, &split_full);
   torch::Tensor ws;
-  if (splits > 1) ws = split_workspace(a, rb::gemm_split_ws_bytes(M, N, splits));
+  if (splits > 1) ws = split_workspace(a, rb::gemm_split_ws_bytes(M, N, splits, split_full));
   const int rc = rb::gemm_bf16(a.data_ptr(), lda, a_t, b.data_ptr(), ldb, b_t, out.data_ptr(), ldd, rptr, ldr,
                                M, N, K, static_cast<int>(epi), static_cast<float>(alpha), err_ptr(a), sms,
                                at::cuda::getCurrentCUDAStream(), static_cast<int>(variant),
-                               splits > 1 ? ws.data_ptr() : nullptr, splits);
+                               splits > 1 ? ws.data_ptr() : nullptr, splits, split_full);
   TORCH_CHECK(rc == 0, "gemm_bf16 failed with code ", rc);
 }
 

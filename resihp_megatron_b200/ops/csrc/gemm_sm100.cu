@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -62,7 +63,38 @@ struct GemmArgs {
   int splits;
   float* split_ws;
   int* split_cnt;
+  // split only the tiles past the first `split_full` (the partial last wave): those run as
+  // `splits` shares each, the earlier ones whole
+  int split_full;
 };
+
+// One work unit of the CTA-pair kernel: tiles [0, full) whole, then the tail tiles' k shares in
+// share-major order (every tail tile's first share before any second share).  `tail_idx` < 0 for
+// a whole tile.
+struct PairUnit {
+  int tile, share, kb_lo, kb_hi, tail_idx;
+};
+
+__device__ __forceinline__ PairUnit pair_unit(int u, int num_tiles, int full, int splits, int kblocks) {
+  PairUnit w;
+  if (u < full || splits == 1) {
+    w.tile = u;
+    w.share = 0;
+    w.kb_lo = 0;
+    w.kb_hi = kblocks;
+    w.tail_idx = -1;
+    return w;
+  }
+  const int tail = num_tiles - full;
+  const int v = u - full;
+  const int kb_share = (kblocks + splits - 1) / splits;
+  w.tail_idx = v % tail;
+  w.tile = full + w.tail_idx;
+  w.share = v / tail;
+  w.kb_lo = w.share * kb_share;
+  w.kb_hi = min(kblocks, w.kb_lo + kb_share);
+  return w;
+}
 
 template <int BN>
 struct GemmCfg {
@@ -758,11 +790,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const int kblocks = (p.K + BK - 1) / BK;
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  const int splits = p.splits > 1 ? 2 : 1;  // the reduction below handles two shares
-  // unit u: tile u % num_tiles, k share u / num_tiles -- every tile's first share runs before any
-  // second share, so the units of a wave share A / B panels in L2 exactly as unsplit tiles do
-  const int num_units = num_tiles * splits;
-  const int kb_share = (kblocks + splits - 1) / splits;
+  const int splits = p.splits > 1 ? min(p.splits, 4) : 1;
+  const int full = splits > 1 ? min(max(p.split_full, 0), num_tiles) : num_tiles;
+  const int num_units = full + splits * (num_tiles - full);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -771,8 +801,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       for (int u = pair; u < num_units && !*abort_flag; u += num_pairs) {
-        const int tile = u % num_tiles;
-        const int kb_lo = (u / num_tiles) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
+        const PairUnit w = pair_unit(u, num_tiles, full, splits, kblocks);
+        const int tile = w.tile, kb_lo = w.kb_lo, kb_hi = w.kb_hi;
         int mb, nb;
         tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
         const int m0 = mb * 2 * BM + static_cast<int>(cta) * BM;
@@ -825,7 +855,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int acc = 0;
       uint32_t aphase = 0;
       for (int u = pair; u < num_units; u += num_pairs) {
-        const int kb_lo = (u / num_tiles) * kb_share, kb_hi = min(kblocks, kb_lo + kb_share);
+        const PairUnit w = pair_unit(u, num_tiles, full, splits, kblocks);
+        const int kb_lo = w.kb_lo, kb_hi = w.kb_hi;
         if (!mbar_wait(tempty_bar(acc), aphase ^ 1, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::BN;
@@ -869,7 +900,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t aphase = 0;
     for (int u = pair; u < num_units; u += num_pairs) {
-      const int tile = u % num_tiles, share = u / num_tiles;
+      const PairUnit w = pair_unit(u, num_tiles, full, splits, kblocks);
+      const int tile = w.tile, share = w.share;
+      const bool split_unit = w.tail_idx >= 0;
       int mb, nb;
       tile_coords(tile, num_m, num_n, C::GROUP_M, mb, nb);
       if (!warp_wait(tfull_bar(acc), aphase, abort_flag, p.err)) break;
@@ -877,9 +910,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const int row = mb * 2 * BM + static_cast<int>(cta) * BM + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::BN;
-      // workspace slots of this (tile, CTA, warp): `splits` consecutive 32 x 256 fp32 blocks
-      const long long slot0 = static_cast<long long>((tile * 2 + static_cast<int>(cta)) * 4 + q) * splits;
-      if (splits == 1) {
+      // workspace slots of this (tail tile, CTA, warp): `splits` consecutive 32 x BN fp32 blocks
+      const long long slot0 =
+          static_cast<long long>((max(w.tail_idx, 0) * 2 + static_cast<int>(cta)) * 4 + q) * splits;
+      if (!split_unit) {
 #pragma unroll 1
         for (int c = 0; c < C::BN / 32; ++c) {
           uint32_t r[32];
@@ -907,32 +941,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         if (leader) mbar_arrive(tempty_bar(acc));
         else mbar_arrive_cluster(release + acc * 8);
       }
-      if (splits > 1) {
+      if (split_unit) {
         // the accumulator is released already; the unit that arrives last reduces the slots
         __threadfence();
         __syncwarp();
-        int* cnt = p.split_cnt + (tile * 2 + static_cast<int>(cta)) * 4 + q;
+        int* cnt = p.split_cnt + (w.tail_idx * 2 + static_cast<int>(cta)) * 4 + q;
         int last = 0;
-        if (lane == 0) last = atomicAdd(cnt, 1) == 1;
+        if (lane == 0) last = atomicAdd(cnt, 1) == splits - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence();
-          // exactly two shares (the host plans 1 or 2): all 64 loads of a chunk are independent and
-          // in flight together -- a per-term loop over the shares serialised them, one L2 round
-          // trip per column, and made the split kernel ~10x slower than the unsplit one
+          // shares added in a fixed order; every share's 32 loads of a chunk are independent and in
+          // flight together (one load per round trip made an earlier version ~10x slower)
           const float* s0 = p.split_ws + slot0 * (32 * C::BN);
-          const float* s1 = s0 + 32 * C::BN;
 #pragma unroll 1
           for (int c = 0; c < C::BN / 32; ++c) {
             const int col0 = nb * C::BN + c * 32;
-            float a0[32], a1[32];
+            float a0[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) a0[i] = __ldcg(s0 + (c * 32 + i) * 32 + lane);
+            for (int sh = 1; sh < splits; ++sh) {
+              float b[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a1[i] = __ldcg(s1 + (c * 32 + i) * 32 + lane);
+              for (int i = 0; i < 32; ++i) b[i] = __ldcg(s0 + sh * (32 * C::BN) + (c * 32 + i) * 32 + lane);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) a0[i] += b[i];
+            }
             uint32_t r[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(a0[i] + a1[i]);
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(a0[i]);
             if (row_ok && col0 < p.N) store_chunk<EPI>(r, row, col0, p);
           }
           if (lane == 0) *cnt = 0;  // ready for the next launch (the host also clears it first)
@@ -1025,7 +1062,8 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   }
   const int tiles = ((a.M + 2 * C::BM - 1) / (2 * C::BM)) * ((a.N + C::BN - 1) / C::BN);
   int pairs = num_sms / 2;
-  const int units = tiles * (a.splits > 1 ? a.splits : 1);
+  const int full = a.splits > 1 ? a.split_full : tiles;
+  const int units = full + (a.splits > 1 ? a.splits : 1) * (tiles - full);
   if (units < pairs) pairs = units;
   kern<<<2 * pairs, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, a);
   return static_cast<int>(cudaGetLastError());
@@ -1140,41 +1178,54 @@ constexpr int kPairStages = 6;
 constexpr bool kAutoSplit = false;
 
 static bool use_pair_kernel(int M, int N, int variant) {
-  return (variant >= 2 && variant <= 5) || (variant == 0 && M >= 512 && N >= 256);
+  return (variant >= 2 && variant <= 6) || (variant == 0 && M >= 512 && N >= 256);
 }
 
-// Work units per output tile of the CTA-pair kernel.  Split-K in two shares pays when the tile
-// count leaves the last wave of SM pairs mostly idle (e.g. 256 tiles = 3.46 waves on 74 pairs ->
-// 512 units = 6.92 waves) and each share keeps >= 32 k-blocks; tile counts above 6 waves (where
-// the tail matters little) keep one unit per tile, which also bounds the workspace.
-int gemm_pair_splits(int M, int N, int K, int variant, int num_sms) {
+// Split plan of the CTA-pair kernel: returns the shares per split tile (1 = no split) and sets
+// `*full` to the number of leading tiles that run whole.  The automatic plan (variant 0 when
+// kAutoSplit, and variant 6) splits only the tiles of the partial last wave: with `tail` tiles
+// left after the full waves of the SM pairs, each is split into s = pairs / tail shares (at most
+// 4), so the last round takes 1 / s of a tile instead of a whole one; it is used when that saves
+// at least 5 % of the makespan and each share keeps >= 16 k-blocks.  Variant 3 splits every tile
+// in two.
+int gemm_pair_splits(int M, int N, int K, int variant, int num_sms, int* full) {
+  const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  *full = static_cast<int>(tiles);
   if (!use_pair_kernel(M, N, variant) || variant == 2 || variant == 4 || variant == 5) return 1;
   const int kblocks = (K + 63) / 64;
-  if (variant == 3) return kblocks >= 2 ? 2 : 1;
+  if (variant == 3) {
+    *full = 0;
+    return kblocks >= 2 ? 2 : 1;
+  }
+  if (variant == 0 && !kAutoSplit) return 1;
   const long long pairs = num_sms / 2;
-  const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
-  if (!kAutoSplit || pairs <= 0 || kblocks < 64 || tiles > 6 * pairs) return 1;
-  auto efficiency = [&](long long units) {
-    const long long waves = (units + pairs - 1) / pairs;
-    return static_cast<double>(units) / static_cast<double>(waves * pairs);
-  };
-  return efficiency(2 * tiles) > efficiency(tiles) + 0.04 ? 2 : 1;
+  if (pairs <= 0 || kblocks < 32) return 1;
+  const long long f = tiles / pairs * pairs, tail = tiles - f;
+  if (f == 0 || tail == 0) return 1;
+  const int shares = static_cast<int>(std::min<long long>({4, pairs / tail, kblocks / 16}));
+  if (shares < 2) return 1;
+  const double gain = (1.0 - 1.0 / shares) / (static_cast<double>(f / pairs) + 1.0);
+  if (gain < 0.05) return 1;
+  *full = static_cast<int>(f);
+  return shares;
 }
 
-// Workspace of a split launch: one 32 x 256 fp32 slot per (tile, CTA, epilogue warp, share),
-// then one counter per (tile, CTA, epilogue warp).
-long long gemm_split_ws_bytes(int M, int N, int splits) {
+// Workspace of a split launch: one 32 x 256 fp32 slot per (split tile, CTA, epilogue warp, share),
+// then one counter per (split tile, CTA, epilogue warp).
+long long gemm_split_ws_bytes(int M, int N, int splits, int full) {
   const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
-  return tiles * 8 * splits * (32LL * 256 * 4) + tiles * 8 * 4;
+  const long long tail = tiles - full;
+  return tail * 8 * splits * (32LL * 256 * 4) + tail * 8 * 4;
 }
 
 // A(m,k) = a_mn ? A[k*lda + m] : A[m*lda + k];  B(n,k) = b_mn ? B[k*ldb + n] : B[n*ldb + k].
 // Returns 0 on success, a negative value for a bad argument, else a CUDA error code.
-// `split_ws` (gemm_split_ws_bytes(M, N, splits) bytes, 16-byte aligned) is needed when
+// `split_ws` (gemm_split_ws_bytes(M, N, splits, split_full) bytes, 16-byte aligned) is needed when
 // `splits` (gemm_pair_splits) is above 1.
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn,
               void* D, long long ldd, const void* R, long long ldr, int M, int N, int K, int epi,
-              float alpha, int* err, int num_sms, cudaStream_t stream, int variant, void* split_ws, int splits) {
+              float alpha, int* err, int num_sms, cudaStream_t stream, int variant, void* split_ws, int splits,
+              int split_full) {
   if (M <= 0 || N <= 0 || K <= 0) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
   if ((lda * 2) % 16 || (ldb * 2) % 16) return -5;
@@ -1185,8 +1236,8 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
   CUtensorMap ta, tb;
   int rc;
   // variant: 0 auto (CTA pair for large tiles, split-K where it fills the last wave), 1 single
-  // CTA, 2 CTA pair without split, 3 CTA pair with split-K forced, 4 CTA pair with a 7-stage ring,
-  // 5 CTA pair with 256 x 128 tiles
+  // CTA, 2 CTA pair without split, 3 CTA pair with every tile split in two, 4 CTA pair with a
+  // 7-stage ring, 5 CTA pair with 256 x 128 tiles, 6 CTA pair with the partial last wave split
   const bool use_pair = use_pair_kernel(M, N, variant);
   const int stages = variant == 4 ? 7 : kPairStages;
   const int pair_bn = variant == 5 ? 128 : 256;
@@ -1202,10 +1253,13 @@ int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long 
     if (splits > 1) {
       if (split_ws == nullptr || (reinterpret_cast<uintptr_t>(split_ws) & 15)) return -8;
       const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+      if (split_full < 0 || split_full >= tiles || splits > 4) return -9;
+      const long long tail = tiles - split_full;
       ga.splits = splits;
+      ga.split_full = split_full;
       ga.split_ws = reinterpret_cast<float*>(split_ws);
-      ga.split_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(split_ws) + tiles * 8 * splits * (32LL * 256 * 4));
-      const cudaError_t e = cudaMemsetAsync(ga.split_cnt, 0, static_cast<size_t>(tiles * 8 * 4), stream);
+      ga.split_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(split_ws) + tail * 8 * splits * (32LL * 256 * 4));
+      const cudaError_t e = cudaMemsetAsync(ga.split_cnt, 0, static_cast<size_t>(tail * 8 * 4), stream);
       if (e != cudaSuccess) return static_cast<int>(e);
     }
     switch (epi) {

@@ -12,10 +12,12 @@ namespace rb {
 
 int gemm_bf16(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn, void* D,
               long long ldd, const void* R, long long ldr, int M, int N, int K, int epi, float alpha,
-              int* err, int num_sms, cudaStream_t stream, int variant = 0, void* split_ws = nullptr, int splits = 1);
-// Split-K plan of the CTA-pair GEMM (1 = none) and the workspace bytes a split launch needs.
-int gemm_pair_splits(int M, int N, int K, int variant, int num_sms);
-long long gemm_split_ws_bytes(int M, int N, int splits);
+              int* err, int num_sms, cudaStream_t stream, int variant = 0, void* split_ws = nullptr, int splits = 1,
+              int split_full = 0);
+// Split-K plan of the CTA-pair GEMM (shares per split tile, 1 = none; `*full` leading tiles run
+// whole) and the workspace bytes a split launch needs.
+int gemm_pair_splits(int M, int N, int K, int variant, int num_sms, int* full);
+long long gemm_split_ws_bytes(int M, int N, int splits, int full);
 
 int rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int T, int H, float eps, cudaStream_t s);
 int rmsnorm_bwd_blocks(int T);

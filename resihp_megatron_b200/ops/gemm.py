@@ -13,7 +13,8 @@ transpose:
 ``variant``: 0 picks the kernel (the 2-CTA ``cta_group::2`` kernel for M >= 512 and N >= 256,
 with split-K in two k shares when the tile count would leave the last wave of SM pairs mostly
 idle), 1 the single-CTA kernel, 2 the CTA pair without split, 3 the CTA pair with split forced,
-4 the CTA pair with a 7-stage operand ring, 5 the CTA pair with 256 x 128 tiles (tuning).
+4 the CTA pair with a 7-stage operand ring, 5 the CTA pair with 256 x 128 tiles, 6 the CTA pair
+with only the partial last wave's tiles split (tuning).
 
 The reference framework has no GEMM of its own; its compute path is Megatron/TE
 (``resihp/runtime/megatron_runtime.py``) and its GEMM probe is ``torch.matmul``

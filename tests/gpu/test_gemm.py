@@ -167,3 +167,27 @@ def test_gemm_pair_ring_and_tile_variants_match(M, N, K, a_t, b_t, variant):
     torch.cuda.synchronize()
     assert int(error_state()[0]) == 0
     assert torch.equal(acc6, acc7)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (2048, 3072, 4096)])
+def test_gemm_tail_split_variant(M, N, K):
+    """Variant 6 splits only the tiles of the partial last wave (2 shares for 256 tiles on 74 SM
+    pairs, 3 for 96 tiles): within bf16 rounding of fp32 and of the unsplit kernel, fp32
+    accumulation exact to fp32 tolerance, and bitwise equal run to run."""
+    from resihp_megatron_b200.ops.gemm import error_state, gemm
+
+    a, b = _mk(M, N, K, False, True, seed=14)
+    ref = _ref(a, b, False, True)
+    scale = ref.abs().max().item()
+    out = gemm(a, b, b_t=True, variant=6)
+    again = gemm(a, b, b_t=True, variant=6)
+    whole = gemm(a, b, b_t=True, variant=2)
+    base = torch.randn(M, N, device="cuda")
+    acc = base.clone()
+    gemm(a, b, b_t=True, out=acc, accumulate=True, variant=6)
+    torch.cuda.synchronize()
+    assert int(error_state()[0]) == 0
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * scale
+    assert (out.float() - whole.float()).abs().max().item() <= 1e-2 * scale
+    assert torch.equal(out, again)
+    assert torch.allclose(acc, base + ref, rtol=1e-4, atol=1e-3)
