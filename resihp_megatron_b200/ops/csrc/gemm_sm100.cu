@@ -1170,12 +1170,13 @@ int gemm_rs_scatter_bf16(const void* X, const void* W, bool w_mn, void* const* r
 // Operand-ring depth of the CTA-pair kernel for variants 0, 2 and 3.
 constexpr int kPairStages = 6;
 
-// Split-K chosen automatically by variant 0.  Off: measured on B200 (events, 20 launches), the
-// unsplit pair kernel is faster or equal on every Llama-3-8B shape that split-K targets -- 4096^3
-// 0.103 vs 0.137 ms, 4096 x 6144 x 4096 0.155 vs 0.210, 4096 x 4096 x 14336 0.358 vs 0.377,
-// 4096 x 4096 x 28672 0.715 vs 0.710 -- the partial-tile traffic costs more than the idle part
-// of the last wave.  It stays selectable (variant 3).
-constexpr bool kAutoSplit = false;
+// Split-K chosen automatically by variant 0: only the tiles of the partial last wave, and only
+// for K >= 8192 (128 k-blocks).  Measured on B200 (events, 20 launches, unsplit vs tail split):
+// 4096 x 4096 x 14336 0.358 vs 0.341 ms, 4096 x 4096 x 28672 0.706 vs 0.670 ms; at K = 4096 the
+// partial tiles' traffic cancels the gain (4096^3 0.104 vs 0.105).  Splitting every tile in two
+// (variant 3) lost on every shape (4096^3 0.104 vs 0.134).
+constexpr bool kAutoSplit = true;
+constexpr int kAutoSplitMinKBlocks = 128;
 
 static bool use_pair_kernel(int M, int N, int variant) {
   return (variant >= 2 && variant <= 6) || (variant == 0 && M >= 512 && N >= 256);
@@ -1199,7 +1200,7 @@ int gemm_pair_splits(int M, int N, int K, int variant, int num_sms, int* full) {
   }
   if (variant == 0 && !kAutoSplit) return 1;
   const long long pairs = num_sms / 2;
-  if (pairs <= 0 || kblocks < 32) return 1;
+  if (pairs <= 0 || kblocks < (variant == 0 ? kAutoSplitMinKBlocks : 32)) return 1;
   const long long f = tiles / pairs * pairs, tail = tiles - f;
   if (f == 0 || tail == 0) return 1;
   const int shares = static_cast<int>(std::min<long long>({4, pairs / tail, kblocks / 16}));

@@ -135,11 +135,11 @@ def test_gemm_split_k_variant(M, N, K, a_t, b_t):
 
 
 def test_gemm_auto_split_on_a_partial_wave_shape():
-    """M = N = K = 4096 is 256 pair tiles (3.46 waves on 74 pairs), the shape split-K is meant for:
-    the default variant stays within bf16 rounding of fp32 and deterministic."""
+    """M = N = 4096 is 256 pair tiles (3.46 waves on 74 pairs); at K = 8192 the default variant
+    splits the partial last wave's tiles: within bf16 rounding of fp32 and deterministic."""
     from resihp_megatron_b200.ops.gemm import error_state, gemm
 
-    a, b = _mk(4096, 4096, 4096, False, True, seed=12)
+    a, b = _mk(4096, 4096, 8192, False, True, seed=12)
     out = gemm(a, b, b_t=True)
     out2 = gemm(a, b, b_t=True)
     ref = _ref(a, b, False, True)
