@@ -713,7 +713,10 @@ __global__ void __launch_bounds__(320, 1)
 //   * both CTAs' TMA loads count on the leader's full barrier (the leader expects both halves);
 //   * the leader issues the MMAs and commits separately to each CTA's empty / accumulator-full
 //     barriers (no multicast);
-//   * epilogue warps of both CTAs release the accumulator on the leader's barrier (8 arrivals).
+//   * epilogue warps of both CTAs release the accumulator on the leader's barrier (8 arrivals);
+//   * optional split-K of the tiles of the partial last wave (`PairUnit`): full waves run whole
+//     tiles, each tail tile runs as up to 4 k shares whose fp32 partials the last-arriving share
+//     adds in a fixed order (deterministic) before the epilogue.
 template <int kStages, int kBN = 256>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA (the pair covers 256)
