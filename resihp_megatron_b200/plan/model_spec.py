@@ -164,5 +164,28 @@ class ModelProfile:
         return asdict(self)
 
     @classmethod
+    def calibrated(cls, spec: ModelSpec, directory=None) -> "ModelProfile | None":
+        """The measured profile (``bench/profile_gpu.py`` output under ``plan/profiles/``) of a
+        model with ``spec``'s layer shape, or None.  Link fields keep the analytic B200 values."""
+        import json
+        from pathlib import Path
+
+        root = Path(directory) if directory is not None else Path(__file__).resolve().parent / "profiles"
+        if not root.is_dir():
+            return None
+        for path in sorted(root.glob("*.json")):
+            doc = json.loads(path.read_text())
+            shape = doc.get("shape", {})
+            if (shape.get("hidden"), shape.get("ffn"), shape.get("heads"), shape.get("kv_heads")) == (
+                    spec.hidden, spec.ffn, spec.num_heads, spec.num_kv_heads):
+                analytic = cls.b200(spec)
+                measured = {k: v for k, v in doc["profile"].items() if k in ("alpha", "beta", "bwd_ratio",
+                                                                             "tp_overhead")}
+                from dataclasses import replace
+
+                return replace(analytic, **measured)
+        return None
+
+    @classmethod
     def from_json(cls, d: dict) -> "ModelProfile":
         return cls(**d)

@@ -43,7 +43,9 @@ def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatche
 
     spec = ModelSpec(num_layers=cfg.layers, hidden=cfg.hidden, ffn=cfg.ffn, num_heads=cfg.heads,
                      num_kv_heads=cfg.kv_heads, vocab=cfg.vocab_size, seq_len=seq_len, micro_batch_size=micro_batch)
-    pc = PlannerConfig(model=spec, profile=ModelProfile.b200(spec), num_stages=pp, num_replicas=dp, tp=tp,
+    # the measured profile of this layer shape when one is committed, else the analytic B200 one
+    profile = ModelProfile.calibrated(spec) or ModelProfile.b200(spec)
+    pc = PlannerConfig(model=spec, profile=profile, num_stages=pp, num_replicas=dp, tp=tp,
                        num_microbatches=num_microbatches, sequence_parallel=sequence_parallel, mem_capacity=math.inf)
     return HeteroPlanner(pc), ClusterTopology.uniform(1, tp * pp * dp)
 
