@@ -167,6 +167,7 @@ class ResilientCommManager:
         t_groups = time.monotonic()
         if self.validate:
             self._validate(len(world), groups, specs)
+            self._check_epoch(generation, world)
         t_end = time.monotonic()
         comms = GenerationComms(generation, rank, tuple(world), {s.name: s for s in specs}, groups, path,
                                 t_end - started)
@@ -257,6 +258,20 @@ class ResilientCommManager:
         with self._mu:
             self._groups_alive += [pg for pg in mine.values() if pg not in self._groups_alive]
         return {s.name: mine.get(s.ranks) if (s.materialized and rank in s.ranks) else None for s in specs}
+
+    def _check_epoch(self, generation: int, world: list[str]) -> None:
+        """Generation handshake: every rank of the new world must be building the same
+        generation (a straggler still in an older transaction would otherwise join collectives
+        meant for another plan).  One MAX all-reduce of (generation, -generation)."""
+        on_gpu = self.backend == "nccl" and self.device
+        device = torch.device(self.device) if on_gpu else torch.device("cpu")
+        epoch = torch.tensor([generation, -generation], dtype=torch.int64, device=device)
+        self.guarded_wait(dist.all_reduce(epoch, op=dist.ReduceOp.MAX, async_op=True),
+                          timeout=self.validate_timeout_s, what="generation handshake")
+        highest, lowest = int(epoch[0].item()), -int(epoch[1].item())
+        if highest != generation or lowest != generation:
+            raise GenerationBuildError(f"ranks of the new world build generations {lowest}..{highest}, "
+                                       f"this rank {generation}", suspects=tuple(range(len(world))))
 
     def _validate(self, world_size: int, groups: dict[str, Any], specs: list[GroupSpec]) -> None:
         """An all-reduce of ones under a deadline on the world and on every group of this rank."""

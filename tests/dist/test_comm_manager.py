@@ -81,3 +81,23 @@ def test_abort_ends_a_blocked_collective_quickly(store):
     out = res[0]
     assert out["aborted"] and out["hooked"]
     assert out["latency"] < 1.0 + 2.0, out
+
+
+def _mismatched_generation(rank, world, port, store_addr):
+    from resihp_megatron_b200.comm.comm_manager import GenerationBuildError, ResilientCommManager
+
+    ids = [f"w{i}" for i in range(world)]
+    mgr = ResilientCommManager("gloo", timeout_s=30)
+    try:  # rank 1 is one transaction behind: it builds generation 4 while rank 0 builds 5
+        mgr.build(5 - rank, ids, ids[rank], [], store_addr=store_addr, store_prefix="epoch/gen/")
+        refused = False
+    except GenerationBuildError:
+        refused = True
+    mgr.destroy()
+    return {"refused": refused}
+
+
+def test_generation_handshake_refuses_ranks_of_different_generations(store):
+    """Every rank of a new world checks that all ranks build the same generation number."""
+    res = spawn(_mismatched_generation, 2, store, timeout=120)
+    assert res[0]["refused"] and res[1]["refused"], res
