@@ -34,9 +34,10 @@ def ensure_process_group(device: torch.device) -> None:
 
 
 def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatches: int, micro_batch: int,
-                   seq_len: int, sequence_parallel: bool = True):
+                   seq_len: int, sequence_parallel: bool = True, vpp: int = 1, split_backward: bool = False):
     """The joint planner for a ``tp x pp x dp`` layout of ``cfg`` on one node, and the node's
-    topology (device ids ``n0g{i}``)."""
+    topology (device ids ``n0g{i}``).  ``vpp``: model chunks per pipeline slot (interleaved
+    schedule); ``split_backward``: zero-bubble schedules with the weight-gradient pass split off."""
     from ..plan.model_spec import ModelProfile, ModelSpec
     from ..plan.planner import HeteroPlanner, PlannerConfig
     from ..plan.topology import ClusterTopology
@@ -46,7 +47,8 @@ def layout_planner(cfg: GPTConfig, *, tp: int, pp: int, dp: int, num_microbatche
     # the measured profile of this layer shape when one is committed, else the analytic B200 one
     profile = ModelProfile.calibrated(spec) or ModelProfile.b200(spec)
     pc = PlannerConfig(model=spec, profile=profile, num_stages=pp, num_replicas=dp, tp=tp,
-                       num_microbatches=num_microbatches, sequence_parallel=sequence_parallel, mem_capacity=math.inf)
+                       num_microbatches=num_microbatches, sequence_parallel=sequence_parallel, mem_capacity=math.inf,
+                       vpp=vpp, split_backward=split_backward)
     return HeteroPlanner(pc), ClusterTopology.uniform(1, tp * pp * dp)
 
 
@@ -54,13 +56,16 @@ class GPUHybridTrainer:
     def __init__(self, cfg: GPTConfig, *, tp: int, pp: int, dp: int, global_batch: int, micro_batch: int = 1,
                  seq_len: int | None = None, tp_impl: str = "fused", dp_impl: str = "fused", seed: int = 0,
                  lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0, device=None,
-                 data_seed: int = 1, migrate: str = "p2p", fp8=None, sequence_parallel: bool = True):
+                 data_seed: int = 1, migrate: str = "p2p", fp8=None, sequence_parallel: bool = True,
+                 vpp: int = 1, split_backward: bool = False):
         """``migrate``: how a reconfiguration moves state on GPUs -- ``"p2p"`` (one strided peer
         copy launch per rank over NVLink, ``parallel.migration``) or ``"nccl"`` (one send/receive
         per slice and kind, ``state.transfer_engine``).  ``fp8``: an ``Fp8Recipe`` (block-scaled
         fp8 projections; the per-layer amax histories migrate and checkpoint with their layers).
         ``sequence_parallel=False``: plain tensor parallelism (replicated token rows, GEMM ->
-        all-reduce)."""
+        all-reduce).  ``vpp``: model chunks per pipeline slot (interleaved 1F1B);
+        ``split_backward``: zero-bubble schedules (the weight-gradient pass of each micro-batch
+        runs separately, where the schedule puts it)."""
         from ..comm.comm_manager import ResilientCommManager
         from ..runtime.gpu_executor import TokenSource
         from ..runtime.gpu_runtime import GPUHybridRuntime
@@ -71,6 +76,8 @@ class GPUHybridTrainer:
             raise ValueError(f"tp {tp} x pp {pp} x dp {dp} != world size {world}")
         if global_batch % micro_batch:
             raise ValueError("the global batch must be a multiple of the micro-batch")
+        if vpp > 1 and pp < 2:
+            raise ValueError("interleaving (vpp > 1) needs at least 2 pipeline stages to alternate between")
         if migrate not in ("p2p", "nccl"):
             raise ValueError(migrate)
         self.migrate = migrate
@@ -82,7 +89,8 @@ class GPUHybridTrainer:
         self.sequence_parallel = sequence_parallel
         self.planner, self.topology = layout_planner(cfg, tp=tp, pp=pp, dp=dp, num_microbatches=n_micro,
                                                      micro_batch=micro_batch, seq_len=self.S,
-                                                     sequence_parallel=sequence_parallel)
+                                                     sequence_parallel=sequence_parallel, vpp=vpp,
+                                                     split_backward=split_backward)
         self.plan = self.planner.initial_plan(self.topology)
         self.schedule, _ = self.planner.schedule(self.plan, self.topology)
         ids = list(self.plan.world)

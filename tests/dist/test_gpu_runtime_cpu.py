@@ -224,3 +224,39 @@ def test_checkpoint_written_by_one_layout_resumes_in_another(tmp_path):
     got = first[0] + second[0]
     for a, b in zip(got, ref):
         assert abs(a - b) <= 1e-2 * abs(b), (got, ref)
+
+
+def _trainer_schedules(rank, world, port):
+    import torch.distributed as dist
+
+    from tests.helpers import fake_kernels
+
+    fake_kernels.install()
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    out = {}
+    try:  # interleaving needs a second pipeline stage to alternate with
+        GPUHybridTrainer(_cfg(), tp=1, pp=1, dp=1, global_batch=4, micro_batch=1, seq_len=S, device="cpu", vpp=2)
+        out["vpp_on_one_stage"] = "accepted"
+    except ValueError as e:
+        out["vpp_on_one_stage"] = str(e)
+    for name, kw in (("1f1b", {}), ("zero_bubble", {"split_backward": True})):
+        tr = GPUHybridTrainer(_cfg(), tp=1, pp=1, dp=1, global_batch=4, micro_batch=1, seq_len=S,
+                              tp_impl="collective", dp_impl="collective", device="cpu", lr=1e-2, **kw)
+        out[name] = {"losses": [tr.train_step() for _ in range(3)], "chunks": len(tr.runtime.chunks),
+                     "w_ops": sum(ins.op.name == "W" for stream in tr.schedule.values() for ins in stream)}
+        tr.close()
+    dist.destroy_process_group()
+    return out
+
+
+def test_hybrid_trainer_zero_bubble_schedule_and_vpp_check():
+    """The trainer's ``split_backward`` schedule (each micro-batch's weight-gradient pass split off)
+    trains like plain 1F1B; ``vpp > 1`` on a single pipeline stage is refused up front."""
+    res = spawn(_trainer_schedules, 1, timeout=300)[0]
+    assert res["zero_bubble"]["w_ops"] == 4 and res["1f1b"]["w_ops"] == 0
+    assert "pipeline stages" in res["vpp_on_one_stage"], res["vpp_on_one_stage"]
+    for name in ("zero_bubble",):
+        for a, b in zip(res[name]["losses"], res["1f1b"]["losses"]):
+            assert abs(a - b) <= 1e-3 * abs(b), (name, res[name]["losses"], res["1f1b"]["losses"])
