@@ -158,12 +158,17 @@ def bench_fp8(a, t: Timer) -> None:
 
     frac(emit("gemm_fp8_fwd_blockscaled", t(lambda: fp8.gemm(xq.rowwise(), wq.rowwise(), out=out)), flops=fl,
               shape=[M, N, K]))
+    frac(emit("gemm_fp8_fwd_register_promotion", t(lambda: fp8.gemm(xq.rowwise(), wq.rowwise(), out=out, variant=1)),
+              flops=fl, shape=[M, N, K]))
     # weight-gradient layout: both operands scaled per row along K (per-column scales of B)
     dy = torch.randn(K, M, device="cuda").bfloat16()
     dyq = fp8.quantize(dy, fp8.E5M2, rowwise=True)
     g = torch.zeros(K, N, device="cuda")
     xq2 = fp8.quantize(torch.randn(N, M, device="cuda").bfloat16(), fp8.E4M3, rowwise=True)
     frac(emit("gemm_fp8_wgrad_blockscaled", t(lambda: fp8.gemm(dyq.rowwise(), xq2.rowwise(), out=g, accumulate=True)),
+              flops=fl, shape=[K, N, M]))
+    frac(emit("gemm_fp8_wgrad_register_promotion",
+              t(lambda: fp8.gemm(dyq.rowwise(), xq2.rowwise(), out=g, accumulate=True, variant=1)),
               flops=fl, shape=[K, N, M]))
     try:
         a8, b8 = x.to(torch.float8_e4m3fn), w.to(torch.float8_e4m3fn)

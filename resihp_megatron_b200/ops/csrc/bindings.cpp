@@ -765,8 +765,10 @@ static void check_scale(const torch::Tensor& s, int64_t kb, int64_t row, int64_t
 void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, int64_t sa_kb, int64_t sa_row,
               int64_t sa_shift, const torch::Tensor& b, int64_t b_fmt, const torch::Tensor& sb, int64_t sb_kb,
               int64_t sb_row, int64_t sb_shift, const c10::optional<torch::Tensor>& out, int64_t epi, double alpha,
-              const c10::optional<torch::Tensor>& residual, const std::vector<int64_t>& rs_ptrs, int64_t rs_slot) {
+              const c10::optional<torch::Tensor>& residual, const std::vector<int64_t>& rs_ptrs, int64_t rs_slot,
+              int64_t variant) {
   check_fp8(a, "a");
+  TORCH_CHECK(variant >= 0 && variant <= 2, "gemm_fp8: variant is 0 (tensor-core scaling), 1 (register promotion) or 2");
   check_fp8(b, "b");
   // Every shape rule of the kernel is checked here, before any pointer or tensor map is formed.
   TORCH_CHECK(a.size(0) > 0 && a.size(1) > 0 && b.size(0) > 0 && a.size(0) % 128 == 0 && a.size(1) % 128 == 0 &&
@@ -803,12 +805,16 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
   }
   check_scale(sa, sa_kb, sa_row, sa_shift, M, K, "sa");
   check_scale(sb, sb_kb, sb_row, sb_shift, N, K, "sb");
+  if (variant == 1 && sb_shift == 0)
+    TORCH_CHECK(sb_row == 1 && sb_kb % 4 == 0 && reinterpret_cast<uintptr_t>(sb.data_ptr()) % 16 == 0,
+                "gemm_fp8: per-column B scales need unit row stride, K-block stride a multiple of 4, 16-byte base");
   const c10::cuda::CUDAGuard g(a.device());
   RB_CALL(rb::gemm_fp8(a.data_ptr(), static_cast<int>(a_fmt), b.data_ptr(), static_cast<int>(b_fmt),
                        sa.data_ptr<float>(), sa_kb, sa_row, static_cast<int>(sa_shift), sb.data_ptr<float>(), sb_kb,
                        sb_row, static_cast<int>(sb_shift), dptr, ldd, M, N, K, static_cast<int>(epi),
                        static_cast<float>(alpha), err_ptr(a), num_sms(a.get_device()), cur_stream(), rptr, ldr,
-                       dst.empty() ? nullptr : dst.data(), static_cast<int>(dst.size()), static_cast<int>(rs_slot)),
+                       dst.empty() ? nullptr : dst.data(), static_cast<int>(dst.size()), static_cast<int>(rs_slot),
+                       static_cast<int>(variant)),
           "gemm_fp8");
 }
 
@@ -841,7 +847,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM", py::arg("a"), py::arg("a_fmt"), py::arg("sa"),
         py::arg("sa_kb"), py::arg("sa_row"), py::arg("sa_shift"), py::arg("b"), py::arg("b_fmt"), py::arg("sb"),
         py::arg("sb_kb"), py::arg("sb_row"), py::arg("sb_shift"), py::arg("out"), py::arg("epi"), py::arg("alpha"),
-        py::arg("residual") = py::none(), py::arg("rs_ptrs") = std::vector<int64_t>{}, py::arg("rs_slot") = 0);
+        py::arg("residual") = py::none(), py::arg("rs_ptrs") = std::vector<int64_t>{}, py::arg("rs_slot") = 0,
+        py::arg("variant") = 0);
   m.def("adam_step", &adam_step);
   m.def("sumsq", &sumsq);
   m.def("cross_entropy", &cross_entropy);

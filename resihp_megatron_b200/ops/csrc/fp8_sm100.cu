@@ -527,6 +527,312 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
   return static_cast<int>(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------- hardware block-scaled GEMM
+// gemm_fp8_mx_sm100: the same product with the scales applied by the tensor core
+// (tcgen05.mma.kind::mxf8f6f4.block_scale, one E8M0 scale per 32 K-elements of every A row and
+// every B row).  A power-of-two 1 x 128 (or 128 x 128) scale 2^e is the E8M0 byte e + 127,
+// repeated over the four 32-deep sub-blocks of its 128-deep K-block, so the hardware applies
+// exactly the scales the promotion kernel applies, and no promotion warps or partial
+// accumulators are needed.  Per CTA: a 128 x 256 output tile, 4-deep ring of 128 x 128-byte A and
+// 256 x 128-byte B tiles plus the K-block's scale factors, single 256-column TMEM accumulator.
+//   warp 0     : producer.  All lanes turn the K-block's fp32 scales into E8M0 words in the
+//                layout tcgen05.cp expects (row r of a 128-row group: 16-byte row r % 32,
+//                word r / 32), fence them into the async proxy; lane 0 issues the two TMA loads.
+//   warp 1     : TMEM allocator and single-thread issuer: per K-block three tcgen05.cp
+//                (32x128b.warpx4: A's 128 rows into 4 columns, B's 256 rows into 8 columns,
+//                two alternating column sets) and four block-scaled MMAs (K = 32 each).
+//   warps 2..9 : epilogue, two warps per TMEM lane quadrant, 128 columns each: the whole row
+//                segment is read into registers, the accumulator is released at once (the next
+//                tile's MMAs start while these warps convert and store), then stored.
+struct Mx8Cfg {
+  static constexpr int BM = 128, BN = 256, BK = 128;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int SFA_BYTES = 512;            // 128 rows x one 32-bit word of E8M0 bytes
+  static constexpr int SF_BYTES = SFA_BYTES * 3;   // A, then B's two 128-row groups
+  static constexpr int STAGES = 4;
+  static constexpr int TMEM_COLS = 512;  // accumulator in 0..255, scale factors from column 256
+  static constexpr int SF_COL = 256;
+  static constexpr int NUM_BARS = 2 * STAGES + 3;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES + SF_BYTES) + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 320;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int GROUP_M = 16;
+  static_assert(SMEM_BYTES <= 232448, "over the 227 KB of dynamic shared memory a CTA may have");
+};
+
+// Instruction descriptor of kind::mxf8f6f4.block_scale: A / B formats (E4M3 0, E5M2 1), K-major
+// operands, N >> 3 at bit 17, E8M0 scale factors (bit 23), M >> 4 at bit 24; the scale-factor
+// byte selectors (bits 4-5 for B, 29-30 for A) stay 0: every byte of a scale word is the same.
+__host__ __device__ constexpr uint32_t make_idesc_mx8(int M, int N, int a_fmt, int b_fmt) {
+  return (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(b_fmt) << 10) |
+         ((static_cast<uint32_t>(N) >> 3) << 17) | (1u << 23) | ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_mx8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Shared memory -> TMEM copy of 32 rows x 16 bytes, broadcast to all four 32-lane quadrants:
+// TMEM lane 32 q + l, columns 0..3, get bytes 16 l .. 16 l + 15 of the block.
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// E8M0 byte of a power-of-two fp32 scale, repeated in all four bytes of a word.
+__device__ __forceinline__ uint32_t e8m0_word(float s) { return ((__float_as_uint(s) >> 23) & 0xffu) * 0x01010101u; }
+
+__device__ __forceinline__ void mx8_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = Mx8Cfg::GROUP_M * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * Mx8Cfg::GROUP_M;
+  const int gsize = min(num_m - first_m, Mx8Cfg::GROUP_M);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(320, 1)
+    gemm_fp8_mx_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      F8GemmArgs p) {
+  using C = Mx8Cfg;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* sSF = sB + STAGES * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSF + STAGES * C::SF_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  const uint32_t tfull_bar = smem_u32(&bars[2 * STAGES]);
+  const uint32_t tempty_bar = smem_u32(&bars[2 * STAGES + 1]);
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 2]);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, C::EPI_WARPS);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = p.M / C::BM;
+  const int num_n = (p.N + C::BN - 1) / C::BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = p.K / C::BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (whole warp)
+    // The scales of work item i (the K-block kb of the CTA's tile i / kblocks) are loaded at
+    // item i - 4 into one of four register sets (the loop is unrolled by 4 so that every set is
+    // a fixed group of registers): their global-load latency overlaps the ring's waits instead
+    // of stalling every K-block.
+    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int total = my_tiles * kblocks;
+    float fa[4][4], fb[4][8];
+    auto load_scales = [&](int i, float (&a)[4], float (&b)[8]) {
+      if (i >= total) return;
+      const int tile = blockIdx.x + (i / kblocks) * gridDim.x, kb = i % kblocks;
+      int mb, nb;
+      mx8_tile_coords(tile, num_m, num_n, mb, nb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = mb * C::BM + lane + 32 * j;
+        a[j] = __ldg(p.sa + kb * p.sa_kb + static_cast<long long>(m >> p.sa_shift) * p.sa_row);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int n = nb * C::BN + (j >> 2) * 128 + lane + 32 * (j & 3);
+        // rows past N are zero-filled by the TMA; give them scale 1
+        b[j] = n < p.N ? __ldg(p.sb + kb * p.sb_kb + static_cast<long long>(n >> p.sb_shift) * p.sb_row) : 1.0f;
+      }
+    };
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load_scales(u, fa[u], fb[u]);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool ok = true;
+    for (int i0 = 0; i0 < total && ok; i0 += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u;
+        if (!ok || i >= total) break;
+        const int tile = blockIdx.x + (i / kblocks) * gridDim.x, kb = i % kblocks;
+        int mb, nb;
+        mx8_tile_coords(tile, num_m, num_n, mb, nb);
+        int go = 0;
+        if (lane == 0) go = (!*abort_flag && mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, go, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sf = sSF + stage * C::SF_BYTES + lane * 16;
+        *reinterpret_cast<uint4*>(sf) =
+            make_uint4(e8m0_word(fa[u][0]), e8m0_word(fa[u][1]), e8m0_word(fa[u][2]), e8m0_word(fa[u][3]));
+        *reinterpret_cast<uint4*>(sf + C::SFA_BYTES) =
+            make_uint4(e8m0_word(fb[u][0]), e8m0_word(fb[u][1]), e8m0_word(fb[u][2]), e8m0_word(fb[u][3]));
+        *reinterpret_cast<uint4*>(sf + 2 * C::SFA_BYTES) =
+            make_uint4(e8m0_word(fb[u][4]), e8m0_word(fb[u][5]), e8m0_word(fb[u][6]), e8m0_word(fb[u][7]));
+        fence_proxy_async_smem();  // the words are read by tcgen05.cp (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t fbar = full_bar(stage);
+          mbar_arrive_expect_tx(fbar, C::A_BYTES + C::B_BYTES);
+          tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fbar, kb * C::BK, mb * C::BM);
+          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fbar, kb * C::BK, nb * C::BN);
+        }
+        load_scales(i + 4, fa[u], fb[u]);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (lane == 0)
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0, set = 0;
+      uint32_t phase = 0, tphase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar, tphase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sf = smem_u32(sSF + stage * C::SF_BYTES);
+          const uint32_t t_sfa = tmem_base + C::SF_COL + set * 16;
+          const uint32_t t_sfb = t_sfa + 4;
+          // 32 rows of 16 bytes: 8-row core matrices 128 bytes apart, no swizzle
+          tmem_cp_32x128b_warpx4(t_sfa, make_smem_desc(sf, 128, 128, kSwizzleNone));
+          tmem_cp_32x128b_warpx4(t_sfb, make_smem_desc(sf + C::SFA_BYTES, 128, 128, kSwizzleNone));
+          tmem_cp_32x128b_warpx4(t_sfb + 4, make_smem_desc(sf + 2 * C::SFA_BYTES, 128, 128, kSwizzleNone));
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 32; ++k) {
+            const uint64_t ad = make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
+            umma_mx8(tmem_base, ad, bd, p.idesc, t_sfa, t_sfb, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          set ^= 1;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar);
+        tphase ^= 1;
+      }
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint32_t tphase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      mx8_tile_coords(tile, num_m, num_n, mb, nb);
+      if (!f8_warp_wait(tfull_bar, tphase, abort_flag, p.err)) break;
+      tphase ^= 1;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld_32x32b_x32(tb, r0);
+      tmem_ld_32x32b_x32(tb + 32, r1);
+      tmem_ld_32x32b_x32(tb + 64, r2);
+      tmem_ld_32x32b_x32(tb + 96, r3);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar);  // the next tile's MMAs may overwrite the accumulator
+      const int row = mb * C::BM + q * 32 + lane;
+      const int col0 = nb * C::BN + half * 128;
+      if (col0 < p.N) {
+        float v[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r0[j]);
+          v[32 + j] = __uint_as_float(r1[j]);
+        }
+        f8_store_row<EPI>(v, row, col0, p);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r2[j]);
+          v[32 + j] = __uint_as_float(r3[j]);
+        }
+        f8_store_row<EPI>(v, row, col0 + 64, p);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int EPI>
+int launch_mx8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a, int num_sms, cudaStream_t s) {
+  auto kern = gemm_fp8_mx_sm100<EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Mx8Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  const int tiles = (a.M / Mx8Cfg::BM) * ((a.N + Mx8Cfg::BN - 1) / Mx8Cfg::BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kern<<<grid, Mx8Cfg::THREADS, Mx8Cfg::SMEM_BYTES, s>>>(ta, tb, a);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
@@ -551,8 +857,9 @@ int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d,
 int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
              int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
              int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream, const void* R,
-             long long ldr, void* const* rs_dst, int world, int rs_slot) {
+             long long ldr, void* const* rs_dst, int world, int rs_slot, int variant) {
   if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 128) return -3;
+  if (variant < 0 || variant > 2) return -3;
   if ((a_fmt != kFp8E4M3 && a_fmt != kFp8E5M2) || (b_fmt != kFp8E4M3 && b_fmt != kFp8E5M2)) return -3;
   if ((sa_shift != 0 && sa_shift != 7) || (sb_shift != 0 && sb_shift != 7)) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
@@ -571,17 +878,29 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
   }
   if (epi == kF8EpiBF16Res && (R == nullptr || (reinterpret_cast<uintptr_t>(R) & 15) || ldr % 8 || ldr < N)) return -9;
   const bool sb_vec = sb_shift == 0;
-  if (sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;
+  const bool mx = variant != 1;  // 0 (default) and 2: scales applied by the tensor core
+  if (!mx && sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_2d_sw128(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, 128, 128)) return -100 - rc;
-  if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, 128)) return -100 - rc;
+  if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, mx ? Mx8Cfg::BN : 128))
+    return -100 - rc;
   a.M = M; a.N = N; a.K = K;
-  a.idesc = make_idesc_f8(128, 128, a_fmt, b_fmt);
+  a.idesc = mx ? make_idesc_mx8(Mx8Cfg::BM, Mx8Cfg::BN, a_fmt, b_fmt) : make_idesc_f8(128, 128, a_fmt, b_fmt);
   a.D = D; a.ldd = ldd; a.alpha = alpha;
   a.sa = sa; a.sa_kb = sa_kb; a.sa_row = sa_row; a.sa_shift = sa_shift;
   a.sb = sb; a.sb_kb = sb_kb; a.sb_row = sb_row; a.sb_shift = sb_shift;
   a.err = err;
   a.R = static_cast<const __nv_bfloat16*>(R); a.ldr = ldr;
+  if (mx) {
+    switch (epi) {
+      case kF8EpiBF16: return launch_mx8<kF8EpiBF16>(ta, tb, a, num_sms, stream);
+      case kF8EpiF32: return launch_mx8<kF8EpiF32>(ta, tb, a, num_sms, stream);
+      case kF8EpiF32Acc: return launch_mx8<kF8EpiF32Acc>(ta, tb, a, num_sms, stream);
+      case kF8EpiBF16Res: return launch_mx8<kF8EpiBF16Res>(ta, tb, a, num_sms, stream);
+      case kF8EpiScatter: return launch_mx8<kF8EpiScatter>(ta, tb, a, num_sms, stream);
+    }
+    return -2;
+  }
   switch (epi) {
     case kF8EpiBF16: return sb_vec ? launch_fp8<true, kF8EpiBF16>(ta, tb, a, num_sms, stream)
                                    : launch_fp8<false, kF8EpiBF16>(ta, tb, a, num_sms, stream);

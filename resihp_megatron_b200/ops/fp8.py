@@ -234,18 +234,23 @@ def _check_operands(a: Fp8Operand, b: Fp8Operand) -> None:
 
 def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
          accumulate: bool = False, alpha: float = 1.0, residual: torch.Tensor | None = None,
-         scatter: tuple[list[int], int] | None = None) -> torch.Tensor | None:
+         scatter: tuple[list[int], int] | None = None, variant: int = 0) -> torch.Tensor | None:
     """``out [a.rows, b.rows] (+)= alpha * block-scaled a @ b^T`` (all dims multiples of 128).
     ``residual``: bf16 ``out = product + residual``.  ``scatter = (recv_ptrs, slot)``: no local
     output; row ``m`` is stored (bf16) into rank ``m // (rows / world)``'s receive buffer
     ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter.
-    Shapes and scale addressing are validated here, before the extension is called."""
+    Shapes and scale addressing are validated here, before the extension is called.
+    ``variant``: 0 (default) applies the scales in the tensor core (block-scaled MMA, E8M0 scale
+    per 32 K-elements; exact for these power-of-two scales), 1 promotes per 128-deep K-block in
+    registers (the earlier kernel, kept for comparison)."""
     _check_operands(a, b)
+    if variant not in (0, 1, 2):
+        raise ValueError("variant is 0 (tensor-core scaling), 1 (register promotion) or 2")
     if scatter is not None:
         ptrs, slot = scatter
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, None, EPI_SCATTER,
-                       float(alpha), None, [int(p) for p in ptrs], int(slot))
+                       float(alpha), None, [int(p) for p in ptrs], int(slot), variant=variant)
         count(1)
         return None
     if residual is not None:
@@ -253,7 +258,7 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
             out = torch.empty(a.rows, b.rows, dtype=torch.bfloat16, device=a.data.device)
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, EPI_BF16_RES,
-                       float(alpha), residual)
+                       float(alpha), residual, variant=variant)
         count(1)
         return out
     if accumulate:
@@ -267,7 +272,8 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
         out = torch.empty(a.rows, b.rows, dtype=torch.float32 if epi != EPI_BF16 else torch.bfloat16,
                           device=a.data.device)
     ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
-                   b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, epi, float(alpha))
+                   b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, epi, float(alpha),
+                   variant=variant)
     count(1)
     return out
 

@@ -50,8 +50,11 @@ def _check(out, ref, tol):
     assert err <= tol * ref.float().abs().max().item() + 1e-30, err
 
 
+@pytest.mark.parametrize("variant", [0, 1])
 @pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1024, 1024, 2048), (128, 128, 128)])
-def test_gemm_forward_dgrad_wgrad(M, N, K):
+def test_gemm_forward_dgrad_wgrad(M, N, K, variant):
+    """Variant 0 applies the scales in the tensor core (block-scaled MMA), 1 in registers per
+    K-block; both against the PyTorch emulation of the same block-scaled product."""
     x = _x(M, K, seed=1, spread=1.0)
     w = (_x(N, K, seed=2, spread=0.5).float() * 0.05).bfloat16()
     dy = (_x(M, N, seed=4, spread=1.0).float() * 1e-3).bfloat16()
@@ -59,17 +62,17 @@ def test_gemm_forward_dgrad_wgrad(M, N, K):
     wq = fp8.quantize(w, fp8.E4M3, two_d=True, rowwise=True, colwise=True)
     dyq = fp8.quantize(dy, fp8.E5M2, rowwise=True, colwise=True)
     # forward: per-row A scales, 128 x 128 B scales
-    y = fp8.gemm(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32)
+    y = fp8.gemm(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32, variant=variant)
     _check(y, fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32), 1e-5)
-    yb = fp8.gemm(xq.rowwise(), wq.rowwise())
+    yb = fp8.gemm(xq.rowwise(), wq.rowwise(), variant=variant)
     _check(yb, fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32), 8e-3)
     # dgrad: E5M2 x E4M3, transposed 2-D weight scales
-    dx = fp8.gemm(dyq.rowwise(), wq.colwise(), out_dtype=torch.float32)
+    dx = fp8.gemm(dyq.rowwise(), wq.colwise(), out_dtype=torch.float32, variant=variant)
     _check(dx, fp8.gemm_reference(dyq.rowwise(), wq.colwise(), out_dtype=torch.float32), 1e-5)
     # wgrad: per-column B scales, fp32 accumulate with alpha
     g0 = torch.randn(N, K, device="cuda")
     g = g0.clone()
-    fp8.gemm(dyq.colwise(), xq.colwise(), out=g, accumulate=True, alpha=0.5)
+    fp8.gemm(dyq.colwise(), xq.colwise(), out=g, accumulate=True, alpha=0.5, variant=variant)
     ref = g0.clone()
     fp8.gemm_reference(dyq.colwise(), xq.colwise(), out=ref, accumulate=True, alpha=0.5)
     _check(g - g0, ref - g0, 1e-5)
@@ -112,7 +115,8 @@ def test_gelu_fwd_bwd():
     assert torch.equal(h2, dh)
 
 
-def test_gemm_residual_and_scatter_epilogues():
+@pytest.mark.parametrize("variant", [0, 1])
+def test_gemm_residual_and_scatter_epilogues(variant):
     M, N, K, world = 512, 256, 384, 4
     x = _x(M, K, seed=5, spread=1.0)
     w = (_x(N, K, seed=6, spread=0.5).float() * 0.05).bfloat16()
@@ -120,13 +124,13 @@ def test_gemm_residual_and_scatter_epilogues():
     xq = fp8.quantize(x, fp8.E4M3)
     wq = fp8.quantize(w, fp8.E4M3, two_d=True)
     ref = fp8.gemm_reference(xq.rowwise(), wq.rowwise(), out_dtype=torch.float32)
-    y = fp8.gemm(xq.rowwise(), wq.rowwise(), residual=res)
+    y = fp8.gemm(xq.rowwise(), wq.rowwise(), residual=res, variant=variant)
     _check(y, ref + res.float(), 8e-3)
     # scatter: rows of rank q's share land in slot 1 of buffer q ([world][M / world][N])
     rows = M // world
     bufs = [torch.zeros(world, rows, N, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
-    fp8.gemm(xq.rowwise(), wq.rowwise(), scatter=([b.data_ptr() for b in bufs], 1))
-    full = fp8.gemm(xq.rowwise(), wq.rowwise())
+    fp8.gemm(xq.rowwise(), wq.rowwise(), scatter=([b.data_ptr() for b in bufs], 1), variant=variant)
+    full = fp8.gemm(xq.rowwise(), wq.rowwise(), variant=variant)
     for q in range(world):
         assert torch.equal(bufs[q][1], full[q * rows:(q + 1) * rows])
         assert bufs[q][0].abs().sum().item() == 0 and bufs[q][2:].abs().sum().item() == 0
@@ -186,3 +190,27 @@ def test_quantize_of_the_activation_equals_activation_then_quantize(act):
     assert torch.equal(got.q_row.view(torch.uint8), ref.q_row.view(torch.uint8))
     assert torch.equal(got.q_col.view(torch.uint8), ref.q_col.view(torch.uint8))
     assert torch.equal(got.s_row, ref.s_row) and torch.equal(got.s_col, ref.s_col)
+
+
+def test_gemm_tensor_core_scaling_tracks_register_promotion_with_wide_scale_spread():
+    """Rows of A and B whose magnitudes span many binades, so that every 1 x 128 row scale and
+    every 128 x 128 weight scale differs: the tensor-core scaled product (per-row E8M0 words in
+    TMEM) and the register-promoted one agree to fp32 summation order, and both track the
+    emulation -- a scale placed on the wrong row or row group would not."""
+    M, N, K = 512, 768, 1024
+    g = torch.Generator(device="cuda").manual_seed(11)
+    rs = torch.exp2(torch.randint(-12, 12, (M, 1), device="cuda", generator=g).float())
+    cs = torch.exp2(torch.randint(-12, 12, (N, 1), device="cuda", generator=g).float())
+    x = (torch.randn(M, K, device="cuda", generator=g) * rs).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * cs).bfloat16()
+    xq = fp8.quantize(x, fp8.E4M3, rowwise=True)
+    wq = fp8.quantize(w, fp8.E4M3, two_d=True, rowwise=True)
+    wv = fp8.quantize(w, fp8.E4M3, rowwise=True)  # per-row B scales as well
+    for b in (wq.rowwise(), wv.rowwise()):
+        ref = fp8.gemm_reference(xq.rowwise(), b, out_dtype=torch.float32)
+        y0 = fp8.gemm(xq.rowwise(), b, out_dtype=torch.float32, variant=0)
+        y1 = fp8.gemm(xq.rowwise(), b, out_dtype=torch.float32, variant=1)
+        # relative to each row's own magnitude: small rows must be right too
+        scale = ref.abs().amax(dim=1, keepdim=True) + 1e-30
+        assert ((y0 - ref).abs() / scale).max().item() < 1e-5
+        assert ((y1 - ref).abs() / scale).max().item() < 1e-5

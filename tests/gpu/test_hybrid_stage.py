@@ -122,3 +122,30 @@ def test_single_rank_stage_matches_llama_model_in_fp8_with_gelu():
                           (P.g(p + "wo"), M.g(p + "wo")), (P.g(p + "w2"), M.g(p + "w2"))):
             err = (got - want).abs().max().item()
             assert err <= 1e-5 * (want.abs().max().item() + 1e-12), err
+
+
+def test_hybrid_trainer_split_backward_matches_1f1b_on_one_gpu():
+    """``split_backward=True`` runs each micro-batch's weight-gradient pass as its own W op after
+    the input-gradient pass (the zero-bubble order); on one GPU it computes the same sums in the
+    same order as plain 1F1B, so the losses agree to bf16 rounding of the deferred GEMMs."""
+    import torch.distributed as dist
+
+    from resihp_megatron_b200.models.config import TINY
+    from resihp_megatron_b200.train.hybrid_trainer import GPUHybridTrainer, ensure_process_group
+
+    cfg = TINY.with_(hidden=256, heads=2, kv_heads=1, ffn=512, layers=2, vocab_size=512, seq_len=256)
+    ensure_process_group(torch.device("cuda", torch.cuda.current_device()))
+    try:
+        runs = {}
+        for name, kw in (("1f1b", {}), ("zb", {"split_backward": True})):
+            torch.manual_seed(0)
+            tr = GPUHybridTrainer(cfg, tp=1, pp=1, dp=1, global_batch=4, micro_batch=1, seq_len=256, lr=3e-3,
+                                  tp_impl="collective", dp_impl="collective", **kw)
+            w_ops = sum(ins.op.name == "W" for stream in tr.schedule.values() for ins in stream)
+            runs[name] = (w_ops, [tr.train_step() for _ in range(4)])
+            tr.close()
+        assert runs["1f1b"][0] == 0 and runs["zb"][0] == 4
+        for a, b in zip(runs["1f1b"][1], runs["zb"][1]):
+            assert math.isfinite(b) and abs(a - b) <= 2e-3 * abs(a), (runs["1f1b"][1], runs["zb"][1])
+    finally:
+        dist.destroy_process_group()
