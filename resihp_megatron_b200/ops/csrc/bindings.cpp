@@ -809,12 +809,14 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
     TORCH_CHECK(sb_row == 1 && sb_kb % 4 == 0 && reinterpret_cast<uintptr_t>(sb.data_ptr()) % 16 == 0,
                 "gemm_fp8: per-column B scales need unit row stride, K-block stride a multiple of 4, 16-byte base");
   const c10::cuda::CUDAGuard g(a.device());
+  torch::Tensor sf_ws;  // packed scale words of the block-scaled path (stream-ordered, from the caching allocator)
+  if (variant != 1) sf_ws = torch::empty({rb::gemm_fp8_sf_bytes(M, N, K)}, a.options().dtype(torch::kUInt8));
   RB_CALL(rb::gemm_fp8(a.data_ptr(), static_cast<int>(a_fmt), b.data_ptr(), static_cast<int>(b_fmt),
                        sa.data_ptr<float>(), sa_kb, sa_row, static_cast<int>(sa_shift), sb.data_ptr<float>(), sb_kb,
                        sb_row, static_cast<int>(sb_shift), dptr, ldd, M, N, K, static_cast<int>(epi),
                        static_cast<float>(alpha), err_ptr(a), num_sms(a.get_device()), cur_stream(), rptr, ldr,
                        dst.empty() ? nullptr : dst.data(), static_cast<int>(dst.size()), static_cast<int>(rs_slot),
-                       static_cast<int>(variant)),
+                       static_cast<int>(variant), sf_ws.defined() ? sf_ws.data_ptr() : nullptr),
           "gemm_fp8");
 }
 

@@ -12,8 +12,11 @@
 // with it when the rows are gathered from other ranks.  Each CTA folds the magnitude of its tile into one atomicMax on the tensor's amax
 // word (bit pattern of |x|, so NaN and inf win), the input of the delayed-scaling history.
 //
-// GEMM (gemm_fp8_sm100).  D[m, n] = alpha * sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A(m, k) B(n, k)
-// for A [M, K] and B [N, K], both K-major fp8, K-blocks of 128.  One persistent CTA per SM:
+// GEMM.  D[m, n] = alpha * sum_kb sa(m, kb) sb(n, kb) sum_{k in kb} A(m, k) B(n, k) for A [M, K]
+// and B [N, K], both K-major fp8, K-blocks of 128.  Two kernels compute it: gemm_fp8_mx_sm100
+// (the default, described where it is defined) lets the tensor core apply the scales through
+// the block-scaled MMA; gemm_fp8_sm100 (variant 1) promotes each K-block's partial product in
+// registers.  The latter, one persistent CTA per SM:
 //   warp 0     : TMA producer, 6-deep ring of 128 x 128-byte A and B tiles, 128B swizzle
 //   warp 1     : TMEM allocator and single-thread issuer: per K-block four
 //                tcgen05.mma.kind::f8f6f4 (K = 32 each) into one of four 128-column TMEM
@@ -209,6 +212,10 @@ struct F8GemmArgs {
   // slot `rs_slot` of its receive buffer ([world][rs_rows][N], possibly another GPU's memory)
   int rs_slot, rs_rows;
   void* rs_dst[kF8MaxTP];
+  // gemm_fp8_mx_sm100: E8M0 scale words packed by mx8_pack_scales, [K-block][128-row group][512 B]
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int sfb_groups;  // 128-row groups of B after padding N to the 256-row tile
 };
 
 struct F8Cfg {
@@ -535,9 +542,11 @@ int launch_fp8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
 // exactly the scales the promotion kernel applies, and no promotion warps or partial
 // accumulators are needed.  Per CTA: a 128 x 256 output tile, 4-deep ring of 128 x 128-byte A and
 // 256 x 128-byte B tiles plus the K-block's scale factors, single 256-column TMEM accumulator.
-//   warp 0     : producer.  All lanes turn the K-block's fp32 scales into E8M0 words in the
-//                layout tcgen05.cp expects (row r of a 128-row group: 16-byte row r % 32,
-//                word r / 32), fence them into the async proxy; lane 0 issues the two TMA loads.
+//   warp 0     : producer (one thread): per K-block the A and B tiles by TMA and the K-block's
+//                scale words by two untiled bulk copies, all on one barrier.  The words are
+//                packed beforehand by mx8_pack_scales in the layout tcgen05.cp expects (row r of
+//                a 128-row group: 16-byte row r % 32, word r / 32, the E8M0 byte four times), so
+//                the scales travel like the operands: no register round trip, no proxy fence.
 //   warp 1     : TMEM allocator and single-thread issuer: per K-block three tcgen05.cp
 //                (32x128b.warpx4: A's 128 rows into 4 columns, B's 256 rows into 8 columns,
 //                two alternating column sets) and four block-scaled MMAs (K = 32 each).
@@ -587,6 +596,20 @@ __device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t 
 
 // E8M0 byte of a power-of-two fp32 scale, repeated in all four bytes of a word.
 __device__ __forceinline__ uint32_t e8m0_word(float s) { return ((__float_as_uint(s) >> 23) & 0xffu) * 0x01010101u; }
+
+// Packs fp32 power-of-two scales (scale of row r in K-block kb at s[kb * s_kb + (r >> shift) *
+// s_row]) into E8M0 words for the block-scaled GEMM: for K-block kb and 128-row group g, a
+// 512-byte block at (kb * groups + g) * 512 whose word (r % 32) * 4 + (r % 128) / 32 holds row r's
+// byte four times.  Rows in [rows, rows_pad) get scale 1 (their operand rows are zero-filled).
+__global__ void mx8_pack_scales(const float* __restrict__ s, long long s_kb, long long s_row, int shift, int rows,
+                                int rows_pad, int kblocks, uint32_t* __restrict__ out) {
+  const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= static_cast<long long>(rows_pad) * kblocks) return;
+  const int kb = static_cast<int>(t / rows_pad), r = static_cast<int>(t % rows_pad);
+  const int rr = r & 127;
+  const uint32_t w = r < rows ? e8m0_word(s[kb * s_kb + static_cast<long long>(r >> shift) * s_row]) : 0x7f7f7f7fu;
+  out[(static_cast<long long>(kb) * (rows_pad / 128) + (r >> 7)) * 128 + (rr & 31) * 4 + (rr >> 5)] = w;
+}
 
 __device__ __forceinline__ void mx8_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = Mx8Cfg::GROUP_M * num_n;
@@ -653,78 +676,41 @@ __global__ void __launch_bounds__(320, 1)
   const int kblocks = p.K / C::BK;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer (whole warp)
-    // The scales of work item i (the K-block kb of the CTA's tile i / kblocks) are loaded at
-    // item i - 4 into one of four register sets (the loop is unrolled by 4 so that every set is
-    // a fixed group of registers): their global-load latency overlaps the ring's waits instead
-    // of stalling every K-block.
-    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int total = my_tiles * kblocks;
-    float fa[4][4], fb[4][8];
-    auto load_scales = [&](int i, float (&a)[4], float (&b)[8]) {
-      if (i >= total) return;
-      const int tile = blockIdx.x + (i / kblocks) * gridDim.x, kb = i % kblocks;
-      int mb, nb;
-      mx8_tile_coords(tile, num_m, num_n, mb, nb);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int m = mb * C::BM + lane + 32 * j;
-        a[j] = __ldg(p.sa + kb * p.sa_kb + static_cast<long long>(m >> p.sa_shift) * p.sa_row);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int n = nb * C::BN + (j >> 2) * 128 + lane + 32 * (j & 3);
-        // rows past N are zero-filled by the TMA; give them scale 1
-        b[j] = n < p.N ? __ldg(p.sb + kb * p.sb_kb + static_cast<long long>(n >> p.sb_shift) * p.sb_row) : 1.0f;
-      }
-    };
-#pragma unroll
-    for (int u = 0; u < 4; ++u) load_scales(u, fa[u], fb[u]);
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, issued_parity = 0;
-    bool ok = true;
-    for (int i0 = 0; i0 < total && ok; i0 += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u;
-        if (!ok || i >= total) break;
-        const int tile = blockIdx.x + (i / kblocks) * gridDim.x, kb = i % kblocks;
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      const int a_groups = p.M / 128;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         int mb, nb;
         mx8_tile_coords(tile, num_m, num_n, mb, nb);
-        int go = 0;
-        if (lane == 0) go = (!*abort_flag && mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, go, 0)) {
-          ok = false;
-          break;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+          tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fb, kb * C::BK, mb * C::BM);
+          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * C::BK, nb * C::BN);
+          const uint32_t sf = smem_u32(sSF + stage * C::SF_BYTES);
+          bulk_load_1d(sf, p.sfa + (static_cast<long long>(kb) * a_groups + mb) * C::SFA_BYTES, C::SFA_BYTES, fb);
+          bulk_load_1d(sf + C::SFA_BYTES, p.sfb + (static_cast<long long>(kb) * p.sfb_groups + 2 * nb) * C::SFA_BYTES,
+                       2 * C::SFA_BYTES, fb);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        uint8_t* sf = sSF + stage * C::SF_BYTES + lane * 16;
-        *reinterpret_cast<uint4*>(sf) =
-            make_uint4(e8m0_word(fa[u][0]), e8m0_word(fa[u][1]), e8m0_word(fa[u][2]), e8m0_word(fa[u][3]));
-        *reinterpret_cast<uint4*>(sf + C::SFA_BYTES) =
-            make_uint4(e8m0_word(fb[u][0]), e8m0_word(fb[u][1]), e8m0_word(fb[u][2]), e8m0_word(fb[u][3]));
-        *reinterpret_cast<uint4*>(sf + 2 * C::SFA_BYTES) =
-            make_uint4(e8m0_word(fb[u][4]), e8m0_word(fb[u][5]), e8m0_word(fb[u][6]), e8m0_word(fb[u][7]));
-        fence_proxy_async_smem();  // the words are read by tcgen05.cp (async proxy)
-        __syncwarp();
-        if (lane == 0) {
-          const uint32_t fbar = full_bar(stage);
-          mbar_arrive_expect_tx(fbar, C::A_BYTES + C::B_BYTES);
-          tma_load_2d(smem_u32(sA + stage * C::A_BYTES), &tmA, fbar, kb * C::BK, mb * C::BM);
-          tma_load_2d(smem_u32(sB + stage * C::B_BYTES), &tmB, fbar, kb * C::BK, nb * C::BN);
-        }
-        load_scales(i + 4, fa[u], fb[u]);
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
+        if (!ok) break;
       }
-    }
-    if (lane == 0)
       for (int s = 0; s < STAGES; ++s)
         if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -835,6 +821,11 @@ int launch_mx8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
 
 }  // namespace
 
+long long gemm_fp8_sf_bytes(int M, int N, int K) {
+  const long long n_pad = (N + Mx8Cfg::BN - 1) / Mx8Cfg::BN * Mx8Cfg::BN;
+  return 4LL * (K / 128) * (M + n_pad);
+}
+
 int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d, void* q_row, float* s_row,
                  void* q_col, float* s_col, unsigned int* amax, cudaStream_t s, int s_row_major, int act) {
   if (R <= 0 || C <= 0 || C % kQT || (fmt != kFp8E4M3 && fmt != kFp8E5M2)) return -3;
@@ -857,7 +848,7 @@ int fp8_quantize(const void* x, long long ldx, int R, int C, int fmt, int two_d,
 int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa, long long sa_kb, long long sa_row,
              int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
              int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream, const void* R,
-             long long ldr, void* const* rs_dst, int world, int rs_slot, int variant) {
+             long long ldr, void* const* rs_dst, int world, int rs_slot, int variant, void* sf_ws) {
   if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 128) return -3;
   if (variant < 0 || variant > 2) return -3;
   if ((a_fmt != kFp8E4M3 && a_fmt != kFp8E5M2) || (b_fmt != kFp8E4M3 && b_fmt != kFp8E5M2)) return -3;
@@ -892,6 +883,19 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
   a.err = err;
   a.R = static_cast<const __nv_bfloat16*>(R); a.ldr = ldr;
   if (mx) {
+    if (sf_ws == nullptr || (reinterpret_cast<uintptr_t>(sf_ws) & 15)) return -10;
+    const int kblocks = K / 128;
+    const int n_pad = (N + Mx8Cfg::BN - 1) / Mx8Cfg::BN * Mx8Cfg::BN;
+    uint32_t* wa = static_cast<uint32_t*>(sf_ws);
+    uint32_t* wb = wa + static_cast<long long>(kblocks) * M;  // one word per row per K-block
+    const long long na = static_cast<long long>(kblocks) * M, nb = static_cast<long long>(kblocks) * n_pad;
+    mx8_pack_scales<<<static_cast<unsigned>((na + 255) / 256), 256, 0, stream>>>(sa, sa_kb, sa_row, sa_shift, M, M,
+                                                                                 kblocks, wa);
+    mx8_pack_scales<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, stream>>>(sb, sb_kb, sb_row, sb_shift, N,
+                                                                                 n_pad, kblocks, wb);
+    a.sfa = reinterpret_cast<const uint8_t*>(wa);
+    a.sfb = reinterpret_cast<const uint8_t*>(wb);
+    a.sfb_groups = n_pad / 128;
     switch (epi) {
       case kF8EpiBF16: return launch_mx8<kF8EpiBF16>(ta, tb, a, num_sms, stream);
       case kF8EpiF32: return launch_mx8<kF8EpiF32>(ta, tb, a, num_sms, stream);

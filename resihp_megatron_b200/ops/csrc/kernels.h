@@ -151,7 +151,9 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
              int sa_shift, const float* sb, long long sb_kb, long long sb_row, int sb_shift, void* D, long long ldd,
              int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream,
              const void* R = nullptr, long long ldr = 0, void* const* rs_dst = nullptr, int world = 0,
-             int rs_slot = 0, int variant = 0);
+             int rs_slot = 0, int variant = 0, void* sf_ws = nullptr);
+// Bytes of the packed E8M0 scale words gemm_fp8's block-scaled path (variant 0 / 2) needs as `sf_ws`.
+long long gemm_fp8_sf_bytes(int M, int N, int K);
 // tcgen05 backward; returns 1 for shapes it does not handle.  `nl2`: B * Hq * S floats of scratch.
 int attention_bwd_sm100(const AttnBwdArgs& a, int D, float* nl2, int* err, cudaStream_t s, int variant = -1);
 }  // namespace rb

@@ -251,7 +251,7 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, None, EPI_SCATTER,
                        float(alpha), None, [int(p) for p in ptrs], int(slot), variant=variant)
-        count(1)
+        count(_launches(variant))
         return None
     if residual is not None:
         if out is None:
@@ -259,7 +259,7 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, EPI_BF16_RES,
                        float(alpha), residual, variant=variant)
-        count(1)
+        count(_launches(variant))
         return out
     if accumulate:
         if out is None or out.dtype != torch.float32:
@@ -274,8 +274,13 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
     ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                    b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, epi, float(alpha),
                    variant=variant)
-    count(1)
+    count(_launches(variant))
     return out
+
+
+def _launches(variant: int) -> int:
+    """Kernels one ``gemm`` call launches: the block-scaled path packs A's and B's scales first."""
+    return 1 if variant == 1 else 3
 
 
 # ---------------------------------------------------------------------------- PyTorch emulation
