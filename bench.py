@@ -721,14 +721,16 @@ def run_hybrid(args, rank: int, world: int, local: int) -> None:
             out["reconfig"] = recfg
         if want_chaos(args, world):
             out["chaos"] = chaos_trial("ours")
+        if not want_failstop(args, world):
+            # printed before the teardown: a rank that fails to leave cleanly cannot lose the line
+            print(json.dumps(out), flush=True)
     if alive:
         dist.barrier()
         trainer.close()
         dist.barrier()
-    if rank == 0:
+    if rank == 0 and want_failstop(args, world):
         # after every rank released its collectives: the GPU fail-stop trial runs its own job
-        if want_failstop(args, world):
-            out["failstop"] = failstop_trial(world)
+        out["failstop"] = failstop_trial(world)
         print(json.dumps(out), flush=True)
 
 
