@@ -768,7 +768,7 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
               const c10::optional<torch::Tensor>& residual, const std::vector<int64_t>& rs_ptrs, int64_t rs_slot,
               int64_t variant) {
   check_fp8(a, "a");
-  TORCH_CHECK(variant >= 0 && variant <= 2, "gemm_fp8: variant is 0 (tensor-core scaling), 1 (register promotion) or 2");
+  TORCH_CHECK(variant >= 0 && variant <= 3, "gemm_fp8: variant is 0 (auto), 1 (register promotion), 2 (single-CTA tensor-core scaling) or 3 (CTA pair)");
   check_fp8(b, "b");
   // Every shape rule of the kernel is checked here, before any pointer or tensor map is formed.
   TORCH_CHECK(a.size(0) > 0 && a.size(1) > 0 && b.size(0) > 0 && a.size(0) % 128 == 0 && a.size(1) % 128 == 0 &&
@@ -805,6 +805,7 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
   }
   check_scale(sa, sa_kb, sa_row, sa_shift, M, K, "sa");
   check_scale(sb, sb_kb, sb_row, sb_shift, N, K, "sb");
+  TORCH_CHECK(variant != 3 || M % 256 == 0, "gemm_fp8: the CTA-pair kernel (variant 3) needs M a multiple of 256");
   if (variant == 1 && sb_shift == 0)
     TORCH_CHECK(sb_row == 1 && sb_kb % 4 == 0 && reinterpret_cast<uintptr_t>(sb.data_ptr()) % 16 == 0,
                 "gemm_fp8: per-column B scales need unit row stride, K-block stride a multiple of 4, 16-byte base");

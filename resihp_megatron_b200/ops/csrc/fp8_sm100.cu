@@ -819,6 +819,281 @@ int launch_mx8(const CUtensorMap& ta, const CUtensorMap& tb, const F8GemmArgs& a
   return static_cast<int>(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------- CTA-pair block-scaled GEMM
+// gemm_fp8_mx_pair_sm100: the block-scaled product on a CTA pair (cta_group::2), 256 x 256
+// output tiles.  Each CTA holds its 128 rows of A, its 128 rows of the tile's 256 B rows, the
+// scale words of its A rows and those of all 256 B rows (the tensor core of each CTA scales its
+// half of D by every column's B scale).  Per CTA and K-block that is 33.5 KB instead of the
+// single-CTA kernel's 49.5 KB for the same MMA time, so the 6-stage ring covers twice the load
+// latency.  All loads of both CTAs (tiles and scale words, the latter through an unswizzled
+// tensor map over the packed words) complete on the leader's stage barrier; the leader's single
+// thread issues per K-block three tcgen05.cp.cta_group::2 (each CTA's words into its own TMEM)
+// and four MMAs of 256 x 256 x 32, and commits to both CTAs' barriers.  Epilogue as in the
+// single-CTA kernel: eight warps per CTA drain their 128-column row segments into registers and
+// release the accumulator (16 arrivals on the leader's barrier) before storing.
+struct Mx8PairCfg {
+  static constexpr int BM = 128;   // rows per CTA (the pair covers 256)
+  static constexpr int BN = 256;   // columns of the pair's tile
+  static constexpr int BNH = 128;  // B rows held per CTA
+  static constexpr int BK = 128;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BNH * BK;
+  static constexpr int SFA_BYTES = 512;
+  static constexpr int SF_BYTES = 3 * SFA_BYTES;  // this CTA's A rows, then all 256 B rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SF_COL = 256;
+  static constexpr int NUM_BARS = 2 * STAGES + 3;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 320;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int GROUP_M = 8;  // in 256-row pair tiles
+  static_assert(SMEM_BYTES <= 232448, "over the 227 KB of dynamic shared memory a CTA may have");
+};
+
+__device__ __forceinline__ void umma_mx8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void mx8p_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = Mx8PairCfg::GROUP_M * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * Mx8PairCfg::GROUP_M;
+  const int gsize = min(num_m - first_m, Mx8PairCfg::GROUP_M);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    gemm_fp8_mx_pair_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmS, F8GemmArgs p) {
+  using C = Mx8PairCfg;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* sSF = sB + STAGES * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSF + STAGES * C::SF_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  const uint32_t tfull_bar = smem_u32(&bars[2 * STAGES]);
+  const uint32_t tempty_bar = smem_u32(&bars[2 * STAGES + 1]);
+  const uint32_t final_bar = smem_u32(&bars[2 * STAGES + 2]);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, 2 * C::EPI_WARPS);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmS);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = p.M / (2 * C::BM);
+  const int num_n = (p.N + C::BN - 1) / C::BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = p.K / C::BK;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int a_groups = p.M / 128;
+  const int sfb_row0 = kblocks * a_groups;  // packed words: A's blocks, then B's
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      for (int tile = pair; tile < num_tiles && !*abort_flag; tile += num_pairs) {
+        int mb, nb;
+        mx8p_tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * C::BM + static_cast<int>(cta) * C::BM;
+        const int n0 = nb * C::BN + static_cast<int>(cta) * C::BNH;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = full_bar(stage);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * C::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(fb_local, 0);
+          const uint32_t sf = smem_u32(sSF + stage * C::SF_BYTES);
+          tma_load_2d_pair(smem_u32(sA + stage * C::A_BYTES), &tmA, fb, kb * C::BK, m0);
+          tma_load_2d_pair(smem_u32(sB + stage * C::B_BYTES), &tmB, fb, kb * C::BK, n0);
+          tma_load_2d_pair(sf, &tmS, fb, 0, kb * a_groups + 2 * mb + static_cast<int>(cta));
+          tma_load_2d_pair(sf + C::SFA_BYTES, &tmS, fb, 0, sfb_row0 + kb * p.sfb_groups + 2 * nb);
+          tma_load_2d_pair(sf + 2 * C::SFA_BYTES, &tmS, fb, 0, sfb_row0 + kb * p.sfb_groups + 2 * nb + 1);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // the leader's barriers count both CTAs' loads; the peer's loads of a stage complete
+      // before the leader's barrier phase does
+      if (leader)
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait(full_bar(s), (issued_parity >> s) & 1, nullptr, p.err, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int stage = 0, set = 0;
+      uint32_t phase = 0, tphase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        if (!mbar_wait(tempty_bar, tphase ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sf = smem_u32(sSF + stage * C::SF_BYTES);
+          const uint32_t t_sfa = tmem_base + C::SF_COL + set * 16;
+          const uint32_t t_sfb = t_sfa + 4;
+          tmem_cp_32x128b_warpx4_pair(t_sfa, make_smem_desc(sf, 128, 128, kSwizzleNone));
+          tmem_cp_32x128b_warpx4_pair(t_sfb, make_smem_desc(sf + C::SFA_BYTES, 128, 128, kSwizzleNone));
+          tmem_cp_32x128b_warpx4_pair(t_sfb + 4, make_smem_desc(sf + 2 * C::SFA_BYTES, 128, 128, kSwizzleNone));
+          const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 32; ++k) {
+            const uint64_t ad = make_smem_desc(a_base + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = make_smem_desc(b_base + k * 32, 16, 1024, kSwizzle128B);
+            umma_mx8_pair(tmem_base, ad, bd, p.idesc, t_sfa, t_sfb, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty_bar(stage));
+          umma_commit_pair(mapa_shared(empty_bar(stage), 1));
+          set ^= 1;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar);
+        umma_commit_pair(mapa_shared(tfull_bar, 1));
+        tphase ^= 1;
+      }
+      umma_commit_pair(final_bar);
+      mbar_wait(final_bar, 0, nullptr, p.err, 200000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t release = leader ? tempty_bar : mapa_shared(tempty_bar, 0);
+    uint32_t tphase = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+      int mb, nb;
+      mx8p_tile_coords(tile, num_m, num_n, mb, nb);
+      if (!f8_warp_wait(tfull_bar, tphase, abort_flag, p.err)) break;
+      tphase ^= 1;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld_32x32b_x32(tb, r0);
+      tmem_ld_32x32b_x32(tb + 32, r1);
+      tmem_ld_32x32b_x32(tb + 64, r2);
+      tmem_ld_32x32b_x32(tb + 96, r3);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(release);
+        else mbar_arrive_cluster(release);
+      }
+      const int row = mb * 2 * C::BM + static_cast<int>(cta) * C::BM + q * 32 + lane;
+      const int col0 = nb * C::BN + half * 128;
+      if (col0 < p.N) {
+        float v[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r0[j]);
+          v[32 + j] = __uint_as_float(r1[j]);
+        }
+        f8_store_row<EPI>(v, row, col0, p);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r2[j]);
+          v[32 + j] = __uint_as_float(r3[j]);
+        }
+        f8_store_row<EPI>(v, row, col0 + 64, p);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs may still read its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int EPI>
+int launch_mx8_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts, const F8GemmArgs& a,
+                    int num_sms, cudaStream_t s) {
+  auto kern = gemm_fp8_mx_pair_sm100<EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Mx8PairCfg::SMEM_BYTES);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  const int tiles = (a.M / (2 * Mx8PairCfg::BM)) * ((a.N + Mx8PairCfg::BN - 1) / Mx8PairCfg::BN);
+  int pairs = num_sms / 2;
+  if (tiles < pairs) pairs = tiles;
+  kern<<<2 * pairs, Mx8PairCfg::THREADS, Mx8PairCfg::SMEM_BYTES, s>>>(ta, tb, ts, a);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 long long gemm_fp8_sf_bytes(int M, int N, int K) {
@@ -850,7 +1125,7 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
              int M, int N, int K, int epi, float alpha, int* err, int num_sms, cudaStream_t stream, const void* R,
              long long ldr, void* const* rs_dst, int world, int rs_slot, int variant, void* sf_ws) {
   if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 128) return -3;
-  if (variant < 0 || variant > 2) return -3;
+  if (variant < 0 || variant > 3) return -3;
   if ((a_fmt != kFp8E4M3 && a_fmt != kFp8E5M2) || (b_fmt != kFp8E4M3 && b_fmt != kFp8E5M2)) return -3;
   if ((sa_shift != 0 && sa_shift != 7) || (sb_shift != 0 && sb_shift != 7)) return -3;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) return -4;
@@ -869,14 +1144,20 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
   }
   if (epi == kF8EpiBF16Res && (R == nullptr || (reinterpret_cast<uintptr_t>(R) & 15) || ldr % 8 || ldr < N)) return -9;
   const bool sb_vec = sb_shift == 0;
-  const bool mx = variant != 1;  // 0 (default) and 2: scales applied by the tensor core
+  // variant 0 (default) and 2: tensor-core scaling on single CTAs; 1: register promotion; 3:
+  // tensor-core scaling on CTA pairs (M a multiple of 256).  Measured at 8192^3 (events, same
+  // box): single CTAs 0.464-0.479 ms, CTA pairs 0.493 ms, so the pair is not the default.
+  const bool mx = variant != 1;
+  const bool pair = variant == 3;
+  if (pair && M % 256) return -3;
   if (!mx && sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;
   CUtensorMap ta, tb;
   if (int rc = make_tmap_2d_sw128(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, K, 128, 128)) return -100 - rc;
-  if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, mx ? Mx8Cfg::BN : 128))
-    return -100 - rc;
+  const uint32_t b_box = (mx && !pair) ? Mx8Cfg::BN : 128;
+  if (int rc = make_tmap_2d_sw128(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, K, 128, b_box)) return -100 - rc;
   a.M = M; a.N = N; a.K = K;
-  a.idesc = mx ? make_idesc_mx8(Mx8Cfg::BM, Mx8Cfg::BN, a_fmt, b_fmt) : make_idesc_f8(128, 128, a_fmt, b_fmt);
+  a.idesc = pair ? make_idesc_mx8(2 * Mx8PairCfg::BM, Mx8PairCfg::BN, a_fmt, b_fmt)
+                 : mx ? make_idesc_mx8(Mx8Cfg::BM, Mx8Cfg::BN, a_fmt, b_fmt) : make_idesc_f8(128, 128, a_fmt, b_fmt);
   a.D = D; a.ldd = ldd; a.alpha = alpha;
   a.sa = sa; a.sa_kb = sa_kb; a.sa_row = sa_row; a.sa_shift = sa_shift;
   a.sb = sb; a.sb_kb = sb_kb; a.sb_row = sb_row; a.sb_shift = sb_shift;
@@ -896,6 +1177,21 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
     a.sfa = reinterpret_cast<const uint8_t*>(wa);
     a.sfb = reinterpret_cast<const uint8_t*>(wb);
     a.sfb_groups = n_pad / 128;
+    if (pair) {
+      // the packed words as rows of 512 bytes (128 words): A's K-block-major blocks, then B's
+      CUtensorMap ts;
+      const uint64_t rows = static_cast<uint64_t>(kblocks) * (M + n_pad) / 128;
+      if (int rc = make_tmap_2d_plain(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, sf_ws, 128, rows, 128, 128, 1))
+        return -100 - rc;
+      switch (epi) {
+        case kF8EpiBF16: return launch_mx8_pair<kF8EpiBF16>(ta, tb, ts, a, num_sms, stream);
+        case kF8EpiF32: return launch_mx8_pair<kF8EpiF32>(ta, tb, ts, a, num_sms, stream);
+        case kF8EpiF32Acc: return launch_mx8_pair<kF8EpiF32Acc>(ta, tb, ts, a, num_sms, stream);
+        case kF8EpiBF16Res: return launch_mx8_pair<kF8EpiBF16Res>(ta, tb, ts, a, num_sms, stream);
+        case kF8EpiScatter: return launch_mx8_pair<kF8EpiScatter>(ta, tb, ts, a, num_sms, stream);
+      }
+      return -2;
+    }
     switch (epi) {
       case kF8EpiBF16: return launch_mx8<kF8EpiBF16>(ta, tb, a, num_sms, stream);
       case kF8EpiF32: return launch_mx8<kF8EpiF32>(ta, tb, a, num_sms, stream);

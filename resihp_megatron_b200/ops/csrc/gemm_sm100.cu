@@ -1020,6 +1020,19 @@ int make_tmap_2d_sw128(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_byte
   return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
+int make_tmap_2d_plain(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_bytes, const void* ptr, uint64_t inner,
+                       uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
 // 2-D bf16 tensor map, 128B swizzle: `inner` contiguous elements per row, `outer` rows.
 int make_tmap_bf16_2d(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer,
                       uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {

@@ -13,4 +13,8 @@ namespace rb {
 int make_tmap_2d_sw128(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_bytes, const void* ptr, uint64_t inner,
                        uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
 
+// The same without swizzle (rows of the box land contiguously in shared memory).
+int make_tmap_2d_plain(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_bytes, const void* ptr, uint64_t inner,
+                       uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer);
+
 }  // namespace rb

@@ -240,12 +240,15 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
     output; row ``m`` is stored (bf16) into rank ``m // (rows / world)``'s receive buffer
     ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter.
     Shapes and scale addressing are validated here, before the extension is called.
-    ``variant``: 0 (default) applies the scales in the tensor core (block-scaled MMA, E8M0 scale
-    per 32 K-elements; exact for these power-of-two scales), 1 promotes per 128-deep K-block in
+    ``variant``: 0 (default) and 2 apply the scales in the tensor core (block-scaled MMA, E8M0
+    scale per 32 K-elements; exact for these power-of-two scales) on single CTAs, 3 on CTA pairs
+    (``a.rows`` a multiple of 256; measured slower at 8192^3), 1 promotes per 128-deep K-block in
     registers (the earlier kernel, kept for comparison)."""
     _check_operands(a, b)
-    if variant not in (0, 1, 2):
-        raise ValueError("variant is 0 (tensor-core scaling), 1 (register promotion) or 2")
+    if variant not in (0, 1, 2, 3):
+        raise ValueError("variant is 0 (default), 1 (register promotion), 2 (single CTA) or 3 (CTA pair)")
+    if variant == 3 and a.rows % 256:
+        raise Fp8ShapeError(f"the CTA-pair kernel needs a.rows a multiple of 256, got {a.rows}")
     if scatter is not None:
         ptrs, slot = scatter
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
