@@ -17,6 +17,7 @@
 // This file is new work: the reference framework has no GEMM of its own (its compute
 // validation probe `resihp/detect/validation.py:17-31` calls torch.matmul).
 #include <cuda.h>
+#include <cstring>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
@@ -717,7 +718,14 @@ __global__ void __launch_bounds__(320, 1)
 //   * optional split-K of the tiles of the partial last wave (`PairUnit`): full waves run whole
 //     tiles, each tail tile runs as up to 4 k shares whose fp32 partials the last-arriving share
 //     adds in a fixed order (deterministic) before the epilogue.
-template <int kStages, int kBN = 256>
+// Epilogues the CTA-pair kernel writes with TMA (shared-memory staging, tile store or fp32
+// reduce-add) when its ring leaves room for the staging buffers.
+template <int EPI>
+constexpr bool pair_tma_epi() {
+  return EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiF32Acc;
+}
+
+template <int kStages, int kBN = 256, int EPI = kEpiBF16>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA (the pair covers 256)
   static constexpr int BN = kBN;  // columns of the pair's tile (256, or 128 for more tiles per wave)
@@ -729,7 +737,13 @@ struct PairCfg {
   static constexpr int STAGES = kStages;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  // TMA epilogue: per epilogue warp two 32 x 32 staging tiles of the output type
+  static constexpr int OUT_BYTES = (EPI == kEpiF32 || EPI == kEpiF32Acc) ? 4 : 2;
+  static constexpr int STG_TILE = 32 * 32 * OUT_BYTES;
+  static constexpr int BASE_BYTES = 1024 + STAGES * STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr bool TMA_EPI = pair_tma_epi<EPI>() && BASE_BYTES + 8 * STG_TILE <= 232448;
+  static constexpr int STG_BYTES = TMA_EPI ? 8 * STG_TILE : 0;
+  static constexpr int SMEM_BYTES = BASE_BYTES + STG_BYTES;
   static constexpr int THREADS = 192;
   static constexpr int GROUP_M = 8;  // in 256-row pair tiles
   static_assert(SMEM_BYTES <= 232448, "over the 227 KB of dynamic shared memory a CTA may have");
@@ -738,15 +752,16 @@ struct PairCfg {
 template <bool A_MN, bool B_MN, int EPI, int kStages, int kBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         GemmArgs p) {
-  using C = PairCfg<kStages, kBN>;
+                         const __grid_constant__ CUtensorMap tmD, GemmArgs p) {
+  using C = PairCfg<kStages, kBN, EPI>;
   constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_BYTES);
+  uint8_t* stg = sB + STAGES * C::B_BYTES;  // TMA epilogue staging (C::STG_BYTES)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + C::STG_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -902,6 +917,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const uint32_t release = leader ? 0u : mapa_shared(tempty_bar(0), 0);  // peer: leader's barrier
     int acc = 0;
     uint32_t aphase = 0;
+    int stg_buf = 0;
     for (int u = pair; u < num_units; u += num_pairs) {
       const PairUnit w = pair_unit(u, num_tiles, full, splits, kblocks);
       const int tile = w.tile, share = w.share;
@@ -916,7 +932,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       // workspace slots of this (tail tile, CTA, warp): `splits` consecutive 32 x BN fp32 blocks
       const long long slot0 =
           static_cast<long long>((max(w.tail_idx, 0) * 2 + static_cast<int>(cta)) * 4 + q) * splits;
-      if (!split_unit) {
+      if (!split_unit && C::TMA_EPI) {
+        // 32 x 32 output boxes through two staging tiles per warp: each lane writes its row into
+        // the tile, the tile goes to global memory as one TMA store (fp32 accumulate: TMA
+        // reduce-add in L2); TMA clips rows past M and columns past N.
+        const int row0 = mb * 2 * BM + static_cast<int>(cta) * BM + q * 32;
+#pragma unroll 1
+        for (int c = 0; c < C::BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_acc + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = nb * C::BN + c * 32;
+          if (row0 >= p.M || col0 >= p.N) continue;
+          uint8_t* tile = stg + (q * 2 + stg_buf) * C::STG_TILE;
+          if (lane == 0) bulk_wait_group_read<1>();  // this tile's previous store has read it
+          __syncwarp();
+          if constexpr (C::OUT_BYTES == 2) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * p.alpha, __uint_as_float(r[2 * i + 1]) * p.alpha);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(tile + lane * 64 + j * 16) =
+                  make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(tile + lane * 128 + j * 16) =
+                  make_float4(__uint_as_float(r[4 * j]) * p.alpha, __uint_as_float(r[4 * j + 1]) * p.alpha,
+                              __uint_as_float(r[4 * j + 2]) * p.alpha, __uint_as_float(r[4 * j + 3]) * p.alpha);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (EPI == kEpiF32Acc) tma_reduce_add_2d(&tmD, smem_u32(tile), col0, row0);
+            else tma_store_2d(&tmD, smem_u32(tile), col0, row0);
+            bulk_commit_group();
+          }
+          stg_buf ^= 1;
+        }
+      } else if (!split_unit) {
 #pragma unroll 1
         for (int c = 0; c < C::BN / 32; ++c) {
           uint32_t r[32];
@@ -981,6 +1037,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       acc ^= 1;
       if (acc == 0) aphase ^= 1;
     }
+    if (C::TMA_EPI && lane == 0) bulk_wait_group_all();  // this warp's stores have landed
   }
 
   tc_fence_before();
@@ -1068,7 +1125,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
 template <bool A_MN, bool B_MN, int EPI, int kStages, int kBN>
 static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_sms,
                             cudaStream_t stream) {
-  using C = PairCfg<kStages, kBN>;
+  using C = PairCfg<kStages, kBN, EPI>;
   auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI, kStages, kBN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -1076,12 +1133,20 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_set = true;
   }
+  CUtensorMap td;  // output boxes of 32 x 32 for the TMA epilogue (unused otherwise)
+  std::memset(&td, 0, sizeof(td));
+  if (C::TMA_EPI) {
+    const bool f32 = C::OUT_BYTES == 4;
+    if (int rc = make_tmap_2d_plain(&td, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                    C::OUT_BYTES, a.D, a.N, a.M, a.ldd, 32, 32))
+      return -100 - rc;
+  }
   const int tiles = ((a.M + 2 * C::BM - 1) / (2 * C::BM)) * ((a.N + C::BN - 1) / C::BN);
   int pairs = num_sms / 2;
   const int full = a.splits > 1 ? a.split_full : tiles;
   const int units = full + (a.splits > 1 ? a.splits : 1) * (tiles - full);
   if (units < pairs) pairs = units;
-  kern<<<2 * pairs, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, a);
+  kern<<<2 * pairs, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, td, a);
   return static_cast<int>(cudaGetLastError());
 }
 
