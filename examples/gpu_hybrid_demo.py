@@ -61,13 +61,15 @@ def main(argv=None) -> None:
         fp8 = Fp8Recipe()
     binding = GPUHybridBinding(GPU_DEMO, client, mgr, micro_batch=1, seq_len=GPU_DEMO.seq_len, device=device,
                                tp_impl=args.tp_impl, lr=args.lr, hook=injector.on_hook if injector else None, fp8=fp8)
-    result = ResilientTrainer(client, mgr, binding).run(args.iterations)
+    trainer = ResilientTrainer(client, mgr, binding)
+    result = trainer.run(args.iterations)
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     me = client.worker_id
     info = {"worker": me, "losses": {str(k): v for k, v in result.losses.items()}, "generations": result.generations,
             "standby": result.standby, "reconfigurations": result.reconfigurations,
-            "last_transfer": binding.last_transfer, "last_recovery": binding.last_recovery}
+            "last_transfer": binding.last_transfer, "last_recovery": binding.last_recovery,
+            "build_steps_s": getattr(trainer, "build_steps_s", None)}
     if binding.committed is not None and not result.standby:
         plan, _ = binding.committed
         g = plan.group_of_device(me)

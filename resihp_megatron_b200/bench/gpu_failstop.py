@@ -73,9 +73,12 @@ def run_trial(n: int, iterations: int = 6, kill_iteration: int = 2, out: str | N
         if agent is not None:
             agent.stop(kill_workers=True)
         coord.stop()
-    phases = None
+    phases, events = None, None
     if stamp.exists():
-        phases = breakdown(history, float(stamp.read_text().split()[1]))
+        t_fault = float(stamp.read_text().split()[1])
+        phases = breakdown(history, t_fault)
+        # the coordinator's transaction events, seconds after the fault (machine-wide monotonic clock)
+        events = [(h["event"], round(h["t"] - t_fault, 4)) for h in history if h["t"] >= t_fault][:16]
     losses, rebuild = {}, {}
     for w in codes:
         f = outdir / f"{w}.json"
@@ -83,8 +86,13 @@ def run_trial(n: int, iterations: int = 6, kill_iteration: int = 2, out: str | N
             info = json.loads(f.read_text())
             if not info["standby"]:
                 losses[w] = {int(k): v for k, v in info["losses"].items()}
-                rebuild[w] = info.get("last_recovery")
+                steps = dict(info.get("build_steps_s") or {})
+                if stamp.exists():  # absolute instants -> seconds after the fault
+                    t_fault = float(stamp.read_text().split()[1])
+                    steps = {k: (round(v - t_fault, 4) if k.endswith("_at") else v) for k, v in steps.items()}
+                rebuild[w] = dict(info.get("last_recovery") or {}, worker_steps_s=steps)
     return {"gpus": n, "layout": f"tp{tp}pp{pp}dp{dp}", "victim": victim, "codes": codes, "phases_s": phases,
+            "events_s": events,
             "losses": losses, "rebuild_s": rebuild, "out": str(outdir)}
 
 

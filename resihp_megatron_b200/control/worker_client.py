@@ -59,6 +59,8 @@ class WorkerClient:
         self._shutdown = False
         self._conn: Connection | None = None
         self._stopped = threading.Event()
+        # arrival time (time.monotonic, machine-wide) of every notice / PREPARE, by generation
+        self.arrivals: dict[str, float] = {}
         self._handlers = {P.RECONFIG_NOTICE: self._got_notice, P.SELF_FENCE: self._got_self_fence,
                           P.PREPARE: self._got_prepare, P.COMMIT: self._got_commit, P.SHUTDOWN: self._got_shutdown}
 
@@ -190,6 +192,7 @@ class WorkerClient:
         if m["gen"] <= self._notice_gen:
             return []
         self._latest_notice = m
+        self.arrivals[f"notice{m['gen']}"] = time.monotonic()
         if self._blocked_in_control:
             self._acknowledge()
             return []
@@ -201,6 +204,7 @@ class WorkerClient:
     def _got_prepare(self, m: dict) -> list:
         if m["gen"] >= self._notice_gen:
             self._prepared[m["gen"]] = m
+            self.arrivals[f"prepare{m['gen']}"] = time.monotonic()
         return []
 
     def _got_commit(self, m: dict) -> list:

@@ -134,8 +134,11 @@ class ResilientTrainer:
         while True:
             self.client.set_recovery_info(**self.txm.recovery_info())
             prepare = self.client.wait_prepare(timeout=self.prepare_timeout)
+            t0 = time.monotonic()
             if self.comms is not None:
                 self.hooks.teardown()  # before the old communicators go away
+            self._steps_s = {"wait_prepare_s": round(t0 - started, 4), "teardown_s": round(time.monotonic() - t0, 4),
+                             "rejoin_at": started}
             outcome = self._enter(prepare)
             if outcome is _Join.MEMBER:
                 self._record(prepare, started)
@@ -173,11 +176,22 @@ class ResilientTrainer:
         gen, world, payload = prepare["gen"], prepare["world"], prepare["payload"]
         store = tuple(prepare["store_addr"]) if prepare.get("store_addr") else None
         self.comms = None
-        comms = self.mgr.build(gen, world, self.client.worker_id, self.binding.group_specs(world, payload),
-                               store_addr=store, store_prefix=prepare["store_prefix"])
+        steps = getattr(self, "_steps_s", {})
+        t = time.monotonic()
+        specs = self.binding.group_specs(world, payload)
+        t, steps["group_specs_s"] = time.monotonic(), round(time.monotonic() - t, 4)
+        comms = self.mgr.build(gen, world, self.client.worker_id, specs, store_addr=store,
+                               store_prefix=prepare["store_prefix"])
+        t, steps["comms_s"] = time.monotonic(), round(time.monotonic() - t, 4)
         self.binding.recover(comms, payload, self.txm)
+        t, steps["recover_s"] = time.monotonic(), round(time.monotonic() - t, 4)
         self.runtime = self.binding.build_runtime(comms, payload)
+        t, steps["build_runtime_s"] = time.monotonic(), round(time.monotonic() - t, 4)
         self.hooks.rebuild(comms, payload)
+        steps["hooks_rebuild_s"] = round(time.monotonic() - t, 4)
+        steps["ready_at"] = time.monotonic()
+        steps.update({k + "_at": v for k, v in getattr(self.client, "arrivals", {}).items() if k.endswith(str(gen))})
+        self.build_steps_s = steps  # where this worker's time between PREPARE and READY went
         self.comms = comms
         self.client.send_ready(gen)
         self.client.wait_commit(gen, timeout=self.prepare_timeout)
