@@ -30,6 +30,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include <cstdint>
 
 #include "kernels.h"
@@ -557,6 +559,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool misaligned(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) != 0; }
 
+// A second stream of the current device with its fork / join events, created on first use and
+// kept for the life of the process; stream == nullptr if creation failed (then one stream is used).
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+SideStream& side_stream() {
+  constexpr int kMaxDevices = 64;
+  static SideStream per_device[kMaxDevices];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    static SideStream none;
+    return none;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  SideStream& s = per_device[dev];
+  if (s.stream == nullptr) {
+    cudaStream_t st = nullptr;
+    cudaEvent_t f = nullptr, j = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+        cudaEventCreateWithFlags(&f, cudaEventDisableTiming) == cudaSuccess &&
+        cudaEventCreateWithFlags(&j, cudaEventDisableTiming) == cudaSuccess) {
+      s.stream = st;
+      s.fork = f;
+      s.join = j;
+    } else {
+      cudaGetLastError();  // clear; the caller falls back to one stream
+    }
+  }
+  return s;
+}
+
 // Exponentials per 8 score columns evaluated on the FMA pipe (ex2_fma) by default.  Measured on
 // B200 at B=2 S=4096 (forward / backward TFLOP/s for shares 0..3): 797/585, 768/581, 751/572,
 // 732/561 -- with the softmax's dependency chains broken up the MUFU unit is not the limit, so
@@ -576,9 +612,24 @@ int launch_bwd(dim3 grid_dkdv, dim3 grid_dq, const CUtensorMap& tq, const CUtens
     if (e != cudaSuccess) return static_cast<int>(e);
     attr = true;
   }
+  // dK/dV and dQ read the same inputs and write disjoint outputs: dQ runs on a second stream so
+  // its CTAs fill the SMs the dK/dV grid's partial last wave leaves idle (and the other way
+  // round); the caller's stream waits for both.  Each output is still computed by one fixed CTA.
+  SideStream& side = side_stream();
+  if (side.stream == nullptr) {
+    attn_bwd_dkdv_sm100_kernel<kFma><<<grid_dkdv, kThreads, kSmemDkdv, stream>>>(tq, tk, tv, tdo, p);
+    attn_bwd_dq_sm100_kernel<kFma><<<grid_dq, kThreads, kSmemDq, stream>>>(tq, tk, tv, tdo, p);
+    return static_cast<int>(cudaGetLastError());
+  }
+  cudaError_t e = cudaEventRecord(side.fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(side.stream, side.fork, 0);
+  if (e != cudaSuccess) return static_cast<int>(e);
   attn_bwd_dkdv_sm100_kernel<kFma><<<grid_dkdv, kThreads, kSmemDkdv, stream>>>(tq, tk, tv, tdo, p);
-  attn_bwd_dq_sm100_kernel<kFma><<<grid_dq, kThreads, kSmemDq, stream>>>(tq, tk, tv, tdo, p);
-  return static_cast<int>(cudaGetLastError());
+  attn_bwd_dq_sm100_kernel<kFma><<<grid_dq, kThreads, kSmemDq, side.stream>>>(tq, tk, tv, tdo, p);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventRecord(side.join, side.stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, side.join, 0);
+  return static_cast<int>(e);
 }
 
 }  // namespace
