@@ -812,6 +812,8 @@ void gemm_fp8(const torch::Tensor& a, int64_t a_fmt, const torch::Tensor& sa, in
   const c10::cuda::CUDAGuard g(a.device());
   torch::Tensor sf_ws;  // packed scale words of the block-scaled path (stream-ordered, from the caching allocator)
   if (variant != 1) sf_ws = torch::empty({rb::gemm_fp8_sf_bytes(M, N, K)}, a.options().dtype(torch::kUInt8));
+  // (variant 0 may still pick the register-promotion kernel for a small product; it then leaves
+  // the workspace unused)
   RB_CALL(rb::gemm_fp8(a.data_ptr(), static_cast<int>(a_fmt), b.data_ptr(), static_cast<int>(b_fmt),
                        sa.data_ptr<float>(), sa_kb, sa_row, static_cast<int>(sa_shift), sb.data_ptr<float>(), sb_kb,
                        sb_row, static_cast<int>(sb_shift), dptr, ldd, M, N, K, static_cast<int>(epi),

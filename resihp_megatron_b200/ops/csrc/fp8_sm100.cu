@@ -49,6 +49,8 @@ namespace rb {
 namespace {
 
 enum : int { kF8EpiBF16 = 0, kF8EpiF32 = 1, kF8EpiF32Acc = 2, kF8EpiBF16Res = 3, kF8EpiScatter = 4 };
+// Products (2 M N K) below this run the register-promotion kernel by default (see gemm_fp8).
+constexpr double kF8SmallFlops = 3.0e10;
 constexpr int kF8MaxTP = 8;
 
 
@@ -1144,10 +1146,16 @@ int gemm_fp8(const void* A, int a_fmt, const void* B, int b_fmt, const float* sa
   }
   if (epi == kF8EpiBF16Res && (R == nullptr || (reinterpret_cast<uintptr_t>(R) & 15) || ldr % 8 || ldr < N)) return -9;
   const bool sb_vec = sb_shift == 0;
-  // variant 0 (default) and 2: tensor-core scaling on single CTAs; 1: register promotion; 3:
-  // tensor-core scaling on CTA pairs (M a multiple of 256).  Measured at 8192^3 (events, same
-  // box): single CTAs 0.464-0.479 ms, CTA pairs 0.493 ms, so the pair is not the default.
-  const bool mx = variant != 1;
+  // variant 2: tensor-core scaling on single CTAs; 1: register promotion; 3: tensor-core scaling
+  // on CTA pairs (M a multiple of 256).  Measured at 8192^3 (events, same box): single CTAs
+  // 0.464-0.479 ms, CTA pairs 0.493 ms, so the pair is not the default.  Variant 0 (default) is
+  // variant 2, except for products under kF8SmallFlops, which take the register-promotion kernel:
+  // it needs no scale-packing launches, and on these sizes those cost more than the promotion
+  // (4096 x 1024 x 2048: 0.041 / 0.038 ms against 0.045 / 0.042 in two runs; 4096 x 3072 x 2048:
+  // 0.081 against 0.063, so the threshold sits between them).
+  const bool promotable = !sb_vec || (sb_row == 1 && sb_kb % 4 == 0 && !(reinterpret_cast<uintptr_t>(sb) & 15));
+  const bool small = variant == 0 && 2.0 * M * N * K < kF8SmallFlops && promotable;
+  const bool mx = variant != 1 && !small;
   const bool pair = variant == 3;
   if (pair && M % 256) return -3;
   if (!mx && sb_vec && (sb_row != 1 || sb_kb % 4 || (reinterpret_cast<uintptr_t>(sb) & 15))) return -7;

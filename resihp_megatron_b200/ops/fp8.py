@@ -240,8 +240,9 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
     output; row ``m`` is stored (bf16) into rank ``m // (rows / world)``'s receive buffer
     ``[world][rows / world][N]`` at ``slot`` -- the partial products of a reduce-scatter.
     Shapes and scale addressing are validated here, before the extension is called.
-    ``variant``: 0 (default) and 2 apply the scales in the tensor core (block-scaled MMA, E8M0
-    scale per 32 K-elements; exact for these power-of-two scales) on single CTAs, 3 on CTA pairs
+    ``variant``: 2 applies the scales in the tensor core (block-scaled MMA, E8M0 scale per 32
+    K-elements; exact for these power-of-two scales) on single CTAs, 0 (default) likewise except
+    for products under ``SMALL_FLOPS`` (register promotion: no scale-packing launches), 3 on CTA pairs
     (``a.rows`` a multiple of 256; measured slower at 8192^3), 1 promotes per 128-deep K-block in
     registers (the earlier kernel, kept for comparison)."""
     _check_operands(a, b)
@@ -254,7 +255,7 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, None, EPI_SCATTER,
                        float(alpha), None, [int(p) for p in ptrs], int(slot), variant=variant)
-        count(_launches(variant))
+        count(_launches(a, b, variant))
         return None
     if residual is not None:
         if out is None:
@@ -262,7 +263,7 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
         ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                        b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, EPI_BF16_RES,
                        float(alpha), residual, variant=variant)
-        count(_launches(variant))
+        count(_launches(a, b, variant))
         return out
     if accumulate:
         if out is None or out.dtype != torch.float32:
@@ -277,13 +278,25 @@ def gemm(a: Fp8Operand, b: Fp8Operand, *, out: torch.Tensor | None = None, out_d
     ext().gemm_fp8(a.data.view(torch.uint8), a.fmt, a.scale, a.kb_stride, a.row_stride, a.shift,
                    b.data.view(torch.uint8), b.fmt, b.scale, b.kb_stride, b.row_stride, b.shift, out, epi, float(alpha),
                    variant=variant)
-    count(_launches(variant))
+    count(_launches(a, b, variant))
     return out
 
 
-def _launches(variant: int) -> int:
+SMALL_FLOPS = 3.0e10  # variant 0 below this product size: the register-promotion kernel
+
+
+def _promotes(a: Fp8Operand, b: Fp8Operand, variant: int) -> bool:
+    """Whether ``gemm`` runs the register-promotion kernel (the rule of the native dispatch)."""
+    if variant == 1:
+        return True
+    if variant != 0 or 2.0 * a.rows * b.rows * a.K >= SMALL_FLOPS:
+        return False
+    return b.shift != 0 or (b.row_stride == 1 and b.kb_stride % 4 == 0 and b.scale.data_ptr() % 16 == 0)
+
+
+def _launches(a: Fp8Operand, b: Fp8Operand, variant: int) -> int:
     """Kernels one ``gemm`` call launches: the block-scaled path packs A's and B's scales first."""
-    return 1 if variant == 1 else 3
+    return 1 if _promotes(a, b, variant) else 3
 
 
 # ---------------------------------------------------------------------------- PyTorch emulation

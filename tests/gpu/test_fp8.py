@@ -50,12 +50,12 @@ def _check(out, ref, tol):
     assert err <= tol * ref.float().abs().max().item() + 1e-30, err
 
 
-@pytest.mark.parametrize("variant", [0, 1, 3])
-@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1024, 1024, 2048), (256, 128, 128)])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1024, 1024, 2048), (256, 128, 128), (4096, 1280, 256)])
 def test_gemm_forward_dgrad_wgrad(M, N, K, variant):
-    """Variants 0 and 3 apply the scales in the tensor core (block-scaled MMA; single CTAs and CTA
-    pairs), 1 in registers per K-block; all against the PyTorch emulation of the same block-scaled
-    product."""
+    """Variants 2 and 3 apply the scales in the tensor core (block-scaled MMA; single CTAs and CTA
+    pairs), 1 in registers per K-block, 0 picks by size; all against the PyTorch emulation of the
+    same block-scaled product.  The forward of 4096 x 1280 runs 160 tiles with a partly empty last column of tiles."""
     x = _x(M, K, seed=1, spread=1.0)
     w = (_x(N, K, seed=2, spread=0.5).float() * 0.05).bfloat16()
     dy = (_x(M, N, seed=4, spread=1.0).float() * 1e-3).bfloat16()
@@ -118,7 +118,7 @@ def test_gelu_fwd_bwd():
     assert torch.equal(h2, dh)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 3])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 def test_gemm_residual_and_scatter_epilogues(variant):
     M, N, K, world = 512, 256, 384, 4
     x = _x(M, K, seed=5, spread=1.0)
