@@ -46,6 +46,32 @@ def pid_alive(pid: int) -> bool:
     return reaped == 0
 
 
+PF_EXITING = 0x4  # Linux task flag: the task has entered exit (set before its memory is torn down)
+
+
+def parse_stat_exiting(stat: str) -> bool:
+    """``/proc/<pid>/stat`` text -> whether the task is exiting or already a zombie / dead.  The
+    command name is parenthesised and may itself contain spaces or parentheses, so the fields are
+    taken after the last ``)``: state, ppid, pgrp, session, tty, tpgid, flags, ..."""
+    rest = stat[stat.rfind(")") + 2:].split()
+    if len(rest) < 7:
+        return False
+    return rest[0] in ("Z", "X", "x") or bool(int(rest[6]) & PF_EXITING)
+
+
+def pid_exiting(pid: int) -> bool:
+    """Whether ``pid`` has started to exit (Linux).  A SIGKILLed GPU process can take a few hundred
+    milliseconds between this point and the closing of its sockets -- the driver unmaps its device
+    memory first -- so this sees a dead worker well before its control connection drops."""
+    if pid <= 0:
+        return False
+    try:
+        with open(f"/proc/{pid}/stat", encoding="ascii", errors="replace") as fh:
+            return parse_stat_exiting(fh.read())
+    except (OSError, ValueError):
+        return False
+
+
 @dataclass
 class LocalWorker:
     worker_id: str
@@ -64,6 +90,8 @@ class LocalWorker:
             return f"exited with {code}"
         if self.proc is None and self.pid and not pid_alive(self.pid):
             return "process gone"
+        if self.pid and pid_exiting(self.pid):
+            return "process exiting"
         silent = now - self.last_hb
         if self.conn is not None and silent > stall_after:
             return f"heartbeat stalled {silent:.1f}s (hang)"
