@@ -127,3 +127,25 @@ def test_gemm_validates_shapes_and_scales_before_any_native_call(monkeypatch):
         fp8.gemm(good, other_k)
     # the error is both a ValueError and a RuntimeError (callers catching either keep working)
     assert issubclass(fp8.Fp8ShapeError, ValueError) and issubclass(fp8.Fp8ShapeError, RuntimeError)
+
+
+def test_kernel_choice_by_product_size():
+    """``variant=0`` sends products under ``SMALL_FLOPS`` to the register-promotion kernel (one
+    launch) when B's scales allow it, everything else to the block-scaled MMA (two scale-packing
+    launches + the GEMM); the launch count reported for a call follows the same rule."""
+    import torch
+
+    def op(rows, K, shift, row_stride=1, kb_stride=None):
+        nkb = K // 128
+        scale = torch.ones(max(1, (rows >> shift)) * nkb + 16)
+        kb_stride = (rows >> shift) if kb_stride is None else kb_stride
+        return fp8.Fp8Operand(torch.zeros(rows, K, dtype=torch.uint8), scale, kb_stride, row_stride, shift, fp8.E4M3)
+
+    small_a, small_b = op(4096, 2048, 0), op(1024, 2048, 7)     # 1.7e10 FLOPs
+    big_a, big_b = op(4096, 2048, 0), op(4096, 2048, 7)         # 6.9e10 FLOPs
+    assert fp8._promotes(small_a, small_b, 0) and fp8._launches(small_a, small_b, 0) == 1
+    assert not fp8._promotes(big_a, big_b, 0) and fp8._launches(big_a, big_b, 0) == 3
+    assert not fp8._promotes(small_a, small_b, 2) and fp8._promotes(big_a, big_b, 1)
+    # per-column B scales the promotion kernel cannot read (K-block stride not a multiple of 4)
+    odd = op(1024, 2048, 0, kb_stride=1026)
+    assert not fp8._promotes(small_a, odd, 0)
