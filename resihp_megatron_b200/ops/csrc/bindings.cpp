@@ -667,16 +667,40 @@ void moe_grad_push(const torch::Tensor& dout, const torch::Tensor& gates, const 
 // residual stream itself; None when the experts read a normalised copy (transformer blocks).
 void moe_grad_pull(const c10::optional<torch::Tensor>& residual_grad, const torch::Tensor& gates,
                    const torch::Tensor& dgate, const torch::Tensor& topi, const torch::Tensor& route_row, int64_t k,
-                   int64_t E, const std::vector<int64_t>& dxbuf, torch::Tensor& dx, torch::Tensor& dlogits) {
+                   int64_t E, const std::vector<int64_t>& dxbuf, torch::Tensor& dx, torch::Tensor& dlogits,
+                   const c10::optional<torch::Tensor>& router_w) {
   CHECK_BF16(dx);
   if (residual_grad.has_value()) CHECK_BF16((*residual_grad));
+  if (router_w.has_value()) {
+    CHECK_BF16((*router_w));
+    TORCH_CHECK(router_w->dim() == 2 && router_w->size(0) == E && router_w->size(1) == dx.size(1) &&
+                    router_w->is_contiguous(), "moe_grad_pull: router_w must be a contiguous [E, H] tensor");
+  }
   const c10::cuda::CUDAGuard g(dx.device());
   auto b = as_ptrs(dxbuf);
   RB_CALL(rb::moe_grad_pull(residual_grad.has_value() ? residual_grad->data_ptr() : nullptr, gates.data_ptr<float>(),
                             dgate.data_ptr<float>(), topi.data_ptr<int>(),
                             reinterpret_cast<const long long*>(route_row.data_ptr<int64_t>()), dx.size(0), k,
                             dx.size(1), E, static_cast<int>(b.size()), b.data(), dx.data_ptr(),
-                            dlogits.data_ptr<float>(), cur_stream()), "moe_grad_pull");
+                            dlogits.data_ptr<float>(), cur_stream(),
+                            router_w.has_value() ? router_w->data_ptr() : nullptr),
+          "moe_grad_pull");
+}
+
+// grad [E, H] fp32 += dlogits [T, E]^T x [T, H] (bf16), two fixed-order passes (deterministic).
+void moe_router_wgrad(const torch::Tensor& dlogits, const torch::Tensor& x, torch::Tensor& grad) {
+  CHECK_F32(dlogits);
+  CHECK_BF16(x);
+  CHECK_F32(grad);
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && dlogits.dim() == 2 && dlogits.is_contiguous() &&
+                  grad.is_contiguous(), "moe_router_wgrad: contiguous 2-D tensors");
+  const int T = x.size(0), H = x.size(1), E = dlogits.size(1);
+  TORCH_CHECK(dlogits.size(0) == T && grad.size(0) == E && grad.size(1) == H, "moe_router_wgrad: shapes");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto ws = torch::empty({rb::moe_router_wgrad_ws_floats(T, H, E)}, grad.options());
+  RB_CALL(rb::moe_router_wgrad(dlogits.data_ptr<float>(), x.data_ptr(), T, H, E, ws.data_ptr<float>(),
+                               grad.data_ptr<float>(), cur_stream()),
+          "moe_router_wgrad");
 }
 
 // ---------------------------------------------------------------- block-scaled fp8
@@ -890,7 +914,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_combine", &moe_combine);
   m.def("moe_grad_push", &moe_grad_push);
-  m.def("moe_grad_pull", &moe_grad_pull);
+  m.def("moe_grad_pull", &moe_grad_pull, "expert-parallel gradient pull (+ the router path)", py::arg("residual_grad"),
+        py::arg("gates"), py::arg("dgate"), py::arg("topi"), py::arg("route_row"), py::arg("k"), py::arg("E"),
+        py::arg("dxbuf"), py::arg("dx"), py::arg("dlogits"), py::arg("router_w") = py::none());
+  m.def("moe_router_wgrad", &moe_router_wgrad, "router weight gradient, deterministic");
   m.def("tp_rs_gemm", &tp_rs_gemm);
   m.def("symm_copy2d_build", &symm_copy2d_build);
   m.def("symm_copy2d_run", &symm_copy2d_run);

@@ -134,7 +134,12 @@ int moe_grad_push(const void* dout, const float* gates, const void* ycache, cons
                   int H, int world, void* const* dyrecv, float* dgate, cudaStream_t s);
 int moe_grad_pull(const void* dout, const float* gates, const float* dgate, const int* topi,
                   const long long* route_row, int T, int k, int H, int E, int world, void* const* dxbuf, void* dx,
-                  float* dlogits, cudaStream_t s);
+                  float* dlogits, cudaStream_t s, const void* router_w = nullptr);
+// Router weight gradient grad [E, H] fp32 += dlogits [T, E]^T x [T, H] (bf16), deterministic;
+// `partial` holds moe_router_wgrad_ws_floats(T, H, E) floats.
+long long moe_router_wgrad_ws_floats(int T, int H, int E);
+int moe_router_wgrad(const float* dlogits, const void* x, int T, int H, int E, float* partial, float* grad,
+                     cudaStream_t s);
 // Tensor-parallel fused GEMMs (gemm_sm100.cu).
 int gemm_ag_bf16(const void* x_full, const void* const* x_src, int world, int self, int chunk_rows, const void* W,
                  bool w_mn, void* Y, int M, int N, int K, int* ready, const int* abort_word, int* err, int num_sms,

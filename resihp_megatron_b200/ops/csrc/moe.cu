@@ -13,8 +13,9 @@
 //              kept for the backward.
 //   grad push  one warp per (token, slot): dy_k = gate_k * dout to the holder's receive row,
 //              dgate_k = <dout, y_k>.
-//   grad pull  one warp per token: dx = dout + sum_k dx_k (from the holders) and the router
-//              logit gradient of the softmax over the selected logits.
+//   grad pull  one warp per token: the router logit gradient of the softmax over the selected
+//              logits dl, and dx = dout + sum_k dx_k (from the holders) + dl W_r (the router path).
+//   router wgrad  dW_r += dl^T x in two fixed-order passes (token chunks, then their sum).
 // Replaces the reference's counts all-to-all + autograd all_to_all_single + index_add
 // (resihp/runtime/moe.py:149-265, call sites C11/C12).  Only plain loads and stores touch peer
 // memory; the expert GEMMs read only local buffers.
@@ -257,10 +258,25 @@ __global__ void moe_grad_push_kernel(const __nv_bfloat16* __restrict__ dout, con
 __global__ void moe_grad_pull_kernel(const __nv_bfloat16* __restrict__ dout, const float* __restrict__ gates,
                                      const float* __restrict__ dgate, const int* __restrict__ topi,
                                      const long long* __restrict__ route_row, int T, int k, int H, int E, MoeRoutes r,
-                                     __nv_bfloat16* __restrict__ dx, float* __restrict__ dlogits) {
+                                     const __nv_bfloat16* __restrict__ router_w, __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ dlogits) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
+  // router logit gradient of the softmax over the selected logits (every lane holds it):
+  // gates = softmax(l_sel) -> dl_sel_i = g_i (dgate_i - sum_j g_j dgate_j); zero elsewhere
+  float s = 0.f;
+  for (int i = 0; i < k; ++i) s += gates[t * k + i] * dgate[t * k + i];
+  float dl[kMaxE];
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) dl[e] = 0.f;
+  for (int i = 0; i < k; ++i) {
+    const int sel = topi[t * k + i];
+    const float v = gates[t * k + i] * (dgate[t * k + i] - s);
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+      if (e == sel) dl[e] = v;
+  }
   for (int j = lane; j < H / 8; j += 32) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (dout != nullptr) {  // the residual path, when the experts' input is the residual stream
@@ -286,6 +302,20 @@ __global__ void moe_grad_pull_kernel(const __nv_bfloat16* __restrict__ dout, con
         acc[2 * q + 1] += f.y;
       }
     }
+    if (router_w != nullptr) {  // the router path: dx += dl W_r (experts in a fixed order)
+#pragma unroll
+      for (int e = 0; e < kMaxE; ++e) {
+        if (e >= E) break;
+        const uint4 wv = reinterpret_cast<const uint4*>(router_w + static_cast<long long>(e) * H)[j];
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ww[q]);
+          acc[2 * q] = fmaf(dl[e], f.x, acc[2 * q]);
+          acc[2 * q + 1] = fmaf(dl[e], f.y, acc[2 * q + 1]);
+        }
+      }
+    }
     uint4 o;
     o.x = pack_bf16x2(acc[0], acc[1]);
     o.y = pack_bf16x2(acc[2], acc[3]);
@@ -294,13 +324,51 @@ __global__ void moe_grad_pull_kernel(const __nv_bfloat16* __restrict__ dout, con
     reinterpret_cast<uint4*>(dx + static_cast<long long>(t) * H)[j] = o;
   }
   if (lane == 0) {
-    // gates = softmax(l_sel): dl_sel_i = g_i (dgate_i - sum_j g_j dgate_j)
-    float s = 0.f;
-    for (int i = 0; i < k; ++i) s += gates[t * k + i] * dgate[t * k + i];
-    for (int e = 0; e < E; ++e) dlogits[static_cast<long long>(t) * E + e] = 0.f;
-    for (int i = 0; i < k; ++i)
-      dlogits[static_cast<long long>(t) * E + topi[t * k + i]] = gates[t * k + i] * (dgate[t * k + i] - s);
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+      if (e < E) dlogits[static_cast<long long>(t) * E + e] = dl[e];
   }
+}
+
+// Router weight gradient, deterministic in two passes.  Pass 1: CTA (column block cb, token
+// chunk c) sums dl[t, e] * x[t, h] over its chunk's tokens in order for 256 columns (one per
+// thread) and every expert, into partial[c][e][h].  Pass 2: one thread per (e, h) adds the chunks'
+// partials in chunk order to the fp32 gradient.
+constexpr int kRwCols = 256;
+constexpr int kRwChunk = 256;
+
+__global__ void __launch_bounds__(kRwCols) moe_router_wgrad_kernel(const float* __restrict__ dlogits,
+                                                                    const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                                    int E, float* __restrict__ partial) {
+  const int h = blockIdx.x * kRwCols + threadIdx.x;
+  const int c = blockIdx.y;
+  __shared__ float sdl[kRwChunk * kMaxE];
+  const int t0 = c * kRwChunk, t1 = min(T, t0 + kRwChunk);
+  for (int i = threadIdx.x; i < (t1 - t0) * E; i += kRwCols) sdl[i] = dlogits[static_cast<long long>(t0) * E + i];
+  __syncthreads();
+  if (h >= H) return;
+  float acc[kMaxE];
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) acc[e] = 0.f;
+  for (int t = t0; t < t1; ++t) {
+    const float xv = __bfloat162float(x[static_cast<long long>(t) * H + h]);
+    const float* d = sdl + (t - t0) * E;
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+      if (e < E) acc[e] = fmaf(d[e], xv, acc[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e)
+    if (e < E) partial[(static_cast<long long>(c) * E + e) * H + h] = acc[e];
+}
+
+__global__ void moe_router_wgrad_reduce_kernel(const float* __restrict__ partial, int chunks, int E, int H,
+                                               float* __restrict__ grad) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(E) * H) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += partial[static_cast<long long>(c) * E * H + i];
+  grad[i] += s;
 }
 
 MoeRoutes make_routes(int world, int me, int E, int k, void* const* peers) {
@@ -369,12 +437,28 @@ int moe_grad_push(const void* dout, const float* gates, const void* ycache, cons
 
 int moe_grad_pull(const void* dout, const float* gates, const float* dgate, const int* topi,
                   const long long* route_row, int T, int k, int H, int E, int world, void* const* dxbuf, void* dx,
-                  float* dlogits, cudaStream_t s) {
-  if (world > kMaxE || H % 8) return -1;
+                  float* dlogits, cudaStream_t s, const void* router_w) {
+  if (world > kMaxE || E > kMaxE || k > kMaxK || H % 8) return -1;
   const MoeRoutes r = make_routes(world, 0, E, k, dxbuf);
   moe_grad_pull_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(dout), gates,
                                                           dgate, topi, route_row, T, k, H, E, r,
+                                                          reinterpret_cast<const __nv_bfloat16*>(router_w),
                                                           reinterpret_cast<__nv_bfloat16*>(dx), dlogits);
+  return static_cast<int>(cudaGetLastError());
+}
+
+long long moe_router_wgrad_ws_floats(int T, int H, int E) {
+  return static_cast<long long>((T + kRwChunk - 1) / kRwChunk) * E * H;
+}
+
+int moe_router_wgrad(const float* dlogits, const void* x, int T, int H, int E, float* partial, float* grad,
+                     cudaStream_t s) {
+  if (E > kMaxE || E <= 0 || T <= 0 || H <= 0) return -1;
+  const int chunks = (T + kRwChunk - 1) / kRwChunk;
+  moe_router_wgrad_kernel<<<dim3((H + kRwCols - 1) / kRwCols, chunks), kRwCols, 0, s>>>(
+      dlogits, reinterpret_cast<const __nv_bfloat16*>(x), T, H, E, partial);
+  const long long n = static_cast<long long>(E) * H;
+  moe_router_wgrad_reduce_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(partial, chunks, E, H, grad);
   return static_cast<int>(cudaGetLastError());
 }
 

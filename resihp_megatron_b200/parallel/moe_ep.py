@@ -287,12 +287,12 @@ class ExpertParallelMoE:
         T = s["T"]
         dx = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device) if out is None else out
         dlogits = torch.empty(T, self.E, dtype=torch.float32, device=self.device)
+        # dx = residual path + expert paths + router path (dl W_r), all in one pass per token
         ext().moe_grad_pull(s["dout"] if residual else None, s["gates"], s["dgate"], s["topi"], s["route_row"], self.k,
-                            self.E, self.heap.peer_ptrs("dxrecv"), dx, dlogits)
-        ops.count(1)
-        # router path: [T, E] x [E, H] products with E <= 16 (too narrow for the tensor-core tiles)
-        router_grad.add_(dlogits.t() @ s["x"].float())
-        dx.add_((dlogits @ router_w.float()).bfloat16())
+                            self.E, self.heap.peer_ptrs("dxrecv"), dx, dlogits, router_w.contiguous())
+        # router weight gradient dl^T x: E <= 16 rows, too narrow for the tensor-core tiles
+        ext().moe_router_wgrad(dlogits, s["x"].contiguous(), router_grad)
+        ops.count(3)
         self._barrier()
         return dx
 
